@@ -1,0 +1,531 @@
+#pragma once
+// Persistent warp-specialised bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   C[M,N] = sum_k A[m,k] * B[n,k]        (f32 accumulation in TMEM)
+//
+// A and B are each either K-major (row-major [rows, K]) or MN-major (stored
+// transposed, row-major [K, rows]); the UMMA descriptors take either layout,
+// so the three GEMMs of a linear layer (fwd, dX, dW) need no transposes.
+//
+// CTA tile 128 x 256 x 64, 4-stage TMA ring, two TMEM accumulators (2 x 256
+// columns) so the epilogue of tile i overlaps the main loop of tile i+1.
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
+// TMEM owner, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+//
+// Epilogues (fused so no extra pass over the output is needed):
+//   EPI_BF16        C -> bf16, optionally + residual R (R may alias C)
+//   EPI_F32         C -> f32, optionally + beta * C_old (gradient accumulation)
+//   EPI_SWIGLU      B rows interleaved in blocks of 128 [gate|up]; writes
+//                   H = silu(g)*u (bf16, N/2 columns) and the pre-activation GU
+//   EPI_SWIGLU_BWD  C = dH; reads GU, writes dGU (interleaved like GU)
+//   EPI_CE          C = logits; per (row, N-tile) max and sum(exp), target
+//                   logit capture, optional bf16 logits store
+//   EPI_ROPE        C = [q | k | v] projections; rotate-half RoPE on q and k
+//                   heads using per-position cos/sin tables
+//
+// No TMA load here uses cluster multicast.
+#include <cudaTypedefs.h>
+#include <algorithm>
+
+#include "host_util.h"
+
+#include "ptx.cuh"
+
+namespace oxi {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK * 2;   // 32 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int GEMM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 8;
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, EPI_CE = 4, EPI_ROPE = 5 };
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles;
+  void* D;                 // main output
+  int64_t ldd;
+  const __nv_bfloat16* R;  // residual (BF16) / GU (SWIGLU_BWD)
+  int64_t ldr;
+  void* D2;                // GU output (SWIGLU)
+  int64_t ldd2;
+  float beta;              // F32: C = acc + beta * C_old
+  float alpha;             // scale applied to the accumulator
+  // CE
+  const int64_t* targets;
+  float* part_max;         // [M, tiles_n]
+  float* part_sum;         // [M, tiles_n]
+  float* tgt_logit;        // [M]
+  // RoPE
+  const float* rope_cos;   // [S, hd/2]
+  const float* rope_sin;
+  int rope_seq, rope_hd, rope_q_cols, rope_k_cols;  // q columns [0,q), k columns [q, q+k)
+  int vec_ok;              // output rows are 16-byte aligned
+  int* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
+  // Group GROUP_M row-tiles together so consecutive CTAs share B tiles in L2.
+  const int per_group = GROUP_M * p.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(p.tiles_m - first_m, GROUP_M);
+  const int r = t - g * per_group;
+  tm = first_m + (r % gm);
+  tn = r / gm;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+// ------------------------------------------------------------------ stores
+__device__ __forceinline__ void store_bf16_row(__nv_bfloat16* dst, const float* v, int ncols_valid, bool vec) {
+  if (vec && ncols_valid >= 32) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf16(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf16(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf16(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf16(v[q * 8 + 6], v[q * 8 + 7]);
+      d4[q] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols_valid) dst[j] = __float2bfloat16(v[j]);
+  }
+}
+__device__ __forceinline__ void load_bf16_row(const __nv_bfloat16* src, float* v, int ncols_valid, bool vec) {
+  if (vec && ncols_valid >= 32) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w = s4[q];
+      float2 a = unpack_bf16(w.x), b = unpack_bf16(w.y), c = unpack_bf16(w.z), d = unpack_bf16(w.w);
+      v[q * 8 + 0] = a.x; v[q * 8 + 1] = a.y; v[q * 8 + 2] = b.x; v[q * 8 + 3] = b.y;
+      v[q * 8 + 4] = c.x; v[q * 8 + 5] = c.y; v[q * 8 + 6] = d.x; v[q * 8 + 7] = d.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (j < ncols_valid) ? __bfloat162float(src[j]) : 0.f;
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment is required by the 128B swizzle atoms.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_parity[STAGES];
+      bool armed[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) { armed[s] = false; armed_parity[s] = 0; }
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          armed[stage] = true;
+          armed_parity[stage] = phase;
+          uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
+          uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], m0, k0);
+            tma_load_2d(a_dst + BK * 128, &tmA, &full[stage], m0 + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tma_load_2d(b_dst + q * BK * 128, &tmB, &full[stage], n0 + 64 * q, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Drain the copies this thread issued before leaving (bounded).
+        for (int s = 0; s < STAGES; ++s)
+          if (armed[s]) mbar_wait(&full[s], armed_parity[s], nullptr, p.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad, bd;
+            if (!A_MN) ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            else       ad = umma_desc_sw128(a_addr + k * 2048, BK * 128, 1024);
+            if (!B_MN) bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
+            else       bd = umma_desc_sw128(b_addr + k * 2048, BK * 128, 1024);
+            tc_mma_f16(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec = p.vec_ok != 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      const int m0 = tm * BM, n0 = tn * BN;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t tbase = tmem_base + lane_base + acc * BN;
+
+      if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_SWIGLU_BWD) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tc_wait_ld();
+          if (c == BN / 32 - 1) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          const int col = n0 + c * 32;
+          const int nvalid = min(32, p.N - col);
+          if (!row_ok || nvalid <= 0) continue;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+          if constexpr (EPI == EPI_BF16) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col;
+            if (p.R) {
+              float rr[32];
+              load_bf16_row(p.R + (int64_t)row * p.ldr + col, rr, nvalid, vec);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += rr[j];
+            }
+            store_bf16_row(dst, v, nvalid, vec);
+          } else if constexpr (EPI == EPI_F32) {
+            float* dst = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col;
+            if (vec && nvalid >= 32) {
+              float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 o = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+                if (p.beta != 0.f) {
+                  float4 old = d4[q];
+                  o.x += p.beta * old.x; o.y += p.beta * old.y; o.z += p.beta * old.z; o.w += p.beta * old.w;
+                }
+                d4[q] = o;
+              }
+            } else {
+              for (int j = 0; j < nvalid; ++j) dst[j] = v[j] + (p.beta != 0.f ? p.beta * dst[j] : 0.f);
+            }
+          } else {  // EPI_SWIGLU_BWD: v = dH columns; GU interleaved in blocks of 128
+            const int blk = col / 128, off = col % 128;
+            const __nv_bfloat16* gp = p.R + (int64_t)row * p.ldr + blk * 256 + off;
+            const __nv_bfloat16* up = gp + 128;
+            float g[32], u[32];
+            load_bf16_row(gp, g, nvalid, vec);
+            load_bf16_row(up, u, nvalid, vec);
+            float dg[32], du[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float s = 1.f / (1.f + __expf(-g[j]));
+              const float sg = g[j] * s;
+              du[j] = v[j] * sg;
+              dg[j] = v[j] * u[j] * s * (1.f + g[j] * (1.f - s));
+            }
+            __nv_bfloat16* dgp = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + blk * 256 + off;
+            store_bf16_row(dgp, dg, nvalid, vec);
+            store_bf16_row(dgp + 128, du, nvalid, vec);
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
+        // tile columns [0,128) gate, [128,256) up, for output columns n0/2 + [0,128)
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(tbase + c * 32, rg);
+          tmem_ld32(tbase + 128 + c * 32, ru);
+          tc_wait_ld();
+          if (c == 3) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          const int hcol = n0 / 2 + c * 32;
+          const int nvalid = min(32, p.N / 2 - hcol);
+          if (!row_ok || nvalid <= 0) continue;
+          float g[32], u[32], h[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            g[j] = __uint_as_float(rg[j]);
+            u[j] = __uint_as_float(ru[j]);
+            h[j] = silu_f(g[j]) * u[j];
+          }
+          store_bf16_row(reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + hcol, h, nvalid, vec);
+          if (p.D2) {
+            __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.D2) + (int64_t)row * p.ldd2 + n0 + c * 32;
+            store_bf16_row(gu, g, nvalid, vec);
+            store_bf16_row(gu + 128, u, nvalid, vec);
+          }
+        }
+      } else if constexpr (EPI == EPI_CE) {
+        float run_max = -INFINITY, run_sum = 0.f;
+        const int64_t tgt = row_ok ? p.targets[row] : -1;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tc_wait_ld();
+          if (c == BN / 32 - 1) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          const int col = n0 + c * 32;
+          const int nvalid = min(32, p.N - col);
+          if (!row_ok || nvalid <= 0) continue;
+          float v[32];
+          float cmax = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __uint_as_float(r[j]) * p.alpha;
+            if (j < nvalid) cmax = fmaxf(cmax, v[j]);
+          }
+          const float nmax = fmaxf(run_max, cmax);
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nvalid) s += __expf(v[j] - nmax);
+          run_sum = run_sum * __expf(run_max - nmax) + s;
+          run_max = nmax;
+          if (tgt >= col && tgt < col + nvalid) {
+            float tv = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col + j == tgt) tv = v[j];
+            p.tgt_logit[row] = tv;
+          }
+          if (p.D) store_bf16_row(reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col, v, nvalid, vec);
+        }
+        if (row_ok) {
+          p.part_max[(int64_t)row * p.tiles_n + tn] = run_max;
+          p.part_sum[(int64_t)row * p.tiles_n + tn] = run_sum;
+        }
+      } else if constexpr (EPI == EPI_ROPE) {
+        // Heads are rope_hd wide; each pair of 32-column chunks (c, c + half/32)
+        // forms the rotate-half pair for one head.
+        const int hd = p.rope_hd, half = hd / 2;
+        const int pos = row % p.rope_seq;
+        const int nch = BN / 32, pair_off = half / 32;
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          const int col = n0 + c * 32;
+          const int in_head = (c * 32) % hd;   // tiles start at head boundaries (BN % hd == 0)
+          if (in_head >= half) continue;        // handled with its partner
+          uint32_t r1[32], r2[32];
+          tmem_ld32(tbase + c * 32, r1);
+          tmem_ld32(tbase + (c + pair_off) * 32, r2);
+          tc_wait_ld();
+          const bool last = (c + pair_off == nch - 1) || (c == nch - 1);
+          if (last) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          const int nvalid = min(32, p.N - col);
+          if (!row_ok || nvalid <= 0) continue;
+          float x1[32], x2[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) { x1[j] = __uint_as_float(r1[j]); x2[j] = __uint_as_float(r2[j]); }
+          const bool rot = col < p.rope_q_cols + p.rope_k_cols;
+          if (rot) {
+            const float* cs = p.rope_cos + (int64_t)pos * half + in_head;
+            const float* sn = p.rope_sin + (int64_t)pos * half + in_head;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float cj = cs[j], sj = sn[j];
+              const float a = x1[j], b = x2[j];
+              x1[j] = a * cj - b * sj;
+              x2[j] = b * cj + a * sj;
+            }
+          }
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col;
+          store_bf16_row(dst, x1, nvalid, vec);
+          const int nvalid2 = min(32, p.N - (col + half));
+          if (nvalid2 > 0) store_bf16_row(dst + half, x2, nvalid2, vec);
+        }
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ====================================================================== host
+inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    OXI_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q));
+    OXI_CHECK(q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [rows, cols] with row stride
+// `ld` elements, box {box_cols, box_rows}, 128-byte swizzle, zero OOB fill.
+inline CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
+  OXI_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  OXI_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes (ld % 8 == 0)");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  OXI_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+inline int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    OXI_CUDA_CHECK(cudaGetDevice(&dev));
+    OXI_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
+constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+template <bool A_MN, bool B_MN, int EPI>
+static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, cudaStream_t st) {
+  auto kern = gemm_kernel<A_MN, B_MN, EPI>;
+  static bool attr = false;
+  if (!attr) {
+    OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
+    attr = true;
+  }
+  int grid = std::min(p.num_tiles, num_sms());
+  if (grid <= 0) return;
+  kern<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int EPI>
+static void launch_epi(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
+                       cudaStream_t st) {
+  if (!a_mn && !b_mn) launch_t<false, false, EPI>(ta, tb, p, st);
+  else if (!a_mn && b_mn) launch_t<false, true, EPI>(ta, tb, p, st);
+  else if (a_mn && !b_mn) launch_t<true, false, EPI>(ta, tb, p, st);
+  else launch_t<true, true, EPI>(ta, tb, p, st);
+}
+
+// Operand description (row-major storage, unit inner stride):
+//  K-major operand with R rows: stored [R, K]  (mn=false)
+//  MN-major operand with R rows: stored [K, R] (mn=true)
+struct Operand {
+  const void* ptr;
+  int64_t rows, k, ld;
+  bool mn;
+};
+
+inline CUtensorMap operand_tmap(const Operand& o, int tile_rows) {
+  if (!o.mn) return make_tmap_bf16(o.ptr, o.rows, o.k, o.ld, BK, tile_rows);
+  // stored [K, rows]; box = 64 row-elements (inner) x BK k-rows
+  return make_tmap_bf16(o.ptr, o.k, o.rows, o.ld, 64, BK);
+}
+
+inline void fill_common(GemmParams& p, const Operand& a, const Operand& b) {
+  OXI_CHECK(a.k == b.k, "GEMM K mismatch: ", a.k, " vs ", b.k);
+  p.M = (int)a.rows;
+  p.N = (int)b.rows;
+  p.K = (int)a.k;
+  p.tiles_m = (p.M + BM - 1) / BM;
+  p.tiles_n = (p.N + BN - 1) / BN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.alpha = 1.f;
+}
+
+inline bool aligned16(const void* ptr, int64_t ld, int esize) {
+  return ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0) && ((ld * esize) % 16 == 0);
+}
+
+}  // namespace oxi

@@ -1,0 +1,49 @@
+"""Access to the compiled kernel library and its per-device status word.
+
+Every kernel receives a pointer to a small int32 status buffer on its device.
+Bounded waits and debug checks record an error code there instead of trapping;
+``check_status`` reads it back (a host sync) and raises if it is non-zero.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _ext
+
+_STATUS = {}
+
+ERRORS = {
+    1: "pipeline wait timed out",
+    2: "cross-GPU wait timed out",
+    3: "bounds check failed",
+    4: "non-finite value",
+}
+
+
+def ext():
+    """The extension module; raises if it cannot be built/loaded."""
+    return _ext.load(required=True)
+
+
+def status(device) -> torch.Tensor:
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(16, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = t
+    return t
+
+
+def read_status(device, reset: bool = True) -> int:
+    s = status(device)
+    v = int(s[0].item())
+    if reset and v:
+        s.zero_()
+    return v
+
+
+def check_status(device) -> None:
+    v = read_status(device)
+    if v:
+        raise RuntimeError(f"oxidizr kernel status {v}: {ERRORS.get(v, 'unknown error')}")
