@@ -1,0 +1,29 @@
+// Launchers of the memory-bound kernels (norms.cu, train_ew.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace oxi {
+
+// mode: 0 RMSNorm, 1 LayerNorm, 2 gated RMSNorm (rmsnorm(x * silu(gate)))
+void launch_norm_fwd(int mode, const void* x, const void* gate, const void* w, bool wf32, const void* b, void* y,
+                     float* rstd, float* mean, int64_t rows, int H, float eps, cudaStream_t st);
+void launch_norm_bwd(int mode, const void* dy, const void* x, const void* gate, const void* w, bool wf32,
+                     const float* rstd, const float* mean, const void* dres, void* dx, void* dgate, float* dw,
+                     float* db, int64_t rows, int H, cudaStream_t st);
+
+void launch_ce_finish(const float* pmax, const float* psum, int nt, const float* tgt_logit, const int64_t* targets,
+                      float* lse, float* loss, int64_t rows, cudaStream_t st);
+void launch_ce_bwd(void* logits, int64_t ld, int64_t V, int64_t rows, const float* lse, const int64_t* targets,
+                   const float* gscale, float inv_count, cudaStream_t st);
+void launch_embed_fwd(const int64_t* ids, const void* w, void* out, int64_t rows, int H, cudaStream_t st);
+void launch_embed_bwd(const int64_t* ids, const void* dy, float* dw, int64_t rows, int H, cudaStream_t st);
+void launch_rope_bwd(void* x, int64_t ld, int64_t rows, int ncols_rot, int hd, const float* cos, const float* sin,
+                     int seq, cudaStream_t st);
+void launch_sqsum(const float* g, int64_t n, float* out, cudaStream_t st);
+void launch_clip_coef(const float* sqsum, float max_norm, float pre_scale, float* coef, float* norm_out,
+                      cudaStream_t st);
+void launch_adamw(float* p, void* p16, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
+                  float eps, float wd, float bc1, float bc2, const float* gscale, cudaStream_t st);
+
+}  // namespace oxi

@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "kernels.h"
+#include "kernels_ew.h"
 
 using oxi::Mat;
 
@@ -119,6 +120,122 @@ void gemm_rope(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
                         (int)cos.size(0), (int)hd, (int)q_cols, (int)k_cols, status_ptr(status), stream());
 }
 
+// ------------------------------------------------------------ norms
+void check_bf16_rows(const torch::Tensor& t, int64_t rows, int64_t H, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.is_contiguous() && t.numel() == rows * H, what,
+              " must be a contiguous bf16 CUDA tensor with ", rows, "x", H, " elements");
+}
+
+void norm_fwd(int64_t mode, torch::Tensor x, c10::optional<torch::Tensor> gate, torch::Tensor w,
+              c10::optional<torch::Tensor> b, torch::Tensor y, torch::Tensor rstd, c10::optional<torch::Tensor> mean,
+              double eps) {
+  c10::cuda::CUDAGuard g(x.device());
+  const int64_t H = x.size(-1), rows = x.numel() / H;
+  check_bf16_rows(x, rows, H, "x");
+  check_bf16_rows(y, rows, H, "y");
+  TORCH_CHECK(w.is_contiguous() && w.numel() == H, "weight shape");
+  const bool wf32 = w.scalar_type() == torch::kFloat32;
+  if (mode == 2) check_bf16_rows(*gate, rows, H, "gate");
+  const void* bp = nullptr;
+  if (mode == 1) {
+    TORCH_CHECK(b.has_value() && b->scalar_type() == w.scalar_type() && b->numel() == H, "bias");
+    bp = b->data_ptr();
+  }
+  oxi::launch_norm_fwd((int)mode, x.data_ptr(), mode == 2 ? gate->data_ptr() : nullptr, w.data_ptr(), wf32, bp,
+                       y.data_ptr(), rstd.data_ptr<float>(), mode == 1 ? mean->data_ptr<float>() : nullptr, rows,
+                       (int)H, (float)eps, stream());
+}
+
+void norm_bwd(int64_t mode, torch::Tensor dy, torch::Tensor x, c10::optional<torch::Tensor> gate, torch::Tensor w,
+              torch::Tensor rstd, c10::optional<torch::Tensor> mean, c10::optional<torch::Tensor> dres,
+              torch::Tensor dx, c10::optional<torch::Tensor> dgate, torch::Tensor dw, c10::optional<torch::Tensor> db) {
+  c10::cuda::CUDAGuard g(x.device());
+  const int64_t H = x.size(-1), rows = x.numel() / H;
+  check_bf16_rows(dy, rows, H, "dy");
+  check_bf16_rows(x, rows, H, "x");
+  check_bf16_rows(dx, rows, H, "dx");
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.numel() == H && dw.is_contiguous(), "dw must be f32 [H]");
+  const void* dr = nullptr;
+  if (dres.has_value() && dres->defined()) {
+    check_bf16_rows(*dres, rows, H, "dres");
+    dr = dres->data_ptr();
+  }
+  oxi::launch_norm_bwd((int)mode, dy.data_ptr(), x.data_ptr(), mode == 2 ? gate->data_ptr() : nullptr, w.data_ptr(),
+                       w.scalar_type() == torch::kFloat32, rstd.data_ptr<float>(),
+                       mode == 1 ? mean->data_ptr<float>() : nullptr, dr, dx.data_ptr(),
+                       mode == 2 ? dgate->data_ptr() : nullptr, dw.data_ptr<float>(),
+                       mode == 1 ? db->data_ptr<float>() : nullptr, rows, (int)H, stream());
+}
+
+// ------------------------------------------------------------ CE
+void ce_finish(torch::Tensor pmax, torch::Tensor psum, torch::Tensor tgt_logit, torch::Tensor targets,
+               torch::Tensor lse, torch::Tensor loss) {
+  c10::cuda::CUDAGuard g(pmax.device());
+  oxi::launch_ce_finish(pmax.data_ptr<float>(), psum.data_ptr<float>(), (int)pmax.size(1), tgt_logit.data_ptr<float>(),
+                        targets.data_ptr<int64_t>(), lse.data_ptr<float>(), loss.data_ptr<float>(), pmax.size(0),
+                        stream());
+}
+
+void ce_bwd(torch::Tensor logits, int64_t V, torch::Tensor lse, torch::Tensor targets, torch::Tensor gscale,
+            double inv_count) {
+  c10::cuda::CUDAGuard g(logits.device());
+  TORCH_CHECK(logits.scalar_type() == torch::kBFloat16 && logits.stride(1) == 1, "logits");
+  oxi::launch_ce_bwd(logits.data_ptr(), logits.stride(0), V, logits.size(0), lse.data_ptr<float>(),
+                     targets.data_ptr<int64_t>(), gscale.data_ptr<float>(), (float)inv_count, stream());
+}
+
+// ------------------------------------------------------------ embedding / rope
+void embed_fwd(torch::Tensor ids, torch::Tensor w, torch::Tensor out) {
+  c10::cuda::CUDAGuard g(w.device());
+  TORCH_CHECK(ids.scalar_type() == torch::kInt64 && ids.is_contiguous(), "ids must be contiguous int64");
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && out.is_contiguous(), "embedding tensors");
+  oxi::launch_embed_fwd(ids.data_ptr<int64_t>(), w.data_ptr(), out.data_ptr(), ids.numel(), (int)w.size(1), stream());
+}
+
+void embed_bwd(torch::Tensor ids, torch::Tensor dy, torch::Tensor dw) {
+  c10::cuda::CUDAGuard g(dy.device());
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous() && dy.is_contiguous(), "embedding grad");
+  oxi::launch_embed_bwd(ids.data_ptr<int64_t>(), dy.data_ptr(), dw.data_ptr<float>(), ids.numel(), (int)dw.size(1),
+                        stream());
+}
+
+void rope_bwd(torch::Tensor x, int64_t ncols_rot, int64_t hd, torch::Tensor cos, torch::Tensor sin) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "rope_bwd x");
+  oxi::launch_rope_bwd(x.data_ptr(), x.stride(0), x.size(0), (int)ncols_rot, (int)hd, cos.data_ptr<float>(),
+                       sin.data_ptr<float>(), (int)cos.size(0), stream());
+}
+
+// ------------------------------------------------------------ optimizer
+void sqsum(torch::Tensor g, torch::Tensor out) {
+  c10::cuda::CUDAGuard gd(g.device());
+  TORCH_CHECK(g.scalar_type() == torch::kFloat32 && g.is_contiguous(), "sqsum input must be contiguous f32");
+  oxi::launch_sqsum(g.data_ptr<float>(), g.numel(), out.data_ptr<float>(), stream());
+}
+
+void clip_coef(torch::Tensor sq, double max_norm, double pre_scale, torch::Tensor coef, torch::Tensor norm) {
+  c10::cuda::CUDAGuard gd(sq.device());
+  oxi::launch_clip_coef(sq.data_ptr<float>(), (float)max_norm, (float)pre_scale, coef.data_ptr<float>(),
+                        norm.data_ptr<float>(), stream());
+}
+
+void adamw(torch::Tensor p, c10::optional<torch::Tensor> p16, torch::Tensor g, torch::Tensor m, torch::Tensor v,
+           double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+           c10::optional<torch::Tensor> gscale) {
+  c10::cuda::CUDAGuard gd(p.device());
+  TORCH_CHECK(p.scalar_type() == torch::kFloat32 && g.scalar_type() == torch::kFloat32 && p.is_contiguous() &&
+                  g.is_contiguous() && m.is_contiguous() && v.is_contiguous() && p.numel() == g.numel() &&
+                  m.numel() == p.numel() && v.numel() == p.numel(), "adamw: flat f32 buffers of equal size");
+  void* p16p = nullptr;
+  if (p16.has_value() && p16->defined()) {
+    TORCH_CHECK(p16->scalar_type() == torch::kBFloat16 && p16->numel() == p.numel() && p16->is_contiguous(), "p16");
+    p16p = p16->data_ptr();
+  }
+  oxi::launch_adamw(p.data_ptr<float>(), p16p, g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                    p.numel(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
+                    gscale.has_value() && gscale->defined() ? gscale->data_ptr<float>() : nullptr, stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -128,4 +245,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, "GEMM with fused SwiGLU backward epilogue");
   m.def("gemm_ce", &gemm_ce, "lm_head GEMM with fused cross-entropy partials");
   m.def("gemm_rope", &gemm_rope, "QKV GEMM with fused rotate-half RoPE epilogue");
+  m.def("norm_fwd", &norm_fwd, "RMSNorm / LayerNorm / gated RMSNorm forward");
+  m.def("norm_bwd", &norm_bwd, "RMSNorm / LayerNorm / gated RMSNorm backward");
+  m.def("ce_finish", &ce_finish, "combine CE partials into lse and per-row loss");
+  m.def("ce_bwd", &ce_bwd, "in-place softmax-minus-onehot gradient of the logits");
+  m.def("embed_fwd", &embed_fwd, "embedding gather");
+  m.def("embed_bwd", &embed_bwd, "embedding scatter-add into f32 grad");
+  m.def("rope_bwd", &rope_bwd, "in-place inverse rotate-half RoPE");
+  m.def("sqsum", &sqsum, "sum of squares (atomically added into out)");
+  m.def("clip_coef", &clip_coef, "global-norm clip coefficient on device");
+  m.def("adamw", &adamw, "flat multi-tensor AdamW (f32 master, bf16 copy)");
 }

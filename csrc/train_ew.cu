@@ -1,0 +1,294 @@
+// Memory-bound training kernels: cross-entropy finish/backward, embedding
+// gather/scatter, RoPE backward, gradient-norm, clip coefficient and the flat
+// multi-tensor AdamW update.  All are single-pass over their data with 16-byte
+// vector accesses; none synchronises with the host.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "host_util.h"
+#include "kernels_ew.h"
+
+namespace oxi {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+// --------------------------------------------------------------- CE finish
+// One warp per row: lse = logsumexp over the per-tile (max, sum) partials;
+// loss = lse - target_logit (0 for ignored rows, target < 0).
+__global__ void ce_finish_kernel(const float* __restrict__ pmax, const float* __restrict__ psum, int nt,
+                                 const float* __restrict__ tgt_logit, const int64_t* __restrict__ targets,
+                                 float* __restrict__ lse, float* __restrict__ loss, int64_t rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= rows) return;
+  float m = -INFINITY;
+  for (int i = lane; i < nt; i += 32) m = fmaxf(m, pmax[row * nt + i]);
+  m = warp_max(m);
+  float s = 0.f;
+  for (int i = lane; i < nt; i += 32) {
+    const float mi = pmax[row * nt + i];
+    if (mi > -INFINITY) s += psum[row * nt + i] * __expf(mi - m);
+  }
+  s = warp_sum(s);
+  if (lane == 0) {
+    const float l = m + logf(s);
+    lse[row] = l;
+    loss[row] = targets[row] >= 0 ? (l - tgt_logit[row]) : 0.f;
+  }
+}
+
+// ------------------------------------------------------------------ CE bwd
+// In place: logits[r, v] <- (exp(logits - lse[r]) - [v == t_r]) * scale, where
+// scale = (*gscale) * inv_count.  Rows with target < 0 get zero gradient.
+__global__ void ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, int64_t V,
+                              const float* __restrict__ lse, const int64_t* __restrict__ targets,
+                              const float* __restrict__ gscale, float inv_count) {
+  const int64_t row = blockIdx.y;
+  const float l = lse[row];
+  const int64_t t = targets[row];
+  const float sc = (t >= 0) ? (*gscale) * inv_count : 0.f;
+  __nv_bfloat16* rp = logits + row * ld;
+  const int64_t nvec = V / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 u = reinterpret_cast<uint4*>(rp)[i];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = __bfloat1622float2(h[k]);
+      const int64_t c = i * 8 + 2 * k;
+      f.x = (__expf(f.x - l) - (c == t ? 1.f : 0.f)) * sc;
+      f.y = (__expf(f.y - l) - (c + 1 == t ? 1.f : 0.f)) * sc;
+      h[k] = __floats2bfloat162_rn(f.x, f.y);
+    }
+    reinterpret_cast<uint4*>(rp)[i] = u;
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t c = nvec * 8 + threadIdx.x; c < V; c += blockDim.x) {
+      const float f = __bfloat162float(rp[c]);
+      rp[c] = __float2bfloat16((__expf(f - l) - (c == t ? 1.f : 0.f)) * sc);
+    }
+  }
+}
+
+// --------------------------------------------------------------- embedding
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ w,
+                                 __nv_bfloat16* __restrict__ out, int64_t rows, int H) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const uint4* src = reinterpret_cast<const uint4*>(w + ids[row] * (int64_t)H);
+  uint4* dst = reinterpret_cast<uint4*>(out + row * (int64_t)H);
+  for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+}
+
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dy,
+                                 float* __restrict__ dw, int64_t rows, int H) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(dy + row * (int64_t)H);
+  float* dst = dw + ids[row] * (int64_t)H;
+  for (int i = lane; i < H / 4; i += 32) {
+    const float2 a = __bfloat1622float2(src[2 * i]);
+    const float2 b = __bfloat1622float2(src[2 * i + 1]);
+    atomicAdd(reinterpret_cast<float4*>(dst) + i, make_float4(a.x, a.y, b.x, b.y));
+  }
+}
+
+// ---------------------------------------------------------------- RoPE bwd
+// In place on the first `ncols_rot` columns of x [rows, ld] (heads of width hd):
+// inverse rotate-half rotation (rotation by -angle).
+__global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int64_t rows, int ncols_rot, int hd,
+                                const float* __restrict__ cos, const float* __restrict__ sin, int seq) {
+  const int half = hd / 2;
+  const int pairs_per_row = ncols_rot / 2;
+  const int64_t total = rows * pairs_per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / pairs_per_row;
+    const int p = (int)(i % pairs_per_row);
+    const int head = p / half, j = p % half;
+    const int pos = (int)(row % seq);
+    __nv_bfloat16* base = x + row * ld + head * hd;
+    const float c = cos[pos * half + j], s = sin[pos * half + j];
+    const float d1 = __bfloat162float(base[j]), d2 = __bfloat162float(base[j + half]);
+    base[j] = __float2bfloat16(d1 * c + d2 * s);
+    base[j + half] = __float2bfloat16(d2 * c - d1 * s);
+  }
+}
+
+// --------------------------------------------------------- grad norm / clip
+__global__ void sqsum_kernel(const float* __restrict__ g, int64_t n, float* __restrict__ out) {
+  float s = 0.f;
+  const int64_t nv = n / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(g)[i];
+    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = nv * 4 + threadIdx.x; i < n; i += blockDim.x) s += g[i] * g[i];
+  s = warp_sum(s);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) atomicAdd(out, t);
+  }
+}
+
+// coef = min(1, max_norm / (sqrt(sqsum) + 1e-6)) * pre_scale; also writes the norm.
+__global__ void clip_coef_kernel(const float* __restrict__ sqsum, float max_norm, float pre_scale,
+                                 float* __restrict__ coef, float* __restrict__ norm_out) {
+  const float nrm = sqrtf(*sqsum) * pre_scale;
+  *norm_out = nrm;
+  float c = pre_scale;
+  if (max_norm > 0.f && nrm > max_norm) c *= max_norm / (nrm + 1e-6f);
+  *coef = c;
+}
+
+// ------------------------------------------------------------------- AdamW
+// Decoupled AdamW on flat f32 master weights, f32 moments; writes the bf16
+// model copy.  g is scaled by *gscale (clip coefficient and 1/world).
+__global__ void adamw_kernel(float* __restrict__ p, __nv_bfloat16* __restrict__ p16, const float* __restrict__ g,
+                             float* __restrict__ m, float* __restrict__ v, int64_t n, float lr, float b1, float b2,
+                             float eps, float wd, float bc1, float bc2, const float* __restrict__ gscale) {
+  const float gs = gscale ? *gscale : 1.f;
+  const float rb1 = 1.f / bc1, rb2 = 1.f / bc2;
+  const int64_t nv = n / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 pv = reinterpret_cast<float4*>(p)[i];
+    const float4 gv = reinterpret_cast<const float4*>(g)[i];
+    float4 mv = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float* pp = &pv.x;
+    const float* gg = &gv.x;
+    float* mm = &mv.x;
+    float* vvv = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float gk = gg[k] * gs;
+      mm[k] = b1 * mm[k] + (1.f - b1) * gk;
+      vvv[k] = b2 * vvv[k] + (1.f - b2) * gk * gk;
+      const float upd = (mm[k] * rb1) / (sqrtf(vvv[k] * rb2) + eps);
+      pp[k] = pp[k] - lr * upd - lr * wd * pp[k];
+    }
+    reinterpret_cast<float4*>(p)[i] = pv;
+    reinterpret_cast<float4*>(m)[i] = mv;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    if (p16) {
+      uint2 o;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+      h[0] = __floats2bfloat162_rn(pv.x, pv.y);
+      h[1] = __floats2bfloat162_rn(pv.z, pv.w);
+      reinterpret_cast<uint2*>(p16)[i] = o;
+    }
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t i = nv * 4 + threadIdx.x; i < n; i += blockDim.x) {
+      const float gk = g[i] * gs;
+      m[i] = b1 * m[i] + (1.f - b1) * gk;
+      v[i] = b2 * v[i] + (1.f - b2) * gk * gk;
+      const float upd = (m[i] * rb1) / (sqrtf(v[i] * rb2) + eps);
+      p[i] = p[i] - lr * upd - lr * wd * p[i];
+      if (p16) p16[i] = __float2bfloat16(p[i]);
+    }
+  }
+}
+
+}  // namespace
+
+void launch_ce_finish(const float* pmax, const float* psum, int nt, const float* tgt_logit, const int64_t* targets,
+                      float* lse, float* loss, int64_t rows, cudaStream_t st) {
+  if (!rows) return;
+  ce_finish_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(pmax, psum, nt, tgt_logit, targets, lse, loss, rows);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_ce_bwd(void* logits, int64_t ld, int64_t V, int64_t rows, const float* lse, const int64_t* targets,
+                   const float* gscale, float inv_count, cudaStream_t st) {
+  if (!rows) return;
+  OXI_CHECK(ld % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0, "logits rows must be 16-byte aligned");
+  OXI_CHECK(rows < 65536 * 32768LL, "too many rows");
+  const int64_t nvec = V / 8;
+  unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 64));
+  dim3 grid(gx, (unsigned)rows);
+  ce_bwd_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, V, lse, targets, gscale,
+                                      inv_count);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_embed_fwd(const int64_t* ids, const void* w, void* out, int64_t rows, int H, cudaStream_t st) {
+  if (!rows) return;
+  OXI_CHECK(H % 8 == 0, "embedding width must be a multiple of 8");
+  embed_fwd_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(ids, reinterpret_cast<const __nv_bfloat16*>(w),
+                                                                 reinterpret_cast<__nv_bfloat16*>(out), rows, H);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_embed_bwd(const int64_t* ids, const void* dy, float* dw, int64_t rows, int H, cudaStream_t st) {
+  if (!rows) return;
+  OXI_CHECK(H % 8 == 0, "embedding width must be a multiple of 8");
+  embed_bwd_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(ids, reinterpret_cast<const __nv_bfloat16*>(dy), dw,
+                                                                 rows, H);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_rope_bwd(void* x, int64_t ld, int64_t rows, int ncols_rot, int hd, const float* cos, const float* sin,
+                     int seq, cudaStream_t st) {
+  if (!rows || !ncols_rot) return;
+  const int64_t total = rows * (ncols_rot / 2);
+  const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 16);
+  rope_bwd_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), ld, rows, ncols_rot, hd, cos, sin, seq);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_sqsum(const float* g, int64_t n, float* out, cudaStream_t st) {
+  if (!n) return;
+  const unsigned grid = (unsigned)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)sm_count() * 4);
+  sqsum_kernel<<<grid, 256, 0, st>>>(g, n, out);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_clip_coef(const float* sqsum, float max_norm, float pre_scale, float* coef, float* norm_out,
+                      cudaStream_t st) {
+  clip_coef_kernel<<<1, 1, 0, st>>>(sqsum, max_norm, pre_scale, coef, norm_out);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_adamw(float* p, void* p16, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
+                  float eps, float wd, float bc1, float bc2, const float* gscale, cudaStream_t st) {
+  if (!n) return;
+  OXI_CHECK((reinterpret_cast<uintptr_t>(p) & 15) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0 &&
+                (reinterpret_cast<uintptr_t>(m) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0 &&
+                (reinterpret_cast<uintptr_t>(p16) & 7) == 0,
+            "AdamW buffers must be 16-byte aligned");
+  const unsigned grid = (unsigned)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)sm_count() * 8);
+  adamw_kernel<<<grid, 256, 0, st>>>(p, reinterpret_cast<__nv_bfloat16*>(p16), g, m, v, n, lr, b1, b2, eps, wd, bc1,
+                                     bc2, gscale);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace oxi

@@ -1,0 +1,214 @@
+"""Checkpoint files in the upstream layout, plus an optimizer sidecar.
+
+Files in ``checkpoint_dir`` (trainer.rs:465-551, config.rs:390-470, 646-686):
+
+* ``{prefix}_step_{N}.safetensors``  weights, upstream tensor names, model dtype
+* ``checkpoint_step_{N}.meta.json``   step/timestamp/config hash/data hash/file/dtype
+* ``{prefix}_final.safetensors``     final weights, no meta
+* ``config.json``                    inference config, written once
+* ``{prefix}_step_{N}.optim.safetensors``  (new) f32 master weights, AdamW
+  moments, step, data cursor; upstream ignores it, and a checkpoint without it
+  resumes like upstream (fresh moments)
+
+``prefix = {name}_{max_seq_len}_{params}_{dtype}`` (config.rs:126-134).
+"""
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import re
+from typing import Dict, Optional, Tuple
+
+import torch
+from safetensors.torch import load_file, save_file
+
+from .config import ModelConfig, blazr_config_json, serde_json_dumps
+from .utils.hashing import compute_file_hash, compute_model_config_hash
+
+_STEP_RE = re.compile(r"_step_(\d+)\.safetensors$")
+
+
+def _cpu_contig(sd: Dict[str, torch.Tensor]) -> Dict[str, torch.Tensor]:
+    return {k: v.detach().to("cpu").contiguous().clone() for k, v in sd.items()}
+
+
+class CheckpointMeta:
+    FIELDS = ("step", "timestamp", "model_config_hash", "data_file_path", "data_file_hash", "checkpoint_file",
+              "dtype")
+
+    def __init__(self, step, timestamp, model_config_hash, data_file_path, data_file_hash, checkpoint_file,
+                 dtype="f32"):
+        self.step = int(step)
+        self.timestamp = timestamp
+        self.model_config_hash = model_config_hash
+        self.data_file_path = data_file_path
+        self.data_file_hash = data_file_hash
+        self.checkpoint_file = checkpoint_file
+        self.dtype = dtype
+
+    @staticmethod
+    def new(step: int, model_cfg: ModelConfig, data_file_path: str, checkpoint_file: str) -> "CheckpointMeta":
+        ts = datetime.datetime.now().strftime("%Y-%m-%d %H:%M:%S")
+        return CheckpointMeta(step, ts, compute_model_config_hash(model_cfg), data_file_path,
+                              compute_file_hash(data_file_path), checkpoint_file, model_cfg.dtype)
+
+    def to_json(self) -> str:
+        return serde_json_dumps({k: getattr(self, k) for k in self.FIELDS}, pretty=True)
+
+    def save(self, checkpoint_dir: str) -> str:
+        path = os.path.join(checkpoint_dir, f"checkpoint_step_{self.step}.meta.json")
+        with open(path, "w") as fh:
+            fh.write(self.to_json())
+        return path
+
+    @staticmethod
+    def load(path: str) -> "CheckpointMeta":
+        with open(path) as fh:
+            d = json.load(fh)
+        missing = [k for k in CheckpointMeta.FIELDS[:-1] if k not in d]
+        if missing:
+            raise ValueError(f"meta file {path} missing fields {missing}")
+        return CheckpointMeta(**{k: d.get(k, "f32") for k in CheckpointMeta.FIELDS})
+
+    def validate(self, model_cfg: ModelConfig, data_file_path: str) -> dict:
+        cur_m = compute_model_config_hash(model_cfg)
+        cur_d = compute_file_hash(data_file_path)
+        v = {
+            "model_matches": self.model_config_hash == cur_m,
+            "data_matches": self.data_file_hash == cur_d,
+            "dtype_matches": self.dtype == model_cfg.dtype,
+            "checkpoint_model_hash": self.model_config_hash, "current_model_hash": cur_m,
+            "checkpoint_data_hash": self.data_file_hash, "current_data_hash": cur_d,
+            "checkpoint_dtype": self.dtype, "current_dtype": model_cfg.dtype,
+        }
+        v["is_valid"] = v["model_matches"] and v["data_matches"]  # dtype may differ
+        return v
+
+
+def find_latest_checkpoint(checkpoint_dir: str) -> Optional[Tuple[str, str, int]]:
+    """Highest ``*_step_N.safetensors`` that has a ``checkpoint_step_N.meta.json``."""
+    if not os.path.isdir(checkpoint_dir):
+        return None
+    best = None
+    for fn in os.listdir(checkpoint_dir):
+        if "_step_" not in fn or not fn.endswith(".safetensors") or fn.endswith(".optim.safetensors"):
+            continue
+        m = _STEP_RE.search(fn)
+        if not m:
+            continue
+        step = int(m.group(1))
+        meta = os.path.join(checkpoint_dir, f"checkpoint_step_{step}.meta.json")
+        if os.path.exists(meta) and (best is None or step > best[2]):
+            best = (os.path.join(checkpoint_dir, fn), meta, step)
+    return best
+
+
+def step_from_filename(path: str) -> int:
+    stem = os.path.basename(path)
+    if stem.endswith(".safetensors"):
+        stem = stem[: -len(".safetensors")]
+    if "_step_" in stem:
+        try:
+            return int(stem.split("_step_")[-1])
+        except ValueError:
+            return 0
+    return 0
+
+
+def save_blazr_config_if_needed(checkpoint_dir: str, model_cfg: ModelConfig) -> bool:
+    os.makedirs(checkpoint_dir, exist_ok=True)
+    path = os.path.join(checkpoint_dir, "config.json")
+    if os.path.exists(path):
+        return False
+    with open(path, "w") as fh:
+        fh.write(blazr_config_json(model_cfg))
+    return True
+
+
+def save_weights(model, path: str) -> None:
+    save_file(_cpu_contig(model.export_ref()), path)
+
+
+def load_weights(model, path: str) -> None:
+    sd = load_file(path)
+    model.import_ref(sd)
+
+
+def optim_sidecar_path(weights_path: str) -> str:
+    assert weights_path.endswith(".safetensors")
+    return weights_path[: -len(".safetensors")] + ".optim.safetensors"
+
+
+def save_checkpoint(model, optimizer, step: int, model_cfg: ModelConfig, checkpoint_dir: str,
+                    data_file_path: Optional[str], max_checkpoints: int, extra: Optional[dict] = None) -> str:
+    """trainer.rs:465-493 (+ sidecar).  Returns the weights path."""
+    os.makedirs(checkpoint_dir, exist_ok=True)
+    prefix = model_cfg.checkpoint_prefix()
+    path = os.path.join(checkpoint_dir, f"{prefix}_step_{step}.safetensors")
+    save_weights(model, path)
+    if optimizer is not None:
+        st = {k: v for k, v in optimizer.state_tensors().items()}
+        meta = {"step": str(optimizer.step_count), "format": "oxidizr_b200.flat_adamw.v1"}
+        if extra:
+            meta.update({k: str(v) for k, v in extra.items()})
+        save_file(_cpu_contig(st), optim_sidecar_path(path), metadata=meta)
+    if data_file_path:
+        try:
+            CheckpointMeta.new(step, model_cfg, data_file_path, path).save(checkpoint_dir)
+        except OSError as e:
+            print(f"Warning: Failed to save checkpoint metadata: {e}")
+    if max_checkpoints > 0:
+        cleanup_old_checkpoints(checkpoint_dir, max_checkpoints)
+    return path
+
+
+def cleanup_old_checkpoints(checkpoint_dir: str, max_checkpoints: int) -> None:
+    """Keep the newest ``max_checkpoints`` step files (trainer.rs:496-541)."""
+    found = []
+    for fn in os.listdir(checkpoint_dir):
+        if "_step_" in fn and fn.endswith(".safetensors") and not fn.endswith(".optim.safetensors"):
+            m = _STEP_RE.search(fn)
+            if m:
+                found.append((int(m.group(1)), os.path.join(checkpoint_dir, fn)))
+    found.sort()
+    for step, path in found[: max(0, len(found) - max_checkpoints)]:
+        for p in (path, optim_sidecar_path(path), os.path.join(checkpoint_dir, f"checkpoint_step_{step}.meta.json")):
+            try:
+                os.remove(p)
+            except FileNotFoundError:
+                pass
+
+
+def save_final(model, model_cfg: ModelConfig, checkpoint_dir: str, name: str = "final") -> str:
+    os.makedirs(checkpoint_dir, exist_ok=True)
+    path = os.path.join(checkpoint_dir, f"{model_cfg.checkpoint_prefix()}_{name}.safetensors")
+    save_weights(model, path)
+    return path
+
+
+def load_optimizer_sidecar(optimizer, weights_path: str) -> Optional[dict]:
+    sp = optim_sidecar_path(weights_path)
+    if optimizer is None or not os.path.exists(sp):
+        return None
+    from safetensors import safe_open
+    with safe_open(sp, framework="pt") as fh:
+        meta = dict(fh.metadata() or {})
+        tens = {k: fh.get_tensor(k) for k in fh.keys()}
+    optimizer.load_state_tensors(tens, int(meta.get("step", "0")))
+    return meta
+
+
+def clear_checkpoint_directory(checkpoint_dir: str) -> int:
+    """commands/train.rs:90-136 (without the prompt)."""
+    n = 0
+    if not os.path.isdir(checkpoint_dir):
+        return 0
+    for fn in os.listdir(checkpoint_dir):
+        if fn.endswith(".safetensors") or fn.endswith(".meta.json") or fn == "config.json":
+            try:
+                os.remove(os.path.join(checkpoint_dir, fn))
+                n += 1
+            except OSError as e:
+                print(f"Warning: Failed to remove {fn}: {e}")
+    return n

@@ -1,0 +1,143 @@
+"""Fine-grained mixture of experts (model.rs:461-752), computed sparsely.
+
+Router ``Linear(H, E)`` without bias; routing probabilities are the softmax of
+the router logits; each token picks its top-k experts by logit and weights
+them with the softmax over those k logits (model.rs:541-556).  Shared experts
+are always on (model.rs:574-576).  Upstream runs every expert densely on every
+token and weighs the outputs with a dense [T, E] matrix; running each expert
+only on its routed tokens gives the same output for the same routing.
+
+Auxiliary load-balancing loss:
+* ``mean_sq`` (default, upstream formula model.rs:585-590):
+  ``mean_e((mean_t p_te)^2)`` -- differentiable here (upstream detaches it);
+* ``switch``: ``E * sum_e f_e * P_e`` with f_e the routed-token fraction.
+
+Expert weights are stored stacked ([E, 2I, H] gate|up interleaved, [E, H, I])
+so a grouped GEMM can address them; ``export_ref`` writes the upstream
+per-expert names ``experts.{e}.{gate,up,down}_proj.weight``.  Several shared
+experts are one SwiGLU of width ``num_shared_experts * I`` (the sum of SwiGLU
+experts equals one SwiGLU over the concatenated intermediate dimension).
+
+With expert parallelism (``ep_group`` set) each rank holds E/ep experts and the
+token dispatch/combine goes through :mod:`oxidizr_b200.parallel.ep`.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ..ops import api
+from .attention import SwiGLU
+from .common import RefModule, _assign, interleave_gu, normal_, split_gu, take
+
+
+def route(logits: torch.Tensor, k: int):
+    """Top-k routing: returns (probs [T,E] f32, top_idx [T,k] int64, top_w [T,k] f32)."""
+    lf = logits.float()
+    probs = torch.softmax(lf, -1)
+    topv, topi = torch.topk(lf, k, dim=-1)
+    topw = torch.softmax(topv, -1)
+    return probs, topi, topw
+
+
+def aux_loss(probs: torch.Tensor, topi: torch.Tensor, E: int, kind: str = "mean_sq") -> torch.Tensor:
+    if kind == "switch":
+        f = torch.bincount(topi.reshape(-1), minlength=E).float() / topi.numel()
+        return E * (f.detach() * probs.mean(0)).sum()
+    usage = probs.mean(0)
+    return usage.pow(2).mean()
+
+
+class MoE(RefModule):
+    def __init__(self, cfg, device=None, dtype=None, ep_group=None):
+        super().__init__()
+        H = cfg.hidden_size
+        self.E = cfg.num_experts
+        self.k = cfg.experts_per_tok
+        self.I = cfg.intermediate_size
+        self.H = H
+        self.aux_kind = cfg.moe_aux_loss or "mean_sq"
+        self.ep_group = ep_group
+        if ep_group is not None:
+            import torch.distributed as dist
+            self.ep_size = dist.get_world_size(ep_group)
+            self.ep_rank = dist.get_rank(ep_group)
+        else:
+            self.ep_size, self.ep_rank = 1, 0
+        assert self.E % self.ep_size == 0, "num_experts must be divisible by the expert-parallel size"
+        self.E_local = self.E // self.ep_size
+        self.router = nn.Parameter(torch.empty(self.E, H, device=device, dtype=dtype))
+        self.w_gu = nn.Parameter(torch.empty(self.E_local, 2 * self.I, H, device=device, dtype=dtype))
+        self.w_down = nn.Parameter(torch.empty(self.E_local, H, self.I, device=device, dtype=dtype))
+        self.n_shared = cfg.n_shared_experts
+        self.shared = SwiGLU(H, self.n_shared * self.I, device, dtype) if self.n_shared > 0 else None
+        # expert parameters are not data-parallel-replicated under EP
+        self.w_gu._oxi_expert = True
+        self.w_down._oxi_expert = True
+
+    def reset_parameters(self, std, gen=None):
+        normal_(self.router, std, gen)
+        normal_(self.w_gu, std, gen)
+        normal_(self.w_down, std, gen)
+        if self.shared is not None:
+            self.shared.reset_parameters(std, gen)
+
+    # ------------------------------------------------------------ compute
+    def _experts_local(self, xs: torch.Tensor, counts) -> torch.Tensor:
+        """Run local expert e on rows [off_e, off_e + counts[e]) of xs."""
+        ys = torch.empty_like(xs)
+        off = 0
+        for e, c in enumerate(counts):
+            if c:
+                ys[off:off + c] = api.swiglu_mlp(xs[off:off + c], self.w_gu[e], self.w_down[e])
+            off += c
+        return ys
+
+    def forward(self, h: torch.Tensor, resid: torch.Tensor):
+        B, S, H = h.shape
+        x = h.reshape(-1, H)
+        logits = api.linear(x, self.router)
+        probs, topi, topw = route(logits, self.k)
+        aux = aux_loss(probs, topi, self.E, self.aux_kind)
+        if self.ep_size > 1:
+            from ..parallel.ep import ep_moe
+            y = ep_moe(self, x, topi, topw)
+        else:
+            flat_e = topi.reshape(-1)
+            order = torch.argsort(flat_e, stable=True)
+            tok = order // self.k
+            counts = torch.bincount(flat_e, minlength=self.E).tolist()
+            xs = x.index_select(0, tok)
+            ys = self._experts_local(xs, counts)
+            wts = topw.reshape(-1).index_select(0, order).to(ys.dtype)
+            y = torch.zeros_like(x).index_add_(0, tok, ys * wts[:, None])
+        y = y.view(B, S, H)
+        if self.shared is not None:
+            return self.shared(h, resid + y), aux
+        return resid + y, aux
+
+    # ------------------------------------------------------------ names
+    def export_ref(self, prefix, out):
+        out[prefix + "router.gate.weight"] = self.router.detach()
+        base = self.ep_rank * self.E_local
+        for e in range(self.E_local):
+            g, u = split_gu(self.w_gu.detach()[e])
+            p = f"{prefix}experts.{base + e}."
+            out[p + "gate_proj.weight"] = g
+            out[p + "up_proj.weight"] = u
+            out[p + "down_proj.weight"] = self.w_down.detach()[e]
+        if self.shared is not None:
+            self.shared.export_ref(prefix + "shared_expert.", out)
+
+    def import_ref(self, prefix, sd):
+        _assign(self.router, sd, prefix + "router.gate.weight")
+        base = self.ep_rank * self.E_local
+        with torch.no_grad():
+            for e in range(self.E_local):
+                p = f"{prefix}experts.{base + e}."
+                w = interleave_gu(take(sd, p + "gate_proj.weight"), take(sd, p + "up_proj.weight"))
+                self.w_gu[e].copy_(w.to(self.w_gu.dtype))
+                self.w_down[e].copy_(take(sd, p + "down_proj.weight").to(self.w_down.dtype))
+        if self.shared is not None:
+            self.shared.import_ref(prefix + "shared_expert.", sd)

@@ -20,9 +20,14 @@ ERRORS = {
 }
 
 
-def ext():
+def raw_ext():
     """The extension module; raises if it cannot be built/loaded."""
     return _ext.load(required=True)
+
+
+def ext():
+    """The extension module (behind the launch-counting proxy)."""
+    return counted_ext()
 
 
 def status(device) -> torch.Tensor:
@@ -47,3 +52,46 @@ def check_status(device) -> None:
     v = read_status(device)
     if v:
         raise RuntimeError(f"oxidizr kernel status {v}: {ERRORS.get(v, 'unknown error')}")
+
+
+class _Counter:
+    """Counts calls into the kernel library (each call launches one kernel,
+    except a handful that launch two; see ``LAUNCHES_PER_CALL``)."""
+
+    LAUNCHES_PER_CALL = {"gemm_ce": 1, "adamw": 1}
+
+    def __init__(self):
+        self.enabled = False
+        self.count = 0
+
+    def wrap(self, mod):
+        counter = self
+
+        class _Proxy:
+            def __getattr__(self, name):
+                fn = getattr(mod, name)
+                if not callable(fn):
+                    return fn
+
+                def call(*a, **k):
+                    if counter.enabled:
+                        counter.count += counter.LAUNCHES_PER_CALL.get(name, 1)
+                    return fn(*a, **k)
+                return call
+
+            def __dir__(self):
+                return dir(mod)
+
+        return _Proxy()
+
+
+launch_counter = _Counter()
+_PROXY = None
+
+
+def counted_ext():
+    """The extension behind a proxy that counts kernel launches while enabled."""
+    global _PROXY
+    if _PROXY is None:
+        _PROXY = launch_counter.wrap(raw_ext())
+    return _PROXY

@@ -1,0 +1,108 @@
+"""Device-dispatching op API used by the models.
+
+bf16 CUDA tensors run the sm_100a kernels (``ops.fused`` and friends); CPU
+tensors (and non-bf16 CUDA tensors, e.g. an f32 model moved to the GPU) run
+the PyTorch statement of the same math from ``ops.reference`` under autograd.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as R
+
+
+def _native(t: torch.Tensor) -> bool:
+    return t.is_cuda and t.dtype == torch.bfloat16
+
+
+def embedding(ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    if _native(w):
+        from .fused import Embedding
+        return Embedding.apply(ids, w)
+    return F.embedding(ids, w)
+
+
+def rmsnorm(x, w, eps: float = 1e-5):
+    if _native(x):
+        from .fused import Norm
+        return Norm.apply(x, None, w, None, 0, eps)
+    return R.rmsnorm(x, w, eps)
+
+
+def layernorm(x, w, b, eps: float = 1e-6):
+    if _native(x):
+        from .fused import Norm
+        return Norm.apply(x, None, w, b, 1, eps)
+    return R.layernorm(x, w, b, eps)
+
+
+def gated_rmsnorm(y, gate, w, eps: float = 1e-6):
+    if _native(y):
+        from .fused import Norm
+        return Norm.apply(y, gate, w, None, 2, eps)
+    return R.gated_rmsnorm(y, gate, w, eps)
+
+
+def linear(x, w, bias=None, resid=None):
+    if _native(x):
+        from .fused import Linear
+        return Linear.apply(x, w, bias, resid)
+    y = F.linear(x, w.to(x.dtype), None if bias is None else bias.to(x.dtype))
+    return y if resid is None else resid + y
+
+
+def qkv_rope(x, w_qkv, cos, sin, hd: int, q_cols: int, k_cols: int):
+    """x W_qkv^T with rotate-half RoPE applied to the q and k heads.
+    cos/sin are [S, hd/2] f32 tables; token rows are [B*S] in sequence order."""
+    if _native(x) and hd in (64, 128):
+        from .fused import LinearRope
+        return LinearRope.apply(x, w_qkv, cos, sin, hd, q_cols, k_cols)
+    y = F.linear(x, w_qkv.to(x.dtype))
+    B, S = x.shape[0], x.shape[1]
+    q = y[..., :q_cols].reshape(B, S, -1, hd).transpose(1, 2)
+    k = y[..., q_cols:q_cols + k_cols].reshape(B, S, -1, hd).transpose(1, 2)
+    q = R.apply_rope(q, cos[:S], sin[:S]).transpose(1, 2).reshape(B, S, q_cols)
+    k = R.apply_rope(k, cos[:S], sin[:S]).transpose(1, 2).reshape(B, S, k_cols)
+    return torch.cat([q, k, y[..., q_cols + k_cols:]], -1)
+
+
+def swiglu_mlp(x, w_gu, w_down, resid=None):
+    """resid + down(silu(gate x) * up x); w_gu rows interleaved [g 128 | u 128]..."""
+    I = w_gu.shape[0] // 2
+    if _native(x) and I % 128 == 0:
+        from .fused import SwiGLUMLP
+        return SwiGLUMLP.apply(x, w_gu, w_down, resid)
+    gu = F.linear(x, w_gu.to(x.dtype))
+    nb = I // 128 if I % 128 == 0 else None
+    if nb:
+        gu = gu.reshape(*gu.shape[:-1], nb, 2, 128)
+        g, u = gu[..., 0, :].reshape(*x.shape[:-1], I), gu[..., 1, :].reshape(*x.shape[:-1], I)
+    else:
+        g, u = gu[..., :I], gu[..., I:]
+    y = F.linear(F.silu(g) * u, w_down.to(x.dtype))
+    return y if resid is None else resid + y
+
+
+def attention(q, k, v, scale: float, causal: bool = True):
+    from .attention import attention as _att
+    return _att(q, k, v, scale, causal)
+
+
+def linear_cross_entropy(x, w, targets, ignore_index: int = -100):
+    if _native(x):
+        from .fused import LinearCrossEntropy
+        return LinearCrossEntropy.apply(x, w, targets, ignore_index)
+    logits = F.linear(x, w.to(x.dtype))
+    return F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), targets.reshape(-1).long(),
+                           ignore_index=ignore_index)
+
+
+def causal_conv1d(x, w, b, act: bool = True):
+    """x [B, S, C] channels-last; w [C, 1, k]; b [C]."""
+    if _native(x):
+        from .ssm import causal_conv1d_cuda
+        return causal_conv1d_cuda(x, w, b, act)
+    return R.causal_conv1d(x, w, b, act)

@@ -1,0 +1,244 @@
+"""Autograd functions over the sm_100a kernels (CUDA, bf16 activations).
+
+Weight gradients: when a parameter carries a ``main_grad`` attribute (a view
+into the flat f32 gradient buffer of :mod:`oxidizr_b200.optim`), backward
+accumulates its gradient there with a fused GEMM epilogue (``C += A B^T``) or
+an atomic scatter, then calls ``param._oxi_grad_ready()`` if present (the DDP
+bucket hook), and returns ``None`` to autograd.  Without ``main_grad`` the
+gradient is returned normally.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from ._C import ext, status
+from .gemm import mm
+
+
+def _ready(p):
+    cb = getattr(p, "_oxi_grad_ready", None)
+    if cb is not None:
+        cb()
+
+
+def _wgrad_gemm(p: torch.nn.Parameter, dy2: torch.Tensor, x2: torch.Tensor):
+    """dW = dy^T @ x ([N, K]) accumulated into p.main_grad, else returned."""
+    mg = getattr(p, "main_grad", None)
+    if mg is not None:
+        mm(dy2, x2, a_t=True, b_t=True, out=mg.view(dy2.shape[1], x2.shape[1]), beta=1.0)
+        _ready(p)
+        return None
+    g = mm(dy2, x2, a_t=True, b_t=True, out_dtype=torch.float32)
+    return g.to(p.dtype)
+
+
+def _vec_grad(p: torch.nn.Parameter, g32: torch.Tensor):
+    mg = getattr(p, "main_grad", None)
+    if mg is not None:
+        mg.view(-1).add_(g32.view(-1))
+        _ready(p)
+        return None
+    return g32.to(p.dtype).view(p.shape)
+
+
+def _c(t: torch.Tensor) -> torch.Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------- embedding
+class Embedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, w):
+        ids_f = _c(ids.reshape(-1))
+        out = torch.empty(ids_f.numel(), w.shape[1], dtype=w.dtype, device=w.device)
+        ext().embed_fwd(ids_f, w, out)
+        ctx.save_for_backward(ids_f)
+        ctx.w = w
+        return out.view(*ids.shape, w.shape[1])
+
+    @staticmethod
+    def backward(ctx, dy):
+        (ids,) = ctx.saved_tensors
+        w = ctx.w
+        dy = _c(dy.reshape(-1, w.shape[1]))
+        mg = getattr(w, "main_grad", None)
+        if mg is not None:
+            ext().embed_bwd(ids, dy, mg.view(w.shape))
+            _ready(w)
+            return None, None
+        g = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        ext().embed_bwd(ids, dy, g)
+        return None, g.to(w.dtype)
+
+
+# ------------------------------------------------------------------- norms
+class Norm(torch.autograd.Function):
+    """mode 0 RMSNorm(x)*w, 1 LayerNorm(x)*w+b, 2 RMSNorm(x*silu(gate))*w."""
+
+    @staticmethod
+    def forward(ctx, x, gate, w, b, mode: int, eps: float):
+        xc = _c(x)
+        H = x.shape[-1]
+        rows = xc.numel() // H
+        y = torch.empty_like(xc)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        mean = torch.empty(rows, dtype=torch.float32, device=x.device) if mode == 1 else None
+        gc = _c(gate) if gate is not None else None
+        ext().norm_fwd(mode, xc, gc, w, b, y, rstd, mean, eps)
+        ctx.save_for_backward(xc, gc, rstd, mean)
+        ctx.w, ctx.b, ctx.mode = w, b, mode
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        xc, gc, rstd, mean = ctx.saved_tensors
+        w, b, mode = ctx.w, ctx.b, ctx.mode
+        H = xc.shape[-1]
+        dyc = _c(dy)
+        dx = torch.empty_like(xc)
+        dgate = torch.empty_like(gc) if mode == 2 else None
+        dw = torch.zeros(H, dtype=torch.float32, device=xc.device)
+        db = torch.zeros(H, dtype=torch.float32, device=xc.device) if mode == 1 else None
+        ext().norm_bwd(mode, dyc, xc, gc, w, rstd, mean, None, dx, dgate, dw, db)
+        gw = _vec_grad(w, dw)
+        gb = _vec_grad(b, db) if mode == 1 else None
+        return dx, dgate, gw, gb, None, None
+
+
+# ----------------------------------------------------------------- linears
+class Linear(torch.autograd.Function):
+    """y = x W^T (+ bias) (+ resid).  x [..., K], W [N, K]."""
+
+    @staticmethod
+    def forward(ctx, x, w, bias, resid):
+        K = x.shape[-1]
+        x2 = _c(x.reshape(-1, K))
+        r2 = _c(resid.reshape(-1, w.shape[0])) if resid is not None else None
+        y = mm(x2, w, resid=r2)
+        if bias is not None:
+            y.add_(bias.to(y.dtype))
+        ctx.save_for_backward(x2)
+        ctx.w, ctx.has_bias, ctx.has_resid, ctx.bias = w, bias is not None, resid is not None, bias
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x2,) = ctx.saved_tensors
+        w = ctx.w
+        dy2 = _c(dy.reshape(-1, w.shape[0]))
+        dx = mm(dy2, w, b_t=True).view(*dy.shape[:-1], w.shape[1]) if ctx.needs_input_grad[0] else None
+        gw = _wgrad_gemm(w, dy2, x2)
+        gb = _vec_grad(ctx.bias, dy2.float().sum(0)) if ctx.has_bias else None
+        dres = dy if ctx.has_resid else None
+        return dx, gw, gb, dres
+
+
+class LinearRope(torch.autograd.Function):
+    """qkv = rope(x W^T) with RoPE on the first q_cols + k_cols columns."""
+
+    @staticmethod
+    def forward(ctx, x, w, cos, sin, hd: int, q_cols: int, k_cols: int):
+        K = x.shape[-1]
+        x2 = _c(x.reshape(-1, K))
+        out = torch.empty(x2.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+        ext().gemm_rope(x2, w, out, cos, sin, hd, q_cols, k_cols, status(x.device))
+        ctx.save_for_backward(x2, cos, sin)
+        ctx.w, ctx.hd, ctx.rot = w, hd, q_cols + k_cols
+        return out.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, cos, sin = ctx.saved_tensors
+        w = ctx.w
+        dy2 = dy.reshape(-1, w.shape[0]).contiguous().clone()
+        ext().rope_bwd(dy2, ctx.rot, ctx.hd, cos, sin)
+        dx = mm(dy2, w, b_t=True).view(*dy.shape[:-1], w.shape[1])
+        gw = _wgrad_gemm(w, dy2, x2)
+        return dx, gw, None, None, None, None, None
+
+
+class SwiGLUMLP(torch.autograd.Function):
+    """y = resid + (silu(x Wg^T) * (x Wu^T)) Wd^T with W_gu interleaved in 128-row blocks."""
+
+    @staticmethod
+    def forward(ctx, x, w_gu, w_down, resid):
+        K = x.shape[-1]
+        x2 = _c(x.reshape(-1, K))
+        M = x2.shape[0]
+        I = w_gu.shape[0] // 2
+        h = torch.empty(M, I, dtype=x.dtype, device=x.device)
+        gu = torch.empty(M, 2 * I, dtype=x.dtype, device=x.device)
+        ext().gemm_swiglu(x2, w_gu, h, gu, status(x.device))
+        r2 = _c(resid.reshape(-1, w_down.shape[0])) if resid is not None else None
+        y = mm(h, w_down, resid=r2)
+        ctx.save_for_backward(x2, h, gu)
+        ctx.w_gu, ctx.w_down, ctx.has_resid = w_gu, w_down, resid is not None
+        return y.view(*x.shape[:-1], w_down.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, h, gu = ctx.saved_tensors
+        w_gu, w_down = ctx.w_gu, ctx.w_down
+        dy2 = _c(dy.reshape(-1, w_down.shape[0]))
+        g_down = _wgrad_gemm(w_down, dy2, h)
+        dgu = torch.empty_like(gu)
+        ext().gemm_swiglu_bwd(dy2, w_down, gu, dgu, status(dy.device))
+        g_gu = _wgrad_gemm(w_gu, dgu, x2)
+        dx = mm(dgu, w_gu, b_t=True).view(*dy.shape[:-1], w_gu.shape[1])
+        return dx, g_gu, g_down, (dy if ctx.has_resid else None)
+
+
+# ------------------------------------------------------------- LM head + CE
+class LinearCrossEntropy(torch.autograd.Function):
+    """Mean token cross-entropy of logits = x W^T without a separate softmax pass.
+
+    Forward: one GEMM whose epilogue writes the bf16 logits plus per-(row,
+    256-column tile) max and sum-of-exp partials and the target logit; a small
+    kernel combines the partials into log-sum-exp and per-row loss.
+    Backward: softmax-minus-one-hot in place on the saved logits, then the dX
+    and dW GEMMs read it directly.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w, targets, ignore_index: int = -100):
+        K = x.shape[-1]
+        x2 = _c(x.reshape(-1, K))
+        M, V = x2.shape[0], w.shape[0]
+        tg = _c(targets.reshape(-1)).long()
+        if ignore_index != -1:
+            tg = torch.where(tg == ignore_index, torch.full_like(tg, -1), tg)
+        nt = (V + 255) // 256
+        ldl = (V + 7) // 8 * 8
+        logits = torch.empty(M, ldl, dtype=x.dtype, device=x.device)
+        pm = torch.empty(M, nt, dtype=torch.float32, device=x.device)
+        ps = torch.empty_like(pm)
+        tl = torch.zeros(M, dtype=torch.float32, device=x.device)
+        ext().gemm_ce(x2, w, tg, pm, ps, tl, logits, 1.0, status(x.device))
+        lse = torch.empty(M, dtype=torch.float32, device=x.device)
+        loss = torch.empty(M, dtype=torch.float32, device=x.device)
+        ext().ce_finish(pm, ps, tl, tg, lse, loss)
+        count = (tg >= 0).sum().clamp_min(1)
+        ctx.save_for_backward(x2, logits, lse, tg, count)
+        ctx.w, ctx.V, ctx.xshape = w, V, x.shape
+        return loss.sum() / count
+
+    @staticmethod
+    def backward(ctx, dloss):
+        x2, logits, lse, tg, count = ctx.saved_tensors
+        w, V = ctx.w, ctx.V
+        gscale = (dloss.float() / count.float()).reshape(1).contiguous()
+        ext().ce_bwd(logits, V, lse, tg, gscale, 1.0)
+        dl = logits[:, :V]
+        dx = mm(dl, w, b_t=True)
+        gw = _wgrad_gemm(w, dl, x2)
+        return dx.view(ctx.xshape), gw, None, None
+
+
+# -------------------------------------------------------------- attention
+def flash_attention(q, k, v, scale: float, causal: bool = True):
+    """q [B, S, Hq, D], k/v [B, S, Hk, D] -> [B, S, Hq, D]."""
+    from .attention import attention_cuda
+    return attention_cuda(q, k, v, scale, causal)

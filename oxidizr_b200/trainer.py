@@ -1,0 +1,201 @@
+"""Training loop (trainer.rs): gradient accumulation, loss = CE + alpha * aux,
+optimizer step, headless JSON / interactive logging, periodic and final
+checkpoints.
+
+Differences from upstream, by design (upstream behaviour in brackets):
+* true gradient accumulation, one optimizer step per ``gradient_accumulation``
+  micro-batches [upstream steps inside the accumulation loop, trainer.rs:237,245];
+* true global-norm clipping at ``max_grad_norm`` (default 1.0) on the device
+  [upstream pre-scales the next step's loss by the previous norm, trainer.rs:131-141];
+* the MoE auxiliary loss is differentiable [detached, model.rs:589-590];
+* no host synchronisation inside a step: the loss and grad norm are read only
+  when a log line is printed.
+
+Headless line (trainer.rs:336-337)::
+
+  {"step": 1, "loss": 11.5161, "grad_norm": 0.2542, "learning_rate": 3.000000e-4, "epoch": 0.00, "it/s": 3.24, "vram": "0"}
+
+Interactive mode appends ``{"epoch":..,"grad_norm":..,"learning_rate":..,"loss":..,"step":..}``
+(alphabetical keys, serde_json's default map) to ``runs/<ts>/steps.json``.
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+import time
+from collections import deque
+from typing import Callable, Optional
+
+import torch
+
+from .checkpoint import save_blazr_config_if_needed, save_checkpoint, save_final
+from .config import LitConfig, serde_json_dumps
+
+
+def rust_exp(x: float, prec: int = 6) -> str:
+    """Rust ``{:.6e}``: mantissa with ``prec`` decimals, exponent without sign padding."""
+    s = f"{x:.{prec}e}"
+    mant, exp = s.split("e")
+    return f"{mant}e{int(exp)}"
+
+
+def format_duration(secs: float) -> str:
+    t = int(round(secs))
+    d, h, m, s = t // 86400, (t % 86400) // 3600, (t % 3600) // 60, t % 60
+    if d:
+        return f"{d}d{h:02d}h"
+    if h:
+        return f"{h}h{m:02d}m"
+    if m:
+        return f"{m}m{s:02d}s"
+    return f"{s}s"
+
+
+def vram_string(device) -> str:
+    if torch.device(device).type != "cuda":
+        return "0"
+    try:
+        return str(int(torch.cuda.memory_reserved(device) / (1024 * 1024)))
+    except Exception:
+        return "0"
+
+
+class NonFiniteLoss(RuntimeError):
+    pass
+
+
+class Trainer:
+    def __init__(self, cfg: LitConfig, model, optimizer, loader, *, device, headless: bool = True,
+                 steps_json_path: Optional[str] = None, start_step: int = 0, data_file_path: Optional[str] = None,
+                 rank: int = 0, world_size: int = 1, dataset_size: Optional[int] = None,
+                 out: Callable[[str], None] = print, on_checkpoint: Optional[Callable] = None):
+        self.cfg = cfg
+        self.tc = cfg.trainer
+        self.model = model
+        self.opt = optimizer
+        self.loader = loader
+        self.device = torch.device(device)
+        self.headless = headless
+        self.steps_json_path = steps_json_path
+        self.global_step = start_step
+        self.start_step = start_step
+        self.data_file_path = data_file_path
+        self.rank, self.world_size = rank, world_size
+        self.out = out
+        self.batch_size = loader.batch_size
+        self.seq_len = loader.seq_len
+        self.dataset_size = dataset_size if dataset_size is not None else loader.dataset_size()
+        tps = self.batch_size * self.seq_len * self.tc.gradient_accumulation * world_size
+        self.steps_per_epoch = max(1, (self.dataset_size + tps - 1) // tps)
+        self.total_steps = self.steps_per_epoch * self.tc.num_epochs
+        self.on_checkpoint = on_checkpoint
+        self.last_loss = None
+        self.last_grad_norm = None
+
+    @property
+    def effective_steps(self) -> int:
+        if self.tc.max_steps == 0:
+            return self.total_steps
+        return min(self.tc.max_steps, self.total_steps)
+
+    # ------------------------------------------------------------ one step
+    def training_step(self):
+        """Returns (mean CE loss, grad norm) as device scalars."""
+        accum = self.tc.gradient_accumulation
+        alpha = float(self.tc.load_balance_alpha)
+        total_ce = torch.zeros((), dtype=torch.float32, device=self.device)
+        for micro in range(accum):
+            if hasattr(self.opt, "accumulating"):
+                self.opt.accumulating = micro < accum - 1
+            x, y = self.loader.next_batch()
+            ce, aux = self.model(x, y)
+            loss = ce.float()
+            if aux:
+                loss = loss + alpha * torch.stack([a.float() for a in aux]).mean()
+            (loss / accum).backward()
+            total_ce = total_ce + ce.detach().float()
+        gnorm = self.opt.step()
+        self.global_step += 1
+        return total_ce / accum, gnorm
+
+    def _check_finite(self, loss: float):
+        if not math.isfinite(loss):
+            raise NonFiniteLoss("NaN loss detected")
+
+    # ------------------------------------------------------------ loops
+    def fit(self):
+        if self.rank == 0:
+            save_blazr_config_if_needed(self.tc.checkpoint_dir, self.cfg.model)
+        if self.headless:
+            self._fit_headless()
+        else:
+            self._fit_normal()
+
+    def _fit_headless(self):
+        t0 = time.perf_counter()
+        for step in range(self.start_step, self.effective_steps):
+            loss_t, gn_t = self.training_step()
+            if step % self.tc.log_interval == 0 or step == 0:
+                loss, gn = float(loss_t), float(gn_t)
+                self._check_finite(loss)
+                self.last_loss, self.last_grad_norm = loss, gn
+                elapsed = time.perf_counter() - t0
+                samples = (step + 1 - self.start_step) * self.batch_size * self.tc.gradient_accumulation
+                its = samples / elapsed if elapsed > 0 else 0.0
+                epoch = (step + 1) / self.steps_per_epoch
+                if self.rank == 0:
+                    self.out('{"step": %d, "loss": %.4f, "grad_norm": %.4f, "learning_rate": %s, "epoch": %.2f, '
+                             '"it/s": %.2f, "vram": "%s"}' % (step + 1, loss, gn, rust_exp(self.tc.learning_rate),
+                                                             epoch, its, vram_string(self.device)))
+        self._final()
+
+    def _fit_normal(self):
+        window = deque(maxlen=5)
+        t_last = time.perf_counter()
+        total = self.effective_steps
+        if self.start_step > 0 and self.rank == 0:
+            self.out(f"Resuming from step {self.start_step}")
+        for step in range(self.start_step, total):
+            loss_t, gn_t = self.training_step()
+            now = time.perf_counter()
+            window.append(now - t_last)
+            t_last = now
+            avg = sum(window) / len(window)
+            its = 1.0 / avg if avg > 0 else 0.0
+            if step % self.tc.log_interval == 0 or step == 0:
+                loss, gn = float(loss_t), float(gn_t)
+                self._check_finite(loss)
+                self.last_loss, self.last_grad_norm = loss, gn
+                epoch = (step + 1) / self.steps_per_epoch
+                if self.rank == 0:
+                    if self.steps_json_path:
+                        line = serde_json_dumps({"epoch": epoch, "grad_norm": gn,
+                                                 "learning_rate": float(self.tc.learning_rate), "loss": loss,
+                                                 "step": step + 1})
+                        with open(self.steps_json_path, "a") as fh:
+                            fh.write(line + "\n")
+                    eta = format_duration(avg * (total - step - 1))
+                    self.out(f"[{step + 1:>7}/{total:<7}] {eta} loss: {loss:.4f} | grad: {gn:.4f} | {its:.2f} it/s")
+            if step > 0 and step % self.tc.save_interval == 0:
+                if self.rank == 0:
+                    self.out(f"Checkpoint saved: step {step}")
+                self.save(step)
+        self._final()
+        if self.rank == 0 and self.last_loss is not None:
+            self.out(f"Training complete | final loss: {self.last_loss:.4f} | grad: {self.last_grad_norm:.4f}")
+
+    # ------------------------------------------------------------ checkpoints
+    def save(self, step: int):
+        if self.on_checkpoint is not None:
+            self.on_checkpoint(step)
+            return
+        if self.rank == 0:
+            save_checkpoint(self.model, self.opt, step, self.cfg.model, self.tc.checkpoint_dir, self.data_file_path,
+                            self.tc.max_checkpoints, extra={"data_cursor": getattr(self.loader, "cursor", 0)})
+
+    def _final(self):
+        if self.rank == 0:
+            prefix = self.cfg.model.checkpoint_prefix()
+            self.out(f"Saving final checkpoint to {self.tc.checkpoint_dir}/{prefix}_final.safetensors")
+            save_final(self.model, self.cfg.model, self.tc.checkpoint_dir)

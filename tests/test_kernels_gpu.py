@@ -1,0 +1,144 @@
+"""Memory-bound kernels (norms, CE, embedding, RoPE bwd, AdamW) and the full
+model on CUDA vs the fp32 PyTorch reference."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-8)).item()
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("H", [256, 2048, 1536, 4096])
+def test_norms_fwd_bwd(mode, H):
+    from oxidizr_b200.ops import reference as R
+    from oxidizr_b200.ops.fused import Norm
+    torch.manual_seed(mode * 7 + H)
+    T = 333
+    x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_()
+    g = torch.randn(T, H, device="cuda").bfloat16().requires_grad_() if mode == 2 else None
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_()
+    b = (0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_() if mode == 1 else None
+    y = Norm.apply(x, g, w, b, mode, 1e-5)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    gr = g.detach().float().requires_grad_() if mode == 2 else None
+    br = b.detach().float().requires_grad_() if mode == 1 else None
+    if mode == 0:
+        yr = R.rmsnorm(xr, wr, 1e-5)
+    elif mode == 1:
+        yr = R.layernorm(xr, wr, br, 1e-5)
+    else:
+        yr = R.gated_rmsnorm(xr, gr, wr, 1e-5)
+    yr.backward(dy.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 2e-2
+    assert _rel(w.grad, wr.grad) < 2e-2
+    if mode == 1:
+        assert _rel(b.grad, br.grad) < 2e-2
+    if mode == 2:
+        assert _rel(g.grad, gr.grad) < 2e-2
+
+
+def test_linear_cross_entropy():
+    from oxidizr_b200.ops.fused import LinearCrossEntropy
+    torch.manual_seed(0)
+    T, H, V = 1000, 512, 5003
+    x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_()
+    w = (torch.randn(V, H, device="cuda") / H ** 0.5).bfloat16().requires_grad_()
+    t = torch.randint(0, V, (T,), device="cuda")
+    t[5] = -100
+    loss = LinearCrossEntropy.apply(x, w, t, -100)
+    loss.backward()
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    lr = torch.nn.functional.cross_entropy(xr @ wr.t(), t, ignore_index=-100)
+    lr.backward()
+    assert abs(loss.item() - lr.item()) < 2e-3 * abs(lr.item())
+    assert _rel(x.grad, xr.grad) < 3e-2
+    assert _rel(w.grad, wr.grad) < 3e-2
+
+
+def test_embedding_and_rope_bwd():
+    from oxidizr_b200.ops._C import ext
+    from oxidizr_b200.ops.fused import Embedding
+    from oxidizr_b200.ops import reference as R
+    torch.manual_seed(1)
+    V, H = 1000, 256
+    w = torch.randn(V, H, device="cuda").bfloat16().requires_grad_()
+    ids = torch.randint(0, V, (4, 50), device="cuda")
+    y = Embedding.apply(ids, w)
+    assert torch.equal(y, w.detach()[ids])
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    ref = torch.zeros(V, H, device="cuda").index_add_(0, ids.reshape(-1), dy.reshape(-1, H).float())
+    assert _rel(w.grad, ref) < 1e-2
+    # rope backward == transpose of the forward rotation
+    S, hd = 64, 128
+    cos, sin = R.rope_tables(hd, S, 10000.0, device="cuda")
+    x = torch.randn(2, S, 3, hd, device="cuda")
+    d = torch.randn(2 * S, 3 * hd, device="cuda").bfloat16()
+    xr = x.requires_grad_()
+    yr = R.apply_rope(xr.transpose(1, 2), cos, sin).transpose(1, 2)
+    yr.backward(d.float().view(2, S, 3, hd))
+    dd = d.clone()
+    ext().rope_bwd(dd, 3 * hd, hd, cos.contiguous(), sin.contiguous())
+    assert _rel(dd.view(2, S, 3, hd), xr.grad) < 1e-2
+
+
+def test_adamw_kernel_matches_reference():
+    from oxidizr_b200.ops._C import ext
+    from oxidizr_b200.ops import reference as R
+    torch.manual_seed(2)
+    n = 10007
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    pr, mr, vr = p.clone(), m.clone(), v.clone()
+    scale = torch.tensor([0.5], device="cuda")
+    for step in (1, 2, 3):
+        ext().adamw(p, p16, g, m, v, 1e-3, 0.9, 0.999, 1e-8, 0.01, 1 - 0.9 ** step, 1 - 0.999 ** step, scale)
+        R.adamw_step(pr, g, mr, vr, step, 1e-3, grad_scale=0.5)
+    assert torch.allclose(p, pr, atol=1e-6, rtol=1e-5)
+    assert torch.equal(p16, p.bfloat16())
+    sq = torch.zeros(1, device="cuda")
+    ext().sqsum(g, sq)
+    assert abs(sq.item() - (g * g).sum().item()) < 1e-3 * (g * g).sum().item()
+
+
+def _small_cfg(**kw):
+    from oxidizr_b200.config import LitConfig
+    m = {"name": "t", "hidden_size": 256, "num_layers": 2, "num_heads": 2, "kv_heads": 1, "intermediate_size": 256,
+         "vocab_size": 1000, "max_seq_len": 64, "rope_theta": 10000.0, "dtype": "bf16"}
+    m.update(kw)
+    return LitConfig.from_dict({"model": m, "trainer": {
+        "learning_rate": 1e-3, "batch_size": 2, "max_steps": 1, "num_epochs": 1, "gradient_accumulation": 1,
+        "checkpoint_dir": "/tmp/x", "log_interval": 1, "save_interval": 10, "load_balance_alpha": 0.0,
+        "group_size": 4, "beta_kl": 0.04}})
+
+
+@pytest.mark.parametrize("hd_heads", [(256, 2, 1), (512, 8, 2)])
+def test_gqa_model_matches_cpu_reference(hd_heads):
+    from oxidizr_b200.models import build_model
+    H, nh, kvh = hd_heads
+    cfg = _small_cfg(hidden_size=H, num_heads=nh, kv_heads=kvh)
+    torch.manual_seed(0)
+    gpu = build_model(cfg.model, device="cuda", seed=3)
+    cpu = build_model(cfg.model, device="cpu", seed=3, dtype=torch.float32)
+    cpu.import_ref({k: v.float().cpu() for k, v in gpu.export_ref().items()})
+    ids = torch.randint(0, 1000, (2, 65))
+    lg, _ = gpu(ids[:, :-1].cuda(), ids[:, 1:].cuda())
+    lc, _ = cpu(ids[:, :-1], ids[:, 1:])
+    assert abs(lg.item() - lc.item()) < 2e-2
+    lg.backward()
+    lc.backward()
+    gg = {k: v for k, v in zip([n for n, _ in gpu.named_parameters()], [p.grad for p in gpu.parameters()])}
+    gc = {k: v for k, v in zip([n for n, _ in cpu.named_parameters()], [p.grad for p in cpu.parameters()])}
+    for k in gc:
+        assert _rel(gg[k].cpu(), gc[k]) < 6e-2, k
