@@ -45,7 +45,9 @@ enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, 
 
 struct GemmParams {
   int M, N, K;
-  int tiles_m, tiles_n, num_tiles;
+  int tiles_m, tiles_n, num_tiles;  // num_tiles counts work units (tiles x splits)
+  int splits;                        // split-K factor (F32 accumulate epilogue only)
+  int kb_per_split;
   void* D;                 // main output
   int64_t ldd;
   const __nv_bfloat16* R;  // residual (BF16) / GU (SWIGLU_BWD)
@@ -69,6 +71,7 @@ struct GemmParams {
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
   // Group GROUP_M row-tiles together so consecutive CTAs share B tiles in L2.
+  t /= p.splits;
   const int per_group = GROUP_M * p.tiles_n;
   const int g = t / per_group;
   const int first_m = g * GROUP_M;
@@ -76,6 +79,13 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm,
   const int r = t - g * per_group;
   tm = first_m + (r % gm);
   tn = r / gm;
+}
+
+// k-block range of work unit t
+__device__ __forceinline__ void unit_krange(int t, const GemmParams& p, int num_kb, int& kb0, int& kb1) {
+  const int sp = t % p.splits;
+  kb0 = sp * p.kb_per_split;
+  kb1 = min(num_kb, kb0 + p.kb_per_split);
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
@@ -169,10 +179,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int s = 0; s < STAGES; ++s) { armed[s] = false; armed_parity[s] = 0; }
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        int tm, tn;
+        int tm, tn, kb0, kb1;
         tile_coords(t, p, tm, tn);
+        unit_krange(t, p, num_kb, kb0, kb1);
         const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           armed[stage] = true;
@@ -215,7 +226,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        int kb0, kb1;
+        unit_krange(t, p, num_kb, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_STAGE_BYTES);
@@ -227,7 +240,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             else       ad = umma_desc_sw128(a_addr + k * 2048, BK * 128, 1024);
             if (!B_MN) bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
             else       bd = umma_desc_sw128(b_addr + k * 2048, BK * 128, 1024);
-            tc_mma_f16(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+            tc_mma_f16(d_tmem, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -281,7 +294,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             store_bf16_row(dst, v, nvalid, vec);
           } else if constexpr (EPI == EPI_F32) {
             float* dst = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col;
-            if (vec && nvalid >= 32) {
+            if (p.splits > 1) {
+              // split-K partial sums accumulate into the output (beta == 1)
+              if (vec && nvalid >= 32) {
+                float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  atomicAdd(d4 + q, make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]));
+              } else {
+                for (int j = 0; j < nvalid; ++j) atomicAdd(dst + j, v[j]);
+              }
+            } else if (vec && nvalid >= 32) {
               float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
@@ -520,8 +543,26 @@ inline void fill_common(GemmParams& p, const Operand& a, const Operand& b) {
   p.K = (int)a.k;
   p.tiles_m = (p.M + BM - 1) / BM;
   p.tiles_n = (p.N + BN - 1) / BN;
+  p.splits = 1;
+  p.kb_per_split = (p.K + BK - 1) / BK;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.alpha = 1.f;
+}
+
+// Split K across CTAs when there are too few output tiles to fill the GPU
+// (weight-gradient GEMMs: small M x N, K = tokens).  Only valid for an
+// accumulating f32 output, whose epilogue adds with atomics.
+inline void choose_splits(GemmParams& p) {
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const int sms = num_sms();
+  if (tiles >= 2 * sms || num_kb < 32) return;
+  int s = (2 * sms + tiles - 1) / tiles;
+  s = std::min(s, num_kb / 16);
+  if (s <= 1) return;
+  p.kb_per_split = (num_kb + s - 1) / s;
+  p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  p.num_tiles = tiles * p.splits;
 }
 
 inline bool aligned16(const void* ptr, int64_t ld, int esize) {

@@ -37,6 +37,7 @@ void launch_gemm(const Mat& a, bool a_mn, const Mat& b, bool b_mn, void* out, in
   } else {
     p.vec_ok = aligned16(out, ldo, 4);
     p.beta = beta;
+    if (beta == 1.0f) choose_splits(p);
     launch_epi<EPI_F32>(a_mn, b_mn, ta, tb, p, st);
   }
 }

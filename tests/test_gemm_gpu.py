@@ -134,3 +134,21 @@ def test_gemm_rope(hd):
     yr = y * c + rot * s
     ref = torch.cat([yr[:, :, :nh + kvh], y[:, :, nh + kvh:]], 2).reshape(M, N)
     assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 4096), (128, 2048, 16384), (300, 1000, 3000)])
+def test_gemm_splitk_accumulate(M, N, K):
+    """Few output tiles and long K: the f32 accumulate path splits K across CTAs."""
+    from oxidizr_b200.ops.gemm import mm
+    torch.manual_seed(5)
+    a = torch.randn(K, M, device="cuda").bfloat16()
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    if M % 8:
+        a = torch.nn.functional.pad(a, (0, 8 - M % 8))[:, :M]
+    if N % 8:
+        b = torch.nn.functional.pad(b, (0, 8 - N % 8))[:, :N]
+    base = torch.randn(M, N, device="cuda")
+    out = base.clone()
+    mm(a, b, a_t=True, b_t=True, out=out, beta=1.0)
+    ref = base + a.float().t() @ b.float()
+    assert _rel(out, ref) < 1e-4
