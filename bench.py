@@ -171,17 +171,20 @@ def main():
     B, S, V = tcfg.batch_size, m.max_seq_len, m.vocab_size
     torch.manual_seed(1234)
     model = build_model(m, device=dev, seed=0)
-    flat = FlatParams(list(model.named_parameters()), dev)
     ocfg = AdamWConfig(lr=tcfg.learning_rate)
     backend = args.sync_backend
     if world > 1:
-        from oxidizr_b200.parallel.ddp import DDPAdamW
         if backend == "auto":
-            backend = "nccl"
-        opt = DDPAdamW(flat, ocfg, backend=backend)
+            backend = "fused"
+        if backend == "fused":
+            from oxidizr_b200.parallel.fused_ar import FusedDDPAdamW
+            opt = FusedDDPAdamW(list(model.named_parameters()), ocfg, dev)
+        else:
+            from oxidizr_b200.parallel.ddp import DDPAdamW
+            opt = DDPAdamW(FlatParams(list(model.named_parameters()), dev), ocfg, backend=backend)
     else:
         backend = "single"
-        opt = AdamW(flat, ocfg)
+        opt = AdamW(FlatParams(list(model.named_parameters()), dev), ocfg)
 
     # ---------------- device-timed steps on device-resident synthetic tokens
     gen = torch.Generator(device=dev)
@@ -292,7 +295,10 @@ def main():
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
+    if hasattr(opt, "close"):
+        opt.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 

@@ -1,0 +1,288 @@
+// NVLink data-parallel runtime: CUDA-IPC symmetric buffers and the fused
+// gradient reduce-scatter / clip / AdamW / parameter all-gather kernels.
+//
+// Every rank owns, in device memory mapped by all peers:
+//   send  bf16 [N]   the rank's gradient, rounded to bf16 (NVLink payload)
+//   param bf16 [N]   the model parameters (flat)
+//   pad   signal pad: epoch flags written by peers, partial norms
+// and privately: the reduced f32 gradient of its shards, and f32 master
+// weights / AdamW moments of its shards only (optimizer state sharded W ways).
+//
+// Bucket b covers flat range [lo, lo + len), len a multiple of W * 64; rank r
+// owns [lo + r*len/W, lo + (r+1)*len/W).  Per step (epoch e, monotonic):
+//   1. bucket ready in backward: grad f32 -> bf16 into send[lo..]   (local)
+//   2. rs kernel: post epoch into every peer's ready[b][r]; wait until
+//      ready[b][*] >= e in the local pad; sum the owned shard over all peers'
+//      send buffers (P2P 16-byte loads), f32 accumulate -> rgrad; sum(g^2)
+//   3. norm kernel: exchange partial sum(g^2) through the pads -> clip coef
+//   4. adamw_ag kernel: AdamW on the owned shards (f32 master), bf16 result
+//      stored to every peer's param buffer (P2P 16-byte stores); post epoch
+//      into every peer's ag[r]; wait until ag[*] >= e locally.
+// Cross-GPU ordering: data stores, then a system-scope fence, then a release
+// store of the flag; the waiter acquires the flag before reading data.  All
+// waits are bounded (OXI_WAIT_LIMIT_NS); on timeout the kernel records
+// OXI_ERR_TIMEOUT_PEER in the status word, skips its work and returns.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "host_util.h"
+#include "kernels_comm.h"
+#include "ptx.cuh"
+
+namespace oxi {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until flags[i*stride] >= epoch for i in [0, W) (local pad).  One thread.
+__device__ bool wait_flags(const int* flags, int W, int stride, int epoch, int* status, volatile int* abort) {
+  const uint64_t t0 = globaltimer();
+  for (int i = 0; i < W; ++i) {
+    uint32_t spins = 0;
+    while (ld_acquire_sys(flags + (int64_t)i * stride) < epoch) {
+      if ((++spins & 255u) == 0) {
+        if (abort && *abort) return false;
+        if (globaltimer() - t0 > OXI_WAIT_LIMIT_NS) {
+          record_error(status, OXI_ERR_TIMEOUT_PEER);
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void add8(float* acc, uint4 u) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    acc[2 * i] += f.x;
+    acc[2 * i + 1] += f.y;
+  }
+}
+
+__global__ void grad_to_bf16_kernel(const float* __restrict__ g, __nv_bfloat16* __restrict__ out, int64_t n) {
+  const int64_t nv = n / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(g)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(g)[2 * i + 1];
+    reinterpret_cast<uint4*>(out)[i] =
+        make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+  }
+}
+
+// Reduce-scatter of one bucket.  peers_send[i] = rank i's send buffer (bf16 [N]).
+__global__ void rs_bucket_kernel(const uint64_t* __restrict__ peers_send, const uint64_t* __restrict__ peer_pads,
+                                 int* __restrict__ my_pad, int rank, int W, int bucket, int epoch, int64_t lo,
+                                 int64_t len, float* __restrict__ rgrad, float* __restrict__ sumsq, int* status) {
+  __shared__ int ok_s;
+  __shared__ float red[32];
+  const int64_t shard = len / W;
+  const int64_t s0 = lo + rank * shard;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      // the send buffer of this bucket was written by the previous kernel on
+      // this stream; make it visible system-wide, then tell every peer.
+      __threadfence_system();
+      for (int i = 0; i < W; ++i) {
+        int* pad = reinterpret_cast<int*>(peer_pads[i]);
+        st_release_sys(pad + PAD_READY + bucket * PAD_MAXW + rank, epoch);
+      }
+    }
+    ok_s = wait_flags(my_pad + PAD_READY + bucket * PAD_MAXW, W, 1, epoch, status, nullptr) ? 1 : 0;
+  }
+  __syncthreads();
+  float ss = 0.f;
+  if (ok_s) {
+    const int64_t nv = shard / 8;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int i = 0; i < W; ++i) {
+        const int src = (rank + i) % W;  // stagger peers so ranks do not all hit the same one
+        const uint4 u = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers_send[src]) + s0)[v];
+        add8(acc, u);
+      }
+      float* o = rgrad + v * 8;  // rgrad points at this bucket's shard
+      reinterpret_cast<float4*>(o)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) atomicAdd(sumsq, t);
+  }
+}
+
+// Exchange partial sums of squares; coef = min(1, max_norm / (norm + 1e-6)) / W.
+__global__ void norm_exchange_kernel(const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad, int rank,
+                                     int W, int epoch, const float* __restrict__ sumsq, float max_norm,
+                                     float* __restrict__ coef, float* __restrict__ norm_out, int* status) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const float mine = *sumsq;
+  for (int i = 0; i < W; ++i) {
+    int* pad = reinterpret_cast<int*>(peer_pads[i]);
+    reinterpret_cast<volatile float*>(pad + PAD_NORMV)[rank] = mine;
+  }
+  __threadfence_system();
+  for (int i = 0; i < W; ++i) st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_NORMF + rank, epoch);
+  if (!wait_flags(my_pad + PAD_NORMF, W, 1, epoch, status, nullptr)) {
+    *coef = 0.f;  // no update on a failed exchange
+    *norm_out = NAN;
+    return;
+  }
+  float tot = 0.f;
+  for (int i = 0; i < W; ++i) tot += reinterpret_cast<volatile float*>(my_pad + PAD_NORMV)[i];
+  const float nrm = sqrtf(tot) / W;  // norm of the averaged gradient
+  *norm_out = nrm;
+  float c = 1.f / W;
+  if (max_norm > 0.f && nrm > max_norm) c *= max_norm / (nrm + 1e-6f);
+  *coef = c;
+}
+
+// AdamW on the owned shards + bf16 parameter all-gather over P2P stores.
+// buckets: [nb][3] int64 = {lo, len, shard_offset_in_rgrad}
+__global__ void adamw_allgather_kernel(const int64_t* __restrict__ buckets, int nb, int rank, int W,
+                                       const float* __restrict__ rgrad, float* __restrict__ master,
+                                       float* __restrict__ m, float* __restrict__ v,
+                                       const uint64_t* __restrict__ peers_param, const uint64_t* __restrict__ peer_pads,
+                                       int* __restrict__ my_pad, int epoch, float lr, float b1, float b2, float eps,
+                                       float wd, float bc1, float bc2, const float* __restrict__ coef,
+                                       int* __restrict__ done_ctr, int* status) {
+  const float gs = *coef;
+  const float rb1 = 1.f / bc1, rb2 = 1.f / bc2;
+  const bool failed = status && *reinterpret_cast<volatile int*>(status) != 0;
+  if (!failed) {
+    for (int b = 0; b < nb; ++b) {
+      const int64_t lo = buckets[3 * b], len = buckets[3 * b + 1], so = buckets[3 * b + 2];
+      const int64_t shard = len / W;
+      const int64_t p0 = lo + rank * shard;
+      const int64_t nv = shard / 8;
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+        float pw[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int64_t e = so + i * 8 + k;
+          const float g = rgrad[e] * gs;
+          const float mk = b1 * m[e] + (1.f - b1) * g;
+          const float vk = b2 * v[e] + (1.f - b2) * g * g;
+          m[e] = mk;
+          v[e] = vk;
+          const float pp = master[e];
+          const float np = pp - lr * ((mk * rb1) / (sqrtf(vk * rb2) + eps)) - lr * wd * pp;
+          master[e] = np;
+          pw[k] = np;
+        }
+        const uint4 packed = make_uint4(pack_bf16(pw[0], pw[1]), pack_bf16(pw[2], pw[3]), pack_bf16(pw[4], pw[5]),
+                                        pack_bf16(pw[6], pw[7]));
+        for (int j = 0; j < W; ++j) {
+          const int dst = (rank + j) % W;
+          reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers_param[dst]) + p0)[i] = packed;
+        }
+      }
+    }
+  }
+  // last CTA to finish publishes this rank's epoch to every peer, then waits for all
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = (atomicAdd(done_ctr, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    *done_ctr = 0;
+    __threadfence_system();
+    for (int i = 0; i < W; ++i) st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_AGF + rank, epoch);
+    wait_flags(my_pad + PAD_AGF, W, 1, epoch, status, nullptr);
+  }
+}
+
+int sms() {
+  static int n = 0;
+  if (!n) {
+    int d;
+    cudaGetDevice(&d);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+  }
+  return n;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- host side
+void* ipc_alloc(size_t nbytes, std::string* handle) {
+  void* p = nullptr;
+  OXI_CUDA_CHECK(cudaMalloc(&p, nbytes));
+  OXI_CUDA_CHECK(cudaMemset(p, 0, nbytes));
+  cudaIpcMemHandle_t h;
+  OXI_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));
+  handle->assign(reinterpret_cast<const char*>(&h), sizeof(h));
+  return p;
+}
+
+void ipc_free(void* p) { OXI_CUDA_CHECK(cudaFree(p)); }
+
+void* ipc_open(const std::string& handle) {
+  OXI_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  OXI_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return p;
+}
+
+void ipc_close(void* p) { OXI_CUDA_CHECK(cudaIpcCloseMemHandle(p)); }
+
+void launch_grad_to_bf16(const float* g, void* out, int64_t n, cudaStream_t st) {
+  OXI_CHECK(n % 8 == 0, "bucket length must be a multiple of 8");
+  if (!n) return;
+  const unsigned grid = (unsigned)std::min<int64_t>((n / 8 + 255) / 256, (int64_t)sms() * 4);
+  grad_to_bf16_kernel<<<grid, 256, 0, st>>>(g, reinterpret_cast<__nv_bfloat16*>(out), n);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_rs_bucket(const uint64_t* peers_send, const uint64_t* peer_pads, int* my_pad, int rank, int W, int bucket,
+                      int epoch, int64_t lo, int64_t len, float* rgrad, float* sumsq, int ctas, int* status,
+                      cudaStream_t st) {
+  OXI_CHECK(W <= PAD_MAXW && bucket < PAD_MAXB, "too many ranks or buckets");
+  OXI_CHECK(len % (W * 8) == 0, "bucket length must divide into 8-element shards");
+  rs_bucket_kernel<<<ctas, 512, 0, st>>>(peers_send, peer_pads, my_pad, rank, W, bucket, epoch, lo, len, rgrad, sumsq,
+                                          status);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_norm_exchange(const uint64_t* peer_pads, int* my_pad, int rank, int W, int epoch, const float* sumsq,
+                          float max_norm, float* coef, float* norm_out, int* status, cudaStream_t st) {
+  norm_exchange_kernel<<<1, 32, 0, st>>>(peer_pads, my_pad, rank, W, epoch, sumsq, max_norm, coef, norm_out, status);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_adamw_allgather(const int64_t* buckets, int nb, int rank, int W, const float* rgrad, float* master,
+                            float* m, float* v, const uint64_t* peers_param, const uint64_t* peer_pads, int* my_pad,
+                            int epoch, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                            const float* coef, int* done_ctr, int* status, cudaStream_t st) {
+  adamw_allgather_kernel<<<sms() * 2, 256, 0, st>>>(buckets, nb, rank, W, rgrad, master, m, v, peers_param, peer_pads,
+                                                    my_pad, epoch, lr, b1, b2, eps, wd, bc1, bc2, coef, done_ctr,
+                                                    status);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace oxi

@@ -1,0 +1,780 @@
+// Causal flash attention for sm_100a (tcgen05 + TMEM + TMA), forward.
+//
+// One CTA per (128-query tile, query head, batch).  Q (128 x D) stays in
+// shared memory; K/V tiles of 128 keys stream through a 2-stage TMA ring.
+//   S_j = Q K_j^T        tcgen05.mma, f32 accumulator in TMEM (2 buffers)
+//   P_j = exp2(S_j*c - m) softmax warps: one thread per query row, P written
+//                        to shared memory in the 128B-swizzled K-major layout
+//   O  += P_j V_j        tcgen05.mma, f32 accumulator in TMEM (V as MN-major B)
+// The running max is only moved (and O rescaled) when the row max grows by
+// more than 2^8, so the TMEM read-modify-write of O is rare after the first
+// tiles.  The MMA warp issues S_{j+1} before waiting for P_j, so QK^T of the
+// next tile overlaps the softmax of the current one.
+//
+// Layout: q/k/v are row-major [B*S, H*D] views (row stride ld*), head h at
+// columns [h*D, (h+1)*D); GQA maps query head h to kv head h / (Hq/Hk).
+// Outputs: o [B*S, Hq*D] bf16, lse [B, Hq, S] f32 (natural log).
+// Warps: 0 TMA, 1 MMA + TMEM owner, 2..5 softmax/correction/epilogue.
+// No TMA load here uses cluster multicast; every wait is bounded.
+#include <algorithm>
+#include <cudaTypedefs.h>
+
+#include "gemm_kernel.cuh"
+#include "kernels_attn.h"
+
+namespace oxi {
+namespace {
+
+constexpr int FA_BM = 128, FA_BN = 128;
+constexpr int FA_THREADS = 192;
+
+struct FaParams {
+  int B, S, Hq, Hk, D;
+  float scale_log2;  // softmax scale * log2(e)
+  int causal;
+  __nv_bfloat16* o;
+  int64_t ldo;
+  float* lse;
+  int* status;
+};
+
+template <int D>
+struct FaSmem {
+  static constexpr int Q_BYTES = FA_BM * D * 2;
+  static constexpr int KV_BYTES = FA_BN * D * 2;
+  static constexpr int P_BYTES = FA_BM * FA_BN * 2;
+  static constexpr int KST = 3;               // K stages: K_j is freed as soon as S_j is done
+  static constexpr int VST = D <= 64 ? 3 : 2; // V stages: V_j is freed after PV_j
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + VST * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+  static_assert(TOTAL <= 232448, "shared memory budget");
+};
+
+// UMMA descriptor of the kk-th K=16 slice of a K-major SW128 tile whose K
+// extent is split into 64-element (128-byte) blocks of `block_bytes` each.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, uint32_t block_bytes) {
+  return umma_desc_sw128(base + (kk >> 2) * block_bytes + (kk & 3) * 32, 16, 1024);
+}
+
+template <int D>
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, FaParams p) {
+  using L = FaSmem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sP = smem + L::OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [3]
+  uint64_t* k_empty = bars + 4;   // [3]
+  uint64_t* v_full = bars + 7;    // [3]
+  uint64_t* v_empty = bars + 10;  // [3]
+  uint64_t* s_full = bars + 13;   // [2]
+  uint64_t* s_empty = bars + 15;  // [2]
+  uint64_t* p_full = bars + 17;
+  uint64_t* pv_done = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_qt = (p.S + FA_BM - 1) / FA_BM;
+  const int qt = n_qt - 1 - blockIdx.x;  // longest (causal) tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hk);
+  const int q0 = qt * FA_BM;
+  const int row0 = b * p.S;
+  const int n_kt_all = (p.S + FA_BN - 1) / FA_BN;
+  const int nk = p.causal ? min(n_kt_all, (q0 + FA_BM - 1) / FA_BN + 1) : n_kt_all;
+  constexpr int KB = D / 64;  // 64-column blocks per row
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);  // one arrival per softmax warp
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_S0 = tmem, TM_O = tmem + 2 * FA_BN;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(q_full, L::Q_BYTES);
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb) tma_load_2d(sQ + kb * FA_BM * 128, &tmQ, q_full, h * D + kb * 64, row0 + q0);
+      // K_j runs ahead of V_j: K stages free up when S_j completes, V stages
+      // when PV_j completes, so K loads are issued as early as possible.
+      int jv = 0;
+      for (int j = 0; j < nk && ok; ++j) {
+        const int ks = j % L::KST, ku = j / L::KST;
+        if (!mbar_wait(&k_empty[ks], (ku & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[ks], L::KV_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          tma_load_2d(sK + ks * L::KV_BYTES + kb * FA_BN * 128, &tmK, &k_full[ks], hk * D + kb * 64,
+                      row0 + j * FA_BN);
+        // issue every V load whose stage is already free (never more than one behind K)
+        while (jv <= j) {
+          const int vs = jv % L::VST, vu = jv / L::VST;
+          if (jv < j && !mbar_try_wait(smem_u32(&v_empty[vs]), (vu & 1) ^ 1)) break;
+          if (jv == j && !mbar_wait(&v_empty[vs], (vu & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[vs], L::KV_BYTES);
+#pragma unroll
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d(sV + vs * L::KV_BYTES + kb * FA_BN * 128, &tmV, &v_full[vs], hk * D + kb * 64,
+                        row0 + jv * FA_BN);
+          ++jv;
+        }
+      }
+      // drain: wait for every copy issued to land before leaving
+      if (!ok) {
+        mbar_wait(q_full, 0, nullptr, p.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = umma_idesc_bf16(FA_BM, FA_BN, false, false);
+      constexpr uint32_t IDESC_O = umma_idesc_bf16(FA_BM, D, false, true);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status);
+      const uint32_t aQ = smem_u32(sQ);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1, u = j >> 1;
+        const int ks = j % L::KST, ku = j / L::KST;
+        if (!mbar_wait(&k_full[ks], ku & 1, abort_flag, p.status)) return false;
+        if (!mbar_wait(&s_empty[st], (u & 1) ^ 1, abort_flag, p.status)) return false;
+        tc_fence_after();
+        const uint32_t aK = smem_u32(sK + ks * L::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma_f16(TM_S0 + st * FA_BN, kmajor_desc(aQ, kk, FA_BM * 128), kmajor_desc(aK, kk, FA_BN * 128),
+                     IDESC_S, kk != 0);
+        tc_commit(&s_full[st]);
+        tc_commit(&k_empty[ks]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nk && ok; ++j) {
+        if (j + 1 < nk && !issue_s(j + 1)) { ok = false; break; }
+        if (!mbar_wait(p_full, j & 1, abort_flag, p.status)) { ok = false; break; }
+        const int vs = j % L::VST, vu = j / L::VST;
+        if (!mbar_wait(&v_full[vs], vu & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t aP = smem_u32(sP);
+        const uint32_t aV = smem_u32(sV + vs * L::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < FA_BN / 16; ++kk)
+          tc_mma_f16(TM_O, kmajor_desc(aP, kk, FA_BM * 128), umma_desc_sw128(aV + kk * 2048, FA_BN * 128, 1024),
+                     IDESC_O, (j | kk) != 0);
+        tc_commit(pv_done);
+        tc_commit(&v_empty[vs]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------- softmax warps
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;       // query row within the tile (== TMEM lane)
+    const int qpos = q0 + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk && ok; ++j) {
+      const int st = j & 1, u = j >> 1;
+      if (!mbar_wait(&s_full[st], u & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      // Two compact passes over 32-column TMEM chunks: (1) row max, (2) exp2,
+      // row sum, bf16 P to shared memory.  Masking is branch-free: keys past
+      // `lim` (causal diagonal or sequence end) become -inf.
+      const int k0 = j * FA_BN;
+      const bool need_mask = (p.causal && k0 + FA_BN - 1 > q0) || (k0 + FA_BN > p.S);
+      const int lim = p.causal ? min(qpos, p.S - 1) : p.S - 1;
+      const uint32_t s_base = TM_S0 + st * FA_BN + lane_base;
+      // the whole S row (128 columns) in one batch of TMEM loads, one wait
+      uint32_t rr[4][32];
+      tmem_ld32(s_base + 0, rr[0]);
+      tmem_ld32(s_base + 32, rr[1]);
+      tmem_ld32(s_base + 64, rr[2]);
+      tmem_ld32(s_base + 96, rr[3]);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[st]);  // S buffer may be overwritten now
+      // 8 independent max accumulators keep the dependency chains short
+      float mx[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) mx[q] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int kc = k0 + c * 32;
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          float v = __uint_as_float(rr[c][t]) * p.scale_log2;
+          if (need_mask) v = (kc + t > lim) ? -INFINITY : v;
+          rr[c][t] = __float_as_uint(v);
+          mx[t & 7] = fmaxf(mx[t & 7], v);
+        }
+      }
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      // move the reference max only when it grows by more than 2^8
+      const bool move = (mt > m + 8.f);
+      const float m_new = move ? mt : m;
+      const float alpha = move ? ex2_approx(m - m_new) : 1.f;  // exp2(-inf) = 0 on the first tile
+      const float mref = (m_new == -INFINITY) ? 0.f : m_new;
+      const bool rescale_warp = __any_sync(0xffffffffu, move && j > 0);
+      m = m_new;
+      if (j > 0) {
+        // P buffer and O are owned by the previous PV MMA until it completes
+        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        if (rescale_warp) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; c += 2) {
+            uint32_t o0[32], o1[32];
+            tmem_ld32(TM_O + lane_base + c * 32, o0);
+            tmem_ld32(TM_O + lane_base + c * 32 + 32, o1);
+            tc_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              o0[t] = __float_as_uint(__uint_as_float(o0[t]) * alpha);
+              o1[t] = __float_as_uint(__uint_as_float(o1[t]) * alpha);
+            }
+            tmem_st32(TM_O + lane_base + c * 32, o0);
+            tmem_st32(TM_O + lane_base + c * 32 + 32, o1);
+          }
+          tc_wait_st();
+        }
+      }
+      float rsa[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) rsa[q] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const float a = ex2_approx(__uint_as_float(rr[c][t]) - mref);
+          const float bb = ex2_approx(__uint_as_float(rr[c][t + 1]) - mref);
+          rsa[(t >> 1) & 7] += a + bb;
+          pk[t / 2] = pack_bf16(a, bb);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ch = c * 4 + q;  // 8-key chunk index 0..15
+          sw128_store16(sP + (ch >> 3) * (FA_BM * 128), r, ch & 7,
+                        make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]));
+        }
+      }
+      const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
+      l = l * alpha + rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(pv_done, (nk - 1) & 1, abort_flag, p.status)) {
+      tc_fence_after();
+      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      const bool valid = qpos < p.S;
+      __nv_bfloat16* orow = p.o + (int64_t)(row0 + qpos) * p.ldo + h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(TM_O + lane_base + c * 32, o);
+        tc_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
+            w.y = pack_bf16(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
+            w.z = pack_bf16(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
+            w.w = pack_bf16(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
+            dst[q] = w;
+          }
+        }
+      }
+      if (valid) p.lse[((int64_t)b * p.Hq + h) * p.S + qpos] = (m + __log2f(l)) * 0.69314718055994530942f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+void launch_fa_fwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
+                     int64_t ldo, float* lse, int B, int S, int Hq, int Hk, float scale, bool causal, int* status,
+                     cudaStream_t st) {
+  using L = FaSmem<D>;
+  const int64_t T = (int64_t)B * S;
+  CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * D, ldq, 64, FA_BM);
+  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * D, ldk, 64, FA_BN);
+  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * D, ldv, 64, FA_BN);
+  FaParams p;
+  p.B = B; p.S = S; p.Hq = Hq; p.Hk = Hk; p.D = D;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.ldo = ldo;
+  p.lse = lse;
+  p.status = status;
+  auto kern = fa_fwd_kernel<D>;
+  static bool attr = false;
+  if (!attr) {
+    OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    attr = true;
+  }
+  dim3 grid((S + FA_BM - 1) / FA_BM, Hq, B);
+  kern<<<grid, FA_THREADS, L::TOTAL, st>>>(tq, tk, tv, p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+
+// ===================================================================== backward
+// One CTA per (128-key tile j, kv head hk, batch b); loops over the query heads
+// of the GQA group and over the query tiles i >= j (causal).  Per (h, i):
+//   S^T  = K Q_i^T, dP^T = V dO_i^T            (TMEM)
+//   P^T  = exp2(S^T c - lse_i), dS^T = P^T (dP^T - delta_i) * scale
+//                                              (softmax warps -> swizzled smem)
+//   dV += P^T dO_i, dK += dS^T Q_i             (TMEM accumulators)
+//   dQ_i = dS K -> f32 atomics into dq_acc     (TMEM, aliases S^T)
+// dS^T in shared memory serves as the K-major A of dK and, read as MN-major,
+// as the A of dQ; Q, dO and K are read as K-major or MN-major B operands from
+// the same tiles.
+struct FaBwdParams {
+  int B, S, Hq, Hk;
+  float scale, scale_log2;
+  int causal;
+  const float* lse;    // [B, Hq, S]
+  const float* delta;  // [B, Hq, S]
+  float* dq_acc;       // [B*S, Hq*D] f32, zero-initialised
+  int64_t ld_dq;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t ld_dkv;
+  int* status;
+};
+
+template <int D>
+struct FaBwdSmem {
+  static constexpr int T_BYTES = 128 * D * 2;   // K, V, Q, dO tiles
+  static constexpr int P_BYTES = 128 * 128 * 2;  // P^T, dS^T
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + T_BYTES;
+  static constexpr int OFF_Q = OFF_V + T_BYTES;
+  static constexpr int OFF_DO = OFF_Q + T_BYTES;
+  static constexpr int OFF_PT = OFF_DO + T_BYTES;
+  static constexpr int OFF_DST = OFF_PT + P_BYTES;
+  static constexpr int OFF_VEC = OFF_DST + P_BYTES;   // lse (log2), delta: 2 x 128 f32
+  static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                  FaBwdParams p) {
+  using L = FaBwdSmem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sDO = smem + L::OFF_DO;
+  uint8_t* sPt = smem + L::OFF_PT;
+  uint8_t* sDSt = smem + L::OFF_DST;
+  float* s_lse = reinterpret_cast<float*>(smem + L::OFF_VEC);
+  float* s_delta = s_lse + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* sdp_full = bars + 2;
+  uint64_t* p_ready = bars + 3;
+  uint64_t* it_done = bars + 4;
+  uint64_t* dq_read = bars + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int jt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int group = p.Hq / p.Hk;
+  const int n_qt = (p.S + 127) / 128;
+  const int i_start = p.causal ? jt : 0;
+  const int n_i = n_qt - i_start;
+  const int n_it = group * n_i;
+  const int row0 = b * p.S;
+  const int k0 = jt * 128;
+  constexpr int KB = D / 64;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(sdp_full, 1);
+    mbar_init(p_ready, 4);   // one arrival per softmax warp
+    mbar_init(it_done, 1);
+    mbar_init(dq_read, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_DV = tmem, TM_DK = tmem + D, TM_S = tmem + 2 * D, TM_DP = tmem + 2 * D + 128;
+  const uint32_t TM_DQ = TM_S;  // dQ reuses the S^T columns once they are consumed
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * L::T_BYTES);
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb) {
+        tma_load_2d(sK + kb * 128 * 128, &tmK, kv_full, hk * D + kb * 64, row0 + k0);
+        tma_load_2d(sV + kb * 128 * 128, &tmV, kv_full, hk * D + kb * 64, row0 + k0);
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int h = hk * group + it / n_i;
+        const int i = i_start + it % n_i;
+        if (!mbar_wait(it_done, (it & 1) ^ 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(qdo_full, 2 * L::T_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb) {
+          tma_load_2d(sQ + kb * 128 * 128, &tmQ, qdo_full, h * D + kb * 64, row0 + i * 128);
+          tma_load_2d(sDO + kb * 128 * 128, &tmDO, qdo_full, h * D + kb * 64, row0 + i * 128);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_SS = umma_idesc_bf16(128, 128, false, false);  // S^T, dP^T
+      constexpr uint32_t ID_KV = umma_idesc_bf16(128, D, false, true);     // dV, dK
+      constexpr uint32_t ID_Q = umma_idesc_bf16(128, D, true, true);       // dQ
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
+      const uint32_t aPt = smem_u32(sPt), aDSt = smem_u32(sDSt);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (!mbar_wait(qdo_full, it & 1, abort_flag, p.status)) { ok = false; break; }
+        if (it > 0 && !mbar_wait(dq_read, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          tc_mma_f16(TM_S, kmajor_desc(aK, kk, 128 * 128), kmajor_desc(aQ, kk, 128 * 128), ID_SS, kk != 0);
+          tc_mma_f16(TM_DP, kmajor_desc(aV, kk, 128 * 128), kmajor_desc(aDO, kk, 128 * 128), ID_SS, kk != 0);
+        }
+        tc_commit(sdp_full);
+        if (!mbar_wait(p_ready, it & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk) {
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          // dV += P^T dO ; dK += dS^T Q  (B operands MN-major: rows = queries)
+          tc_mma_f16(TM_DV, kmajor_desc(aPt, kk, 128 * 128), umma_desc_sw128(aDO + kk * 2048, 128 * 128, 1024),
+                     ID_KV, acc);
+          tc_mma_f16(TM_DK, kmajor_desc(aDSt, kk, 128 * 128), umma_desc_sw128(aQ + kk * 2048, 128 * 128, 1024),
+                     ID_KV, acc);
+          // dQ = dS K: A = dS^T read MN-major (M = queries), B = K MN-major (rows = keys)
+          tc_mma_f16(TM_DQ, umma_desc_sw128(aDSt + kk * 2048, 128 * 128, 1024),
+                     umma_desc_sw128(aK + kk * 2048, 128 * 128, 1024), ID_Q, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(it_done);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // key row for P/dS; query row for the dQ epilogue
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int tid = threadIdx.x - 64;
+    const int kpos = k0 + r;
+    bool ok = true;
+    for (int it = 0; it < n_it && ok; ++it) {
+      const int h = hk * group + it / n_i;
+      const int i = i_start + it % n_i;
+      const int q0 = i * 128;
+      named_bar_sync(1, 128);  // previous iteration is done with s_lse / s_delta
+      {
+        const int qp = q0 + tid;
+        const int64_t vi = ((int64_t)b * p.Hq + h) * p.S + qp;
+        s_lse[tid] = qp < p.S ? p.lse[vi] * 1.4426950408889634f : 0.f;
+        s_delta[tid] = qp < p.S ? p.delta[vi] : 0.f;
+      }
+      named_bar_sync(1, 128);
+      if (!mbar_wait(sdp_full, it & 1, abort_flag, p.status)) { ok = false; break; }
+      // P^T / dS^T smem is free once the previous iteration's MMAs completed
+      if (!mbar_wait(it_done, (it & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = p.causal && (q0 < k0 + 128);
+#pragma unroll 1
+      for (int c2 = 0; c2 < 4; c2 += 2) {
+        uint32_t sr[2][32], dr[2][32];
+        tmem_ld32(TM_S + lane_base + c2 * 32, sr[0]);
+        tmem_ld32(TM_S + lane_base + c2 * 32 + 32, sr[1]);
+        tmem_ld32(TM_DP + lane_base + c2 * 32, dr[0]);
+        tmem_ld32(TM_DP + lane_base + c2 * 32 + 32, dr[1]);
+        tc_wait_ld();
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int c = c2 + h2;
+          uint32_t pk[16], dk[16];
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            float pv[2], dsv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int qc = c * 32 + t + e;
+              const int qp = q0 + qc;
+              const bool valid = (qp < p.S) && (kpos < p.S) && (!diag || qp >= kpos);
+              const float pp =
+                  valid ? ex2_approx(__uint_as_float(sr[h2][t + e]) * p.scale_log2 - s_lse[qc]) : 0.f;
+              pv[e] = pp;
+              dsv[e] = pp * (__uint_as_float(dr[h2][t + e]) - s_delta[qc]) * p.scale;
+            }
+            pk[t / 2] = pack_bf16(pv[0], pv[1]);
+            dk[t / 2] = pack_bf16(dsv[0], dsv[1]);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int ch = c * 4 + q;  // 8-query chunk index 0..15
+            sw128_store16(sPt + (ch >> 3) * (128 * 128), r, ch & 7,
+                          make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]));
+            sw128_store16(sDSt + (ch >> 3) * (128 * 128), r, ch & 7,
+                          make_uint4(dk[q * 4], dk[q * 4 + 1], dk[q * 4 + 2], dk[q * 4 + 3]));
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      // dQ of this (h, i): thread r owns query row r
+      if (!mbar_wait(it_done, it & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      const int qp = q0 + r;
+      float* dqrow = p.dq_acc + (int64_t)(row0 + qp) * p.ld_dq + h * D;
+#pragma unroll 1
+      for (int c2 = 0; c2 < D / 32; c2 += 2) {
+        uint32_t o[2][32];
+        tmem_ld32(TM_DQ + lane_base + c2 * 32, o[0]);
+        tmem_ld32(TM_DQ + lane_base + c2 * 32 + 32, o[1]);
+        tc_wait_ld();
+        if (qp < p.S) {
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            float4* d4 = reinterpret_cast<float4*>(dqrow + (c2 + h2) * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              atomicAdd(d4 + q, make_float4(__uint_as_float(o[h2][q * 4]), __uint_as_float(o[h2][q * 4 + 1]),
+                                            __uint_as_float(o[h2][q * 4 + 2]), __uint_as_float(o[h2][q * 4 + 3])));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_read);
+    }
+    // dK, dV of this key tile (thread r owns key row r)
+    if (ok && n_it > 0) {
+      tc_fence_after();
+      const bool valid = kpos < p.S;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + (int64_t)(row0 + kpos) * p.ld_dkv + hk * D;
+        const uint32_t src = (which == 0 ? TM_DV : TM_DK) + lane_base;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(src + c * 32, o);
+          tc_wait_ld();
+          if (valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              d4[q] = make_uint4(pack_bf16(__uint_as_float(o[q * 8]), __uint_as_float(o[q * 8 + 1])),
+                                 pack_bf16(__uint_as_float(o[q * 8 + 2]), __uint_as_float(o[q * 8 + 3])),
+                                 pack_bf16(__uint_as_float(o[q * 8 + 4]), __uint_as_float(o[q * 8 + 5])),
+                                 pack_bf16(__uint_as_float(o[q * 8 + 6]), __uint_as_float(o[q * 8 + 7])));
+          }
+        }
+      }
+    } else if (n_it == 0 && kpos < p.S) {
+      // no query attends to this key tile: zero gradients
+      __nv_bfloat16* dv = p.dv + (int64_t)(row0 + kpos) * p.ld_dkv + hk * D;
+      __nv_bfloat16* dk = p.dk + (int64_t)(row0 + kpos) * p.ld_dkv + hk * D;
+      for (int c = 0; c < D; ++c) { dv[c] = __float2bfloat16(0.f); dk[c] = __float2bfloat16(0.f); }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[b, h, s] = sum_d dO * O  (one warp per (token, head) row)
+__global__ void fa_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
+                                   const __nv_bfloat16* __restrict__ dout, int64_t lddo, float* __restrict__ delta,
+                                   int B, int S, int Hq, int D) {
+  const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)B * S * Hq;
+  if (w >= rows) return;
+  const int64_t t = w / Hq;
+  const int h = (int)(w % Hq);
+  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(o + t * ldo + (int64_t)h * D);
+  const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(dout + t * lddo + (int64_t)h * D);
+  float s = 0.f;
+  for (int i = lane; i < D / 2; i += 32) {
+    const float2 x = __bfloat1622float2(a[i]), y = __bfloat1622float2(g[i]);
+    s += x.x * y.x + x.y * y.y;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) {
+    const int b = (int)(t / S), sp = (int)(t % S);
+    delta[((int64_t)b * Hq + h) * S + sp] = s;
+  }
+}
+
+// dq (bf16, row stride lddq) = dq_acc (f32)
+__global__ void fa_dq_convert_kernel(const float* __restrict__ acc, int64_t ldacc, __nv_bfloat16* __restrict__ dq,
+                                     int64_t lddq, int64_t rows, int cols) {
+  const int64_t nv = rows * (cols / 8);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (cols / 8);
+    const int c = (int)(i % (cols / 8)) * 8;
+    const float4 a = *reinterpret_cast<const float4*>(acc + r * ldacc + c);
+    const float4 b = *reinterpret_cast<const float4*>(acc + r * ldacc + c + 4);
+    *reinterpret_cast<uint4*>(dq + r * lddq + c) =
+        make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+  }
+}
+
+template <int D>
+void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                     const void* dout, int64_t lddo, const float* lse, const float* delta, float* dq_acc,
+                     int64_t ld_dq, void* dk, void* dv, int64_t ld_dkv, int B, int S, int Hq, int Hk, float scale,
+                     bool causal, int* status, cudaStream_t st) {
+  using L = FaBwdSmem<D>;
+  const int64_t T = (int64_t)B * S;
+  CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * D, ldq, 64, 128);
+  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * D, ldk, 64, 128);
+  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * D, ldv, 64, 128);
+  CUtensorMap tdo = make_tmap_bf16(dout, T, (int64_t)Hq * D, lddo, 64, 128);
+  FaBwdParams p;
+  p.B = B; p.S = S; p.Hq = Hq; p.Hk = Hk;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  p.lse = lse;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.ld_dq = ld_dq;
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
+  p.ld_dkv = ld_dkv;
+  p.status = status;
+  auto kern = fa_bwd_kernel<D>;
+  static bool attr = false;
+  if (!attr) {
+    OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    attr = true;
+  }
+  dim3 grid((S + 127) / 128, Hk, B);
+  kern<<<grid, FA_THREADS, L::TOTAL, st>>>(tq, tk, tv, tdo, p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace
+
+void launch_fa_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
+                   int64_t ldo, float* lse, int B, int S, int Hq, int Hk, int D, float scale, bool causal,
+                   int* status, cudaStream_t st) {
+  OXI_CHECK(Hq % Hk == 0, "query heads must be a multiple of kv heads");
+  OXI_CHECK(ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0, "output rows must be 16-byte aligned");
+  if (B == 0 || S == 0) return;
+  if (D == 64) launch_fa_fwd_t<64>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hk, scale, causal, status, st);
+  else if (D == 128) launch_fa_fwd_t<128>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hk, scale, causal, status, st);
+  else OXI_CHECK(false, "flash attention supports head_dim 64 or 128, got ", D);
+}
+
+
+void launch_fa_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                   const void* o, int64_t ldo, const void* dout, int64_t lddo, const float* lse, float* delta,
+                   float* dq_acc, void* dq, int64_t lddq, void* dk, void* dv, int64_t ld_dkv, int B, int S, int Hq,
+                   int Hk, int D, float scale, bool causal, int* status, cudaStream_t st) {
+  OXI_CHECK(Hq % Hk == 0, "query heads must be a multiple of kv heads");
+  OXI_CHECK(ld_dkv % 8 == 0 && lddq % 8 == 0, "gradient rows must be 16-byte aligned");
+  if (B == 0 || S == 0) return;
+  const int64_t T = (int64_t)B * S;
+  const int64_t rows = T * Hq;
+  fa_bwd_prep_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(o), ldo, reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B,
+      S, Hq, D);
+  OXI_CUDA_CHECK(cudaGetLastError());
+  OXI_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, (size_t)T * Hq * D * sizeof(float), st));
+  if (D == 64)
+    launch_fa_bwd_t<64>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq_acc, (int64_t)Hq * D, dk, dv, ld_dkv, B,
+                        S, Hq, Hk, scale, causal, status, st);
+  else if (D == 128)
+    launch_fa_bwd_t<128>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq_acc, (int64_t)Hq * D, dk, dv, ld_dkv, B,
+                         S, Hq, Hk, scale, causal, status, st);
+  else
+    OXI_CHECK(false, "flash attention supports head_dim 64 or 128, got ", D);
+  const int64_t nv = T * (Hq * D / 8);
+  fa_dq_convert_kernel<<<(unsigned)std::min<int64_t>((nv + 255) / 256, 148 * 16), 256, 0, st>>>(
+      dq_acc, (int64_t)Hq * D, reinterpret_cast<__nv_bfloat16*>(dq), lddq, T, Hq * D);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace oxi

@@ -1,0 +1,34 @@
+// NVLink data-parallel runtime (comm.cu): IPC buffers and fused collectives.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <cuda_runtime.h>
+
+namespace oxi {
+
+// Signal pad layout (int32 words; PAD_NORMV holds f32 values).
+constexpr int PAD_MAXW = 16;
+constexpr int PAD_MAXB = 512;
+constexpr int PAD_READY = 0;                                // [PAD_MAXB][PAD_MAXW]
+constexpr int PAD_NORMF = PAD_READY + PAD_MAXB * PAD_MAXW;  // [PAD_MAXW]
+constexpr int PAD_NORMV = PAD_NORMF + PAD_MAXW;             // [PAD_MAXW] f32
+constexpr int PAD_AGF = PAD_NORMV + PAD_MAXW;               // [PAD_MAXW]
+constexpr int PAD_WORDS = PAD_AGF + PAD_MAXW;
+
+void* ipc_alloc(size_t nbytes, std::string* handle);
+void ipc_free(void* p);
+void* ipc_open(const std::string& handle);
+void ipc_close(void* p);
+
+void launch_grad_to_bf16(const float* g, void* out, int64_t n, cudaStream_t st);
+void launch_rs_bucket(const uint64_t* peers_send, const uint64_t* peer_pads, int* my_pad, int rank, int W, int bucket,
+                      int epoch, int64_t lo, int64_t len, float* rgrad, float* sumsq, int ctas, int* status,
+                      cudaStream_t st);
+void launch_norm_exchange(const uint64_t* peer_pads, int* my_pad, int rank, int W, int epoch, const float* sumsq,
+                          float max_norm, float* coef, float* norm_out, int* status, cudaStream_t st);
+void launch_adamw_allgather(const int64_t* buckets, int nb, int rank, int W, const float* rgrad, float* master,
+                            float* m, float* v, const uint64_t* peers_param, const uint64_t* peer_pads, int* my_pad,
+                            int epoch, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
+                            const float* coef, int* done_ctr, int* status, cudaStream_t st);
+
+}  // namespace oxi

@@ -6,6 +6,9 @@
 
 #include "kernels.h"
 #include "kernels_ew.h"
+#include "kernels_attn.h"
+#include "kernels_comm.h"
+#include "kernels_ssm.h"
 
 using oxi::Mat;
 
@@ -236,6 +239,233 @@ void adamw(torch::Tensor p, c10::optional<torch::Tensor> p16, torch::Tensor g, t
                     gscale.has_value() && gscale->defined() ? gscale->data_ptr<float>() : nullptr, stream());
 }
 
+// ------------------------------------------------------------ attention
+// q, k, v: [B*S, H*D]-shaped row-major bf16 views (unit inner stride)
+void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse, int64_t B,
+               int64_t S, int64_t Hq, int64_t Hk, int64_t D, double scale, bool causal, torch::Tensor status) {
+  c10::cuda::CUDAGuard g(q.device());
+  for (auto* t : {&q, &k, &v, &o})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 &&
+                    t->size(0) == B * S, "attention operands must be bf16 [B*S, H*D] with unit inner stride");
+  TORCH_CHECK(q.size(1) == Hq * D && k.size(1) == Hk * D && v.size(1) == Hk * D && o.size(1) == Hq * D, "head dims");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.numel() == B * Hq * S && lse.is_contiguous(), "lse");
+  oxi::launch_fa_fwd(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), o.data_ptr(),
+                     o.stride(0), lse.data_ptr<float>(), (int)B, (int)S, (int)Hq, (int)Hk, (int)D, (float)scale, causal,
+                     status_ptr(status), stream());
+}
+
+void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
+               torch::Tensor lse, torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dq, torch::Tensor dk,
+               torch::Tensor dv, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D, double scale, bool causal,
+               torch::Tensor status) {
+  c10::cuda::CUDAGuard g(q.device());
+  for (auto* t : {&q, &k, &v, &o, &dout, &dq, &dk, &dv})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 &&
+                    t->size(0) == B * S, "attention tensors must be bf16 [B*S, H*D] with unit inner stride");
+  TORCH_CHECK(dk.stride(0) == dv.stride(0), "dk and dv must share a row stride");
+  TORCH_CHECK(dq_acc.scalar_type() == torch::kFloat32 && dq_acc.is_contiguous() && dq_acc.numel() == B * S * Hq * D,
+              "dq_acc must be contiguous f32 [B*S, Hq*D]");
+  TORCH_CHECK(delta.scalar_type() == torch::kFloat32 && delta.numel() == B * Hq * S, "delta");
+  oxi::launch_fa_bwd(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), o.data_ptr(),
+                     o.stride(0), dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(),
+                     dq_acc.data_ptr<float>(), dq.data_ptr(), dq.stride(0), dk.data_ptr(), dv.data_ptr(),
+                     dk.stride(0), (int)B, (int)S, (int)Hq, (int)Hk, (int)D, (float)scale, causal, status_ptr(status),
+                     stream());
+}
+
+// ------------------------------------------------------------ NVLink DDP runtime
+// Allocates nbytes of zeroed device memory exportable over CUDA IPC; returns
+// (uint8 tensor owning it, IPC handle bytes).
+std::tuple<torch::Tensor, py::bytes> ipc_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  std::string h;
+  void* p = oxi::ipc_alloc((size_t)nbytes, &h);
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  torch::Tensor t = torch::from_blob(p, {nbytes}, [](void* q) { oxi::ipc_free(q); }, opts);
+  return {t, py::bytes(h)};
+}
+
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  return reinterpret_cast<int64_t>(oxi::ipc_open(std::string(handle)));
+}
+
+void ipc_close(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  oxi::ipc_close(reinterpret_cast<void*>(ptr));
+}
+
+int64_t pad_words() { return oxi::PAD_WORDS; }
+
+void grad_to_bf16(torch::Tensor g, torch::Tensor out) {
+  c10::cuda::CUDAGuard gd(g.device());
+  TORCH_CHECK(g.scalar_type() == torch::kFloat32 && out.scalar_type() == torch::kBFloat16 && g.numel() == out.numel()
+              && g.is_contiguous() && out.is_contiguous(), "grad_to_bf16");
+  oxi::launch_grad_to_bf16(g.data_ptr<float>(), out.data_ptr(), g.numel(), stream());
+}
+
+void rs_bucket(torch::Tensor peers_send, torch::Tensor peer_pads, torch::Tensor my_pad, int64_t rank, int64_t W,
+               int64_t bucket, int64_t epoch, int64_t lo, int64_t len, torch::Tensor rgrad_shard, torch::Tensor sumsq,
+               int64_t ctas, torch::Tensor status) {
+  c10::cuda::CUDAGuard gd(my_pad.device());
+  oxi::launch_rs_bucket(reinterpret_cast<const uint64_t*>(peers_send.data_ptr<int64_t>()),
+                        reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
+                        (int)rank, (int)W, (int)bucket, (int)epoch, lo, len, rgrad_shard.data_ptr<float>(),
+                        sumsq.data_ptr<float>(), (int)ctas, status_ptr(status), stream());
+}
+
+void norm_exchange(torch::Tensor peer_pads, torch::Tensor my_pad, int64_t rank, int64_t W, int64_t epoch,
+                   torch::Tensor sumsq, double max_norm, torch::Tensor coef, torch::Tensor norm, torch::Tensor status) {
+  c10::cuda::CUDAGuard gd(my_pad.device());
+  oxi::launch_norm_exchange(reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
+                            (int)rank, (int)W, (int)epoch, sumsq.data_ptr<float>(), (float)max_norm,
+                            coef.data_ptr<float>(), norm.data_ptr<float>(), status_ptr(status), stream());
+}
+
+void adamw_allgather(torch::Tensor buckets, int64_t rank, int64_t W, torch::Tensor rgrad, torch::Tensor master,
+                     torch::Tensor m, torch::Tensor v, torch::Tensor peers_param, torch::Tensor peer_pads,
+                     torch::Tensor my_pad, int64_t epoch, double lr, double b1, double b2, double eps, double wd,
+                     double bc1, double bc2, torch::Tensor coef, torch::Tensor done_ctr, torch::Tensor status) {
+  c10::cuda::CUDAGuard gd(my_pad.device());
+  TORCH_CHECK(buckets.scalar_type() == torch::kInt64 && buckets.is_cuda() && buckets.dim() == 2 && buckets.size(1) == 3,
+              "buckets must be int64 CUDA [nb, 3]");
+  oxi::launch_adamw_allgather(buckets.data_ptr<int64_t>(), (int)buckets.size(0), (int)rank, (int)W,
+                              rgrad.data_ptr<float>(), master.data_ptr<float>(), m.data_ptr<float>(),
+                              v.data_ptr<float>(), reinterpret_cast<const uint64_t*>(peers_param.data_ptr<int64_t>()),
+                              reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
+                              (int)epoch, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1,
+                              (float)bc2, coef.data_ptr<float>(), done_ctr.data_ptr<int>(), status_ptr(status),
+                              stream());
+}
+
+// ------------------------------------------------------------ SSM
+void conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias, torch::Tensor y, int64_t B,
+                int64_t S, bool act) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && x.size(0) == B * S,
+              "conv1d x must be bf16 [B*S, C] with unit inner stride");
+  const int64_t C = x.size(1);
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && w.numel() % C == 0, "conv1d weight");
+  TORCH_CHECK(y.sizes() == x.sizes() && y.stride(1) == 1, "conv1d y");
+  const void* bp = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->numel() == C, "conv1d bias");
+    bp = bias->data_ptr();
+  }
+  oxi::launch_conv1d_fwd(x.data_ptr(), x.stride(0), w.data_ptr(), bp, y.data_ptr(), y.stride(0), (int)B, (int)S,
+                         (int)C, (int)(w.numel() / C), act, stream());
+}
+
+void conv1d_bwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias, torch::Tensor dy,
+                torch::Tensor dx, torch::Tensor dw, c10::optional<torch::Tensor> db, int64_t B, int64_t S, bool act) {
+  c10::cuda::CUDAGuard g(x.device());
+  const int64_t C = x.size(1);
+  TORCH_CHECK(dy.stride(1) == 1 && dx.stride(1) == 1 && dy.size(1) == C && dx.size(1) == C, "conv1d grads");
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.numel() == w.numel() && dw.is_contiguous(), "dw f32");
+  const void* bp = nullptr;
+  float* dbp = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    bp = bias->data_ptr();
+    TORCH_CHECK(db.has_value() && db->scalar_type() == torch::kFloat32 && db->numel() == C, "db f32");
+    dbp = db->data_ptr<float>();
+  }
+  oxi::launch_conv1d_bwd(x.data_ptr(), x.stride(0), w.data_ptr(), bp, dy.data_ptr(), dy.stride(0), dx.data_ptr(),
+                         dx.stride(0), dw.data_ptr<float>(), dbp, (int)B, (int)S, (int)C, (int)(w.numel() / C), act,
+                         stream());
+}
+
+// x [B, S, H, P], Bm/Cm [B, S, H, N] (any strides), loga/gamma/beta [B, S, H]
+static oxi::SsmScanIO scan_io(torch::Tensor x, torch::Tensor Bm, torch::Tensor Cm, torch::Tensor loga,
+                              torch::Tensor gamma, c10::optional<torch::Tensor> beta) {
+  for (auto* t : {&x, &Bm, &Cm, &loga, &gamma})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32, "scan tensors must be f32 CUDA");
+  TORCH_CHECK(x.dim() == 4 && Bm.dim() == 4 && Cm.dim() == 4 && loga.dim() == 3, "scan ranks");
+  TORCH_CHECK(x.stride(3) == 1 && Bm.stride(3) == 1 && Cm.stride(3) == 1, "scan inner dims must be contiguous");
+  TORCH_CHECK(Bm.strides() == Cm.strides(), "B and C must share strides");
+  TORCH_CHECK(gamma.strides() == loga.strides(), "gamma/loga strides");
+  oxi::SsmScanIO io{};
+  io.x = x.data_ptr<float>(); io.Bm = Bm.data_ptr<float>(); io.Cm = Cm.data_ptr<float>();
+  io.loga = loga.data_ptr<float>(); io.gamma = gamma.data_ptr<float>();
+  if (beta.has_value() && beta->defined()) {
+    TORCH_CHECK(beta->strides() == loga.strides(), "beta strides");
+    io.beta = beta->data_ptr<float>();
+  }
+  for (int i = 0; i < 3; ++i) {
+    io.xs[i] = x.stride(i);
+    io.bs[i] = Bm.stride(i);
+    io.ss[i] = loga.stride(i);
+  }
+  return io;
+}
+
+torch::Tensor ssm_scan_fwd(torch::Tensor x, torch::Tensor Bm, torch::Tensor Cm, torch::Tensor loga,
+                           torch::Tensor gamma, c10::optional<torch::Tensor> beta) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto io = scan_io(x, Bm, Cm, loga, gamma, beta);
+  auto y = torch::empty_strided(x.sizes(), x.strides(), x.options());
+  io.y = y.data_ptr<float>();
+  oxi::launch_ssm_scan(io, x.size(0), x.size(1), x.size(2), Bm.size(3), x.size(3), io.beta != nullptr, 0, stream());
+  return y;
+}
+
+// returns (dx, dB, dC, dgamma, dbeta); dB/dC have B's strides (a zero head stride sums over heads)
+std::vector<torch::Tensor> ssm_scan_bwd(torch::Tensor x, torch::Tensor Bm, torch::Tensor Cm, torch::Tensor loga,
+                                        torch::Tensor gamma, c10::optional<torch::Tensor> beta, torch::Tensor dy) {
+  c10::cuda::CUDAGuard g(x.device());
+  auto io = scan_io(x, Bm, Cm, loga, gamma, beta);
+  TORCH_CHECK(dy.strides() == x.strides() && dy.scalar_type() == torch::kFloat32, "dy must match x");
+  io.dy = dy.data_ptr<float>();
+  auto dx = torch::empty_strided(x.sizes(), x.strides(), x.options());
+  // gradient buffers with B's (possibly zero) strides: allocate the storage B spans
+  auto make_like = [&](const torch::Tensor& t) {
+    auto base = torch::zeros({t.size(0), t.size(1), t.stride(2) == 0 ? 1 : t.size(2), t.size(3)}, t.options());
+    return base.expand(t.sizes());
+  };
+  auto dB = make_like(Bm), dC = make_like(Cm);
+  TORCH_CHECK(dB.strides() == Bm.strides(), "B must be contiguous or a head-broadcast of a contiguous tensor");
+  auto dgam = torch::zeros_like(gamma);
+  torch::Tensor dbet;
+  io.dx = dx.data_ptr<float>(); io.dB = dB.data_ptr<float>(); io.dC = dC.data_ptr<float>();
+  io.dgamma = dgam.data_ptr<float>();
+  if (io.beta) {
+    dbet = torch::zeros_like(gamma);
+    io.dbeta = dbet.data_ptr<float>();
+  }
+  const bool two = io.beta != nullptr;
+  oxi::launch_ssm_scan(io, x.size(0), x.size(1), x.size(2), Bm.size(3), x.size(3), two, 1, stream());
+  oxi::launch_ssm_scan(io, x.size(0), x.size(1), x.size(2), Bm.size(3), x.size(3), two, 2, stream());
+  return {dx, dB, dC, dgam, dbet.defined() ? dbet : torch::Tensor()};
+}
+
+std::vector<torch::Tensor> mamba1_scan_fwd(torch::Tensor u, torch::Tensor delta, torch::Tensor A, torch::Tensor Bm,
+                                           torch::Tensor Cm, double clamp) {
+  c10::cuda::CUDAGuard g(u.device());
+  for (auto* t : {&u, &delta, &A, &Bm, &Cm})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous(), "mamba1 scan: f32 contiguous");
+  const int64_t B = u.size(0), S = u.size(1), D = u.size(2);
+  TORCH_CHECK(A.size(1) == 16 && Bm.size(2) == 16, "Mamba1 state size is 16");
+  auto y = torch::empty_like(u);
+  auto hs = torch::empty({B, S, D, 16}, u.options());
+  oxi::launch_mamba1_fwd(u.data_ptr<float>(), delta.data_ptr<float>(), A.data_ptr<float>(), Bm.data_ptr<float>(),
+                         Cm.data_ptr<float>(), y.data_ptr<float>(), hs.data_ptr<float>(), (int)B, (int)S, (int)D,
+                         (float)clamp, stream());
+  return {y, hs};
+}
+
+std::vector<torch::Tensor> mamba1_scan_bwd(torch::Tensor u, torch::Tensor delta, torch::Tensor A, torch::Tensor Bm,
+                                           torch::Tensor Cm, torch::Tensor hs, torch::Tensor dy, double clamp) {
+  c10::cuda::CUDAGuard g(u.device());
+  const int64_t B = u.size(0), S = u.size(1), D = u.size(2);
+  auto dyc = dy.contiguous();
+  auto du = torch::empty_like(u), ddelta = torch::empty_like(u);
+  auto dA = torch::zeros_like(A), dB = torch::zeros_like(Bm), dC = torch::zeros_like(Cm);
+  oxi::launch_mamba1_bwd(u.data_ptr<float>(), delta.data_ptr<float>(), A.data_ptr<float>(), Bm.data_ptr<float>(),
+                         Cm.data_ptr<float>(), hs.data_ptr<float>(), dyc.data_ptr<float>(), du.data_ptr<float>(),
+                         ddelta.data_ptr<float>(), dA.data_ptr<float>(), dB.data_ptr<float>(), dC.data_ptr<float>(),
+                         (int)B, (int)S, (int)D, (float)clamp, stream());
+  return {du, ddelta, dA, dB, dC};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -255,4 +485,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sqsum", &sqsum, "sum of squares (atomically added into out)");
   m.def("clip_coef", &clip_coef, "global-norm clip coefficient on device");
   m.def("adamw", &adamw, "flat multi-tensor AdamW (f32 master, bf16 copy)");
+  m.def("flash_fwd", &flash_fwd, "causal flash attention forward (tcgen05)");
+  m.def("flash_bwd", &flash_bwd, "causal flash attention backward (tcgen05)");
+  m.def("conv1d_fwd", &conv1d_fwd, "depthwise causal conv1d (+bias, +SiLU) forward");
+  m.def("conv1d_bwd", &conv1d_bwd, "depthwise causal conv1d backward");
+  m.def("ssm_scan_fwd", &ssm_scan_fwd, "Mamba2/3 selective scan forward");
+  m.def("ssm_scan_bwd", &ssm_scan_bwd, "Mamba2/3 selective scan backward");
+  m.def("mamba1_scan_fwd", &mamba1_scan_fwd, "Mamba1 selective scan forward (saves states)");
+  m.def("mamba1_scan_bwd", &mamba1_scan_bwd, "Mamba1 selective scan backward");
+  m.def("ipc_alloc", &ipc_alloc, "zeroed device buffer exportable over CUDA IPC");
+  m.def("ipc_open", &ipc_open, "map a peer's IPC buffer");
+  m.def("ipc_close", &ipc_close, "unmap a peer's IPC buffer");
+  m.def("pad_words", &pad_words, "int32 words of one signal pad");
+  m.def("grad_to_bf16", &grad_to_bf16, "f32 gradient -> bf16 NVLink payload");
+  m.def("rs_bucket", &rs_bucket, "P2P reduce-scatter of one gradient bucket");
+  m.def("norm_exchange", &norm_exchange, "cross-rank gradient norm and clip coefficient");
+  m.def("adamw_allgather", &adamw_allgather, "sharded AdamW + P2P bf16 parameter all-gather");
 }

@@ -1,0 +1,387 @@
+// Selective state-space scans on CUDA cores: the Mamba2 SSD recurrence, the
+// Mamba3 trapezoidal two-term recurrence, and the Mamba1 diagonal scan.
+//
+// Mamba2/3 (per batch b, head h; state H_t is N x P):
+//   H_t = alpha_t H_{t-1} + gamma_t B_t x_t^T + beta_t B_{t-1} x_{t-1}^T
+//   y_t = H_t^T C_t
+// Mamba2: alpha = exp(A dt), gamma = dt, beta = 0 (mamba2.rs:381-482).
+// Mamba3: alpha = exp(A dt), gamma = lambda dt, beta = (1 - lambda) dt alpha
+//         (mamba3.rs:638-752; B, C already normed/biased/rotated).
+// This is the exact recurrence the chunked SSD evaluates, so results do not
+// depend on the chunk size.
+//
+// One CTA of 8 warps per (b, h).  Warp w owns P/8 columns p of the state, lane
+// l owns rows n = l + 32 k (k < N/32): every thread holds (N/32) x (P/8)
+// state values in registers.  y_t[p] reduces over n with warp shuffles, so a
+// time step needs no block-level synchronisation.  Inputs of step t+1 are
+// loaded while step t computes.
+//
+// Backward (two kernels; no per-step state is stored):
+//   dC_t = H_t dy_t                                    (forward recompute)
+//   G_t = C_t dy_t^T + alpha_{t+1} G_{t+1}             (reverse adjoint scan)
+//   dx_t = gamma_t G_t^T B_t + beta_{t+1} G_{t+1}^T B_t
+//   dB_t = gamma_t G_t x_t + beta_{t+1} G_{t+1} x_t
+//   dgamma_t = <G_t, B_t x_t^T>,  dbeta_t = <G_t, B_{t-1} x_{t-1}^T>
+// d(log alpha_t) = <G_t, alpha_t H_{t-1}> is recovered outside the kernel
+// from q_t = <G_t, H_t> = <dy_t, y_t> + q_{t+1} - v_{t+1}, v = gamma dgamma +
+// beta dbeta, since <G_t, alpha_t H_{t-1}> = q_t - v_t.
+//
+// Mamba1 (mamba.rs:212-291): per channel d, state h (N = 16):
+//   h_t = exp(delta_t A_d) h_{t-1} + delta_t x_t B_t ;  y_t = C_t . h_t
+// one thread per (b, d); the backward reads the per-step states the forward
+// saved.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "host_util.h"
+#include "kernels_ssm.h"
+
+namespace oxi {
+namespace {
+
+constexpr int SCAN_WARPS = 8;
+
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+struct ScanArgs {
+  const float *x, *Bm, *Cm, *loga, *gamma, *beta, *dy;
+  float *y, *dx, *dB, *dC, *dgamma, *dbeta;
+  int Bsz, S, H;
+  // element strides (batch, time, head) of x/dx/y/dy [.., P] and B/C/dB/dC [.., N]
+  int64_t xs_b, xs_t, xs_h;
+  int64_t bs_b, bs_t, bs_h;
+  int64_t ss_b, ss_t, ss_h;  // scalars loga/gamma/beta/dgamma/dbeta [B, S, H]
+};
+
+// ---------------------------------------------------------------- forward
+template <int NL, int PW, bool TWO, bool DC>
+__global__ void __launch_bounds__(SCAN_WARPS * 32) ssm_scan_fwd_kernel(ScanArgs a) {
+  const int bh = blockIdx.x;
+  const int b = bh / a.H, h = bh % a.H;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int p0 = warp * PW;
+  const float* xb = a.x + b * a.xs_b + h * a.xs_h + p0;
+  const float* Bb = a.Bm + b * a.bs_b + h * a.bs_h + lane;
+  const float* Cb = a.Cm + b * a.bs_b + h * a.bs_h + lane;
+  const int64_t so = b * a.ss_b + h * a.ss_h;
+  float st[NL][PW];
+#pragma unroll
+  for (int i = 0; i < NL; ++i)
+#pragma unroll
+    for (int j = 0; j < PW; ++j) st[i][j] = 0.f;
+  float bprev[NL], xprev[PW];
+#pragma unroll
+  for (int i = 0; i < NL; ++i) bprev[i] = 0.f;
+#pragma unroll
+  for (int j = 0; j < PW; ++j) xprev[j] = 0.f;
+  // prefetched inputs of the current step
+  float bn[NL], cn[NL], xv[PW], la, ga, be;
+  auto load = [&](int t) {
+#pragma unroll
+    for (int i = 0; i < NL; ++i) {
+      bn[i] = Bb[t * a.bs_t + 32 * i];
+      cn[i] = Cb[t * a.bs_t + 32 * i];
+    }
+#pragma unroll
+    for (int j = 0; j < PW; ++j) xv[j] = xb[t * a.xs_t + j];
+    la = a.loga[so + t * a.ss_t];
+    ga = a.gamma[so + t * a.ss_t];
+    be = TWO ? a.beta[so + t * a.ss_t] : 0.f;
+  };
+  if (a.S > 0) load(0);
+  for (int t = 0; t < a.S; ++t) {
+    float cbn[NL], ccn[NL], cx[PW];
+#pragma unroll
+    for (int i = 0; i < NL; ++i) { cbn[i] = bn[i]; ccn[i] = cn[i]; }
+#pragma unroll
+    for (int j = 0; j < PW; ++j) cx[j] = xv[j];
+    const float al = __expf(la), g = ga, bt = be;
+    if (t + 1 < a.S) load(t + 1);
+    float ypart[PW];
+#pragma unroll
+    for (int j = 0; j < PW; ++j) ypart[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NL; ++i) {
+      const float gb = g * cbn[i];
+      const float bb = TWO ? bt * bprev[i] : 0.f;
+#pragma unroll
+      for (int j = 0; j < PW; ++j) {
+        float v = al * st[i][j] + gb * cx[j];
+        if (TWO) v += bb * xprev[j];
+        st[i][j] = v;
+        ypart[j] += ccn[i] * v;
+      }
+    }
+    if (DC) {
+      // dC_t[n] = sum_p H_t[n, p] dy_t[p]: this warp's partial over its p columns
+      const float* dyb = a.dy + b * a.xs_b + h * a.xs_h + p0 + t * a.xs_t;
+      float dyv[PW];
+#pragma unroll
+      for (int j = 0; j < PW; ++j) dyv[j] = dyb[j];
+#pragma unroll
+      for (int i = 0; i < NL; ++i) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < PW; ++j) s += st[i][j] * dyv[j];
+        atomicAdd(a.dC + b * a.bs_b + h * a.bs_h + t * a.bs_t + lane + 32 * i, s);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < PW; ++j) {
+        const float yv = warp_allsum(ypart[j]);
+        if (lane == j % 32) a.y[b * a.xs_b + h * a.xs_h + t * a.xs_t + p0 + j] = yv;
+      }
+    }
+    if (TWO) {
+#pragma unroll
+      for (int i = 0; i < NL; ++i) bprev[i] = cbn[i];
+#pragma unroll
+      for (int j = 0; j < PW; ++j) xprev[j] = cx[j];
+    }
+  }
+}
+
+// ------------------------------------------------------- reverse adjoint
+template <int NL, int PW, bool TWO>
+__global__ void __launch_bounds__(SCAN_WARPS * 32) ssm_scan_bwd_kernel(ScanArgs a) {
+  const int bh = blockIdx.x;
+  const int b = bh / a.H, h = bh % a.H;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int p0 = warp * PW;
+  const int64_t xo = b * a.xs_b + h * a.xs_h + p0;
+  const int64_t bo = b * a.bs_b + h * a.bs_h + lane;
+  const int64_t so = b * a.ss_b + h * a.ss_h;
+  float G[NL][PW];  // adjoint G_{t+1} on entry to step t
+#pragma unroll
+  for (int i = 0; i < NL; ++i)
+#pragma unroll
+    for (int j = 0; j < PW; ++j) G[i][j] = 0.f;
+  float al_next = 0.f, be_next = 0.f;  // alpha_{t+1}, beta_{t+1}
+  for (int t = a.S - 1; t >= 0; --t) {
+    float bn[NL], cn[NL], bp[NL], xv[PW], xp[PW], dyv[PW];
+#pragma unroll
+    for (int i = 0; i < NL; ++i) {
+      bn[i] = a.Bm[bo + t * a.bs_t + 32 * i];
+      cn[i] = a.Cm[bo + t * a.bs_t + 32 * i];
+      bp[i] = (TWO && t > 0) ? a.Bm[bo + (t - 1) * a.bs_t + 32 * i] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < PW; ++j) {
+      xv[j] = a.x[xo + t * a.xs_t + j];
+      xp[j] = (TWO && t > 0) ? a.x[xo + (t - 1) * a.xs_t + j] : 0.f;
+      dyv[j] = a.dy[xo + t * a.xs_t + j];
+    }
+    const float g = a.gamma[so + t * a.ss_t];
+    const float be = TWO ? a.beta[so + t * a.ss_t] : 0.f;
+    // terms with G_{t+1} (beta_{t+1}): contributions of x_t, B_t to u_{t+1}
+    float dxp[PW], dbn[NL];
+#pragma unroll
+    for (int j = 0; j < PW; ++j) dxp[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NL; ++i) dbn[i] = 0.f;
+    if (TWO) {
+#pragma unroll
+      for (int i = 0; i < NL; ++i)
+#pragma unroll
+        for (int j = 0; j < PW; ++j) {
+          dxp[j] += be_next * G[i][j] * bn[i];
+          dbn[i] += be_next * G[i][j] * xv[j];
+        }
+    }
+    // G_t = C_t dy_t^T + alpha_{t+1} G_{t+1}
+#pragma unroll
+    for (int i = 0; i < NL; ++i)
+#pragma unroll
+      for (int j = 0; j < PW; ++j) G[i][j] = cn[i] * dyv[j] + al_next * G[i][j];
+    float dg = 0.f, dbt = 0.f;
+#pragma unroll
+    for (int i = 0; i < NL; ++i) {
+      float sx = 0.f, sxp = 0.f;
+#pragma unroll
+      for (int j = 0; j < PW; ++j) {
+        sx += G[i][j] * xv[j];
+        if (TWO) sxp += G[i][j] * xp[j];
+        dxp[j] += g * G[i][j] * bn[i];
+      }
+      dbn[i] += g * sx;
+      dg += bn[i] * sx;
+      if (TWO) dbt += bp[i] * sxp;
+    }
+    // dx_t[p]: reduce over n (lanes); dB_t[n]: partial over this warp's p -> atomics
+#pragma unroll
+    for (int j = 0; j < PW; ++j) {
+      const float v = warp_allsum(dxp[j]);
+      if (lane == j % 32) a.dx[xo + t * a.xs_t + j] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < NL; ++i) atomicAdd(a.dB + bo + t * a.bs_t + 32 * i, dbn[i]);
+    dg = warp_allsum(dg);
+    if (TWO) dbt = warp_allsum(dbt);
+    if (lane == 0) {
+      atomicAdd(a.dgamma + so + t * a.ss_t, dg);
+      if (TWO) atomicAdd(a.dbeta + so + t * a.ss_t, dbt);
+    }
+    al_next = __expf(a.loga[so + t * a.ss_t]);
+    be_next = be;
+  }
+}
+
+// ---------------------------------------------------------------- Mamba1
+constexpr int M1N = 16;
+
+__global__ void mamba1_fwd_kernel(const float* __restrict__ u, const float* __restrict__ delta,
+                                  const float* __restrict__ A, const float* __restrict__ Bm,
+                                  const float* __restrict__ Cm, float* __restrict__ y, float* __restrict__ hs,
+                                  int Bsz, int S, int Dch, float clamp) {
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= (int64_t)Bsz * Dch) return;
+  const int b = (int)(id / Dch), d = (int)(id % Dch);
+  float h[M1N], Ad[M1N];
+#pragma unroll
+  for (int n = 0; n < M1N; ++n) {
+    h[n] = 0.f;
+    Ad[n] = A[d * M1N + n];
+  }
+  for (int t = 0; t < S; ++t) {
+    const int64_t r = (int64_t)b * S + t;
+    const float dl = delta[r * Dch + d], xv = u[r * Dch + d];
+    float acc = 0.f;
+#pragma unroll
+    for (int n = 0; n < M1N; ++n) {
+      float v = __expf(dl * Ad[n]) * h[n] + dl * xv * Bm[r * M1N + n];
+      if (clamp > 0.f) v = fminf(fmaxf(v, -clamp), clamp);
+      h[n] = v;
+      acc += v * Cm[r * M1N + n];
+      hs[(r * Dch + d) * M1N + n] = v;
+    }
+    y[r * Dch + d] = acc;
+  }
+}
+
+__global__ void mamba1_bwd_kernel(const float* __restrict__ u, const float* __restrict__ delta,
+                                  const float* __restrict__ A, const float* __restrict__ Bm,
+                                  const float* __restrict__ Cm, const float* __restrict__ hs,
+                                  const float* __restrict__ dy, float* __restrict__ du, float* __restrict__ ddelta,
+                                  float* __restrict__ dA, float* __restrict__ dB, float* __restrict__ dC, int Bsz,
+                                  int S, int Dch, float clamp) {
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= (int64_t)Bsz * Dch) return;
+  const int b = (int)(id / Dch), d = (int)(id % Dch);
+  float g[M1N], Ad[M1N], dAd[M1N];
+#pragma unroll
+  for (int n = 0; n < M1N; ++n) {
+    g[n] = 0.f;
+    Ad[n] = A[d * M1N + n];
+    dAd[n] = 0.f;
+  }
+  for (int t = S - 1; t >= 0; --t) {
+    const int64_t r = (int64_t)b * S + t;
+    const float dl = delta[r * Dch + d], xv = u[r * Dch + d], gy = dy[r * Dch + d];
+    float dxv = 0.f, ddl = 0.f;
+#pragma unroll
+    for (int n = 0; n < M1N; ++n) {
+      const float hn = hs[(r * Dch + d) * M1N + n];
+      const float hp = t > 0 ? hs[((r - 1) * Dch + d) * M1N + n] : 0.f;
+      const float cv = Cm[r * M1N + n], bv = Bm[r * M1N + n];
+      g[n] += gy * cv;
+      atomicAdd(&dC[r * M1N + n], gy * hn);
+      // clamp: gradient passes only where the state was not clipped
+      if (clamp > 0.f && (hn >= clamp || hn <= -clamp)) g[n] = 0.f;
+      const float e = __expf(dl * Ad[n]);
+      ddl += g[n] * (Ad[n] * e * hp + xv * bv);
+      dAd[n] += g[n] * dl * e * hp;
+      dxv += g[n] * dl * bv;
+      atomicAdd(&dB[r * M1N + n], g[n] * dl * xv);
+      g[n] *= e;  // propagate to h_{t-1}
+    }
+    du[r * Dch + d] = dxv;
+    ddelta[r * Dch + d] = ddl;
+  }
+#pragma unroll
+  for (int n = 0; n < M1N; ++n) atomicAdd(&dA[d * M1N + n], dAd[n]);
+}
+
+template <int NL, int PW>
+void dispatch_two(const ScanArgs& a, bool two, bool dc, cudaStream_t st) {
+  const dim3 grid(a.Bsz * a.H), block(SCAN_WARPS * 32);
+  if (dc) {
+    if (two) ssm_scan_fwd_kernel<NL, PW, true, true><<<grid, block, 0, st>>>(a);
+    else ssm_scan_fwd_kernel<NL, PW, false, true><<<grid, block, 0, st>>>(a);
+  } else {
+    if (two) ssm_scan_fwd_kernel<NL, PW, true, false><<<grid, block, 0, st>>>(a);
+    else ssm_scan_fwd_kernel<NL, PW, false, false><<<grid, block, 0, st>>>(a);
+  }
+}
+
+template <int NL, int PW>
+void dispatch_bwd(const ScanArgs& a, bool two, cudaStream_t st) {
+  const dim3 grid(a.Bsz * a.H), block(SCAN_WARPS * 32);
+  if (two) ssm_scan_bwd_kernel<NL, PW, true><<<grid, block, 0, st>>>(a);
+  else ssm_scan_bwd_kernel<NL, PW, false><<<grid, block, 0, st>>>(a);
+}
+
+#define OXI_SCAN_SHAPES(X) \
+  X(1, 2) X(2, 2) X(4, 2) X(1, 8) X(2, 8) X(4, 8) X(1, 16) X(2, 16) X(4, 16) X(1, 32) X(2, 32) X(4, 32) X(1, 4) X(2, 4) X(4, 4)
+
+bool run_fwd(int N, int P, const ScanArgs& a, bool two, bool dc, cudaStream_t st) {
+  const int NL = N / 32, PW = P / SCAN_WARPS;
+#define X(nl, pw) \
+  if (NL == nl && PW == pw) { dispatch_two<nl, pw>(a, two, dc, st); return true; }
+  OXI_SCAN_SHAPES(X)
+#undef X
+  return false;
+}
+
+bool run_bwd(int N, int P, const ScanArgs& a, bool two, cudaStream_t st) {
+  const int NL = N / 32, PW = P / SCAN_WARPS;
+#define X(nl, pw) \
+  if (NL == nl && PW == pw) { dispatch_bwd<nl, pw>(a, two, st); return true; }
+  OXI_SCAN_SHAPES(X)
+#undef X
+  return false;
+}
+
+}  // namespace
+
+void launch_ssm_scan(const SsmScanIO& io, int Bsz, int S, int H, int N, int P, bool two, int mode,
+                     cudaStream_t st) {
+  OXI_CHECK(N % 32 == 0 && P % SCAN_WARPS == 0, "scan: state size must be a multiple of 32 and head dim of 8");
+  if (!Bsz || !S || !H) return;
+  ScanArgs a;
+  a.x = io.x; a.Bm = io.Bm; a.Cm = io.Cm; a.loga = io.loga; a.gamma = io.gamma; a.beta = io.beta; a.dy = io.dy;
+  a.y = io.y; a.dx = io.dx; a.dB = io.dB; a.dC = io.dC; a.dgamma = io.dgamma; a.dbeta = io.dbeta;
+  a.Bsz = Bsz; a.S = S; a.H = H;
+  a.xs_b = io.xs[0]; a.xs_t = io.xs[1]; a.xs_h = io.xs[2];
+  a.bs_b = io.bs[0]; a.bs_t = io.bs[1]; a.bs_h = io.bs[2];
+  a.ss_b = io.ss[0]; a.ss_t = io.ss[1]; a.ss_h = io.ss[2];
+  bool ok;
+  if (mode == 0) ok = run_fwd(N, P, a, two, false, st);        // y
+  else if (mode == 1) ok = run_fwd(N, P, a, two, true, st);    // dC
+  else ok = run_bwd(N, P, a, two, st);                         // dx, dB, dgamma, dbeta
+  OXI_CHECK(ok, "scan: unsupported (state, head_dim) = (", N, ", ", P, ")");
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_mamba1_fwd(const float* u, const float* delta, const float* A, const float* Bm, const float* Cm, float* y,
+                       float* hs, int Bsz, int S, int Dch, float clamp, cudaStream_t st) {
+  const int64_t n = (int64_t)Bsz * Dch;
+  if (!n || !S) return;
+  mamba1_fwd_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(u, delta, A, Bm, Cm, y, hs, Bsz, S, Dch, clamp);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_mamba1_bwd(const float* u, const float* delta, const float* A, const float* Bm, const float* Cm,
+                       const float* hs, const float* dy, float* du, float* ddelta, float* dA, float* dB, float* dC,
+                       int Bsz, int S, int Dch, float clamp, cudaStream_t st) {
+  const int64_t n = (int64_t)Bsz * Dch;
+  if (!n || !S) return;
+  mamba1_bwd_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(u, delta, A, Bm, Cm, hs, dy, du, ddelta, dA, dB, dC,
+                                                                 Bsz, S, Dch, clamp);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace oxi

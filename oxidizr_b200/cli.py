@@ -179,14 +179,19 @@ def run_train(args, argv: List[str]) -> int:
     say(f"Initializing model with {m.estimate_params_banner()} parameters...")
     ep_group = group if (m.ep_size and m.ep_size > 1 and world > 1) else None
     model = build_model(m, device=device, ep_group=ep_group)
-    flat = FlatParams(list(model.named_parameters()), device)
     ocfg = AdamWConfig(lr=t.learning_rate,
                        weight_decay=t.weight_decay if t.weight_decay is not None else 0.01,
                        max_grad_norm=t.max_grad_norm if t.max_grad_norm is not None else 1.0)
-    if world > 1:
+    if world > 1 and backend == "fused" and device.type == "cuda":
+        from .parallel.fused_ar import FusedDDPAdamW
+        opt = FusedDDPAdamW(list(model.named_parameters()), ocfg, device, group=group)
+        flat = None
+    elif world > 1:
         from .parallel.ddp import DDPAdamW
+        flat = FlatParams(list(model.named_parameters()), device)
         opt = DDPAdamW(flat, ocfg, backend=backend if backend != "single" else "nccl", group=group)
     else:
+        flat = FlatParams(list(model.named_parameters()), device)
         opt = AdamW(flat, ocfg)
 
     # ------------------------------------------------------------ resume
@@ -236,7 +241,8 @@ def run_train(args, argv: List[str]) -> int:
     if resume_path:
         say(f"Loading checkpoint from: {resume_path}")
         C.load_weights(model, resume_path)
-        flat.master.copy_(flat.flat.float()) if flat.master is not flat.flat else None
+        if flat is not None and flat.master is not flat.flat:
+            flat.master.copy_(flat.flat.float())
         meta = C.load_optimizer_sidecar(opt, resume_path)
         if meta and "data_cursor" in meta:
             cursor = int(meta["data_cursor"])

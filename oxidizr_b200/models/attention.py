@@ -43,10 +43,7 @@ class GQAAttention(RefModule):
         cos, sin = RopeCache.get(self.hd, S, self.theta, h.device)
         qc, kc = self.nh * self.hd, self.kvh * self.hd
         qkv = api.qkv_rope(h, self.w_qkv, cos, sin, self.hd, qc, kc)
-        q = qkv[..., :qc].view(B, S, self.nh, self.hd)
-        k = qkv[..., qc:qc + kc].view(B, S, self.kvh, self.hd)
-        v = qkv[..., qc + kc:].view(B, S, self.kvh, self.hd)
-        o = api.attention(q, k, v, self.scale, causal=True).reshape(B, S, qc)
+        o = api.attention_qkv(qkv, self.nh, self.kvh, self.hd, self.scale, causal=True)
         return api.linear(o, self.o_proj, resid=resid)
 
     def export_ref(self, prefix, out):

@@ -208,10 +208,6 @@ class Mamba2Mixer(RefModule):
         gn = self.g * self.N
         Bm = xBC[..., self.I:self.I + gn].reshape(B, S, self.g, self.N)
         Cm = xBC[..., self.I + gn:].reshape(B, S, self.g, self.N)
-        rep = self.Hs // self.g
-        if rep > 1:
-            Bm = Bm.repeat_interleave(rep, dim=2)
-            Cm = Cm.repeat_interleave(rep, dim=2)
         dtv = _softplus_dt(dt, self.dt_bias)
         y = ssm.ssd(x, dtv, self.A(), Bm, Cm, self.chunk, diag_only_g=self.compat)
         y = y.float() + x.float() * self.D.float()[:, None]

@@ -91,6 +91,11 @@ def attention(q, k, v, scale: float, causal: bool = True):
     return _att(q, k, v, scale, causal)
 
 
+def attention_qkv(qkv, Hq: int, Hk: int, D: int, scale: float, causal: bool = True):
+    from .attention import attention_qkv as _aq
+    return _aq(qkv, Hq, Hk, D, scale, causal)
+
+
 def linear_cross_entropy(x, w, targets, ignore_index: int = -100):
     if _native(x):
         from .fused import LinearCrossEntropy

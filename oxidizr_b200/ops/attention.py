@@ -14,11 +14,28 @@ from . import reference as R
 
 def _has_native_fa() -> bool:
     from ._C import ext
-    return hasattr(ext(), "flash_fwd")
+    e = ext()
+    return hasattr(e, "flash_fwd") and hasattr(e, "flash_bwd")
+
+
+def native_ok(D: int, Dv: int = None) -> bool:
+    return (Dv is None or Dv == D) and D in (64, 128) and _has_native_fa()
+
+
+def attention_qkv(qkv, Hq: int, Hk: int, D: int, scale: float, causal: bool = True):
+    """Attention over the fused [B, S, (Hq + 2 Hk) * D] projection; returns [B, S, Hq * D]."""
+    if qkv.is_cuda and qkv.dtype == torch.bfloat16 and native_ok(D):
+        from .flash import FlashAttentionQKV
+        return FlashAttentionQKV.apply(qkv, Hq, Hk, D, scale, causal)
+    B, S, _ = qkv.shape
+    q = qkv[..., :Hq * D].view(B, S, Hq, D)
+    k = qkv[..., Hq * D:(Hq + Hk) * D].view(B, S, Hk, D)
+    v = qkv[..., (Hq + Hk) * D:].view(B, S, Hk, D)
+    return attention(q, k, v, scale, causal).reshape(B, S, Hq * D)
 
 
 def attention_cuda(q, k, v, scale: float, causal: bool = True):
-    if _has_native_fa():
+    if native_ok(q.shape[-1], v.shape[-1]) and q.dtype == torch.bfloat16:
         from .flash import FlashAttention
         return FlashAttention.apply(q, k, v, scale, causal)
     # library attention, used only until the native kernel is present

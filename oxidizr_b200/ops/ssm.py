@@ -24,26 +24,45 @@ def causal_conv1d_cuda(x, w, b, act: bool = True):
     return R.causal_conv1d(x.float(), w.float(), None if b is None else b.float(), act).to(x.dtype)
 
 
+def _expand_heads(t, H):
+    G = t.shape[2]
+    return t if G == H else t.repeat_interleave(H // G, dim=2)
+
+
+def _scan_ok(x, N):
+    return x.is_cuda and _ext_has("ssm_scan_fwd") and N % 32 == 0 and x.shape[-1] % 8 == 0 and \
+        (N // 32) in (1, 2, 4) and (x.shape[-1] // 8) in (1, 2, 4, 8, 16, 32)
+
+
 def ssd(x, dt, A, Bm, Cm, chunk: int, diag_only_g: bool = False):
-    """Mamba2 SSD core (no D skip).  x [B,S,H,P], dt [B,S,H], A [H], B/C [B,S,H,N]."""
-    if x.is_cuda and not diag_only_g and _ext_has("ssd_fwd"):
-        from .ssm_kernels import SSD
-        return SSD.apply(x, dt, A, Bm, Cm, chunk)
+    """Mamba2 SSD core (no D skip), f32 result.  x [B,S,H,P], dt [B,S,H],
+    A [H], B/C [B,S,G,N] with G dividing H (grouped B/C are shared by heads)."""
+    H, N = x.shape[2], Bm.shape[-1]
+    if not diag_only_g and _scan_ok(x, N):
+        from .ssm_kernels import SSMScan
+        dtf = dt.float()
+        return SSMScan.apply(x, Bm, Cm, A.float()[None, None, :] * dtf, dtf, None)
     f = lambda t: t.float()
-    return R.ssd_chunked(f(x), f(dt), f(A), f(Bm), f(Cm), chunk, diag_only_g).to(x.dtype)
+    return R.ssd_chunked(f(x), f(dt), f(A), f(_expand_heads(Bm, H)), f(_expand_heads(Cm, H)), chunk, diag_only_g)
 
 
 def mamba3_scan(x, dt, A, Bm, Cm, lam, chunk: int, compat: bool = False):
-    if x.is_cuda and not compat and _ext_has("ssd_fwd"):
-        from .ssm_kernels import Mamba3Scan
-        return Mamba3Scan.apply(x, dt, A, Bm, Cm, lam, chunk)
+    """Trapezoidal two-term scan (no D skip), f32 result.  B/C [B,S,H,N] per head."""
+    N = Bm.shape[-1]
+    if not compat and _scan_ok(x, N):
+        from .ssm_kernels import SSMScan
+        dtf, lamf = dt.float(), lam.float()
+        loga = A.float()[None, None, :] * dtf
+        beta = (1 - lamf) * dtf * torch.exp(loga)
+        return SSMScan.apply(x, Bm, Cm, loga, lamf * dtf, beta)
     f = lambda t: t.float()
-    return R.mamba3_scan(f(x), f(dt), f(A), f(Bm), f(Cm), f(lam), chunk, compat).to(x.dtype)
+    return R.mamba3_scan(f(x), f(dt), f(A), f(Bm), f(Cm), f(lam), chunk, compat)
 
 
 def selective_scan(u, delta, A, Bm, Cm, clamp=None):
-    if u.is_cuda and _ext_has("selective_scan_fwd"):
-        from .ssm_kernels import SelectiveScan
-        return SelectiveScan.apply(u, delta, A, Bm, Cm, clamp)
+    """Mamba1 scan, f32 result."""
+    if u.is_cuda and _ext_has("mamba1_scan_fwd") and A.shape[-1] == 16:
+        from .ssm_kernels import Mamba1Scan
+        return Mamba1Scan.apply(u, delta, A, Bm, Cm, clamp)
     f = lambda t: t.float()
-    return R.selective_scan(f(u), f(delta), f(A), f(Bm), f(Cm), clamp).to(u.dtype)
+    return R.selective_scan(f(u), f(delta), f(A), f(Bm), f(Cm), clamp)

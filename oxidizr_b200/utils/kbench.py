@@ -82,12 +82,87 @@ def bench_gemm(shapes, iters=20):
     return rows
 
 
+def bench_attn(B=8, S=2048, Hq=16, Hk=8, D=128, iters=20):
+    """Causal attention fwd and fwd+bwd vs torch SDPA; FLOPs count the causal half."""
+    import math
+    from ..ops.flash import FlashAttentionQKV
+    peaks = measured_peaks()
+    N = (Hq + 2 * Hk) * D
+    qkv = torch.randn(B, S, N, device="cuda").bfloat16().requires_grad_()
+    scale = 1.0 / math.sqrt(D)
+    flops_f = 4.0 * B * Hq * S * S * D / 2
+    def ours_f():
+        with torch.no_grad():
+            FlashAttentionQKV.apply(qkv, Hq, Hk, D, scale, True)
+    do = torch.randn(B, S, Hq * D, device="cuda").bfloat16()
+    def ours_fb():
+        o = FlashAttentionQKV.apply(qkv, Hq, Hk, D, scale, True)
+        o.backward(do)
+    q = qkv[..., :Hq * D].view(B, S, Hq, D).transpose(1, 2)
+    k = qkv[..., Hq * D:(Hq + Hk) * D].view(B, S, Hk, D).transpose(1, 2)
+    v = qkv[..., (Hq + Hk) * D:].view(B, S, Hk, D).transpose(1, 2)
+    sd = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale,
+                                                                   enable_gqa=Hk != Hq)
+    def ref_f():
+        with torch.no_grad():
+            sd()
+    def ref_fb():
+        o = sd()
+        o.backward(do.view(B, S, Hq, D).transpose(1, 2))
+    res = {}
+    for name, fn, fl in (("ours_fwd", ours_f, flops_f), ("ours_fwd_bwd", ours_fb, 3.5 * flops_f),
+                         ("sdpa_fwd", ref_f, flops_f), ("sdpa_fwd_bwd", ref_fb, 3.5 * flops_f)):
+        ms = time_fn(fn, iters)
+        res[name] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
+                     "frac_of_peak": round(fl / ms / 1e9 / peaks["bf16_tflops"], 3)}
+    out = {"B": B, "S": S, "Hq": Hq, "Hk": Hk, "D": D, "peak_source": peaks["source"], **res}
+    print(json.dumps(out), flush=True)
+    return out
+
+
+def run_once(what: str):
+    """Launch one kernel of a small case a few times (targets for ncu captures)."""
+    import math
+    torch.manual_seed(0)
+    if what in ("fa_fwd", "fa_bwd"):
+        from ..ops.flash import FlashAttentionQKV
+        B, S, Hq, Hk, D = 1, 2048, 16, 8, 128
+        qkv = torch.randn(B, S, (Hq + 2 * Hk) * D, device="cuda").bfloat16().requires_grad_()
+        for _ in range(3):
+            o = FlashAttentionQKV.apply(qkv, Hq, Hk, D, 1.0 / math.sqrt(D), True)
+            if what == "fa_bwd":
+                o.backward(torch.ones_like(o))
+    elif what == "gemm":
+        from ..ops.gemm import mm
+        a = torch.randn(8192, 4096, device="cuda").bfloat16()
+        b = torch.randn(8192, 4096, device="cuda").bfloat16()
+        for _ in range(3):
+            mm(a, b)
+    elif what == "gemm_dw":
+        from ..ops.gemm import mm
+        a = torch.randn(16384, 2048, device="cuda").bfloat16()
+        b = torch.randn(16384, 2048, device="cuda").bfloat16()
+        out = torch.zeros(2048, 2048, device="cuda")
+        for _ in range(3):
+            mm(a, b, a_t=True, b_t=True, out=out, beta=1.0)
+    torch.cuda.synchronize()
+    print(f"{what}: ok")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm"])
+    ap.add_argument("what", choices=["gemm", "attn", "once"])
+    ap.add_argument("--kernel", default="fa_fwd", help="for 'once': fa_fwd | fa_bwd | gemm | gemm_dw")
     ap.add_argument("--shapes", nargs="*", default=None, help="M,N,K[,layout] with layout nn|nt|tt")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)
+    if args.what == "once":
+        run_once(args.kernel)
+        return
+    if args.what == "attn":
+        bench_attn(iters=args.iters)
+        bench_attn(D=64, Hq=32, Hk=8, iters=args.iters)
+        return
     if args.what == "gemm":
         if args.shapes:
             shapes = []
