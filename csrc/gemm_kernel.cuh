@@ -67,6 +67,15 @@ struct GemmParams {
   int rope_seq, rope_hd, rope_q_cols, rope_k_cols;  // q columns [0,q), k columns [q, q+k)
   int vec_ok;              // output rows are 16-byte aligned
   int* status;
+  // grouped (MoE) modes: 0 none; 1 group-M (A rows split into expert segments,
+  // B rows offset by expert); 2 group-K (K split into expert segments, one
+  // output matrix per expert).  seg_off[0..n_groups] are 128-aligned row
+  // offsets of the segments, on the device.
+  int group_mode;
+  int n_groups;
+  const int* seg_off;
+  int64_t b_group_stride;  // B tensor-map rows per expert
+  int64_t d_group_stride;  // output elements per expert (group-K)
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
@@ -86,6 +95,45 @@ __device__ __forceinline__ void unit_krange(int t, const GemmParams& p, int num_
   const int sp = t % p.splits;
   kb0 = sp * p.kb_per_split;
   kb1 = min(num_kb, kb0 + p.kb_per_split);
+}
+
+struct Unit {
+  int tm, tn, kb0, kb1, e;
+  bool valid;
+};
+
+// Work unit t -> output tile, k-block range, expert; identical in every role.
+__device__ __forceinline__ Unit unit_info(int t, const GemmParams& p, int num_kb) {
+  Unit u;
+  u.e = 0;
+  if (p.group_mode == 0) {
+    tile_coords(t, p, u.tm, u.tn);
+    unit_krange(t, p, num_kb, u.kb0, u.kb1);
+    u.valid = true;
+  } else if (p.group_mode == 1) {
+    u.tm = t / p.tiles_n;
+    u.tn = t % p.tiles_n;
+    u.kb0 = 0;
+    u.kb1 = num_kb;
+    const int m0 = u.tm * BM;
+    u.valid = m0 < __ldg(p.seg_off + p.n_groups);
+    if (u.valid) {
+      int lo = 0, hi = p.n_groups;  // last e with seg_off[e] <= m0
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(p.seg_off + mid) <= m0) lo = mid; else hi = mid;
+      }
+      u.e = lo;
+    }
+  } else {
+    const int per = p.tiles_m * p.tiles_n;
+    u.e = t / per;
+    tile_coords(t % per, p, u.tm, u.tn);
+    u.kb0 = __ldg(p.seg_off + u.e) / BK;
+    u.kb1 = __ldg(p.seg_off + u.e + 1) / BK;
+    u.valid = u.kb1 > u.kb0;
+  }
+  return u;
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
@@ -179,10 +227,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int s = 0; s < STAGES; ++s) { armed[s] = false; armed_parity[s] = 0; }
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        int tm, tn, kb0, kb1;
-        tile_coords(t, p, tm, tn);
-        unit_krange(t, p, num_kb, kb0, kb1);
-        const int m0 = tm * BM, n0 = tn * BN;
+        const Unit un = unit_info(t, p, num_kb);
+        if (!un.valid) continue;
+        const int kb0 = un.kb0, kb1 = un.kb1;
+        const int m0 = un.tm * BM, n0 = un.tn * BN;
+        const int boff = (int)(un.e * p.b_group_stride);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
@@ -198,10 +247,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             tma_load_2d(a_dst + BK * 128, &tmA, &full[stage], m0 + 64, k0);
           }
           if (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0 + boff);
           } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) tma_load_2d(b_dst + q * BK * 128, &tmB, &full[stage], n0 + 64 * q, k0);
+            for (int q = 0; q < 4; ++q)
+              tma_load_2d(b_dst + q * BK * 128, &tmB, &full[stage], n0 + 64 * q, k0 + boff);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -223,11 +273,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const Unit un = unit_info(t, p, num_kb);
+        if (!un.valid) continue;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        int kb0, kb1;
-        unit_krange(t, p, num_kb, kb0, kb1);
+        const int kb0 = un.kb0, kb1 = un.kb1;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
@@ -261,9 +312,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint32_t acc_phase = 0;
     const bool vec = p.vec_ok != 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(t, p, tm, tn);
-      const int m0 = tm * BM, n0 = tn * BN;
+      const Unit un = unit_info(t, p, num_kb);
+      if (!un.valid) continue;
+      const int tn = un.tn;
+      const int m0 = un.tm * BM, n0 = un.tn * BN;
+      void* Dp = p.D;
+      if (p.group_mode == 2) Dp = (char*)p.D + un.e * p.d_group_stride * (EPI == EPI_F32 ? 4 : 2);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
@@ -284,7 +338,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
           if constexpr (EPI == EPI_BF16) {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col;
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
             if (p.R) {
               float rr[32];
               load_bf16_row(p.R + (int64_t)row * p.ldr + col, rr, nvalid, vec);
@@ -293,7 +347,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
             store_bf16_row(dst, v, nvalid, vec);
           } else if constexpr (EPI == EPI_F32) {
-            float* dst = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col;
+            float* dst = reinterpret_cast<float*>(Dp) + (int64_t)row * p.ldd + col;
             if (p.splits > 1) {
               // split-K partial sums accumulate into the output (beta == 1)
               if (vec && nvalid >= 32) {
@@ -333,7 +387,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               du[j] = v[j] * sg;
               dg[j] = v[j] * u[j] * s * (1.f + g[j] * (1.f - s));
             }
-            __nv_bfloat16* dgp = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + blk * 256 + off;
+            __nv_bfloat16* dgp = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + blk * 256 + off;
             store_bf16_row(dgp, dg, nvalid, vec);
             store_bf16_row(dgp + 128, du, nvalid, vec);
           }
@@ -357,7 +411,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             u[j] = __uint_as_float(ru[j]);
             h[j] = silu_f(g[j]) * u[j];
           }
-          store_bf16_row(reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + hcol, h, nvalid, vec);
+          store_bf16_row(reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + hcol, h, nvalid, vec);
           if (p.D2) {
             __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.D2) + (int64_t)row * p.ldd2 + n0 + c * 32;
             store_bf16_row(gu, g, nvalid, vec);
@@ -397,7 +451,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               if (col + j == tgt) tv = v[j];
             p.tgt_logit[row] = tv;
           }
-          if (p.D) store_bf16_row(reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col, v, nvalid, vec);
+          if (Dp) store_bf16_row(reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col, v, nvalid, vec);
         }
         if (row_ok) {
           p.part_max[(int64_t)row * p.tiles_n + tn] = run_max;
@@ -437,7 +491,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               x2[j] = b * cj + a * sj;
             }
           }
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
           store_bf16_row(dst, x1, nvalid, vec);
           const int nvalid2 = min(32, p.N - (col + half));
           if (nvalid2 > 0) store_bf16_row(dst + half, x2, nvalid2, vec);

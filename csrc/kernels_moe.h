@@ -1,0 +1,20 @@
+// Launchers of the MoE kernels (moe.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+
+namespace oxi {
+void launch_moe_permute(const void* x, int64_t ldx, const int64_t* topi, int64_t T, int k, int E, int H, int* counts,
+                        int* seg_off, int* cursor, int* pos, void* xp, cudaStream_t st);
+void launch_moe_zero_pad(const int* seg_off, const int* counts, int E, void* m, int H, cudaStream_t st);
+void launch_moe_combine(const void* yp, const int* pos, const float* w, int64_t T, int k, int H, const void* resid,
+                        void* y, cudaStream_t st);
+void launch_moe_combine_bwd(const void* dy, const void* yp, const int* pos, const float* w, int64_t T, int k, int H,
+                            void* dyp, float* dw, cudaStream_t st);
+void launch_moe_gather_sum(const void* dxp, const int* pos, int64_t T, int k, int H, void* dx, cudaStream_t st);
+void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& b, bool b_mn, int n_groups,
+                         const int* seg_off, int64_t group_rows_b, void* out, int64_t ldo, void* out2, int64_t ldo2,
+                         const void* aux, int64_t ldaux, int* status, cudaStream_t st);
+}  // namespace oxi

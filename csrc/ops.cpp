@@ -9,6 +9,7 @@
 #include "kernels_attn.h"
 #include "kernels_comm.h"
 #include "kernels_ssm.h"
+#include "kernels_moe.h"
 
 using oxi::Mat;
 
@@ -466,6 +467,81 @@ std::vector<torch::Tensor> mamba1_scan_bwd(torch::Tensor u, torch::Tensor delta,
   return {du, ddelta, dA, dB, dC};
 }
 
+// ------------------------------------------------------------ MoE
+// returns (counts [E] i32, seg_off [E+1] i32, pos [T*k] i32, xp [rows_cap, H] bf16)
+std::vector<torch::Tensor> moe_permute(torch::Tensor x, torch::Tensor topi, int64_t E, int64_t rows_cap) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "moe x");
+  TORCH_CHECK(topi.scalar_type() == torch::kInt64 && topi.is_contiguous() && topi.dim() == 2, "topi int64 [T,k]");
+  const int64_t T = topi.size(0), k = topi.size(1), H = x.size(1);
+  auto io = torch::TensorOptions().dtype(torch::kInt32).device(x.device());
+  auto counts = torch::empty({E}, io), seg = torch::empty({E + 1}, io), cursor = torch::empty({E}, io);
+  auto pos = torch::empty({T * k}, io);
+  auto xp = torch::empty({rows_cap, H}, x.options());
+  oxi::launch_moe_permute(x.data_ptr(), x.stride(0), topi.data_ptr<int64_t>(), T, (int)k, (int)E, (int)H,
+                          counts.data_ptr<int>(), seg.data_ptr<int>(), cursor.data_ptr<int>(), pos.data_ptr<int>(),
+                          xp.data_ptr(), stream());
+  return {counts, seg, pos, xp};
+}
+
+void moe_zero_pad(torch::Tensor seg, torch::Tensor counts, torch::Tensor m) {
+  c10::cuda::CUDAGuard g(m.device());
+  oxi::launch_moe_zero_pad(seg.data_ptr<int>(), counts.data_ptr<int>(), (int)counts.numel(), m.data_ptr(),
+                           (int)m.size(1), stream());
+}
+
+torch::Tensor moe_combine(torch::Tensor yp, torch::Tensor pos, torch::Tensor w, int64_t T, int64_t k,
+                          c10::optional<torch::Tensor> resid) {
+  c10::cuda::CUDAGuard g(yp.device());
+  const int64_t H = yp.size(1);
+  auto y = torch::empty({T, H}, yp.options());
+  const void* rp = nullptr;
+  if (resid.has_value() && resid->defined()) {
+    TORCH_CHECK(resid->is_contiguous() && resid->numel() == T * H, "resid");
+    rp = resid->data_ptr();
+  }
+  oxi::launch_moe_combine(yp.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(), T, (int)k, (int)H, rp,
+                          y.data_ptr(), stream());
+  return y;
+}
+
+std::vector<torch::Tensor> moe_combine_bwd(torch::Tensor dy, torch::Tensor yp, torch::Tensor pos, torch::Tensor w,
+                                           int64_t k) {
+  c10::cuda::CUDAGuard g(dy.device());
+  const int64_t T = dy.size(0), H = dy.size(1);
+  auto dyp = torch::empty_like(yp);
+  auto dw = torch::empty({T, k}, w.options());
+  oxi::launch_moe_combine_bwd(dy.data_ptr(), yp.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(), T, (int)k,
+                              (int)H, dyp.data_ptr(), dw.data_ptr<float>(), stream());
+  return {dyp, dw};
+}
+
+torch::Tensor moe_gather_sum(torch::Tensor dxp, torch::Tensor pos, int64_t T, int64_t k) {
+  c10::cuda::CUDAGuard g(dxp.device());
+  const int64_t H = dxp.size(1);
+  auto dx = torch::empty({T, H}, dxp.options());
+  oxi::launch_moe_gather_sum(dxp.data_ptr(), pos.data_ptr<int>(), T, (int)k, (int)H, dx.data_ptr(), stream());
+  return dx;
+}
+
+void gemm_grouped(int64_t mode, int64_t epi, torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, int64_t n_groups,
+                  torch::Tensor seg_off, int64_t group_rows_b, torch::Tensor out, c10::optional<torch::Tensor> out2,
+                  c10::optional<torch::Tensor> aux, torch::Tensor status) {
+  c10::cuda::CUDAGuard g(a.device());
+  Mat ma = bf16_mat(a, "a"), mb = bf16_mat(b, "b");
+  TORCH_CHECK(seg_off.scalar_type() == torch::kInt32 && seg_off.numel() == n_groups + 1, "seg_off");
+  TORCH_CHECK(out.stride(-1) == 1, "out inner stride");
+  void* o2 = nullptr;
+  int64_t ld2 = 0;
+  if (out2.has_value() && out2->defined()) { o2 = out2->data_ptr(); ld2 = out2->stride(0); }
+  const void* ax = nullptr;
+  int64_t ldax = 0;
+  if (aux.has_value() && aux->defined()) { ax = aux->data_ptr(); ldax = aux->stride(0); }
+  const int64_t ldo = out.stride(out.dim() - 2);
+  oxi::launch_gemm_grouped((int)mode, (int)epi, ma, a_mn, mb, b_mn, (int)n_groups, seg_off.data_ptr<int>(),
+                           group_rows_b, out.data_ptr(), ldo, o2, ld2, ax, ldax, status_ptr(status), stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -493,6 +569,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ssm_scan_bwd", &ssm_scan_bwd, "Mamba2/3 selective scan backward");
   m.def("mamba1_scan_fwd", &mamba1_scan_fwd, "Mamba1 selective scan forward (saves states)");
   m.def("mamba1_scan_bwd", &mamba1_scan_bwd, "Mamba1 selective scan backward");
+  m.def("moe_permute", &moe_permute, "MoE counting-sort permutation into aligned expert segments");
+  m.def("moe_zero_pad", &moe_zero_pad, "zero the padding rows of expert segments");
+  m.def("moe_combine", &moe_combine, "weighted combine of expert outputs (+ residual)");
+  m.def("moe_combine_bwd", &moe_combine_bwd, "backward of the combine");
+  m.def("moe_gather_sum", &moe_gather_sum, "sum permuted rows back per token");
+  m.def("gemm_grouped", &gemm_grouped, "grouped (per-expert) tcgen05 GEMM");
   m.def("ipc_alloc", &ipc_alloc, "zeroed device buffer exportable over CUDA IPC");
   m.def("ipc_open", &ipc_open, "map a peer's IPC buffer");
   m.def("ipc_close", &ipc_close, "unmap a peer's IPC buffer");

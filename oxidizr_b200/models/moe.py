@@ -32,6 +32,13 @@ from .attention import SwiGLU
 from .common import RefModule, _assign, interleave_gu, normal_, split_gu, take
 
 
+def _grouped_ok(x, w_gu) -> bool:
+    if not x.is_cuda:
+        return False
+    from ..ops.moe_kernels import grouped_ok
+    return grouped_ok(x, w_gu)
+
+
 def route(logits: torch.Tensor, k: int):
     """Top-k routing: returns (probs [T,E] f32, top_idx [T,k] int64, top_w [T,k] f32)."""
     lf = logits.float()
@@ -103,6 +110,13 @@ class MoE(RefModule):
         if self.ep_size > 1:
             from ..parallel.ep import ep_moe
             y = ep_moe(self, x, topi, topw)
+        elif _grouped_ok(x, self.w_gu):
+            from ..ops.moe_kernels import GroupedExperts
+            r = resid.reshape(-1, H)
+            if self.shared is not None:
+                y = GroupedExperts.apply(x, topi, topw, self.w_gu, self.w_down, r).view(B, S, H)
+                return self.shared(h, y), aux
+            return GroupedExperts.apply(x, topi, topw, self.w_gu, self.w_down, r).view(B, S, H), aux
         else:
             flat_e = topi.reshape(-1)
             order = torch.argsort(flat_e, stable=True)
