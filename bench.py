@@ -37,35 +37,51 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "train tokens/sec (box, device-timed, max over ranks) at 1/2/4/8 B200 vs ref NCCL build"
-CONFIG_NAME = "llama-gqa-1.3b (BASELINE config 2)"
+
+_TRAINER = {
+    "learning_rate": 3e-4, "max_steps": 0, "num_epochs": 1, "gradient_accumulation": 1,
+    "checkpoint_dir": "/tmp/oxidizr_bench_ckpt", "log_interval": 1000000, "save_interval": 1000000,
+    "load_balance_alpha": 0.0, "group_size": 4, "beta_kl": 0.04,
+}
+
+# The BASELINE.json configs (2 is the headline; 3-5 are the other model families).
+MODELS = {
+    "llama": ("llama-gqa-1.3b (BASELINE config 2)", 8, {
+        "name": "llama_gqa_bench", "hidden_size": 2048, "num_layers": 16, "num_heads": 16, "kv_heads": 8,
+        "intermediate_size": 5632, "vocab_size": 128354, "max_seq_len": 2048, "rope_theta": 10000.0}),
+    "hybrid": ("hybrid-mamba2-mla-moe (BASELINE config 3)", 16, {
+        "name": "hybrid_bench", "hidden_size": 768, "num_layers": 8, "num_heads": 12,
+        "mamba_layers": [0, 1, 2, 4, 5, 6], "mamba2_num_heads": 24, "mamba2_head_dim": 64,
+        "mamba2_state_size": 128, "mamba2_chunk_size": 256, "mamba2_n_groups": 1, "mamba2_conv_kernel": 4,
+        "mamba2_expand": 2, "kv_latent_dim": 256, "q_latent_dim": 512, "d_rope": 32, "num_experts": 32,
+        "experts_per_tok": 4, "shared_expert_enabled": True, "num_shared_experts": 1, "intermediate_size": 512,
+        "vocab_size": 100277, "max_seq_len": 1024, "rope_theta": 10000.0}),
+    "mamba3": ("mamba3-mimo4 (BASELINE config 4)", 4, {
+        "name": "mamba3_bench", "hidden_size": 1024, "num_layers": 24, "num_heads": 16,
+        "mamba_layers": list(range(24)), "mamba3_enabled": True, "mamba3_complex_rope": True,
+        "mamba3_mimo_rank": 4, "mamba3_use_conv": False, "mamba2_num_heads": 32, "mamba2_head_dim": 64,
+        "mamba2_state_size": 128, "mamba2_chunk_size": 256, "mamba2_n_groups": 1, "mamba2_conv_kernel": 4,
+        "mamba2_expand": 2, "vocab_size": 100277, "max_seq_len": 4096, "rope_theta": 10000.0}),
+    "moe": ("fine-grained-moe-64e (BASELINE config 5)", 4, {
+        "name": "moe_bench", "hidden_size": 2048, "num_layers": 16, "num_heads": 16, "kv_heads": 4,
+        "num_experts": 64, "experts_per_tok": 8, "shared_expert_enabled": True, "num_shared_experts": 2,
+        "intermediate_size": 1024, "vocab_size": 128354, "max_seq_len": 4096, "rope_theta": 500000.0}),
+}
+CONFIG_NAME = MODELS["llama"][0]
 
 
-def bench_config():
+def bench_config(model: str = "llama"):
     from oxidizr_b200.config import LitConfig
-    d = {
-        "model": {
-            "name": "llama_gqa_bench", "hidden_size": 2048, "num_layers": 16, "num_heads": 16, "kv_heads": 8,
-            "intermediate_size": 5632, "vocab_size": 128354, "max_seq_len": 2048, "rope_theta": 10000.0,
-            "dtype": "bf16", "init_std": 0.02, "seed": 0,
-        },
-        "trainer": {
-            "learning_rate": 3e-4, "batch_size": 8, "max_steps": 0, "num_epochs": 1, "gradient_accumulation": 1,
-            "checkpoint_dir": "/tmp/oxidizr_bench_ckpt", "log_interval": 1000000, "save_interval": 1000000,
-            "load_balance_alpha": 0.0, "group_size": 4, "beta_kl": 0.04,
-        },
-    }
+    _, batch, m = MODELS[model]
+    d = {"model": dict(m, dtype="bf16", init_std=0.02, seed=0), "trainer": dict(_TRAINER, batch_size=batch)}
+    if model in ("hybrid", "moe"):
+        d["trainer"]["load_balance_alpha"] = 0.01
     return LitConfig.from_dict(d)
 
 
 def flops_per_token(m) -> float:
-    """6 * matmul params + causal attention (6 * S * H * L, fwd+bwd, half-masked)."""
-    H, L, V, S = m.hidden_size, m.num_layers, m.vocab_size, m.max_seq_len
-    hd = H // m.num_heads
-    kv = m.kv_heads * hd
-    I = m.intermediate_size
-    per_layer = H * (H + 2 * kv) + H * H + 3 * H * I
-    dense = L * per_layer + V * H  # lm_head
-    return 6.0 * dense + 6.0 * S * H * L
+    from oxidizr_b200.utils.flops import flops_per_token as f
+    return f(m)
 
 
 class ClockSampler:
@@ -140,6 +156,8 @@ def main():
     ap.add_argument("--impl", default="oxidizr_b200", choices=["oxidizr_b200", "reference"])
     ap.add_argument("--sync-backend", default=os.environ.get("OXI_SYNC_BACKEND", "auto"))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--model", default="llama", choices=sorted(MODELS),
+                    help="llama = the headline config; hybrid / mamba3 / moe = the other BASELINE configs")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -166,7 +184,7 @@ def main():
     from oxidizr_b200.trainer import Trainer
     from oxidizr_b200 import data as D
 
-    cfg = bench_config()
+    cfg = bench_config(args.model)
     m, tcfg = cfg.model, cfg.trainer
     B, S, V = tcfg.batch_size, m.max_seq_len, m.vocab_size
     torch.manual_seed(1234)
@@ -285,9 +303,9 @@ def main():
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded uniform u32 tokens, random-init weights)",
-        "config": {"model": CONFIG_NAME, "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
+        "config": {"model": MODELS[args.model][0], "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
                    "micro_batch_per_gpu": B, "grad_accum": 1, "sync_backend": backend,
-                   "l2": "no flush: per-step working set (2.6 GB weights + 20 GB optimizer state) >> 126 MB L2"},
+                   "l2": "no flush: per-step working set (weights, optimizer state, activations: GBs) >> 126 MB L2"},
         "clocks": clocks, "e2e": e2e, "gpu_launches": n_launch,
         "model_tflops_per_gpu": round(achieved_tf, 1),
         "mfu_vs_measured_sustained": round(achieved_tf / pk["bf16_tflops_sustained"], 3),

@@ -2,7 +2,8 @@
 // gradient reduce-scatter / clip / AdamW / parameter all-gather kernels.
 //
 // Every rank owns, in device memory mapped by all peers:
-//   send  bf16 [N]   the rank's gradient, rounded to bf16 (NVLink payload)
+//   recv  bf16 [N]   per bucket, W slots of this rank's shard: peers push
+//                    their bf16-rounded gradient of the shard into slot r
 //   param bf16 [N]   the model parameters (flat)
 //   pad   signal pad: epoch flags written by peers, partial norms
 // and privately: the reduced f32 gradient of its shards, and f32 master
@@ -10,10 +11,11 @@
 //
 // Bucket b covers flat range [lo, lo + len), len a multiple of W * 64; rank r
 // owns [lo + r*len/W, lo + (r+1)*len/W).  Per step (epoch e, monotonic):
-//   1. bucket ready in backward: grad f32 -> bf16 into send[lo..]   (local)
-//   2. rs kernel: post epoch into every peer's ready[b][r]; wait until
-//      ready[b][*] >= e in the local pad; sum the owned shard over all peers'
-//      send buffers (P2P 16-byte loads), f32 accumulate -> rgrad; sum(g^2)
+//   1. bucket ready in backward: push kernel casts grad f32 -> bf16 and
+//      stores each owner's part into the owner's recv slot (P2P 16-byte
+//      stores); its last CTA posts epoch into every peer's ready[b][r]
+//   2. reduce kernel: wait until ready[b][*] >= e in the local pad; sum the W
+//      slots of the owned shard (local loads), f32 -> rgrad; sum(g^2)
 //   3. norm kernel: exchange partial sum(g^2) through the pads -> clip coef
 //   4. adamw_ag kernel: AdamW on the owned shards (f32 master), bf16 result
 //      stored to every peer's param buffer (P2P 16-byte stores); post epoch
@@ -25,6 +27,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -46,14 +49,13 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 }
 
 // Wait until flags[i*stride] >= epoch for i in [0, W) (local pad).  One thread.
-__device__ bool wait_flags(const int* flags, int W, int stride, int epoch, int* status, volatile int* abort) {
+__device__ bool wait_flags(const int* flags, int W, int stride, int epoch, int* status, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer();
   for (int i = 0; i < W; ++i) {
     uint32_t spins = 0;
     while (ld_acquire_sys(flags + (int64_t)i * stride) < epoch) {
       if ((++spins & 255u) == 0) {
-        if (abort && *abort) return false;
-        if (globaltimer() - t0 > OXI_WAIT_LIMIT_NS) {
+        if (globaltimer() - t0 > limit_ns) {
           record_error(status, OXI_ERR_TIMEOUT_PEER);
           return false;
         }
@@ -83,40 +85,72 @@ __global__ void grad_to_bf16_kernel(const float* __restrict__ g, __nv_bfloat16* 
   }
 }
 
-// Reduce-scatter of one bucket.  peers_send[i] = rank i's send buffer (bf16 [N]).
-__global__ void rs_bucket_kernel(const uint64_t* __restrict__ peers_send, const uint64_t* __restrict__ peer_pads,
-                                 int* __restrict__ my_pad, int rank, int W, int bucket, int epoch, int64_t lo,
-                                 int64_t len, float* __restrict__ rgrad, float* __restrict__ sumsq, int* status) {
+// Reduce-scatter of one bucket, push then reduce.
+//
+// push: every rank casts its f32 gradient of the bucket to bf16 and stores the
+// part owned by rank s straight into rank s's receive buffer, in the slot of
+// the sender: recv_s[lo + r*shard + i] = bf16(grad_r[lo + s*shard + i]).
+// NVLink stores are posted writes, so no thread waits on a round trip.  The
+// last CTA to finish publishes the bucket's epoch in every peer's pad.
+template <int W>
+__global__ void __launch_bounds__(256) push_bucket_kernel(const float* __restrict__ grad, int64_t lo, int64_t len,
+                                                          int rank, const uint64_t* __restrict__ peers_recv,
+                                                          const uint64_t* __restrict__ peer_pads, int bucket,
+                                                          int epoch, int* __restrict__ done_ctr) {
+  const int64_t shard = len / W;
+  const int64_t nv = len / 8;
+  const int64_t sv = shard / 8;  // 8-element vectors per shard
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(grad + lo)[2 * v];
+    const float4 b = reinterpret_cast<const float4*>(grad + lo)[2 * v + 1];
+    const int owner = (int)(v / sv);
+    const int64_t i = v - (int64_t)owner * sv;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers_recv[owner]) + lo + (int64_t)rank * shard;
+    reinterpret_cast<uint4*>(dst)[i] =
+        make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+  }
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int last;
+  if (threadIdx.x == 0) last = (atomicAdd(done_ctr + bucket, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    done_ctr[bucket] = 0;
+    __threadfence_system();
+    for (int i = 0; i < W; ++i)
+      st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_READY + bucket * PAD_MAXW + rank, epoch);
+  }
+}
+
+// reduce: wait until every rank has pushed the bucket, then sum the W slots of
+// this rank's shard from local memory (f32), store the reduced shard and add
+// its sum of squares.
+template <int W>
+__global__ void __launch_bounds__(512) reduce_bucket_kernel(const __nv_bfloat16* __restrict__ recv,
+                                                            int* __restrict__ my_pad, int bucket, int epoch,
+                                                            int64_t lo, int64_t len, float* __restrict__ rgrad,
+                                                            float* __restrict__ sumsq, int* status,
+                                                            uint64_t wait_ns) {
   __shared__ int ok_s;
   __shared__ float red[32];
   const int64_t shard = len / W;
-  const int64_t s0 = lo + rank * shard;
-  if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) {
-      // the send buffer of this bucket was written by the previous kernel on
-      // this stream; make it visible system-wide, then tell every peer.
-      __threadfence_system();
-      for (int i = 0; i < W; ++i) {
-        int* pad = reinterpret_cast<int*>(peer_pads[i]);
-        st_release_sys(pad + PAD_READY + bucket * PAD_MAXW + rank, epoch);
-      }
-    }
-    ok_s = wait_flags(my_pad + PAD_READY + bucket * PAD_MAXW, W, 1, epoch, status, nullptr) ? 1 : 0;
-  }
+  if (threadIdx.x == 0)
+    ok_s = wait_flags(my_pad + PAD_READY + bucket * PAD_MAXW, W, 1, epoch, status, wait_ns) ? 1 : 0;
   __syncthreads();
   float ss = 0.f;
   if (ok_s) {
-    const int64_t nv = shard / 8;
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(recv + lo);
+    const int64_t sv = shard / 8;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < sv; v += (int64_t)gridDim.x * blockDim.x) {
+      uint4 u[W];
+#pragma unroll
+      for (int r = 0; r < W; ++r) u[r] = src[r * sv + v];
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int i = 0; i < W; ++i) {
-        const int src = (rank + i) % W;  // stagger peers so ranks do not all hit the same one
-        const uint4 u = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers_send[src]) + s0)[v];
-        add8(acc, u);
-      }
-      float* o = rgrad + v * 8;  // rgrad points at this bucket's shard
-      reinterpret_cast<float4*>(o)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      reinterpret_cast<float4*>(o)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+      for (int r = 0; r < W; ++r) add8(acc, u[r]);
+      float4* o = reinterpret_cast<float4*>(rgrad + v * 8);  // rgrad points at this bucket's shard
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 #pragma unroll
       for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
     }
@@ -136,7 +170,8 @@ __global__ void rs_bucket_kernel(const uint64_t* __restrict__ peers_send, const 
 // Exchange partial sums of squares; coef = min(1, max_norm / (norm + 1e-6)) / W.
 __global__ void norm_exchange_kernel(const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad, int rank,
                                      int W, int epoch, const float* __restrict__ sumsq, float max_norm,
-                                     float* __restrict__ coef, float* __restrict__ norm_out, int* status) {
+                                     float* __restrict__ coef, float* __restrict__ norm_out, int* status,
+                                     uint64_t wait_ns) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   const float mine = *sumsq;
   for (int i = 0; i < W; ++i) {
@@ -145,7 +180,7 @@ __global__ void norm_exchange_kernel(const uint64_t* __restrict__ peer_pads, int
   }
   __threadfence_system();
   for (int i = 0; i < W; ++i) st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_NORMF + rank, epoch);
-  if (!wait_flags(my_pad + PAD_NORMF, W, 1, epoch, status, nullptr)) {
+  if (!wait_flags(my_pad + PAD_NORMF, W, 1, epoch, status, wait_ns)) {
     *coef = 0.f;  // no update on a failed exchange
     *norm_out = NAN;
     return;
@@ -161,43 +196,58 @@ __global__ void norm_exchange_kernel(const uint64_t* __restrict__ peer_pads, int
 
 // AdamW on the owned shards + bf16 parameter all-gather over P2P stores.
 // buckets: [nb][3] int64 = {lo, len, shard_offset_in_rgrad}
-__global__ void adamw_allgather_kernel(const int64_t* __restrict__ buckets, int nb, int rank, int W,
-                                       const float* __restrict__ rgrad, float* __restrict__ master,
-                                       float* __restrict__ m, float* __restrict__ v,
-                                       const uint64_t* __restrict__ peers_param, const uint64_t* __restrict__ peer_pads,
-                                       int* __restrict__ my_pad, int epoch, float lr, float b1, float b2, float eps,
-                                       float wd, float bc1, float bc2, const float* __restrict__ coef,
-                                       int* __restrict__ done_ctr, int* status) {
+__device__ __forceinline__ float adamw_one(float g, float& m, float& v, float& p, float b1, float b2, float rb1,
+                                           float rb2, float lr, float eps, float wd) {
+  m = b1 * m + (1.f - b1) * g;
+  v = b2 * v + (1.f - b2) * g * g;
+  p = p - lr * ((m * rb1) / (sqrtf(v * rb2) + eps)) - lr * wd * p;
+  return p;
+}
+
+template <int W>
+__global__ void __launch_bounds__(256) adamw_allgather_kernel(
+    const int64_t* __restrict__ buckets, int nb, int rank, const float* __restrict__ rgrad,
+    float* __restrict__ master, float* __restrict__ m, float* __restrict__ v, const uint64_t* __restrict__ peers_param,
+    const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad, int epoch, float lr, float b1, float b2,
+    float eps, float wd, float bc1, float bc2, const float* __restrict__ coef, int* __restrict__ done_ctr, int* status,
+    uint64_t wait_ns) {
   const float gs = *coef;
   const float rb1 = 1.f / bc1, rb2 = 1.f / bc2;
   const bool failed = status && *reinterpret_cast<volatile int*>(status) != 0;
   if (!failed) {
+    __nv_bfloat16* dst[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) dst[j] = reinterpret_cast<__nv_bfloat16*>(peers_param[(rank + j) % W]);
     for (int b = 0; b < nb; ++b) {
       const int64_t lo = buckets[3 * b], len = buckets[3 * b + 1], so = buckets[3 * b + 2];
       const int64_t shard = len / W;
       const int64_t p0 = lo + rank * shard;
       const int64_t nv = shard / 8;
       for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e = so + i * 8;  // shard offsets are multiples of 8 elements
+        float4 g4[2], m4[2], v4[2], p4[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          g4[h] = reinterpret_cast<const float4*>(rgrad + e)[h];
+          m4[h] = reinterpret_cast<const float4*>(m + e)[h];
+          v4[h] = reinterpret_cast<const float4*>(v + e)[h];
+          p4[h] = reinterpret_cast<const float4*>(master + e)[h];
+        }
         float pw[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int64_t e = so + i * 8 + k;
-          const float g = rgrad[e] * gs;
-          const float mk = b1 * m[e] + (1.f - b1) * g;
-          const float vk = b2 * v[e] + (1.f - b2) * g * g;
-          m[e] = mk;
-          v[e] = vk;
-          const float pp = master[e];
-          const float np = pp - lr * ((mk * rb1) / (sqrtf(vk * rb2) + eps)) - lr * wd * pp;
-          master[e] = np;
-          pw[k] = np;
+        for (int h = 0; h < 2; ++h) {
+          pw[4 * h + 0] = adamw_one(g4[h].x * gs, m4[h].x, v4[h].x, p4[h].x, b1, b2, rb1, rb2, lr, eps, wd);
+          pw[4 * h + 1] = adamw_one(g4[h].y * gs, m4[h].y, v4[h].y, p4[h].y, b1, b2, rb1, rb2, lr, eps, wd);
+          pw[4 * h + 2] = adamw_one(g4[h].z * gs, m4[h].z, v4[h].z, p4[h].z, b1, b2, rb1, rb2, lr, eps, wd);
+          pw[4 * h + 3] = adamw_one(g4[h].w * gs, m4[h].w, v4[h].w, p4[h].w, b1, b2, rb1, rb2, lr, eps, wd);
+          reinterpret_cast<float4*>(m + e)[h] = m4[h];
+          reinterpret_cast<float4*>(v + e)[h] = v4[h];
+          reinterpret_cast<float4*>(master + e)[h] = p4[h];
         }
         const uint4 packed = make_uint4(pack_bf16(pw[0], pw[1]), pack_bf16(pw[2], pw[3]), pack_bf16(pw[4], pw[5]),
                                         pack_bf16(pw[6], pw[7]));
-        for (int j = 0; j < W; ++j) {
-          const int dst = (rank + j) % W;
-          reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers_param[dst]) + p0)[i] = packed;
-        }
+#pragma unroll
+        for (int j = 0; j < W; ++j) reinterpret_cast<uint4*>(dst[j] + p0)[i] = packed;
       }
     }
   }
@@ -211,7 +261,7 @@ __global__ void adamw_allgather_kernel(const int64_t* __restrict__ buckets, int 
     *done_ctr = 0;
     __threadfence_system();
     for (int i = 0; i < W; ++i) st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_AGF + rank, epoch);
-    wait_flags(my_pad + PAD_AGF, W, 1, epoch, status, nullptr);
+    wait_flags(my_pad + PAD_AGF, W, 1, epoch, status, wait_ns);
   }
 }
 
@@ -259,29 +309,52 @@ void launch_grad_to_bf16(const float* g, void* out, int64_t n, cudaStream_t st) 
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_rs_bucket(const uint64_t* peers_send, const uint64_t* peer_pads, int* my_pad, int rank, int W, int bucket,
-                      int epoch, int64_t lo, int64_t len, float* rgrad, float* sumsq, int ctas, int* status,
-                      cudaStream_t st) {
+void launch_rs_bucket(const float* grad, const uint64_t* peers_recv, const void* my_recv, const uint64_t* peer_pads,
+                      int* my_pad, int* done_ctr, int rank, int W, int bucket, int epoch, int64_t lo, int64_t len,
+                      float* rgrad, float* sumsq, int ctas, int* status, int64_t wait_ns, cudaStream_t st) {
   OXI_CHECK(W <= PAD_MAXW && bucket < PAD_MAXB, "too many ranks or buckets");
   OXI_CHECK(len % (W * 8) == 0, "bucket length must divide into 8-element shards");
-  rs_bucket_kernel<<<ctas, 512, 0, st>>>(peers_send, peer_pads, my_pad, rank, W, bucket, epoch, lo, len, rgrad, sumsq,
-                                          status);
+  const int push_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / 8 + 255) / 256, 1), (int64_t)ctas * 2);
+  const int red_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / W / 8 + 511) / 512, 1), (int64_t)ctas);
+  const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(my_recv);
+  switch (W) {
+#define OXI_RS(N)                                                                                                \
+  case N:                                                                                                        \
+    push_bucket_kernel<N><<<push_ctas, 256, 0, st>>>(grad, lo, len, rank, peers_recv, peer_pads, bucket, epoch,  \
+                                                     done_ctr);                                                  \
+    reduce_bucket_kernel<N><<<red_ctas, 512, 0, st>>>(rv, my_pad, bucket, epoch, lo, len, rgrad, sumsq, status, \
+                                                      (uint64_t)wait_ns);                                        \
+    break;
+    OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)
+#undef OXI_RS
+    default: OXI_CHECK(false, "fused data parallelism supports 1..8 ranks per node, got ", W);
+  }
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_norm_exchange(const uint64_t* peer_pads, int* my_pad, int rank, int W, int epoch, const float* sumsq,
-                          float max_norm, float* coef, float* norm_out, int* status, cudaStream_t st) {
-  norm_exchange_kernel<<<1, 32, 0, st>>>(peer_pads, my_pad, rank, W, epoch, sumsq, max_norm, coef, norm_out, status);
+                          float max_norm, float* coef, float* norm_out, int* status, int64_t wait_ns,
+                          cudaStream_t st) {
+  norm_exchange_kernel<<<1, 32, 0, st>>>(peer_pads, my_pad, rank, W, epoch, sumsq, max_norm, coef, norm_out, status,
+                                         (uint64_t)wait_ns);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_adamw_allgather(const int64_t* buckets, int nb, int rank, int W, const float* rgrad, float* master,
                             float* m, float* v, const uint64_t* peers_param, const uint64_t* peer_pads, int* my_pad,
                             int epoch, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
-                            const float* coef, int* done_ctr, int* status, cudaStream_t st) {
-  adamw_allgather_kernel<<<sms() * 2, 256, 0, st>>>(buckets, nb, rank, W, rgrad, master, m, v, peers_param, peer_pads,
-                                                    my_pad, epoch, lr, b1, b2, eps, wd, bc1, bc2, coef, done_ctr,
-                                                    status);
+                            const float* coef, int* done_ctr, int* status, int64_t wait_ns, cudaStream_t st) {
+  switch (W) {
+#define OXI_AG(N)                                                                                                 \
+  case N:                                                                                                         \
+    adamw_allgather_kernel<N><<<sms() * 4, 256, 0, st>>>(buckets, nb, rank, rgrad, master, m, v, peers_param,     \
+                                                         peer_pads, my_pad, epoch, lr, b1, b2, eps, wd, bc1, bc2, \
+                                                         coef, done_ctr, status, (uint64_t)wait_ns);             \
+    break;
+    OXI_AG(1) OXI_AG(2) OXI_AG(3) OXI_AG(4) OXI_AG(5) OXI_AG(6) OXI_AG(7) OXI_AG(8)
+#undef OXI_AG
+    default: OXI_CHECK(false, "fused data parallelism supports 1..8 ranks per node, got ", W);
+  }
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -11,11 +11,14 @@
 // tiles.  The MMA warp issues S_{j+1} before waiting for P_j, so QK^T of the
 // next tile overlaps the softmax of the current one.
 //
-// Layout: q/k/v are row-major [B*S, H*D] views (row stride ld*), head h at
-// columns [h*D, (h+1)*D); GQA maps query head h to kv head h / (Hq/Hk).
-// Outputs: o [B*S, Hq*D] bf16, lse [B, Hq, S] f32 (natural log).
+// Layout: q/k are row-major [B*S, H*DQ] views and v [B*S, Hk*DV] (row strides
+// ld*), head h at columns [h*DQ, (h+1)*DQ) resp. [h*DV, ...); GQA maps query
+// head h to kv head h / (Hq/Hk).  DQ may exceed DV (multi-head latent attention
+// concatenates a RoPE part to q and k): a DQ that is not a multiple of 64 is
+// staged in whole 64-column blocks and the QK^T MMA stops at DQ.
+// Outputs: o [B*S, Hq*DV] bf16, lse [B, Hq, S] f32 (natural log).
 // Warps: 0 TMA, 1 MMA + TMEM owner, 2..5 softmax/correction/epilogue.
-// No TMA load here uses cluster multicast; every wait is bounded.
+// Every TMA load here reads local memory for one CTA; every wait is bounded.
 #include <algorithm>
 #include <cudaTypedefs.h>
 
@@ -29,7 +32,7 @@ constexpr int FA_BM = 128, FA_BN = 128;
 constexpr int FA_THREADS = 192;
 
 struct FaParams {
-  int B, S, Hq, Hk, D;
+  int B, S, Hq, Hk;
   float scale_log2;  // softmax scale * log2(e)
   int causal;
   __nv_bfloat16* o;
@@ -38,17 +41,20 @@ struct FaParams {
   int* status;
 };
 
-template <int D>
+template <int DQ, int DV>
 struct FaSmem {
-  static constexpr int Q_BYTES = FA_BM * D * 2;
-  static constexpr int KV_BYTES = FA_BN * D * 2;
+  static constexpr int KBQ = (DQ + 63) / 64;  // 64-column blocks of a q/k row
+  static constexpr int KBV = DV / 64;         // 64-column blocks of a v row
+  static constexpr int Q_BYTES = FA_BM * KBQ * 128;
+  static constexpr int K_BYTES = FA_BN * KBQ * 128;
+  static constexpr int V_BYTES = FA_BN * KBV * 128;
   static constexpr int P_BYTES = FA_BM * FA_BN * 2;
-  static constexpr int KST = 3;               // K stages: K_j is freed as soon as S_j is done
-  static constexpr int VST = D <= 64 ? 3 : 2; // V stages: V_j is freed after PV_j
+  static constexpr int KST = 3;                // K stages: K_j is freed as soon as S_j is done
+  static constexpr int VST = DV <= 64 ? 3 : 2; // V stages: V_j is freed after PV_j
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + VST * KV_BYTES;
+  static constexpr int OFF_V = OFF_K + KST * K_BYTES;
+  static constexpr int OFF_P = OFF_V + VST * V_BYTES;
   static constexpr int OFF_BAR = OFF_P + P_BYTES;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
   static_assert(TOTAL <= 232448, "shared memory budget");
@@ -60,11 +66,11 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, uint32_t 
   return umma_desc_sw128(base + (kk >> 2) * block_bytes + (kk & 3) * 32, 16, 1024);
 }
 
-template <int D>
+template <int DQ, int DV>
 __global__ void __launch_bounds__(FA_THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, FaParams p) {
-  using L = FaSmem<D>;
+  using L = FaSmem<DQ, DV>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::OFF_Q;
@@ -93,7 +99,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const int row0 = b * p.S;
   const int n_kt_all = (p.S + FA_BN - 1) / FA_BN;
   const int nk = p.causal ? min(n_kt_all, (q0 + FA_BM - 1) / FA_BN + 1) : n_kt_all;
-  constexpr int KB = D / 64;  // 64-column blocks per row
+  constexpr int KBQ = L::KBQ, KBV = L::KBV;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -130,27 +136,27 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       bool ok = true;
       mbar_arrive_expect_tx(q_full, L::Q_BYTES);
 #pragma unroll
-      for (int kb = 0; kb < KB; ++kb) tma_load_2d(sQ + kb * FA_BM * 128, &tmQ, q_full, h * D + kb * 64, row0 + q0);
+      for (int kb = 0; kb < KBQ; ++kb) tma_load_2d(sQ + kb * FA_BM * 128, &tmQ, q_full, h * DQ + kb * 64, row0 + q0);
       // K_j runs ahead of V_j: K stages free up when S_j completes, V stages
       // when PV_j completes, so K loads are issued as early as possible.
       int jv = 0;
       for (int j = 0; j < nk && ok; ++j) {
         const int ks = j % L::KST, ku = j / L::KST;
         if (!mbar_wait(&k_empty[ks], (ku & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[ks], L::KV_BYTES);
+        mbar_arrive_expect_tx(&k_full[ks], L::K_BYTES);
 #pragma unroll
-        for (int kb = 0; kb < KB; ++kb)
-          tma_load_2d(sK + ks * L::KV_BYTES + kb * FA_BN * 128, &tmK, &k_full[ks], hk * D + kb * 64,
+        for (int kb = 0; kb < KBQ; ++kb)
+          tma_load_2d(sK + ks * L::K_BYTES + kb * FA_BN * 128, &tmK, &k_full[ks], hk * DQ + kb * 64,
                       row0 + j * FA_BN);
         // issue every V load whose stage is already free (never more than one behind K)
         while (jv <= j) {
           const int vs = jv % L::VST, vu = jv / L::VST;
           if (jv < j && !mbar_try_wait(smem_u32(&v_empty[vs]), (vu & 1) ^ 1)) break;
           if (jv == j && !mbar_wait(&v_empty[vs], (vu & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[vs], L::KV_BYTES);
+          mbar_arrive_expect_tx(&v_full[vs], L::V_BYTES);
 #pragma unroll
-          for (int kb = 0; kb < KB; ++kb)
-            tma_load_2d(sV + vs * L::KV_BYTES + kb * FA_BN * 128, &tmV, &v_full[vs], hk * D + kb * 64,
+          for (int kb = 0; kb < KBV; ++kb)
+            tma_load_2d(sV + vs * L::V_BYTES + kb * FA_BN * 128, &tmV, &v_full[vs], hk * DV + kb * 64,
                         row0 + jv * FA_BN);
           ++jv;
         }
@@ -164,7 +170,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t IDESC_S = umma_idesc_bf16(FA_BM, FA_BN, false, false);
-      constexpr uint32_t IDESC_O = umma_idesc_bf16(FA_BM, D, false, true);
+      constexpr uint32_t IDESC_O = umma_idesc_bf16(FA_BM, DV, false, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status);
       const uint32_t aQ = smem_u32(sQ);
       auto issue_s = [&](int j) -> bool {
@@ -173,9 +179,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (!mbar_wait(&k_full[ks], ku & 1, abort_flag, p.status)) return false;
         if (!mbar_wait(&s_empty[st], (u & 1) ^ 1, abort_flag, p.status)) return false;
         tc_fence_after();
-        const uint32_t aK = smem_u32(sK + ks * L::KV_BYTES);
+        const uint32_t aK = smem_u32(sK + ks * L::K_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
+        for (int kk = 0; kk < DQ / 16; ++kk)
           tc_mma_f16(TM_S0 + st * FA_BN, kmajor_desc(aQ, kk, FA_BM * 128), kmajor_desc(aK, kk, FA_BN * 128),
                      IDESC_S, kk != 0);
         tc_commit(&s_full[st]);
@@ -190,7 +196,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (!mbar_wait(&v_full[vs], vu & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t aP = smem_u32(sP);
-        const uint32_t aV = smem_u32(sV + vs * L::KV_BYTES);
+        const uint32_t aV = smem_u32(sV + vs * L::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < FA_BN / 16; ++kk)
           tc_mma_f16(TM_O, kmajor_desc(aP, kk, FA_BM * 128), umma_desc_sw128(aV + kk * 2048, FA_BN * 128, 1024),
@@ -259,7 +265,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         tc_fence_after();
         if (rescale_warp) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; c += 2) {
+          for (int c = 0; c < DV / 32; c += 2) {
             uint32_t o0[32], o1[32];
             tmem_ld32(TM_O + lane_base + c * 32, o0);
             tmem_ld32(TM_O + lane_base + c * 32 + 32, o1);
@@ -306,9 +312,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       tc_fence_after();
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const bool valid = qpos < p.S;
-      __nv_bfloat16* orow = p.o + (int64_t)(row0 + qpos) * p.ldo + h * D;
+      __nv_bfloat16* orow = p.o + (int64_t)(row0 + qpos) * p.ldo + h * DV;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < DV / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(TM_O + lane_base + c * 32, o);
         tc_wait_ld();
@@ -337,24 +343,24 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   }
 }
 
-template <int D>
+template <int DQ, int DV>
 void launch_fa_fwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
                      int64_t ldo, float* lse, int B, int S, int Hq, int Hk, float scale, bool causal, int* status,
                      cudaStream_t st) {
-  using L = FaSmem<D>;
+  using L = FaSmem<DQ, DV>;
   const int64_t T = (int64_t)B * S;
-  CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * D, ldq, 64, FA_BM);
-  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * D, ldk, 64, FA_BN);
-  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * D, ldv, 64, FA_BN);
+  CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * DQ, ldq, 64, FA_BM);
+  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * DQ, ldk, 64, FA_BN);
+  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * DV, ldv, 64, FA_BN);
   FaParams p;
-  p.B = B; p.S = S; p.Hq = Hq; p.Hk = Hk; p.D = D;
+  p.B = B; p.S = S; p.Hq = Hq; p.Hk = Hk;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.ldo = ldo;
   p.lse = lse;
   p.status = status;
-  auto kern = fa_fwd_kernel<D>;
+  auto kern = fa_fwd_kernel<DQ, DV>;
   static bool attr = false;
   if (!attr) {
     OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
@@ -383,39 +389,45 @@ struct FaBwdParams {
   int causal;
   const float* lse;    // [B, Hq, S]
   const float* delta;  // [B, Hq, S]
-  float* dq_acc;       // [B*S, Hq*D] f32, zero-initialised
+  float* dq_acc;       // [B*S, Hq*DQ] f32, zero-initialised
   int64_t ld_dq;
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
-  int64_t ld_dkv;
+  int64_t ld_dk, ld_dv;
   int* status;
 };
 
-template <int D>
+template <int DQ, int DV>
 struct FaBwdSmem {
-  static constexpr int T_BYTES = 128 * D * 2;   // K, V, Q, dO tiles
-  static constexpr int P_BYTES = 128 * 128 * 2;  // P^T, dS^T
+  static constexpr int KBQ = (DQ + 63) / 64;
+  static constexpr int KBV = DV / 64;
+  static constexpr int NQ = KBQ * 64;             // DQ rounded up to whole 64-column blocks
+  static constexpr int TQ_BYTES = 128 * NQ * 2;   // K, Q tiles
+  static constexpr int TV_BYTES = 128 * DV * 2;   // V, dO tiles
+  static constexpr int P_BYTES = 128 * 128 * 2;   // P^T, dS^T
   static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + T_BYTES;
-  static constexpr int OFF_Q = OFF_V + T_BYTES;
-  static constexpr int OFF_DO = OFF_Q + T_BYTES;
-  static constexpr int OFF_PT = OFF_DO + T_BYTES;
+  static constexpr int OFF_V = OFF_K + TQ_BYTES;
+  static constexpr int OFF_Q = OFF_V + TV_BYTES;
+  static constexpr int OFF_DO = OFF_Q + TQ_BYTES;
+  static constexpr int OFF_PT = OFF_DO + TV_BYTES;
   static constexpr int OFF_DST = OFF_PT + P_BYTES;
   static constexpr int OFF_VEC = OFF_DST + P_BYTES;   // lse (log2), delta: 2 x 128 f32
   static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+  static_assert(TOTAL <= 232448, "shared memory budget");
+  static_assert(DV + NQ + 256 <= 512, "TMEM budget: dV, dK, S^T and dP^T accumulators");
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
-template <int D>
+template <int DQ, int DV>
 __global__ void __launch_bounds__(FA_THREADS, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                   FaBwdParams p) {
-  using L = FaBwdSmem<D>;
+  using L = FaBwdSmem<DQ, DV>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem + L::OFF_K;
@@ -445,7 +457,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const int n_it = group * n_i;
   const int row0 = b * p.S;
   const int k0 = jt * 128;
-  constexpr int KB = D / 64;
+  constexpr int KBQ = L::KBQ, KBV = L::KBV, NQ = L::NQ;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -469,35 +481,38 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t TM_DV = tmem, TM_DK = tmem + D, TM_S = tmem + 2 * D, TM_DP = tmem + 2 * D + 128;
+  const uint32_t TM_DV = tmem, TM_DK = tmem + DV, TM_S = tmem + DV + NQ, TM_DP = tmem + DV + NQ + 128;
   const uint32_t TM_DQ = TM_S;  // dQ reuses the S^T columns once they are consumed
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * L::T_BYTES);
+      mbar_arrive_expect_tx(kv_full, L::TQ_BYTES + L::TV_BYTES);
 #pragma unroll
-      for (int kb = 0; kb < KB; ++kb) {
-        tma_load_2d(sK + kb * 128 * 128, &tmK, kv_full, hk * D + kb * 64, row0 + k0);
-        tma_load_2d(sV + kb * 128 * 128, &tmV, kv_full, hk * D + kb * 64, row0 + k0);
-      }
+      for (int kb = 0; kb < KBQ; ++kb) tma_load_2d(sK + kb * 128 * 128, &tmK, kv_full, hk * DQ + kb * 64, row0 + k0);
+#pragma unroll
+      for (int kb = 0; kb < KBV; ++kb) tma_load_2d(sV + kb * 128 * 128, &tmV, kv_full, hk * DV + kb * 64, row0 + k0);
       for (int it = 0; it < n_it; ++it) {
         const int h = hk * group + it / n_i;
         const int i = i_start + it % n_i;
         if (!mbar_wait(it_done, (it & 1) ^ 1, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * L::T_BYTES);
+        mbar_arrive_expect_tx(qdo_full, L::TQ_BYTES + L::TV_BYTES);
 #pragma unroll
-        for (int kb = 0; kb < KB; ++kb) {
-          tma_load_2d(sQ + kb * 128 * 128, &tmQ, qdo_full, h * D + kb * 64, row0 + i * 128);
-          tma_load_2d(sDO + kb * 128 * 128, &tmDO, qdo_full, h * D + kb * 64, row0 + i * 128);
-        }
+        for (int kb = 0; kb < KBQ; ++kb)
+          tma_load_2d(sQ + kb * 128 * 128, &tmQ, qdo_full, h * DQ + kb * 64, row0 + i * 128);
+#pragma unroll
+        for (int kb = 0; kb < KBV; ++kb)
+          tma_load_2d(sDO + kb * 128 * 128, &tmDO, qdo_full, h * DV + kb * 64, row0 + i * 128);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t ID_SS = umma_idesc_bf16(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t ID_KV = umma_idesc_bf16(128, D, false, true);     // dV, dK
-      constexpr uint32_t ID_Q = umma_idesc_bf16(128, D, true, true);       // dQ
+      // dK and dQ run over whole 64-column blocks (N = NQ); the columns past DQ
+      // are never stored.
+      constexpr uint32_t ID_V = umma_idesc_bf16(128, DV, false, true);     // dV
+      constexpr uint32_t ID_K = umma_idesc_bf16(128, NQ, false, true);     // dK
+      constexpr uint32_t ID_Q = umma_idesc_bf16(128, NQ, true, true);      // dQ
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
       const uint32_t aPt = smem_u32(sPt), aDSt = smem_u32(sDSt);
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.status);
@@ -506,10 +521,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (it > 0 && !mbar_wait(dq_read, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
+        for (int kk = 0; kk < DQ / 16; ++kk)
           tc_mma_f16(TM_S, kmajor_desc(aK, kk, 128 * 128), kmajor_desc(aQ, kk, 128 * 128), ID_SS, kk != 0);
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk)
           tc_mma_f16(TM_DP, kmajor_desc(aV, kk, 128 * 128), kmajor_desc(aDO, kk, 128 * 128), ID_SS, kk != 0);
-        }
         tc_commit(sdp_full);
         if (!mbar_wait(p_ready, it & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
@@ -518,9 +534,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
           // dV += P^T dO ; dK += dS^T Q  (B operands MN-major: rows = queries)
           tc_mma_f16(TM_DV, kmajor_desc(aPt, kk, 128 * 128), umma_desc_sw128(aDO + kk * 2048, 128 * 128, 1024),
-                     ID_KV, acc);
+                     ID_V, acc);
           tc_mma_f16(TM_DK, kmajor_desc(aDSt, kk, 128 * 128), umma_desc_sw128(aQ + kk * 2048, 128 * 128, 1024),
-                     ID_KV, acc);
+                     ID_K, acc);
           // dQ = dS K: A = dS^T read MN-major (M = queries), B = K MN-major (rows = keys)
           tc_mma_f16(TM_DQ, umma_desc_sw128(aDSt + kk * 2048, 128 * 128, 1024),
                      umma_desc_sw128(aK + kk * 2048, 128 * 128, 1024), ID_Q, kk > 0 ? 1u : 0u);
@@ -599,16 +615,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       if (!mbar_wait(it_done, it & 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
       const int qp = q0 + r;
-      float* dqrow = p.dq_acc + (int64_t)(row0 + qp) * p.ld_dq + h * D;
+      float* dqrow = p.dq_acc + (int64_t)(row0 + qp) * p.ld_dq + h * DQ;
 #pragma unroll 1
-      for (int c2 = 0; c2 < D / 32; c2 += 2) {
+      for (int c2 = 0; c2 < DQ / 32; c2 += 2) {
+        const int nc = (c2 + 1 < DQ / 32) ? 2 : 1;  // 32-column chunks in this batch
         uint32_t o[2][32];
         tmem_ld32(TM_DQ + lane_base + c2 * 32, o[0]);
-        tmem_ld32(TM_DQ + lane_base + c2 * 32 + 32, o[1]);
+        if (nc == 2) tmem_ld32(TM_DQ + lane_base + c2 * 32 + 32, o[1]);
         tc_wait_ld();
         if (qp < p.S) {
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
+            if (h2 >= nc) break;
             float4* d4 = reinterpret_cast<float4*>(dqrow + (c2 + h2) * 32);
 #pragma unroll
             for (int q = 0; q < 8; ++q)
@@ -627,10 +645,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const bool valid = kpos < p.S;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
-        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + (int64_t)(row0 + kpos) * p.ld_dkv + hk * D;
+        __nv_bfloat16* dst = which == 0 ? p.dv + (int64_t)(row0 + kpos) * p.ld_dv + hk * DV
+                                        : p.dk + (int64_t)(row0 + kpos) * p.ld_dk + hk * DQ;
         const uint32_t src = (which == 0 ? TM_DV : TM_DK) + lane_base;
+        const int ncol = which == 0 ? DV : DQ;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < ncol / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(src + c * 32, o);
           tc_wait_ld();
@@ -647,9 +667,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       }
     } else if (n_it == 0 && kpos < p.S) {
       // no query attends to this key tile: zero gradients
-      __nv_bfloat16* dv = p.dv + (int64_t)(row0 + kpos) * p.ld_dkv + hk * D;
-      __nv_bfloat16* dk = p.dk + (int64_t)(row0 + kpos) * p.ld_dkv + hk * D;
-      for (int c = 0; c < D; ++c) { dv[c] = __float2bfloat16(0.f); dk[c] = __float2bfloat16(0.f); }
+      __nv_bfloat16* dv = p.dv + (int64_t)(row0 + kpos) * p.ld_dv + hk * DV;
+      __nv_bfloat16* dk = p.dk + (int64_t)(row0 + kpos) * p.ld_dk + hk * DQ;
+      for (int c = 0; c < DV; ++c) dv[c] = __float2bfloat16(0.f);
+      for (int c = 0; c < DQ; ++c) dk[c] = __float2bfloat16(0.f);
     }
   }
 
@@ -700,17 +721,17 @@ __global__ void fa_dq_convert_kernel(const float* __restrict__ acc, int64_t ldac
   }
 }
 
-template <int D>
+template <int DQ, int DV>
 void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                      const void* dout, int64_t lddo, const float* lse, const float* delta, float* dq_acc,
-                     int64_t ld_dq, void* dk, void* dv, int64_t ld_dkv, int B, int S, int Hq, int Hk, float scale,
-                     bool causal, int* status, cudaStream_t st) {
-  using L = FaBwdSmem<D>;
+                     int64_t ld_dq, void* dk, int64_t ld_dk, void* dv, int64_t ld_dv, int B, int S, int Hq, int Hk,
+                     float scale, bool causal, int* status, cudaStream_t st) {
+  using L = FaBwdSmem<DQ, DV>;
   const int64_t T = (int64_t)B * S;
-  CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * D, ldq, 64, 128);
-  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * D, ldk, 64, 128);
-  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * D, ldv, 64, 128);
-  CUtensorMap tdo = make_tmap_bf16(dout, T, (int64_t)Hq * D, lddo, 64, 128);
+  CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * DQ, ldq, 64, 128);
+  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * DQ, ldk, 64, 128);
+  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * DV, ldv, 64, 128);
+  CUtensorMap tdo = make_tmap_bf16(dout, T, (int64_t)Hq * DV, lddo, 64, 128);
   FaBwdParams p;
   p.B = B; p.S = S; p.Hq = Hq; p.Hk = Hk;
   p.scale = scale;
@@ -722,9 +743,10 @@ void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   p.ld_dq = ld_dq;
   p.dk = reinterpret_cast<__nv_bfloat16*>(dk);
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
-  p.ld_dkv = ld_dkv;
+  p.ld_dk = ld_dk;
+  p.ld_dv = ld_dv;
   p.status = status;
-  auto kern = fa_bwd_kernel<D>;
+  auto kern = fa_bwd_kernel<DQ, DV>;
   static bool attr = false;
   if (!attr) {
     OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
@@ -737,43 +759,61 @@ void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
 
 }  // namespace
 
+bool fa_supported(int Dqk, int Dv) {
+  return (Dqk == 64 && Dv == 64) || (Dqk == 128 && Dv == 128) || (Dqk == 96 && Dv == 64) ||
+         (Dqk == 128 && Dv == 64);
+}
+
+bool fa_bwd_supported(int Dqk, int Dv) {
+  return (Dqk == 64 && Dv == 64) || (Dqk == 128 && Dv == 128) || (Dqk == 96 && Dv == 64) ||
+         (Dqk == 128 && Dv == 64);
+}
+
 void launch_fa_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
-                   int64_t ldo, float* lse, int B, int S, int Hq, int Hk, int D, float scale, bool causal,
+                   int64_t ldo, float* lse, int B, int S, int Hq, int Hk, int Dqk, int Dv, float scale, bool causal,
                    int* status, cudaStream_t st) {
   OXI_CHECK(Hq % Hk == 0, "query heads must be a multiple of kv heads");
   OXI_CHECK(ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(o) & 15) == 0, "output rows must be 16-byte aligned");
+  OXI_CHECK(fa_supported(Dqk, Dv), "flash attention forward has no kernel for head dims (qk ", Dqk, ", v ", Dv, ")");
   if (B == 0 || S == 0) return;
-  if (D == 64) launch_fa_fwd_t<64>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hk, scale, causal, status, st);
-  else if (D == 128) launch_fa_fwd_t<128>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hk, scale, causal, status, st);
-  else OXI_CHECK(false, "flash attention supports head_dim 64 or 128, got ", D);
+#define OXI_FA_FWD(DQ_, DV_)                                                                                    \
+  if (Dqk == DQ_ && Dv == DV_)                                                                                 \
+    return launch_fa_fwd_t<DQ_, DV_>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hk, scale, causal, status, st);
+  OXI_FA_FWD(64, 64)
+  OXI_FA_FWD(128, 128)
+  OXI_FA_FWD(96, 64)
+  OXI_FA_FWD(128, 64)
+#undef OXI_FA_FWD
 }
-
 
 void launch_fa_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                    const void* o, int64_t ldo, const void* dout, int64_t lddo, const float* lse, float* delta,
-                   float* dq_acc, void* dq, int64_t lddq, void* dk, void* dv, int64_t ld_dkv, int B, int S, int Hq,
-                   int Hk, int D, float scale, bool causal, int* status, cudaStream_t st) {
+                   float* dq_acc, void* dq, int64_t lddq, void* dk, int64_t ld_dk, void* dv, int64_t ld_dv, int B,
+                   int S, int Hq, int Hk, int Dqk, int Dv, float scale, bool causal, int* status, cudaStream_t st) {
   OXI_CHECK(Hq % Hk == 0, "query heads must be a multiple of kv heads");
-  OXI_CHECK(ld_dkv % 8 == 0 && lddq % 8 == 0, "gradient rows must be 16-byte aligned");
+  OXI_CHECK(ld_dk % 8 == 0 && ld_dv % 8 == 0 && lddq % 8 == 0, "gradient rows must be 16-byte aligned");
+  OXI_CHECK(fa_bwd_supported(Dqk, Dv), "flash attention backward has no kernel for head dims (qk ", Dqk, ", v ", Dv,
+            ")");
   if (B == 0 || S == 0) return;
   const int64_t T = (int64_t)B * S;
   const int64_t rows = T * Hq;
   fa_bwd_prep_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(o), ldo, reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B,
-      S, Hq, D);
+      S, Hq, Dv);
   OXI_CUDA_CHECK(cudaGetLastError());
-  OXI_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, (size_t)T * Hq * D * sizeof(float), st));
-  if (D == 64)
-    launch_fa_bwd_t<64>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq_acc, (int64_t)Hq * D, dk, dv, ld_dkv, B,
-                        S, Hq, Hk, scale, causal, status, st);
-  else if (D == 128)
-    launch_fa_bwd_t<128>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq_acc, (int64_t)Hq * D, dk, dv, ld_dkv, B,
-                         S, Hq, Hk, scale, causal, status, st);
-  else
-    OXI_CHECK(false, "flash attention supports head_dim 64 or 128, got ", D);
-  const int64_t nv = T * (Hq * D / 8);
+  OXI_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, (size_t)T * Hq * Dqk * sizeof(float), st));
+#define OXI_FA_BWD(DQ_, DV_)                                                                                       \
+  if (Dqk == DQ_ && Dv == DV_)                                                                                    \
+    launch_fa_bwd_t<DQ_, DV_>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq_acc, (int64_t)Hq * Dqk, dk, ld_dk, \
+                              dv, ld_dv, B, S, Hq, Hk, scale, causal, status, st);
+  OXI_FA_BWD(64, 64)
+  OXI_FA_BWD(128, 128)
+  OXI_FA_BWD(96, 64)
+  OXI_FA_BWD(128, 64)
+#undef OXI_FA_BWD
+  const int64_t nv = T * (Hq * Dqk / 8);
   fa_dq_convert_kernel<<<(unsigned)std::min<int64_t>((nv + 255) / 256, 148 * 16), 256, 0, st>>>(
-      dq_acc, (int64_t)Hq * D, reinterpret_cast<__nv_bfloat16*>(dq), lddq, T, Hq * D);
+      dq_acc, (int64_t)Hq * Dqk, reinterpret_cast<__nv_bfloat16*>(dq), lddq, T, Hq * Dqk);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

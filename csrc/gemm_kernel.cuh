@@ -23,7 +23,7 @@
 //   EPI_ROPE        C = [q | k | v] projections; rotate-half RoPE on q and k
 //                   heads using per-position cos/sin tables
 //
-// No TMA load here uses cluster multicast.
+// Every TMA load here is issued by one CTA for itself and reads local memory.
 #include <cudaTypedefs.h>
 #include <algorithm>
 

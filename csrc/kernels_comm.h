@@ -6,6 +6,9 @@
 
 namespace oxi {
 
+// Peer waits give up after wait_ns nanoseconds, record OXI_ERR_TIMEOUT_PEER in
+// the status word, skip their work and return.
+
 // Signal pad layout (int32 words; PAD_NORMV holds f32 values).
 constexpr int PAD_MAXW = 16;
 constexpr int PAD_MAXB = 512;
@@ -21,14 +24,17 @@ void* ipc_open(const std::string& handle);
 void ipc_close(void* p);
 
 void launch_grad_to_bf16(const float* g, void* out, int64_t n, cudaStream_t st);
-void launch_rs_bucket(const uint64_t* peers_send, const uint64_t* peer_pads, int* my_pad, int rank, int W, int bucket,
-                      int epoch, int64_t lo, int64_t len, float* rgrad, float* sumsq, int ctas, int* status,
-                      cudaStream_t st);
+// Push-then-reduce reduce-scatter of one bucket (two kernels on `st`).
+// done_ctr: int [PAD_MAXB] zeroed scratch.
+void launch_rs_bucket(const float* grad, const uint64_t* peers_recv, const void* my_recv, const uint64_t* peer_pads,
+                      int* my_pad, int* done_ctr, int rank, int W, int bucket, int epoch, int64_t lo, int64_t len,
+                      float* rgrad, float* sumsq, int ctas, int* status, int64_t wait_ns, cudaStream_t st);
 void launch_norm_exchange(const uint64_t* peer_pads, int* my_pad, int rank, int W, int epoch, const float* sumsq,
-                          float max_norm, float* coef, float* norm_out, int* status, cudaStream_t st);
+                          float max_norm, float* coef, float* norm_out, int* status, int64_t wait_ns,
+                          cudaStream_t st);
 void launch_adamw_allgather(const int64_t* buckets, int nb, int rank, int W, const float* rgrad, float* master,
                             float* m, float* v, const uint64_t* peers_param, const uint64_t* peer_pads, int* my_pad,
                             int epoch, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
-                            const float* coef, int* done_ctr, int* status, cudaStream_t st);
+                            const float* coef, int* done_ctr, int* status, int64_t wait_ns, cudaStream_t st);
 
 }  // namespace oxi

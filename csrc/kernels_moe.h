@@ -17,4 +17,12 @@ void launch_moe_gather_sum(const void* dxp, const int* pos, int64_t T, int k, in
 void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& b, bool b_mn, int n_groups,
                          const int* seg_off, int64_t group_rows_b, void* out, int64_t ldo, void* out2, int64_t ldo2,
                          const void* aux, int64_t ldaux, int* status, cudaStream_t st);
+// Router (router.cu): logits [T, E] (bf16 or f32, row stride ld) -> top-k
+// indices / weights [T, k], mean routing probability usage [E] (f32), and
+// optional per-expert selection counts [E].
+void launch_router_fwd(const void* logits, bool bf16, int64_t ld, int64_t T, int E, int k, int64_t* topi, float* topw,
+                       float* usage, int* counts, cudaStream_t st);
+void launch_router_bwd(const void* logits, bool bf16, int64_t ld, int64_t T, int E, int k, const int64_t* topi,
+                       const float* topw, const float* dtopw, const float* dusage, void* dlogits, int64_t ldd,
+                       cudaStream_t st);
 }  // namespace oxi

@@ -243,35 +243,41 @@ void adamw(torch::Tensor p, c10::optional<torch::Tensor> p16, torch::Tensor g, t
 // ------------------------------------------------------------ attention
 // q, k, v: [B*S, H*D]-shaped row-major bf16 views (unit inner stride)
 void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor lse, int64_t B,
-               int64_t S, int64_t Hq, int64_t Hk, int64_t D, double scale, bool causal, torch::Tensor status) {
+               int64_t S, int64_t Hq, int64_t Hk, int64_t Dqk, int64_t Dv, double scale, bool causal,
+               torch::Tensor status) {
   c10::cuda::CUDAGuard g(q.device());
   for (auto* t : {&q, &k, &v, &o})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 &&
                     t->size(0) == B * S, "attention operands must be bf16 [B*S, H*D] with unit inner stride");
-  TORCH_CHECK(q.size(1) == Hq * D && k.size(1) == Hk * D && v.size(1) == Hk * D && o.size(1) == Hq * D, "head dims");
+  TORCH_CHECK(q.size(1) == Hq * Dqk && k.size(1) == Hk * Dqk && v.size(1) == Hk * Dv && o.size(1) == Hq * Dv,
+              "head dims");
   TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.numel() == B * Hq * S && lse.is_contiguous(), "lse");
   oxi::launch_fa_fwd(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), o.data_ptr(),
-                     o.stride(0), lse.data_ptr<float>(), (int)B, (int)S, (int)Hq, (int)Hk, (int)D, (float)scale, causal,
-                     status_ptr(status), stream());
+                     o.stride(0), lse.data_ptr<float>(), (int)B, (int)S, (int)Hq, (int)Hk, (int)Dqk, (int)Dv,
+                     (float)scale, causal, status_ptr(status), stream());
 }
 
 void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
                torch::Tensor lse, torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dq, torch::Tensor dk,
-               torch::Tensor dv, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D, double scale, bool causal,
-               torch::Tensor status) {
+               torch::Tensor dv, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t Dqk, int64_t Dv, double scale,
+               bool causal, torch::Tensor status) {
   c10::cuda::CUDAGuard g(q.device());
   for (auto* t : {&q, &k, &v, &o, &dout, &dq, &dk, &dv})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 &&
                     t->size(0) == B * S, "attention tensors must be bf16 [B*S, H*D] with unit inner stride");
-  TORCH_CHECK(dk.stride(0) == dv.stride(0), "dk and dv must share a row stride");
-  TORCH_CHECK(dq_acc.scalar_type() == torch::kFloat32 && dq_acc.is_contiguous() && dq_acc.numel() == B * S * Hq * D,
-              "dq_acc must be contiguous f32 [B*S, Hq*D]");
+  TORCH_CHECK(dq.size(1) == Hq * Dqk && dk.size(1) == Hk * Dqk && dv.size(1) == Hk * Dv, "gradient head dims");
+  TORCH_CHECK(dq_acc.scalar_type() == torch::kFloat32 && dq_acc.is_contiguous() && dq_acc.numel() == B * S * Hq * Dqk,
+              "dq_acc must be contiguous f32 [B*S, Hq*Dqk]");
   TORCH_CHECK(delta.scalar_type() == torch::kFloat32 && delta.numel() == B * Hq * S, "delta");
   oxi::launch_fa_bwd(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), o.data_ptr(),
                      o.stride(0), dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(),
-                     dq_acc.data_ptr<float>(), dq.data_ptr(), dq.stride(0), dk.data_ptr(), dv.data_ptr(),
-                     dk.stride(0), (int)B, (int)S, (int)Hq, (int)Hk, (int)D, (float)scale, causal, status_ptr(status),
-                     stream());
+                     dq_acc.data_ptr<float>(), dq.data_ptr(), dq.stride(0), dk.data_ptr(), dk.stride(0), dv.data_ptr(),
+                     dv.stride(0), (int)B, (int)S, (int)Hq, (int)Hk, (int)Dqk, (int)Dv, (float)scale, causal,
+                     status_ptr(status), stream());
+}
+
+bool flash_supported(int64_t Dqk, int64_t Dv, bool backward) {
+  return backward ? oxi::fa_bwd_supported((int)Dqk, (int)Dv) : oxi::fa_supported((int)Dqk, (int)Dv);
 }
 
 // ------------------------------------------------------------ NVLink DDP runtime
@@ -305,28 +311,34 @@ void grad_to_bf16(torch::Tensor g, torch::Tensor out) {
   oxi::launch_grad_to_bf16(g.data_ptr<float>(), out.data_ptr(), g.numel(), stream());
 }
 
-void rs_bucket(torch::Tensor peers_send, torch::Tensor peer_pads, torch::Tensor my_pad, int64_t rank, int64_t W,
-               int64_t bucket, int64_t epoch, int64_t lo, int64_t len, torch::Tensor rgrad_shard, torch::Tensor sumsq,
-               int64_t ctas, torch::Tensor status) {
+void rs_bucket(torch::Tensor grad, torch::Tensor peers_recv, torch::Tensor my_recv, torch::Tensor peer_pads,
+               torch::Tensor my_pad, torch::Tensor done_ctr, int64_t rank, int64_t W, int64_t bucket, int64_t epoch,
+               int64_t lo, int64_t len, torch::Tensor rgrad_shard, torch::Tensor sumsq, int64_t ctas,
+               torch::Tensor status, int64_t wait_ns) {
   c10::cuda::CUDAGuard gd(my_pad.device());
-  oxi::launch_rs_bucket(reinterpret_cast<const uint64_t*>(peers_send.data_ptr<int64_t>()),
-                        reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
-                        (int)rank, (int)W, (int)bucket, (int)epoch, lo, len, rgrad_shard.data_ptr<float>(),
-                        sumsq.data_ptr<float>(), (int)ctas, status_ptr(status), stream());
+  TORCH_CHECK(grad.scalar_type() == torch::kFloat32 && grad.is_contiguous(), "grad must be contiguous f32");
+  TORCH_CHECK(done_ctr.scalar_type() == torch::kInt32 && done_ctr.numel() >= oxi::PAD_MAXB, "done_ctr");
+  oxi::launch_rs_bucket(grad.data_ptr<float>(), reinterpret_cast<const uint64_t*>(peers_recv.data_ptr<int64_t>()),
+                        my_recv.data_ptr(), reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()),
+                        my_pad.data_ptr<int>(), done_ctr.data_ptr<int>(), (int)rank, (int)W, (int)bucket, (int)epoch,
+                        lo, len, rgrad_shard.data_ptr<float>(), sumsq.data_ptr<float>(), (int)ctas,
+                        status_ptr(status), wait_ns, stream());
 }
 
 void norm_exchange(torch::Tensor peer_pads, torch::Tensor my_pad, int64_t rank, int64_t W, int64_t epoch,
-                   torch::Tensor sumsq, double max_norm, torch::Tensor coef, torch::Tensor norm, torch::Tensor status) {
+                   torch::Tensor sumsq, double max_norm, torch::Tensor coef, torch::Tensor norm, torch::Tensor status,
+                   int64_t wait_ns) {
   c10::cuda::CUDAGuard gd(my_pad.device());
   oxi::launch_norm_exchange(reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
                             (int)rank, (int)W, (int)epoch, sumsq.data_ptr<float>(), (float)max_norm,
-                            coef.data_ptr<float>(), norm.data_ptr<float>(), status_ptr(status), stream());
+                            coef.data_ptr<float>(), norm.data_ptr<float>(), status_ptr(status), wait_ns, stream());
 }
 
 void adamw_allgather(torch::Tensor buckets, int64_t rank, int64_t W, torch::Tensor rgrad, torch::Tensor master,
                      torch::Tensor m, torch::Tensor v, torch::Tensor peers_param, torch::Tensor peer_pads,
                      torch::Tensor my_pad, int64_t epoch, double lr, double b1, double b2, double eps, double wd,
-                     double bc1, double bc2, torch::Tensor coef, torch::Tensor done_ctr, torch::Tensor status) {
+                     double bc1, double bc2, torch::Tensor coef, torch::Tensor done_ctr, torch::Tensor status,
+                     int64_t wait_ns) {
   c10::cuda::CUDAGuard gd(my_pad.device());
   TORCH_CHECK(buckets.scalar_type() == torch::kInt64 && buckets.is_cuda() && buckets.dim() == 2 && buckets.size(1) == 3,
               "buckets must be int64 CUDA [nb, 3]");
@@ -336,7 +348,7 @@ void adamw_allgather(torch::Tensor buckets, int64_t rank, int64_t W, torch::Tens
                               reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
                               (int)epoch, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1,
                               (float)bc2, coef.data_ptr<float>(), done_ctr.data_ptr<int>(), status_ptr(status),
-                              stream());
+                              wait_ns, stream());
 }
 
 // ------------------------------------------------------------ SSM
@@ -484,6 +496,41 @@ std::vector<torch::Tensor> moe_permute(torch::Tensor x, torch::Tensor topi, int6
   return {counts, seg, pos, xp};
 }
 
+std::vector<torch::Tensor> router_fwd(torch::Tensor logits, int64_t k) {
+  c10::cuda::CUDAGuard g(logits.device());
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1 &&
+                  (logits.scalar_type() == torch::kBFloat16 || logits.scalar_type() == torch::kFloat32),
+              "router logits must be bf16/f32 [T, E] with unit inner stride");
+  const int64_t T = logits.size(0), E = logits.size(1);
+  auto dev = logits.device();
+  auto topi = torch::empty({T, k}, torch::TensorOptions().dtype(torch::kInt64).device(dev));
+  auto topw = torch::empty({T, k}, torch::TensorOptions().dtype(torch::kFloat32).device(dev));
+  auto usage = torch::empty({E}, torch::TensorOptions().dtype(torch::kFloat32).device(dev));
+  auto counts = torch::empty({E}, torch::TensorOptions().dtype(torch::kInt32).device(dev));
+  oxi::launch_router_fwd(logits.data_ptr(), logits.scalar_type() == torch::kBFloat16, logits.stride(0), T, (int)E,
+                         (int)k, topi.data_ptr<int64_t>(), topw.data_ptr<float>(), usage.data_ptr<float>(),
+                         counts.data_ptr<int>(), stream());
+  return {topi, topw, usage, counts};
+}
+
+torch::Tensor router_bwd(torch::Tensor logits, torch::Tensor topi, torch::Tensor topw, torch::Tensor dtopw,
+                         c10::optional<torch::Tensor> dusage) {
+  c10::cuda::CUDAGuard g(logits.device());
+  TORCH_CHECK(topi.is_contiguous() && topw.is_contiguous() && dtopw.is_contiguous() &&
+                  dtopw.scalar_type() == torch::kFloat32 && dtopw.numel() == topw.numel(), "router bwd operands");
+  const int64_t T = logits.size(0), E = logits.size(1), k = topi.size(1);
+  auto dl = torch::empty({T, E}, logits.options());
+  const float* du = nullptr;
+  if (dusage.has_value() && dusage->defined()) {
+    TORCH_CHECK(dusage->scalar_type() == torch::kFloat32 && dusage->is_contiguous() && dusage->numel() == E, "dusage");
+    du = dusage->data_ptr<float>();
+  }
+  oxi::launch_router_bwd(logits.data_ptr(), logits.scalar_type() == torch::kBFloat16, logits.stride(0), T, (int)E,
+                         (int)k, topi.data_ptr<int64_t>(), topw.data_ptr<float>(), dtopw.data_ptr<float>(), du,
+                         dl.data_ptr(), dl.stride(0), stream());
+  return dl;
+}
+
 void moe_zero_pad(torch::Tensor seg, torch::Tensor counts, torch::Tensor m) {
   c10::cuda::CUDAGuard g(m.device());
   oxi::launch_moe_zero_pad(seg.data_ptr<int>(), counts.data_ptr<int>(), (int)counts.numel(), m.data_ptr(),
@@ -563,12 +610,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw, "flat multi-tensor AdamW (f32 master, bf16 copy)");
   m.def("flash_fwd", &flash_fwd, "causal flash attention forward (tcgen05)");
   m.def("flash_bwd", &flash_bwd, "causal flash attention backward (tcgen05)");
+  m.def("flash_supported", &flash_supported, "whether a flash kernel exists for head dims (qk, v)");
   m.def("conv1d_fwd", &conv1d_fwd, "depthwise causal conv1d (+bias, +SiLU) forward");
   m.def("conv1d_bwd", &conv1d_bwd, "depthwise causal conv1d backward");
   m.def("ssm_scan_fwd", &ssm_scan_fwd, "Mamba2/3 selective scan forward");
   m.def("ssm_scan_bwd", &ssm_scan_bwd, "Mamba2/3 selective scan backward");
   m.def("mamba1_scan_fwd", &mamba1_scan_fwd, "Mamba1 selective scan forward (saves states)");
   m.def("mamba1_scan_bwd", &mamba1_scan_bwd, "Mamba1 selective scan backward");
+  m.def("router_fwd", &router_fwd, "MoE router softmax + top-k + usage");
+  m.def("router_bwd", &router_bwd, "MoE router backward");
   m.def("moe_permute", &moe_permute, "MoE counting-sort permutation into aligned expert segments");
   m.def("moe_zero_pad", &moe_zero_pad, "zero the padding rows of expert segments");
   m.def("moe_combine", &moe_combine, "weighted combine of expert outputs (+ residual)");
@@ -580,7 +630,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close, "unmap a peer's IPC buffer");
   m.def("pad_words", &pad_words, "int32 words of one signal pad");
   m.def("grad_to_bf16", &grad_to_bf16, "f32 gradient -> bf16 NVLink payload");
-  m.def("rs_bucket", &rs_bucket, "P2P reduce-scatter of one gradient bucket");
+  m.def("rs_bucket", &rs_bucket, "NVLink push + local reduce of one gradient bucket");
   m.def("norm_exchange", &norm_exchange, "cross-rank gradient norm and clip coefficient");
   m.def("adamw_allgather", &adamw_allgather, "sharded AdamW + P2P bf16 parameter all-gather");
 }

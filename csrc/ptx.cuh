@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the kernels use:
-// mbarriers, TMA (cp.async.bulk.tensor, never with cluster multicast),
+// mbarriers, TMA (cp.async.bulk.tensor, single-CTA loads of local memory),
 // tcgen05 (TMEM alloc, MMA, commit, ld) and bounded spin-waits.
 //
 // Every wait on an mbarrier or a flag is bounded by a %globaltimer deadline.

@@ -49,11 +49,26 @@ def route(logits: torch.Tensor, k: int):
 
 
 def aux_loss(probs: torch.Tensor, topi: torch.Tensor, E: int, kind: str = "mean_sq") -> torch.Tensor:
+    return aux_from_usage(probs.mean(0), torch.bincount(topi.reshape(-1), minlength=E), topi.numel(), E, kind)
+
+
+def aux_from_usage(usage: torch.Tensor, counts: torch.Tensor, n_sel: int, E: int, kind: str) -> torch.Tensor:
+    """Load-balancing loss from the mean routing probability per expert."""
     if kind == "switch":
-        f = torch.bincount(topi.reshape(-1), minlength=E).float() / topi.numel()
-        return E * (f.detach() * probs.mean(0)).sum()
-    usage = probs.mean(0)
+        f = counts.float() / n_sel
+        return E * (f.detach() * usage).sum()
     return usage.pow(2).mean()
+
+
+def route_with_aux(logits: torch.Tensor, k: int, E: int, kind: str):
+    """(top_idx, top_w, aux): the fused router kernel on CUDA, torch ops elsewhere."""
+    if logits.is_cuda:
+        from ..ops.moe_kernels import RouterTopK, router_ok
+        if router_ok(logits, k):
+            topi, topw, usage, counts = RouterTopK.apply(logits, k)
+            return topi, topw, aux_from_usage(usage, counts, topi.numel(), E, kind)
+    probs, topi, topw = route(logits, k)
+    return topi, topw, aux_loss(probs, topi, E, kind)
 
 
 class MoE(RefModule):
@@ -105,8 +120,7 @@ class MoE(RefModule):
         B, S, H = h.shape
         x = h.reshape(-1, H)
         logits = api.linear(x, self.router)
-        probs, topi, topw = route(logits, self.k)
-        aux = aux_loss(probs, topi, self.E, self.aux_kind)
+        topi, topw, aux = route_with_aux(logits, self.k, self.E, self.aux_kind)
         if self.ep_size > 1:
             from ..parallel.ep import ep_moe
             y = ep_moe(self, x, topi, topw)

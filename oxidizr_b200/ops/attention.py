@@ -2,8 +2,8 @@
 
 CUDA: the sm_100a flash-attention kernels (``csrc/flash_attn.cu``) when built;
 CPU: the materialised reference (model.rs:362-377).
-Layout: q [B, S, Hq, D], k/v [B, S, Hk, D] (GQA when Hk < Hq), output
-[B, S, Hq, D].
+Layout: q/k [B, S, H, Dqk], v [B, S, Hk, Dv] (GQA when Hk < Hq; Dqk > Dv for
+multi-head latent attention), output [B, S, Hq, Dv].
 """
 from __future__ import annotations
 
@@ -19,7 +19,15 @@ def _has_native_fa() -> bool:
 
 
 def native_ok(D: int, Dv: int = None) -> bool:
-    return (Dv is None or Dv == D) and D in (64, 128) and _has_native_fa()
+    """A flash kernel (forward and backward) exists for head dims (qk D, v Dv)."""
+    if not _has_native_fa():
+        return False
+    from ._C import ext
+    e = ext()
+    Dv = D if Dv is None else Dv
+    if hasattr(e, "flash_supported"):
+        return bool(e.flash_supported(D, Dv, True))
+    return Dv == D and D in (64, 128)
 
 
 def attention_qkv(qkv, Hq: int, Hk: int, D: int, scale: float, causal: bool = True):

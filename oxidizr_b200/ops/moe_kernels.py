@@ -84,3 +84,30 @@ def grouped_ok(x: torch.Tensor, w_gu: torch.Tensor) -> bool:
     E, I2, H = w_gu.shape
     return (x.is_cuda and x.dtype == torch.bfloat16 and I2 % 256 == 0 and H % 64 == 0
             and hasattr(ext(), "gemm_grouped"))
+
+
+class RouterTopK(torch.autograd.Function):
+    """Softmax router + top-k + renormalised weights + mean probability (csrc/router.cu).
+
+    Returns ``(topi [T,k] int64, topw [T,k] f32, usage [E] f32, counts [E] int32)``;
+    ``usage`` (mean routing probability per expert) and ``topw`` carry gradients.
+    """
+
+    @staticmethod
+    def forward(ctx, logits, k: int):
+        topi, topw, usage, counts = ext().router_fwd(logits, int(k))
+        ctx.save_for_backward(logits, topi, topw)
+        ctx.mark_non_differentiable(topi, counts)
+        return topi, topw, usage, counts
+
+    @staticmethod
+    def backward(ctx, _dtopi, dtopw, dusage, _dcounts):
+        logits, topi, topw = ctx.saved_tensors
+        dtopw = torch.zeros_like(topw) if dtopw is None else dtopw.float().contiguous()
+        du = None if dusage is None else dusage.float().contiguous()
+        return ext().router_bwd(logits, topi, topw, dtopw, du), None
+
+
+def router_ok(logits, k: int) -> bool:
+    return (logits.is_cuda and logits.dim() == 2 and logits.shape[1] <= 256 and k <= 16
+            and logits.dtype in (torch.bfloat16, torch.float32) and hasattr(ext(), "router_fwd"))

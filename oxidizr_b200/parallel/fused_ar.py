@@ -8,7 +8,9 @@ issued from our own kernels:
 
 * buckets of parameters (reverse order of use) are reduced as soon as
   backward has produced all their gradients, on a side stream, so the
-  transfers overlap the rest of backward;
+  transfers overlap the rest of backward: each rank casts its gradient to
+  bf16 and pushes every owner's part into the owner's receive slots (NVLink
+  stores), then sums its own shard's slots locally;
 * each rank keeps f32 master weights and AdamW moments for its 1/W shard of
   every bucket only (optimizer state sharded W ways);
 * after backward: one tiny kernel exchanges partial norms (global-norm clip),
@@ -67,13 +69,16 @@ class FusedDDPAdamW:
     """Drop-in optimizer for data-parallel training over NVLink (sync backend ``fused``)."""
 
     def __init__(self, named_params: Sequence[Tuple[str, torch.nn.Parameter]], cfg: AdamWConfig, device,
-                 group=None, bucket_bytes: int = 32 << 20, rs_ctas: int = 16):
+                 group=None, bucket_bytes: int = 32 << 20, rs_ctas: int = 16,
+                 peer_timeout_s: float = 30.0):
         self.cfg = cfg
         self.device = torch.device(device)
         self.group = group
         self.rank = dist.get_rank(group)
         self.W = dist.get_world_size(group)
         self.rs_ctas = rs_ctas
+        # a peer that has not posted its flag within this time is reported as failed
+        self.wait_ns = int(peer_timeout_s * 1e9)
         self.names = [n for n, _ in named_params]
         self.params = [p for _, p in named_params]
         assert all(p.dtype == torch.bfloat16 for p in self.params), "fused DDP needs bf16 parameters"
@@ -108,11 +113,10 @@ class FusedDDPAdamW:
         self.shard_numel = shard_off
         # ---- buffers
         dev = self.device
-        self.send = SymmetricBuffer(self.N * 2, dev, group)
+        self.recv = SymmetricBuffer(self.N * 2, dev, group)
         self.param = SymmetricBuffer(self.N * 2, dev, group)
         self.pad = SymmetricBuffer(ext().pad_words() * 4, dev, group)
         self.flat = self.param.local.view(torch.bfloat16)
-        self.send_flat = self.send.local.view(torch.bfloat16)
         self.pad_local = self.pad.local.view(torch.int32)
         self.grad = torch.zeros(self.N, dtype=torch.float32, device=dev)
         with torch.no_grad():
@@ -135,6 +139,7 @@ class FusedDDPAdamW:
         self._coef = torch.zeros(1, dtype=torch.float32, device=dev)
         self._norm = torch.zeros(1, dtype=torch.float32, device=dev)
         self._done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._push_done = torch.zeros(512, dtype=torch.int32, device=dev)
         self.comm_stream = torch.cuda.Stream(device=dev)
         self.epoch = 1
         self.step_count = 0
@@ -172,9 +177,9 @@ class FusedDDPAdamW:
             if not self._sumsq_zeroed:
                 self._sumsq.zero_()
                 self._sumsq_zeroed = True
-            e.grad_to_bf16(self.grad[lo:lo + ln], self.send_flat[lo:lo + ln])
-            e.rs_bucket(self.send.ptr_table, self.pad.ptr_table, self.pad_local, self.rank, self.W, bi, self.epoch,
-                        lo, ln, self.rgrad[so:so + ln // self.W], self._sumsq, self.rs_ctas, status(self.device))
+            e.rs_bucket(self.grad, self.recv.ptr_table, self.recv.local, self.pad.ptr_table, self.pad_local,
+                        self._push_done, self.rank, self.W, bi, self.epoch, lo, ln, self.rgrad[so:so + ln // self.W],
+                        self._sumsq, self.rs_ctas, status(self.device), self.wait_ns)
 
     # ------------------------------------------------------------ step
     def step(self, grad_scale: float = 1.0) -> torch.Tensor:
@@ -191,13 +196,14 @@ class FusedDDPAdamW:
         self.step_count += 1
         t = self.step_count
         e.norm_exchange(self.pad.ptr_table, self.pad_local, self.rank, self.W, self.epoch, self._sumsq,
-                        float(c.max_grad_norm or 0.0), self._coef, self._norm, status(self.device))
+                        float(c.max_grad_norm or 0.0), self._coef, self._norm, status(self.device),
+                        self.wait_ns)
         if grad_scale != 1.0:
             self._coef.mul_(grad_scale)
         e.adamw_allgather(self.bucket_table, self.rank, self.W, self.rgrad, self.master, self.m, self.v,
                           self.param.ptr_table, self.pad.ptr_table, self.pad_local, self.epoch, c.lr, c.beta1,
                           c.beta2, c.eps, c.weight_decay, 1.0 - c.beta1 ** t, 1.0 - c.beta2 ** t, self._coef,
-                          self._done, status(self.device))
+                          self._done, status(self.device), self.wait_ns)
         self.grad.zero_()
         self.epoch += 1
         self._pending = [len(b[3]) for b in self.buckets]
@@ -235,5 +241,5 @@ class FusedDDPAdamW:
 
     def close(self):
         torch.cuda.synchronize(self.device)
-        for b in (self.send, self.param, self.pad):
+        for b in (self.recv, self.param, self.pad):
             b.close()

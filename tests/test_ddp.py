@@ -51,3 +51,29 @@ def test_fused_ddp_matches_nccl(tmp_path):
         assert abs(la - lb) < 2e-2 * abs(la), (a["losses"], b["losses"])
     for na, nb in zip(a["grad_norms"], b["grad_norms"]):
         assert abs(na - nb) < 5e-2 * abs(na) + 1e-3, (a["grad_norms"], b["grad_norms"])
+
+
+@pytest.mark.gpu
+def test_peer_wait_gives_up_and_reports():
+    """A peer flag that nobody sets: the norm exchange stops waiting after its
+    limit, records the peer-timeout status and disables the update (coef 0),
+    and the device stays usable afterwards.  Runs as one kernel on one GPU."""
+    import time
+    from oxidizr_b200.ops._C import ext, read_status, status
+    dev = torch.device("cuda", 0)
+    read_status(dev)
+    pad = torch.zeros(ext().pad_words(), dtype=torch.int32, device=dev)
+    # a two-rank job whose "peer" pad is our own: rank 0 posts its flag, rank 1's never comes
+    table = torch.tensor([pad.data_ptr(), pad.data_ptr()], dtype=torch.int64, device=dev)
+    sumsq = torch.ones(1, device=dev)
+    coef = torch.full((1,), 7.0, device=dev)
+    norm = torch.zeros(1, device=dev)
+    t0 = time.time()
+    ext().norm_exchange(table, pad, 0, 2, 1, sumsq, 1.0, coef, norm, status(dev), int(0.2e9))
+    torch.cuda.synchronize(dev)
+    dt = time.time() - t0
+    assert read_status(dev) == 2  # OXI_ERR_TIMEOUT_PEER
+    assert coef.item() == 0.0 and norm.isnan().item()
+    assert dt < 5.0
+    x = torch.randn(1000, device=dev)
+    assert abs((x * 2).sum().item() - 2 * x.sum().item()) < 1e-2

@@ -26,7 +26,7 @@ def test_flash_fwd(D, B, S, Hq, Hk):
     o = torch.empty(B * S, Hq * D, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B, Hq, S, device="cuda")
     scale = 1.0 / math.sqrt(D)
-    ext().flash_fwd(q, k, v, o, lse, B, S, Hq, Hk, D, scale, True, status("cuda"))
+    ext().flash_fwd(q, k, v, o, lse, B, S, Hq, Hk, D, D, scale, True, status("cuda"))
     torch.cuda.synchronize()
     check_status("cuda")
     qr, kr, vr = (t.reshape(B, S, -1, D) for t in (q, k, v))
@@ -66,4 +66,32 @@ def test_flash_bwd_qkv(D, B, S, Hq, Hk):
     g, gr = qkv.grad.float(), x.grad
     for name, sl in (("q", slice(0, Hq * D)), ("k", slice(Hq * D, (Hq + Hk) * D)), ("v", slice((Hq + Hk) * D, N))):
         e = ((g[..., sl] - gr[..., sl]).norm() / gr[..., sl].norm()).item()
+        assert e < 3e-2, (name, e)
+
+
+@pytest.mark.parametrize("Dqk,Dv", [(96, 64), (128, 64)])
+@pytest.mark.parametrize("B,S,H", [(2, 300, 3), (1, 512, 12)])
+def test_flash_mla_head_dims(Dqk, Dv, B, S, H):
+    """Multi-head latent attention shapes: q/k carry a RoPE part (Dqk > Dv)."""
+    from oxidizr_b200.ops.flash import FlashAttention
+    from oxidizr_b200.ops._C import check_status
+    torch.manual_seed(Dqk + S + H)
+    q = torch.randn(B, S, H, Dqk, device="cuda").bfloat16().requires_grad_()
+    k = torch.randn(B, S, H, Dqk, device="cuda").bfloat16().requires_grad_()
+    # v as a strided view of a wider buffer, like the fused k|v up-projection output
+    kv = torch.randn(B, S, 2 * H * Dv, device="cuda").bfloat16()
+    v = kv[..., H * Dv:].view(B, S, H, Dv).requires_grad_()
+    scale = 1.0 / math.sqrt(Dqk)
+    o = FlashAttention.apply(q, k, v, scale, True)
+    do = torch.randn_like(o)
+    o.backward(do)
+    torch.cuda.synchronize()
+    check_status("cuda")
+    qr, kr, vr = (t.detach().float().requires_grad_() for t in (q, k, v))
+    ref = _ref(qr, kr, vr, scale)
+    ref.backward(do.float())
+    assert o.shape == (B, S, H, Dv)
+    assert ((o.float() - ref).norm() / ref.norm()).item() < 1e-2
+    for name, a, r in (("q", q.grad, qr.grad), ("k", k.grad, kr.grad), ("v", v.grad, vr.grad)):
+        e = ((a.float() - r).norm() / r.norm()).item()
         assert e < 3e-2, (name, e)

@@ -176,3 +176,26 @@ def test_grouped_experts_vs_dense(T, H, I, E, k):
     assert _rel(w_gu.grad, gr.grad) < 3e-2
     assert _rel(w_down.grad, dr.grad) < 3e-2
     assert _rel(topw.grad, twr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("T,E,k,dt", [(1000, 32, 4, torch.bfloat16), (777, 64, 8, torch.float32),
+                                      (300, 256, 16, torch.bfloat16), (50, 8, 2, torch.float32)])
+def test_router_topk_vs_torch(T, E, k, dt):
+    from oxidizr_b200.models.moe import aux_from_usage, route
+    from oxidizr_b200.ops.moe_kernels import RouterTopK
+    torch.manual_seed(T + E)
+    # distinct, exactly representable logits per row: no ties, so the top-k order is unique
+    perm = torch.stack([torch.randperm(E) for _ in range(T)]).float()
+    logits = ((perm - E / 2) / 32).to("cuda", dt).requires_grad_()
+    topi, topw, usage, counts = RouterTopK.apply(logits, k)
+    cw = torch.randn(T, k, device="cuda")
+    aux = aux_from_usage(usage, counts, T * k, E, "mean_sq")
+    ((topw * cw).sum() + 3.0 * aux).backward()
+    lr = logits.detach().float().requires_grad_()
+    probs, ti, tw = route(lr, k)
+    assert torch.equal(topi.cpu(), ti.cpu())
+    assert torch.allclose(topw, tw, atol=1e-5, rtol=1e-4)
+    assert torch.allclose(usage, probs.mean(0), atol=1e-6, rtol=1e-4)
+    assert torch.equal(counts.long().cpu(), torch.bincount(ti.reshape(-1), minlength=E).cpu())
+    ((tw * cw).sum() + 3.0 * probs.mean(0).pow(2).mean()).backward()
+    assert _rel(logits.grad, lr.grad) < (1e-2 if dt == torch.bfloat16 else 1e-4)
