@@ -188,18 +188,16 @@ def main():
     m, tcfg = cfg.model, cfg.trainer
     B, S, V = tcfg.batch_size, m.max_seq_len, m.vocab_size
     torch.manual_seed(1234)
-    model = build_model(m, device=dev, seed=0)
+    # MoE configs: experts spread over all ranks (expert parallel = data parallel group)
+    ep = world if (world > 1 and m.num_experts) else 1
+    model = build_model(m, device=dev, seed=0, ep_group=dist.group.WORLD if ep > 1 else None)
     ocfg = AdamWConfig(lr=tcfg.learning_rate)
     backend = args.sync_backend
     if world > 1:
         if backend == "auto":
             backend = "fused"
-        if backend == "fused":
-            from oxidizr_b200.parallel.fused_ar import FusedDDPAdamW
-            opt = FusedDDPAdamW(list(model.named_parameters()), ocfg, dev)
-        else:
-            from oxidizr_b200.parallel.ddp import DDPAdamW
-            opt = DDPAdamW(FlatParams(list(model.named_parameters()), dev), ocfg, backend=backend)
+        from oxidizr_b200.parallel.ddp import make_ddp_optimizer
+        opt = make_ddp_optimizer(model.named_parameters(), ocfg, dev, backend)
     else:
         backend = "single"
         opt = AdamW(FlatParams(list(model.named_parameters()), dev), ocfg)
@@ -303,7 +301,7 @@ def main():
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded uniform u32 tokens, random-init weights)",
-        "config": {"model": MODELS[args.model][0], "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
+        "config": {"model": MODELS[args.model][0], "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}" + (f"+ep{ep}" if ep > 1 else ""),
                    "micro_batch_per_gpu": B, "grad_accum": 1, "sync_backend": backend,
                    "l2": "no flush: per-step working set (weights, optimizer state, activations: GBs) >> 126 MB L2"},
         "clocks": clocks, "e2e": e2e, "gpu_launches": n_launch,

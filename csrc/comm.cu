@@ -93,21 +93,37 @@ __global__ void grad_to_bf16_kernel(const float* __restrict__ g, __nv_bfloat16* 
 // NVLink stores are posted writes, so no thread waits on a round trip.  The
 // last CTA to finish publishes the bucket's epoch in every peer's pad.
 template <int W>
-__global__ void __launch_bounds__(256) push_bucket_kernel(const float* __restrict__ grad, int64_t lo, int64_t len,
+__global__ void __launch_bounds__(512) push_bucket_kernel(const float* __restrict__ grad, int64_t lo, int64_t len,
                                                           int rank, const uint64_t* __restrict__ peers_recv,
                                                           const uint64_t* __restrict__ peer_pads, int bucket,
                                                           int epoch, int* __restrict__ done_ctr) {
+  constexpr int UNR = 4;  // 8-element vectors per thread in flight (128 B of f32 loads)
   const int64_t shard = len / W;
   const int64_t nv = len / 8;
   const int64_t sv = shard / 8;  // 8-element vectors per shard
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
-    const float4 a = reinterpret_cast<const float4*>(grad + lo)[2 * v];
-    const float4 b = reinterpret_cast<const float4*>(grad + lo)[2 * v + 1];
-    const int owner = (int)(v / sv);
-    const int64_t i = v - (int64_t)owner * sv;
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers_recv[owner]) + lo + (int64_t)rank * shard;
-    reinterpret_cast<uint4*>(dst)[i] =
-        make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float4* g4 = reinterpret_cast<const float4*>(grad + lo);
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nv; base += stride * UNR) {
+    float4 a[UNR], b[UNR];
+#pragma unroll
+    for (int r = 0; r < UNR; ++r) {
+      const int64_t v = base + r * stride;
+      if (v < nv) {
+        a[r] = g4[2 * v];
+        b[r] = g4[2 * v + 1];
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < UNR; ++r) {
+      const int64_t v = base + r * stride;
+      if (v < nv) {
+        const int owner = (int)(v / sv);
+        const int64_t i = v - (int64_t)owner * sv;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers_recv[owner]) + lo + (int64_t)rank * shard;
+        reinterpret_cast<uint4*>(dst)[i] = make_uint4(pack_bf16(a[r].x, a[r].y), pack_bf16(a[r].z, a[r].w),
+                                                      pack_bf16(b[r].x, b[r].y), pack_bf16(b[r].z, b[r].w));
+      }
+    }
   }
   __threadfence_system();
   __syncthreads();
@@ -139,20 +155,31 @@ __global__ void __launch_bounds__(512) reduce_bucket_kernel(const __nv_bfloat16*
   __syncthreads();
   float ss = 0.f;
   if (ok_s) {
+    constexpr int UNR = (16 / W) < 1 ? 1 : ((16 / W) > 4 ? 4 : 16 / W);
     const uint4* src = reinterpret_cast<const uint4*>(recv + lo);
     const int64_t sv = shard / 8;
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < sv; v += (int64_t)gridDim.x * blockDim.x) {
-      uint4 u[W];
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < sv; base += stride * UNR) {
+      uint4 u[UNR][W];
 #pragma unroll
-      for (int r = 0; r < W; ++r) u[r] = src[r * sv + v];
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int q = 0; q < UNR; ++q) {
+        const int64_t v = base + q * stride;
 #pragma unroll
-      for (int r = 0; r < W; ++r) add8(acc, u[r]);
-      float4* o = reinterpret_cast<float4*>(rgrad + v * 8);  // rgrad points at this bucket's shard
-      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        for (int r = 0; r < W; ++r) u[q][r] = v < sv ? src[r * sv + v] : make_uint4(0u, 0u, 0u, 0u);
+      }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
+      for (int q = 0; q < UNR; ++q) {
+        const int64_t v = base + q * stride;
+        if (v >= sv) break;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int r = 0; r < W; ++r) add8(acc, u[q][r]);
+        float4* o = reinterpret_cast<float4*>(rgrad + v * 8);  // rgrad points at this bucket's shard
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
+      }
     }
   }
 #pragma unroll
@@ -164,6 +191,111 @@ __global__ void __launch_bounds__(512) reduce_bucket_kernel(const __nv_bfloat16*
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
     if (threadIdx.x == 0) atomicAdd(sumsq, t);
+  }
+}
+
+// Reduce-scatter of one bucket, pull through the TMA engine.
+//
+// Every rank has cast its gradient of the bucket to bf16 in its own send
+// buffer (grad_to_bf16) and posts the bucket's epoch (CTA 0).  Each CTA of the
+// owner then streams its chunks of the owned shard from all W send buffers
+// into shared memory with bulk copies (one producer thread, RS_STAGES deep;
+// the copy engine keeps the NVLink reads in flight, not the threads) and the
+// consumer warps sum the W slices in f32.
+constexpr int RS_STAGES = 3;
+constexpr int RS_STAGE_BYTES = 8192;  // small enough to share an SM with a GEMM CTA
+constexpr int RS_CONSUMERS = 128;
+__host__ __device__ constexpr int rs_chunk_elems(int W) { return (RS_STAGE_BYTES / 2 / W) / 64 * 64; }
+
+template <int W>
+__global__ void __launch_bounds__(RS_CONSUMERS + 32) rs_tma_kernel(
+    const uint64_t* __restrict__ peers_send, const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad,
+    int rank, int bucket, int epoch, int64_t lo, int64_t len, float* __restrict__ rgrad, float* __restrict__ sumsq,
+    int* status, uint64_t wait_ns) {
+  constexpr int CE = rs_chunk_elems(W);  // elements per peer per chunk (a multiple of 64)
+  __shared__ __align__(128) uint4 sbuf[RS_STAGES * RS_STAGE_BYTES / 16];
+  __shared__ uint64_t full[RS_STAGES], empty[RS_STAGES];
+  __shared__ int abort_s, ok_s;
+  __shared__ float red[8];
+  const __nv_bfloat16* stage_base = reinterpret_cast<const __nv_bfloat16*>(sbuf);
+  const int64_t shard = len / W;
+  const int64_t s0 = lo + rank * shard;
+  const int64_t nch = (shard + CE - 1) / CE;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < RS_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], RS_CONSUMERS / 32);
+    }
+    abort_s = 0;
+    fence_mbar_init();
+    if (blockIdx.x == 0) {
+      // the send buffer of this bucket was written by the previous kernel on
+      // this stream; make it visible system-wide, then tell every peer.
+      __threadfence_system();
+      for (int i = 0; i < W; ++i)
+        st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_READY + bucket * PAD_MAXW + rank, epoch);
+    }
+    ok_s = wait_flags(my_pad + PAD_READY + bucket * PAD_MAXW, W, 1, epoch, status, wait_ns) ? 1 : 0;
+  }
+  __syncthreads();
+  float ss = 0.f;
+  if (ok_s) {
+    if (warp == 0) {
+      if (lane == 0) {
+        int64_t it = 0;
+        for (int64_t c = blockIdx.x; c < nch; c += gridDim.x, ++it) {
+          const int st = (int)(it % RS_STAGES);
+          const uint32_t ph = (uint32_t)((it / RS_STAGES) & 1);
+          if (!mbar_wait(&empty[st], ph ^ 1, &abort_s, status)) break;
+          const int64_t e0 = c * CE;
+          const int n = (int)min((int64_t)CE, shard - e0);
+          mbar_arrive_expect_tx(&full[st], (uint32_t)(W * n * 2));
+#pragma unroll
+          for (int r = 0; r < W; ++r) {
+            const int peer = (rank + r) % W;  // stagger peers so ranks do not all hit the same one
+            bulk_load(const_cast<__nv_bfloat16*>(stage_base) + (st * W + r) * CE,
+                      reinterpret_cast<const __nv_bfloat16*>(peers_send[peer]) + s0 + e0, (uint32_t)(n * 2),
+                      &full[st]);
+          }
+        }
+        // leave no copy in flight into this CTA's shared memory
+        for (int64_t j = (it > RS_STAGES ? it - RS_STAGES : 0); j < it; ++j)
+          mbar_wait(&full[j % RS_STAGES], (uint32_t)((j / RS_STAGES) & 1), nullptr, status);
+      }
+      __syncwarp();
+    } else {
+      const int t = threadIdx.x - 32;
+      int64_t it = 0;
+      for (int64_t c = blockIdx.x; c < nch; c += gridDim.x, ++it) {
+        const int st = (int)(it % RS_STAGES);
+        const uint32_t ph = (uint32_t)((it / RS_STAGES) & 1);
+        if (!mbar_wait(&full[st], ph, &abort_s, status)) break;
+        const int64_t e0 = c * CE;
+        const int n = (int)min((int64_t)CE, shard - e0);
+        for (int v = t; v < n / 8; v += RS_CONSUMERS) {
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int r = 0; r < W; ++r) add8(acc, reinterpret_cast<const uint4*>(stage_base + (st * W + r) * CE)[v]);
+          float4* o = reinterpret_cast<float4*>(rgrad + e0 + v * 8);  // rgrad points at this bucket's shard
+          o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+          o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0 && warp > 0) red[warp - 1] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tsum = 0.f;
+    for (int i = 0; i < RS_CONSUMERS / 32; ++i) tsum += red[i];
+    atomicAdd(sumsq, tsum);
   }
 }
 
@@ -204,6 +336,12 @@ __device__ __forceinline__ float adamw_one(float g, float& m, float& v, float& p
   return p;
 }
 
+// One CTA updates 2048-element chunks of the owned shards (8 elements per
+// thread), stages the bf16 result in shared memory and sends it to every rank
+// (itself included) with W bulk stores; the copy engine carries the NVLink
+// writes while the threads go on with the next chunk (double-buffered).
+constexpr int AG_CHUNK = 2048;
+
 template <int W>
 __global__ void __launch_bounds__(256) adamw_allgather_kernel(
     const int64_t* __restrict__ buckets, int nb, int rank, const float* __restrict__ rgrad,
@@ -211,45 +349,67 @@ __global__ void __launch_bounds__(256) adamw_allgather_kernel(
     const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad, int epoch, float lr, float b1, float b2,
     float eps, float wd, float bc1, float bc2, const float* __restrict__ coef, int* __restrict__ done_ctr, int* status,
     uint64_t wait_ns) {
+  __shared__ __align__(128) uint4 stage[2][AG_CHUNK / 8];
   const float gs = *coef;
   const float rb1 = 1.f / bc1, rb2 = 1.f / bc2;
   const bool failed = status && *reinterpret_cast<volatile int*>(status) != 0;
+  int sb = 0;  // staging buffer
   if (!failed) {
-    __nv_bfloat16* dst[W];
-#pragma unroll
-    for (int j = 0; j < W; ++j) dst[j] = reinterpret_cast<__nv_bfloat16*>(peers_param[(rank + j) % W]);
     for (int b = 0; b < nb; ++b) {
       const int64_t lo = buckets[3 * b], len = buckets[3 * b + 1], so = buckets[3 * b + 2];
       const int64_t shard = len / W;
       const int64_t p0 = lo + rank * shard;
-      const int64_t nv = shard / 8;
-      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t e = so + i * 8;  // shard offsets are multiples of 8 elements
-        float4 g4[2], m4[2], v4[2], p4[2];
+      const int64_t nch = (shard + AG_CHUNK - 1) / AG_CHUNK;
+      for (int64_t c = blockIdx.x; c < nch; c += gridDim.x) {
+        const int64_t c0 = c * AG_CHUNK;
+        const int n = (int)min((int64_t)AG_CHUNK, shard - c0);
+        // the staging buffer is free once the bulk stores issued from it two chunks ago have read it
+        if (threadIdx.x == 0) bulk_wait_read<1>();
+        __syncthreads();
+        const int i = threadIdx.x;
+        if (i * 8 < n) {
+          const int64_t e = so + c0 + i * 8;  // shard offsets are multiples of 64 elements
+          float4 g4[2], m4[2], v4[2], p4[2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          g4[h] = reinterpret_cast<const float4*>(rgrad + e)[h];
-          m4[h] = reinterpret_cast<const float4*>(m + e)[h];
-          v4[h] = reinterpret_cast<const float4*>(v + e)[h];
-          p4[h] = reinterpret_cast<const float4*>(master + e)[h];
+          for (int h = 0; h < 2; ++h) {
+            g4[h] = reinterpret_cast<const float4*>(rgrad + e)[h];
+            m4[h] = reinterpret_cast<const float4*>(m + e)[h];
+            v4[h] = reinterpret_cast<const float4*>(v + e)[h];
+            p4[h] = reinterpret_cast<const float4*>(master + e)[h];
+          }
+          float pw[8];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            pw[4 * h + 0] = adamw_one(g4[h].x * gs, m4[h].x, v4[h].x, p4[h].x, b1, b2, rb1, rb2, lr, eps, wd);
+            pw[4 * h + 1] = adamw_one(g4[h].y * gs, m4[h].y, v4[h].y, p4[h].y, b1, b2, rb1, rb2, lr, eps, wd);
+            pw[4 * h + 2] = adamw_one(g4[h].z * gs, m4[h].z, v4[h].z, p4[h].z, b1, b2, rb1, rb2, lr, eps, wd);
+            pw[4 * h + 3] = adamw_one(g4[h].w * gs, m4[h].w, v4[h].w, p4[h].w, b1, b2, rb1, rb2, lr, eps, wd);
+            reinterpret_cast<float4*>(m + e)[h] = m4[h];
+            reinterpret_cast<float4*>(v + e)[h] = v4[h];
+            reinterpret_cast<float4*>(master + e)[h] = p4[h];
+          }
+          stage[sb][i] = make_uint4(pack_bf16(pw[0], pw[1]), pack_bf16(pw[2], pw[3]), pack_bf16(pw[4], pw[5]),
+                                    pack_bf16(pw[6], pw[7]));
         }
-        float pw[8];
+        fence_proxy_async_smem();  // the staged bytes are read by the bulk-copy (async) proxy
+        __syncthreads();
+        if (threadIdx.x == 0) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          pw[4 * h + 0] = adamw_one(g4[h].x * gs, m4[h].x, v4[h].x, p4[h].x, b1, b2, rb1, rb2, lr, eps, wd);
-          pw[4 * h + 1] = adamw_one(g4[h].y * gs, m4[h].y, v4[h].y, p4[h].y, b1, b2, rb1, rb2, lr, eps, wd);
-          pw[4 * h + 2] = adamw_one(g4[h].z * gs, m4[h].z, v4[h].z, p4[h].z, b1, b2, rb1, rb2, lr, eps, wd);
-          pw[4 * h + 3] = adamw_one(g4[h].w * gs, m4[h].w, v4[h].w, p4[h].w, b1, b2, rb1, rb2, lr, eps, wd);
-          reinterpret_cast<float4*>(m + e)[h] = m4[h];
-          reinterpret_cast<float4*>(v + e)[h] = v4[h];
-          reinterpret_cast<float4*>(master + e)[h] = p4[h];
+          for (int j = 0; j < W; ++j) {
+            const int dst = (rank + j) % W;
+            bulk_store(reinterpret_cast<__nv_bfloat16*>(peers_param[dst]) + p0 + c0, &stage[sb][0],
+                       (uint32_t)(n * 2));
+          }
+          bulk_commit();
         }
-        const uint4 packed = make_uint4(pack_bf16(pw[0], pw[1]), pack_bf16(pw[2], pw[3]), pack_bf16(pw[4], pw[5]),
-                                        pack_bf16(pw[6], pw[7]));
-#pragma unroll
-        for (int j = 0; j < W; ++j) reinterpret_cast<uint4*>(dst[j] + p0)[i] = packed;
+        sb ^= 1;
       }
     }
+  }
+  // every bulk store of this CTA has been performed before the epoch is published
+  if (threadIdx.x == 0) {
+    bulk_wait<0>();
+    fence_proxy_async_global();
   }
   // last CTA to finish publishes this rank's epoch to every peer, then waits for all
   __threadfence_system();
@@ -309,25 +469,42 @@ void launch_grad_to_bf16(const float* g, void* out, int64_t n, cudaStream_t st) 
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_rs_bucket(const float* grad, const uint64_t* peers_recv, const void* my_recv, const uint64_t* peer_pads,
+void launch_rs_bucket(int mode, const float* grad, const uint64_t* peers_buf, void* my_buf, const uint64_t* peer_pads,
                       int* my_pad, int* done_ctr, int rank, int W, int bucket, int epoch, int64_t lo, int64_t len,
                       float* rgrad, float* sumsq, int ctas, int* status, int64_t wait_ns, cudaStream_t st) {
   OXI_CHECK(W <= PAD_MAXW && bucket < PAD_MAXB, "too many ranks or buckets");
-  OXI_CHECK(len % (W * 8) == 0, "bucket length must divide into 8-element shards");
-  const int push_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / 8 + 255) / 256, 1), (int64_t)ctas * 2);
-  const int red_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / W / 8 + 511) / 512, 1), (int64_t)ctas);
-  const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(my_recv);
-  switch (W) {
+  OXI_CHECK(len % (W * 64) == 0, "bucket length must divide into 64-element shards");
+  OXI_CHECK(W >= 1 && W <= 8, "fused data parallelism supports 1..8 ranks per node, got ", W);
+  if (mode == 0) {
+    // pull: local cast into the send buffer, then TMA-fed reduction of the owned shard
+    launch_grad_to_bf16(grad + lo, reinterpret_cast<__nv_bfloat16*>(my_buf) + lo, len, st);
+    const int64_t nch = (len / W + rs_chunk_elems(W) - 1) / rs_chunk_elems(W);
+    const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)ctas));
+    switch (W) {
+#define OXI_RS(N)                                                                                              \
+  case N:                                                                                                      \
+    rs_tma_kernel<N><<<g, RS_CONSUMERS + 32, 0, st>>>(peers_buf, peer_pads, my_pad, rank, bucket, epoch, lo, len, \
+                                                      rgrad, sumsq, status, (uint64_t)wait_ns);                 \
+    break;
+      OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)
+#undef OXI_RS
+    }
+  } else {
+    // push: cast + NVLink stores into the owners' receive slots, then a local reduction
+    const int push_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / 8 + 511) / 512, 1), (int64_t)ctas);
+    const int red_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / W / 8 + 511) / 512, 1), (int64_t)ctas);
+    const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(my_buf);
+    switch (W) {
 #define OXI_RS(N)                                                                                                \
   case N:                                                                                                        \
-    push_bucket_kernel<N><<<push_ctas, 256, 0, st>>>(grad, lo, len, rank, peers_recv, peer_pads, bucket, epoch,  \
+    push_bucket_kernel<N><<<push_ctas, 512, 0, st>>>(grad, lo, len, rank, peers_buf, peer_pads, bucket, epoch,   \
                                                      done_ctr);                                                  \
     reduce_bucket_kernel<N><<<red_ctas, 512, 0, st>>>(rv, my_pad, bucket, epoch, lo, len, rgrad, sumsq, status, \
                                                       (uint64_t)wait_ns);                                        \
     break;
-    OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)
+      OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)
 #undef OXI_RS
-    default: OXI_CHECK(false, "fused data parallelism supports 1..8 ranks per node, got ", W);
+    }
   }
   OXI_CUDA_CHECK(cudaGetLastError());
 }

@@ -24,9 +24,12 @@ void* ipc_open(const std::string& handle);
 void ipc_close(void* p);
 
 void launch_grad_to_bf16(const float* g, void* out, int64_t n, cudaStream_t st);
-// Push-then-reduce reduce-scatter of one bucket (two kernels on `st`).
-// done_ctr: int [PAD_MAXB] zeroed scratch.
-void launch_rs_bucket(const float* grad, const uint64_t* peers_recv, const void* my_recv, const uint64_t* peer_pads,
+// Reduce-scatter of one bucket.  mode 0 (pull): cast grad into this rank's
+// send buffer `my_buf`, then read the owned shard from every peer's send
+// buffer with TMA bulk copies.  mode 1 (push): cast + store each owner's part
+// into the owner's receive buffer, then reduce locally.  `peers_buf` holds the
+// peers' send (pull) or receive (push) buffers.  done_ctr: int [PAD_MAXB].
+void launch_rs_bucket(int mode, const float* grad, const uint64_t* peers_buf, void* my_buf, const uint64_t* peer_pads,
                       int* my_pad, int* done_ctr, int rank, int W, int bucket, int epoch, int64_t lo, int64_t len,
                       float* rgrad, float* sumsq, int ctas, int* status, int64_t wait_ns, cudaStream_t st);
 void launch_norm_exchange(const uint64_t* peer_pads, int* my_pad, int rank, int W, int epoch, const float* sumsq,

@@ -10,6 +10,7 @@
 #include "kernels_comm.h"
 #include "kernels_ssm.h"
 #include "kernels_moe.h"
+#include "kernels_ep.h"
 
 using oxi::Mat;
 
@@ -311,15 +312,16 @@ void grad_to_bf16(torch::Tensor g, torch::Tensor out) {
   oxi::launch_grad_to_bf16(g.data_ptr<float>(), out.data_ptr(), g.numel(), stream());
 }
 
-void rs_bucket(torch::Tensor grad, torch::Tensor peers_recv, torch::Tensor my_recv, torch::Tensor peer_pads,
+void rs_bucket(int64_t mode, torch::Tensor grad, torch::Tensor peers_buf, torch::Tensor my_buf, torch::Tensor peer_pads,
                torch::Tensor my_pad, torch::Tensor done_ctr, int64_t rank, int64_t W, int64_t bucket, int64_t epoch,
                int64_t lo, int64_t len, torch::Tensor rgrad_shard, torch::Tensor sumsq, int64_t ctas,
                torch::Tensor status, int64_t wait_ns) {
   c10::cuda::CUDAGuard gd(my_pad.device());
   TORCH_CHECK(grad.scalar_type() == torch::kFloat32 && grad.is_contiguous(), "grad must be contiguous f32");
   TORCH_CHECK(done_ctr.scalar_type() == torch::kInt32 && done_ctr.numel() >= oxi::PAD_MAXB, "done_ctr");
-  oxi::launch_rs_bucket(grad.data_ptr<float>(), reinterpret_cast<const uint64_t*>(peers_recv.data_ptr<int64_t>()),
-                        my_recv.data_ptr(), reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()),
+  oxi::launch_rs_bucket((int)mode, grad.data_ptr<float>(),
+                        reinterpret_cast<const uint64_t*>(peers_buf.data_ptr<int64_t>()), my_buf.data_ptr(),
+                        reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()),
                         my_pad.data_ptr<int>(), done_ctr.data_ptr<int>(), (int)rank, (int)W, (int)bucket, (int)epoch,
                         lo, len, rgrad_shard.data_ptr<float>(), sumsq.data_ptr<float>(), (int)ctas,
                         status_ptr(status), wait_ns, stream());
@@ -349,6 +351,106 @@ void adamw_allgather(torch::Tensor buckets, int64_t rank, int64_t W, torch::Tens
                               (int)epoch, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1,
                               (float)bc2, coef.data_ptr<float>(), done_ctr.data_ptr<int>(), status_ptr(status),
                               wait_ns, stream());
+}
+
+// ------------------------------------------------------------ expert parallelism (NVLink)
+namespace {
+const uint64_t* u64p(const torch::Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == torch::kInt64 && t.is_cuda() && t.is_contiguous(), "pointer tables: int64 CUDA");
+  return reinterpret_cast<const uint64_t*>(t.data_ptr<int64_t>());
+}
+}  // namespace
+
+int64_t ep_pad_words() { return oxi::EP_PAD_WORDS; }
+
+std::vector<torch::Tensor> ep_counts(torch::Tensor local_counts, torch::Tensor peer_pads, torch::Tensor my_pad,
+                                     int64_t rank, int64_t W, int64_t seq, torch::Tensor status, int64_t wait_ns) {
+  c10::cuda::CUDAGuard g(my_pad.device());
+  TORCH_CHECK(local_counts.scalar_type() == torch::kInt32 && local_counts.is_contiguous(), "counts int32");
+  const int64_t E = local_counts.numel(), El = E / W;
+  auto io = torch::TensorOptions().dtype(torch::kInt32).device(my_pad.device());
+  auto all = torch::empty({W, E}, io), seg = torch::empty({El + 1}, io), rc = torch::empty({El}, io);
+  oxi::launch_ep_counts(local_counts.data_ptr<int>(), u64p(peer_pads), my_pad.data_ptr<int>(), (int)rank, (int)W,
+                        (int)E, (int)seq, all.data_ptr<int>(), seg.data_ptr<int>(), rc.data_ptr<int>(),
+                        status_ptr(status), wait_ns, stream());
+  return {all, seg, rc};
+}
+
+torch::Tensor ep_dispatch(torch::Tensor x, torch::Tensor topi, torch::Tensor topw, torch::Tensor all_counts,
+                          int64_t rank, int64_t W, torch::Tensor cursor, torch::Tensor peers_xrecv,
+                          torch::Tensor peers_metaw, torch::Tensor done_ctr, torch::Tensor peer_pads, int64_t seq,
+                          torch::Tensor status) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [T, H]");
+  TORCH_CHECK(topi.scalar_type() == torch::kInt64 && topi.is_contiguous() && topw.is_contiguous() &&
+                  topw.scalar_type() == torch::kFloat32, "topi int64 / topw f32 [T, k]");
+  const int64_t T = topi.size(0), k = topi.size(1), E = all_counts.size(1);
+  auto pos = torch::empty({T * k}, torch::TensorOptions().dtype(torch::kInt32).device(x.device()));
+  oxi::launch_ep_dispatch(x.data_ptr(), x.stride(0), topi.data_ptr<int64_t>(), topw.data_ptr<float>(), T, (int)k,
+                          (int)x.size(1), all_counts.data_ptr<int>(), (int)rank, (int)W, (int)E, cursor.data_ptr<int>(),
+                          u64p(peers_xrecv), u64p(peers_metaw), pos.data_ptr<int>(), done_ctr.data_ptr<int>(),
+                          u64p(peer_pads), (int)seq, status_ptr(status), stream());
+  return pos;
+}
+
+void ep_wait(torch::Tensor my_pad, int64_t kind, int64_t W, int64_t seq, torch::Tensor status, int64_t wait_ns) {
+  c10::cuda::CUDAGuard g(my_pad.device());
+  oxi::launch_ep_wait(my_pad.data_ptr<int>(), (int)kind, (int)W, (int)seq, status_ptr(status), wait_ns, stream());
+}
+
+void ep_signal(torch::Tensor peer_pads, int64_t kind, int64_t rank, int64_t W, int64_t seq) {
+  c10::cuda::CUDAGuard g(peer_pads.device());
+  oxi::launch_ep_signal(u64p(peer_pads), (int)kind, (int)rank, (int)W, (int)seq, stream());
+}
+
+torch::Tensor ep_combine(torch::Tensor topi, torch::Tensor topw, torch::Tensor pos, int64_t El, int64_t H,
+                         torch::Tensor peers_yout, c10::optional<torch::Tensor> resid, torch::Tensor my_pad, int64_t W,
+                         int64_t seq, torch::Tensor status, int64_t wait_ns) {
+  c10::cuda::CUDAGuard g(topi.device());
+  const int64_t T = topi.size(0), k = topi.size(1);
+  auto y = torch::empty({T, H}, torch::TensorOptions().dtype(torch::kBFloat16).device(topi.device()));
+  const void* rp = nullptr;
+  if (resid.has_value() && resid->defined()) {
+    TORCH_CHECK(resid->is_contiguous() && resid->numel() == T * H && resid->scalar_type() == torch::kBFloat16,
+                "resid bf16 [T, H] contiguous");
+    rp = resid->data_ptr();
+  }
+  oxi::launch_ep_combine(topi.data_ptr<int64_t>(), topw.data_ptr<float>(), pos.data_ptr<int>(), T, (int)k, (int)H,
+                         (int)El, u64p(peers_yout), rp, y.data_ptr(), my_pad.data_ptr<int>(), (int)W, (int)seq,
+                         status_ptr(status), wait_ns, stream());
+  return y;
+}
+
+void ep_push_dy(torch::Tensor dy, torch::Tensor topi, torch::Tensor pos, int64_t El, torch::Tensor peers_dyrecv,
+                torch::Tensor done_ctr, torch::Tensor peer_pads, int64_t rank, int64_t W, int64_t seq,
+                torch::Tensor status) {
+  c10::cuda::CUDAGuard g(dy.device());
+  TORCH_CHECK(dy.scalar_type() == torch::kBFloat16 && dy.is_contiguous(), "dy bf16 contiguous");
+  const int64_t T = topi.size(0), k = topi.size(1);
+  oxi::launch_ep_push_dy(dy.data_ptr(), topi.data_ptr<int64_t>(), pos.data_ptr<int>(), T, (int)k, (int)dy.size(-1),
+                         (int)El, u64p(peers_dyrecv), done_ctr.data_ptr<int>(), u64p(peer_pads), (int)rank, (int)W,
+                         (int)seq, status_ptr(status), stream());
+}
+
+void ep_scale_rows(torch::Tensor dyrecv, torch::Tensor yout, torch::Tensor metaw, torch::Tensor dwrow,
+                   torch::Tensor seg_off, torch::Tensor recv_counts, int64_t El) {
+  c10::cuda::CUDAGuard g(dyrecv.device());
+  oxi::launch_ep_scale_rows(dyrecv.data_ptr(), yout.data_ptr(), metaw.data_ptr<float>(), dwrow.data_ptr<float>(),
+                            seg_off.data_ptr<int>(), recv_counts.data_ptr<int>(), (int)El, (int)dyrecv.size(1),
+                            dyrecv.size(0), stream());
+}
+
+std::vector<torch::Tensor> ep_gather(torch::Tensor topi, torch::Tensor pos, int64_t H, int64_t El,
+                                     torch::Tensor peers_dx, torch::Tensor peers_dwrow, torch::Tensor my_pad,
+                                     int64_t W, int64_t seq, torch::Tensor status, int64_t wait_ns) {
+  c10::cuda::CUDAGuard g(topi.device());
+  const int64_t T = topi.size(0), k = topi.size(1);
+  auto dx = torch::empty({T, H}, torch::TensorOptions().dtype(torch::kBFloat16).device(topi.device()));
+  auto dw = torch::empty({T, k}, torch::TensorOptions().dtype(torch::kFloat32).device(topi.device()));
+  oxi::launch_ep_gather(topi.data_ptr<int64_t>(), pos.data_ptr<int>(), T, (int)k, (int)H, (int)El, u64p(peers_dx),
+                        u64p(peers_dwrow), dx.data_ptr(), dw.data_ptr<float>(), my_pad.data_ptr<int>(), (int)W,
+                        (int)seq, status_ptr(status), wait_ns, stream());
+  return {dx, dw};
 }
 
 // ------------------------------------------------------------ SSM
@@ -625,6 +727,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &moe_combine_bwd, "backward of the combine");
   m.def("moe_gather_sum", &moe_gather_sum, "sum permuted rows back per token");
   m.def("gemm_grouped", &gemm_grouped, "grouped (per-expert) tcgen05 GEMM");
+  m.def("ep_pad_words", &ep_pad_words, "int32 words of one expert-parallel signal pad");
+  m.def("ep_counts", &ep_counts, "expert-parallel count all-gather over NVLink");
+  m.def("ep_dispatch", &ep_dispatch, "expert-parallel token dispatch (P2P stores)");
+  m.def("ep_wait", &ep_wait, "bounded wait for an expert-parallel flag from every peer");
+  m.def("ep_signal", &ep_signal, "post an expert-parallel flag to every peer");
+  m.def("ep_combine", &ep_combine, "expert-parallel weighted combine (P2P loads) + residual");
+  m.def("ep_push_dy", &ep_push_dy, "expert-parallel backward: push output gradients to the owners");
+  m.def("ep_scale_rows", &ep_scale_rows, "owner side: routing-weight gradient and scaling of received rows");
+  m.def("ep_gather", &ep_gather, "expert-parallel backward: gather input gradients and weight gradients");
   m.def("ipc_alloc", &ipc_alloc, "zeroed device buffer exportable over CUDA IPC");
   m.def("ipc_open", &ipc_open, "map a peer's IPC buffer");
   m.def("ipc_close", &ipc_close, "unmap a peer's IPC buffer");

@@ -182,14 +182,13 @@ def run_train(args, argv: List[str]) -> int:
     ocfg = AdamWConfig(lr=t.learning_rate,
                        weight_decay=t.weight_decay if t.weight_decay is not None else 0.01,
                        max_grad_norm=t.max_grad_norm if t.max_grad_norm is not None else 1.0)
-    if world > 1 and backend == "fused" and device.type == "cuda":
-        from .parallel.fused_ar import FusedDDPAdamW
-        opt = FusedDDPAdamW(list(model.named_parameters()), ocfg, device, group=group)
-        flat = None
-    elif world > 1:
-        from .parallel.ddp import DDPAdamW
-        flat = FlatParams(list(model.named_parameters()), device)
-        opt = DDPAdamW(flat, ocfg, backend=backend if backend != "single" else "nccl", group=group)
+    if world > 1:
+        from .parallel.ddp import make_ddp_optimizer
+        be = backend if backend != "single" else "nccl"
+        if be == "fused" and device.type != "cuda":
+            be = "cpustaging"
+        opt = make_ddp_optimizer(model.named_parameters(), ocfg, device, be, group=group)
+        flat = getattr(opt, "flat", None) if be != "fused" else None
     else:
         flat = FlatParams(list(model.named_parameters()), device)
         opt = AdamW(flat, ocfg)

@@ -61,14 +61,14 @@ def aux_from_usage(usage: torch.Tensor, counts: torch.Tensor, n_sel: int, E: int
 
 
 def route_with_aux(logits: torch.Tensor, k: int, E: int, kind: str):
-    """(top_idx, top_w, aux): the fused router kernel on CUDA, torch ops elsewhere."""
+    """(top_idx, top_w, aux, counts): the fused router kernel on CUDA, torch ops elsewhere."""
     if logits.is_cuda:
         from ..ops.moe_kernels import RouterTopK, router_ok
         if router_ok(logits, k):
             topi, topw, usage, counts = RouterTopK.apply(logits, k)
-            return topi, topw, aux_from_usage(usage, counts, topi.numel(), E, kind)
+            return topi, topw, aux_from_usage(usage, counts, topi.numel(), E, kind), counts
     probs, topi, topw = route(logits, k)
-    return topi, topw, aux_loss(probs, topi, E, kind)
+    return topi, topw, aux_loss(probs, topi, E, kind), None
 
 
 class MoE(RefModule):
@@ -94,14 +94,27 @@ class MoE(RefModule):
         self.w_down = nn.Parameter(torch.empty(self.E_local, H, self.I, device=device, dtype=dtype))
         self.n_shared = cfg.n_shared_experts
         self.shared = SwiGLU(H, self.n_shared * self.I, device, dtype) if self.n_shared > 0 else None
-        # expert parameters are not data-parallel-replicated under EP
-        self.w_gu._oxi_expert = True
-        self.w_down._oxi_expert = True
+        # under expert parallelism the expert weights are shards, not replicas:
+        # the data-parallel optimizers keep them out of the gradient all-reduce
+        if self.ep_size > 1:
+            self.w_gu._oxi_ep_local = True
+            self.w_down._oxi_ep_local = True
 
     def reset_parameters(self, std, gen=None):
         normal_(self.router, std, gen)
-        normal_(self.w_gu, std, gen)
-        normal_(self.w_down, std, gen)
+        if self.ep_size > 1:
+            # draw every expert (same stream of numbers as one process holding all
+            # of them) and keep this rank's slice
+            lo = self.ep_rank * self.E_local
+            for p in (self.w_gu, self.w_down):
+                full = torch.empty((self.E,) + tuple(p.shape[1:]), device=p.device, dtype=p.dtype)
+                normal_(full, std, gen)
+                with torch.no_grad():
+                    p.copy_(full[lo:lo + self.E_local])
+                del full
+        else:
+            normal_(self.w_gu, std, gen)
+            normal_(self.w_down, std, gen)
         if self.shared is not None:
             self.shared.reset_parameters(std, gen)
 
@@ -120,10 +133,13 @@ class MoE(RefModule):
         B, S, H = h.shape
         x = h.reshape(-1, H)
         logits = api.linear(x, self.router)
-        topi, topw, aux = route_with_aux(logits, self.k, self.E, self.aux_kind)
+        topi, topw, aux, counts = route_with_aux(logits, self.k, self.E, self.aux_kind)
         if self.ep_size > 1:
-            from ..parallel.ep import ep_moe
-            y = ep_moe(self, x, topi, topw)
+            from ..parallel import ep
+            if counts is not None and ep.nvlink_ok(self, x):
+                y = ep.ep_moe_nvlink(self, x, topi, topw, counts, resid.reshape(-1, H)).view(B, S, H)
+                return (self.shared(h, y) if self.shared is not None else y), aux
+            y = ep.ep_moe(self, x, topi, topw)
         elif _grouped_ok(x, self.w_gu):
             from ..ops.moe_kernels import GroupedExperts
             r = resid.reshape(-1, H)

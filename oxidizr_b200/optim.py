@@ -85,8 +85,66 @@ class FlatParams:
             p.grad = None
 
 
+def split_local(named_params):
+    """(replicated, local): local = expert-parallel shards (``param._oxi_ep_local``)."""
+    rep = [(n, p) for n, p in named_params if not getattr(p, "_oxi_ep_local", False)]
+    loc = [(n, p) for n, p in named_params if getattr(p, "_oxi_ep_local", False)]
+    return rep, loc
+
+
+class LocalAdamW:
+    """AdamW over parameters that each data-parallel rank holds alone (expert
+    shards).  Their gradients are sums over every rank's tokens, so the same
+    device coefficient (clip x 1/world) as the all-reduced gradients applies."""
+
+    def __init__(self, named_params, cfg: "AdamWConfig", device):
+        self.flat = FlatParams(named_params, device)
+        self.cfg = cfg
+        self.m = torch.zeros_like(self.flat.master)
+        self.v = torch.zeros_like(self.flat.master)
+
+    def sq_into(self, buf: torch.Tensor) -> None:
+        """buf += sum(g^2) over the local gradients (device)."""
+        self.flat.fold_autograd_grads()
+        if self.flat.device.type == "cuda":
+            from .ops._C import ext
+            ext().sqsum(self.flat.grad, buf)
+        else:
+            buf.add_(self.flat.grad.pow(2).sum())
+
+    def update(self, coef: torch.Tensor, step: int) -> None:
+        c, f = self.cfg, self.flat
+        bc1, bc2 = 1.0 - c.beta1 ** step, 1.0 - c.beta2 ** step
+        if f.device.type == "cuda":
+            from .ops._C import ext
+            ext().adamw(f.master, f.flat if f.flat is not f.master else None, f.grad, self.m, self.v, c.lr, c.beta1,
+                        c.beta2, c.eps, c.weight_decay, bc1, bc2, coef)
+        else:
+            g = f.grad * coef
+            self.m.mul_(c.beta1).add_(g, alpha=1 - c.beta1)
+            self.v.mul_(c.beta2).addcmul_(g, g, value=1 - c.beta2)
+            p = f.master
+            p.sub_(c.lr * (self.m / bc1) / ((self.v / bc2).sqrt() + c.eps) + c.lr * c.weight_decay * p)
+            if f.flat is not f.master:
+                f.flat.copy_(p)
+        f.zero_grad()
+
+    def state_tensors(self) -> Dict[str, torch.Tensor]:
+        return {"master": self.flat.master, "exp_avg": self.m, "exp_avg_sq": self.v}
+
+
 class AdamW:
-    """Single-process optimizer over a :class:`FlatParams`."""
+    """Single-process optimizer over a :class:`FlatParams`.
+
+    ``local`` (optional :class:`LocalAdamW`) holds parameters that are not
+    replicated; ``_local_sq`` lets a data-parallel subclass reduce their
+    squared norm across ranks before the clip coefficient is formed.
+    """
+
+    local: Optional["LocalAdamW"] = None
+
+    def _local_sq(self, buf: torch.Tensor) -> None:
+        self.local.sq_into(buf)
 
     def __init__(self, flat: FlatParams, cfg: AdamWConfig):
         self.flat, self.cfg = flat, cfg
@@ -118,17 +176,28 @@ class AdamW:
             e = ext()
             self._sq.zero_()
             e.sqsum(f.grad, self._sq)
+            if self.local is not None:
+                self._local_sq(self._sq)
             e.clip_coef(self._sq, float(c.max_grad_norm or 0.0), float(grad_scale), self._coef, self._norm)
             e.adamw(f.master, f.flat if f.flat is not f.master else None, f.grad, self.m, self.v, c.lr, c.beta1,
                     c.beta2, c.eps, c.weight_decay, bc1, bc2, self._coef)
+            if self.local is not None:
+                self.local.update(self._coef, t)
         else:
             g = f.grad * grad_scale
-            nrm = g.norm()
+            sq = g.pow(2).sum()
+            if self.local is not None:
+                lsq = torch.zeros(1, dtype=torch.float32)
+                self._local_sq(lsq)
+                sq = sq + lsq[0] * grad_scale * grad_scale
+            nrm = sq.sqrt()
             self._norm.copy_(nrm.reshape(1))
             coef = 1.0
             if c.max_grad_norm and nrm.item() > c.max_grad_norm:
                 coef = c.max_grad_norm / (nrm.item() + 1e-6)
             g = g * coef
+            if self.local is not None:
+                self.local.update(torch.tensor(coef * grad_scale, dtype=torch.float32), t)
             self.m.mul_(c.beta1).add_(g, alpha=1 - c.beta1)
             self.v.mul_(c.beta2).addcmul_(g, g, value=1 - c.beta2)
             upd = (self.m / bc1) / ((self.v / bc2).sqrt() + c.eps)

@@ -23,7 +23,7 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
-from ..optim import AdamW, AdamWConfig, FlatParams
+from ..optim import AdamW, AdamWConfig, FlatParams, LocalAdamW, split_local
 
 
 class Bucket:
@@ -38,8 +38,9 @@ class DDPAdamW(AdamW):
     """AdamW over a FlatParams whose gradient is all-reduced across the group."""
 
     def __init__(self, flat: FlatParams, cfg: AdamWConfig, backend: str = "nccl", group=None,
-                 bucket_bytes: int = 64 << 20, overlap: bool = True):
+                 bucket_bytes: int = 64 << 20, overlap: bool = True, local: Optional[LocalAdamW] = None):
         super().__init__(flat, cfg)
+        self.local = local
         self.group = group
         self.world = dist.get_world_size(group)
         self.backend = backend
@@ -75,6 +76,13 @@ class DDPAdamW(AdamW):
             for i in g:
                 f.params[i]._oxi_grad_ready = (lambda bb=b: self._on_ready(bb))
 
+    def _local_sq(self, buf: torch.Tensor) -> None:
+        """Squared norm of the expert shards, summed over the group (each rank holds different ones)."""
+        tmp = torch.zeros_like(buf)
+        self.local.sq_into(tmp)
+        dist.all_reduce(tmp, group=self.group)
+        buf.add_(tmp)
+
     def _on_ready(self, b: Bucket):
         if self.accumulating:
             return
@@ -108,3 +116,16 @@ class DDPAdamW(AdamW):
         else:
             dist.all_reduce(f.grad, group=self.group)
         return super().step(grad_scale / self.world)
+
+
+def make_ddp_optimizer(named_params, cfg: AdamWConfig, device, backend: str, group=None, **kw):
+    """Data-parallel AdamW over a model's parameters for ``backend`` in
+    ``cpustaging | nccl | fused``.  Expert-parallel shards (``_oxi_ep_local``)
+    are updated locally; everything else is averaged over the group."""
+    named_params = list(named_params)
+    if backend == "fused":
+        from .fused_ar import FusedDDPAdamW
+        return FusedDDPAdamW(named_params, cfg, device, group=group, **kw)
+    rep, loc = split_local(named_params)
+    local = LocalAdamW(loc, cfg, device) if loc else None
+    return DDPAdamW(FlatParams(rep, device), cfg, backend=backend, group=group, local=local, **kw)

@@ -1,25 +1,37 @@
 """Expert parallelism for the MoE layer.
 
 Upstream has no expert parallelism (every expert runs on every token in one
-process, model.rs:561-565).  Here each of ``ep`` ranks holds E/ep experts:
+process, model.rs:561-565).  Here each of ``W`` ranks of an expert-parallel
+group holds E/W experts, and every token row travels to the rank that owns
+each of its top-k experts.  Two implementations of the same exchange:
 
-1. every (token, slot) pair is sorted by global expert id, which orders it by
-   destination rank and then by local expert;
-2. per-destination counts are exchanged, then the token rows (and local expert
-   ids) are exchanged with an all-to-all;
-3. each rank runs its local experts on the rows it received with the grouped
-   tcgen05 GEMM (:class:`~oxidizr_b200.ops.moe_kernels.GroupedExperts`, one
-   expert per row);
-4. the expert outputs travel back with the reverse all-to-all and are
-   combined with the routing weights (fused with the residual add).
+* ``nvlink`` (default on CUDA, :class:`EPExperts`): the sm_100a kernels of
+  ``csrc/ep.cu``.  The per-expert counts are all-gathered through NVLink signal
+  pads; the dispatch kernel writes token rows straight into the owners'
+  receive buffers (P2P stores, CUDA-IPC symmetric memory); the owners run the
+  grouped tcgen05 expert GEMMs on their receive buffer; the combine kernel
+  reads the k expert rows of each token back over NVLink and adds them,
+  weighted, to the residual.  Backward pushes output gradients to the owners,
+  which compute the routing-weight gradients and the expert backward GEMMs;
+  the sources gather the input gradients.  Every wait is bounded.
+* ``nccl`` (baseline, and the CPU/gloo path, :func:`ep_moe`): NCCL/gloo
+  all-to-all of the permuted rows (``torch.distributed.nn`` keeps it
+  differentiable), split sizes read on the host.
 
-The all-to-all here is NCCL's (``torch.distributed.nn`` keeps it
-differentiable); its split sizes are read on the host once per layer.
+Expert weight gradients are sums over the tokens of every rank; the
+data-parallel optimizers scale them by 1/W like the averaged dense gradients
+and keep them out of the all-reduce (``param._oxi_ep_local``).
 """
 from __future__ import annotations
 
+import os
+from typing import Optional
+
 import torch
 import torch.distributed as dist
+
+# flag kinds of csrc/kernels_ep.h
+K_DISPATCHED, K_YREADY, K_DYPUSHED, K_DXREADY = 1, 2, 3, 4
 
 
 def _a2a(x: torch.Tensor, out_splits, in_splits, group):
@@ -29,10 +41,9 @@ def _a2a(x: torch.Tensor, out_splits, in_splits, group):
 
 
 def ep_moe(moe, x: torch.Tensor, topi: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
-    """Routed-expert output (without residual / shared experts) for tokens x [T, H]."""
+    """Routed-expert output (without residual / shared experts) for tokens x [T, H], over all-to-all."""
     group = moe.ep_group
     W, El = moe.ep_size, moe.E_local
-    T, H = x.shape
     k = topi.shape[1]
     flat = topi.reshape(-1)
     order = torch.argsort(flat, stable=True)
@@ -49,23 +60,183 @@ def ep_moe(moe, x: torch.Tensor, topi: torch.Tensor, topw: torch.Tensor) -> torc
     dist.all_to_all_single(ids_recv, local_ids, r_split, s_split, group=group)
     x_recv = _a2a(x_send, r_split, s_split, group)
     R = x_recv.shape[0]
-    if R > 0:
-        from ..models.moe import _grouped_ok
-        if _grouped_ok(x_recv, moe.w_gu):
-            from ..ops.moe_kernels import GroupedExperts
-            ones = torch.ones(R, 1, dtype=torch.float32, device=x.device)
-            y_recv = GroupedExperts.apply(x_recv, ids_recv[:, None], ones, moe.w_gu, moe.w_down, None)
-        else:
-            from ..ops import api
-            y_recv = torch.zeros_like(x_recv)
-            for e in range(El):
-                sel = (ids_recv == e).nonzero().squeeze(1)
-                if sel.numel():
-                    y_recv = y_recv.index_copy(0, sel, api.swiglu_mlp(x_recv.index_select(0, sel), moe.w_gu[e],
-                                                                      moe.w_down[e]))
+    from ..models.moe import _grouped_ok
+    if R > 0 and _grouped_ok(x_recv, moe.w_gu):
+        from ..ops.moe_kernels import GroupedExperts
+        ones = torch.ones(R, 1, dtype=torch.float32, device=x.device)
+        y_recv = GroupedExperts.apply(x_recv, ids_recv[:, None], ones, moe.w_gu, moe.w_down, None)
     else:
-        # keep the expert weights in the graph so every rank reaches the same collectives
-        y_recv = x_recv + 0.0 * (moe.w_gu.sum() + moe.w_down.sum()).to(x_recv.dtype)
+        from ..ops import api
+        # every expert joins the graph (with zero rows if unused) so all ranks see the same backward
+        y_recv = torch.zeros_like(x_recv)
+        for e in range(El):
+            sel = (ids_recv == e).nonzero().squeeze(1)
+            y_recv = y_recv.index_copy(0, sel, api.swiglu_mlp(x_recv.index_select(0, sel), moe.w_gu[e],
+                                                              moe.w_down[e]))
     y_send = _a2a(y_recv, s_split, r_split, group)
     w_sorted = topw.reshape(-1).index_select(0, order).to(y_send.dtype)
     return torch.zeros_like(x).index_add(0, tok, y_send * w_sorted[:, None])
+
+
+# ---------------------------------------------------------------------- NVLink
+class EPGroup:
+    """Signal pad and exchange counter shared by the MoE layers of one group."""
+
+    _groups = {}
+
+    @classmethod
+    def get(cls, group, device) -> "EPGroup":
+        key = (id(group), torch.device(device).index)
+        if key not in cls._groups:
+            cls._groups[key] = EPGroup(group, device)
+        return cls._groups[key]
+
+    def __init__(self, group, device, timeout_s: Optional[float] = None):
+        from ..ops._C import ext
+        from .fused_ar import SymmetricBuffer
+        self.group = group
+        self.device = torch.device(device)
+        self.W = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.pad = SymmetricBuffer(ext().ep_pad_words() * 4, self.device, group)
+        self.pad_local = self.pad.local.view(torch.int32)
+        self.done = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.cursor = torch.zeros(256, dtype=torch.int32, device=self.device)
+        t = timeout_s if timeout_s is not None else float(os.environ.get("OXI_PEER_TIMEOUT_S", 30.0))
+        self.wait_ns = int(t * 1e9)
+        self.seq = 0
+
+    def next_seq(self) -> int:
+        self.seq += 1
+        return self.seq
+
+
+class EPLayerBuffers:
+    """The symmetric receive/output buffers of one MoE layer (grown collectively)."""
+
+    def __init__(self, grp: EPGroup, H: int):
+        self.grp, self.H = grp, H
+        self.cap = 0
+        self.bufs = None
+
+    def ensure(self, rows: int):
+        if rows <= self.cap:
+            return
+        from .fused_ar import SymmetricBuffer
+        g = self.grp
+        cap = max(128, (int(rows * 1.15) + 127) // 128 * 128)
+        torch.cuda.synchronize(g.device)
+        if self.bufs is not None:
+            for b in self.bufs.values():
+                b.close()
+            dist.barrier(group=g.group)
+        H = self.H
+        self.bufs = {
+            "xrecv": SymmetricBuffer(cap * H * 2, g.device, g.group),
+            "yout": SymmetricBuffer(cap * H * 2, g.device, g.group),
+            "dyrecv": SymmetricBuffer(cap * H * 2, g.device, g.group),
+            "metaw": SymmetricBuffer(cap * 4, g.device, g.group),
+            "dwrow": SymmetricBuffer(cap * 4, g.device, g.group),
+        }
+        self.cap = cap
+
+    def local(self, name: str, dtype, cols: int = 0) -> torch.Tensor:
+        t = self.bufs[name].local.view(dtype)
+        return t.view(self.cap, cols) if cols else t
+
+    def table(self, name: str) -> torch.Tensor:
+        return self.bufs[name].ptr_table
+
+
+def _rows_needed(all_counts: torch.Tensor, W: int, El: int) -> int:
+    """Largest 128-aligned receive-buffer size any rank needs (same on every rank)."""
+    per_expert = all_counts.sum(0).view(W, El)  # [dest, local expert]
+    return int((((per_expert + 127) // 128) * 128).sum(1).max().item())
+
+
+class EPExperts(torch.autograd.Function):
+    """resid + sum_j topw[t, j] * SwiGLU_{topi[t, j]}(x_t), experts spread over the group (NVLink)."""
+
+    @staticmethod
+    def forward(ctx, x, topi, topw, counts, w_gu, w_down, resid, moe):
+        from ..ops._C import ext, status
+        e = ext()
+        g: EPGroup = moe._ep
+        buf: EPLayerBuffers = moe._ep_buf
+        T, H = x.shape
+        El, I2, _ = w_gu.shape
+        I = I2 // 2
+        W, rank = g.W, g.rank
+        st = status(x.device)
+        xc = x if x.stride(1) == 1 else x.contiguous()
+        topi = topi.contiguous()
+        tw = topw.float().contiguous()
+        seq = g.next_seq()
+        all_counts, seg, rc = e.ep_counts(counts.int().contiguous(), g.pad.ptr_table, g.pad_local, rank, W, seq, st,
+                                          g.wait_ns)
+        buf.ensure(_rows_needed(all_counts.cpu(), W, El))
+        cap = buf.cap
+        xr = buf.local("xrecv", torch.bfloat16, H)
+        yo = buf.local("yout", torch.bfloat16, H)
+        e.moe_zero_pad(seg, rc, xr)
+        pos = e.ep_dispatch(xc, topi, tw, all_counts, rank, W, g.cursor, buf.table("xrecv"), buf.table("metaw"),
+                            g.done[0:1], g.pad.ptr_table, seq, st)
+        e.ep_wait(g.pad_local, K_DISPATCHED, W, seq, st, g.wait_ns)
+        h = torch.empty(cap, I, dtype=x.dtype, device=x.device)
+        gu = torch.empty(cap, I2, dtype=x.dtype, device=x.device)
+        e.gemm_grouped(1, 2, xr, False, w_gu.view(El * I2, H), False, El, seg, I2, h, gu, None, st)
+        e.gemm_grouped(1, 0, h, False, w_down.view(El * H, I), False, El, seg, H, yo, None, None, st)
+        e.ep_signal(g.pad.ptr_table, K_YREADY, rank, W, seq)
+        y = e.ep_combine(topi, tw, pos, El, H, buf.table("yout"), resid.contiguous() if resid is not None else None,
+                         g.pad_local, W, seq, st, g.wait_ns)
+        ctx.save_for_backward(topi, tw, pos, h, gu, seg, rc)
+        ctx.moe, ctx.w_gu, ctx.w_down, ctx.has_resid = moe, w_gu, w_down, resid is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..ops._C import ext, status
+        from ..ops.moe_kernels import _wgrad_grouped
+        e = ext()
+        topi, tw, pos, h, gu, seg, rc = ctx.saved_tensors
+        moe = ctx.moe
+        g: EPGroup = moe._ep
+        buf: EPLayerBuffers = moe._ep_buf
+        w_gu, w_down = ctx.w_gu, ctx.w_down
+        El, I2, H = w_gu.shape
+        I = I2 // 2
+        W, rank = g.W, g.rank
+        st = status(dy.device)
+        dy = dy.contiguous()
+        seq = g.next_seq()
+        xr = buf.local("xrecv", torch.bfloat16, H)
+        yo = buf.local("yout", torch.bfloat16, H)
+        dyr = buf.local("dyrecv", torch.bfloat16, H)
+        e.ep_push_dy(dy, topi, pos, El, buf.table("dyrecv"), g.done[1:2], g.pad.ptr_table, rank, W, seq, st)
+        e.ep_wait(g.pad_local, K_DYPUSHED, W, seq, st, g.wait_ns)
+        e.ep_scale_rows(dyr, yo, buf.local("metaw", torch.float32), buf.local("dwrow", torch.float32), seg, rc, El)
+        g_down = _wgrad_grouped(w_down, dyr, h, seg, El)
+        dgu = torch.empty_like(gu)
+        e.gemm_grouped(1, 3, dyr, False, w_down.view(El * H, I), True, El, seg, H, dgu, None, gu, st)
+        g_gu = _wgrad_grouped(w_gu, dgu, xr, seg, El)
+        # the gradient of the received rows overwrites yout (consumed above)
+        e.gemm_grouped(1, 0, dgu, False, w_gu.view(El * I2, H), True, El, seg, I2, yo, None, None, st)
+        e.ep_signal(g.pad.ptr_table, K_DXREADY, rank, W, seq)
+        dx, dtw = e.ep_gather(topi, pos, H, El, buf.table("yout"), buf.table("dwrow"), g.pad_local, W, seq, st,
+                              g.wait_ns)
+        return dx, None, dtw, None, g_gu, g_down, (dy if ctx.has_resid else None), None
+
+
+def nvlink_ok(moe, x) -> bool:
+    if not x.is_cuda or os.environ.get("OXI_EP_BACKEND", "nvlink") != "nvlink":
+        return False
+    from ..ops._C import ext
+    from ..ops.moe_kernels import grouped_ok
+    return hasattr(ext(), "ep_dispatch") and grouped_ok(x, moe.w_gu) and moe.k <= 16 and moe.E <= 256
+
+
+def ep_moe_nvlink(moe, x, topi, topw, counts, resid):
+    if getattr(moe, "_ep", None) is None:
+        moe._ep = EPGroup.get(moe.ep_group, x.device)
+        moe._ep_buf = EPLayerBuffers(moe._ep, x.shape[1])
+    return EPExperts.apply(x, topi, topw, counts, moe.w_gu, moe.w_down, resid, moe)

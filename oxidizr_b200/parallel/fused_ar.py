@@ -9,8 +9,10 @@ issued from our own kernels:
 * buckets of parameters (reverse order of use) are reduced as soon as
   backward has produced all their gradients, on a side stream, so the
   transfers overlap the rest of backward: each rank casts its gradient to
-  bf16 and pushes every owner's part into the owner's receive slots (NVLink
-  stores), then sums its own shard's slots locally;
+  bf16 in its send buffer, and the owner of each shard streams the W slices
+  over NVLink into shared memory with TMA bulk copies and sums them in f32
+  (``OXI_RS_MODE=push``: NVLink stores into the owners' receive slots, then a
+  local sum);
 * each rank keeps f32 master weights and AdamW moments for its 1/W shard of
   every bucket only (optimizer state sharded W ways);
 * after backward: one tiny kernel exchanges partial norms (global-norm clip),
@@ -22,13 +24,14 @@ start-up and for checkpoint gathers.
 """
 from __future__ import annotations
 
-from typing import List, Sequence, Tuple
+import os
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
 
 from ..ops._C import ext, status
-from ..optim import AdamWConfig
+from ..optim import AdamWConfig, LocalAdamW, split_local
 
 ALIGN = 64
 
@@ -69,16 +72,20 @@ class FusedDDPAdamW:
     """Drop-in optimizer for data-parallel training over NVLink (sync backend ``fused``)."""
 
     def __init__(self, named_params: Sequence[Tuple[str, torch.nn.Parameter]], cfg: AdamWConfig, device,
-                 group=None, bucket_bytes: int = 32 << 20, rs_ctas: int = 16,
+                 group=None, bucket_bytes: int = 32 << 20, rs_ctas: Optional[int] = None,
                  peer_timeout_s: float = 30.0):
         self.cfg = cfg
         self.device = torch.device(device)
         self.group = group
         self.rank = dist.get_rank(group)
         self.W = dist.get_world_size(group)
-        self.rs_ctas = rs_ctas
+        # CTAs per reduce-scatter kernel (they share SMs with the backward GEMMs)
+        self.rs_ctas = int(rs_ctas if rs_ctas is not None else os.environ.get("OXI_RS_CTAS", 32))
         # a peer that has not posted its flag within this time is reported as failed
         self.wait_ns = int(peer_timeout_s * 1e9)
+        named_params, local = split_local(list(named_params))
+        # expert-parallel shards: updated locally with the same clip coefficient
+        self.local = LocalAdamW(local, cfg, device) if local else None
         self.names = [n for n, _ in named_params]
         self.params = [p for _, p in named_params]
         assert all(p.dtype == torch.bfloat16 for p in self.params), "fused DDP needs bf16 parameters"
@@ -113,7 +120,10 @@ class FusedDDPAdamW:
         self.shard_numel = shard_off
         # ---- buffers
         dev = self.device
-        self.recv = SymmetricBuffer(self.N * 2, dev, group)
+        # bf16 gradient exchange buffer: this rank's send buffer (pull mode) or
+        # the receive slots of its shards (push mode)
+        self.xfer = SymmetricBuffer(self.N * 2, dev, group)
+        self.rs_mode = 1 if os.environ.get("OXI_RS_MODE", "pull") == "push" else 0
         self.param = SymmetricBuffer(self.N * 2, dev, group)
         self.pad = SymmetricBuffer(ext().pad_words() * 4, dev, group)
         self.flat = self.param.local.view(torch.bfloat16)
@@ -177,9 +187,9 @@ class FusedDDPAdamW:
             if not self._sumsq_zeroed:
                 self._sumsq.zero_()
                 self._sumsq_zeroed = True
-            e.rs_bucket(self.grad, self.recv.ptr_table, self.recv.local, self.pad.ptr_table, self.pad_local,
-                        self._push_done, self.rank, self.W, bi, self.epoch, lo, ln, self.rgrad[so:so + ln // self.W],
-                        self._sumsq, self.rs_ctas, status(self.device), self.wait_ns)
+            e.rs_bucket(self.rs_mode, self.grad, self.xfer.ptr_table, self.xfer.local, self.pad.ptr_table,
+                        self.pad_local, self._push_done, self.rank, self.W, bi, self.epoch, lo, ln,
+                        self.rgrad[so:so + ln // self.W], self._sumsq, self.rs_ctas, status(self.device), self.wait_ns)
 
     # ------------------------------------------------------------ step
     def step(self, grad_scale: float = 1.0) -> torch.Tensor:
@@ -195,6 +205,8 @@ class FusedDDPAdamW:
         e = ext()
         self.step_count += 1
         t = self.step_count
+        if self.local is not None:
+            self.local.sq_into(self._sumsq)  # joins this rank's partial of the global norm
         e.norm_exchange(self.pad.ptr_table, self.pad_local, self.rank, self.W, self.epoch, self._sumsq,
                         float(c.max_grad_norm or 0.0), self._coef, self._norm, status(self.device),
                         self.wait_ns)
@@ -204,6 +216,8 @@ class FusedDDPAdamW:
                           self.param.ptr_table, self.pad.ptr_table, self.pad_local, self.epoch, c.lr, c.beta1,
                           c.beta2, c.eps, c.weight_decay, 1.0 - c.beta1 ** t, 1.0 - c.beta2 ** t, self._coef,
                           self._done, status(self.device), self.wait_ns)
+        if self.local is not None:
+            self.local.update(self._coef, t)
         self.grad.zero_()
         self.epoch += 1
         self._pending = [len(b[3]) for b in self.buckets]
@@ -241,5 +255,5 @@ class FusedDDPAdamW:
 
     def close(self):
         torch.cuda.synchronize(self.device)
-        for b in (self.recv, self.param, self.pad):
+        for b in (self.xfer, self.param, self.pad):
             b.close()

@@ -54,13 +54,8 @@ def main(argv=None):
     cfg = small_config(dev.type)
     model = build_model(cfg.model, device=dev, seed=0)
     ocfg = AdamWConfig(lr=1e-3)
-    if args.backend == "fused":
-        from .fused_ar import FusedDDPAdamW
-        opt = FusedDDPAdamW(list(model.named_parameters()), ocfg, dev, bucket_bytes=1 << 18)
-    else:
-        from .ddp import DDPAdamW
-        opt = DDPAdamW(FlatParams(list(model.named_parameters()), dev), ocfg, backend=args.backend,
-                       bucket_bytes=1 << 18)
+    from .ddp import make_ddp_optimizer
+    opt = make_ddp_optimizer(model.named_parameters(), ocfg, dev, args.backend, bucket_bytes=1 << 18)
     g = torch.Generator(device="cpu").manual_seed(100 + rank)
     losses, norms = [], []
     for step in range(args.steps):
