@@ -126,8 +126,8 @@ def save_blazr_config_if_needed(checkpoint_dir: str, model_cfg: ModelConfig) -> 
     return True
 
 
-def save_weights(model, path: str) -> None:
-    save_file(_cpu_contig(model.export_ref()), path)
+def save_weights(model, path: str, state_dict: Optional[Dict[str, torch.Tensor]] = None) -> None:
+    save_file(_cpu_contig(state_dict if state_dict is not None else model.export_ref()), path)
 
 
 def load_weights(model, path: str) -> None:
@@ -141,14 +141,19 @@ def optim_sidecar_path(weights_path: str) -> str:
 
 
 def save_checkpoint(model, optimizer, step: int, model_cfg: ModelConfig, checkpoint_dir: str,
-                    data_file_path: Optional[str], max_checkpoints: int, extra: Optional[dict] = None) -> str:
-    """trainer.rs:465-493 (+ sidecar).  Returns the weights path."""
+                    data_file_path: Optional[str], max_checkpoints: int, extra: Optional[dict] = None,
+                    state_dict: Optional[Dict[str, torch.Tensor]] = None,
+                    optim_state: Optional[Dict[str, torch.Tensor]] = None) -> str:
+    """trainer.rs:465-493 (+ sidecar).  Returns the weights path.
+
+    ``state_dict`` / ``optim_state``: already gathered tensors (data-parallel
+    runs gather them collectively on every rank, then rank 0 writes)."""
     os.makedirs(checkpoint_dir, exist_ok=True)
     prefix = model_cfg.checkpoint_prefix()
     path = os.path.join(checkpoint_dir, f"{prefix}_step_{step}.safetensors")
-    save_weights(model, path)
+    save_weights(model, path, state_dict)
     if optimizer is not None:
-        st = {k: v for k, v in optimizer.state_tensors().items()}
+        st = dict(optim_state if optim_state is not None else optimizer.state_tensors())
         meta = {"step": str(optimizer.step_count), "format": "oxidizr_b200.flat_adamw.v1"}
         if extra:
             meta.update({k: str(v) for k, v in extra.items()})
@@ -173,18 +178,48 @@ def cleanup_old_checkpoints(checkpoint_dir: str, max_checkpoints: int) -> None:
                 found.append((int(m.group(1)), os.path.join(checkpoint_dir, fn)))
     found.sort()
     for step, path in found[: max(0, len(found) - max_checkpoints)]:
-        for p in (path, optim_sidecar_path(path), os.path.join(checkpoint_dir, f"checkpoint_step_{step}.meta.json")):
+        stem = path[: -len(".safetensors")]
+        locals_ = [os.path.join(checkpoint_dir, f) for f in os.listdir(checkpoint_dir)
+                   if f.startswith(os.path.basename(stem) + ".optim.local")]
+        for p in [path, optim_sidecar_path(path), os.path.join(checkpoint_dir, f"checkpoint_step_{step}.meta.json")] + \
+                locals_:
             try:
                 os.remove(p)
             except FileNotFoundError:
                 pass
 
 
-def save_final(model, model_cfg: ModelConfig, checkpoint_dir: str, name: str = "final") -> str:
+def save_final(model, model_cfg: ModelConfig, checkpoint_dir: str, name: str = "final",
+               state_dict: Optional[Dict[str, torch.Tensor]] = None) -> str:
     os.makedirs(checkpoint_dir, exist_ok=True)
     path = os.path.join(checkpoint_dir, f"{model_cfg.checkpoint_prefix()}_{name}.safetensors")
-    save_weights(model, path)
+    save_weights(model, path, state_dict)
     return path
+
+
+def local_sidecar_path(weights_path: str, rank: int) -> str:
+    """Per-rank optimizer state of parameters that rank holds alone (expert shards)."""
+    assert weights_path.endswith(".safetensors")
+    return weights_path[: -len(".safetensors")] + f".optim.local{rank}.safetensors"
+
+
+def save_local_optimizer(local_opt, weights_path: str, rank: int, step: int) -> None:
+    save_file(_cpu_contig(local_opt.state_tensors()), local_sidecar_path(weights_path, rank),
+              metadata={"step": str(step), "format": "oxidizr_b200.flat_adamw.v1"})
+
+
+def load_local_optimizer(local_opt, weights_path: str, rank: int) -> bool:
+    sp = local_sidecar_path(weights_path, rank)
+    if local_opt is None or not os.path.exists(sp):
+        return False
+    tens = load_file(sp)
+    with torch.no_grad():
+        local_opt.flat.master.copy_(tens["master"].to(local_opt.flat.master.device))
+        if local_opt.flat.flat is not local_opt.flat.master:
+            local_opt.flat.flat.copy_(local_opt.flat.master)
+        local_opt.m.copy_(tens["exp_avg"].to(local_opt.m.device))
+        local_opt.v.copy_(tens["exp_avg_sq"].to(local_opt.v.device))
+    return True
 
 
 def load_optimizer_sidecar(optimizer, weights_path: str) -> Optional[dict]:

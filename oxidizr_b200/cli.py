@@ -85,7 +85,11 @@ def _free_port() -> int:
 
 
 def _launch_workers(gpu_ids: List[int], argv: List[str], run_dir: str) -> int:
-    """One process per GPU; returns the first non-zero exit code (or 0)."""
+    """One process per GPU; returns the first non-zero exit code (or 0).
+
+    Watchdog: once a worker has failed, the others get ``OXI_FAIL_GRACE``
+    seconds (default 30) to notice it through the process group and exit;
+    the ones still running after that are terminated (then killed)."""
     port = _free_port()
     procs = []
     for rank, gid in enumerate(gpu_ids):
@@ -94,11 +98,30 @@ def _launch_workers(gpu_ids: List[int], argv: List[str], run_dir: str) -> int:
                     "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "OXIDIZED_RUN_DIR": run_dir,
                     "OXI_GPU_ID": str(gid)})
         procs.append(subprocess.Popen([sys.executable, "-m", "oxidizr_b200"] + argv, env=env))
-    rc = 0
-    for p in procs:
-        r = p.wait()
-        rc = rc or r
-    return rc
+    grace = float(os.environ.get("OXI_FAIL_GRACE", "30"))
+    rc, failed_at = 0, None
+    while True:
+        codes = [p.poll() for p in procs]
+        for r, c in enumerate(codes):
+            if c not in (None, 0) and failed_at is None:
+                failed_at = time.time()
+                rc = c
+                print(f"Worker {r} exited with code {c}", file=sys.stderr)
+        if all(c is not None for c in codes):
+            break
+        if failed_at is not None and time.time() - failed_at > grace:
+            for p in procs:
+                if p.poll() is None:
+                    p.terminate()
+            for p in procs:
+                try:
+                    p.wait(timeout=10)
+                except subprocess.TimeoutExpired:
+                    p.kill()
+                    p.wait()
+            break
+        time.sleep(0.2)
+    return rc or next((c for c in (p.returncode for p in procs) if c), 0)
 
 
 def run_train(args, argv: List[str]) -> int:
@@ -240,9 +263,10 @@ def run_train(args, argv: List[str]) -> int:
     if resume_path:
         say(f"Loading checkpoint from: {resume_path}")
         C.load_weights(model, resume_path)
-        if flat is not None and flat.master is not flat.flat:
-            flat.master.copy_(flat.flat.float())
+        opt.sync_master_from_params()
         meta = C.load_optimizer_sidecar(opt, resume_path)
+        if getattr(opt, "local", None) is not None:
+            C.load_local_optimizer(opt.local, resume_path, rank)
         if meta and "data_cursor" in meta:
             cursor = int(meta["data_cursor"])
         if start_step:

@@ -133,6 +133,32 @@ class LitGPT(RefModule):
         out[prefix + "lm_head.weight"] = self.lm_head.detach()
         return out
 
+    def _ep_group(self):
+        for m in self.modules():
+            if isinstance(m, MoE) and m.ep_size > 1:
+                return m.ep_group
+        return None
+
+    def export_ref_gathered(self, dst: int = 0) -> Optional["OrderedDict[str, torch.Tensor]"]:
+        """``export_ref`` with the expert shards of expert-parallel layers gathered
+        to rank ``dst`` (collective over the expert-parallel group; other ranks
+        get None).  Without expert parallelism it is plain ``export_ref``."""
+        sd = self.export_ref()
+        g = self._ep_group()
+        if g is None:
+            return sd
+        import torch.distributed as dist
+        mine = {k: v.cpu() for k, v in sd.items() if ".experts." in k}
+        rank = dist.get_rank(g)
+        parts = [None] * dist.get_world_size(g) if rank == dst else None
+        dist.gather_object(mine, parts, dst=dist.get_global_rank(g, dst), group=g)
+        if rank != dst:
+            return None
+        out = OrderedDict((k, v) for k, v in sd.items() if ".experts." not in k)
+        for part in parts:
+            out.update(part)
+        return out
+
     def import_ref(self, sd: dict, prefix: str = "") -> None:
         _assign(self.embed_tokens, sd, prefix + "embed_tokens.weight")
         for i, layer in enumerate(self.layers):

@@ -132,6 +132,11 @@ class LocalAdamW:
     def state_tensors(self) -> Dict[str, torch.Tensor]:
         return {"master": self.flat.master, "exp_avg": self.m, "exp_avg_sq": self.v}
 
+    def sync_master_from_params(self) -> None:
+        if self.flat.master is not self.flat.flat:
+            with torch.no_grad():
+                self.flat.master.copy_(self.flat.flat.float())
+
 
 class AdamW:
     """Single-process optimizer over a :class:`FlatParams`.
@@ -209,6 +214,15 @@ class AdamW:
         return self._norm
 
     # ------------------------------------------------------------ state
+    def sync_master_from_params(self) -> None:
+        """Re-derive the f32 master weights after the parameters were loaded."""
+        f = self.flat
+        if f.master is not f.flat:
+            with torch.no_grad():
+                f.master.copy_(f.flat.float())
+        if self.local is not None:
+            self.local.sync_master_from_params()
+
     def state_tensors(self) -> Dict[str, torch.Tensor]:
         return {"master": self.flat.master, "exp_avg": self.m, "exp_avg_sq": self.v}
 

@@ -71,6 +71,8 @@ class SymmetricBuffer:
 class FusedDDPAdamW:
     """Drop-in optimizer for data-parallel training over NVLink (sync backend ``fused``)."""
 
+    collective_state = True  # state_tensors() gathers the shards: every rank calls it
+
     def __init__(self, named_params: Sequence[Tuple[str, torch.nn.Parameter]], cfg: AdamWConfig, device,
                  group=None, bucket_bytes: int = 32 << 20, rs_ctas: Optional[int] = None,
                  peer_timeout_s: float = 30.0):
@@ -240,6 +242,15 @@ class FusedDDPAdamW:
         """Full master / moments in flat layout (collective: every rank must call)."""
         return {"master": self._gather_full(self.master), "exp_avg": self._gather_full(self.m),
                 "exp_avg_sq": self._gather_full(self.v)}
+
+    def sync_master_from_params(self) -> None:
+        """Re-derive this rank's f32 master shards after the parameters were loaded."""
+        with torch.no_grad():
+            for lo, ln, so, _ in self.buckets:
+                sh = ln // self.W
+                self.master[so:so + sh].copy_(self.flat[lo + self.rank * sh: lo + (self.rank + 1) * sh].float())
+        if self.local is not None:
+            self.local.sync_master_from_params()
 
     def load_state_tensors(self, d, step: int):
         with torch.no_grad():

@@ -102,6 +102,9 @@ class Trainer:
     # ------------------------------------------------------------ one step
     def training_step(self):
         """Returns (mean CE loss, grad norm) as device scalars."""
+        from .utils.faults import fault_for, nvtx_range, profile_window
+        fault = fault_for(self.rank, self.global_step)
+        profile_window(self.global_step)
         accum = self.tc.gradient_accumulation
         alpha = float(self.tc.load_balance_alpha)
         total_ce = torch.zeros((), dtype=torch.float32, device=self.device)
@@ -109,14 +112,19 @@ class Trainer:
             if hasattr(self.opt, "accumulating"):
                 self.opt.accumulating = micro < accum - 1
             x, y = self.loader.next_batch()
-            ce, aux = self.model(x, y)
+            with nvtx_range("forward"):
+                ce, aux = self.model(x, y)
             loss = ce.float()
             if aux:
                 loss = loss + alpha * torch.stack([a.float() for a in aux]).mean()
-            (loss / accum).backward()
+            with nvtx_range("backward"):
+                (loss / accum).backward()
             total_ce = total_ce + ce.detach().float()
-        gnorm = self.opt.step()
+        with nvtx_range("optimizer"):
+            gnorm = self.opt.step()
         self.global_step += 1
+        if fault == "nan":
+            total_ce = total_ce * float("nan")
         return total_ce / accum, gnorm
 
     def _check_finite(self, loss: float):
@@ -186,16 +194,38 @@ class Trainer:
             self.out(f"Training complete | final loss: {self.last_loss:.4f} | grad: {self.last_grad_norm:.4f}")
 
     # ------------------------------------------------------------ checkpoints
+    def _gather_weights(self):
+        """Weights in upstream names on rank 0 (collective when experts are sharded)."""
+        if hasattr(self.model, "export_ref_gathered"):
+            return self.model.export_ref_gathered()
+        return self.model.export_ref() if self.rank == 0 else None
+
     def save(self, step: int):
+        """Every rank calls this: sharded optimizer state and expert shards are
+        gathered collectively; rank 0 writes the files, each rank writes the
+        state of the parameters it holds alone."""
         if self.on_checkpoint is not None:
             self.on_checkpoint(step)
             return
+        sd = self._gather_weights()
+        st = None
+        if getattr(self.opt, "collective_state", False) or self.rank == 0:
+            st = self.opt.state_tensors()
+        from .checkpoint import save_local_optimizer
+        prefix = self.cfg.model.checkpoint_prefix()
+        path = os.path.join(self.tc.checkpoint_dir, f"{prefix}_step_{step}.safetensors")
         if self.rank == 0:
             save_checkpoint(self.model, self.opt, step, self.cfg.model, self.tc.checkpoint_dir, self.data_file_path,
-                            self.tc.max_checkpoints, extra={"data_cursor": getattr(self.loader, "cursor", 0)})
+                            self.tc.max_checkpoints, extra={"data_cursor": getattr(self.loader, "cursor", 0)},
+                            state_dict=sd, optim_state=st)
+        local = getattr(self.opt, "local", None)
+        if local is not None:
+            os.makedirs(self.tc.checkpoint_dir, exist_ok=True)
+            save_local_optimizer(local, path, self.rank, step)
 
     def _final(self):
+        sd = self._gather_weights()
         if self.rank == 0:
             prefix = self.cfg.model.checkpoint_prefix()
             self.out(f"Saving final checkpoint to {self.tc.checkpoint_dir}/{prefix}_final.safetensors")
-            save_final(self.model, self.cfg.model, self.tc.checkpoint_dir)
+            save_final(self.model, self.cfg.model, self.tc.checkpoint_dir, state_dict=sd)
