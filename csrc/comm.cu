@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(512) push_bucket_kernel(const float* __restric
                                                           int rank, const uint64_t* __restrict__ peers_recv,
                                                           const uint64_t* __restrict__ peer_pads, int bucket,
                                                           int epoch, int* __restrict__ done_ctr) {
-  constexpr int UNR = 4;  // 8-element vectors per thread in flight (128 B of f32 loads)
+  constexpr int UNR = 8;  // 8-element vectors per thread in flight (256 B of f32 loads)
   const int64_t shard = len / W;
   const int64_t nv = len / 8;
   const int64_t sv = shard / 8;  // 8-element vectors per shard
@@ -194,41 +194,24 @@ __global__ void __launch_bounds__(512) reduce_bucket_kernel(const __nv_bfloat16*
   }
 }
 
-// Reduce-scatter of one bucket, pull through the TMA engine.
-//
-// Every rank has cast its gradient of the bucket to bf16 in its own send
-// buffer (grad_to_bf16) and posts the bucket's epoch (CTA 0).  Each CTA of the
-// owner then streams its chunks of the owned shard from all W send buffers
-// into shared memory with bulk copies (one producer thread, RS_STAGES deep;
-// the copy engine keeps the NVLink reads in flight, not the threads) and the
-// consumer warps sum the W slices in f32.
-constexpr int RS_STAGES = 3;
-constexpr int RS_STAGE_BYTES = 8192;  // small enough to share an SM with a GEMM CTA
-constexpr int RS_CONSUMERS = 128;
-__host__ __device__ constexpr int rs_chunk_elems(int W) { return (RS_STAGE_BYTES / 2 / W) / 64 * 64; }
-
+// Reduce-scatter of one bucket, pull: every rank has cast its gradient of the
+// bucket to bf16 in its own send buffer (grad_to_bf16) and posts the bucket's
+// epoch (CTA 0); the owner of each shard then reads the W slices with 16-byte
+// loads and sums them in f32.  NVLink reads take microseconds, so each thread
+// keeps UNR vectors of every peer in flight (measured on B200: about 2 MB in
+// flight per GPU saturates a peer link).
 template <int W>
-__global__ void __launch_bounds__(RS_CONSUMERS + 32) rs_tma_kernel(
-    const uint64_t* __restrict__ peers_send, const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad,
-    int rank, int bucket, int epoch, int64_t lo, int64_t len, float* __restrict__ rgrad, float* __restrict__ sumsq,
-    int* status, uint64_t wait_ns) {
-  constexpr int CE = rs_chunk_elems(W);  // elements per peer per chunk (a multiple of 64)
-  __shared__ __align__(128) uint4 sbuf[RS_STAGES * RS_STAGE_BYTES / 16];
-  __shared__ uint64_t full[RS_STAGES], empty[RS_STAGES];
-  __shared__ int abort_s, ok_s;
-  __shared__ float red[8];
-  const __nv_bfloat16* stage_base = reinterpret_cast<const __nv_bfloat16*>(sbuf);
+__global__ void __launch_bounds__(512) rs_pull_kernel(const uint64_t* __restrict__ peers_send,
+                                                      const uint64_t* __restrict__ peer_pads,
+                                                      int* __restrict__ my_pad, int rank, int bucket, int epoch,
+                                                      int64_t lo, int64_t len, float* __restrict__ rgrad,
+                                                      float* __restrict__ sumsq, int* status, uint64_t wait_ns) {
+  constexpr int UNR = (16 / W) < 1 ? 1 : ((16 / W) > 8 ? 8 : 16 / W);
+  __shared__ int ok_s;
+  __shared__ float red[32];
   const int64_t shard = len / W;
   const int64_t s0 = lo + rank * shard;
-  const int64_t nch = (shard + CE - 1) / CE;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < RS_STAGES; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], RS_CONSUMERS / 32);
-    }
-    abort_s = 0;
-    fence_mbar_init();
     if (blockIdx.x == 0) {
       // the send buffer of this bucket was written by the previous kernel on
       // this stream; make it visible system-wide, then tell every peer.
@@ -241,61 +224,46 @@ __global__ void __launch_bounds__(RS_CONSUMERS + 32) rs_tma_kernel(
   __syncthreads();
   float ss = 0.f;
   if (ok_s) {
-    if (warp == 0) {
-      if (lane == 0) {
-        int64_t it = 0;
-        for (int64_t c = blockIdx.x; c < nch; c += gridDim.x, ++it) {
-          const int st = (int)(it % RS_STAGES);
-          const uint32_t ph = (uint32_t)((it / RS_STAGES) & 1);
-          if (!mbar_wait(&empty[st], ph ^ 1, &abort_s, status)) break;
-          const int64_t e0 = c * CE;
-          const int n = (int)min((int64_t)CE, shard - e0);
-          mbar_arrive_expect_tx(&full[st], (uint32_t)(W * n * 2));
+    const uint4* src[W];
 #pragma unroll
-          for (int r = 0; r < W; ++r) {
-            const int peer = (rank + r) % W;  // stagger peers so ranks do not all hit the same one
-            bulk_load(const_cast<__nv_bfloat16*>(stage_base) + (st * W + r) * CE,
-                      reinterpret_cast<const __nv_bfloat16*>(peers_send[peer]) + s0 + e0, (uint32_t)(n * 2),
-                      &full[st]);
-          }
-        }
-        // leave no copy in flight into this CTA's shared memory
-        for (int64_t j = (it > RS_STAGES ? it - RS_STAGES : 0); j < it; ++j)
-          mbar_wait(&full[j % RS_STAGES], (uint32_t)((j / RS_STAGES) & 1), nullptr, status);
+    for (int i = 0; i < W; ++i) {
+      const int peer = (rank + i) % W;  // stagger peers so ranks do not all hit the same one
+      src[i] = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers_send[peer]) + s0);
+    }
+    const int64_t nv = shard / 8;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nv; base += stride * UNR) {
+      uint4 u[UNR][W];
+#pragma unroll
+      for (int r = 0; r < UNR; ++r) {
+        const int64_t v = base + r * stride;
+#pragma unroll
+        for (int i = 0; i < W; ++i) u[r][i] = v < nv ? src[i][v] : make_uint4(0u, 0u, 0u, 0u);
       }
-      __syncwarp();
-    } else {
-      const int t = threadIdx.x - 32;
-      int64_t it = 0;
-      for (int64_t c = blockIdx.x; c < nch; c += gridDim.x, ++it) {
-        const int st = (int)(it % RS_STAGES);
-        const uint32_t ph = (uint32_t)((it / RS_STAGES) & 1);
-        if (!mbar_wait(&full[st], ph, &abort_s, status)) break;
-        const int64_t e0 = c * CE;
-        const int n = (int)min((int64_t)CE, shard - e0);
-        for (int v = t; v < n / 8; v += RS_CONSUMERS) {
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int r = 0; r < W; ++r) add8(acc, reinterpret_cast<const uint4*>(stage_base + (st * W + r) * CE)[v]);
-          float4* o = reinterpret_cast<float4*>(rgrad + e0 + v * 8);  // rgrad points at this bucket's shard
-          o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-          o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      for (int r = 0; r < UNR; ++r) {
+        const int64_t v = base + r * stride;
+        if (v >= nv) break;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
+        for (int i = 0; i < W; ++i) add8(acc, u[r][i]);
+        float4* o = reinterpret_cast<float4*>(rgrad + v * 8);  // rgrad points at this bucket's shard
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
       }
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0 && warp > 0) red[warp - 1] = ss;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float tsum = 0.f;
-    for (int i = 0; i < RS_CONSUMERS / 32; ++i) tsum += red[i];
-    atomicAdd(sumsq, tsum);
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) atomicAdd(sumsq, t);
   }
 }
 
@@ -476,15 +444,14 @@ void launch_rs_bucket(int mode, const float* grad, const uint64_t* peers_buf, vo
   OXI_CHECK(len % (W * 64) == 0, "bucket length must divide into 64-element shards");
   OXI_CHECK(W >= 1 && W <= 8, "fused data parallelism supports 1..8 ranks per node, got ", W);
   if (mode == 0) {
-    // pull: local cast into the send buffer, then TMA-fed reduction of the owned shard
+    // pull: local cast into the send buffer, then the owner sums the W slices of its shard
     launch_grad_to_bf16(grad + lo, reinterpret_cast<__nv_bfloat16*>(my_buf) + lo, len, st);
-    const int64_t nch = (len / W + rs_chunk_elems(W) - 1) / rs_chunk_elems(W);
-    const int g = (int)std::max<int64_t>(1, std::min<int64_t>(nch, (int64_t)ctas));
+    const int g = (int)std::max<int64_t>(1, std::min<int64_t>((len / W / 8 + 511) / 512, (int64_t)ctas));
     switch (W) {
-#define OXI_RS(N)                                                                                              \
-  case N:                                                                                                      \
-    rs_tma_kernel<N><<<g, RS_CONSUMERS + 32, 0, st>>>(peers_buf, peer_pads, my_pad, rank, bucket, epoch, lo, len, \
-                                                      rgrad, sumsq, status, (uint64_t)wait_ns);                 \
+#define OXI_RS(N)                                                                                                \
+  case N:                                                                                                        \
+    rs_pull_kernel<N><<<g, 512, 0, st>>>(peers_buf, peer_pads, my_pad, rank, bucket, epoch, lo, len, rgrad, sumsq, \
+                                         status, (uint64_t)wait_ns);                                             \
     break;
       OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)
 #undef OXI_RS

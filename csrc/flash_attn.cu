@@ -30,6 +30,7 @@ namespace {
 
 constexpr int FA_BM = 128, FA_BN = 128;
 constexpr int FA_THREADS = 192;
+constexpr int FA_BWD_THREADS = 320;  // TMA warp, MMA warp, 8 softmax/epilogue warps
 
 struct FaParams {
   int B, S, Hq, Hk;
@@ -423,7 +424,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 }
 
 template <int DQ, int DV>
-__global__ void __launch_bounds__(FA_THREADS, 1)
+__global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                   FaBwdParams p) {
@@ -463,9 +464,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     mbar_init(kv_full, 1);
     mbar_init(qdo_full, 1);
     mbar_init(sdp_full, 1);
-    mbar_init(p_ready, 4);   // one arrival per softmax warp
+    mbar_init(p_ready, 8);   // one arrival per softmax warp
     mbar_init(it_done, 1);
-    mbar_init(dq_read, 4);
+    mbar_init(dq_read, 8);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -546,7 +547,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
     __syncwarp();
   } else {
+    // warps 2..9: warp w reads TMEM lanes 32*(w%4).. (its row quarter) and
+    // handles column half `half` of every 128-wide tile it processes.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // key row for P/dS; query row for the dQ epilogue
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const int tid = threadIdx.x - 64;
@@ -556,90 +560,78 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const int h = hk * group + it / n_i;
       const int i = i_start + it % n_i;
       const int q0 = i * 128;
-      named_bar_sync(1, 128);  // previous iteration is done with s_lse / s_delta
-      {
+      named_bar_sync(1, 256);  // previous iteration is done with s_lse / s_delta
+      if (tid < 128) {
         const int qp = q0 + tid;
         const int64_t vi = ((int64_t)b * p.Hq + h) * p.S + qp;
         s_lse[tid] = qp < p.S ? p.lse[vi] * 1.4426950408889634f : 0.f;
         s_delta[tid] = qp < p.S ? p.delta[vi] : 0.f;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (!mbar_wait(sdp_full, it & 1, abort_flag, p.status)) { ok = false; break; }
       // P^T / dS^T smem is free once the previous iteration's MMAs completed
       if (!mbar_wait(it_done, (it & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
       const bool diag = p.causal && (q0 < k0 + 128);
 #pragma unroll 1
-      for (int c2 = 0; c2 < 4; c2 += 2) {
-        uint32_t sr[2][32], dr[2][32];
-        tmem_ld32(TM_S + lane_base + c2 * 32, sr[0]);
-        tmem_ld32(TM_S + lane_base + c2 * 32 + 32, sr[1]);
-        tmem_ld32(TM_DP + lane_base + c2 * 32, dr[0]);
-        tmem_ld32(TM_DP + lane_base + c2 * 32 + 32, dr[1]);
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;  // 32-query chunk 0..3
+        uint32_t sr[32], dr[32];
+        tmem_ld32(TM_S + lane_base + c * 32, sr);
+        tmem_ld32(TM_DP + lane_base + c * 32, dr);
         tc_wait_ld();
+        uint32_t pk[16], dk[16];
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int c = c2 + h2;
-          uint32_t pk[16], dk[16];
+        for (int t = 0; t < 32; t += 2) {
+          float pv[2], dsv[2];
 #pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            float pv[2], dsv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int qc = c * 32 + t + e;
-              const int qp = q0 + qc;
-              const bool valid = (qp < p.S) && (kpos < p.S) && (!diag || qp >= kpos);
-              const float pp =
-                  valid ? ex2_approx(__uint_as_float(sr[h2][t + e]) * p.scale_log2 - s_lse[qc]) : 0.f;
-              pv[e] = pp;
-              dsv[e] = pp * (__uint_as_float(dr[h2][t + e]) - s_delta[qc]) * p.scale;
-            }
-            pk[t / 2] = pack_bf16(pv[0], pv[1]);
-            dk[t / 2] = pack_bf16(dsv[0], dsv[1]);
+          for (int e = 0; e < 2; ++e) {
+            const int qc = c * 32 + t + e;
+            const int qp = q0 + qc;
+            const bool valid = (qp < p.S) && (kpos < p.S) && (!diag || qp >= kpos);
+            const float pp = valid ? ex2_approx(__uint_as_float(sr[t + e]) * p.scale_log2 - s_lse[qc]) : 0.f;
+            pv[e] = pp;
+            dsv[e] = pp * (__uint_as_float(dr[t + e]) - s_delta[qc]) * p.scale;
           }
+          pk[t / 2] = pack_bf16(pv[0], pv[1]);
+          dk[t / 2] = pack_bf16(dsv[0], dsv[1]);
+        }
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int ch = c * 4 + q;  // 8-query chunk index 0..15
-            sw128_store16(sPt + (ch >> 3) * (128 * 128), r, ch & 7,
-                          make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]));
-            sw128_store16(sDSt + (ch >> 3) * (128 * 128), r, ch & 7,
-                          make_uint4(dk[q * 4], dk[q * 4 + 1], dk[q * 4 + 2], dk[q * 4 + 3]));
-          }
+        for (int q = 0; q < 4; ++q) {
+          const int ch = c * 4 + q;  // 8-query chunk index 0..15
+          sw128_store16(sPt + (ch >> 3) * (128 * 128), r, ch & 7,
+                        make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]));
+          sw128_store16(sDSt + (ch >> 3) * (128 * 128), r, ch & 7,
+                        make_uint4(dk[q * 4], dk[q * 4 + 1], dk[q * 4 + 2], dk[q * 4 + 3]));
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
-      // dQ of this (h, i): thread r owns query row r
+      // dQ of this (h, i): thread r owns query row r; the two halves take alternate 32-column chunks
       if (!mbar_wait(it_done, it & 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
       const int qp = q0 + r;
       float* dqrow = p.dq_acc + (int64_t)(row0 + qp) * p.ld_dq + h * DQ;
 #pragma unroll 1
-      for (int c2 = 0; c2 < DQ / 32; c2 += 2) {
-        const int nc = (c2 + 1 < DQ / 32) ? 2 : 1;  // 32-column chunks in this batch
-        uint32_t o[2][32];
-        tmem_ld32(TM_DQ + lane_base + c2 * 32, o[0]);
-        if (nc == 2) tmem_ld32(TM_DQ + lane_base + c2 * 32 + 32, o[1]);
+      for (int c = half; c < DQ / 32; c += 2) {
+        uint32_t o[32];
+        tmem_ld32(TM_DQ + lane_base + c * 32, o);
         tc_wait_ld();
         if (qp < p.S) {
+          float4* d4 = reinterpret_cast<float4*>(dqrow + c * 32);
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            if (h2 >= nc) break;
-            float4* d4 = reinterpret_cast<float4*>(dqrow + (c2 + h2) * 32);
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              atomicAdd(d4 + q, make_float4(__uint_as_float(o[h2][q * 4]), __uint_as_float(o[h2][q * 4 + 1]),
-                                            __uint_as_float(o[h2][q * 4 + 2]), __uint_as_float(o[h2][q * 4 + 3])));
-          }
+          for (int q = 0; q < 8; ++q)
+            atomicAdd(d4 + q, make_float4(__uint_as_float(o[q * 4]), __uint_as_float(o[q * 4 + 1]),
+                                          __uint_as_float(o[q * 4 + 2]), __uint_as_float(o[q * 4 + 3])));
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_read);
     }
-    // dK, dV of this key tile (thread r owns key row r)
+    // dK, dV of this key tile (thread r owns key row r; halves take alternate chunks)
     if (ok && n_it > 0) {
       tc_fence_after();
       const bool valid = kpos < p.S;
@@ -650,7 +642,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         const uint32_t src = (which == 0 ? TM_DV : TM_DK) + lane_base;
         const int ncol = which == 0 ? DV : DQ;
 #pragma unroll 1
-        for (int c = 0; c < ncol / 32; ++c) {
+        for (int c = half; c < ncol / 32; c += 2) {
           uint32_t o[32];
           tmem_ld32(src + c * 32, o);
           tc_wait_ld();
@@ -665,7 +657,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           }
         }
       }
-    } else if (n_it == 0 && kpos < p.S) {
+    } else if (n_it == 0 && kpos < p.S && half == 0) {
       // no query attends to this key tile: zero gradients
       __nv_bfloat16* dv = p.dv + (int64_t)(row0 + kpos) * p.ld_dv + hk * DV;
       __nv_bfloat16* dk = p.dk + (int64_t)(row0 + kpos) * p.ld_dk + hk * DQ;
@@ -753,7 +745,7 @@ void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
     attr = true;
   }
   dim3 grid((S + 127) / 128, Hk, B);
-  kern<<<grid, FA_THREADS, L::TOTAL, st>>>(tq, tk, tv, tdo, p);
+  kern<<<grid, FA_BWD_THREADS, L::TOTAL, st>>>(tq, tk, tv, tdo, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

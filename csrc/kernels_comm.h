@@ -40,4 +40,10 @@ void launch_adamw_allgather(const int64_t* buckets, int nb, int rank, int W, con
                             int epoch, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2,
                             const float* coef, int* done_ctr, int* status, int64_t wait_ns, cudaStream_t st);
 
+// NVLink microbenchmark kernels (p2pbench.cu): move `bytes` bytes from/to a
+// (peer) buffer with SM loads / stores or bulk copies; nothing waits on a peer.
+void launch_p2p_read(const void* src, int64_t bytes, void* sink, int ctas, int threads, int unr, cudaStream_t st);
+void launch_p2p_write(void* dst, int64_t bytes, int ctas, int threads, int unr, cudaStream_t st);
+void launch_p2p_bulk(bool write, void* peer, int64_t bytes, int ctas, int chunk, int stages, int* status,
+                     cudaStream_t st);
 }  // namespace oxi

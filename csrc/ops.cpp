@@ -453,6 +453,39 @@ std::vector<torch::Tensor> ep_gather(torch::Tensor topi, torch::Tensor pos, int6
   return {dx, dw};
 }
 
+// ------------------------------------------------------------ NVLink microbenchmarks
+bool enable_peer_access(int64_t device, int64_t peer) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  int can = 0;
+  C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&can, (int)device, (int)peer));
+  if (!can) return false;
+  cudaError_t e = cudaDeviceEnablePeerAccess((int)peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return true;
+  }
+  C10_CUDA_CHECK(e);
+  return true;
+}
+
+void p2p_read(int64_t src, int64_t bytes, torch::Tensor sink, int64_t ctas, int64_t threads, int64_t unr) {
+  c10::cuda::CUDAGuard g(sink.device());
+  oxi::launch_p2p_read(reinterpret_cast<const void*>(src), bytes, sink.data_ptr(), (int)ctas, (int)threads, (int)unr,
+                       stream());
+}
+
+void p2p_write(int64_t dst, int64_t bytes, torch::Tensor on_device, int64_t ctas, int64_t threads, int64_t unr) {
+  c10::cuda::CUDAGuard g(on_device.device());
+  oxi::launch_p2p_write(reinterpret_cast<void*>(dst), bytes, (int)ctas, (int)threads, (int)unr, stream());
+}
+
+void p2p_bulk(bool write, int64_t peer, int64_t bytes, int64_t ctas, int64_t chunk, int64_t stages,
+              torch::Tensor status) {
+  c10::cuda::CUDAGuard g(status.device());
+  oxi::launch_p2p_bulk(write, reinterpret_cast<void*>(peer), bytes, (int)ctas, (int)chunk, (int)stages,
+                       status_ptr(status), stream());
+}
+
 // ------------------------------------------------------------ SSM
 void conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias, torch::Tensor y, int64_t B,
                 int64_t S, bool act) {
@@ -736,6 +769,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_push_dy", &ep_push_dy, "expert-parallel backward: push output gradients to the owners");
   m.def("ep_scale_rows", &ep_scale_rows, "owner side: routing-weight gradient and scaling of received rows");
   m.def("ep_gather", &ep_gather, "expert-parallel backward: gather input gradients and weight gradients");
+  m.def("enable_peer_access", &enable_peer_access, "cudaDeviceEnablePeerAccess(device -> peer)");
+  m.def("p2p_read", &p2p_read, "microbenchmark: SM loads from (peer) memory");
+  m.def("p2p_write", &p2p_write, "microbenchmark: SM stores to (peer) memory");
+  m.def("p2p_bulk", &p2p_bulk, "microbenchmark: bulk (TMA engine) copies from/to (peer) memory");
   m.def("ipc_alloc", &ipc_alloc, "zeroed device buffer exportable over CUDA IPC");
   m.def("ipc_open", &ipc_open, "map a peer's IPC buffer");
   m.def("ipc_close", &ipc_close, "unmap a peer's IPC buffer");

@@ -9,10 +9,9 @@ issued from our own kernels:
 * buckets of parameters (reverse order of use) are reduced as soon as
   backward has produced all their gradients, on a side stream, so the
   transfers overlap the rest of backward: each rank casts its gradient to
-  bf16 in its send buffer, and the owner of each shard streams the W slices
-  over NVLink into shared memory with TMA bulk copies and sums them in f32
-  (``OXI_RS_MODE=push``: NVLink stores into the owners' receive slots, then a
-  local sum);
+  bf16 in its send buffer, and the owner of each shard reads the W slices
+  over NVLink and sums them in f32 (``OXI_RS_MODE=push``: NVLink stores into
+  the owners' receive slots, then a local sum);
 * each rank keeps f32 master weights and AdamW moments for its 1/W shard of
   every bucket only (optimizer state sharded W ways);
 * after backward: one tiny kernel exchanges partial norms (global-norm clip),
@@ -82,7 +81,7 @@ class FusedDDPAdamW:
         self.rank = dist.get_rank(group)
         self.W = dist.get_world_size(group)
         # CTAs per reduce-scatter kernel (they share SMs with the backward GEMMs)
-        self.rs_ctas = int(rs_ctas if rs_ctas is not None else os.environ.get("OXI_RS_CTAS", 32))
+        self.rs_ctas = int(rs_ctas if rs_ctas is not None else os.environ.get("OXI_RS_CTAS", 64))
         # a peer that has not posted its flag within this time is reported as failed
         self.wait_ns = int(peer_timeout_s * 1e9)
         named_params, local = split_local(list(named_params))

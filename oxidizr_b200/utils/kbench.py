@@ -120,6 +120,77 @@ def bench_attn(B=8, S=2048, Hq=16, Hk=8, D=128, iters=20):
     return out
 
 
+def bench_attn_mla(B=16, S=1024, H=12, Dqk=96, Dv=64, iters=20):
+    """Multi-head latent attention shapes (q/k carry a RoPE part): ours vs torch SDPA."""
+    import math
+    from ..ops.flash import FlashAttention
+    peaks = measured_peaks()
+    q = torch.randn(B, S, H, Dqk, device="cuda").bfloat16().requires_grad_()
+    k = torch.randn(B, S, H, Dqk, device="cuda").bfloat16().requires_grad_()
+    v = torch.randn(B, S, H, Dv, device="cuda").bfloat16().requires_grad_()
+    do = torch.randn(B, S, H, Dv, device="cuda").bfloat16()
+    scale = 1.0 / math.sqrt(Dqk)
+    flops_f = 2.0 * B * H * S * S * (Dqk + Dv) / 2
+    def ours_f():
+        with torch.no_grad():
+            FlashAttention.apply(q, k, v, scale, True)
+    def ours_fb():
+        FlashAttention.apply(q, k, v, scale, True).backward(do)
+    qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
+    sd = lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, is_causal=True, scale=scale)
+    def ref_f():
+        with torch.no_grad():
+            sd()
+    def ref_fb():
+        sd().backward(do.transpose(1, 2))
+    res = {}
+    for name, fn, fl in (("ours_fwd", ours_f, flops_f), ("ours_fwd_bwd", ours_fb, 3.5 * flops_f),
+                         ("sdpa_fwd", ref_f, flops_f), ("sdpa_fwd_bwd", ref_fb, 3.5 * flops_f)):
+        ms = time_fn(fn, iters)
+        res[name] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
+                     "frac_of_peak": round(fl / ms / 1e9 / peaks["bf16_tflops"], 3)}
+    out = {"mla": True, "B": B, "S": S, "H": H, "Dqk": Dqk, "Dv": Dv, "peak_source": peaks["source"], **res}
+    print(json.dumps(out), flush=True)
+    return out
+
+
+def bench_ssm(iters=10):
+    """Selective-scan kernels at the hybrid (Mamba2) and Mamba3 bench shapes: time and the
+    effective HBM rate of the scan inputs/outputs (f32)."""
+    from ..ops import ssm
+    peaks = measured_peaks()
+    out = []
+    for name, (B, S, H, P, N, three) in (("mamba2_cfg3", (16, 1024, 24, 64, 128, False)),
+                                         ("mamba3_cfg4", (4, 4096, 32, 256, 128, True))):
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(B, S, H, P, device="cuda", generator=g).bfloat16().requires_grad_()
+        dt = (torch.rand(B, S, H, device="cuda", generator=g) * 0.1 + 0.001).requires_grad_()
+        A = -torch.rand(H, device="cuda", generator=g) - 0.5
+        Bm = torch.randn(B, S, H if three else 1, N, device="cuda", generator=g).requires_grad_()
+        Cm = torch.randn(B, S, H if three else 1, N, device="cuda", generator=g).requires_grad_()
+        lam = torch.rand(B, S, H, device="cuda", generator=g).requires_grad_()
+        if three:
+            f = lambda: ssm.mamba3_scan(x, dt, A, Bm, Cm, lam, 256)
+        else:
+            f = lambda: ssm.ssd(x, dt, A, Bm, Cm, 256)
+        dy = torch.randn(B, S, H, P, device="cuda", generator=g)
+        def fwd():
+            with torch.no_grad():
+                f()
+        def fb():
+            f().backward(dy)
+        ms_f = time_fn(fwd, iters)
+        ms_fb = time_fn(fb, iters)
+        # algorithmic f32 bytes of the scan: x, y, B, C, per-step scalars (fwd); x, y, dy, dx, B, C, dB, dC (bwd)
+        nb = 4.0 * B * S * (H * P * 2 + 2 * (H if three else 1) * N + 3 * H)
+        row = {"name": name, "B": B, "S": S, "H": H, "P": P, "N": N, "fwd_ms": round(ms_f, 3),
+               "fwd_bwd_ms": round(ms_fb, 3), "fwd_GBps": round(nb / ms_f / 1e6, 1),
+               "fwd_frac_of_hbm": round(nb / ms_f / 1e6 / peaks["hbm_gbs"], 3)}
+        print(json.dumps(row), flush=True)
+        out.append(row)
+    return out
+
+
 def run_once(what: str):
     """Launch one kernel of a small case a few times (targets for ncu captures)."""
     import math
@@ -151,7 +222,7 @@ def run_once(what: str):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn", "once"])
+    ap.add_argument("what", choices=["gemm", "attn", "ssm", "once"])
     ap.add_argument("--kernel", default="fa_fwd", help="for 'once': fa_fwd | fa_bwd | gemm | gemm_dw")
     ap.add_argument("--shapes", nargs="*", default=None, help="M,N,K[,layout] with layout nn|nt|tt")
     ap.add_argument("--iters", type=int, default=20)
@@ -162,6 +233,10 @@ def main(argv=None):
     if args.what == "attn":
         bench_attn(iters=args.iters)
         bench_attn(D=64, Hq=32, Hk=8, iters=args.iters)
+        bench_attn_mla(iters=args.iters)
+        return
+    if args.what == "ssm":
+        bench_ssm(iters=args.iters)
         return
     if args.what == "gemm":
         if args.shapes:
