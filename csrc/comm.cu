@@ -194,34 +194,35 @@ __global__ void __launch_bounds__(512) reduce_bucket_kernel(const __nv_bfloat16*
   }
 }
 
+// One thread: make this rank's send buffer of the bucket visible, post the
+// bucket's epoch in every peer's pad and wait (bounded) for every peer's post.
+__global__ void rs_flags_kernel(const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad, int rank, int W,
+                                int bucket, int epoch, int* status, uint64_t wait_ns) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  __threadfence_system();
+  for (int i = 0; i < W; ++i)
+    st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_READY + bucket * PAD_MAXW + rank, epoch);
+  wait_flags(my_pad + PAD_READY + bucket * PAD_MAXW, W, 1, epoch, status, wait_ns);
+}
+
 // Reduce-scatter of one bucket, pull: every rank has cast its gradient of the
 // bucket to bf16 in its own send buffer (grad_to_bf16) and posts the bucket's
 // epoch (CTA 0); the owner of each shard then reads the W slices with 16-byte
 // loads and sums them in f32.  NVLink reads take microseconds, so each thread
 // keeps UNR vectors of every peer in flight (measured on B200: about 2 MB in
 // flight per GPU saturates a peer link).
+// Posting and waiting for the bucket's flags is done by rs_flags_kernel (one
+// thread) just before this kernel on the same stream, so no SM spins here
+// while peers are still in their backward pass.
 template <int W>
-__global__ void __launch_bounds__(512) rs_pull_kernel(const uint64_t* __restrict__ peers_send,
-                                                      const uint64_t* __restrict__ peer_pads,
-                                                      int* __restrict__ my_pad, int rank, int bucket, int epoch,
-                                                      int64_t lo, int64_t len, float* __restrict__ rgrad,
-                                                      float* __restrict__ sumsq, int* status, uint64_t wait_ns) {
+__global__ void __launch_bounds__(512) rs_pull_kernel(const uint64_t* __restrict__ peers_send, int rank, int64_t lo,
+                                                      int64_t len, float* __restrict__ rgrad,
+                                                      float* __restrict__ sumsq, const int* status) {
   constexpr int UNR = (16 / W) < 1 ? 1 : ((16 / W) > 8 ? 8 : 16 / W);
-  __shared__ int ok_s;
   __shared__ float red[32];
   const int64_t shard = len / W;
   const int64_t s0 = lo + rank * shard;
-  if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) {
-      // the send buffer of this bucket was written by the previous kernel on
-      // this stream; make it visible system-wide, then tell every peer.
-      __threadfence_system();
-      for (int i = 0; i < W; ++i)
-        st_release_sys(reinterpret_cast<int*>(peer_pads[i]) + PAD_READY + bucket * PAD_MAXW + rank, epoch);
-    }
-    ok_s = wait_flags(my_pad + PAD_READY + bucket * PAD_MAXW, W, 1, epoch, status, wait_ns) ? 1 : 0;
-  }
-  __syncthreads();
+  const int ok_s = (status == nullptr || *reinterpret_cast<const volatile int*>(status) == 0) ? 1 : 0;
   float ss = 0.f;
   if (ok_s) {
     const uint4* src[W];
@@ -446,12 +447,12 @@ void launch_rs_bucket(int mode, const float* grad, const uint64_t* peers_buf, vo
   if (mode == 0) {
     // pull: local cast into the send buffer, then the owner sums the W slices of its shard
     launch_grad_to_bf16(grad + lo, reinterpret_cast<__nv_bfloat16*>(my_buf) + lo, len, st);
+    rs_flags_kernel<<<1, 32, 0, st>>>(peer_pads, my_pad, rank, W, bucket, epoch, status, (uint64_t)wait_ns);
     const int g = (int)std::max<int64_t>(1, std::min<int64_t>((len / W / 8 + 511) / 512, (int64_t)ctas));
     switch (W) {
 #define OXI_RS(N)                                                                                                \
   case N:                                                                                                        \
-    rs_pull_kernel<N><<<g, 512, 0, st>>>(peers_buf, peer_pads, my_pad, rank, bucket, epoch, lo, len, rgrad, sumsq, \
-                                         status, (uint64_t)wait_ns);                                             \
+    rs_pull_kernel<N><<<g, 512, 0, st>>>(peers_buf, rank, lo, len, rgrad, sumsq, status);                        \
     break;
       OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)
 #undef OXI_RS

@@ -189,9 +189,9 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(
     const int64_t* __restrict__ topi, const float* __restrict__ topw, const int* __restrict__ pos, int64_t T, int k,
     int H, int El, const uint64_t* __restrict__ peers_yout, const __nv_bfloat16* __restrict__ resid,
     __nv_bfloat16* __restrict__ y, const int* my_pad, int W, int seq, int* status, uint64_t wait_ns) {
-  __shared__ int ok_s;
-  if (threadIdx.x == 0) ok_s = ep_wait_all(my_pad, EP_K_YREADY, W, seq, status, wait_ns) ? 1 : 0;
-  __syncthreads();
+  // the wait for every owner's expert outputs ran in ep_wait_kernel just before
+  // this launch (one thread spins, not the whole grid)
+  const int ok_s = (status == nullptr || *reinterpret_cast<const volatile int*>(status) == 0) ? 1 : 0;
   const int lane = threadIdx.x & 31;
   const int nvec = H / 8;
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T;
@@ -317,9 +317,8 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(
     const int64_t* __restrict__ topi, const int* __restrict__ pos, int64_t T, int k, int H, int El,
     const uint64_t* __restrict__ peers_dx, const uint64_t* __restrict__ peers_dwrow, __nv_bfloat16* __restrict__ dx,
     float* __restrict__ dw, const int* my_pad, int W, int seq, int* status, uint64_t wait_ns) {
-  __shared__ int ok_s;
-  if (threadIdx.x == 0) ok_s = ep_wait_all(my_pad, EP_K_DXREADY, W, seq, status, wait_ns) ? 1 : 0;
-  __syncthreads();
+  // the wait for every owner's input gradients ran in ep_wait_kernel just before this launch
+  const int ok_s = (status == nullptr || *reinterpret_cast<const volatile int*>(status) == 0) ? 1 : 0;
   const int lane = threadIdx.x & 31;
   const int nvec = H / 8;
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T;
@@ -414,6 +413,7 @@ void launch_ep_combine(const int64_t* topi, const float* topw, const int* pos, i
                        const uint64_t* peers_yout, const void* resid, void* y, const int* my_pad, int W, int seq,
                        int* status, int64_t wait_ns, cudaStream_t st) {
   OXI_CHECK(k >= 1 && k <= 16 && H % 8 == 0, "combine: k <= 16, H % 8 == 0");
+  ep_wait_kernel<<<1, 32, 0, st>>>(my_pad, EP_K_YREADY, W, seq, status, (uint64_t)wait_ns);
   const auto* r = reinterpret_cast<const __nv_bfloat16*>(resid);
   auto* yy = reinterpret_cast<__nv_bfloat16*>(y);
   if (k <= 4)
@@ -448,6 +448,7 @@ void launch_ep_gather(const int64_t* topi, const int* pos, int64_t T, int k, int
                       const uint64_t* peers_dwrow, void* dx, float* dw, const int* my_pad, int W, int seq, int* status,
                       int64_t wait_ns, cudaStream_t st) {
   OXI_CHECK(k >= 1 && k <= 16 && H % 8 == 0, "gather: k <= 16, H % 8 == 0");
+  ep_wait_kernel<<<1, 32, 0, st>>>(my_pad, EP_K_DXREADY, W, seq, status, (uint64_t)wait_ns);
   auto* d = reinterpret_cast<__nv_bfloat16*>(dx);
   if (k <= 4)
     ep_gather_kernel<4><<<warp_grid(T), 256, 0, st>>>(topi, pos, T, k, H, El, peers_dx, peers_dwrow, d, dw, my_pad, W,

@@ -29,3 +29,36 @@ void launch_mamba1_bwd(const float* u, const float* delta, const float* A, const
                        const float* hs, const float* dy, float* du, float* ddelta, float* dA, float* dB, float* dC,
                        int B, int S, int D, float clamp, cudaStream_t st);
 }  // namespace oxi
+
+namespace oxi {
+// Tensor-core chunked SSD (ssd.cu), single-term recurrence
+//   H_t = exp(loga_t) H_{t-1} + gamma_t B_t x_t^T,  y_t = H_t^T C_t,
+// N = 128, P % 64 == 0, S % 128 == 0.  x: bf16 [B*S, >= H*P] (row stride ldx);
+// B/C: bf16 [B*S, >= G*N] (head h uses group h / (H/G)); loga/gamma f32
+// [B, S, H].  fwd: y f32 [B*S, H*P], hs bf16 [B*H*(S/128)*N, P] chunk-start
+// states.  bwd: dy bf16 [B*S, H*P], dhs bf16 (scratch like hs); dx f32 [B*S,
+// H*P]; dB/dC f32 [B*S, H*N] and dgamma f32 [B, S, H] accumulated (zero them).
+struct SsdTcIO {
+  int B, S, H, P, N, G;
+  const void* x;
+  int64_t ldx;
+  const void* Bm;
+  int64_t ldb;
+  const void* Cm;
+  int64_t ldc;
+  const float* loga;
+  const float* gamma;
+  float* y;
+  void* hs;
+  const void* dy;
+  void* dhs;
+  float* dx;
+  float* dB;
+  float* dC;
+  float* dgamma;
+  int* status;
+};
+bool ssd_tc_supported(int N, int P, int S);
+void launch_ssd_fwd(const SsdTcIO& io, cudaStream_t st);
+void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st);
+}  // namespace oxi

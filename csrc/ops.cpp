@@ -486,6 +486,71 @@ void p2p_bulk(bool write, int64_t peer, int64_t bytes, int64_t ctas, int64_t chu
                        status_ptr(status), stream());
 }
 
+// ------------------------------------------------------------ tensor-core SSD
+namespace {
+void ssd_check(const torch::Tensor& t, int64_t rows, int64_t cols, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.dim() == 2 && t.stride(1) == 1 &&
+                  t.size(0) == rows && t.size(1) >= cols, what, ": bf16 [rows, >= cols] with unit inner stride");
+}
+}  // namespace
+
+bool ssd_tc_supported(int64_t N, int64_t P, int64_t S) { return oxi::ssd_tc_supported((int)N, (int)P, (int)S); }
+
+std::vector<torch::Tensor> ssd_tc_fwd(torch::Tensor x, torch::Tensor Bm, torch::Tensor Cm, torch::Tensor loga,
+                                      torch::Tensor gamma, int64_t B, int64_t S, int64_t H, int64_t P, int64_t G,
+                                      torch::Tensor status) {
+  c10::cuda::CUDAGuard g(x.device());
+  ssd_check(x, B * S, H * P, "x");
+  ssd_check(Bm, B * S, G * 128, "B");
+  ssd_check(Cm, B * S, G * 128, "C");
+  TORCH_CHECK(loga.scalar_type() == torch::kFloat32 && loga.is_contiguous() && loga.numel() == B * S * H &&
+                  gamma.scalar_type() == torch::kFloat32 && gamma.is_contiguous() && gamma.numel() == B * S * H,
+              "loga / gamma: f32 contiguous [B, S, H]");
+  const int64_t nc = S / 128;
+  auto y = torch::empty({B * S, H * P}, x.options().dtype(torch::kFloat32));
+  auto hs = torch::empty({B * H * nc * 128, P}, x.options());
+  oxi::SsdTcIO io{};
+  io.B = (int)B; io.S = (int)S; io.H = (int)H; io.P = (int)P; io.N = 128; io.G = (int)G;
+  io.x = x.data_ptr(); io.ldx = x.stride(0);
+  io.Bm = Bm.data_ptr(); io.ldb = Bm.stride(0);
+  io.Cm = Cm.data_ptr(); io.ldc = Cm.stride(0);
+  io.loga = loga.data_ptr<float>(); io.gamma = gamma.data_ptr<float>();
+  io.y = y.data_ptr<float>(); io.hs = hs.data_ptr();
+  io.status = status_ptr(status);
+  oxi::launch_ssd_fwd(io, stream());
+  return {y, hs};
+}
+
+std::vector<torch::Tensor> ssd_tc_bwd(torch::Tensor x, torch::Tensor Bm, torch::Tensor Cm, torch::Tensor loga,
+                                      torch::Tensor gamma, torch::Tensor hs, torch::Tensor dy, int64_t B, int64_t S,
+                                      int64_t H, int64_t P, int64_t G, torch::Tensor status) {
+  c10::cuda::CUDAGuard g(x.device());
+  ssd_check(x, B * S, H * P, "x");
+  ssd_check(Bm, B * S, G * 128, "B");
+  ssd_check(Cm, B * S, G * 128, "C");
+  TORCH_CHECK(dy.scalar_type() == torch::kBFloat16 && dy.is_contiguous() && dy.numel() == B * S * H * P,
+              "dy: bf16 contiguous [B*S, H*P]");
+  TORCH_CHECK(hs.is_contiguous() && hs.scalar_type() == torch::kBFloat16, "hs");
+  auto f32 = x.options().dtype(torch::kFloat32);
+  auto dx = torch::empty({B * S, H * P}, f32);
+  auto dB = torch::zeros({B * S, H * 128}, f32);
+  auto dC = torch::zeros({B * S, H * 128}, f32);
+  auto dg = torch::zeros({B, S, H}, f32);
+  auto dhs = torch::empty_like(hs);
+  oxi::SsdTcIO io{};
+  io.B = (int)B; io.S = (int)S; io.H = (int)H; io.P = (int)P; io.N = 128; io.G = (int)G;
+  io.x = x.data_ptr(); io.ldx = x.stride(0);
+  io.Bm = Bm.data_ptr(); io.ldb = Bm.stride(0);
+  io.Cm = Cm.data_ptr(); io.ldc = Cm.stride(0);
+  io.loga = loga.data_ptr<float>(); io.gamma = gamma.data_ptr<float>();
+  io.hs = hs.data_ptr(); io.dy = dy.data_ptr(); io.dhs = dhs.data_ptr();
+  io.dx = dx.data_ptr<float>(); io.dB = dB.data_ptr<float>(); io.dC = dC.data_ptr<float>();
+  io.dgamma = dg.data_ptr<float>();
+  io.status = status_ptr(status);
+  oxi::launch_ssd_bwd(io, stream());
+  return {dx, dB, dC, dg};
+}
+
 // ------------------------------------------------------------ SSM
 void conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias, torch::Tensor y, int64_t B,
                 int64_t S, bool act) {
@@ -748,6 +813,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_supported", &flash_supported, "whether a flash kernel exists for head dims (qk, v)");
   m.def("conv1d_fwd", &conv1d_fwd, "depthwise causal conv1d (+bias, +SiLU) forward");
   m.def("conv1d_bwd", &conv1d_bwd, "depthwise causal conv1d backward");
+  m.def("ssd_tc_supported", &ssd_tc_supported, "whether the tensor-core SSD handles (N, P, S)");
+  m.def("ssd_tc_fwd", &ssd_tc_fwd, "tensor-core chunked SSD forward");
+  m.def("ssd_tc_bwd", &ssd_tc_bwd, "tensor-core chunked SSD backward");
   m.def("ssm_scan_fwd", &ssm_scan_fwd, "Mamba2/3 selective scan forward");
   m.def("ssm_scan_bwd", &ssm_scan_bwd, "Mamba2/3 selective scan backward");
   m.def("mamba1_scan_fwd", &mamba1_scan_fwd, "Mamba1 selective scan forward (saves states)");

@@ -1,0 +1,808 @@
+// Chunked state-space scan (Mamba2 SSD form) on the tensor cores, sm_100a.
+//
+// Per batch b and head h the recurrence (state H is N x P, N = 128):
+//   H_t = exp(a_t) H_{t-1} + g_t B_t x_t^T ,   y_t = H_t^T C_t
+// (mamba2.rs:381-482; Mamba3's two-term update is run as this recurrence on an
+// interleaved sequence of twice the length, see ops/ssd_tc.py).  With chunks of
+// L = 128 steps and Lam_t = sum_{u<=t} a_u inside a chunk:
+//   M[t,s]  = (C_t . B_s) exp(Lam_t - Lam_s) g_s   (s <= t)
+//   Y       = M X + diag(exp Lam) C H_prev
+//   H_end   = exp(Lam_L) H_prev + B^T diag(w) X,   w_s = exp(Lam_L - Lam_s) g_s
+// Every product is a tcgen05.mma (bf16 in, f32 accumulate in TMEM); operands
+// come from 128B-swizzled shared memory tiles that TMA loads (x, B, C, dy,
+// stored states) or that the math warps write (M, scaled x / dy, bf16 state).
+// A CTA owns (b, h, 64 columns of P); its state stays in TMEM across chunks.
+//
+// Backward, pass 1 (reverse over chunks, per (b, h, p-block)), dH = adjoint of
+// H_end:   dX = M^T dY + diag(w) B dH ;  dH_prev = exp(Lam_L) dH + C^T diag(exp Lam) dY
+//          dg_s += exp(Lam_L - Lam_s) <x_s, (B dH)_s>
+//          (stores every chunk's dH, bf16, for pass 2)
+// Backward, pass 2 (chunk-parallel): dM = dY X^T, dS = dM o D o g,
+//          dC = dS B + diag(exp Lam) dY H_prev^T ,  dB = dS^T C + diag(w) X dH^T
+//          dg_s += sum_t dM[t,s] S[t,s] D[t,s]
+// (partial sums over p-blocks are added with f32 atomics).  d(a_t) follows
+// outside from <dy, y> and dg (see ops/ssd_tc.py).
+//
+// Warps: 0 TMA, 1 MMA + TMEM owner, 2..5 math (thread m <-> TMEM lane m).
+// Every TMA load fills this CTA's shared memory only; every wait is bounded.
+#include <algorithm>
+#include <cudaTypedefs.h>
+
+#include "gemm_kernel.cuh"
+#include "kernels_ssm.h"
+
+namespace oxi {
+namespace {
+
+constexpr int SL = 128;         // chunk length
+constexpr int SN = 128;         // state size
+constexpr int SP = 64;          // P columns per CTA
+constexpr int T_NN = SL * SN * 2;   // 32 KB: [128 rows][128] bf16 (two 64-col blocks)
+constexpr int T_NP = SL * SP * 2;   // 16 KB: [128 rows][64] bf16
+constexpr int SSD_THREADS = 192;
+
+__device__ __forceinline__ uint64_t kdesc(uint32_t base, int kk) {  // K-major, 64-col blocks of 16 KB
+  return umma_desc_sw128(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t mdesc(uint32_t base, int kk) {  // MN-major, K rows of 128 B
+  return umma_desc_sw128(base + kk * 2048, 16384, 1024);
+}
+
+struct SsdParams {
+  int B, S, H, P, G;          // G: groups of B/C (head h uses group h / (H / G))
+  int nc;                     // chunks per sequence
+  const float* loga;          // [B, S, H]
+  const float* gamma;         // [B, S, H]
+  float* y;                   // [B*S, H*P] f32 (fwd)
+  __nv_bfloat16* hs;          // [B*H*nc*N, P] chunk-start states (fwd writes, bwd reads via TMA)
+  __nv_bfloat16* dhs;         // [B*H*nc*N, P] chunk-end adjoints (bwd pass 1 writes)
+  float* dx;                  // [B*S, H*P] f32
+  float* dB;                  // [B*S, H*N] f32 (atomics)
+  float* dC;                  // [B*S, H*N] f32 (atomics)
+  float* dgamma;              // [B, S, H] f32 (atomics)
+  int* status;
+};
+
+// 128 math threads: inclusive cumsum of a over the chunk (thread m holds a_m).
+__device__ __forceinline__ float chunk_cumsum(float a, int m, float* s_part) {
+  const int lane = m & 31, q = m >> 5;
+  float v = a;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  if (lane == 31) s_part[q] = v;
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  float off = 0.f;
+  for (int i = 0; i < q; ++i) off += s_part[i];
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  return v + off;
+}
+__device__ __forceinline__ void math_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// row m of a [128][64] bf16 SW128 tile -> 64 floats
+__device__ __forceinline__ void load_row64(const uint8_t* tile, int m, float* out) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(tile + m * 128 + (((c ^ (m & 7)) & 7) << 4));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16(w[i]);
+      out[c * 8 + 2 * i] = f.x;
+      out[c * 8 + 2 * i + 1] = f.y;
+    }
+  }
+}
+__device__ __forceinline__ void store_row64(uint8_t* tile, int m, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    sw128_store16(tile, m, c,
+                  make_uint4(pack_bf16(v[c * 8], v[c * 8 + 1]), pack_bf16(v[c * 8 + 2], v[c * 8 + 3]),
+                             pack_bf16(v[c * 8 + 4], v[c * 8 + 5]), pack_bf16(v[c * 8 + 6], v[c * 8 + 7])));
+}
+// TMEM row (lane base + 64 columns from col0) -> 64 floats
+__device__ __forceinline__ void tmem_row64(uint32_t addr, float* out) {
+  uint32_t r0[32], r1[32];
+  tmem_ld32(addr, r0);
+  tmem_ld32(addr + 32, r1);
+  tc_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    out[i] = __uint_as_float(r0[i]);
+    out[32 + i] = __uint_as_float(r1[i]);
+  }
+}
+
+// =================================================================== forward
+struct FwdSmem {
+  static constexpr int OFF_C = 0;
+  static constexpr int OFF_B = OFF_C + T_NN;
+  static constexpr int OFF_X = OFF_B + T_NN;
+  static constexpr int OFF_P = OFF_X + T_NP;
+  static constexpr int OFF_H = OFF_P + T_NN;
+  static constexpr int OFF_W = OFF_H + T_NP;
+  static constexpr int OFF_VEC = OFF_W + T_NP;      // lam[128], gam[128], part[8]
+  static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4 + 64;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(SSD_THREADS, 1)
+    ssd_fwd_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, SsdParams p) {
+  using L = FwdSmem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sX = smem + L::OFF_X, *sP = smem + L::OFF_P,
+          *sH = smem + L::OFF_H, *sW = smem + L::OFF_W;
+  float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
+  float* s_gam = s_lam + 128;
+  float* s_part = s_gam + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t *ld_full = bars + 0, *s_full = bars + 1, *p_full = bars + 2, *y_full = bars + 3, *w_full = bars + 4,
+           *h_full = bars + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int bh = blockIdx.x, pb = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int g = h / (p.H / p.G);
+  const int row0 = b * p.S;
+  if (threadIdx.x == 0) {
+    mbar_init(ld_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(y_full, 1);
+    mbar_init(w_full, 4);
+    mbar_init(h_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_S = tmem, TM_YD = tmem + 128, TM_YO = tmem + 192, TM_H = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int c = 0; c < p.nc; ++c) {
+        if (c > 0 && !mbar_wait(h_full, (c - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(ld_full, 2 * T_NN + T_NP);
+        const int r = row0 + c * SL;
+        tma_load_2d(sC, &tmC, ld_full, g * SN, r);
+        tma_load_2d(sC + 16384, &tmC, ld_full, g * SN + 64, r);
+        tma_load_2d(sB, &tmB, ld_full, g * SN, r);
+        tma_load_2d(sB + 16384, &tmB, ld_full, g * SN + 64, r);
+        tma_load_2d(sX, &tmX, ld_full, h * p.P + pb * SP, r);
+      }
+      if (p.nc > 0) mbar_wait(ld_full, (p.nc - 1) & 1, nullptr, p.status);  // no copy in flight at exit
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t ID_Y = umma_idesc_bf16(128, 64, false, true);
+      constexpr uint32_t ID_H = umma_idesc_bf16(128, 64, true, true);
+      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aX = smem_u32(sX), aP = smem_u32(sP),
+                     aH = smem_u32(sH), aW = smem_u32(sW);
+      for (int c = 0; c < p.nc; ++c) {
+        if (!mbar_wait(ld_full, c & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aB, kk), ID_S, kk != 0);
+        tc_commit(s_full);
+        if (!mbar_wait(p_full, c & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_YD, kdesc(aP, kk), mdesc(aX, kk), ID_Y, kk != 0);
+        if (c > 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_YO, kdesc(aC, kk), mdesc(aH, kk), ID_Y, kk != 0);
+        }
+        tc_commit(y_full);
+        if (!mbar_wait(w_full, c & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_H, mdesc(aB, kk), mdesc(aW, kk), ID_H, (c > 0 || kk > 0));
+        tc_commit(h_full);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int m = (warp & 3) * 32 + lane;  // chunk row t (S, Y) / state row n (H)
+    const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
+    bool ok = true;
+    for (int c = 0; c < p.nc && ok; ++c) {
+      const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
+      const float lam = chunk_cumsum(p.loga[si], m, s_part);
+      const float gm = p.gamma[si];
+      s_lam[m] = lam;
+      s_gam[m] = gm;
+      math_bar();
+      const float lam_end = s_lam[SL - 1];
+      // previous chunk's state -> bf16 B operand (and the backward's copy), then decay it
+      if (c > 0) {
+        if (!mbar_wait(h_full, (c - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        float hv[64];
+        tmem_row64(TM_H + lb, hv);
+        store_row64(sH, m, hv);
+        __nv_bfloat16* hs = p.hs + (((int64_t)bh * p.nc + c) * SN + m) * p.P + pb * SP;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<uint4*>(hs)[q] =
+              make_uint4(pack_bf16(hv[q * 8], hv[q * 8 + 1]), pack_bf16(hv[q * 8 + 2], hv[q * 8 + 3]),
+                         pack_bf16(hv[q * 8 + 4], hv[q * 8 + 5]), pack_bf16(hv[q * 8 + 6], hv[q * 8 + 7]));
+        const float dec = __expf(lam_end);
+        uint32_t u0[32], u1[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          u0[i] = __float_as_uint(hv[i] * dec);
+          u1[i] = __float_as_uint(hv[32 + i] * dec);
+        }
+        tmem_st32(TM_H + lb, u0);
+        tmem_st32(TM_H + lb + 32, u1);
+        tc_wait_st();
+      } else {
+        // chunk 0 starts from a zero state; keep the stored copy consistent
+        __nv_bfloat16* hs = p.hs + (((int64_t)bh * p.nc + 0) * SN + m) * p.P + pb * SP;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(hs)[q] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      // M = (C B^T) o decay o g  -> sP (bf16, K-major over s)
+      if (!mbar_wait(s_full, c & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        uint32_t sr[32];
+        tmem_ld32(TM_S + lb + q * 32, sr);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          float v[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int s = q * 32 + t + e;
+            v[e] = (s <= m) ? __uint_as_float(sr[t + e]) * __expf(lam - s_lam[s]) * s_gam[s] : 0.f;
+          }
+          pk[t / 2] = pack_bf16(v[0], v[1]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int ch = q * 4 + j;  // 8-column chunk 0..15
+          sw128_store16(sP + (ch >> 3) * 16384, m, ch & 7, make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]));
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // W = diag(w) X, w_s = exp(lam_end - lam_s) g_s (row s = m); sW is free once
+      // the previous chunk's state MMA completed (waited above for c > 0)
+      {
+        float xv[64];
+        load_row64(sX, m, xv);
+        const float w = __expf(lam_end - lam) * gm;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) xv[i] *= w;
+        store_row64(sW, m, xv);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(w_full);
+      // y = Yd + exp(lam_t) Yo
+      if (!mbar_wait(y_full, c & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      float yd[64];
+      tmem_row64(TM_YD + lb, yd);
+      if (c > 0) {
+        float yo[64];
+        tmem_row64(TM_YO + lb, yo);
+        const float e = __expf(lam);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) yd[i] += e * yo[i];
+      }
+      float* yr = p.y + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        reinterpret_cast<float4*>(yr)[i] = make_float4(yd[4 * i], yd[4 * i + 1], yd[4 * i + 2], yd[4 * i + 3]);
+      tc_fence_before();
+    }
+    // the last state MMA must finish before TMEM is released
+    if (ok && p.nc > 0) mbar_wait(h_full, (p.nc - 1) & 1, abort_flag, p.status);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ====================================================== backward, pass 1
+struct Bwd1Smem {
+  static constexpr int OFF_C = 0;
+  static constexpr int OFF_B = OFF_C + T_NN;
+  static constexpr int OFF_X = OFF_B + T_NN;
+  static constexpr int OFF_DY = OFF_X + T_NP;
+  static constexpr int OFF_P = OFF_DY + T_NP;
+  static constexpr int OFF_E = OFF_P + T_NN;
+  static constexpr int OFF_DH = OFF_E + T_NP;
+  static constexpr int OFF_VEC = OFF_DH + T_NP;
+  static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4 + 64;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(SSD_THREADS, 1)
+    ssd_bwd1_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmDY, SsdParams p) {
+  using L = Bwd1Smem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sX = smem + L::OFF_X, *sDY = smem + L::OFF_DY,
+          *sP = smem + L::OFF_P, *sE = smem + L::OFF_E, *sDH = smem + L::OFF_DH;
+  float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
+  float* s_gam = s_lam + 128;
+  float* s_part = s_gam + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t *ld_full = bars + 0, *s_full = bars + 1, *p_full = bars + 2, *m_full = bars + 3, *t_free = bars + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int bh = blockIdx.x, pb = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int g = h / (p.H / p.G);
+  const int row0 = b * p.S;
+  if (threadIdx.x == 0) {
+    mbar_init(ld_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(m_full, 1);
+    mbar_init(t_free, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_S = tmem, TM_DX = tmem + 128, TM_BDH = tmem + 192, TM_DH = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < p.nc; ++i) {
+        const int c = p.nc - 1 - i;
+        if (i > 0 && !mbar_wait(t_free, (i - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(ld_full, 2 * T_NN + 2 * T_NP);
+        const int r = row0 + c * SL;
+        tma_load_2d(sC, &tmC, ld_full, g * SN, r);
+        tma_load_2d(sC + 16384, &tmC, ld_full, g * SN + 64, r);
+        tma_load_2d(sB, &tmB, ld_full, g * SN, r);
+        tma_load_2d(sB + 16384, &tmB, ld_full, g * SN + 64, r);
+        tma_load_2d(sX, &tmX, ld_full, h * p.P + pb * SP, r);
+        tma_load_2d(sDY, &tmDY, ld_full, h * p.P + pb * SP, r);
+      }
+      if (p.nc > 0) mbar_wait(ld_full, (p.nc - 1) & 1, nullptr, p.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t ID_DX = umma_idesc_bf16(128, 64, true, true);
+      constexpr uint32_t ID_BDH = umma_idesc_bf16(128, 64, false, true);
+      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aDY = smem_u32(sDY), aP = smem_u32(sP),
+                     aE = smem_u32(sE), aDH = smem_u32(sDH);
+      for (int i = 0; i < p.nc; ++i) {
+        if (!mbar_wait(ld_full, i & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aB, kk), ID_S, kk != 0);
+        tc_commit(s_full);
+        if (!mbar_wait(p_full, i & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DX, mdesc(aP, kk), mdesc(aDY, kk), ID_DX, kk != 0);
+        if (i > 0) {  // dH of the last chunk is zero
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_BDH, kdesc(aB, kk), mdesc(aDH, kk), ID_BDH, kk != 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DH, mdesc(aC, kk), mdesc(aE, kk), ID_DX, (i > 0 || kk > 0));
+        tc_commit(m_full);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int m = (warp & 3) * 32 + lane;
+    const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < p.nc && ok; ++i) {
+      const int c = p.nc - 1 - i;
+      const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
+      const float lam = chunk_cumsum(p.loga[si], m, s_part);
+      const float gm = p.gamma[si];
+      s_lam[m] = lam;
+      s_gam[m] = gm;
+      math_bar();
+      const float lam_end = s_lam[SL - 1];
+      if (!mbar_wait(ld_full, i & 1, abort_flag, p.status)) { ok = false; break; }
+      // dH (adjoint of this chunk's end state) -> bf16 operand + stored copy, then decay it
+      if (i > 0) {
+        float hv[64];
+        tmem_row64(TM_DH + lb, hv);
+        store_row64(sDH, m, hv);
+        __nv_bfloat16* dst = p.dhs + (((int64_t)bh * p.nc + c) * SN + m) * p.P + pb * SP;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<uint4*>(dst)[q] =
+              make_uint4(pack_bf16(hv[q * 8], hv[q * 8 + 1]), pack_bf16(hv[q * 8 + 2], hv[q * 8 + 3]),
+                         pack_bf16(hv[q * 8 + 4], hv[q * 8 + 5]), pack_bf16(hv[q * 8 + 6], hv[q * 8 + 7]));
+        const float dec = __expf(lam_end);
+        uint32_t u0[32], u1[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          u0[k] = __float_as_uint(hv[k] * dec);
+          u1[k] = __float_as_uint(hv[32 + k] * dec);
+        }
+        tmem_st32(TM_DH + lb, u0);
+        tmem_st32(TM_DH + lb + 32, u1);
+        tc_wait_st();
+      } else {
+        __nv_bfloat16* dst = p.dhs + (((int64_t)bh * p.nc + c) * SN + m) * p.P + pb * SP;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(dst)[q] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      // E = diag(exp lam) dY (row t = m)
+      {
+        float dv[64];
+        load_row64(sDY, m, dv);
+        const float e = __expf(lam);
+#pragma unroll
+        for (int k = 0; k < 64; ++k) dv[k] *= e;
+        store_row64(sE, m, dv);
+      }
+      // M = (C B^T) o decay o g -> sP
+      if (!mbar_wait(s_full, i & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        uint32_t sr[32];
+        tmem_ld32(TM_S + lb + q * 32, sr);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          float v[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int s = q * 32 + t + e;
+            v[e] = (s <= m) ? __uint_as_float(sr[t + e]) * __expf(lam - s_lam[s]) * s_gam[s] : 0.f;
+          }
+          pk[t / 2] = pack_bf16(v[0], v[1]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int ch = q * 4 + j;
+          sw128_store16(sP + (ch >> 3) * 16384, m, ch & 7, make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]));
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // dx (row s = m) = dX + w_s (B dH)_s ;  dg_s += exp(lam_end - lam_s) <x_s, (B dH)_s>
+      if (!mbar_wait(m_full, i & 1, abort_flag, p.status)) { ok = false; break; }
+      tc_fence_after();
+      float dxv[64];
+      tmem_row64(TM_DX + lb, dxv);
+      if (i > 0) {
+        float bd[64], xv[64];
+        tmem_row64(TM_BDH + lb, bd);
+        load_row64(sX, m, xv);
+        const float dec = __expf(lam_end - lam);
+        const float w = dec * gm;
+        float dot = 0.f;
+#pragma unroll
+        for (int k = 0; k < 64; ++k) {
+          dxv[k] += w * bd[k];
+          dot += xv[k] * bd[k];
+        }
+        atomicAdd(p.dgamma + si, dec * dot);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(t_free);  // tiles (x, dy, B, C) may be reloaded
+      float* dr = p.dx + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        reinterpret_cast<float4*>(dr)[k] = make_float4(dxv[4 * k], dxv[4 * k + 1], dxv[4 * k + 2], dxv[4 * k + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ====================================================== backward, pass 2
+struct Bwd2Smem {
+  static constexpr int OFF_C = 0;
+  static constexpr int OFF_B = OFF_C + T_NN;
+  static constexpr int OFF_X = OFF_B + T_NN;
+  static constexpr int OFF_DY = OFF_X + T_NP;
+  static constexpr int OFF_H = OFF_DY + T_NP;
+  static constexpr int OFF_DH = OFF_H + T_NP;
+  static constexpr int OFF_DS = OFF_DH + T_NP;
+  static constexpr int OFF_E = OFF_DS + T_NN;
+  static constexpr int OFF_W = OFF_E + T_NP;
+  static constexpr int OFF_VEC = OFF_W + T_NP;      // lam, gam, part, colsum[128]
+  static constexpr int OFF_BAR = OFF_VEC + 3 * 128 * 4 + 64;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(SSD_THREADS, 1)
+    ssd_bwd2_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmDY,
+                    const __grid_constant__ CUtensorMap tmHS, const __grid_constant__ CUtensorMap tmDHS, SsdParams p) {
+  using L = Bwd2Smem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sX = smem + L::OFF_X, *sDY = smem + L::OFF_DY,
+          *sH = smem + L::OFF_H, *sDH = smem + L::OFF_DH, *sDS = smem + L::OFF_DS, *sE = smem + L::OFF_E,
+          *sW = smem + L::OFF_W;
+  float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
+  float* s_gam = s_lam + 128;
+  float* s_col = s_gam + 128;
+  float* s_part = s_col + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t *ld_full = bars + 0, *s_full = bars + 1, *p_full = bars + 2, *m_full = bars + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int bh = blockIdx.x, c = blockIdx.y, pb = blockIdx.z;
+  const int b = bh / p.H, h = bh % p.H;
+  const int g = h / (p.H / p.G);
+  const int row0 = b * p.S;
+  const int r = row0 + c * SL;
+  const int hrow = (bh * p.nc + c) * SN;
+  if (threadIdx.x == 0) {
+    mbar_init(ld_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(m_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t TM_S = tmem, TM_DM = tmem + 128;  // reused: dC in TM_S, dB in TM_DM
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(ld_full, 2 * T_NN + 4 * T_NP);
+      tma_load_2d(sC, &tmC, ld_full, g * SN, r);
+      tma_load_2d(sC + 16384, &tmC, ld_full, g * SN + 64, r);
+      tma_load_2d(sB, &tmB, ld_full, g * SN, r);
+      tma_load_2d(sB + 16384, &tmB, ld_full, g * SN + 64, r);
+      tma_load_2d(sX, &tmX, ld_full, h * p.P + pb * SP, r);
+      tma_load_2d(sDY, &tmDY, ld_full, h * p.P + pb * SP, r);
+      tma_load_2d(sH, &tmHS, ld_full, pb * SP, hrow);
+      tma_load_2d(sDH, &tmDHS, ld_full, pb * SP, hrow);
+      mbar_wait(ld_full, 0, nullptr, p.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_SS = umma_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t ID_DC1 = umma_idesc_bf16(128, 128, false, true);
+      constexpr uint32_t ID_DB1 = umma_idesc_bf16(128, 128, true, true);
+      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aX = smem_u32(sX), aDY = smem_u32(sDY),
+                     aH = smem_u32(sH), aDH = smem_u32(sDH), aDS = smem_u32(sDS), aE = smem_u32(sE),
+                     aW = smem_u32(sW);
+      bool ok = mbar_wait(ld_full, 0, abort_flag, p.status);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aB, kk), ID_SS, kk != 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_DM, kdesc(aDY, kk), kdesc(aX, kk), ID_SS, kk != 0);
+        tc_commit(s_full);
+        ok = mbar_wait(p_full, 0, abort_flag, p.status);
+      }
+      if (ok) {
+        tc_fence_after();
+        // dC = dS B + E H^T   (into the S columns)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aDS, kk), mdesc(aB, kk), ID_DC1, kk != 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_S, kdesc(aE, kk), kdesc(aH, kk), ID_SS, 1u);
+        // dB = dS^T C + W dH^T   (into the dM columns)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DM, mdesc(aDS, kk), mdesc(aC, kk), ID_DB1, kk != 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_DM, kdesc(aW, kk), kdesc(aDH, kk), ID_SS, 1u);
+        tc_commit(m_full);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int m = (warp & 3) * 32 + lane;
+    const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
+    const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
+    const float lam = chunk_cumsum(p.loga[si], m, s_part);
+    const float gm = p.gamma[si];
+    s_lam[m] = lam;
+    s_gam[m] = gm;
+    s_col[m] = 0.f;
+    math_bar();
+    const float lam_end = s_lam[SL - 1];
+    bool ok = mbar_wait(ld_full, 0, abort_flag, p.status);
+    if (ok) {
+      // E = diag(exp lam) dY ; W = diag(w) X   (row m)
+      float v[64];
+      load_row64(sDY, m, v);
+      const float e = __expf(lam);
+#pragma unroll
+      for (int k = 0; k < 64; ++k) v[k] *= e;
+      store_row64(sE, m, v);
+      load_row64(sX, m, v);
+      const float w = __expf(lam_end - lam) * gm;
+#pragma unroll
+      for (int k = 0; k < 64; ++k) v[k] *= w;
+      store_row64(sW, m, v);
+      ok = mbar_wait(s_full, 0, abort_flag, p.status);
+    }
+    if (ok) {
+      tc_fence_after();
+      // dS = dM o decay o g (row t = m);  column sums of dM o S o decay -> dg
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32(TM_S + lb + q * 32, sr);
+        tmem_ld32(TM_DM + lb + q * 32, dr);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          float v[2];
+#pragma unroll
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int s = q * 32 + t + e2;
+            const float d = (s <= m) ? __expf(lam - s_lam[s]) : 0.f;
+            const float dm = __uint_as_float(dr[t + e2]) * d;
+            v[e2] = dm * s_gam[s];
+            float cs = dm * __uint_as_float(sr[t + e2]);
+            // reduce over the 32 rows of this warp before touching shared memory
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+            if (lane == 0) atomicAdd(&s_col[s], cs);
+          }
+          pk[t / 2] = pack_bf16(v[0], v[1]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int ch = q * 4 + j;
+          sw128_store16(sDS + (ch >> 3) * 16384, m, ch & 7, make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]));
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      math_bar();
+      atomicAdd(p.dgamma + si, s_col[m]);
+      ok = mbar_wait(m_full, 0, abort_flag, p.status);
+    }
+    if (ok) {
+      tc_fence_after();
+      // row m: dC_t (t = m) and dB_s (s = m), 128 values each
+      float* dcr = p.dC + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
+      float* dbr = p.dB + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float v[64];
+        tmem_row64(TM_S + lb + half * 64, v);
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          atomicAdd(reinterpret_cast<float4*>(dcr + half * 64) + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+        tmem_row64(TM_DM + lb + half * 64, v);
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          atomicAdd(reinterpret_cast<float4*>(dbr + half * 64) + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+template <typename K>
+void set_smem(K kern, int bytes) {
+  OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+}
+
+}  // namespace
+
+bool ssd_tc_supported(int N, int P, int S) { return N == SN && P % SP == 0 && S % SL == 0 && S > 0; }
+
+void launch_ssd_fwd(const SsdTcIO& io, cudaStream_t st) {
+  OXI_CHECK(ssd_tc_supported(io.N, io.P, io.S), "tensor-core SSD needs N == 128, P % 64 == 0, S % 128 == 0");
+  OXI_CHECK(io.H % io.G == 0, "heads must be a multiple of the B/C groups");
+  const int64_t T = (int64_t)io.B * io.S;
+  CUtensorMap tx = make_tmap_bf16(io.x, T, (int64_t)io.H * io.P, io.ldx, 64, SL);
+  CUtensorMap tb = make_tmap_bf16(io.Bm, T, (int64_t)io.G * SN, io.ldb, 64, SL);
+  CUtensorMap tc = make_tmap_bf16(io.Cm, T, (int64_t)io.G * SN, io.ldc, 64, SL);
+  SsdParams p{};
+  p.B = io.B; p.S = io.S; p.H = io.H; p.P = io.P; p.G = io.G; p.nc = io.S / SL;
+  p.loga = io.loga; p.gamma = io.gamma; p.y = io.y;
+  p.hs = reinterpret_cast<__nv_bfloat16*>(io.hs);
+  p.status = io.status;
+  static bool attr = false;
+  if (!attr) { set_smem(ssd_fwd_kernel, FwdSmem::TOTAL); attr = true; }
+  dim3 grid(io.B * io.H, io.P / SP);
+  ssd_fwd_kernel<<<grid, SSD_THREADS, FwdSmem::TOTAL, st>>>(tx, tb, tc, p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st) {
+  OXI_CHECK(ssd_tc_supported(io.N, io.P, io.S), "tensor-core SSD needs N == 128, P % 64 == 0, S % 128 == 0");
+  const int64_t T = (int64_t)io.B * io.S;
+  const int nc = io.S / SL;
+  CUtensorMap tx = make_tmap_bf16(io.x, T, (int64_t)io.H * io.P, io.ldx, 64, SL);
+  CUtensorMap tb = make_tmap_bf16(io.Bm, T, (int64_t)io.G * SN, io.ldb, 64, SL);
+  CUtensorMap tc = make_tmap_bf16(io.Cm, T, (int64_t)io.G * SN, io.ldc, 64, SL);
+  CUtensorMap tdy = make_tmap_bf16(io.dy, T, (int64_t)io.H * io.P, (int64_t)io.H * io.P, 64, SL);
+  const int64_t hrows = (int64_t)io.B * io.H * nc * SN;
+  CUtensorMap ths = make_tmap_bf16(io.hs, hrows, io.P, io.P, 64, SN);
+  CUtensorMap tdhs = make_tmap_bf16(io.dhs, hrows, io.P, io.P, 64, SN);
+  SsdParams p{};
+  p.B = io.B; p.S = io.S; p.H = io.H; p.P = io.P; p.G = io.G; p.nc = nc;
+  p.loga = io.loga; p.gamma = io.gamma;
+  p.hs = reinterpret_cast<__nv_bfloat16*>(io.hs);
+  p.dhs = reinterpret_cast<__nv_bfloat16*>(io.dhs);
+  p.dx = io.dx; p.dB = io.dB; p.dC = io.dC; p.dgamma = io.dgamma;
+  p.status = io.status;
+  static bool attr = false;
+  if (!attr) {
+    set_smem(ssd_bwd1_kernel, Bwd1Smem::TOTAL);
+    set_smem(ssd_bwd2_kernel, Bwd2Smem::TOTAL);
+    attr = true;
+  }
+  ssd_bwd1_kernel<<<dim3(io.B * io.H, io.P / SP), SSD_THREADS, Bwd1Smem::TOTAL, st>>>(tx, tb, tc, tdy, p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+  ssd_bwd2_kernel<<<dim3(io.B * io.H, nc, io.P / SP), SSD_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs,
+                                                                                          p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace oxi

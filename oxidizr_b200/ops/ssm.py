@@ -38,6 +38,10 @@ def ssd(x, dt, A, Bm, Cm, chunk: int, diag_only_g: bool = False):
     """Mamba2 SSD core (no D skip), f32 result.  x [B,S,H,P], dt [B,S,H],
     A [H], B/C [B,S,G,N] with G dividing H (grouped B/C are shared by heads)."""
     H, N = x.shape[2], Bm.shape[-1]
+    if not diag_only_g:
+        from .ssd_tc import ssd_tc, tc_ok
+        if tc_ok(x, N, x.shape[1]):
+            return ssd_tc(x, dt, A, Bm, Cm)
     if not diag_only_g and _scan_ok(x, N):
         from .ssm_kernels import SSMScan
         dtf = dt.float()
@@ -49,6 +53,10 @@ def ssd(x, dt, A, Bm, Cm, chunk: int, diag_only_g: bool = False):
 def mamba3_scan(x, dt, A, Bm, Cm, lam, chunk: int, compat: bool = False):
     """Trapezoidal two-term scan (no D skip), f32 result.  B/C [B,S,H,N] per head."""
     N = Bm.shape[-1]
+    if not compat:
+        from .ssd_tc import mamba3_tc, tc_ok
+        if tc_ok(x, N, 2 * x.shape[1]):
+            return mamba3_tc(x, dt, A, Bm, Cm, lam)
     if not compat and _scan_ok(x, N):
         from .ssm_kernels import SSMScan
         dtf, lamf = dt.float(), lam.float()

@@ -99,3 +99,59 @@ def test_mamba1_scan(clamp):
     assert _rel(y, yr) < 1e-4
     for g, r in zip((u.grad, delta.grad, A.grad, Bm.grad, Cm.grad), [t.grad for t in ins]):
         assert _rel(g, r) < 1e-3
+
+
+def _tc_inputs(B, S, H, P, N, G, seed):
+    torch.manual_seed(seed)
+    x = torch.randn(B, S, H, P, device="cuda").bfloat16().requires_grad_()
+    dt = (torch.rand(B, S, H, device="cuda") * 0.09 + 0.01).requires_grad_()
+    A = (-torch.rand(H, device="cuda") * 2 - 0.1).requires_grad_()
+    Bg = (torch.randn(B, S, G, N, device="cuda") / N ** 0.25).bfloat16().requires_grad_()
+    Cg = (torch.randn(B, S, G, N, device="cuda") / N ** 0.25).bfloat16().requires_grad_()
+    return x, dt, A, Bg, Cg
+
+
+@pytest.mark.parametrize("B,S,H,P,G", [(2, 256, 4, 64, 1), (1, 384, 4, 128, 2), (2, 128, 2, 64, 2)])
+def test_ssd_tensor_core_mamba2(B, S, H, P, G):
+    """tcgen05 chunked SSD (bf16 operands, f32 state) vs the fp64 chunked reference."""
+    from oxidizr_b200.ops import reference as R
+    from oxidizr_b200.ops.ssd_tc import ssd_tc, tc_ok
+    from oxidizr_b200.ops._C import check_status
+    N = 128
+    x, dt, A, Bg, Cg = _tc_inputs(B, S, H, P, N, G, S + P + G)
+    assert tc_ok(x, N, S)
+    y = ssd_tc(x, dt, A, Bg, Cg)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    torch.cuda.synchronize()
+    check_status("cuda")
+    ins = [t.detach().double().requires_grad_() for t in (x, dt, A, Bg, Cg)]
+    xr, dtr, Ar, Br, Cr = ins
+    yr = R.ssd_chunked(xr, dtr, Ar, Br.repeat_interleave(H // G, 2), Cr.repeat_interleave(H // G, 2), 64)
+    yr.backward(dy.double())
+    assert _rel(y, yr) < 2e-2, _rel(y, yr)
+    for name, g, r in zip(("x", "dt", "A", "B", "C"), (x.grad, dt.grad, A.grad, Bg.grad, Cg.grad), [t.grad for t in ins]):
+        assert _rel(g, r) < 3e-2, (name, _rel(g, r))
+
+
+@pytest.mark.parametrize("B,S,H,P", [(1, 128, 2, 64), (2, 192, 2, 128)])
+def test_ssd_tensor_core_mamba3(B, S, H, P):
+    """Mamba3 two-term scan through the interleaved tensor-core SSD vs the fp64 reference."""
+    from oxidizr_b200.ops import reference as R
+    from oxidizr_b200.ops.ssd_tc import mamba3_tc
+    from oxidizr_b200.ops._C import check_status
+    N = 128
+    x, dt, A, Bm, Cm = _tc_inputs(B, S, H, P, N, H, S + P)
+    lam = torch.rand(B, S, H, device="cuda").requires_grad_()
+    y = mamba3_tc(x, dt, A, Bm, Cm, lam)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    torch.cuda.synchronize()
+    check_status("cuda")
+    ins = [t.detach().double().requires_grad_() for t in (x, dt, A, Bm, Cm, lam)]
+    yr = R.mamba3_scan(*ins, 32)
+    yr.backward(dy.double())
+    assert _rel(y, yr) < 2e-2, _rel(y, yr)
+    for name, g, r in zip(("x", "dt", "A", "B", "C", "lam"), (x.grad, dt.grad, A.grad, Bm.grad, Cm.grad, lam.grad),
+                          [t.grad for t in ins]):
+        assert _rel(g, r) < 3e-2, (name, _rel(g, r))
