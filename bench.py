@@ -309,6 +309,9 @@ def main():
         "mfu_vs_measured_sustained": round(achieved_tf / pk["bf16_tflops_sustained"], 3),
         "loss_after_timed_steps": round(loss_dev, 4),
     }
+    if ep > 1:
+        from oxidizr_b200.parallel.ep import EPLayerBuffers
+        out["ep_buffer_reallocs"] = EPLayerBuffers.reallocs
     if rank == 0:
         print(json.dumps(out), flush=True)
     if hasattr(opt, "close"):

@@ -405,14 +405,13 @@ struct FaBwdSmem {
   static constexpr int NQ = KBQ * 64;             // DQ rounded up to whole 64-column blocks
   static constexpr int TQ_BYTES = 128 * NQ * 2;   // K, Q tiles
   static constexpr int TV_BYTES = 128 * DV * 2;   // V, dO tiles
-  static constexpr int P_BYTES = 128 * 128 * 2;   // P^T, dS^T
+  static constexpr int P_BYTES = 128 * 128 * 2;   // dS^T
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TQ_BYTES;
-  static constexpr int OFF_Q = OFF_V + TV_BYTES;
-  static constexpr int OFF_DO = OFF_Q + TQ_BYTES;
-  static constexpr int OFF_PT = OFF_DO + TV_BYTES;
-  static constexpr int OFF_DST = OFF_PT + P_BYTES;
-  static constexpr int OFF_VEC = OFF_DST + P_BYTES;   // lse (log2), delta: 2 x 128 f32
+  static constexpr int OFF_Q = OFF_V + TV_BYTES;       // [2] (double-buffered)
+  static constexpr int OFF_DO = OFF_Q + 2 * TQ_BYTES;  // [2]
+  static constexpr int OFF_DST = OFF_DO + 2 * TV_BYTES;
+  static constexpr int OFF_VEC = OFF_DST + P_BYTES;   // lse (log2), delta of the current pair: 2 x 128 f32
   static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
   static_assert(TOTAL <= 232448, "shared memory budget");
@@ -423,6 +422,15 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// One CTA per (128-key tile, kv head, batch); loops over the query heads of
+// the GQA group and the query tiles i >= j.  Per (h, i):
+//   S^T = K Q_i^T, dP^T = V dO_i^T               (TMEM)
+//   P^T = exp2(S^T c - lse), dS^T = P^T (dP^T - delta) scale
+//        P^T is written back into TMEM as bf16 (the A operand of dV), dS^T to
+//        128B-swizzled shared memory (A of dK, and read MN-major, A of dQ)
+//   dV += P^T dO_i, dK += dS^T Q_i                (TMEM accumulators)
+//   dQ_i = dS K -> f32 atomics into dq_acc        (TMEM, in the dP^T columns)
+// Q_i / dO_i are double-buffered so the next pair's loads overlap this one.
 template <int DQ, int DV>
 __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -435,18 +443,18 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
   uint8_t* sV = smem + L::OFF_V;
   uint8_t* sQ = smem + L::OFF_Q;
   uint8_t* sDO = smem + L::OFF_DO;
-  uint8_t* sPt = smem + L::OFF_PT;
   uint8_t* sDSt = smem + L::OFF_DST;
   float* s_lse = reinterpret_cast<float*>(smem + L::OFF_VEC);
   float* s_delta = s_lse + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* sdp_full = bars + 2;
-  uint64_t* p_ready = bars + 3;
-  uint64_t* it_done = bars + 4;
-  uint64_t* dq_read = bars + 5;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* sdp_full = bars + 5;
+  uint64_t* p_ready = bars + 6;
+  uint64_t* it_done = bars + 7;
+  uint64_t* dq_read = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -462,7 +470,10 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qdo_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
     mbar_init(sdp_full, 1);
     mbar_init(p_ready, 8);   // one arrival per softmax warp
     mbar_init(it_done, 1);
@@ -483,7 +494,7 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t TM_DV = tmem, TM_DK = tmem + DV, TM_S = tmem + DV + NQ, TM_DP = tmem + DV + NQ + 128;
-  const uint32_t TM_DQ = TM_S;  // dQ reuses the S^T columns once they are consumed
+  const uint32_t TM_DQ = TM_DP;  // dQ reuses the dP^T columns once the softmax warps consumed them
 
   if (warp == 0) {
     if (lane == 0) {
@@ -492,34 +503,46 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       for (int kb = 0; kb < KBQ; ++kb) tma_load_2d(sK + kb * 128 * 128, &tmK, kv_full, hk * DQ + kb * 64, row0 + k0);
 #pragma unroll
       for (int kb = 0; kb < KBV; ++kb) tma_load_2d(sV + kb * 128 * 128, &tmV, kv_full, hk * DV + kb * 64, row0 + k0);
+      int issued = 0;
       for (int it = 0; it < n_it; ++it) {
         const int h = hk * group + it / n_i;
         const int i = i_start + it % n_i;
-        if (!mbar_wait(it_done, (it & 1) ^ 1, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(qdo_full, L::TQ_BYTES + L::TV_BYTES);
+        const int st = it & 1, u = it >> 1;
+        if (!mbar_wait(&qdo_empty[st], (u & 1) ^ 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], L::TQ_BYTES + L::TV_BYTES);
+        uint8_t* q = sQ + st * L::TQ_BYTES;
+        uint8_t* o = sDO + st * L::TV_BYTES;
 #pragma unroll
-        for (int kb = 0; kb < KBQ; ++kb)
-          tma_load_2d(sQ + kb * 128 * 128, &tmQ, qdo_full, h * DQ + kb * 64, row0 + i * 128);
+        for (int kb = 0; kb < KBQ; ++kb) tma_load_2d(q + kb * 128 * 128, &tmQ, &qdo_full[st], h * DQ + kb * 64, row0 + i * 128);
 #pragma unroll
         for (int kb = 0; kb < KBV; ++kb)
-          tma_load_2d(sDO + kb * 128 * 128, &tmDO, qdo_full, h * DV + kb * 64, row0 + i * 128);
+          tma_load_2d(o + kb * 128 * 128, &tmDO, &qdo_full[st], h * DV + kb * 64, row0 + i * 128);
+        ++issued;
       }
+      // leave no copy in flight into shared memory
+      for (int it = (issued > 2 ? issued - 2 : 0); it < issued; ++it)
+        mbar_wait(&qdo_full[it & 1], (it >> 1) & 1, nullptr, p.status);
+      mbar_wait(kv_full, 0, nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t ID_SS = umma_idesc_bf16(128, 128, false, false);  // S^T, dP^T
-      // dK and dQ run over whole 64-column blocks (N = NQ); the columns past DQ
-      // are never stored.
-      constexpr uint32_t ID_V = umma_idesc_bf16(128, DV, false, true);     // dV
+      constexpr uint32_t ID_V = umma_idesc_bf16(128, DV, false, true);     // dV (A from TMEM)
       constexpr uint32_t ID_K = umma_idesc_bf16(128, NQ, false, true);     // dK
       constexpr uint32_t ID_Q = umma_idesc_bf16(128, NQ, true, true);      // dQ
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
-      const uint32_t aPt = smem_u32(sPt), aDSt = smem_u32(sDSt);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aDSt = smem_u32(sDSt);
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.status);
       for (int it = 0; it < n_it && ok; ++it) {
-        if (!mbar_wait(qdo_full, it & 1, abort_flag, p.status)) { ok = false; break; }
-        if (it > 0 && !mbar_wait(dq_read, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        const int st = it & 1;
+        const uint32_t aQ = smem_u32(sQ + st * L::TQ_BYTES), aDO = smem_u32(sDO + st * L::TV_BYTES);
+        if (!mbar_wait(&qdo_full[st], (it >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        if (it > 0) {
+          // S^T columns hold P^T of the previous pair until its dV MMA completed;
+          // the dP^T columns hold its dQ until the softmax warps read it
+          if (!mbar_wait(it_done, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+          if (!mbar_wait(dq_read, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < DQ / 16; ++kk)
@@ -533,16 +556,16 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          // dV += P^T dO ; dK += dS^T Q  (B operands MN-major: rows = queries)
-          tc_mma_f16(TM_DV, kmajor_desc(aPt, kk, 128 * 128), umma_desc_sw128(aDO + kk * 2048, 128 * 128, 1024),
-                     ID_V, acc);
+          // P^T (bf16 in TMEM): queries 0..63 in columns 0..31, 64..127 in columns 64..95
+          const uint32_t aP = TM_S + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
+          tc_mma_f16_ts(TM_DV, aP, umma_desc_sw128(aDO + kk * 2048, 128 * 128, 1024), ID_V, acc);
           tc_mma_f16(TM_DK, kmajor_desc(aDSt, kk, 128 * 128), umma_desc_sw128(aQ + kk * 2048, 128 * 128, 1024),
                      ID_K, acc);
-          // dQ = dS K: A = dS^T read MN-major (M = queries), B = K MN-major (rows = keys)
           tc_mma_f16(TM_DQ, umma_desc_sw128(aDSt + kk * 2048, 128 * 128, 1024),
                      umma_desc_sw128(aK + kk * 2048, 128 * 128, 1024), ID_Q, kk > 0 ? 1u : 0u);
         }
         tc_commit(it_done);
+        tc_commit(&qdo_empty[st]);
       }
     }
     __syncwarp();
@@ -553,24 +576,25 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // key row for P/dS; query row for the dQ epilogue
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const int tid = threadIdx.x - 64;
     const int kpos = k0 + r;
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
       const int h = hk * group + it / n_i;
       const int i = i_start + it % n_i;
       const int q0 = i * 128;
-      named_bar_sync(1, 256);  // previous iteration is done with s_lse / s_delta
-      if (tid < 128) {
-        const int qp = q0 + tid;
-        const int64_t vi = ((int64_t)b * p.Hq + h) * p.S + qp;
-        s_lse[tid] = qp < p.S ? p.lse[vi] * 1.4426950408889634f : 0.f;
-        s_delta[tid] = qp < p.S ? p.delta[vi] : 0.f;
+      named_bar_sync(1, 256);  // every softmax warp is done with the previous pair's vectors
+      {
+        const int tid = threadIdx.x - 64;
+        if (tid < 128) {
+          const int qp = q0 + tid;
+          const int64_t vi = ((int64_t)b * p.Hq + h) * p.S + qp;
+          s_lse[tid] = qp < p.S ? p.lse[vi] * 1.4426950408889634f : 0.f;
+          s_delta[tid] = qp < p.S ? p.delta[vi] : 0.f;
+        }
       }
       named_bar_sync(1, 256);
       if (!mbar_wait(sdp_full, it & 1, abort_flag, p.status)) { ok = false; break; }
-      // P^T / dS^T smem is free once the previous iteration's MMAs completed
-      if (!mbar_wait(it_done, (it & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+      // dS^T smem is free once the previous pair's MMAs completed (waited in the previous dQ step)
       tc_fence_after();
       const bool diag = p.causal && (q0 < k0 + 128);
 #pragma unroll 1
@@ -596,15 +620,16 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
           pk[t / 2] = pack_bf16(pv[0], pv[1]);
           dk[t / 2] = pack_bf16(dsv[0], dsv[1]);
         }
+        // P^T (bf16 pairs) back into this half's own, already read, S^T columns
+        tmem_st16(TM_S + lane_base + (half * 64 + cc * 16), pk);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int ch = c * 4 + q;  // 8-query chunk index 0..15
-          sw128_store16(sPt + (ch >> 3) * (128 * 128), r, ch & 7,
-                        make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]));
           sw128_store16(sDSt + (ch >> 3) * (128 * 128), r, ch & 7,
                         make_uint4(dk[q * 4], dk[q * 4 + 1], dk[q * 4 + 2], dk[q * 4 + 3]));
         }
       }
+      tc_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();

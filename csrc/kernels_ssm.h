@@ -62,3 +62,28 @@ bool ssd_tc_supported(int N, int P, int S);
 void launch_ssd_fwd(const SsdTcIO& io, cudaStream_t st);
 void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st);
 }  // namespace oxi
+
+namespace oxi {
+// Mamba3 B/C prologue (mamba3.cu): rmsnorm + bias + complex RoPE, written in
+// the interleaved two-term layout b2/c2 bf16 [B, 2S, H, N] of the tensor-core
+// scan.  braw/craw bf16 rows of stride ldr (group g at column g*N); ang f32
+// [B, S, H, N/2].  Backward: dbraw/dcraw f32 rows of stride ldd; dw [N],
+// dbb/dcb [H, N] accumulated (zero them); dang f32 [B, S, H, N/2].
+void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
+                      const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* b2,
+                      void* c2, cudaStream_t st);
+void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
+                      const void* cbias, const float* ang, const float* db2, const float* dc2, int B, int S, int H,
+                      int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw, float* dbb,
+                      float* dcb, float* dang, cudaStream_t st);
+}  // namespace oxi
+
+namespace oxi {
+// Mamba3 angles ang[b,t,h,j] = sum_{u<=t} theta[b,u,h,j] dt[b,u,h] (cumsum.cu);
+// sums: f32 scratch [B * ceil(S/128) * H * J].  Backward: dtheta [B,S,H,J],
+// ddt [B,S,H] accumulated (zero it).
+void launch_angle_cumsum(const float* theta, const float* dt, int B, int S, int H, int J, float* sums, float* ang,
+                         cudaStream_t st);
+void launch_angle_cumsum_bwd(const float* theta, const float* dt, const float* dang, int B, int S, int H, int J,
+                             float* sums, float* dtheta, float* ddt, cudaStream_t st);
+}  // namespace oxi

@@ -1,0 +1,244 @@
+// Mamba3 B/C prologue (mamba3.rs:167-211 bc_norm + bias, mamba3.rs:581-612
+// complex RoPE), fused: for every token t and head h
+//   Bn = rmsnorm(B_raw[group(h)]) * w + b_bias[h]      (over the state dim N)
+//   B_rot = rotate(Bn, ang[t, h])   pairs (2j, 2j+1) turned by ang[..., j]
+// and the same for C with c_bias.  The angles (a cumulative sum over time of
+// theta * dt) come in precomputed.  Outputs go straight into the interleaved
+// layout of the two-term scan on the tensor cores (2S steps per sequence):
+//   B2[2t+1] = B_rot_t, B2[2t+2] = B_rot_t (the B_{t-1} of step t+1), B2[0] = 0
+//   C2[2t+1] = C_rot_t, C2[2t] = 0
+// One warp per (token, head); each lane owns 4 consecutive state entries
+// (two rotation pairs) for N = 128.
+//
+// Backward (one warp per token, looping over the heads of each group):
+//   d_rot -> d_n (inverse rotation), d ang = d_re * (-rot_im) + d_im * rot_re
+//   d b_bias[h] += d_n ; d w += d_n * raw / rms ; d raw = rmsnorm-backward(sum_h w d_n)
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstdint>
+
+#include "host_util.h"
+#include "kernels_ssm.h"
+#include "ptx.cuh"
+
+namespace oxi {
+namespace {
+
+constexpr int M3N = 128;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float* v) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void store4(__nv_bfloat16* p, const float* v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+}
+
+// raw [4] -> rotated [4] for one lane; returns nothing, fills out
+__device__ __forceinline__ void norm_bias_rot(const float* raw, float rinv, const float* w, const float* bias,
+                                              float c0, float s0, float c1, float s1, float* out) {
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = raw[i] * rinv * w[i] + bias[i];
+  out[0] = n[0] * c0 - n[1] * s0;
+  out[1] = n[0] * s0 + n[1] * c0;
+  out[2] = n[2] * c1 - n[3] * s1;
+  out[3] = n[2] * s1 + n[3] * c1;
+}
+
+__global__ void __launch_bounds__(256) m3_bc_fwd_kernel(const __nv_bfloat16* __restrict__ braw,
+                                                        const __nv_bfloat16* __restrict__ craw, int64_t ldr,
+                                                        const __nv_bfloat16* __restrict__ w,
+                                                        const __nv_bfloat16* __restrict__ bbias,
+                                                        const __nv_bfloat16* __restrict__ cbias,
+                                                        const float* __restrict__ ang, int Bsz, int S, int H, int G,
+                                                        float eps, __nv_bfloat16* __restrict__ b2,
+                                                        __nv_bfloat16* __restrict__ c2) {
+  const int lane = threadIdx.x & 31;
+  const int64_t items = (int64_t)Bsz * S * H;
+  const int hpg = H / G;
+  float wv[4];
+  load4(w + lane * 4, wv);
+  for (int64_t it = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; it < items;
+       it += (int64_t)gridDim.x * (blockDim.x / 32)) {
+    const int h = (int)(it % H);
+    const int64_t bt = it / H;  // b * S + t
+    const int t = (int)(bt % S);
+    const int64_t b = bt / S;
+    const int g = h / hpg;
+    float rb[4], rc[4], bb[4], cb[4];
+    load4(braw + bt * ldr + g * M3N + lane * 4, rb);
+    load4(craw + bt * ldr + g * M3N + lane * 4, rc);
+    load4(bbias + h * M3N + lane * 4, bb);
+    load4(cbias + h * M3N + lane * 4, cb);
+    const float sb = warp_sum(rb[0] * rb[0] + rb[1] * rb[1] + rb[2] * rb[2] + rb[3] * rb[3]);
+    const float sc = warp_sum(rc[0] * rc[0] + rc[1] * rc[1] + rc[2] * rc[2] + rc[3] * rc[3]);
+    const float rib = rsqrtf(sb / M3N + eps), ric = rsqrtf(sc / M3N + eps);
+    const float2 a = *reinterpret_cast<const float2*>(ang + it * (M3N / 2) + lane * 2);
+    float s0, c0, s1, c1;
+    sincosf(a.x, &s0, &c0);
+    sincosf(a.y, &s1, &c1);
+    float ob[4], oc[4];
+    norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
+    norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);
+    // interleaved rows: token t -> steps 2t (decay + B_{t-1} term) and 2t+1 (B_t term)
+    const int64_t r_odd = (b * 2 * S + 2 * t + 1) * H + h;
+    store4(b2 + r_odd * M3N + lane * 4, ob);
+    store4(c2 + r_odd * M3N + lane * 4, oc);
+    const float z[4] = {0.f, 0.f, 0.f, 0.f};
+    store4(c2 + (r_odd - H) * M3N + lane * 4, z);
+    if (t + 1 < S) store4(b2 + (r_odd + H) * M3N + lane * 4, ob);
+    if (t == 0) store4(b2 + (r_odd - H) * M3N + lane * 4, z);
+  }
+}
+
+// db2/dc2: f32 gradients of the interleaved tensors [B, 2S, H, N].
+__global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __restrict__ braw,
+                                                        const __nv_bfloat16* __restrict__ craw, int64_t ldr,
+                                                        const __nv_bfloat16* __restrict__ w,
+                                                        const __nv_bfloat16* __restrict__ bbias,
+                                                        const __nv_bfloat16* __restrict__ cbias,
+                                                        const float* __restrict__ ang, const float* __restrict__ db2,
+                                                        const float* __restrict__ dc2, int Bsz, int S, int H, int G,
+                                                        float eps, float* __restrict__ dbraw, float* __restrict__ dcraw,
+                                                        int64_t ldd, float* __restrict__ dw, float* __restrict__ dbb,
+                                                        float* __restrict__ dcb, float* __restrict__ dang) {
+  extern __shared__ float s_db[];  // [2][H][N] bias-gradient partials of this block
+  float* s_dbb = s_db;
+  float* s_dcb = s_db + H * M3N;
+  for (int i = threadIdx.x; i < 2 * H * M3N; i += blockDim.x) s_db[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int hpg = H / G;
+  const int64_t tokens = (int64_t)Bsz * S;
+  float wv[4];
+  load4(w + lane * 4, wv);
+  float dw_acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int64_t bt = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; bt < tokens;
+       bt += (int64_t)gridDim.x * (blockDim.x / 32)) {
+    const int t = (int)(bt % S);
+    const int64_t b = bt / S;
+    for (int g = 0; g < G; ++g) {
+      float rb[4], rc[4];
+      load4(braw + bt * ldr + g * M3N + lane * 4, rb);
+      load4(craw + bt * ldr + g * M3N + lane * 4, rc);
+      const float sb = warp_sum(rb[0] * rb[0] + rb[1] * rb[1] + rb[2] * rb[2] + rb[3] * rb[3]);
+      const float sc = warp_sum(rc[0] * rc[0] + rc[1] * rc[1] + rc[2] * rc[2] + rc[3] * rc[3]);
+      const float rib = rsqrtf(sb / M3N + eps), ric = rsqrtf(sc / M3N + eps);
+      float gb[4] = {0.f, 0.f, 0.f, 0.f}, gc[4] = {0.f, 0.f, 0.f, 0.f};  // sum over heads of d_n
+      for (int hh = 0; hh < hpg; ++hh) {
+        const int h = g * hpg + hh;
+        const int64_t it = bt * H + h;
+        const int64_t r_odd = (b * 2 * S + 2 * t + 1) * H + h;
+        const float4 d1 = *reinterpret_cast<const float4*>(db2 + r_odd * M3N + lane * 4);
+        float dB[4] = {d1.x, d1.y, d1.z, d1.w};
+        if (t + 1 < S) {
+          const float4 d2 = *reinterpret_cast<const float4*>(db2 + (r_odd + H) * M3N + lane * 4);
+          dB[0] += d2.x; dB[1] += d2.y; dB[2] += d2.z; dB[3] += d2.w;
+        }
+        const float4 d3 = *reinterpret_cast<const float4*>(dc2 + r_odd * M3N + lane * 4);
+        const float dC[4] = {d3.x, d3.y, d3.z, d3.w};
+        float bb[4], cb[4];
+        load4(bbias + h * M3N + lane * 4, bb);
+        load4(cbias + h * M3N + lane * 4, cb);
+        const float2 a = *reinterpret_cast<const float2*>(ang + it * (M3N / 2) + lane * 2);
+        float s0, c0, s1, c1;
+        sincosf(a.x, &s0, &c0);
+        sincosf(a.y, &s1, &c1);
+        float ob[4], oc[4];
+        norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
+        norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);
+        // d angle of both pairs (B and C share the angles)
+        const float da0 = dB[0] * (-ob[1]) + dB[1] * ob[0] + dC[0] * (-oc[1]) + dC[1] * oc[0];
+        const float da1 = dB[2] * (-ob[3]) + dB[3] * ob[2] + dC[2] * (-oc[3]) + dC[3] * oc[2];
+        *reinterpret_cast<float2*>(dang + it * (M3N / 2) + lane * 2) = make_float2(da0, da1);
+        // inverse rotation -> gradient of the normalised + biased vector
+        float nb[4], nc[4];
+        nb[0] = dB[0] * c0 + dB[1] * s0;  nb[1] = -dB[0] * s0 + dB[1] * c0;
+        nb[2] = dB[2] * c1 + dB[3] * s1;  nb[3] = -dB[2] * s1 + dB[3] * c1;
+        nc[0] = dC[0] * c0 + dC[1] * s0;  nc[1] = -dC[0] * s0 + dC[1] * c0;
+        nc[2] = dC[2] * c1 + dC[3] * s1;  nc[3] = -dC[2] * s1 + dC[3] * c1;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          atomicAdd(s_dbb + h * M3N + lane * 4 + i, nb[i]);
+          atomicAdd(s_dcb + h * M3N + lane * 4 + i, nc[i]);
+          gb[i] += nb[i];
+          gc[i] += nc[i];
+        }
+      }
+      // rmsnorm backward of the shared raw rows (x r w): u = w * g
+      float ub[4], uc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ub[i] = wv[i] * gb[i];
+        uc[i] = wv[i] * gc[i];
+        dw_acc[i] += gb[i] * rb[i] * rib + gc[i] * rc[i] * ric;
+      }
+      const float pb = warp_sum(ub[0] * rb[0] + ub[1] * rb[1] + ub[2] * rb[2] + ub[3] * rb[3]) / M3N;
+      const float pc = warp_sum(uc[0] * rc[0] + uc[1] * rc[1] + uc[2] * rc[2] + uc[3] * rc[3]) / M3N;
+      float* ob_ = dbraw + bt * ldd + g * M3N + lane * 4;
+      float* oc_ = dcraw + bt * ldd + g * M3N + lane * 4;
+      *reinterpret_cast<float4*>(ob_) = make_float4(rib * ub[0] - rb[0] * rib * rib * rib * pb,
+                                                    rib * ub[1] - rb[1] * rib * rib * rib * pb,
+                                                    rib * ub[2] - rb[2] * rib * rib * rib * pb,
+                                                    rib * ub[3] - rb[3] * rib * rib * rib * pb);
+      *reinterpret_cast<float4*>(oc_) = make_float4(ric * uc[0] - rc[0] * ric * ric * ric * pc,
+                                                    ric * uc[1] - rc[1] * ric * ric * ric * pc,
+                                                    ric * uc[2] - rc[2] * ric * ric * ric * pc,
+                                                    ric * uc[3] - rc[3] * ric * ric * ric * pc);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) atomicAdd(dw + lane * 4 + i, dw_acc[i]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < H * M3N; i += blockDim.x) {
+    atomicAdd(dbb + i, s_dbb[i]);
+    atomicAdd(dcb + i, s_dcb[i]);
+  }
+}
+
+unsigned grid_of(int64_t warps_needed) {
+  const int64_t blocks = (warps_needed + 7) / 8;
+  return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+}
+
+}  // namespace
+
+void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
+                      const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* b2,
+                      void* c2, cudaStream_t st) {
+  OXI_CHECK(N == M3N && H % G == 0 && ldr % 4 == 0, "Mamba3 B/C prologue supports state size 128");
+  m3_bc_fwd_kernel<<<grid_of((int64_t)B * S * H), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(braw), reinterpret_cast<const __nv_bfloat16*>(craw), ldr,
+      reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<const __nv_bfloat16*>(bbias),
+      reinterpret_cast<const __nv_bfloat16*>(cbias), ang, B, S, H, G, eps, reinterpret_cast<__nv_bfloat16*>(b2),
+      reinterpret_cast<__nv_bfloat16*>(c2));
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
+                      const void* cbias, const float* ang, const float* db2, const float* dc2, int B, int S, int H,
+                      int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw, float* dbb,
+                      float* dcb, float* dang, cudaStream_t st) {
+  OXI_CHECK(N == M3N && H % G == 0 && H <= 64, "Mamba3 B/C prologue supports state size 128, <= 64 heads");
+  const int64_t blocks = std::min<int64_t>(((int64_t)B * S + 7) / 8, 148 * 4);
+  const int smem = 2 * H * M3N * (int)sizeof(float);
+  if (smem > 48 * 1024)
+    OXI_CUDA_CHECK(cudaFuncSetAttribute(m3_bc_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  m3_bc_bwd_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, smem, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(braw), reinterpret_cast<const __nv_bfloat16*>(craw), ldr,
+      reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<const __nv_bfloat16*>(bbias),
+      reinterpret_cast<const __nv_bfloat16*>(cbias), ang, db2, dc2, B, S, H, G, eps, dbraw, dcraw, ldd, dw, dbb, dcb,
+      dang);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace oxi

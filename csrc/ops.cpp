@@ -551,6 +551,73 @@ std::vector<torch::Tensor> ssd_tc_bwd(torch::Tensor x, torch::Tensor Bm, torch::
   return {dx, dB, dC, dg};
 }
 
+// ------------------------------------------------------------ Mamba3 B/C prologue
+std::vector<torch::Tensor> m3_bc_fwd(torch::Tensor braw, torch::Tensor craw, torch::Tensor w, torch::Tensor bbias,
+                                     torch::Tensor cbias, torch::Tensor ang, int64_t B, int64_t S, int64_t H,
+                                     int64_t G, double eps) {
+  c10::cuda::CUDAGuard g(braw.device());
+  TORCH_CHECK(braw.scalar_type() == torch::kBFloat16 && craw.scalar_type() == torch::kBFloat16 && braw.dim() == 2 &&
+                  craw.dim() == 2 && braw.stride(1) == 1 && craw.stride(1) == 1 && braw.stride(0) == craw.stride(0),
+              "B/C raw: bf16 [B*S, G*N] views sharing a row stride");
+  TORCH_CHECK(ang.scalar_type() == torch::kFloat32 && ang.is_contiguous() && ang.numel() == B * S * H * 64, "ang");
+  TORCH_CHECK(w.is_contiguous() && bbias.is_contiguous() && cbias.is_contiguous() &&
+                  w.scalar_type() == torch::kBFloat16 && bbias.scalar_type() == torch::kBFloat16 &&
+                  cbias.scalar_type() == torch::kBFloat16, "bc_norm weight / biases: bf16 contiguous");
+  auto b2 = torch::empty({B, 2 * S, H, 128}, braw.options());
+  auto c2 = torch::empty({B, 2 * S, H, 128}, braw.options());
+  oxi::launch_m3_bc_fwd(braw.data_ptr(), craw.data_ptr(), braw.stride(0), w.data_ptr(), bbias.data_ptr(),
+                        cbias.data_ptr(), ang.data_ptr<float>(), (int)B, (int)S, (int)H, (int)G, 128, (float)eps,
+                        b2.data_ptr(), c2.data_ptr(), stream());
+  return {b2, c2};
+}
+
+std::vector<torch::Tensor> m3_bc_bwd(torch::Tensor braw, torch::Tensor craw, torch::Tensor w, torch::Tensor bbias,
+                                     torch::Tensor cbias, torch::Tensor ang, torch::Tensor db2, torch::Tensor dc2,
+                                     int64_t B, int64_t S, int64_t H, int64_t G, double eps) {
+  c10::cuda::CUDAGuard g(braw.device());
+  TORCH_CHECK(db2.scalar_type() == torch::kFloat32 && dc2.scalar_type() == torch::kFloat32 && db2.is_contiguous() &&
+                  dc2.is_contiguous() && db2.numel() == B * 2 * S * H * 128, "db2 / dc2: f32 contiguous [B, 2S, H, N]");
+  auto f32 = braw.options().dtype(torch::kFloat32);
+  auto dbraw = torch::empty({B * S, G * 128}, f32);
+  auto dcraw = torch::empty({B * S, G * 128}, f32);
+  auto dw = torch::zeros({128}, f32);
+  auto dbb = torch::zeros({H, 128}, f32);
+  auto dcb = torch::zeros({H, 128}, f32);
+  auto dang = torch::empty({B, S, H, 64}, f32);
+  oxi::launch_m3_bc_bwd(braw.data_ptr(), craw.data_ptr(), braw.stride(0), w.data_ptr(), bbias.data_ptr(),
+                        cbias.data_ptr(), ang.data_ptr<float>(), db2.data_ptr<float>(), dc2.data_ptr<float>(), (int)B,
+                        (int)S, (int)H, (int)G, 128, (float)eps, dbraw.data_ptr<float>(), dcraw.data_ptr<float>(),
+                        dbraw.stride(0), dw.data_ptr<float>(), dbb.data_ptr<float>(), dcb.data_ptr<float>(),
+                        dang.data_ptr<float>(), stream());
+  return {dbraw, dcraw, dw, dbb, dcb, dang};
+}
+
+// ------------------------------------------------------------ Mamba3 angles
+torch::Tensor angle_cumsum(torch::Tensor theta, torch::Tensor dt) {
+  c10::cuda::CUDAGuard g(theta.device());
+  TORCH_CHECK(theta.scalar_type() == torch::kFloat32 && theta.is_contiguous() && theta.dim() == 4 &&
+                  dt.scalar_type() == torch::kFloat32 && dt.is_contiguous(), "theta f32 [B,S,H,J], dt f32 [B,S,H]");
+  const int64_t B = theta.size(0), S = theta.size(1), H = theta.size(2), J = theta.size(3);
+  auto ang = torch::empty_like(theta);
+  auto sums = torch::empty({B * ((S + 127) / 128) * H * J}, theta.options());
+  oxi::launch_angle_cumsum(theta.data_ptr<float>(), dt.data_ptr<float>(), (int)B, (int)S, (int)H, (int)J,
+                           sums.data_ptr<float>(), ang.data_ptr<float>(), stream());
+  return ang;
+}
+
+std::vector<torch::Tensor> angle_cumsum_bwd(torch::Tensor theta, torch::Tensor dt, torch::Tensor dang) {
+  c10::cuda::CUDAGuard g(theta.device());
+  TORCH_CHECK(dang.scalar_type() == torch::kFloat32 && dang.is_contiguous() && dang.sizes() == theta.sizes(), "dang");
+  const int64_t B = theta.size(0), S = theta.size(1), H = theta.size(2), J = theta.size(3);
+  auto dtheta = torch::empty_like(theta);
+  auto ddt = torch::zeros_like(dt);
+  auto sums = torch::empty({B * ((S + 127) / 128) * H * J}, theta.options());
+  oxi::launch_angle_cumsum_bwd(theta.data_ptr<float>(), dt.data_ptr<float>(), dang.data_ptr<float>(), (int)B, (int)S,
+                               (int)H, (int)J, sums.data_ptr<float>(), dtheta.data_ptr<float>(), ddt.data_ptr<float>(),
+                               stream());
+  return {dtheta, ddt};
+}
+
 // ------------------------------------------------------------ SSM
 void conv1d_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias, torch::Tensor y, int64_t B,
                 int64_t S, bool act) {
@@ -816,6 +883,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ssd_tc_supported", &ssd_tc_supported, "whether the tensor-core SSD handles (N, P, S)");
   m.def("ssd_tc_fwd", &ssd_tc_fwd, "tensor-core chunked SSD forward");
   m.def("ssd_tc_bwd", &ssd_tc_bwd, "tensor-core chunked SSD backward");
+  m.def("angle_cumsum", &angle_cumsum, "Mamba3 rotation angles: cumsum over time of theta * dt");
+  m.def("angle_cumsum_bwd", &angle_cumsum_bwd, "backward of angle_cumsum");
+  m.def("m3_bc_fwd", &m3_bc_fwd, "Mamba3 B/C norm + bias + complex RoPE into the interleaved scan layout");
+  m.def("m3_bc_bwd", &m3_bc_bwd, "backward of m3_bc_fwd");
   m.def("ssm_scan_fwd", &ssm_scan_fwd, "Mamba2/3 selective scan forward");
   m.def("ssm_scan_bwd", &ssm_scan_bwd, "Mamba2/3 selective scan backward");
   m.def("mamba1_scan_fwd", &mamba1_scan_fwd, "Mamba1 selective scan forward (saves states)");

@@ -17,10 +17,10 @@
 // H_end:   dX = M^T dY + diag(w) B dH ;  dH_prev = exp(Lam_L) dH + C^T diag(exp Lam) dY
 //          dg_s += exp(Lam_L - Lam_s) <x_s, (B dH)_s>
 //          (stores every chunk's dH, bf16, for pass 2)
-// Backward, pass 2 (chunk-parallel): dM = dY X^T, dS = dM o D o g,
+// Backward, pass 2 (one CTA per chunk, all p-blocks): dM = dY X^T, dS = dM o D o g,
 //          dC = dS B + diag(exp Lam) dY H_prev^T ,  dB = dS^T C + diag(w) X dH^T
 //          dg_s += sum_t dM[t,s] S[t,s] D[t,s]
-// (partial sums over p-blocks are added with f32 atomics).  d(a_t) follows
+// (dg collects the two passes' parts with f32 atomics).  d(a_t) follows
 // outside from <dy, y> and dg (see ops/ssd_tc.py).
 //
 // Warps: 0 TMA, 1 MMA + TMEM owner, 2..5 math (thread m <-> TMEM lane m).
@@ -57,8 +57,8 @@ struct SsdParams {
   __nv_bfloat16* hs;          // [B*H*nc*N, P] chunk-start states (fwd writes, bwd reads via TMA)
   __nv_bfloat16* dhs;         // [B*H*nc*N, P] chunk-end adjoints (bwd pass 1 writes)
   float* dx;                  // [B*S, H*P] f32
-  float* dB;                  // [B*S, H*N] f32 (atomics)
-  float* dC;                  // [B*S, H*N] f32 (atomics)
+  float* dB;                  // [B*S, H*N] f32
+  float* dC;                  // [B*S, H*N] f32
   float* dgamma;              // [B, S, H] f32 (atomics)
   int* status;
 };
@@ -544,17 +544,23 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
 }
 
 // ====================================================== backward, pass 2
+// One CTA per (b, h, chunk) covering every P column, so dB / dC rows are
+// written once (no atomics):
+//   A: dM = sum_pb dY_pb X_pb^T ; S = C B^T            (TMEM, accumulated over p-blocks)
+//   B: dS = dM o D o g (smem bf16), dg_s += sum_t dM o S o D
+//   C: dC = dS B + sum_pb E_pb H_pb^T ,  dB = dS^T C + sum_pb W_pb dH_pb^T
+//      (E = diag(exp lam) dY, W = diag(w) X, per p-block; dC / dB reuse S / dM)
 struct Bwd2Smem {
   static constexpr int OFF_C = 0;
   static constexpr int OFF_B = OFF_C + T_NN;
-  static constexpr int OFF_X = OFF_B + T_NN;
+  static constexpr int OFF_DS = OFF_B + T_NN;
+  static constexpr int OFF_X = OFF_DS + T_NN;
   static constexpr int OFF_DY = OFF_X + T_NP;
   static constexpr int OFF_H = OFF_DY + T_NP;
   static constexpr int OFF_DH = OFF_H + T_NP;
-  static constexpr int OFF_DS = OFF_DH + T_NP;
-  static constexpr int OFF_E = OFF_DS + T_NN;
+  static constexpr int OFF_E = OFF_DH + T_NP;
   static constexpr int OFF_W = OFF_E + T_NP;
-  static constexpr int OFF_VEC = OFF_W + T_NP;      // lam, gam, part, colsum[128]
+  static constexpr int OFF_VEC = OFF_W + T_NP;      // lam, gam, colsum, part
   static constexpr int OFF_BAR = OFF_VEC + 3 * 128 * 4 + 64;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
 };
@@ -566,30 +572,36 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
   using L = Bwd2Smem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sX = smem + L::OFF_X, *sDY = smem + L::OFF_DY,
-          *sH = smem + L::OFF_H, *sDH = smem + L::OFF_DH, *sDS = smem + L::OFF_DS, *sE = smem + L::OFF_E,
+  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sDS = smem + L::OFF_DS, *sX = smem + L::OFF_X,
+          *sDY = smem + L::OFF_DY, *sH = smem + L::OFF_H, *sDH = smem + L::OFF_DH, *sE = smem + L::OFF_E,
           *sW = smem + L::OFF_W;
   float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
   float* s_gam = s_lam + 128;
   float* s_col = s_gam + 128;
   float* s_part = s_col + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t *ld_full = bars + 0, *s_full = bars + 1, *p_full = bars + 2, *m_full = bars + 3;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  uint64_t *cb_full = bars + 0, *t_full = bars + 1, *t_free = bars + 2, *sdm_full = bars + 3, *ds_ready = bars + 4,
+           *ew_ready = bars + 5, *out_full = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int bh = blockIdx.x, c = blockIdx.y, pb = blockIdx.z;
+  const int bh = blockIdx.x, c = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int g = h / (p.H / p.G);
   const int row0 = b * p.S;
   const int r = row0 + c * SL;
   const int hrow = (bh * p.nc + c) * SN;
+  const int npb = p.P / SP;
+  const int nload = 2 * npb;  // pass A loads (x, dy), pass C loads (x, dy, H, dH)
   if (threadIdx.x == 0) {
-    mbar_init(ld_full, 1);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(m_full, 1);
+    mbar_init(cb_full, 1);
+    mbar_init(t_full, 1);
+    mbar_init(t_free, 1);
+    mbar_init(sdm_full, 1);
+    mbar_init(ds_ready, 4);
+    mbar_init(ew_ready, 4);
+    mbar_init(out_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -605,16 +617,26 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(ld_full, 2 * T_NN + 4 * T_NP);
-      tma_load_2d(sC, &tmC, ld_full, g * SN, r);
-      tma_load_2d(sC + 16384, &tmC, ld_full, g * SN + 64, r);
-      tma_load_2d(sB, &tmB, ld_full, g * SN, r);
-      tma_load_2d(sB + 16384, &tmB, ld_full, g * SN + 64, r);
-      tma_load_2d(sX, &tmX, ld_full, h * p.P + pb * SP, r);
-      tma_load_2d(sDY, &tmDY, ld_full, h * p.P + pb * SP, r);
-      tma_load_2d(sH, &tmHS, ld_full, pb * SP, hrow);
-      tma_load_2d(sDH, &tmDHS, ld_full, pb * SP, hrow);
-      mbar_wait(ld_full, 0, nullptr, p.status);
+      mbar_arrive_expect_tx(cb_full, 2 * T_NN);
+      tma_load_2d(sC, &tmC, cb_full, g * SN, r);
+      tma_load_2d(sC + 16384, &tmC, cb_full, g * SN + 64, r);
+      tma_load_2d(sB, &tmB, cb_full, g * SN, r);
+      tma_load_2d(sB + 16384, &tmB, cb_full, g * SN + 64, r);
+      int li = 0;
+      for (; li < nload; ++li) {
+        const int pb = li % npb;
+        const bool pass_c = li >= npb;
+        if (li > 0 && !mbar_wait(t_free, (li - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(t_full, (pass_c ? 4 : 2) * T_NP);
+        tma_load_2d(sX, &tmX, t_full, h * p.P + pb * SP, r);
+        tma_load_2d(sDY, &tmDY, t_full, h * p.P + pb * SP, r);
+        if (pass_c) {
+          tma_load_2d(sH, &tmHS, t_full, pb * SP, hrow);
+          tma_load_2d(sDH, &tmDHS, t_full, pb * SP, hrow);
+        }
+      }
+      if (li > 0) mbar_wait(t_full, (li - 1) & 1, nullptr, p.status);  // no copy in flight at exit
+      mbar_wait(cb_full, 0, nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -625,30 +647,43 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aX = smem_u32(sX), aDY = smem_u32(sDY),
                      aH = smem_u32(sH), aDH = smem_u32(sDH), aDS = smem_u32(sDS), aE = smem_u32(sE),
                      aW = smem_u32(sW);
-      bool ok = mbar_wait(ld_full, 0, abort_flag, p.status);
+      bool ok = mbar_wait(cb_full, 0, abort_flag, p.status);
       if (ok) {
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aB, kk), ID_SS, kk != 0);
+      }
+      // pass A: dM = sum over p-blocks of dY X^T
+      for (int pb = 0; pb < npb && ok; ++pb) {
+        if (!mbar_wait(t_full, pb & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_DM, kdesc(aDY, kk), kdesc(aX, kk), ID_SS, kk != 0);
-        tc_commit(s_full);
-        ok = mbar_wait(p_full, 0, abort_flag, p.status);
+        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_DM, kdesc(aDY, kk), kdesc(aX, kk), ID_SS, (pb > 0 || kk > 0));
+        tc_commit(t_free);
+      }
+      if (ok) {
+        tc_commit(sdm_full);
+        ok = mbar_wait(ds_ready, 0, abort_flag, p.status);
       }
       if (ok) {
         tc_fence_after();
-        // dC = dS B + E H^T   (into the S columns)
+        // dC = dS B (into the S columns), dB = dS^T C (into the dM columns)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aDS, kk), mdesc(aB, kk), ID_DC1, kk != 0);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_S, kdesc(aE, kk), kdesc(aH, kk), ID_SS, 1u);
-        // dB = dS^T C + W dH^T   (into the dM columns)
-#pragma unroll
         for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DM, mdesc(aDS, kk), mdesc(aC, kk), ID_DB1, kk != 0);
+      }
+      // pass C: + E H^T and + W dH^T per p-block
+      for (int pb = 0; pb < npb && ok; ++pb) {
+        if (!mbar_wait(ew_ready, pb & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_S, kdesc(aE, kk), kdesc(aH, kk), ID_SS, 1u);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_DM, kdesc(aW, kk), kdesc(aDH, kk), ID_SS, 1u);
-        tc_commit(m_full);
+        tc_commit(t_free);
       }
+      if (ok) tc_commit(out_full);
     }
     __syncwarp();
   } else {
@@ -662,22 +697,7 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
     s_col[m] = 0.f;
     math_bar();
     const float lam_end = s_lam[SL - 1];
-    bool ok = mbar_wait(ld_full, 0, abort_flag, p.status);
-    if (ok) {
-      // E = diag(exp lam) dY ; W = diag(w) X   (row m)
-      float v[64];
-      load_row64(sDY, m, v);
-      const float e = __expf(lam);
-#pragma unroll
-      for (int k = 0; k < 64; ++k) v[k] *= e;
-      store_row64(sE, m, v);
-      load_row64(sX, m, v);
-      const float w = __expf(lam_end - lam) * gm;
-#pragma unroll
-      for (int k = 0; k < 64; ++k) v[k] *= w;
-      store_row64(sW, m, v);
-      ok = mbar_wait(s_full, 0, abort_flag, p.status);
-    }
+    bool ok = mbar_wait(sdm_full, 0, abort_flag, p.status);
     if (ok) {
       tc_fence_after();
       // dS = dM o decay o g (row t = m);  column sums of dM o S o decay -> dg
@@ -698,7 +718,6 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
             const float dm = __uint_as_float(dr[t + e2]) * d;
             v[e2] = dm * s_gam[s];
             float cs = dm * __uint_as_float(sr[t + e2]);
-            // reduce over the 32 rows of this warp before touching shared memory
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
             if (lane == 0) atomicAdd(&s_col[s], cs);
@@ -714,14 +733,34 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(ds_ready);
       math_bar();
       atomicAdd(p.dgamma + si, s_col[m]);
-      ok = mbar_wait(m_full, 0, abort_flag, p.status);
     }
-    if (ok) {
+    // pass C inputs: E = diag(exp lam) dY_pb, W = diag(w) X_pb (row m)
+    const float e = __expf(lam);
+    const float w = __expf(lam_end - lam) * gm;
+    for (int pb = 0; pb < npb && ok; ++pb) {
+      const int li = npb + pb;
+      if (!mbar_wait(t_full, li & 1, abort_flag, p.status)) { ok = false; break; }
+      // E / W of the previous p-block were read by the MMAs that freed this load slot
+      float v[64];
+      load_row64(sDY, m, v);
+#pragma unroll
+      for (int k = 0; k < 64; ++k) v[k] *= e;
+      store_row64(sE, m, v);
+      load_row64(sX, m, v);
+#pragma unroll
+      for (int k = 0; k < 64; ++k) v[k] *= w;
+      store_row64(sW, m, v);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ew_ready);
+    }
+    if (ok && mbar_wait(out_full, 0, abort_flag, p.status)) {
       tc_fence_after();
-      // row m: dC_t (t = m) and dB_s (s = m), 128 values each
+      // row m: dC_t (t = m) and dB_s (s = m), 128 values each, written once
       float* dcr = p.dC + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
       float* dbr = p.dB + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
 #pragma unroll 1
@@ -730,11 +769,11 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
         tmem_row64(TM_S + lb + half * 64, v);
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          atomicAdd(reinterpret_cast<float4*>(dcr + half * 64) + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+          reinterpret_cast<float4*>(dcr + half * 64)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
         tmem_row64(TM_DM + lb + half * 64, v);
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          atomicAdd(reinterpret_cast<float4*>(dbr + half * 64) + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+          reinterpret_cast<float4*>(dbr + half * 64)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
       }
     }
   }
@@ -800,8 +839,7 @@ void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st) {
   }
   ssd_bwd1_kernel<<<dim3(io.B * io.H, io.P / SP), SSD_THREADS, Bwd1Smem::TOTAL, st>>>(tx, tb, tc, tdy, p);
   OXI_CUDA_CHECK(cudaGetLastError());
-  ssd_bwd2_kernel<<<dim3(io.B * io.H, nc, io.P / SP), SSD_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs,
-                                                                                          p);
+  ssd_bwd2_kernel<<<dim3(io.B * io.H, nc), SSD_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

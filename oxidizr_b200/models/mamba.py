@@ -308,6 +308,24 @@ class Mamba3Mixer(RefModule):
         else:
             x = F.silu(x)
         lam = torch.sigmoid(self.lambda_proj(h).float())
+        dtv = _softplus_dt(dt, self.dt_bias)
+        fused = self._fused_ok(h, x, S)
+        if fused:
+            # fused prologue (norm + bias + complex RoPE) straight into the tensor-core scan layout
+            from ..ops.ssd_tc import Mamba3BC
+            if self.complex_rope:
+                from ..ops.ssd_tc import angle_cumsum
+                theta = self.theta_proj(h).float().reshape(B, S, self.Hs, self.N // 2)
+                ang = angle_cumsum(theta, dtv)
+            else:
+                ang = torch.zeros(B, S, self.Hs, self.N // 2, device=h.device)
+            b2, c2 = Mamba3BC.apply(Bm, Cm, self.bc_norm.weight, self.b_bias, self.c_bias, ang, self.Hs, 1e-6)
+            xh = x.reshape(B, S, self.Hs, self.P)
+            if self.mimo_x_up is not None:
+                xh = self.mimo_x_up(xh)
+            from ..ops.ssd_tc import mamba3_tc_interleaved
+            y = mamba3_tc_interleaved(xh, dtv, self.A(), b2, c2, lam)
+            return self._finish(y, xh, gate, h, resid, B, S)
         Bm = Bm.reshape(B, S, self.g, self.N)
         Cm = Cm.reshape(B, S, self.g, self.N)
         rep = self.Hs // self.g
@@ -317,7 +335,6 @@ class Mamba3Mixer(RefModule):
         w = self.bc_norm.weight
         Bm = api.rmsnorm(Bm.contiguous(), w, 1e-6).float() + self.b_bias.float()
         Cm = api.rmsnorm(Cm.contiguous(), w, 1e-6).float() + self.c_bias.float()
-        dtv = _softplus_dt(dt, self.dt_bias)
         if self.complex_rope:
             theta = self.theta_proj(h).float().reshape(B, S, self.Hs, self.N // 2)
             ang = torch.cumsum(theta * dtv[..., None], 1)
@@ -328,6 +345,17 @@ class Mamba3Mixer(RefModule):
         if self.mimo_x_up is not None:
             xh = self.mimo_x_up(xh)
         y = ssm.mamba3_scan(xh, dtv, self.A(), Bm, Cm, lam, self.chunk, compat=self.compat)
+        return self._finish(y, xh, gate, h, resid, B, S)
+
+    def _fused_ok(self, h, x, S) -> bool:
+        if self.compat or not h.is_cuda or self.conv1d is not None:
+            return False
+        from ..ops.ssd_tc import m3_bc_ok, tc_ok
+        width = self.P * (self.R if self.mimo_x_up is not None else 1)
+        probe = x.new_empty(1, 1, 1, width)
+        return m3_bc_ok(x, self.N, self.Hs, self.g) and tc_ok(probe, self.N, 2 * S)
+
+    def _finish(self, y, xh, gate, h, resid, B, S):
         y = y.float() + xh.float() * self.D.float()[:, None]
         y = y.to(h.dtype)
         if self.mimo_x_down is not None:

@@ -6,6 +6,8 @@ Bounded waits and debug checks record an error code there instead of trapping;
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .. import _ext
@@ -76,7 +78,17 @@ class _Counter:
                 def call(*a, **k):
                     if counter.enabled:
                         counter.count += counter.LAUNCHES_PER_CALL.get(name, 1)
-                    return fn(*a, **k)
+                    if not _DEBUG_SYNC:
+                        return fn(*a, **k)
+                    # debugging aid: find the first launch that faults (OXI_DEBUG_SYNC=1)
+                    import torch
+                    torch.cuda.synchronize()
+                    r = fn(*a, **k)
+                    try:
+                        torch.cuda.synchronize()
+                    except RuntimeError as e:
+                        raise RuntimeError(f"oxidizr kernel call {name!r} failed: {e}") from e
+                    return r
                 return call
 
             def __dir__(self):
@@ -85,6 +97,7 @@ class _Counter:
         return _Proxy()
 
 
+_DEBUG_SYNC = os.environ.get("OXI_DEBUG_SYNC") == "1"
 launch_counter = _Counter()
 _PROXY = None
 

@@ -27,6 +27,20 @@ def mm(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = False
     """
     M = a.shape[1] if a_t else a.shape[0]
     N = b.shape[1] if b_t else b.shape[0]
+    if a.is_cuda and not (_tma_ok(a) and _tma_ok(b)):
+        # TMA needs 16-byte aligned rows: tiny or odd-width projections (e.g. a few
+        # per-head scalars) go through a plain matmul
+        A = a.t() if a_t else a
+        B = b.t() if b_t else b
+        r = alpha * (A.float() @ B.float().t())
+        if resid is not None:
+            r = r + resid.float()
+        if out is not None:
+            if beta != 0.0:
+                r = r + beta * out.float()
+            out.copy_(r.to(out.dtype))
+            return out
+        return r.to(out_dtype)
     if not a.is_cuda:
         A = a.t() if a_t else a
         B = b.t() if b_t else b
@@ -43,6 +57,11 @@ def mm(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = False
         out = torch.empty(M, N, dtype=out_dtype, device=a.device)
     ext().gemm(a, a_t, b, b_t, out, resid, float(beta), float(alpha), status(a.device))
     return out
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    """Rows 16-byte aligned for the TMA descriptors (bf16, unit inner stride)."""
+    return t.dim() == 2 and t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
 
 
 def linear_fwd(x2d: torch.Tensor, w: torch.Tensor, resid: Optional[torch.Tensor] = None) -> torch.Tensor:

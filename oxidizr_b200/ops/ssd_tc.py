@@ -86,3 +86,73 @@ def mamba3_tc(x, dt, A, Bm, Cm, lam):
     g2 = torch.stack([beta, gamma], 2).reshape(Bsz, 2 * S, H)
     y2 = SSDChunkTC.apply(x2, B2, C2, la2, g2)
     return y2.view(Bsz, S, 2, H, P)[:, :, 1]
+
+
+class Mamba3BC(torch.autograd.Function):
+    """Fused Mamba3 B/C prologue (csrc/mamba3.cu): rmsnorm(B_raw) w + b_bias, complex RoPE by
+    ``ang``, written as the interleaved [B, 2S, H, N] tensors of the two-term tensor-core scan
+    (same for C with c_bias).  braw/craw [B, S, G*N] bf16 (views of the input projection)."""
+
+    @staticmethod
+    def forward(ctx, braw, craw, w, bbias, cbias, ang, H: int, eps: float):
+        Bsz, S, GN = braw.shape
+        G = GN // 128
+        b2d, c2d = braw.reshape(Bsz * S, GN), craw.reshape(Bsz * S, GN)
+        angc = ang.float().contiguous()
+        b2, c2 = ext().m3_bc_fwd(b2d, c2d, w.contiguous(), bbias.contiguous(), cbias.contiguous(), angc, Bsz, S, H,
+                                 G, eps)
+        ctx.save_for_backward(b2d, c2d, w, bbias, cbias, angc)
+        ctx.cfg = (Bsz, S, H, G, eps, braw.shape)
+        return b2, c2
+
+    @staticmethod
+    def backward(ctx, db2, dc2):
+        b2d, c2d, w, bbias, cbias, angc = ctx.saved_tensors
+        Bsz, S, H, G, eps, shape = ctx.cfg
+        z = lambda t: torch.zeros(Bsz, 2 * S, H, 128, device=angc.device) if t is None else t.float().contiguous()
+        dbr, dcr, dw, dbb, dcb, dang = ext().m3_bc_bwd(b2d, c2d, w.contiguous(), bbias.contiguous(),
+                                                       cbias.contiguous(), angc, z(db2), z(dc2), Bsz, S, H, G, eps)
+        return (dbr.view(shape).to(b2d.dtype), dcr.view(shape).to(c2d.dtype), dw.to(w.dtype), dbb.to(bbias.dtype),
+                dcb.to(cbias.dtype), dang, None, None)
+
+
+def m3_bc_ok(braw: torch.Tensor, N: int, H: int, G: int) -> bool:
+    return (braw.is_cuda and braw.dtype == torch.bfloat16 and N == 128 and H % G == 0
+            and hasattr(ext(), "m3_bc_fwd"))
+
+
+def mamba3_tc_interleaved(x, dt, A, b2, c2, lam):
+    """Mamba3 two-term scan with B/C already in the interleaved layout (from Mamba3BC)."""
+    Bsz, S, H, P = x.shape
+    dtf, lamf = dt.float(), lam.float()
+    loga = A.float()[None, None, :] * dtf
+    gamma = lamf * dtf
+    beta = (1 - lamf) * dtf * torch.exp(loga)
+    x_prev = torch.cat([torch.zeros_like(x[:, :1]), x[:, :-1]], 1)
+    x2 = torch.stack([x_prev, x], 2).reshape(Bsz, 2 * S, H, P)
+    la2 = torch.stack([loga, torch.zeros_like(loga)], 2).reshape(Bsz, 2 * S, H)
+    g2 = torch.stack([beta, gamma], 2).reshape(Bsz, 2 * S, H)
+    y2 = SSDChunkTC.apply(x2, b2, c2, la2, g2)
+    return y2.view(Bsz, S, 2, H, P)[:, :, 1]
+
+
+class AngleCumsum(torch.autograd.Function):
+    """ang[b, t, h, j] = sum_{u <= t} theta[b, u, h, j] dt[b, u, h] (csrc/cumsum.cu)."""
+
+    @staticmethod
+    def forward(ctx, theta, dt):
+        th, d = theta.float().contiguous(), dt.float().contiguous()
+        ctx.save_for_backward(th, d)
+        return ext().angle_cumsum(th, d)
+
+    @staticmethod
+    def backward(ctx, dang):
+        th, d = ctx.saved_tensors
+        dtheta, ddt = ext().angle_cumsum_bwd(th, d, dang.float().contiguous())
+        return dtheta, ddt
+
+
+def angle_cumsum(theta, dt):
+    if theta.is_cuda and theta.shape[-1] % 32 == 0 and hasattr(ext(), "angle_cumsum"):
+        return AngleCumsum.apply(theta, dt)
+    return torch.cumsum(theta * dt[..., None], 1)

@@ -114,17 +114,24 @@ class EPGroup:
 class EPLayerBuffers:
     """The symmetric receive/output buffers of one MoE layer (grown collectively)."""
 
+    # receive-buffer growth is a collective (IPC handle exchange), so it must be
+    # rare: the first size leaves room for routing imbalance, growth is 1.5x
+    HEADROOM = 1.5
+    reallocs = 0  # class-wide count, reported by the benchmark
+
     def __init__(self, grp: EPGroup, H: int):
         self.grp, self.H = grp, H
         self.cap = 0
         self.bufs = None
 
-    def ensure(self, rows: int):
+    def ensure(self, rows: int, balanced_rows: int = 0):
         if rows <= self.cap:
             return
         from .fused_ar import SymmetricBuffer
         g = self.grp
-        cap = max(128, (int(rows * 1.15) + 127) // 128 * 128)
+        want = max(rows * self.HEADROOM, balanced_rows * self.HEADROOM, self.cap * self.HEADROOM)
+        cap = max(128, (int(want) + 1023) // 1024 * 1024)
+        EPLayerBuffers.reallocs += 1
         torch.cuda.synchronize(g.device)
         if self.bufs is not None:
             for b in self.bufs.values():
@@ -174,7 +181,8 @@ class EPExperts(torch.autograd.Function):
         seq = g.next_seq()
         all_counts, seg, rc = e.ep_counts(counts.int().contiguous(), g.pad.ptr_table, g.pad_local, rank, W, seq, st,
                                           g.wait_ns)
-        buf.ensure(_rows_needed(all_counts.cpu(), W, El))
+        # every rank sees the same counts, so every rank takes the same (collective) decision
+        buf.ensure(_rows_needed(all_counts.cpu(), W, El), balanced_rows=T * topi.shape[1])
         cap = buf.cap
         xr = buf.local("xrecv", torch.bfloat16, H)
         yo = buf.local("yout", torch.bfloat16, H)

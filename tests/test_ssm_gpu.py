@@ -155,3 +155,85 @@ def test_ssd_tensor_core_mamba3(B, S, H, P):
     for name, g, r in zip(("x", "dt", "A", "B", "C", "lam"), (x.grad, dt.grad, A.grad, Bm.grad, Cm.grad, lam.grad),
                           [t.grad for t in ins]):
         assert _rel(g, r) < 3e-2, (name, _rel(g, r))
+
+
+def test_mamba3_fused_prologue_matches_unfused():
+    """Mamba3 mixer: fused B/C prologue + interleaved tensor-core scan == the unfused torch path."""
+    from oxidizr_b200.config import ModelConfig, _build
+    from oxidizr_b200.models.mamba import Mamba3Mixer
+    torch.manual_seed(0)
+    cfg = _build(ModelConfig, {
+        "name": "m3", "hidden_size": 256, "num_layers": 1, "num_heads": 4, "vocab_size": 100, "max_seq_len": 128,
+        "rope_theta": 10000.0, "mamba_layers": [0], "mamba3_enabled": True, "mamba3_complex_rope": True,
+        "mamba3_mimo_rank": 2, "mamba3_use_conv": False, "mamba2_num_heads": 4, "mamba2_head_dim": 128,
+        "mamba2_state_size": 128, "mamba2_chunk_size": 64, "mamba2_n_groups": 1, "mamba2_expand": 2}, "model")
+    mix = Mamba3Mixer(cfg, device="cuda", dtype=torch.bfloat16)
+    mix.reset_parameters(0.05, torch.Generator(device="cuda").manual_seed(1))
+    with torch.no_grad():
+        mix.b_bias.add_(0.1 * torch.randn_like(mix.b_bias))
+        mix.bc_norm.weight.add_(0.1 * torch.randn_like(mix.bc_norm.weight))
+    h = torch.randn(2, 128, 256, device="cuda").bfloat16().requires_grad_()
+    resid = torch.zeros(2, 128, 256, device="cuda").bfloat16()
+    assert mix._fused_ok(h, h[..., :1], 128)
+    y1 = mix(h, resid)
+    dy = torch.randn_like(y1)
+    g1 = torch.autograd.grad(y1, [h] + list(mix.parameters()), dy, allow_unused=True)
+    mix._fused_ok = lambda *a: False
+    y2 = mix(h, resid)
+    g2 = torch.autograd.grad(y2, [h] + list(mix.parameters()), dy, allow_unused=True)
+    assert _rel(y1, y2) < 3e-2, _rel(y1, y2)
+    names = ["h"] + [n for n, _ in mix.named_parameters()]
+    for n, a, b in zip(names, g1, g2):
+        if a is None or b is None:
+            assert a is None and b is None, n
+            continue
+        assert _rel(a, b) < 5e-2, (n, _rel(a, b))
+
+
+def test_angle_cumsum_kernel():
+    from oxidizr_b200.ops.ssd_tc import AngleCumsum
+    torch.manual_seed(5)
+    theta = torch.randn(2, 300, 3, 64, device="cuda").requires_grad_()
+    dt = torch.rand(2, 300, 3, device="cuda").requires_grad_()
+    ang = AngleCumsum.apply(theta, dt)
+    g = torch.randn_like(ang)
+    ang.backward(g)
+    tr, dr = theta.detach().double().requires_grad_(), dt.detach().double().requires_grad_()
+    ref = torch.cumsum(tr * dr[..., None], 1)
+    ref.backward(g.double())
+    assert _rel(ang, ref) < 1e-5
+    assert _rel(theta.grad, tr.grad) < 1e-5
+    assert _rel(dt.grad, dr.grad) < 1e-5
+
+
+def test_mamba3_bc_prologue_kernel():
+    """Fused B/C prologue vs torch: rmsnorm + bias + rotation, interleaved layout, and grads."""
+    from oxidizr_b200.ops import reference as R
+    from oxidizr_b200.ops.ssd_tc import Mamba3BC
+    torch.manual_seed(7)
+    B, S, H, G, N = 2, 64, 4, 2, 128
+    wide = torch.randn(B, S, 2 * G * N + 8, device="cuda").bfloat16()
+    braw = wide[..., :G * N].detach().requires_grad_()
+    craw = wide[..., G * N:2 * G * N].detach().requires_grad_()
+    w = (1 + 0.1 * torch.randn(N, device="cuda")).bfloat16().requires_grad_()
+    bb = (1 + 0.1 * torch.randn(H, N, device="cuda")).bfloat16().requires_grad_()
+    cb = (1 + 0.1 * torch.randn(H, N, device="cuda")).bfloat16().requires_grad_()
+    ang = (3 * torch.randn(B, S, H, N // 2, device="cuda")).requires_grad_()
+    b2, c2 = Mamba3BC.apply(braw, craw, w, bb, cb, ang, H, 1e-6)
+    torch.cuda.synchronize()
+    gb, gc = torch.randn_like(b2, dtype=torch.float32), torch.randn_like(c2, dtype=torch.float32)
+    (b2.float() * gb + c2.float() * gc).sum().backward()
+    ins = [t.detach().double().requires_grad_() for t in (braw, craw, w, bb, cb, ang)]
+    rb, rc, rw, rbb, rcb, ra = ins
+    rep = lambda t: t.view(B, S, G, N).repeat_interleave(H // G, 2)
+    nb = R.rmsnorm(rep(rb), rw, 1e-6) + rbb
+    nc = R.rmsnorm(rep(rc), rw, 1e-6) + rcb
+    bt, ct = R.mamba3_rotate(nb, ra), R.mamba3_rotate(nc, ra)
+    zero = torch.zeros_like(bt[:, :1])
+    b2r = torch.stack([torch.cat([zero, bt[:, :-1]], 1), bt], 2).reshape(B, 2 * S, H, N)
+    c2r = torch.stack([torch.zeros_like(ct), ct], 2).reshape(B, 2 * S, H, N)
+    assert _rel(b2, b2r) < 1e-2 and _rel(c2, c2r) < 1e-2
+    (b2r * gb.double() + c2r * gc.double()).sum().backward()
+    for name, a, r in zip(("braw", "craw", "w", "b_bias", "c_bias", "ang"),
+                          (braw.grad, craw.grad, w.grad, bb.grad, cb.grad, ang.grad), [t.grad for t in ins]):
+        assert _rel(a, r) < 2e-2, (name, _rel(a, r))
