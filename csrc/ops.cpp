@@ -11,6 +11,7 @@
 #include "kernels_ssm.h"
 #include "kernels_moe.h"
 #include "kernels_ep.h"
+#include "host_util.h"
 
 using oxi::Mat;
 
@@ -858,7 +859,12 @@ void gemm_grouped(int64_t mode, int64_t epi, torch::Tensor a, bool a_mn, torch::
 
 }  // namespace
 
+// Raises through the launchers' own error path (no CUDA involved), so a test
+// can check that a failed host-side check reaches Python as an exception.
+void host_check_selftest(int64_t v) { OXI_CHECK(v == 0, "value ", v, " of ", 2.5, " ", true); }
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("host_check_selftest", &host_check_selftest, "raise via the launcher error path unless v == 0");
   m.doc() = "oxidizr_b200 sm_100a kernels";
   m.def("gemm", &gemm, "tcgen05 GEMM out = alpha * a @ b^T (+resid | + beta*out)");
   m.def("gemm_swiglu", &gemm_swiglu, "GEMM with fused SwiGLU epilogue");

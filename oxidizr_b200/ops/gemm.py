@@ -27,21 +27,9 @@ def mm(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = False
     """
     M = a.shape[1] if a_t else a.shape[0]
     N = b.shape[1] if b_t else b.shape[0]
-    if a.is_cuda and not (_tma_ok(a) and _tma_ok(b)):
-        # TMA needs 16-byte aligned rows: tiny or odd-width projections (e.g. a few
-        # per-head scalars) go through a plain matmul
-        A = a.t() if a_t else a
-        B = b.t() if b_t else b
-        r = alpha * (A.float() @ B.float().t())
-        if resid is not None:
-            r = r + resid.float()
-        if out is not None:
-            if beta != 0.0:
-                r = r + beta * out.float()
-            out.copy_(r.to(out.dtype))
-            return out
-        return r.to(out_dtype)
-    if not a.is_cuda:
+    if not a.is_cuda or not (_tma_ok(a) and _tma_ok(b)):
+        # CPU, or rows that are not 16-byte aligned for the TMA descriptors (a
+        # projection to a few per-head scalars): plain fp32-accumulated matmul
         A = a.t() if a_t else a
         B = b.t() if b_t else b
         r = alpha * (A.float() @ B.float().t())
