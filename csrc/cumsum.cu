@@ -1,3 +1,4 @@
+// Sequence scans of the Mamba3 / SSD glue.
 // Mamba3 rotation angles: ang[b, t, c] = sum_{u <= t} theta[b, u, c] * dt[b, u, c / J]
 // (mamba3.rs:490, cumsum over the whole sequence), and its backward
 //   R[t] = sum_{u >= t} dang[u];  dtheta[t] = dt[t] R[t];  ddt[t] = sum_j theta[t, j] R[t, j].
@@ -91,7 +92,58 @@ __global__ void ang_scan_bwd(const float* __restrict__ theta, const float* __res
   }
 }
 
+// w_t = e_t - ga_{t+1} dg_{t+1} (0 past the end); thread -> (b, chunk, h)
+__device__ __forceinline__ float dloga_w(const float* e, const float* ga, const float* dg, int64_t row, int t, int S,
+                                         int H, int h) {
+  float w = e[row * H + h];
+  if (t + 1 < S) w -= ga[(row + 1) * H + h] * dg[(row + 1) * H + h];
+  return w;
+}
+
+__global__ void dloga_chunk_sums(const float* __restrict__ e, const float* __restrict__ ga,
+                                 const float* __restrict__ dg, int B, int S, int H, int nseg,
+                                 float* __restrict__ sums) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)B * nseg * H) return;
+  const int h = (int)(i % H);
+  const int64_t bs = i / H;
+  const int seg = (int)(bs % nseg);
+  const int b = (int)(bs / nseg);
+  float acc = 0.f;
+  const int t0 = seg * SEG, t1 = min(S, t0 + SEG);
+  for (int t = t0; t < t1; ++t) acc += dloga_w(e, ga, dg, (int64_t)b * S + t, t, S, H, h);
+  sums[i] = acc;
+}
+
+__global__ void dloga_scan(const float* __restrict__ e, const float* __restrict__ ga, const float* __restrict__ dg,
+                           const float* __restrict__ sums, int B, int S, int H, int nseg, float* __restrict__ dla) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)B * nseg * H) return;
+  const int h = (int)(i % H);
+  const int64_t bs = i / H;
+  const int seg = (int)(bs % nseg);
+  const int b = (int)(bs / nseg);
+  float acc = 0.f;
+  for (int k = seg + 1; k < nseg; ++k) acc += sums[((int64_t)b * nseg + k) * H + h];
+  const int t0 = seg * SEG, t1 = min(S, t0 + SEG);
+  for (int t = t1 - 1; t >= t0; --t) {
+    const int64_t row = (int64_t)b * S + t;
+    acc += dloga_w(e, ga, dg, row, t, S, H, h);
+    dla[row * H + h] = acc - ga[row * H + h] * dg[row * H + h];
+  }
+}
+
 }  // namespace
+
+void launch_ssd_dloga(const float* e, const float* ga, const float* dg, int B, int S, int H, float* sums, float* dla,
+                      cudaStream_t st) {
+  const int nseg = (S + SEG - 1) / SEG;
+  const int64_t total = (int64_t)B * nseg * H;
+  const unsigned grid = (unsigned)((total + 127) / 128);
+  dloga_chunk_sums<<<grid, 128, 0, st>>>(e, ga, dg, B, S, H, nseg, sums);
+  dloga_scan<<<grid, 128, 0, st>>>(e, ga, dg, sums, B, S, H, nseg, dla);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
 
 void launch_angle_cumsum(const float* theta, const float* dt, int B, int S, int H, int J, float* sums, float* ang,
                          cudaStream_t st) {

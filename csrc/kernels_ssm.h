@@ -64,18 +64,19 @@ void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st);
 }  // namespace oxi
 
 namespace oxi {
-// Mamba3 B/C prologue (mamba3.cu): rmsnorm + bias + complex RoPE, written in
-// the interleaved two-term layout b2/c2 bf16 [B, 2S, H, N] of the tensor-core
-// scan.  braw/craw bf16 rows of stride ldr (group g at column g*N); ang f32
-// [B, S, H, N/2].  Backward: dbraw/dcraw f32 rows of stride ldd; dw [N],
-// dbb/dcb [H, N] accumulated (zero them); dang f32 [B, S, H, N/2].
+// Mamba3 B/C prologue (mamba3.cu): rmsnorm + bias + complex RoPE, written as
+// per-head bf16 B_rot / C_rot [B, S, H, N] plus bcdot f32 [B, S, H] =
+// <B_rot, C_rot>.  braw/craw bf16 rows of stride ldr (group g at column g*N);
+// ang f32 [B, S, H, N/2].  Backward: db/dc f32 [B, S, H, N], dbcdot f32
+// [B, S, H] or null; dbraw/dcraw f32 rows of stride ldd; dw [N], dbb/dcb
+// [H, N] accumulated (zero them); dang f32 [B, S, H, N/2].
 void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
-                      const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* b2,
-                      void* c2, cudaStream_t st);
+                      const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* bout,
+                      void* cout, float* bcdot, cudaStream_t st);
 void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
-                      const void* cbias, const float* ang, const float* db2, const float* dc2, int B, int S, int H,
-                      int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw, float* dbb,
-                      float* dcb, float* dang, cudaStream_t st);
+                      const void* cbias, const float* ang, const float* db, const float* dc, const float* dbcdot,
+                      int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw,
+                      float* dbb, float* dcb, float* dang, cudaStream_t st);
 }  // namespace oxi
 
 namespace oxi {
@@ -86,4 +87,9 @@ void launch_angle_cumsum(const float* theta, const float* dt, int B, int S, int 
                          cudaStream_t st);
 void launch_angle_cumsum_bwd(const float* theta, const float* dt, const float* dang, int B, int S, int H, int J,
                              float* sums, float* dtheta, float* ddt, cudaStream_t st);
+// SSD d loga from the identity q_t = e_t + q_{t+1} - v_{t+1}, dla_t = q_t - v_t
+// with v = gamma * dgamma: e, ga, dg, dla f32 [B, S, H]; sums scratch
+// [B * ceil(S/128) * H].
+void launch_ssd_dloga(const float* e, const float* ga, const float* dg, int B, int S, int H, float* sums, float* dla,
+                      cudaStream_t st);
 }  // namespace oxi

@@ -3,14 +3,14 @@
 //   Bn = rmsnorm(B_raw[group(h)]) * w + b_bias[h]      (over the state dim N)
 //   B_rot = rotate(Bn, ang[t, h])   pairs (2j, 2j+1) turned by ang[..., j]
 // and the same for C with c_bias.  The angles (a cumulative sum over time of
-// theta * dt) come in precomputed.  Outputs go straight into the interleaved
-// layout of the two-term scan on the tensor cores (2S steps per sequence):
-//   B2[2t+1] = B_rot_t, B2[2t+2] = B_rot_t (the B_{t-1} of step t+1), B2[0] = 0
-//   C2[2t+1] = C_rot_t, C2[2t] = 0
-// One warp per (token, head); each lane owns 4 consecutive state entries
-// (two rotation pairs) for N = 128.
+// theta * dt) come in precomputed.  Outputs: per-head B_rot, C_rot [B, S, H, N]
+// bf16 (the operands of the tensor-core scan) and bcdot[t, h] = <B_rot, C_rot>
+// of the bf16-rounded vectors, which the two-term scan needs for its diagonal
+// correction.  One warp per (token, head); each lane owns 4 consecutive state
+// entries (two rotation pairs) for N = 128.
 //
 // Backward (one warp per token, looping over the heads of each group):
+//   dB_rot += dbcdot C_rot, dC_rot += dbcdot B_rot
 //   d_rot -> d_n (inverse rotation), d ang = d_re * (-rot_im) + d_im * rot_re
 //   d b_bias[h] += d_n ; d w += d_n * raw / rms ; d raw = rmsnorm-backward(sum_h w d_n)
 #include <cuda_bf16.h>
@@ -41,6 +41,10 @@ __device__ __forceinline__ void load4(const __nv_bfloat16* p, float* v) {
 __device__ __forceinline__ void store4(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
 }
+__device__ __forceinline__ void round4(float* v) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(__float2bfloat16(v[i]));
+}
 
 // raw [4] -> rotated [4] for one lane; returns nothing, fills out
 __device__ __forceinline__ void norm_bias_rot(const float* raw, float rinv, const float* w, const float* bias,
@@ -60,8 +64,9 @@ __global__ void __launch_bounds__(256) m3_bc_fwd_kernel(const __nv_bfloat16* __r
                                                         const __nv_bfloat16* __restrict__ bbias,
                                                         const __nv_bfloat16* __restrict__ cbias,
                                                         const float* __restrict__ ang, int Bsz, int S, int H, int G,
-                                                        float eps, __nv_bfloat16* __restrict__ b2,
-                                                        __nv_bfloat16* __restrict__ c2) {
+                                                        float eps, __nv_bfloat16* __restrict__ bout,
+                                                        __nv_bfloat16* __restrict__ cout,
+                                                        float* __restrict__ bcdot) {
   const int lane = threadIdx.x & 31;
   const int64_t items = (int64_t)Bsz * S * H;
   const int hpg = H / G;
@@ -89,25 +94,24 @@ __global__ void __launch_bounds__(256) m3_bc_fwd_kernel(const __nv_bfloat16* __r
     float ob[4], oc[4];
     norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
     norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);
-    // interleaved rows: token t -> steps 2t (decay + B_{t-1} term) and 2t+1 (B_t term)
-    const int64_t r_odd = (b * 2 * S + 2 * t + 1) * H + h;
-    store4(b2 + r_odd * M3N + lane * 4, ob);
-    store4(c2 + r_odd * M3N + lane * 4, oc);
-    const float z[4] = {0.f, 0.f, 0.f, 0.f};
-    store4(c2 + (r_odd - H) * M3N + lane * 4, z);
-    if (t + 1 < S) store4(b2 + (r_odd + H) * M3N + lane * 4, ob);
-    if (t == 0) store4(b2 + (r_odd - H) * M3N + lane * 4, z);
+    round4(ob);
+    round4(oc);
+    store4(bout + it * M3N + lane * 4, ob);
+    store4(cout + it * M3N + lane * 4, oc);
+    const float d = warp_sum(ob[0] * oc[0] + ob[1] * oc[1] + ob[2] * oc[2] + ob[3] * oc[3]);
+    if (lane == 0) bcdot[it] = d;
   }
 }
 
-// db2/dc2: f32 gradients of the interleaved tensors [B, 2S, H, N].
+// db/dc: f32 gradients of B_rot / C_rot [B, S, H, N]; dbcdot [B, S, H] (may be null).
 __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __restrict__ braw,
                                                         const __nv_bfloat16* __restrict__ craw, int64_t ldr,
                                                         const __nv_bfloat16* __restrict__ w,
                                                         const __nv_bfloat16* __restrict__ bbias,
                                                         const __nv_bfloat16* __restrict__ cbias,
                                                         const float* __restrict__ ang, const float* __restrict__ db2,
-                                                        const float* __restrict__ dc2, int Bsz, int S, int H, int G,
+                                                        const float* __restrict__ dc2,
+                                                        const float* __restrict__ dbcdot, int Bsz, int S, int H, int G,
                                                         float eps, float* __restrict__ dbraw, float* __restrict__ dcraw,
                                                         int64_t ldd, float* __restrict__ dw, float* __restrict__ dbb,
                                                         float* __restrict__ dcb, float* __restrict__ dang) {
@@ -124,8 +128,6 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
   float dw_acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int64_t bt = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; bt < tokens;
        bt += (int64_t)gridDim.x * (blockDim.x / 32)) {
-    const int t = (int)(bt % S);
-    const int64_t b = bt / S;
     for (int g = 0; g < G; ++g) {
       float rb[4], rc[4];
       load4(braw + bt * ldr + g * M3N + lane * 4, rb);
@@ -137,15 +139,10 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
       for (int hh = 0; hh < hpg; ++hh) {
         const int h = g * hpg + hh;
         const int64_t it = bt * H + h;
-        const int64_t r_odd = (b * 2 * S + 2 * t + 1) * H + h;
-        const float4 d1 = *reinterpret_cast<const float4*>(db2 + r_odd * M3N + lane * 4);
+        const float4 d1 = *reinterpret_cast<const float4*>(db2 + it * M3N + lane * 4);
         float dB[4] = {d1.x, d1.y, d1.z, d1.w};
-        if (t + 1 < S) {
-          const float4 d2 = *reinterpret_cast<const float4*>(db2 + (r_odd + H) * M3N + lane * 4);
-          dB[0] += d2.x; dB[1] += d2.y; dB[2] += d2.z; dB[3] += d2.w;
-        }
-        const float4 d3 = *reinterpret_cast<const float4*>(dc2 + r_odd * M3N + lane * 4);
-        const float dC[4] = {d3.x, d3.y, d3.z, d3.w};
+        const float4 d3 = *reinterpret_cast<const float4*>(dc2 + it * M3N + lane * 4);
+        float dC[4] = {d3.x, d3.y, d3.z, d3.w};
         float bb[4], cb[4];
         load4(bbias + h * M3N + lane * 4, bb);
         load4(cbias + h * M3N + lane * 4, cb);
@@ -156,6 +153,17 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
         float ob[4], oc[4];
         norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
         norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);
+        if (dbcdot) {
+          float rob[4] = {ob[0], ob[1], ob[2], ob[3]}, roc[4] = {oc[0], oc[1], oc[2], oc[3]};
+          round4(rob);
+          round4(roc);
+          const float g = dbcdot[it];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            dB[i] += g * roc[i];
+            dC[i] += g * rob[i];
+          }
+        }
         // d angle of both pairs (B and C share the angles)
         const float da0 = dB[0] * (-ob[1]) + dB[1] * ob[0] + dC[0] * (-oc[1]) + dC[1] * oc[0];
         const float da1 = dB[2] * (-ob[3]) + dB[3] * ob[2] + dC[2] * (-oc[3]) + dC[3] * oc[2];
@@ -213,20 +221,20 @@ unsigned grid_of(int64_t warps_needed) {
 }  // namespace
 
 void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
-                      const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* b2,
-                      void* c2, cudaStream_t st) {
+                      const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* bout,
+                      void* cout, float* bcdot, cudaStream_t st) {
   OXI_CHECK(N == M3N && H % G == 0 && ldr % 4 == 0, "Mamba3 B/C prologue supports state size 128");
   m3_bc_fwd_kernel<<<grid_of((int64_t)B * S * H), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(braw), reinterpret_cast<const __nv_bfloat16*>(craw), ldr,
       reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<const __nv_bfloat16*>(bbias),
-      reinterpret_cast<const __nv_bfloat16*>(cbias), ang, B, S, H, G, eps, reinterpret_cast<__nv_bfloat16*>(b2),
-      reinterpret_cast<__nv_bfloat16*>(c2));
+      reinterpret_cast<const __nv_bfloat16*>(cbias), ang, B, S, H, G, eps, reinterpret_cast<__nv_bfloat16*>(bout),
+      reinterpret_cast<__nv_bfloat16*>(cout), bcdot);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
-                      const void* cbias, const float* ang, const float* db2, const float* dc2, int B, int S, int H,
-                      int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw, float* dbb,
+                      const void* cbias, const float* ang, const float* db2, const float* dc2, const float* dbcdot,
+                      int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw, float* dbb,
                       float* dcb, float* dang, cudaStream_t st) {
   OXI_CHECK(N == M3N && H % G == 0 && H <= 64, "Mamba3 B/C prologue supports state size 128, <= 64 heads");
   const int64_t blocks = std::min<int64_t>(((int64_t)B * S + 7) / 8, 148 * 4);
@@ -236,7 +244,7 @@ void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const voi
   m3_bc_bwd_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, smem, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(braw), reinterpret_cast<const __nv_bfloat16*>(craw), ldr,
       reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<const __nv_bfloat16*>(bbias),
-      reinterpret_cast<const __nv_bfloat16*>(cbias), ang, db2, dc2, B, S, H, G, eps, dbraw, dcraw, ldd, dw, dbb, dcb,
+      reinterpret_cast<const __nv_bfloat16*>(cbias), ang, db2, dc2, dbcdot, B, S, H, G, eps, dbraw, dcraw, ldd, dw, dbb, dcb,
       dang);
   OXI_CUDA_CHECK(cudaGetLastError());
 }

@@ -564,20 +564,29 @@ std::vector<torch::Tensor> m3_bc_fwd(torch::Tensor braw, torch::Tensor craw, tor
   TORCH_CHECK(w.is_contiguous() && bbias.is_contiguous() && cbias.is_contiguous() &&
                   w.scalar_type() == torch::kBFloat16 && bbias.scalar_type() == torch::kBFloat16 &&
                   cbias.scalar_type() == torch::kBFloat16, "bc_norm weight / biases: bf16 contiguous");
-  auto b2 = torch::empty({B, 2 * S, H, 128}, braw.options());
-  auto c2 = torch::empty({B, 2 * S, H, 128}, braw.options());
+  auto bo = torch::empty({B, S, H, 128}, braw.options());
+  auto co = torch::empty({B, S, H, 128}, braw.options());
+  auto dot = torch::empty({B, S, H}, braw.options().dtype(torch::kFloat32));
   oxi::launch_m3_bc_fwd(braw.data_ptr(), craw.data_ptr(), braw.stride(0), w.data_ptr(), bbias.data_ptr(),
                         cbias.data_ptr(), ang.data_ptr<float>(), (int)B, (int)S, (int)H, (int)G, 128, (float)eps,
-                        b2.data_ptr(), c2.data_ptr(), stream());
-  return {b2, c2};
+                        bo.data_ptr(), co.data_ptr(), dot.data_ptr<float>(), stream());
+  return {bo, co, dot};
 }
 
 std::vector<torch::Tensor> m3_bc_bwd(torch::Tensor braw, torch::Tensor craw, torch::Tensor w, torch::Tensor bbias,
-                                     torch::Tensor cbias, torch::Tensor ang, torch::Tensor db2, torch::Tensor dc2,
-                                     int64_t B, int64_t S, int64_t H, int64_t G, double eps) {
+                                     torch::Tensor cbias, torch::Tensor ang, torch::Tensor db, torch::Tensor dc,
+                                     c10::optional<torch::Tensor> dbcdot, int64_t B, int64_t S, int64_t H, int64_t G,
+                                     double eps) {
   c10::cuda::CUDAGuard g(braw.device());
-  TORCH_CHECK(db2.scalar_type() == torch::kFloat32 && dc2.scalar_type() == torch::kFloat32 && db2.is_contiguous() &&
-                  dc2.is_contiguous() && db2.numel() == B * 2 * S * H * 128, "db2 / dc2: f32 contiguous [B, 2S, H, N]");
+  TORCH_CHECK(db.scalar_type() == torch::kFloat32 && dc.scalar_type() == torch::kFloat32 && db.is_contiguous() &&
+                  dc.is_contiguous() && db.numel() == B * S * H * 128 && dc.numel() == db.numel(),
+              "db / dc: f32 contiguous [B, S, H, N]");
+  const float* dd = nullptr;
+  if (dbcdot.has_value() && dbcdot->defined()) {
+    TORCH_CHECK(dbcdot->scalar_type() == torch::kFloat32 && dbcdot->is_contiguous() && dbcdot->numel() == B * S * H,
+                "dbcdot: f32 contiguous [B, S, H]");
+    dd = dbcdot->data_ptr<float>();
+  }
   auto f32 = braw.options().dtype(torch::kFloat32);
   auto dbraw = torch::empty({B * S, G * 128}, f32);
   auto dcraw = torch::empty({B * S, G * 128}, f32);
@@ -586,11 +595,25 @@ std::vector<torch::Tensor> m3_bc_bwd(torch::Tensor braw, torch::Tensor craw, tor
   auto dcb = torch::zeros({H, 128}, f32);
   auto dang = torch::empty({B, S, H, 64}, f32);
   oxi::launch_m3_bc_bwd(braw.data_ptr(), craw.data_ptr(), braw.stride(0), w.data_ptr(), bbias.data_ptr(),
-                        cbias.data_ptr(), ang.data_ptr<float>(), db2.data_ptr<float>(), dc2.data_ptr<float>(), (int)B,
-                        (int)S, (int)H, (int)G, 128, (float)eps, dbraw.data_ptr<float>(), dcraw.data_ptr<float>(),
-                        dbraw.stride(0), dw.data_ptr<float>(), dbb.data_ptr<float>(), dcb.data_ptr<float>(),
-                        dang.data_ptr<float>(), stream());
+                        cbias.data_ptr(), ang.data_ptr<float>(), db.data_ptr<float>(), dc.data_ptr<float>(), dd,
+                        (int)B, (int)S, (int)H, (int)G, 128, (float)eps, dbraw.data_ptr<float>(),
+                        dcraw.data_ptr<float>(), dbraw.stride(0), dw.data_ptr<float>(), dbb.data_ptr<float>(),
+                        dcb.data_ptr<float>(), dang.data_ptr<float>(), stream());
   return {dbraw, dcraw, dw, dbb, dcb, dang};
+}
+
+torch::Tensor ssd_dloga(torch::Tensor e, torch::Tensor ga, torch::Tensor dg) {
+  c10::cuda::CUDAGuard g(e.device());
+  TORCH_CHECK(e.dim() == 3 && e.scalar_type() == torch::kFloat32 && e.is_contiguous() && ga.sizes() == e.sizes() &&
+                  dg.sizes() == e.sizes() && ga.scalar_type() == torch::kFloat32 &&
+                  dg.scalar_type() == torch::kFloat32 && ga.is_contiguous() && dg.is_contiguous(),
+              "e / gamma / dgamma: f32 contiguous [B, S, H]");
+  const int64_t B = e.size(0), S = e.size(1), H = e.size(2);
+  auto dla = torch::empty_like(e);
+  auto sums = torch::empty({B * ((S + 127) / 128) * H}, e.options());
+  oxi::launch_ssd_dloga(e.data_ptr<float>(), ga.data_ptr<float>(), dg.data_ptr<float>(), (int)B, (int)S, (int)H,
+                        sums.data_ptr<float>(), dla.data_ptr<float>(), stream());
+  return dla;
 }
 
 // ------------------------------------------------------------ Mamba3 angles
@@ -891,7 +914,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ssd_tc_bwd", &ssd_tc_bwd, "tensor-core chunked SSD backward");
   m.def("angle_cumsum", &angle_cumsum, "Mamba3 rotation angles: cumsum over time of theta * dt");
   m.def("angle_cumsum_bwd", &angle_cumsum_bwd, "backward of angle_cumsum");
-  m.def("m3_bc_fwd", &m3_bc_fwd, "Mamba3 B/C norm + bias + complex RoPE into the interleaved scan layout");
+  m.def("m3_bc_fwd", &m3_bc_fwd, "Mamba3 B/C norm + bias + complex RoPE (+ <B, C> per head)");
+  m.def("ssd_dloga", &ssd_dloga, "SSD d loga reverse scan");
   m.def("m3_bc_bwd", &m3_bc_bwd, "backward of m3_bc_fwd");
   m.def("ssm_scan_fwd", &ssm_scan_fwd, "Mamba2/3 selective scan forward");
   m.def("ssm_scan_bwd", &ssm_scan_bwd, "Mamba2/3 selective scan backward");

@@ -319,13 +319,16 @@ class Mamba3Mixer(RefModule):
                 ang = angle_cumsum(theta, dtv)
             else:
                 ang = torch.zeros(B, S, self.Hs, self.N // 2, device=h.device)
-            b2, c2 = Mamba3BC.apply(Bm, Cm, self.bc_norm.weight, self.b_bias, self.c_bias, ang, self.Hs, 1e-6)
+            bro, cro, bcdot = Mamba3BC.apply(Bm, Cm, self.bc_norm.weight, self.b_bias, self.c_bias, ang, self.Hs,
+                                             1e-6)
             xh = x.reshape(B, S, self.Hs, self.P)
             if self.mimo_x_up is not None:
                 xh = self.mimo_x_up(xh)
-            from ..ops.ssd_tc import mamba3_tc_interleaved
-            y = mamba3_tc_interleaved(xh, dtv, self.A(), b2, c2, lam)
-            return self._finish(y, xh, gate, h, resid, B, S)
+            from ..ops.ssd_tc import mamba3_tc_k
+            y, c = mamba3_tc_k(xh, dtv, self.A(), bro, cro, lam)
+            # the shifted-state diagonal correction rides on the D skip
+            dskip = self.D.float()[None, None, :] - c * bcdot
+            return self._finish(y, xh, gate, h, resid, B, S, dskip)
         Bm = Bm.reshape(B, S, self.g, self.N)
         Cm = Cm.reshape(B, S, self.g, self.N)
         rep = self.Hs // self.g
@@ -353,10 +356,14 @@ class Mamba3Mixer(RefModule):
         from ..ops.ssd_tc import m3_bc_ok, tc_ok
         width = self.P * (self.R if self.mimo_x_up is not None else 1)
         probe = x.new_empty(1, 1, 1, width)
-        return m3_bc_ok(x, self.N, self.Hs, self.g) and tc_ok(probe, self.N, 2 * S)
+        return m3_bc_ok(x, self.N, self.Hs, self.g) and tc_ok(probe, self.N, S)
 
-    def _finish(self, y, xh, gate, h, resid, B, S):
-        y = y.float() + xh.float() * self.D.float()[:, None]
+    def _finish(self, y, xh, gate, h, resid, B, S, dskip=None):
+        """y + D x (``dskip`` [B, S, H] overrides the per-head D), mimo down, gated norm, out_proj."""
+        if dskip is None:
+            y = y.float() + xh.float() * self.D.float()[:, None]
+        else:
+            y = y.float() + xh.float() * dskip[..., None]
         y = y.to(h.dtype)
         if self.mimo_x_down is not None:
             y = self.mimo_x_down(y)

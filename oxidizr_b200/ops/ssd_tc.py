@@ -9,10 +9,14 @@ backward runs a reverse pass (dx, state adjoints) and a chunk-parallel pass
 scan: with q_t = <G_t, H_t> (G the state adjoint), q_t = <dy_t, y_t> + q_{t+1}
 - v_{t+1} and d loga_t = q_t - v_t, v_t = gamma_t d gamma_t.
 
-Mamba3 (mamba3.rs:638-752) updates H_t = alpha_t H_{t-1} + gamma_t B_t x_t^T +
-beta_t B_{t-1} x_{t-1}^T.  ``mamba3_tc`` runs it as the single-term recurrence
-on 2S steps: step 2t adds beta_t B_{t-1} x_{t-1}^T after the decay alpha_t,
-step 2t+1 adds gamma_t B_t x_t^T with no decay; y_t is read at step 2t+1.
+Mamba3 (mamba3.rs:638-752) updates H_t = alpha_t H_{t-1} + gamma_t u_t +
+beta_t u_{t-1} with u_t = B_t x_t^T and beta_t = (1 - lam_t) dt_t alpha_t.  With
+c_t = beta_{t+1} / alpha_{t+1} = (1 - lam_{t+1}) dt_{t+1} (c_{S-1} = 0) the
+shifted state K_t = H_t + c_t u_t obeys the single-term recurrence
+K_t = alpha_t K_{t-1} + (gamma_t + c_t) u_t, and y_t = C_t^T H_t =
+C_t^T K_t - c_t <B_t, C_t> x_t.  ``mamba3_tc`` therefore runs the tensor-core
+scan once over S steps with gamma' = gamma + c and folds the diagonal
+correction into the D skip: no division by alpha, no extra sequence steps.
 """
 from __future__ import annotations
 
@@ -53,13 +57,14 @@ class SSDChunkTC(torch.autograd.Function):
         dyf = dy.float().reshape(Bsz * S, H * P)
         dyb = dyf.to(torch.bfloat16).contiguous()
         dx, dB, dC, dg = ext().ssd_tc_bwd(x2, B2, C2, la, ga, hs, dyb, Bsz, S, H, P, G, status(dy.device))
-        dB = dB.view(Bsz, S, G, H // G, N).sum(3)
-        dC = dC.view(Bsz, S, G, H // G, N).sum(3)
+        if G < H:
+            dB = dB.view(Bsz, S, G, H // G, N).sum(3)
+            dC = dC.view(Bsz, S, G, H // G, N).sum(3)
+        else:
+            dB = dB.view(Bsz, S, G, N)
+            dC = dC.view(Bsz, S, G, N)
         e = (dyf * y).view(Bsz, S, H, P).sum(-1)
-        v = ga * dg
-        v_next = torch.cat([v[:, 1:], torch.zeros_like(v[:, :1])], 1)
-        q = torch.flip(torch.cumsum(torch.flip(e - v_next, [1]), 1), [1])
-        dla = q - v
+        dla = ext().ssd_dloga(e.contiguous(), ga.view(Bsz, S, H), dg.view(Bsz, S, H).contiguous())
         xd, bd, cd = ctx.dtypes
         return dx.view(Bsz, S, H, P).to(xd), dB.to(bd), dC.to(cd), dla, dg
 
@@ -70,28 +75,35 @@ def ssd_tc(x, dt, A, Bm, Cm):
     return SSDChunkTC.apply(x, Bm, Cm, A.float()[None, None, :] * dtf, dtf)
 
 
-def mamba3_tc(x, dt, A, Bm, Cm, lam):
-    """Mamba3 trapezoidal two-term scan (no D skip) via the interleaved single-term form."""
-    Bsz, S, H, P = x.shape
-    N = Bm.shape[-1]
+def mamba3_coeffs(dt, A, lam):
+    """(loga, gamma', c) of the shifted single-term form, all f32 [B, S, H]."""
     dtf, lamf = dt.float(), lam.float()
     loga = A.float()[None, None, :] * dtf
-    gamma = lamf * dtf
-    beta = (1 - lamf) * dtf * torch.exp(loga)
-    pad = lambda t: torch.cat([torch.zeros_like(t[:, :1]), t[:, :-1]], 1)
-    x2 = torch.stack([pad(x), x], 2).reshape(Bsz, 2 * S, H, P)
-    B2 = torch.stack([pad(Bm), Bm], 2).reshape(Bsz, 2 * S, Bm.shape[2], N)
-    C2 = torch.stack([torch.zeros_like(Cm), Cm], 2).reshape(Bsz, 2 * S, Cm.shape[2], N)
-    la2 = torch.stack([loga, torch.zeros_like(loga)], 2).reshape(Bsz, 2 * S, H)
-    g2 = torch.stack([beta, gamma], 2).reshape(Bsz, 2 * S, H)
-    y2 = SSDChunkTC.apply(x2, B2, C2, la2, g2)
-    return y2.view(Bsz, S, 2, H, P)[:, :, 1]
+    w = (1 - lamf) * dtf
+    c = torch.cat([w[:, 1:], torch.zeros_like(w[:, :1])], 1)
+    return loga, lamf * dtf + c, c
+
+
+def mamba3_tc_k(x, dt, A, Bm, Cm, lam):
+    """Tensor-core scan of the shifted state: returns (y_K, c) with the Mamba3 output
+    y = y_K - (c <B, C>)[..., None] * x.  Bm/Cm per head [B, S, H, N] (bf16)."""
+    loga, gp, c = mamba3_coeffs(dt, A, lam)
+    return SSDChunkTC.apply(x, Bm, Cm, loga, gp), c
+
+
+def mamba3_tc(x, dt, A, Bm, Cm, lam):
+    """Mamba3 trapezoidal two-term scan (no D skip); Bm/Cm per head [B, S, H, N]."""
+    Bb, Cb = Bm.to(torch.bfloat16), Cm.to(torch.bfloat16)
+    y, c = mamba3_tc_k(x, dt, A, Bb, Cb, lam)
+    bcdot = (Bb.float() * Cb.float()).sum(-1)
+    return y - (c * bcdot)[..., None] * x.float()
 
 
 class Mamba3BC(torch.autograd.Function):
     """Fused Mamba3 B/C prologue (csrc/mamba3.cu): rmsnorm(B_raw) w + b_bias, complex RoPE by
-    ``ang``, written as the interleaved [B, 2S, H, N] tensors of the two-term tensor-core scan
-    (same for C with c_bias).  braw/craw [B, S, G*N] bf16 (views of the input projection)."""
+    ``ang``, as per-head bf16 [B, S, H, N] tensors (same for C with c_bias), plus
+    bcdot = <B_rot, C_rot> f32 [B, S, H].  braw/craw [B, S, G*N] bf16 (views of the input
+    projection)."""
 
     @staticmethod
     def forward(ctx, braw, craw, w, bbias, cbias, ang, H: int, eps: float):
@@ -99,19 +111,20 @@ class Mamba3BC(torch.autograd.Function):
         G = GN // 128
         b2d, c2d = braw.reshape(Bsz * S, GN), craw.reshape(Bsz * S, GN)
         angc = ang.float().contiguous()
-        b2, c2 = ext().m3_bc_fwd(b2d, c2d, w.contiguous(), bbias.contiguous(), cbias.contiguous(), angc, Bsz, S, H,
-                                 G, eps)
+        bo, co, dot = ext().m3_bc_fwd(b2d, c2d, w.contiguous(), bbias.contiguous(), cbias.contiguous(), angc, Bsz,
+                                      S, H, G, eps)
         ctx.save_for_backward(b2d, c2d, w, bbias, cbias, angc)
         ctx.cfg = (Bsz, S, H, G, eps, braw.shape)
-        return b2, c2
+        return bo, co, dot
 
     @staticmethod
-    def backward(ctx, db2, dc2):
+    def backward(ctx, db, dc, ddot):
         b2d, c2d, w, bbias, cbias, angc = ctx.saved_tensors
         Bsz, S, H, G, eps, shape = ctx.cfg
-        z = lambda t: torch.zeros(Bsz, 2 * S, H, 128, device=angc.device) if t is None else t.float().contiguous()
+        z = lambda t: torch.zeros(Bsz, S, H, 128, device=angc.device) if t is None else t.float().contiguous()
+        dd = None if ddot is None else ddot.float().contiguous()
         dbr, dcr, dw, dbb, dcb, dang = ext().m3_bc_bwd(b2d, c2d, w.contiguous(), bbias.contiguous(),
-                                                       cbias.contiguous(), angc, z(db2), z(dc2), Bsz, S, H, G, eps)
+                                                       cbias.contiguous(), angc, z(db), z(dc), dd, Bsz, S, H, G, eps)
         return (dbr.view(shape).to(b2d.dtype), dcr.view(shape).to(c2d.dtype), dw.to(w.dtype), dbb.to(bbias.dtype),
                 dcb.to(cbias.dtype), dang, None, None)
 
@@ -119,21 +132,6 @@ class Mamba3BC(torch.autograd.Function):
 def m3_bc_ok(braw: torch.Tensor, N: int, H: int, G: int) -> bool:
     return (braw.is_cuda and braw.dtype == torch.bfloat16 and N == 128 and H % G == 0
             and hasattr(ext(), "m3_bc_fwd"))
-
-
-def mamba3_tc_interleaved(x, dt, A, b2, c2, lam):
-    """Mamba3 two-term scan with B/C already in the interleaved layout (from Mamba3BC)."""
-    Bsz, S, H, P = x.shape
-    dtf, lamf = dt.float(), lam.float()
-    loga = A.float()[None, None, :] * dtf
-    gamma = lamf * dtf
-    beta = (1 - lamf) * dtf * torch.exp(loga)
-    x_prev = torch.cat([torch.zeros_like(x[:, :1]), x[:, :-1]], 1)
-    x2 = torch.stack([x_prev, x], 2).reshape(Bsz, 2 * S, H, P)
-    la2 = torch.stack([loga, torch.zeros_like(loga)], 2).reshape(Bsz, 2 * S, H)
-    g2 = torch.stack([beta, gamma], 2).reshape(Bsz, 2 * S, H)
-    y2 = SSDChunkTC.apply(x2, b2, c2, la2, g2)
-    return y2.view(Bsz, S, 2, H, P)[:, :, 1]
 
 
 class AngleCumsum(torch.autograd.Function):

@@ -55,7 +55,7 @@ def mamba3_scan(x, dt, A, Bm, Cm, lam, chunk: int, compat: bool = False):
     N = Bm.shape[-1]
     if not compat:
         from .ssd_tc import mamba3_tc, tc_ok
-        if tc_ok(x, N, 2 * x.shape[1]):
+        if tc_ok(x, N, x.shape[1]):
             return mamba3_tc(x, dt, A, Bm, Cm, lam)
     if not compat and _scan_ok(x, N):
         from .ssm_kernels import SSMScan

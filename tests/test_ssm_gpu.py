@@ -134,15 +134,17 @@ def test_ssd_tensor_core_mamba2(B, S, H, P, G):
         assert _rel(g, r) < 3e-2, (name, _rel(g, r))
 
 
-@pytest.mark.parametrize("B,S,H,P", [(1, 128, 2, 64), (2, 192, 2, 128)])
+@pytest.mark.parametrize("B,S,H,P", [(1, 128, 2, 64), (2, 256, 2, 128)])
 def test_ssd_tensor_core_mamba3(B, S, H, P):
-    """Mamba3 two-term scan through the interleaved tensor-core SSD vs the fp64 reference."""
+    """Mamba3 two-term scan through the shifted-state tensor-core SSD vs the fp64 reference."""
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops.ssd_tc import mamba3_tc
     from oxidizr_b200.ops._C import check_status
     N = 128
     x, dt, A, Bm, Cm = _tc_inputs(B, S, H, P, N, H, S + P)
     lam = torch.rand(B, S, H, device="cuda").requires_grad_()
+    from oxidizr_b200.ops.ssd_tc import tc_ok
+    assert tc_ok(x, N, S)
     y = mamba3_tc(x, dt, A, Bm, Cm, lam)
     dy = torch.randn_like(y)
     y.backward(dy)
@@ -158,7 +160,7 @@ def test_ssd_tensor_core_mamba3(B, S, H, P):
 
 
 def test_mamba3_fused_prologue_matches_unfused():
-    """Mamba3 mixer: fused B/C prologue + interleaved tensor-core scan == the unfused torch path."""
+    """Mamba3 mixer: fused B/C prologue + shifted-state tensor-core scan == the unfused torch path."""
     from oxidizr_b200.config import ModelConfig, _build
     from oxidizr_b200.models.mamba import Mamba3Mixer
     torch.manual_seed(0)
@@ -207,7 +209,7 @@ def test_angle_cumsum_kernel():
 
 
 def test_mamba3_bc_prologue_kernel():
-    """Fused B/C prologue vs torch: rmsnorm + bias + rotation, interleaved layout, and grads."""
+    """Fused B/C prologue vs torch: rmsnorm + bias + rotation, <B, C>, and grads."""
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops.ssd_tc import Mamba3BC
     torch.manual_seed(7)
@@ -219,21 +221,33 @@ def test_mamba3_bc_prologue_kernel():
     bb = (1 + 0.1 * torch.randn(H, N, device="cuda")).bfloat16().requires_grad_()
     cb = (1 + 0.1 * torch.randn(H, N, device="cuda")).bfloat16().requires_grad_()
     ang = (3 * torch.randn(B, S, H, N // 2, device="cuda")).requires_grad_()
-    b2, c2 = Mamba3BC.apply(braw, craw, w, bb, cb, ang, H, 1e-6)
+    bo, co, dot = Mamba3BC.apply(braw, craw, w, bb, cb, ang, H, 1e-6)
     torch.cuda.synchronize()
-    gb, gc = torch.randn_like(b2, dtype=torch.float32), torch.randn_like(c2, dtype=torch.float32)
-    (b2.float() * gb + c2.float() * gc).sum().backward()
+    gb, gc = torch.randn_like(bo, dtype=torch.float32), torch.randn_like(co, dtype=torch.float32)
+    gd = torch.randn_like(dot)
+    (bo.float() * gb + co.float() * gc + dot * gd).sum().backward()
     ins = [t.detach().double().requires_grad_() for t in (braw, craw, w, bb, cb, ang)]
     rb, rc, rw, rbb, rcb, ra = ins
     rep = lambda t: t.view(B, S, G, N).repeat_interleave(H // G, 2)
     nb = R.rmsnorm(rep(rb), rw, 1e-6) + rbb
     nc = R.rmsnorm(rep(rc), rw, 1e-6) + rcb
     bt, ct = R.mamba3_rotate(nb, ra), R.mamba3_rotate(nc, ra)
-    zero = torch.zeros_like(bt[:, :1])
-    b2r = torch.stack([torch.cat([zero, bt[:, :-1]], 1), bt], 2).reshape(B, 2 * S, H, N)
-    c2r = torch.stack([torch.zeros_like(ct), ct], 2).reshape(B, 2 * S, H, N)
-    assert _rel(b2, b2r) < 1e-2 and _rel(c2, c2r) < 1e-2
-    (b2r * gb.double() + c2r * gc.double()).sum().backward()
+    dr = (bt * ct).sum(-1)
+    assert _rel(bo, bt) < 1e-2 and _rel(co, ct) < 1e-2 and _rel(dot, dr) < 1e-2
+    (bt * gb.double() + ct * gc.double() + dr * gd.double()).sum().backward()
     for name, a, r in zip(("braw", "craw", "w", "b_bias", "c_bias", "ang"),
                           (braw.grad, craw.grad, w.grad, bb.grad, cb.grad, ang.grad), [t.grad for t in ins]):
         assert _rel(a, r) < 2e-2, (name, _rel(a, r))
+
+
+def test_ssd_dloga_scan_kernel():
+    """Reverse scan for SSD d loga vs the torch flip-cumsum formula."""
+    from oxidizr_b200.ops._C import ext
+    torch.manual_seed(9)
+    B, S, H = 2, 300, 5
+    e, ga, dg = (torch.randn(B, S, H, device="cuda") for _ in range(3))
+    dla = ext().ssd_dloga(e, ga, dg)
+    v = (ga * dg).double()
+    v_next = torch.cat([v[:, 1:], torch.zeros_like(v[:, :1])], 1)
+    q = torch.flip(torch.cumsum(torch.flip(e.double() - v_next, [1]), 1), [1])
+    assert _rel(dla, q - v) < 1e-5
