@@ -13,7 +13,7 @@
 // TMEM owner, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
 //
 // Epilogues (fused so no extra pass over the output is needed):
-//   EPI_BF16        C -> bf16, optionally + residual R (R may alias C)
+//   EPI_BF16        C -> bf16, optionally + bias[col] and + residual R (R may alias C)
 //   EPI_F32         C -> f32, optionally + beta * C_old (gradient accumulation)
 //   EPI_SWIGLU      B rows interleaved in blocks of 128 [gate|up]; writes
 //                   H = silu(g)*u (bf16, N/2 columns) and the pre-activation GU
@@ -52,6 +52,7 @@ struct GemmParams {
   int64_t ldd;
   const __nv_bfloat16* R;  // residual (BF16) / GU (SWIGLU_BWD)
   int64_t ldr;
+  const __nv_bfloat16* bias;  // BF16 epilogue: per-column bias [N] (may be null)
   void* D2;                // GU output (SWIGLU)
   int64_t ldd2;
   float beta;              // F32: C = acc + beta * C_old
@@ -339,6 +340,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
           if constexpr (EPI == EPI_BF16) {
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
+            if (p.bias) {
+              float bb[32];
+              load_bf16_row(p.bias + col, bb, nvalid, (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += bb[j];
+            }
             if (p.R) {
               float rr[32];
               load_bf16_row(p.R + (int64_t)row * p.ldr + col, rr, nvalid, vec);

@@ -15,7 +15,8 @@ Operand to_operand(const Mat& m, bool mn) {
 }
 
 void launch_gemm(const Mat& a, bool a_mn, const Mat& b, bool b_mn, void* out, int64_t ldo, bool out_f32,
-                 const void* resid, int64_t ldr, float beta, float alpha, int* status, cudaStream_t st) {
+                 const void* resid, int64_t ldr, float beta, float alpha, int* status, cudaStream_t st,
+                 const void* bias) {
   Operand oa = to_operand(a, a_mn), ob = to_operand(b, b_mn);
   GemmParams p{};
   fill_common(p, oa, ob);
@@ -28,6 +29,7 @@ void launch_gemm(const Mat& a, bool a_mn, const Mat& b, bool b_mn, void* out, in
   CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
   if (!out_f32) {
     p.vec_ok = aligned16(out, ldo, 2);
+    p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
     if (resid) {
       p.R = reinterpret_cast<const __nv_bfloat16*>(resid);
       p.ldr = ldr;
@@ -35,6 +37,7 @@ void launch_gemm(const Mat& a, bool a_mn, const Mat& b, bool b_mn, void* out, in
     }
     launch_epi<EPI_BF16>(a_mn, b_mn, ta, tb, p, st);
   } else {
+    OXI_CHECK(bias == nullptr, "bias epilogue only for bf16 output");
     p.vec_ok = aligned16(out, ldo, 4);
     p.beta = beta;
     if (beta == 1.0f) choose_splits(p);

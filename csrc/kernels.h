@@ -14,10 +14,11 @@ struct Mat {
 };
 
 // ------------------------------------------------------------------- GEMM
-// out[M,N] = alpha * A @ B^T  (+ resid)  or  (+ beta * out) for f32 output.
+// out[M,N] = alpha * A @ B^T (+ bias[N]) (+ resid)  or  (+ beta * out) for f32 output.
 // a_mn=false: A stored [M,K]; a_mn=true: A stored [K,M].  Same for B with N.
 void launch_gemm(const Mat& a, bool a_mn, const Mat& b, bool b_mn, void* out, int64_t ldo, bool out_f32,
-                 const void* resid, int64_t ldr, float beta, float alpha, int* status, cudaStream_t st);
+                 const void* resid, int64_t ldr, float beta, float alpha, int* status, cudaStream_t st,
+                 const void* bias = nullptr);
 // h[M, N/2] = silu(g) * u from x[M,K] @ w[N,K]^T, w rows interleaved [gate128|up128]...;
 // gu (nullable) receives the pre-activation [M, N] in the same interleaved order.
 void launch_gemm_swiglu(const Mat& x, const Mat& w, void* h, int64_t ldh, void* gu, int64_t ldgu, int* status,

@@ -90,6 +90,13 @@ void launch_angle_cumsum_bwd(const float* theta, const float* dt, const float* d
 // SSD d loga from the identity q_t = e_t + q_{t+1} - v_{t+1}, dla_t = q_t - v_t
 // with v = gamma * dgamma: e, ga, dg, dla f32 [B, S, H]; sums scratch
 // [B * ceil(S/128) * H].
+// D-skip epilogue of the SSD (ssm_glue.cu): out = bf16(y + d x) per row of P;
+// backward dx = bf16(dx_scan + d g), dd = <g, x>, e = <g, y> per row.  d per row
+// or per head (r % H).
+void launch_dskip_fwd(const float* y, const void* x, const float* d, int64_t rows, int H, int P, bool per_row,
+                      void* out, cudaStream_t st);
+void launch_dskip_bwd(const void* g, const void* x, const float* y, const float* d, const float* dx_scan,
+                      int64_t rows, int H, int P, bool per_row, void* dx, float* dd, float* e, cudaStream_t st);
 void launch_ssd_dloga(const float* e, const float* ga, const float* dg, int B, int S, int H, float* sums, float* dla,
                       cudaStream_t st);
 }  // namespace oxi

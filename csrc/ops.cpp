@@ -39,7 +39,8 @@ void check_out(const torch::Tensor& o, int64_t rows, int64_t cols, const char* w
 
 // ------------------------------------------------------------------ GEMM
 void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor out,
-          c10::optional<torch::Tensor> resid, double beta, double alpha, torch::Tensor status) {
+          c10::optional<torch::Tensor> resid, double beta, double alpha, torch::Tensor status,
+          c10::optional<torch::Tensor> bias) {
   c10::cuda::CUDAGuard g(a.device());
   Mat ma = bf16_mat(a, "a"), mb = bf16_mat(b, "b");
   const int64_t M = a_mn ? ma.cols : ma.rows, K = a_mn ? ma.rows : ma.cols;
@@ -61,8 +62,14 @@ void gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor 
     rp = resid->data_ptr();
     ldr = resid->stride(0);
   }
+  const void* bp = nullptr;
+  if (bias.has_value() && bias->defined()) {
+    TORCH_CHECK(!f32 && bias->scalar_type() == torch::kBFloat16 && bias->is_contiguous() && bias->numel() == N,
+                "bias: bf16 contiguous [N], bf16 output only");
+    bp = bias->data_ptr();
+  }
   oxi::launch_gemm(ma, a_mn, mb, b_mn, out.data_ptr(), out.stride(0), f32, rp, ldr, (float)beta, (float)alpha,
-                   status_ptr(status), stream());
+                   status_ptr(status), stream(), bp);
 }
 
 void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor h, c10::optional<torch::Tensor> gu,
@@ -534,8 +541,8 @@ std::vector<torch::Tensor> ssd_tc_bwd(torch::Tensor x, torch::Tensor Bm, torch::
   TORCH_CHECK(hs.is_contiguous() && hs.scalar_type() == torch::kBFloat16, "hs");
   auto f32 = x.options().dtype(torch::kFloat32);
   auto dx = torch::empty({B * S, H * P}, f32);
-  auto dB = torch::zeros({B * S, H * 128}, f32);
-  auto dC = torch::zeros({B * S, H * 128}, f32);
+  auto dB = torch::empty({B * S, H * 128}, f32);  // every row written by the chunk pass
+  auto dC = torch::empty({B * S, H * 128}, f32);
   auto dg = torch::zeros({B, S, H}, f32);
   auto dhs = torch::empty_like(hs);
   oxi::SsdTcIO io{};
@@ -600,6 +607,40 @@ std::vector<torch::Tensor> m3_bc_bwd(torch::Tensor braw, torch::Tensor craw, tor
                         dcraw.data_ptr<float>(), dbraw.stride(0), dw.data_ptr<float>(), dbb.data_ptr<float>(),
                         dcb.data_ptr<float>(), dang.data_ptr<float>(), stream());
   return {dbraw, dcraw, dw, dbb, dcb, dang};
+}
+
+torch::Tensor dskip_fwd(torch::Tensor y, torch::Tensor x, torch::Tensor d, int64_t H) {
+  c10::cuda::CUDAGuard g(y.device());
+  TORCH_CHECK(y.dim() == 2 && y.scalar_type() == torch::kFloat32 && y.is_contiguous(), "y: f32 contiguous [T, H*P]");
+  TORCH_CHECK(x.sizes() == y.sizes() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous(), "x: bf16 like y");
+  const int64_t rows = y.size(0) * H, P = y.size(1) / H;
+  TORCH_CHECK(d.scalar_type() == torch::kFloat32 && d.is_contiguous() && (d.numel() == rows || d.numel() == H),
+              "d: f32 [T, H] or [H]");
+  auto out = torch::empty(y.sizes(), x.options());
+  oxi::launch_dskip_fwd(y.data_ptr<float>(), x.data_ptr(), d.data_ptr<float>(), rows, (int)H, (int)P,
+                        d.numel() == rows && rows != H, out.data_ptr(), stream());
+  return out;
+}
+
+std::vector<torch::Tensor> dskip_bwd(torch::Tensor gout, torch::Tensor x, torch::Tensor y, torch::Tensor d,
+                                     torch::Tensor dx_scan, int64_t H) {
+  c10::cuda::CUDAGuard g(y.device());
+  TORCH_CHECK(y.dim() == 2 && y.scalar_type() == torch::kFloat32 && y.is_contiguous(), "y: f32 contiguous [T, H*P]");
+  TORCH_CHECK(x.sizes() == y.sizes() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous(), "x: bf16 like y");
+  TORCH_CHECK(gout.sizes() == y.sizes() && gout.scalar_type() == torch::kBFloat16 && gout.is_contiguous(),
+              "grad: bf16 like y");
+  TORCH_CHECK(dx_scan.sizes() == y.sizes() && dx_scan.scalar_type() == torch::kFloat32 && dx_scan.is_contiguous(),
+              "dx_scan: f32 like y");
+  const int64_t rows = y.size(0) * H, P = y.size(1) / H;
+  TORCH_CHECK(d.scalar_type() == torch::kFloat32 && d.is_contiguous() && (d.numel() == rows || d.numel() == H),
+              "d: f32 [T, H] or [H]");
+  auto dx = torch::empty(y.sizes(), x.options());
+  auto dd = torch::empty({y.size(0), H}, y.options());
+  auto e = torch::empty({y.size(0), H}, y.options());
+  oxi::launch_dskip_bwd(gout.data_ptr(), x.data_ptr(), y.data_ptr<float>(), d.data_ptr<float>(),
+                        dx_scan.data_ptr<float>(), rows, (int)H, (int)P, d.numel() == rows && rows != H, dx.data_ptr(),
+                        dd.data_ptr<float>(), e.data_ptr<float>(), stream());
+  return {dx, dd, e};
 }
 
 torch::Tensor ssd_dloga(torch::Tensor e, torch::Tensor ga, torch::Tensor dg) {
@@ -889,7 +930,9 @@ void host_check_selftest(int64_t v) { OXI_CHECK(v == 0, "value ", v, " of ", 2.5
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("host_check_selftest", &host_check_selftest, "raise via the launcher error path unless v == 0");
   m.doc() = "oxidizr_b200 sm_100a kernels";
-  m.def("gemm", &gemm, "tcgen05 GEMM out = alpha * a @ b^T (+resid | + beta*out)");
+  m.def("gemm", &gemm, "tcgen05 GEMM out = alpha * a @ b^T (+bias) (+resid | + beta*out)", py::arg("a"),
+        py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("out"), py::arg("resid"), py::arg("beta"),
+        py::arg("alpha"), py::arg("status"), py::arg("bias") = py::none());
   m.def("gemm_swiglu", &gemm_swiglu, "GEMM with fused SwiGLU epilogue");
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd, "GEMM with fused SwiGLU backward epilogue");
   m.def("gemm_ce", &gemm_ce, "lm_head GEMM with fused cross-entropy partials");
@@ -916,6 +959,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("angle_cumsum_bwd", &angle_cumsum_bwd, "backward of angle_cumsum");
   m.def("m3_bc_fwd", &m3_bc_fwd, "Mamba3 B/C norm + bias + complex RoPE (+ <B, C> per head)");
   m.def("ssd_dloga", &ssd_dloga, "SSD d loga reverse scan");
+  m.def("dskip_fwd", &dskip_fwd, "SSD D-skip epilogue: bf16(y + d x)");
+  m.def("dskip_bwd", &dskip_bwd, "backward of dskip_fwd (+ <g, y> for d loga)");
   m.def("m3_bc_bwd", &m3_bc_bwd, "backward of m3_bc_fwd");
   m.def("ssm_scan_fwd", &ssm_scan_fwd, "Mamba2/3 selective scan forward");
   m.def("ssm_scan_bwd", &ssm_scan_bwd, "Mamba2/3 selective scan backward");

@@ -200,17 +200,14 @@ class Mamba2Mixer(RefModule):
     def forward(self, h, resid):
         B, S, _ = h.shape
         p = self.in_proj(h)
-        gate = p[..., :self.I]
-        xBC = p[..., self.I:self.I + self.conv_dim]
-        dt = p[..., self.I + self.conv_dim:]
+        gate, xBC, dt = api.split_cols(p, [self.I, self.conv_dim, self.Hs])
         xBC = self.conv1d(xBC.contiguous(), act=True)
         x = xBC[..., :self.I].reshape(B, S, self.Hs, self.P)
         gn = self.g * self.N
         Bm = xBC[..., self.I:self.I + gn].reshape(B, S, self.g, self.N)
         Cm = xBC[..., self.I + gn:].reshape(B, S, self.g, self.N)
         dtv = _softplus_dt(dt, self.dt_bias)
-        y = ssm.ssd(x, dtv, self.A(), Bm, Cm, self.chunk, diag_only_g=self.compat)
-        y = y.float() + x.float() * self.D.float()[:, None]
+        y = ssm.ssd_skip(x, dtv, self.A(), Bm, Cm, self.D, self.chunk, diag_only_g=self.compat)
         y = y.to(h.dtype).reshape(B, S, self.I)
         y = api.gated_rmsnorm(y, gate.contiguous(), self.norm.weight, 1e-6)
         return self.out_proj(y, resid=resid)
@@ -295,11 +292,7 @@ class Mamba3Mixer(RefModule):
         B, S, _ = h.shape
         bc = self.g * self.N
         p = self.in_proj(h)
-        gate = p[..., :self.I]
-        x = p[..., self.I:2 * self.I]
-        Bm = p[..., 2 * self.I:2 * self.I + bc]
-        Cm = p[..., 2 * self.I + bc:2 * self.I + 2 * bc]
-        dt = p[..., 2 * self.I + 2 * bc:]
+        gate, x, Bm, Cm, dt = api.split_cols(p, [self.I, self.I, bc, bc, self.Hs])
         if self.conv1d is not None:
             xbc = self.conv1d(torch.cat([x, Bm, Cm], -1).contiguous(), act=True)
             x = xbc[..., :self.I]
@@ -324,11 +317,10 @@ class Mamba3Mixer(RefModule):
             xh = x.reshape(B, S, self.Hs, self.P)
             if self.mimo_x_up is not None:
                 xh = self.mimo_x_up(xh)
-            from ..ops.ssd_tc import mamba3_tc_k
-            y, c = mamba3_tc_k(xh, dtv, self.A(), bro, cro, lam)
-            # the shifted-state diagonal correction rides on the D skip
-            dskip = self.D.float()[None, None, :] - c * bcdot
-            return self._finish(y, xh, gate, h, resid, B, S, dskip)
+            from ..ops.ssd_tc import mamba3_tc_skip
+            # the shifted-state diagonal correction rides on the fused D skip
+            y = mamba3_tc_skip(xh, dtv, self.A(), bro, cro, lam, self.D, bcdot)
+            return self._finish(y, xh, gate, h, resid, B, S, skipped=True)
         Bm = Bm.reshape(B, S, self.g, self.N)
         Cm = Cm.reshape(B, S, self.g, self.N)
         rep = self.Hs // self.g
@@ -358,12 +350,10 @@ class Mamba3Mixer(RefModule):
         probe = x.new_empty(1, 1, 1, width)
         return m3_bc_ok(x, self.N, self.Hs, self.g) and tc_ok(probe, self.N, S)
 
-    def _finish(self, y, xh, gate, h, resid, B, S, dskip=None):
-        """y + D x (``dskip`` [B, S, H] overrides the per-head D), mimo down, gated norm, out_proj."""
-        if dskip is None:
+    def _finish(self, y, xh, gate, h, resid, B, S, skipped=False):
+        """y + D x (unless ``skipped``: already added), mimo down, gated norm, out_proj."""
+        if not skipped:
             y = y.float() + xh.float() * self.D.float()[:, None]
-        else:
-            y = y.float() + xh.float() * dskip[..., None]
         y = y.to(h.dtype)
         if self.mimo_x_down is not None:
             y = self.mimo_x_down(y)

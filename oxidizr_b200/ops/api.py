@@ -46,6 +46,40 @@ def gated_rmsnorm(y, gate, w, eps: float = 1e-6):
     return R.gated_rmsnorm(y, gate, w, eps)
 
 
+class _SplitCols(torch.autograd.Function):
+    """Column blocks of a projection output as views; the backward writes the block
+    gradients into ONE buffer (a single concatenation) instead of the per-slice
+    zero-fill + copy + sum that autograd does for plain slicing."""
+
+    @staticmethod
+    def forward(ctx, p, sizes):
+        ctx.sizes, ctx.shape, ctx.dtype = sizes, p.shape, p.dtype
+        outs, o = [], 0
+        for n in sizes:
+            outs.append(p.narrow(-1, o, n))
+            o += n
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        lead = ctx.shape[:-1]
+        parts = [torch.zeros(*lead, n, dtype=ctx.dtype, device=grads[0].device if grads[0] is not None else None)
+                 if g is None else g.to(ctx.dtype) for g, n in zip(grads, ctx.sizes)]
+        return torch.cat(parts, -1), None
+
+
+def split_cols(p, sizes):
+    """``p[..., a:b]`` blocks of widths ``sizes`` (summing to p's last dim)."""
+    assert sum(sizes) == p.shape[-1], (sizes, p.shape)
+    if p.requires_grad and torch.is_grad_enabled():
+        return _SplitCols.apply(p, tuple(sizes))
+    outs, o = [], 0
+    for n in sizes:
+        outs.append(p[..., o:o + n])
+        o += n
+    return tuple(outs)
+
+
 def linear(x, w, bias=None, resid=None):
     if _native(x):
         from .fused import Linear

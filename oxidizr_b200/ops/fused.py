@@ -117,9 +117,7 @@ class Linear(torch.autograd.Function):
         K = x.shape[-1]
         x2 = _c(x.reshape(-1, K))
         r2 = _c(resid.reshape(-1, w.shape[0])) if resid is not None else None
-        y = mm(x2, w, resid=r2)
-        if bias is not None:
-            y.add_(bias.to(y.dtype))
+        y = mm(x2, w, resid=r2, bias=bias)
         ctx.save_for_backward(x2)
         ctx.w, ctx.has_bias, ctx.has_resid, ctx.bias = w, bias is not None, resid is not None, bias
         return y.view(*x.shape[:-1], w.shape[0])
@@ -131,7 +129,7 @@ class Linear(torch.autograd.Function):
         dy2 = _c(dy.reshape(-1, w.shape[0]))
         dx = mm(dy2, w, b_t=True).view(*dy.shape[:-1], w.shape[1]) if ctx.needs_input_grad[0] else None
         gw = _wgrad_gemm(w, dy2, x2)
-        gb = _vec_grad(ctx.bias, dy2.float().sum(0)) if ctx.has_bias else None
+        gb = _vec_grad(ctx.bias, dy2.sum(0, dtype=torch.float32)) if ctx.has_bias else None
         dres = dy if ctx.has_resid else None
         return dx, gw, gb, dres
 

@@ -19,8 +19,8 @@ from ._C import ext, status
 
 def mm(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = False,
        out: Optional[torch.Tensor] = None, out_dtype=torch.bfloat16, resid: Optional[torch.Tensor] = None,
-       beta: float = 0.0, alpha: float = 1.0) -> torch.Tensor:
-    """``out = alpha * op(a) @ op(b)^T (+ resid) (+ beta * out)``.
+       beta: float = 0.0, alpha: float = 1.0, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out = alpha * op(a) @ op(b)^T (+ bias) (+ resid) (+ beta * out)``; ``bias`` [N] for bf16 output.
 
     ``op(a) = a`` ([M, K]) when ``a_t`` is False, else ``a^T`` with ``a`` stored [K, M].
     ``op(b) = b`` ([N, K]) when ``b_t`` is False, else ``b^T`` with ``b`` stored [K, N].
@@ -33,6 +33,8 @@ def mm(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = False
         A = a.t() if a_t else a
         B = b.t() if b_t else b
         r = alpha * (A.float() @ B.float().t())
+        if bias is not None:
+            r = r + bias.float()
         if resid is not None:
             r = r + resid.float()
         if out is not None:
@@ -43,7 +45,9 @@ def mm(a: torch.Tensor, b: torch.Tensor, *, a_t: bool = False, b_t: bool = False
         return r.to(out_dtype)
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype, device=a.device)
-    ext().gemm(a, a_t, b, b_t, out, resid, float(beta), float(alpha), status(a.device))
+    if bias is not None:
+        bias = bias.to(torch.bfloat16).contiguous()
+    ext().gemm(a, a_t, b, b_t, out, resid, float(beta), float(alpha), status(a.device), bias)
     return out
 
 

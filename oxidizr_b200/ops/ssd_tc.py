@@ -33,10 +33,14 @@ def tc_ok(x: torch.Tensor, N: int, S: int) -> bool:
 
 
 class SSDChunkTC(torch.autograd.Function):
-    """x [B, S, H, P] bf16; Bg/Cg [B, S, G, 128] (G divides H); loga/gamma [B, S, H] -> y f32 [B, S, H, P]."""
+    """x [B, S, H, P] bf16; Bg/Cg [B, S, G, 128] (G divides H); loga/gamma [B, S, H].
+
+    Without ``dskip``: y f32 [B, S, H, P].  With ``dskip`` ([H] per-head D, or [B, S, H]
+    per token): the D-skip epilogue (csrc/ssm_glue.cu) returns bf16(y + dskip x), and its
+    backward supplies <dy, y> for d loga in the same pass that adds dskip dy to dx."""
 
     @staticmethod
-    def forward(ctx, x, Bg, Cg, loga, gamma):
+    def forward(ctx, x, Bg, Cg, loga, gamma, dskip=None):
         Bsz, S, H, P = x.shape
         G, N = Bg.shape[2], Bg.shape[3]
         x2 = x.reshape(Bsz * S, H * P).to(torch.bfloat16).contiguous()
@@ -45,17 +49,23 @@ class SSDChunkTC(torch.autograd.Function):
         la = loga.float().contiguous()
         ga = gamma.float().contiguous()
         y, hs = ext().ssd_tc_fwd(x2, B2, C2, la, ga, Bsz, S, H, P, G, status(x.device))
-        ctx.save_for_backward(x2, B2, C2, la, ga, hs, y)
         ctx.shape = (Bsz, S, H, P, G, N)
-        ctx.dtypes = (x.dtype, Bg.dtype, Cg.dtype)
-        return y.view(Bsz, S, H, P)
+        ctx.dtypes = (x.dtype, Bg.dtype, Cg.dtype, None if dskip is None else dskip.dtype)
+        if dskip is None:
+            ctx.save_for_backward(x2, B2, C2, la, ga, hs, y)
+            return y.view(Bsz, S, H, P)
+        dsk = dskip.float().contiguous()
+        out = ext().dskip_fwd(y, x2, dsk, H)
+        ctx.save_for_backward(x2, B2, C2, la, ga, hs, y, dsk)
+        return out.view(Bsz, S, H, P)
 
     @staticmethod
     def backward(ctx, dy):
-        x2, B2, C2, la, ga, hs, y = ctx.saved_tensors
+        saved = ctx.saved_tensors
+        x2, B2, C2, la, ga, hs, y = saved[:7]
         Bsz, S, H, P, G, N = ctx.shape
-        dyf = dy.float().reshape(Bsz * S, H * P)
-        dyb = dyf.to(torch.bfloat16).contiguous()
+        xd, bd, cd, dd_dtype = ctx.dtypes
+        dyb = dy.reshape(Bsz * S, H * P).to(torch.bfloat16).contiguous()
         dx, dB, dC, dg = ext().ssd_tc_bwd(x2, B2, C2, la, ga, hs, dyb, Bsz, S, H, P, G, status(dy.device))
         if G < H:
             dB = dB.view(Bsz, S, G, H // G, N).sum(3)
@@ -63,16 +73,24 @@ class SSDChunkTC(torch.autograd.Function):
         else:
             dB = dB.view(Bsz, S, G, N)
             dC = dC.view(Bsz, S, G, N)
-        e = (dyf * y).view(Bsz, S, H, P).sum(-1)
-        dla = ext().ssd_dloga(e.contiguous(), ga.view(Bsz, S, H), dg.view(Bsz, S, H).contiguous())
-        xd, bd, cd = ctx.dtypes
-        return dx.view(Bsz, S, H, P).to(xd), dB.to(bd), dC.to(cd), dla, dg
+        ddskip = None
+        if dd_dtype is None:
+            e = (dy.float().reshape(Bsz * S, H * P) * y).view(Bsz, S, H, P).sum(-1).contiguous()
+            dx = dx.view(Bsz, S, H, P).to(xd)
+        else:
+            dsk = saved[7]
+            dxb, dd, e = ext().dskip_bwd(dyb, x2, y, dsk, dx, H)
+            dx = dxb.view(Bsz, S, H, P).to(xd)
+            ddskip = (dd.view(Bsz, S, H) if dsk.numel() == Bsz * S * H else dd.sum(0)).to(dd_dtype)
+        dla = ext().ssd_dloga(e.view(Bsz, S, H), ga.view(Bsz, S, H), dg.view(Bsz, S, H).contiguous())
+        return dx, dB.to(bd), dC.to(cd), dla, dg, ddskip
 
 
-def ssd_tc(x, dt, A, Bm, Cm):
-    """Mamba2 SSD core (no D skip): loga = A dt, gamma = dt."""
+def ssd_tc(x, dt, A, Bm, Cm, D=None):
+    """Mamba2 SSD core: loga = A dt, gamma = dt.  f32 without ``D``; with the per-head
+    skip ``D`` [H], bf16 y + D x from the fused epilogue."""
     dtf = dt.float()
-    return SSDChunkTC.apply(x, Bm, Cm, A.float()[None, None, :] * dtf, dtf)
+    return SSDChunkTC.apply(x, Bm, Cm, A.float()[None, None, :] * dtf, dtf, D)
 
 
 def mamba3_coeffs(dt, A, lam):
@@ -84,17 +102,19 @@ def mamba3_coeffs(dt, A, lam):
     return loga, lamf * dtf + c, c
 
 
-def mamba3_tc_k(x, dt, A, Bm, Cm, lam):
-    """Tensor-core scan of the shifted state: returns (y_K, c) with the Mamba3 output
-    y = y_K - (c <B, C>)[..., None] * x.  Bm/Cm per head [B, S, H, N] (bf16)."""
+def mamba3_tc_skip(x, dt, A, Bm, Cm, lam, D, bcdot):
+    """Mamba3 scan + D skip through the shifted state, bf16 [B, S, H, P]:
+    y = y_K + (D - c <B, C>) x.  Bm/Cm per head [B, S, H, N] bf16, bcdot = <B, C> [B, S, H]."""
     loga, gp, c = mamba3_coeffs(dt, A, lam)
-    return SSDChunkTC.apply(x, Bm, Cm, loga, gp), c
+    dskip = D.float()[None, None, :] - c * bcdot
+    return SSDChunkTC.apply(x, Bm, Cm, loga, gp, dskip)
 
 
 def mamba3_tc(x, dt, A, Bm, Cm, lam):
     """Mamba3 trapezoidal two-term scan (no D skip); Bm/Cm per head [B, S, H, N]."""
     Bb, Cb = Bm.to(torch.bfloat16), Cm.to(torch.bfloat16)
-    y, c = mamba3_tc_k(x, dt, A, Bb, Cb, lam)
+    loga, gp, c = mamba3_coeffs(dt, A, lam)
+    y = SSDChunkTC.apply(x, Bb, Cb, loga, gp)
     bcdot = (Bb.float() * Cb.float()).sum(-1)
     return y - (c * bcdot)[..., None] * x.float()
 

@@ -50,6 +50,16 @@ def ssd(x, dt, A, Bm, Cm, chunk: int, diag_only_g: bool = False):
     return R.ssd_chunked(f(x), f(dt), f(A), f(_expand_heads(Bm, H)), f(_expand_heads(Cm, H)), chunk, diag_only_g)
 
 
+def ssd_skip(x, dt, A, Bm, Cm, D, chunk: int, diag_only_g: bool = False):
+    """``ssd(...) + D x`` (per-head D); bf16 from the fused tensor-core epilogue, else f32."""
+    if not diag_only_g:
+        from .ssd_tc import ssd_tc, tc_ok
+        if tc_ok(x, Bm.shape[-1], x.shape[1]):
+            return ssd_tc(x, dt, A, Bm, Cm, D)
+    y = ssd(x, dt, A, Bm, Cm, chunk, diag_only_g)
+    return y.float() + x.float() * D.float()[:, None]
+
+
 def mamba3_scan(x, dt, A, Bm, Cm, lam, chunk: int, compat: bool = False):
     """Trapezoidal two-term scan (no D skip), f32 result.  B/C [B,S,H,N] per head."""
     N = Bm.shape[-1]

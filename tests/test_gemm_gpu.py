@@ -58,6 +58,29 @@ def test_gemm_residual_inplace():
     assert _rel(rr, ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 520, 200), (256, 1000, 512)])
+def test_gemm_bias_epilogue(M, N, K):
+    from oxidizr_b200.ops.gemm import mm
+    torch.manual_seed(3)
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = torch.randn(N, K, device="cuda").bfloat16()
+    bias = torch.randn(N, device="cuda").bfloat16()
+    r = torch.randn(M, N, device="cuda").bfloat16()
+    ref = _ref(x, w, False, False) + bias.float()
+    assert _rel(mm(x, w, bias=bias), ref) < 1e-2
+    assert _rel(mm(x, w, bias=bias, resid=r), ref + r.float()) < 1e-2
+
+
+def test_gemm_unaligned_rows_take_the_plain_path():
+    """Rows that are not 16-byte aligned (a 4-wide projection) give the right answer."""
+    from oxidizr_b200.ops.gemm import mm
+    torch.manual_seed(4)
+    dy = torch.randn(256, 4, device="cuda").bfloat16()
+    w = torch.randn(4, 256, device="cuda").bfloat16()
+    out = mm(dy, w, b_t=True)
+    assert _rel(out, dy.float() @ w.float()) < 1e-2
+
+
 def test_gemm_swiglu_fwd_bwd():
     from oxidizr_b200.ops._C import ext, status
     torch.manual_seed(2)

@@ -251,3 +251,25 @@ def test_ssd_dloga_scan_kernel():
     v_next = torch.cat([v[:, 1:], torch.zeros_like(v[:, :1])], 1)
     q = torch.flip(torch.cumsum(torch.flip(e.double() - v_next, [1]), 1), [1])
     assert _rel(dla, q - v) < 1e-5
+
+
+@pytest.mark.parametrize("P,per_row", [(64, False), (256, True), (128, True)])
+def test_dskip_epilogue_kernels(P, per_row):
+    """D-skip epilogue: bf16(y + d x) and its backward (dx, dd, <g, y>) vs torch fp32."""
+    from oxidizr_b200.ops._C import ext
+    torch.manual_seed(11)
+    T, H = 300, 3
+    y = torch.randn(T, H * P, device="cuda")
+    x = torch.randn(T, H * P, device="cuda").bfloat16()
+    d = torch.randn(T, H, device="cuda") if per_row else torch.randn(H, device="cuda")
+    dx_scan = torch.randn(T, H * P, device="cuda")
+    g = torch.randn(T, H * P, device="cuda").bfloat16()
+    out = ext().dskip_fwd(y, x, d.contiguous(), H)
+    dv = (d if per_row else d[None].expand(T, H))[..., None]
+    ref = y.view(T, H, P) + dv * x.float().view(T, H, P)
+    assert _rel(out.view(T, H, P), ref) < 1e-2
+    dx, dd, e = ext().dskip_bwd(g, x, y, d.contiguous(), dx_scan, H)
+    gf = g.float().view(T, H, P)
+    assert _rel(dx.view(T, H, P), dx_scan.view(T, H, P) + dv * gf) < 1e-2
+    assert _rel(dd, (gf * x.float().view(T, H, P)).sum(-1)) < 1e-5
+    assert _rel(e, (gf * y.view(T, H, P)).sum(-1)) < 1e-5
