@@ -227,7 +227,7 @@ def test_mamba3_bc_prologue_kernel():
     torch.cuda.synchronize()
     gb, gc = torch.randn_like(bo, dtype=torch.float32), torch.randn_like(co, dtype=torch.float32)
     gd = torch.randn_like(dot)
-    (bo.float() * gb + co.float() * gc + dot * gd).sum().backward()
+    ((bo.float() * gb + co.float() * gc).sum() + (dot * gd).sum()).backward()
     ins = [t.detach().double().requires_grad_() for t in (braw, craw, w, bb, cb, ang)]
     rb, rc, rw, rbb, rcb, ra = ins
     rep = lambda t: t.view(B, S, G, N).repeat_interleave(H // G, 2)
@@ -236,7 +236,7 @@ def test_mamba3_bc_prologue_kernel():
     bt, ct = R.mamba3_rotate(nb, ra), R.mamba3_rotate(nc, ra)
     dr = (bt * ct).sum(-1)
     assert _rel(bo, bt) < 1e-2 and _rel(co, ct) < 1e-2 and _rel(dot, dr) < 1e-2
-    (bt * gb.double() + ct * gc.double() + dr * gd.double()).sum().backward()
+    ((bt * gb.double() + ct * gc.double()).sum() + (dr * gd.double()).sum()).backward()
     for name, a, r in zip(("braw", "craw", "w", "b_bias", "c_bias", "ang"),
                           (braw.grad, craw.grad, w.grad, bb.grad, cb.grad, ang.grad), [t.grad for t in ins]):
         assert _rel(a, r) < 2e-2, (name, _rel(a, r))
