@@ -11,6 +11,7 @@ void launch_gemm_swiglu(const Mat& x, const Mat& w, void* h, int64_t ldh, void* 
   Operand oa = to_operand(x, false), ob = to_operand(w, false);
   GemmParams p{};
   fill_common(p, oa, ob);
+  use_pairs(p);
   OXI_CHECK(p.N % 256 == 0, "SwiGLU GEMM needs 2*intermediate % 256 == 0");
   p.D = h;
   p.ldd = ldh;
@@ -22,7 +23,7 @@ void launch_gemm_swiglu(const Mat& x, const Mat& w, void* h, int64_t ldh, void* 
   }
   p.status = status;
   if (p.M == 0) return;
-  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
+  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
   launch_t<false, false, EPI_SWIGLU>(ta, tb, p, st);
 }
 
@@ -31,6 +32,7 @@ void launch_gemm_swiglu_bwd(const Mat& dy, const Mat& w_down, const void* gu, in
   Operand oa = to_operand(dy, false), ob = to_operand(w_down, true);
   GemmParams p{};
   fill_common(p, oa, ob);  // N = intermediate
+  use_pairs(p);
   OXI_CHECK(p.N % 128 == 0, "intermediate must be a multiple of 128");
   p.D = dgu;
   p.ldd = lddgu;
@@ -39,7 +41,7 @@ void launch_gemm_swiglu_bwd(const Mat& dy, const Mat& w_down, const void* gu, in
   p.vec_ok = aligned16(dgu, lddgu, 2) && aligned16(gu, ldgu, 2);
   p.status = status;
   if (p.M == 0) return;
-  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
+  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
   launch_t<false, true, EPI_SWIGLU_BWD>(ta, tb, p, st);
 }
 
@@ -50,6 +52,7 @@ void launch_gemm_ce(const Mat& x, const Mat& w, const int64_t* targets, float* p
   Operand oa = to_operand(x, false), ob = to_operand(w, false);
   GemmParams p{};
   fill_common(p, oa, ob);
+  use_pairs(p);
   p.alpha = alpha;
   p.targets = targets;
   p.part_max = part_max;
@@ -63,7 +66,7 @@ void launch_gemm_ce(const Mat& x, const Mat& w, const int64_t* targets, float* p
   }
   p.status = status;
   if (p.M == 0) return;
-  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
+  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
   launch_t<false, false, EPI_CE>(ta, tb, p, st);
 }
 
@@ -72,6 +75,7 @@ void launch_gemm_rope(const Mat& x, const Mat& w, void* out, int64_t ldo, const 
   Operand oa = to_operand(x, false), ob = to_operand(w, false);
   GemmParams p{};
   fill_common(p, oa, ob);
+  use_pairs(p);
   OXI_CHECK(hd == 64 || hd == 128, "RoPE epilogue supports head_dim 64 or 128");
   OXI_CHECK(q_cols % hd == 0 && k_cols % hd == 0 && p.N % hd == 0, "RoPE regions must be whole heads");
   p.D = out;
@@ -85,7 +89,7 @@ void launch_gemm_rope(const Mat& x, const Mat& w, void* out, int64_t ldo, const 
   p.rope_k_cols = k_cols;
   p.status = status;
   if (p.M == 0) return;
-  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
+  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
   launch_t<false, false, EPI_ROPE>(ta, tb, p, st);
 }
 

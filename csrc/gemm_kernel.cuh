@@ -26,6 +26,7 @@
 // Every TMA load here is issued by one CTA for itself and reads local memory.
 #include <cudaTypedefs.h>
 #include <algorithm>
+#include <cstdlib>
 
 #include "host_util.h"
 
@@ -77,7 +78,13 @@ struct GemmParams {
   const int* seg_off;
   int64_t b_group_stride;  // B tensor-map rows per expert
   int64_t d_group_stride;  // output elements per expert (group-K)
+  int cg;                  // 2: CTA-pair tiles (256 x 256, cta_group::2); else one CTA per 128 x 256 tile
 };
+
+// CTA-pair configuration: each CTA holds 128 rows of A and 128 of B's 256 per
+// k-block (32 KB per stage), so six stages fit.
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_B_ROWS = 128;
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
   // Group GROUP_M row-tiles together so consecutive CTAs share B tiles in L2.
@@ -174,33 +181,47 @@ __device__ __forceinline__ void load_bf16_row(const __nv_bfloat16* src, float* v
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+// CG = 1: one CTA per 128 x 256 output tile.
+// CG = 2: a cluster of two CTAs per 256 x 256 tile.  The even CTA ("leader")
+// issues the pair MMAs (cta_group::2); each CTA TMA-loads its own 128 rows of A
+// and its half of B's rows into its own shared memory and counts the bytes on the
+// leader's `full` barrier; the leader's commits arrive on both CTAs' `empty` and
+// `tfull` barriers; both CTAs' epilogue threads release an accumulator on the
+// leader's `tempty`.  Every load reads global memory of this GPU only.
+template <bool A_MN, bool B_MN, int EPI, int CG = 1>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  constexpr int NST = CG == 2 ? PAIR_STAGES : STAGES;
+  constexpr int BROWS = CG == 2 ? PAIR_B_ROWS : BN;   // B rows held by this CTA
+  constexpr int B_BYTES = BROWS * BK * 2;
+  constexpr int ST_BYTES = A_STAGE_BYTES + B_BYTES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment is required by the 128B swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* sB = smem + NST * A_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NST * ST_BYTES);
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
-  uint64_t* tempty = bars + 2 * STAGES + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  uint64_t* empty = bars + NST;
+  uint64_t* tfull = bars + 2 * NST;
+  uint64_t* tempty = bars + 2 * NST + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NST + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int unit0 = CG == 2 ? (int)(blockIdx.x / 2) : (int)blockIdx.x;
+  const int unit_step = CG == 2 ? (int)(gridDim.x / 2) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 128 * CG);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -208,72 +229,103 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // both CTAs' barriers exist before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = (p.K + BK - 1) / BK;
+  // shared::cluster address of an accumulator-release barrier (the leader's)
+  auto release_acc = [&](int a) {
+    if constexpr (CG == 2) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[a]), 0));
+    else mbar_arrive(&tempty[a]);
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t armed_parity[STAGES];
-      bool armed[STAGES];
+      uint32_t armed_parity[NST];
+      bool armed[NST];
 #pragma unroll
-      for (int s = 0; s < STAGES; ++s) { armed[s] = false; armed_parity[s] = 0; }
+      for (int s = 0; s < NST; ++s) { armed[s] = false; armed_parity[s] = 0; }
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int t = unit0; t < p.num_tiles && ok; t += unit_step) {
         const Unit un = unit_info(t, p, num_kb);
         if (!un.valid) continue;
         const int kb0 = un.kb0, kb1 = un.kb1;
-        const int m0 = un.tm * BM, n0 = un.tn * BN;
+        const int m0 = un.tm * BM * CG + (int)rank * BM;
+        const int n0 = un.tn * BN + (int)rank * (CG == 2 ? PAIR_B_ROWS : 0);
         const int boff = (int)(un.e * p.b_group_stride);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          armed[stage] = true;
-          armed_parity[stage] = phase;
+          if (rank == 0) {
+            mbar_arrive_expect_tx(&full[stage], ST_BYTES * CG);
+            armed[stage] = true;
+            armed_parity[stage] = phase;
+          }
           uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
-          uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
           const int k0 = kb * BK;
-          if (!A_MN) {
-            tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
-          } else {
-            tma_load_2d(a_dst, &tmA, &full[stage], m0, k0);
-            tma_load_2d(a_dst + BK * 128, &tmA, &full[stage], m0 + 64, k0);
-          }
-          if (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0 + boff);
-          } else {
+          if constexpr (CG == 2) {
+            const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+            if (!A_MN) {
+              tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
+            } else {
+              tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
+              tma_load_2d_pair(a_dst + BK * 128, &tmA, bar, m0 + 64, k0);
+            }
+            if (!B_MN) {
+              tma_load_2d_pair(b_dst, &tmB, bar, k0, n0 + boff);
+            } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              tma_load_2d(b_dst + q * BK * 128, &tmB, &full[stage], n0 + 64 * q, k0 + boff);
+              for (int q = 0; q < BROWS / 64; ++q)
+                tma_load_2d_pair(b_dst + q * BK * 128, &tmB, bar, n0 + 64 * q, k0 + boff);
+            }
+          } else {
+            if (!A_MN) {
+              tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+            } else {
+              tma_load_2d(a_dst, &tmA, &full[stage], m0, k0);
+              tma_load_2d(a_dst + BK * 128, &tmA, &full[stage], m0 + 64, k0);
+            }
+            if (!B_MN) {
+              tma_load_2d(b_dst, &tmB, &full[stage], k0, n0 + boff);
+            } else {
+#pragma unroll
+              for (int q = 0; q < BROWS / 64; ++q)
+                tma_load_2d(b_dst + q * BK * 128, &tmB, &full[stage], n0 + 64 * q, k0 + boff);
+            }
           }
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == NST) { stage = 0; phase ^= 1; }
         }
       }
       if (!ok) {
-        // Drain the copies this thread issued before leaving (bounded).
-        for (int s = 0; s < STAGES; ++s)
+        // Drain the copies issued into barriers this thread armed before leaving (bounded).
+        for (int s = 0; s < NST; ++s)
           if (armed[s]) mbar_wait(&full[s], armed_parity[s], nullptr, p.status);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, A_MN, B_MN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t IDESC = umma_idesc_bf16(BM * CG, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int t = unit0; t < p.num_tiles && ok; t += unit_step) {
         const Unit un = unit_info(t, p, num_kb);
         if (!un.valid) continue;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status)) { ok = false; break; }
@@ -284,7 +336,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_STAGE_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             uint64_t ad, bd;
@@ -292,13 +344,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             else       ad = umma_desc_sw128(a_addr + k * 2048, BK * 128, 1024);
             if (!B_MN) bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
             else       bd = umma_desc_sw128(b_addr + k * 2048, BK * 128, 1024);
-            tc_mma_f16(d_tmem, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
+            if constexpr (CG == 2) tc_mma_f16_pair(d_tmem, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
+            else tc_mma_f16(d_tmem, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if constexpr (CG == 2) {
+            tc_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
+            tc_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+          } else {
+            tc_commit(&empty[stage]);
+          }
+          if (++stage == NST) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        if constexpr (CG == 2) {
+          tc_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 0));
+          tc_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+        } else {
+          tc_commit(&tfull[acc]);
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -312,11 +375,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool vec = p.vec_ok != 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+    for (int t = unit0; t < p.num_tiles; t += unit_step) {
       const Unit un = unit_info(t, p, num_kb);
       if (!un.valid) continue;
       const int tn = un.tn;
-      const int m0 = un.tm * BM, n0 = un.tn * BN;
+      const int m0 = un.tm * BM * CG + (int)rank * BM, n0 = un.tn * BN;
       void* Dp = p.D;
       if (p.group_mode == 2) Dp = (char*)p.D + un.e * p.d_group_stride * (EPI == EPI_F32 ? 4 : 2);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
@@ -331,7 +394,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
           tc_wait_ld();
-          if (c == BN / 32 - 1) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          if (c == BN / 32 - 1) { tc_fence_before(); release_acc(acc); }
           const int col = n0 + c * 32;
           const int nvalid = min(32, p.N - col);
           if (!row_ok || nvalid <= 0) continue;
@@ -407,7 +470,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tmem_ld32(tbase + c * 32, rg);
           tmem_ld32(tbase + 128 + c * 32, ru);
           tc_wait_ld();
-          if (c == 3) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          if (c == 3) { tc_fence_before(); release_acc(acc); }
           const int hcol = n0 / 2 + c * 32;
           const int nvalid = min(32, p.N / 2 - hcol);
           if (!row_ok || nvalid <= 0) continue;
@@ -433,7 +496,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
           tc_wait_ld();
-          if (c == BN / 32 - 1) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          if (c == BN / 32 - 1) { tc_fence_before(); release_acc(acc); }
           const int col = n0 + c * 32;
           const int nvalid = min(32, p.N - col);
           if (!row_ok || nvalid <= 0) continue;
@@ -480,7 +543,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tmem_ld32(tbase + (c + pair_off) * 32, r2);
           tc_wait_ld();
           const bool last = (c + pair_off == nch - 1) || (c == nch - 1);
-          if (last) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+          if (last) { tc_fence_before(); release_acc(acc); }
           const int nvalid = min(32, p.N - col);
           if (!row_ok || nvalid <= 0) continue;
           float x1[32], x2[32];
@@ -510,10 +573,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // no remote arrive or pair MMA is still aimed at this CTA
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -558,17 +623,64 @@ inline int num_sms() {
 }
 
 constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int GEMM_PAIR_SMEM = PAIR_STAGES * (A_STAGE_BYTES + PAIR_B_ROWS * BK * 2) + 1024 + 256;
+
+// Clusters of two (one CTA per SM) that fit on the device at once.
+template <typename K>
+inline int max_pair_clusters(K kern) {
+  static int n = -1;
+  if (n < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms(), 1, 1);
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = GEMM_PAIR_SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int c = 0;
+    OXI_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&c, kern, &cfg));
+    n = c;
+  }
+  return n;
+}
 
 template <bool A_MN, bool B_MN, int EPI>
 static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, cudaStream_t st) {
-  auto kern = gemm_kernel<A_MN, B_MN, EPI>;
+  if (p.num_tiles <= 0) return;
+  if (p.cg == 2) {
+    auto kern = gemm_kernel<A_MN, B_MN, EPI, 2>;
+    static bool attr = false;
+    if (!attr) {
+      OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_PAIR_SMEM));
+      attr = true;
+    }
+    const int clusters = std::min(p.num_tiles, std::max(1, max_pair_clusters(kern)));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = GEMM_PAIR_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    OXI_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+    return;
+  }
+  auto kern = gemm_kernel<A_MN, B_MN, EPI, 1>;
   static bool attr = false;
   if (!attr) {
     OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
     attr = true;
   }
   int grid = std::min(p.num_tiles, num_sms());
-  if (grid <= 0) return;
   kern<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
@@ -608,7 +720,26 @@ inline void fill_common(GemmParams& p, const Operand& a, const Operand& b) {
   p.kb_per_split = (p.K + BK - 1) / BK;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.alpha = 1.f;
+  p.cg = 1;
 }
+
+// Switch a plain (ungrouped) GEMM to CTA-pair 256 x 256 tiles when it has more
+// than one 128-row tile of output (OXI_GEMM_CG=1 keeps single-CTA tiles).  Call
+// before choose_splits and before building B's tensor map (b_tile_rows).
+inline void use_pairs(GemmParams& p) {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("OXI_GEMM_CG");
+    mode = (e && e[0] == '1') ? 1 : 2;
+  }
+  if (mode != 2 || p.group_mode != 0 || p.M <= BM) return;
+  p.cg = 2;
+  p.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+}
+
+// Rows of B per CTA tile (the box height of B's tensor map when K-major).
+inline int b_tile_rows(const GemmParams& p) { return p.cg == 2 ? PAIR_B_ROWS : BN; }
 
 // Split K across CTAs when there are too few output tiles to fill the GPU
 // (weight-gradient GEMMs: small M x N, K = tokens).  Only valid for an

@@ -20,13 +20,14 @@ void launch_gemm(const Mat& a, bool a_mn, const Mat& b, bool b_mn, void* out, in
   Operand oa = to_operand(a, a_mn), ob = to_operand(b, b_mn);
   GemmParams p{};
   fill_common(p, oa, ob);
+  use_pairs(p);
   p.alpha = alpha;
   p.D = out;
   p.ldd = ldo;
   p.status = status;
   if (p.M == 0 || p.N == 0) return;
   OXI_CHECK(p.K > 0, "GEMM with K == 0 must be handled by the caller");
-  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
+  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
   if (!out_f32) {
     p.vec_ok = aligned16(out, ldo, 2);
     p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
