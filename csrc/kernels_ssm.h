@@ -56,6 +56,11 @@ struct SsdTcIO {
   float* dB;
   float* dC;
   float* dgamma;
+  float* hloc;          // forward scratch [B*H*nc*N, P] f32
+  float* lamend;        // forward scratch [B*H*nc] f32
+  void* out;            // optional bf16 [B*S, H*P] = y + d x (fused D skip)
+  const float* dskip;   // d: [B*S*H] per token or [H] per head
+  int dskip_per_row;
   int* status;
 };
 bool ssd_tc_supported(int N, int P, int S);

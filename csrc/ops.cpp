@@ -504,9 +504,10 @@ void ssd_check(const torch::Tensor& t, int64_t rows, int64_t cols, const char* w
 
 bool ssd_tc_supported(int64_t N, int64_t P, int64_t S) { return oxi::ssd_tc_supported((int)N, (int)P, (int)S); }
 
+// Returns {y f32, hs bf16} and, when dskip is given, out = bf16(y + dskip x) third.
 std::vector<torch::Tensor> ssd_tc_fwd(torch::Tensor x, torch::Tensor Bm, torch::Tensor Cm, torch::Tensor loga,
                                       torch::Tensor gamma, int64_t B, int64_t S, int64_t H, int64_t P, int64_t G,
-                                      torch::Tensor status) {
+                                      torch::Tensor status, c10::optional<torch::Tensor> dskip) {
   c10::cuda::CUDAGuard g(x.device());
   ssd_check(x, B * S, H * P, "x");
   ssd_check(Bm, B * S, G * 128, "B");
@@ -515,8 +516,11 @@ std::vector<torch::Tensor> ssd_tc_fwd(torch::Tensor x, torch::Tensor Bm, torch::
                   gamma.scalar_type() == torch::kFloat32 && gamma.is_contiguous() && gamma.numel() == B * S * H,
               "loga / gamma: f32 contiguous [B, S, H]");
   const int64_t nc = S / 128;
-  auto y = torch::empty({B * S, H * P}, x.options().dtype(torch::kFloat32));
+  auto f32 = x.options().dtype(torch::kFloat32);
+  auto y = torch::empty({B * S, H * P}, f32);
   auto hs = torch::empty({B * H * nc * 128, P}, x.options());
+  auto hloc = torch::empty({B * H * nc * 128, P}, f32);
+  auto lamend = torch::empty({B * H * nc}, f32);
   oxi::SsdTcIO io{};
   io.B = (int)B; io.S = (int)S; io.H = (int)H; io.P = (int)P; io.N = 128; io.G = (int)G;
   io.x = x.data_ptr(); io.ldx = x.stride(0);
@@ -524,8 +528,20 @@ std::vector<torch::Tensor> ssd_tc_fwd(torch::Tensor x, torch::Tensor Bm, torch::
   io.Cm = Cm.data_ptr(); io.ldc = Cm.stride(0);
   io.loga = loga.data_ptr<float>(); io.gamma = gamma.data_ptr<float>();
   io.y = y.data_ptr<float>(); io.hs = hs.data_ptr();
+  io.hloc = hloc.data_ptr<float>(); io.lamend = lamend.data_ptr<float>();
+  torch::Tensor out;
+  if (dskip.has_value() && dskip->defined()) {
+    TORCH_CHECK(dskip->scalar_type() == torch::kFloat32 && dskip->is_contiguous() &&
+                    (dskip->numel() == B * S * H || dskip->numel() == H),
+                "dskip: f32 contiguous [B, S, H] or [H]");
+    out = torch::empty({B * S, H * P}, x.options());
+    io.out = out.data_ptr();
+    io.dskip = dskip->data_ptr<float>();
+    io.dskip_per_row = dskip->numel() == B * S * H && B * S > 1 ? 1 : 0;
+  }
   io.status = status_ptr(status);
   oxi::launch_ssd_fwd(io, stream());
+  if (out.defined()) return {y, hs, out};
   return {y, hs};
 }
 
@@ -953,7 +969,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv1d_fwd", &conv1d_fwd, "depthwise causal conv1d (+bias, +SiLU) forward");
   m.def("conv1d_bwd", &conv1d_bwd, "depthwise causal conv1d backward");
   m.def("ssd_tc_supported", &ssd_tc_supported, "whether the tensor-core SSD handles (N, P, S)");
-  m.def("ssd_tc_fwd", &ssd_tc_fwd, "tensor-core chunked SSD forward");
+  m.def("ssd_tc_fwd", &ssd_tc_fwd, "tensor-core chunked SSD forward (chunk-parallel, optional fused D skip)",
+        py::arg("x"), py::arg("Bm"), py::arg("Cm"), py::arg("loga"), py::arg("gamma"), py::arg("B"), py::arg("S"),
+        py::arg("H"), py::arg("P"), py::arg("G"), py::arg("status"), py::arg("dskip") = py::none());
   m.def("ssd_tc_bwd", &ssd_tc_bwd, "tensor-core chunked SSD backward");
   m.def("angle_cumsum", &angle_cumsum, "Mamba3 rotation angles: cumsum over time of theta * dt");
   m.def("angle_cumsum_bwd", &angle_cumsum_bwd, "backward of angle_cumsum");

@@ -2,16 +2,17 @@
 //
 // Per batch b and head h the recurrence (state H is N x P, N = 128):
 //   H_t = exp(a_t) H_{t-1} + g_t B_t x_t^T ,   y_t = H_t^T C_t
-// (mamba2.rs:381-482; Mamba3's two-term update is run as this recurrence on an
-// interleaved sequence of twice the length, see ops/ssd_tc.py).  With chunks of
+// (mamba2.rs:381-482; Mamba3's two-term update runs as this recurrence on a
+// shifted state, see ops/ssd_tc.py).  With chunks of
 // L = 128 steps and Lam_t = sum_{u<=t} a_u inside a chunk:
 //   M[t,s]  = (C_t . B_s) exp(Lam_t - Lam_s) g_s   (s <= t)
 //   Y       = M X + diag(exp Lam) C H_prev
 //   H_end   = exp(Lam_L) H_prev + B^T diag(w) X,   w_s = exp(Lam_L - Lam_s) g_s
 // Every product is a tcgen05.mma (bf16 in, f32 accumulate in TMEM); operands
 // come from 128B-swizzled shared memory tiles that TMA loads (x, B, C, dy,
-// stored states) or that the math warps write (M, scaled x / dy, bf16 state).
-// A CTA owns (b, h, 64 columns of P); its state stays in TMEM across chunks.
+// stored states) or that the math warps write (M, scaled x / dy / C).
+// Forward: chunk-parallel in three phases (chunk-local end states, an
+// element-wise scan over chunks, then the outputs; see below).
 //
 // Backward, pass 1 (reverse over chunks, per (b, h, p-block)), dH = adjoint of
 // H_end:   dX = M^T dY + diag(w) B dH ;  dH_prev = exp(Lam_L) dH + C^T diag(exp Lam) dY
@@ -60,6 +61,11 @@ struct SsdParams {
   float* dB;                  // [B*S, H*N] f32
   float* dC;                  // [B*S, H*N] f32
   float* dgamma;              // [B, S, H] f32 (atomics)
+  float* hloc;                // [B*H*nc*N, P] f32 chunk-local end states (chunk-parallel forward)
+  float* lamend;              // [B*H*nc] f32 sum of loga over each chunk
+  __nv_bfloat16* out;         // [B*S, H*P] bf16 y + d x (fused D skip; null: none)
+  const float* dskip;         // [B*S*H] (per token) or [H] (per head)
+  int dskip_per_row;
   int* status;
 };
 
@@ -115,153 +121,263 @@ __device__ __forceinline__ void tmem_row64(uint32_t addr, float* out) {
   }
 }
 
-// =================================================================== forward
-struct FwdSmem {
-  static constexpr int OFF_C = 0;
-  static constexpr int OFF_B = OFF_C + T_NN;
+// ============================================ chunk-parallel forward
+// Phase A (ssd_state_kernel, one CTA per (b, h, chunk)): the chunk's own
+// contribution to its end state, Hloc = B^T diag(w) X (w_s = exp(Lam_L - Lam_s) g_s),
+// f32, and Lam_L.  Phase B (ssd_state_scan_kernel): H_c = exp(Lam_L,c) H_{c-1} +
+// Hloc_c over the chunks of each (b, h), storing every chunk-start state (bf16,
+// the backward's copy too).  Phase C (ssd_out_kernel, one CTA per (b, h, chunk)):
+// Y = M X + diag(exp Lam) C H_prev, accumulated in one TMEM tile by scaling C's
+// rows in shared memory, with the optional D-skip epilogue.  Chunks of a
+// sequence run in parallel; only the element-wise phase B walks the chunks.
+struct StateSmem {
+  static constexpr int OFF_B = 0;
   static constexpr int OFF_X = OFF_B + T_NN;
-  static constexpr int OFF_P = OFF_X + T_NP;
-  static constexpr int OFF_H = OFF_P + T_NN;
-  static constexpr int OFF_W = OFF_H + T_NP;
-  static constexpr int OFF_VEC = OFF_W + T_NP;      // lam[128], gam[128], part[8]
+  static constexpr int OFF_VEC = OFF_X + T_NP;   // lam[128], gam[128], part[8]
   static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4 + 64;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
 };
 
-__global__ void __launch_bounds__(SSD_THREADS, 1)
-    ssd_fwd_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, SsdParams p) {
-  using L = FwdSmem;
+__global__ void __launch_bounds__(SSD_THREADS)
+    ssd_state_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB, SsdParams p) {
+  using L = StateSmem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sX = smem + L::OFF_X, *sP = smem + L::OFF_P,
-          *sH = smem + L::OFF_H, *sW = smem + L::OFF_W;
+  uint8_t *sB = smem + L::OFF_B, *sX = smem + L::OFF_X;
   float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
   float* s_gam = s_lam + 128;
   float* s_part = s_gam + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t *ld_full = bars + 0, *s_full = bars + 1, *p_full = bars + 2, *y_full = bars + 3, *w_full = bars + 4,
-           *h_full = bars + 5;
+  uint64_t *ld_b = bars + 0, *ld_x = bars + 1, *w_ready = bars + 2, *x_free = bars + 3, *h_full = bars + 4,
+           *h_free = bars + 5;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int bh = blockIdx.x, pb = blockIdx.y;
+  const int bh = blockIdx.x, c = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int g = h / (p.H / p.G);
-  const int row0 = b * p.S;
+  const int r = b * p.S + c * SL;
+  const int npb = p.P / SP;
   if (threadIdx.x == 0) {
-    mbar_init(ld_full, 1);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(y_full, 1);
-    mbar_init(w_full, 4);
+    mbar_init(ld_b, 1);
+    mbar_init(ld_x, 1);
+    mbar_init(w_ready, 4);
+    mbar_init(x_free, 1);
     mbar_init(h_full, 1);
+    mbar_init(h_free, 4);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmX);
-    tma_prefetch_desc(&tmB);
-    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, 64);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t TM_H = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(ld_b, T_NN);
+      tma_load_2d(sB, &tmB, ld_b, g * SN, r);
+      tma_load_2d(sB + 16384, &tmB, ld_b, g * SN + 64, r);
+      int issued = 0;
+      for (int pb = 0; pb < npb; ++pb) {
+        if (pb > 0 && !mbar_wait(x_free, (pb - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(ld_x, T_NP);
+        tma_load_2d(sX, &tmX, ld_x, h * p.P + pb * SP, r);
+        ++issued;
+      }
+      mbar_wait(ld_b, 0, nullptr, p.status);  // no copy in flight at exit
+      if (issued > 0) mbar_wait(ld_x, (issued - 1) & 1, nullptr, p.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_H = umma_idesc_bf16(128, 64, true, true);
+      const uint32_t aB = smem_u32(sB), aX = smem_u32(sX);
+      bool ok = mbar_wait(ld_b, 0, abort_flag, p.status);
+      for (int pb = 0; pb < npb && ok; ++pb) {
+        if (!mbar_wait(w_ready, pb & 1, abort_flag, p.status)) break;
+        if (pb > 0 && !mbar_wait(h_free, (pb - 1) & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_H, mdesc(aB, kk), mdesc(aX, kk), ID_H, kk > 0);
+        tc_commit(x_free);
+        tc_commit(h_full);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int m = (warp & 3) * 32 + lane;  // chunk step s (W rows) / state row n (Hloc rows)
+    const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
+    const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
+    const float lam = chunk_cumsum(p.loga[si], m, s_part);
+    s_lam[m] = lam;
+    math_bar();
+    const float lam_end = s_lam[SL - 1];
+    if (m == 0) p.lamend[(int64_t)bh * p.nc + c] = lam_end;
+    const float w = __expf(lam_end - lam) * p.gamma[si];
+    for (int pb = 0; pb < npb; ++pb) {
+      if (!mbar_wait(ld_x, pb & 1, abort_flag, p.status)) break;
+      float xv[64];
+      load_row64(sX, m, xv);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) xv[i] *= w;
+      store_row64(sX, m, xv);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(w_ready);
+      if (!mbar_wait(h_full, pb & 1, abort_flag, p.status)) break;
+      tc_fence_after();
+      float hv[64];
+      tmem_row64(TM_H + lb, hv);
+      float* dst = p.hloc + (((int64_t)bh * p.nc + c) * SN + m) * p.P + pb * SP;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        reinterpret_cast<float4*>(dst)[i] = make_float4(hv[4 * i], hv[4 * i + 1], hv[4 * i + 2], hv[4 * i + 3]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(h_free);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(TM_H, 64);
+  }
+}
+
+// hs[bh, c] = state at the start of chunk c (bf16), from the chunk-local states.
+__global__ void __launch_bounds__(256) ssd_state_scan_kernel(SsdParams p) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // n * P + p within one state
+  const int64_t per = (int64_t)SN * p.P;
+  if (e >= per) return;
+  const int bh = blockIdx.y;
+  float hcur = 0.f;
+  const float* lamend = p.lamend + (int64_t)bh * p.nc;
+#pragma unroll 4
+  for (int c = 0; c < p.nc; ++c) {
+    const int64_t idx = ((int64_t)bh * p.nc + c) * per + e;
+    const float loc = p.hloc[idx];
+    p.hs[idx] = __float2bfloat16(hcur);
+    hcur = __expf(__ldg(lamend + c)) * hcur + loc;
+  }
+}
+
+struct OutSmem {
+  static constexpr int OFF_C = 0;
+  static constexpr int OFF_B = OFF_C + T_NN;  // B, then M (bf16, K-major over s)
+  static constexpr int OFF_X = OFF_B + T_NN;
+  static constexpr int OFF_H = OFF_X + T_NP;
+  static constexpr int OFF_VEC = OFF_H + T_NP;  // lam[128], gam[128], part[8]
+  static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4 + 64;
+  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(SSD_THREADS)
+    ssd_out_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH, SsdParams p) {
+  using L = OutSmem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sX = smem + L::OFF_X, *sH = smem + L::OFF_H;
+  float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
+  float* s_gam = s_lam + 128;
+  float* s_part = s_gam + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t *ld_cb = bars + 0, *s_full = bars + 1, *m_ready = bars + 2, *ld_xh = bars + 3, *y_full = bars + 4,
+           *y_free = bars + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int bh = blockIdx.x, c = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int g = h / (p.H / p.G);
+  const int r = b * p.S + c * SL;
+  const int npb = p.P / SP;
+  const int hrow = (bh * p.nc + c) * SN;
+  if (threadIdx.x == 0) {
+    mbar_init(ld_cb, 1);
+    mbar_init(s_full, 1);
+    mbar_init(m_ready, 4);
+    mbar_init(ld_xh, 1);
+    mbar_init(y_full, 1);
+    mbar_init(y_free, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t TM_S = tmem, TM_YD = tmem + 128, TM_YO = tmem + 192, TM_H = tmem + 256;
+  const uint32_t TM_S = tmem, TM_Y = tmem + 128;
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int c = 0; c < p.nc; ++c) {
-        if (c > 0 && !mbar_wait(h_full, (c - 1) & 1, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(ld_full, 2 * T_NN + T_NP);
-        const int r = row0 + c * SL;
-        tma_load_2d(sC, &tmC, ld_full, g * SN, r);
-        tma_load_2d(sC + 16384, &tmC, ld_full, g * SN + 64, r);
-        tma_load_2d(sB, &tmB, ld_full, g * SN, r);
-        tma_load_2d(sB + 16384, &tmB, ld_full, g * SN + 64, r);
-        tma_load_2d(sX, &tmX, ld_full, h * p.P + pb * SP, r);
+      mbar_arrive_expect_tx(ld_cb, 2 * T_NN);
+      tma_load_2d(sC, &tmC, ld_cb, g * SN, r);
+      tma_load_2d(sC + 16384, &tmC, ld_cb, g * SN + 64, r);
+      tma_load_2d(sB, &tmB, ld_cb, g * SN, r);
+      tma_load_2d(sB + 16384, &tmB, ld_cb, g * SN + 64, r);
+      int issued = 0;
+      for (int pb = 0; pb < npb; ++pb) {
+        // the previous p-block's X (D skip) and TMEM tile are done with
+        if (pb > 0 && !mbar_wait(y_free, (pb - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(ld_xh, 2 * T_NP);
+        tma_load_2d(sX, &tmX, ld_xh, h * p.P + pb * SP, r);
+        tma_load_2d(sH, &tmH, ld_xh, pb * SP, hrow);
+        ++issued;
       }
-      if (p.nc > 0) mbar_wait(ld_full, (p.nc - 1) & 1, nullptr, p.status);  // no copy in flight at exit
+      mbar_wait(ld_cb, 0, nullptr, p.status);  // no copy in flight at exit
+      if (issued > 0) mbar_wait(ld_xh, (issued - 1) & 1, nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t ID_Y = umma_idesc_bf16(128, 64, false, true);
-      constexpr uint32_t ID_H = umma_idesc_bf16(128, 64, true, true);
-      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aX = smem_u32(sX), aP = smem_u32(sP),
-                     aH = smem_u32(sH), aW = smem_u32(sW);
-      for (int c = 0; c < p.nc; ++c) {
-        if (!mbar_wait(ld_full, c & 1, abort_flag, p.status)) break;
+      const uint32_t aC = smem_u32(sC), aM = smem_u32(sB), aX = smem_u32(sX), aH = smem_u32(sH);
+      bool ok = mbar_wait(ld_cb, 0, abort_flag, p.status);
+      if (ok) {
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aB, kk), ID_S, kk != 0);
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aM, kk), ID_S, kk != 0);
         tc_commit(s_full);
-        if (!mbar_wait(p_full, c & 1, abort_flag, p.status)) break;
+        ok = mbar_wait(m_ready, 0, abort_flag, p.status);
+      }
+      for (int pb = 0; pb < npb && ok; ++pb) {
+        if (!mbar_wait(ld_xh, pb & 1, abort_flag, p.status)) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_YD, kdesc(aP, kk), mdesc(aX, kk), ID_Y, kk != 0);
-        if (c > 0) {
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_Y, kdesc(aM, kk), mdesc(aX, kk), ID_Y, kk != 0);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_YO, kdesc(aC, kk), mdesc(aH, kk), ID_Y, kk != 0);
-        }
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_Y, kdesc(aC, kk), mdesc(aH, kk), ID_Y, 1);
         tc_commit(y_full);
-        if (!mbar_wait(w_full, c & 1, abort_flag, p.status)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_H, mdesc(aB, kk), mdesc(aW, kk), ID_H, (c > 0 || kk > 0));
-        tc_commit(h_full);
       }
     }
     __syncwarp();
   } else {
-    const int m = (warp & 3) * 32 + lane;  // chunk row t (S, Y) / state row n (H)
+    const int m = (warp & 3) * 32 + lane;  // chunk step t
     const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
-    bool ok = true;
-    for (int c = 0; c < p.nc && ok; ++c) {
-      const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
-      const float lam = chunk_cumsum(p.loga[si], m, s_part);
-      const float gm = p.gamma[si];
-      s_lam[m] = lam;
-      s_gam[m] = gm;
-      math_bar();
-      const float lam_end = s_lam[SL - 1];
-      // previous chunk's state -> bf16 B operand (and the backward's copy), then decay it
-      if (c > 0) {
-        if (!mbar_wait(h_full, (c - 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        tc_fence_after();
-        float hv[64];
-        tmem_row64(TM_H + lb, hv);
-        store_row64(sH, m, hv);
-        __nv_bfloat16* hs = p.hs + (((int64_t)bh * p.nc + c) * SN + m) * p.P + pb * SP;
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          reinterpret_cast<uint4*>(hs)[q] =
-              make_uint4(pack_bf16(hv[q * 8], hv[q * 8 + 1]), pack_bf16(hv[q * 8 + 2], hv[q * 8 + 3]),
-                         pack_bf16(hv[q * 8 + 4], hv[q * 8 + 5]), pack_bf16(hv[q * 8 + 6], hv[q * 8 + 7]));
-        const float dec = __expf(lam_end);
-        uint32_t u0[32], u1[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          u0[i] = __float_as_uint(hv[i] * dec);
-          u1[i] = __float_as_uint(hv[32 + i] * dec);
-        }
-        tmem_st32(TM_H + lb, u0);
-        tmem_st32(TM_H + lb + 32, u1);
-        tc_wait_st();
-      } else {
-        // chunk 0 starts from a zero state; keep the stored copy consistent
-        __nv_bfloat16* hs = p.hs + (((int64_t)bh * p.nc + 0) * SN + m) * p.P + pb * SP;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(hs)[q] = make_uint4(0u, 0u, 0u, 0u);
-      }
-      // M = (C B^T) o decay o g  -> sP (bf16, K-major over s)
-      if (!mbar_wait(s_full, c & 1, abort_flag, p.status)) { ok = false; break; }
+    const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
+    const float lam = chunk_cumsum(p.loga[si], m, s_part);
+    s_lam[m] = lam;
+    s_gam[m] = p.gamma[si];
+    math_bar();
+    const float dsk = p.out ? p.dskip[p.dskip_per_row ? si : h] : 0.f;
+    bool ok = mbar_wait(s_full, 0, abort_flag, p.status);
+    if (ok) {
       tc_fence_after();
+      // M = (C B^T) o decay o g -> over B's tile (B was only needed for S)
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
         uint32_t sr[32];
@@ -273,61 +389,66 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
           float v[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int s = q * 32 + t + e;
-            v[e] = (s <= m) ? __uint_as_float(sr[t + e]) * __expf(lam - s_lam[s]) * s_gam[s] : 0.f;
+            const int s2 = q * 32 + t + e;
+            v[e] = (s2 <= m) ? __uint_as_float(sr[t + e]) * __expf(lam - s_lam[s2]) * s_gam[s2] : 0.f;
           }
           pk[t / 2] = pack_bf16(v[0], v[1]);
         }
+        // every thread of this warp has read its S row chunk before any M row lands in sB
+        __syncwarp();
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int ch = q * 4 + j;  // 8-column chunk 0..15
-          sw128_store16(sP + (ch >> 3) * 16384, m, ch & 7, make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]));
+          const int ch = q * 4 + j;
+          sw128_store16(sB + (ch >> 3) * 16384, m, ch & 7,
+                        make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]));
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      // W = diag(w) X, w_s = exp(lam_end - lam_s) g_s (row s = m); sW is free once
-      // the previous chunk's state MMA completed (waited above for c > 0)
-      {
-        float xv[64];
-        load_row64(sX, m, xv);
-        const float w = __expf(lam_end - lam) * gm;
+      // C row t scaled by exp(Lam_t): the inter-chunk term joins the same accumulator
+      const float el = __expf(lam);
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float cv[64];
+        load_row64(sC + half * 16384, m, cv);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) xv[i] *= w;
-        store_row64(sW, m, xv);
+        for (int i = 0; i < 64; ++i) cv[i] *= el;
+        store_row64(sC + half * 16384, m, cv);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(w_full);
-      // y = Yd + exp(lam_t) Yo
-      if (!mbar_wait(y_full, c & 1, abort_flag, p.status)) { ok = false; break; }
+      if (lane == 0) mbar_arrive(m_ready);
+    }
+    for (int pb = 0; pb < npb && ok; ++pb) {
+      if (!mbar_wait(y_full, pb & 1, abort_flag, p.status)) break;
       tc_fence_after();
-      float yd[64];
-      tmem_row64(TM_YD + lb, yd);
-      if (c > 0) {
-        float yo[64];
-        tmem_row64(TM_YO + lb, yo);
-        const float e = __expf(lam);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) yd[i] += e * yo[i];
-      }
-      float* yr = p.y + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
+      float yv[64];
+      tmem_row64(TM_Y + lb, yv);
+      const int64_t orow = (int64_t)(r + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
+      float* yr = p.y + orow;
 #pragma unroll
       for (int i = 0; i < 16; ++i)
-        reinterpret_cast<float4*>(yr)[i] = make_float4(yd[4 * i], yd[4 * i + 1], yd[4 * i + 2], yd[4 * i + 3]);
+        reinterpret_cast<float4*>(yr)[i] = make_float4(yv[4 * i], yv[4 * i + 1], yv[4 * i + 2], yv[4 * i + 3]);
+      if (p.out) {
+        float xv[64];
+        load_row64(sX, m, xv);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) yv[i] += dsk * xv[i];
+        uint4* orp = reinterpret_cast<uint4*>(p.out + orow);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          orp[q] = make_uint4(pack_bf16(yv[q * 8], yv[q * 8 + 1]), pack_bf16(yv[q * 8 + 2], yv[q * 8 + 3]),
+                              pack_bf16(yv[q * 8 + 4], yv[q * 8 + 5]), pack_bf16(yv[q * 8 + 6], yv[q * 8 + 7]));
+      }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(y_free);
     }
-    // the last state MMA must finish before TMEM is released
-    if (ok && p.nc > 0) mbar_wait(h_full, (p.nc - 1) & 1, abort_flag, p.status);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -797,19 +918,35 @@ bool ssd_tc_supported(int N, int P, int S) { return N == SN && P % SP == 0 && S 
 void launch_ssd_fwd(const SsdTcIO& io, cudaStream_t st) {
   OXI_CHECK(ssd_tc_supported(io.N, io.P, io.S), "tensor-core SSD needs N == 128, P % 64 == 0, S % 128 == 0");
   OXI_CHECK(io.H % io.G == 0, "heads must be a multiple of the B/C groups");
+  OXI_CHECK(io.hloc && io.lamend, "forward scratch missing");
   const int64_t T = (int64_t)io.B * io.S;
+  const int nc = io.S / SL;
   CUtensorMap tx = make_tmap_bf16(io.x, T, (int64_t)io.H * io.P, io.ldx, 64, SL);
   CUtensorMap tb = make_tmap_bf16(io.Bm, T, (int64_t)io.G * SN, io.ldb, 64, SL);
   CUtensorMap tc = make_tmap_bf16(io.Cm, T, (int64_t)io.G * SN, io.ldc, 64, SL);
+  const int64_t hrows = (int64_t)io.B * io.H * nc * SN;
+  CUtensorMap ths = make_tmap_bf16(io.hs, hrows, io.P, io.P, 64, SN);
   SsdParams p{};
-  p.B = io.B; p.S = io.S; p.H = io.H; p.P = io.P; p.G = io.G; p.nc = io.S / SL;
+  p.B = io.B; p.S = io.S; p.H = io.H; p.P = io.P; p.G = io.G; p.nc = nc;
   p.loga = io.loga; p.gamma = io.gamma; p.y = io.y;
   p.hs = reinterpret_cast<__nv_bfloat16*>(io.hs);
+  p.hloc = io.hloc; p.lamend = io.lamend;
+  p.out = reinterpret_cast<__nv_bfloat16*>(io.out);
+  p.dskip = io.dskip; p.dskip_per_row = io.dskip_per_row;
   p.status = io.status;
   static bool attr = false;
-  if (!attr) { set_smem(ssd_fwd_kernel, FwdSmem::TOTAL); attr = true; }
-  dim3 grid(io.B * io.H, io.P / SP);
-  ssd_fwd_kernel<<<grid, SSD_THREADS, FwdSmem::TOTAL, st>>>(tx, tb, tc, p);
+  if (!attr) {
+    set_smem(ssd_state_kernel, StateSmem::TOTAL);
+    set_smem(ssd_out_kernel, OutSmem::TOTAL);
+    attr = true;
+  }
+  const dim3 grid(io.B * io.H, nc);
+  ssd_state_kernel<<<grid, SSD_THREADS, StateSmem::TOTAL, st>>>(tx, tb, p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+  const int64_t per = (int64_t)SN * io.P;
+  ssd_state_scan_kernel<<<dim3((unsigned)((per + 255) / 256), io.B * io.H), 256, 0, st>>>(p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+  ssd_out_kernel<<<grid, SSD_THREADS, OutSmem::TOTAL, st>>>(tx, tb, tc, ths, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -36,8 +36,9 @@ class SSDChunkTC(torch.autograd.Function):
     """x [B, S, H, P] bf16; Bg/Cg [B, S, G, 128] (G divides H); loga/gamma [B, S, H].
 
     Without ``dskip``: y f32 [B, S, H, P].  With ``dskip`` ([H] per-head D, or [B, S, H]
-    per token): the D-skip epilogue (csrc/ssm_glue.cu) returns bf16(y + dskip x), and its
-    backward supplies <dy, y> for d loga in the same pass that adds dskip dy to dx."""
+    per token): the output kernel's D-skip epilogue returns bf16(y + dskip x); the
+    backward's D-skip pass (csrc/ssm_glue.cu) supplies <dy, y> for d loga in the same
+    pass that adds dskip dy to dx."""
 
     @staticmethod
     def forward(ctx, x, Bg, Cg, loga, gamma, dskip=None):
@@ -48,14 +49,14 @@ class SSDChunkTC(torch.autograd.Function):
         C2 = Cg.reshape(Bsz * S, G * N).to(torch.bfloat16).contiguous()
         la = loga.float().contiguous()
         ga = gamma.float().contiguous()
-        y, hs = ext().ssd_tc_fwd(x2, B2, C2, la, ga, Bsz, S, H, P, G, status(x.device))
         ctx.shape = (Bsz, S, H, P, G, N)
         ctx.dtypes = (x.dtype, Bg.dtype, Cg.dtype, None if dskip is None else dskip.dtype)
         if dskip is None:
+            y, hs = ext().ssd_tc_fwd(x2, B2, C2, la, ga, Bsz, S, H, P, G, status(x.device))
             ctx.save_for_backward(x2, B2, C2, la, ga, hs, y)
             return y.view(Bsz, S, H, P)
         dsk = dskip.float().contiguous()
-        out = ext().dskip_fwd(y, x2, dsk, H)
+        y, hs, out = ext().ssd_tc_fwd(x2, B2, C2, la, ga, Bsz, S, H, P, G, status(x.device), dsk)
         ctx.save_for_backward(x2, B2, C2, la, ga, hs, y, dsk)
         return out.view(Bsz, S, H, P)
 
