@@ -570,6 +570,10 @@ std::vector<torch::Tensor> ssd_tc_bwd(torch::Tensor x, torch::Tensor Bm, torch::
   io.hs = hs.data_ptr(); io.dy = dy.data_ptr(); io.dhs = dhs.data_ptr();
   io.dx = dx.data_ptr<float>(); io.dB = dB.data_ptr<float>(); io.dC = dC.data_ptr<float>();
   io.dgamma = dg.data_ptr<float>();
+  const int64_t nc = S / 128;
+  auto hloc = torch::empty({B * H * nc * 128, P}, f32);
+  auto lamend = torch::empty({B * H * nc}, f32);
+  io.hloc = hloc.data_ptr<float>(); io.lamend = lamend.data_ptr<float>();
   io.status = status_ptr(status);
   oxi::launch_ssd_bwd(io, stream());
   return {dx, dB, dC, dg};

@@ -14,10 +14,10 @@
 // Forward: chunk-parallel in three phases (chunk-local end states, an
 // element-wise scan over chunks, then the outputs; see below).
 //
-// Backward, pass 1 (reverse over chunks, per (b, h, p-block)), dH = adjoint of
-// H_end:   dX = M^T dY + diag(w) B dH ;  dH_prev = exp(Lam_L) dH + C^T diag(exp Lam) dY
-//          dg_s += exp(Lam_L - Lam_s) <x_s, (B dH)_s>
-//          (stores every chunk's dH, bf16, for pass 2)
+// Backward, chunk-parallel like the forward, dH = adjoint of a chunk's end state:
+//   dH_prev = exp(Lam_L) dH + C^T diag(exp Lam) dY  (chunk-local part per chunk,
+//            then an element-wise reverse scan storing every chunk's dH, bf16)
+//   dX = M^T dY + diag(w) B dH ; dg_s += exp(Lam_L - Lam_s) <x_s, (B dH)_s>  (ssd_dx_kernel)
 // Backward, pass 2 (one CTA per chunk, all p-blocks): dM = dY X^T, dS = dM o D o g,
 //          dC = dS B + diag(exp Lam) dY H_prev^T ,  dB = dS^T C + diag(w) X dH^T
 //          dg_s += sum_t dM[t,s] S[t,s] D[t,s]
@@ -138,6 +138,10 @@ struct StateSmem {
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
 };
 
+// REVERSE = false: Hloc = B^T diag(w) X (forward).  REVERSE = true: the chunk's
+// own part of the adjoint carried to the previous chunk, C^T diag(exp Lam) dY
+// (tmB then maps C and tmX maps dY).
+template <bool REVERSE>
 __global__ void __launch_bounds__(SSD_THREADS)
     ssd_state_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB, SsdParams p) {
   using L = StateSmem;
@@ -219,7 +223,7 @@ __global__ void __launch_bounds__(SSD_THREADS)
     math_bar();
     const float lam_end = s_lam[SL - 1];
     if (m == 0) p.lamend[(int64_t)bh * p.nc + c] = lam_end;
-    const float w = __expf(lam_end - lam) * p.gamma[si];
+    const float w = REVERSE ? __expf(lam) : __expf(lam_end - lam) * p.gamma[si];
     for (int pb = 0; pb < npb; ++pb) {
       if (!mbar_wait(ld_x, pb & 1, abort_flag, p.status)) break;
       float xv[64];
@@ -251,20 +255,26 @@ __global__ void __launch_bounds__(SSD_THREADS)
   }
 }
 
-// hs[bh, c] = state at the start of chunk c (bf16), from the chunk-local states.
-__global__ void __launch_bounds__(256) ssd_state_scan_kernel(SsdParams p) {
+// Forward: out[bh, c] = state at the start of chunk c, over c = 0, 1, ...
+// Reverse: out[bh, c] = adjoint of chunk c's end state, over c = nc-1, nc-2, ...
+// Both: H <- exp(Lam_L,c) H + loc[c] after storing out[c] (bf16).
+template <bool REVERSE>
+__global__ void __launch_bounds__(256) ssd_state_scan_kernel(const float* __restrict__ loc,
+                                                             const float* __restrict__ lamend_all,
+                                                             __nv_bfloat16* __restrict__ out, int nc, int P) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // n * P + p within one state
-  const int64_t per = (int64_t)SN * p.P;
+  const int64_t per = (int64_t)SN * P;
   if (e >= per) return;
   const int bh = blockIdx.y;
   float hcur = 0.f;
-  const float* lamend = p.lamend + (int64_t)bh * p.nc;
+  const float* lamend = lamend_all + (int64_t)bh * nc;
 #pragma unroll 4
-  for (int c = 0; c < p.nc; ++c) {
-    const int64_t idx = ((int64_t)bh * p.nc + c) * per + e;
-    const float loc = p.hloc[idx];
-    p.hs[idx] = __float2bfloat16(hcur);
-    hcur = __expf(__ldg(lamend + c)) * hcur + loc;
+  for (int i = 0; i < nc; ++i) {
+    const int c = REVERSE ? nc - 1 - i : i;
+    const int64_t idx = ((int64_t)bh * nc + c) * per + e;
+    const float l = loc[idx];
+    out[idx] = __float2bfloat16(hcur);
+    hcur = __expf(__ldg(lamend + c)) * hcur + l;
   }
 }
 
@@ -452,75 +462,81 @@ __global__ void __launch_bounds__(SSD_THREADS)
   }
 }
 
-// ====================================================== backward, pass 1
-struct Bwd1Smem {
-  static constexpr int OFF_C = 0;
+// ============================================ chunk-parallel dx
+// One CTA per (b, h, chunk), all p-blocks: dX = M^T dY + diag(w) B dH (dH = the
+// chunk-end adjoint from the reverse scan) and dg_s += exp(Lam_L - Lam_s) <x_s, (B dH)_s>.
+// M is written over C's tile once S = C B^T has been read; x rows come from global.
+struct DxSmem {
+  static constexpr int OFF_C = 0;  // C, then M
   static constexpr int OFF_B = OFF_C + T_NN;
-  static constexpr int OFF_X = OFF_B + T_NN;
-  static constexpr int OFF_DY = OFF_X + T_NP;
-  static constexpr int OFF_P = OFF_DY + T_NP;
-  static constexpr int OFF_E = OFF_P + T_NN;
-  static constexpr int OFF_DH = OFF_E + T_NP;
-  static constexpr int OFF_VEC = OFF_DH + T_NP;
+  static constexpr int OFF_DY = OFF_B + T_NN;
+  static constexpr int OFF_DH = OFF_DY + T_NP;
+  static constexpr int OFF_VEC = OFF_DH + T_NP;  // lam[128], gam[128], part[8]
   static constexpr int OFF_BAR = OFF_VEC + 2 * 128 * 4 + 64;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
 };
 
-__global__ void __launch_bounds__(SSD_THREADS, 1)
-    ssd_bwd1_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmDY, SsdParams p) {
-  using L = Bwd1Smem;
+__global__ void __launch_bounds__(SSD_THREADS)
+    ssd_dx_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
+                  const __grid_constant__ CUtensorMap tmDY, const __grid_constant__ CUtensorMap tmDH,
+                  const __nv_bfloat16* __restrict__ x, int64_t ldx, SsdParams p) {
+  using L = DxSmem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sX = smem + L::OFF_X, *sDY = smem + L::OFF_DY,
-          *sP = smem + L::OFF_P, *sE = smem + L::OFF_E, *sDH = smem + L::OFF_DH;
+  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sDY = smem + L::OFF_DY, *sDH = smem + L::OFF_DH;
   float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
   float* s_gam = s_lam + 128;
   float* s_part = s_gam + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t *ld_full = bars + 0, *s_full = bars + 1, *p_full = bars + 2, *m_full = bars + 3, *t_free = bars + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+  uint64_t *ld_cb = bars + 0, *s_full = bars + 1, *m_ready = bars + 2, *ld_t = bars + 3, *d_full = bars + 4,
+           *d_free = bars + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int bh = blockIdx.x, pb = blockIdx.y;
+  const int bh = blockIdx.x, c = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int g = h / (p.H / p.G);
-  const int row0 = b * p.S;
+  const int r = b * p.S + c * SL;
+  const int npb = p.P / SP;
+  const int hrow = (bh * p.nc + c) * SN;
   if (threadIdx.x == 0) {
-    mbar_init(ld_full, 1);
+    mbar_init(ld_cb, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(m_full, 1);
-    mbar_init(t_free, 4);
+    mbar_init(m_ready, 4);
+    mbar_init(ld_t, 1);
+    mbar_init(d_full, 1);
+    mbar_init(d_free, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t TM_S = tmem, TM_DX = tmem + 128, TM_BDH = tmem + 192, TM_DH = tmem + 256;
+  const uint32_t TM_S = tmem, TM_DX = tmem + 128, TM_BDH = tmem + 192;
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < p.nc; ++i) {
-        const int c = p.nc - 1 - i;
-        if (i > 0 && !mbar_wait(t_free, (i - 1) & 1, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(ld_full, 2 * T_NN + 2 * T_NP);
-        const int r = row0 + c * SL;
-        tma_load_2d(sC, &tmC, ld_full, g * SN, r);
-        tma_load_2d(sC + 16384, &tmC, ld_full, g * SN + 64, r);
-        tma_load_2d(sB, &tmB, ld_full, g * SN, r);
-        tma_load_2d(sB + 16384, &tmB, ld_full, g * SN + 64, r);
-        tma_load_2d(sX, &tmX, ld_full, h * p.P + pb * SP, r);
-        tma_load_2d(sDY, &tmDY, ld_full, h * p.P + pb * SP, r);
+      mbar_arrive_expect_tx(ld_cb, 2 * T_NN);
+      tma_load_2d(sC, &tmC, ld_cb, g * SN, r);
+      tma_load_2d(sC + 16384, &tmC, ld_cb, g * SN + 64, r);
+      tma_load_2d(sB, &tmB, ld_cb, g * SN, r);
+      tma_load_2d(sB + 16384, &tmB, ld_cb, g * SN + 64, r);
+      int issued = 0;
+      for (int pb = 0; pb < npb; ++pb) {
+        if (pb > 0 && !mbar_wait(d_free, (pb - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(ld_t, 2 * T_NP);
+        tma_load_2d(sDY, &tmDY, ld_t, h * p.P + pb * SP, r);
+        tma_load_2d(sDH, &tmDH, ld_t, pb * SP, hrow);
+        ++issued;
       }
-      if (p.nc > 0) mbar_wait(ld_full, (p.nc - 1) & 1, nullptr, p.status);
+      mbar_wait(ld_cb, 0, nullptr, p.status);  // no copy in flight at exit
+      if (issued > 0) mbar_wait(ld_t, (issued - 1) & 1, nullptr, p.status);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -528,79 +544,38 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       constexpr uint32_t ID_S = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t ID_DX = umma_idesc_bf16(128, 64, true, true);
       constexpr uint32_t ID_BDH = umma_idesc_bf16(128, 64, false, true);
-      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aDY = smem_u32(sDY), aP = smem_u32(sP),
-                     aE = smem_u32(sE), aDH = smem_u32(sDH);
-      for (int i = 0; i < p.nc; ++i) {
-        if (!mbar_wait(ld_full, i & 1, abort_flag, p.status)) break;
+      const uint32_t aM = smem_u32(sC), aB = smem_u32(sB), aDY = smem_u32(sDY), aDH = smem_u32(sDH);
+      bool ok = mbar_wait(ld_cb, 0, abort_flag, p.status);
+      if (ok) {
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aB, kk), ID_S, kk != 0);
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aM, kk), kdesc(aB, kk), ID_S, kk != 0);
         tc_commit(s_full);
-        if (!mbar_wait(p_full, i & 1, abort_flag, p.status)) break;
+        ok = mbar_wait(m_ready, 0, abort_flag, p.status);
+      }
+      for (int pb = 0; pb < npb && ok; ++pb) {
+        if (!mbar_wait(ld_t, pb & 1, abort_flag, p.status)) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DX, mdesc(aP, kk), mdesc(aDY, kk), ID_DX, kk != 0);
-        if (i > 0) {  // dH of the last chunk is zero
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DX, mdesc(aM, kk), mdesc(aDY, kk), ID_DX, kk != 0);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_BDH, kdesc(aB, kk), mdesc(aDH, kk), ID_BDH, kk != 0);
-        }
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DH, mdesc(aC, kk), mdesc(aE, kk), ID_DX, (i > 0 || kk > 0));
-        tc_commit(m_full);
+        for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_BDH, kdesc(aB, kk), mdesc(aDH, kk), ID_BDH, kk != 0);
+        tc_commit(d_full);
       }
     }
     __syncwarp();
   } else {
-    const int m = (warp & 3) * 32 + lane;
+    const int m = (warp & 3) * 32 + lane;  // chunk step (t for M rows, s for dx rows)
     const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
-    bool ok = true;
-    for (int i = 0; i < p.nc && ok; ++i) {
-      const int c = p.nc - 1 - i;
-      const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
-      const float lam = chunk_cumsum(p.loga[si], m, s_part);
-      const float gm = p.gamma[si];
-      s_lam[m] = lam;
-      s_gam[m] = gm;
-      math_bar();
-      const float lam_end = s_lam[SL - 1];
-      if (!mbar_wait(ld_full, i & 1, abort_flag, p.status)) { ok = false; break; }
-      // dH (adjoint of this chunk's end state) -> bf16 operand + stored copy, then decay it
-      if (i > 0) {
-        float hv[64];
-        tmem_row64(TM_DH + lb, hv);
-        store_row64(sDH, m, hv);
-        __nv_bfloat16* dst = p.dhs + (((int64_t)bh * p.nc + c) * SN + m) * p.P + pb * SP;
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          reinterpret_cast<uint4*>(dst)[q] =
-              make_uint4(pack_bf16(hv[q * 8], hv[q * 8 + 1]), pack_bf16(hv[q * 8 + 2], hv[q * 8 + 3]),
-                         pack_bf16(hv[q * 8 + 4], hv[q * 8 + 5]), pack_bf16(hv[q * 8 + 6], hv[q * 8 + 7]));
-        const float dec = __expf(lam_end);
-        uint32_t u0[32], u1[32];
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          u0[k] = __float_as_uint(hv[k] * dec);
-          u1[k] = __float_as_uint(hv[32 + k] * dec);
-        }
-        tmem_st32(TM_DH + lb, u0);
-        tmem_st32(TM_DH + lb + 32, u1);
-        tc_wait_st();
-      } else {
-        __nv_bfloat16* dst = p.dhs + (((int64_t)bh * p.nc + c) * SN + m) * p.P + pb * SP;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(dst)[q] = make_uint4(0u, 0u, 0u, 0u);
-      }
-      // E = diag(exp lam) dY (row t = m)
-      {
-        float dv[64];
-        load_row64(sDY, m, dv);
-        const float e = __expf(lam);
-#pragma unroll
-        for (int k = 0; k < 64; ++k) dv[k] *= e;
-        store_row64(sE, m, dv);
-      }
-      // M = (C B^T) o decay o g -> sP
-      if (!mbar_wait(s_full, i & 1, abort_flag, p.status)) { ok = false; break; }
+    const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
+    const float lam = chunk_cumsum(p.loga[si], m, s_part);
+    const float gm = p.gamma[si];
+    s_lam[m] = lam;
+    s_gam[m] = gm;
+    math_bar();
+    const float lam_end = s_lam[SL - 1];
+    bool ok = mbar_wait(s_full, 0, abort_flag, p.status);
+    if (ok) {
       tc_fence_after();
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
@@ -613,54 +588,64 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
           float v[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int s = q * 32 + t + e;
-            v[e] = (s <= m) ? __uint_as_float(sr[t + e]) * __expf(lam - s_lam[s]) * s_gam[s] : 0.f;
+            const int s2 = q * 32 + t + e;
+            v[e] = (s2 <= m) ? __uint_as_float(sr[t + e]) * __expf(lam - s_lam[s2]) * s_gam[s2] : 0.f;
           }
           pk[t / 2] = pack_bf16(v[0], v[1]);
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int ch = q * 4 + j;
-          sw128_store16(sP + (ch >> 3) * 16384, m, ch & 7, make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]));
+          sw128_store16(sC + (ch >> 3) * 16384, m, ch & 7,
+                        make_uint4(pk[j * 4], pk[j * 4 + 1], pk[j * 4 + 2], pk[j * 4 + 3]));
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      // dx (row s = m) = dX + w_s (B dH)_s ;  dg_s += exp(lam_end - lam_s) <x_s, (B dH)_s>
-      if (!mbar_wait(m_full, i & 1, abort_flag, p.status)) { ok = false; break; }
+      if (lane == 0) mbar_arrive(m_ready);
+    }
+    const float dec = __expf(lam_end - lam);
+    const float w = dec * gm;
+    float dot = 0.f;
+    const bool last = c == p.nc - 1;  // the last chunk's end adjoint is zero
+    for (int pb = 0; pb < npb && ok; ++pb) {
+      if (!mbar_wait(d_full, pb & 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
       float dxv[64];
       tmem_row64(TM_DX + lb, dxv);
-      if (i > 0) {
-        float bd[64], xv[64];
+      if (!last) {
+        float bd[64];
         tmem_row64(TM_BDH + lb, bd);
-        load_row64(sX, m, xv);
-        const float dec = __expf(lam_end - lam);
-        const float w = dec * gm;
-        float dot = 0.f;
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)(r + m) * ldx + h * p.P + pb * SP);
 #pragma unroll
-        for (int k = 0; k < 64; ++k) {
-          dxv[k] += w * bd[k];
-          dot += xv[k] * bd[k];
+        for (int q = 0; q < 8; ++q) {
+          const uint4 u = __ldg(xr + q);
+          const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = unpack_bf16(wv[i]);
+            dot += f.x * bd[q * 8 + 2 * i] + f.y * bd[q * 8 + 2 * i + 1];
+          }
         }
-        atomicAdd(p.dgamma + si, dec * dot);
+#pragma unroll
+        for (int k = 0; k < 64; ++k) dxv[k] += w * bd[k];
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(t_free);  // tiles (x, dy, B, C) may be reloaded
-      float* dr = p.dx + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
+      if (lane == 0) mbar_arrive(d_free);
+      float* dr = p.dx + (int64_t)(r + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
 #pragma unroll
       for (int k = 0; k < 16; ++k)
         reinterpret_cast<float4*>(dr)[k] = make_float4(dxv[4 * k], dxv[4 * k + 1], dxv[4 * k + 2], dxv[4 * k + 3]);
     }
+    if (ok && !last) atomicAdd(p.dgamma + si, dec * dot);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -936,15 +921,16 @@ void launch_ssd_fwd(const SsdTcIO& io, cudaStream_t st) {
   p.status = io.status;
   static bool attr = false;
   if (!attr) {
-    set_smem(ssd_state_kernel, StateSmem::TOTAL);
+    set_smem(ssd_state_kernel<false>, StateSmem::TOTAL);
     set_smem(ssd_out_kernel, OutSmem::TOTAL);
     attr = true;
   }
   const dim3 grid(io.B * io.H, nc);
-  ssd_state_kernel<<<grid, SSD_THREADS, StateSmem::TOTAL, st>>>(tx, tb, p);
+  ssd_state_kernel<false><<<grid, SSD_THREADS, StateSmem::TOTAL, st>>>(tx, tb, p);
   OXI_CUDA_CHECK(cudaGetLastError());
   const int64_t per = (int64_t)SN * io.P;
-  ssd_state_scan_kernel<<<dim3((unsigned)((per + 255) / 256), io.B * io.H), 256, 0, st>>>(p);
+  ssd_state_scan_kernel<false><<<dim3((unsigned)((per + 255) / 256), io.B * io.H), 256, 0, st>>>(
+      p.hloc, p.lamend, p.hs, nc, io.P);
   OXI_CUDA_CHECK(cudaGetLastError());
   ssd_out_kernel<<<grid, SSD_THREADS, OutSmem::TOTAL, st>>>(tx, tb, tc, ths, p);
   OXI_CUDA_CHECK(cudaGetLastError());
@@ -967,16 +953,28 @@ void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st) {
   p.hs = reinterpret_cast<__nv_bfloat16*>(io.hs);
   p.dhs = reinterpret_cast<__nv_bfloat16*>(io.dhs);
   p.dx = io.dx; p.dB = io.dB; p.dC = io.dC; p.dgamma = io.dgamma;
+  p.hloc = io.hloc; p.lamend = io.lamend;
   p.status = io.status;
+  OXI_CHECK(io.hloc && io.lamend, "backward scratch missing");
   static bool attr = false;
   if (!attr) {
-    set_smem(ssd_bwd1_kernel, Bwd1Smem::TOTAL);
+    set_smem(ssd_state_kernel<true>, StateSmem::TOTAL);
+    set_smem(ssd_dx_kernel, DxSmem::TOTAL);
     set_smem(ssd_bwd2_kernel, Bwd2Smem::TOTAL);
     attr = true;
   }
-  ssd_bwd1_kernel<<<dim3(io.B * io.H, io.P / SP), SSD_THREADS, Bwd1Smem::TOTAL, st>>>(tx, tb, tc, tdy, p);
+  const dim3 grid(io.B * io.H, nc);
+  // chunk-local adjoints C^T diag(exp Lam) dY, then the reverse scan -> chunk-end adjoints
+  ssd_state_kernel<true><<<grid, SSD_THREADS, StateSmem::TOTAL, st>>>(tdy, tc, p);
   OXI_CUDA_CHECK(cudaGetLastError());
-  ssd_bwd2_kernel<<<dim3(io.B * io.H, nc), SSD_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs, p);
+  const int64_t per = (int64_t)SN * io.P;
+  ssd_state_scan_kernel<true><<<dim3((unsigned)((per + 255) / 256), io.B * io.H), 256, 0, st>>>(
+      p.hloc, p.lamend, p.dhs, nc, io.P);
+  OXI_CUDA_CHECK(cudaGetLastError());
+  ssd_dx_kernel<<<grid, SSD_THREADS, DxSmem::TOTAL, st>>>(tb, tc, tdy, tdhs, reinterpret_cast<const __nv_bfloat16*>(io.x),
+                                                          io.ldx, p);
+  OXI_CUDA_CHECK(cudaGetLastError());
+  ssd_bwd2_kernel<<<grid, SSD_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
