@@ -651,24 +651,21 @@ __global__ void __launch_bounds__(SSD_THREADS)
 
 // ====================================================== backward, pass 2
 // One CTA per (b, h, chunk) covering every P column, so dB / dC rows are
-// written once (no atomics):
-//   A: dM = sum_pb dY_pb X_pb^T ; S = C B^T            (TMEM, accumulated over p-blocks)
-//   B: dS = dM o D o g (smem bf16), dg_s += sum_t dM o S o D
-//   C: dC = dS B + sum_pb E_pb H_pb^T ,  dB = dS^T C + sum_pb W_pb dH_pb^T
-//      (E = diag(exp lam) dY, W = diag(w) X, per p-block; dC / dB reuse S / dM)
+// written once (no atomics).  Per p-block, straight from the loaded tiles
+// (double-buffered, no math in between):
+//   dM += dY X^T ;  dCp += dY H^T ;  dBp += X dH^T          (four TMEM tiles with S)
+// then dS = dM o D o g (smem bf16), dg_s += sum_t dM o S o D, and
+//   dC = dS B + diag(exp lam) dCp ,  dB = dS^T C + diag(w) dBp
+// with the diagonal scalings applied while reading TMEM out.
 struct Bwd2Smem {
   static constexpr int OFF_C = 0;
   static constexpr int OFF_B = OFF_C + T_NN;
   static constexpr int OFF_DS = OFF_B + T_NN;
-  static constexpr int OFF_X = OFF_DS + T_NN;
-  static constexpr int OFF_DY = OFF_X + T_NP;
-  static constexpr int OFF_H = OFF_DY + T_NP;
-  static constexpr int OFF_DH = OFF_H + T_NP;
-  static constexpr int OFF_E = OFF_DH + T_NP;
-  static constexpr int OFF_W = OFF_E + T_NP;
-  static constexpr int OFF_VEC = OFF_W + T_NP;      // lam, gam, colsum, part
+  static constexpr int OFF_T = OFF_DS + T_NN;            // 2 buffers x (X, dY, H, dH)
+  static constexpr int T_SET = 4 * T_NP;
+  static constexpr int OFF_VEC = OFF_T + 2 * T_SET;      // lam, gam, colsum, part
   static constexpr int OFF_BAR = OFF_VEC + 3 * 128 * 4 + 64;
-  static constexpr int TOTAL = OFF_BAR + 256 + 1024;
+  static constexpr int TOTAL = OFF_BAR + 128 + 1024;
 };
 
 __global__ void __launch_bounds__(SSD_THREADS, 1)
@@ -678,17 +675,15 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
   using L = Bwd2Smem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sDS = smem + L::OFF_DS, *sX = smem + L::OFF_X,
-          *sDY = smem + L::OFF_DY, *sH = smem + L::OFF_H, *sDH = smem + L::OFF_DH, *sE = smem + L::OFF_E,
-          *sW = smem + L::OFF_W;
+  uint8_t *sC = smem + L::OFF_C, *sB = smem + L::OFF_B, *sDS = smem + L::OFF_DS, *sT = smem + L::OFF_T;
   float* s_lam = reinterpret_cast<float*>(smem + L::OFF_VEC);
   float* s_gam = s_lam + 128;
   float* s_col = s_gam + 128;
   float* s_part = s_col + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t *cb_full = bars + 0, *t_full = bars + 1, *t_free = bars + 2, *sdm_full = bars + 3, *ds_ready = bars + 4,
-           *ew_ready = bars + 5, *out_full = bars + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  uint64_t *cb_full = bars + 0, *t_full = bars + 1 /* [2] */, *t_free = bars + 3 /* [2] */, *sdm_full = bars + 5,
+           *ds_ready = bars + 6, *out_full = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -699,27 +694,28 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
   const int r = row0 + c * SL;
   const int hrow = (bh * p.nc + c) * SN;
   const int npb = p.P / SP;
-  const int nload = 2 * npb;  // pass A loads (x, dy), pass C loads (x, dy, H, dH)
   if (threadIdx.x == 0) {
     mbar_init(cb_full, 1);
-    mbar_init(t_full, 1);
-    mbar_init(t_free, 1);
+    mbar_init(&t_full[0], 1);
+    mbar_init(&t_full[1], 1);
+    mbar_init(&t_free[0], 1);
+    mbar_init(&t_free[1], 1);
     mbar_init(sdm_full, 1);
     mbar_init(ds_ready, 4);
-    mbar_init(ew_ready, 4);
     mbar_init(out_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t TM_S = tmem, TM_DM = tmem + 128;  // reused: dC in TM_S, dB in TM_DM
+  // S, then dC = dS B;  dM, then dB = dS^T C;  dY H^T;  X dH^T
+  const uint32_t TM_S = tmem, TM_DM = tmem + 128, TM_CP = tmem + 256, TM_BP = tmem + 384;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -728,20 +724,19 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       tma_load_2d(sC + 16384, &tmC, cb_full, g * SN + 64, r);
       tma_load_2d(sB, &tmB, cb_full, g * SN, r);
       tma_load_2d(sB + 16384, &tmB, cb_full, g * SN + 64, r);
-      int li = 0;
-      for (; li < nload; ++li) {
-        const int pb = li % npb;
-        const bool pass_c = li >= npb;
-        if (li > 0 && !mbar_wait(t_free, (li - 1) & 1, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(t_full, (pass_c ? 4 : 2) * T_NP);
-        tma_load_2d(sX, &tmX, t_full, h * p.P + pb * SP, r);
-        tma_load_2d(sDY, &tmDY, t_full, h * p.P + pb * SP, r);
-        if (pass_c) {
-          tma_load_2d(sH, &tmHS, t_full, pb * SP, hrow);
-          tma_load_2d(sDH, &tmDHS, t_full, pb * SP, hrow);
-        }
+      int pb = 0;
+      for (; pb < npb; ++pb) {
+        const int buf = pb & 1;
+        if (pb >= 2 && !mbar_wait(&t_free[buf], ((pb >> 1) - 1) & 1, abort_flag, p.status)) break;
+        uint8_t* t = sT + buf * L::T_SET;
+        mbar_arrive_expect_tx(&t_full[buf], 4 * T_NP);
+        tma_load_2d(t, &tmX, &t_full[buf], h * p.P + pb * SP, r);
+        tma_load_2d(t + T_NP, &tmDY, &t_full[buf], h * p.P + pb * SP, r);
+        tma_load_2d(t + 2 * T_NP, &tmHS, &t_full[buf], pb * SP, hrow);
+        tma_load_2d(t + 3 * T_NP, &tmDHS, &t_full[buf], pb * SP, hrow);
       }
-      if (li > 0) mbar_wait(t_full, (li - 1) & 1, nullptr, p.status);  // no copy in flight at exit
+      // no copy in flight at exit: the last load into each buffer has landed
+      for (int q = std::max(0, pb - 2); q < pb; ++q) mbar_wait(&t_full[q & 1], (q >> 1) & 1, nullptr, p.status);
       mbar_wait(cb_full, 0, nullptr, p.status);
     }
     __syncwarp();
@@ -750,22 +745,26 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       constexpr uint32_t ID_SS = umma_idesc_bf16(128, 128, false, false);
       constexpr uint32_t ID_DC1 = umma_idesc_bf16(128, 128, false, true);
       constexpr uint32_t ID_DB1 = umma_idesc_bf16(128, 128, true, true);
-      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aX = smem_u32(sX), aDY = smem_u32(sDY),
-                     aH = smem_u32(sH), aDH = smem_u32(sDH), aDS = smem_u32(sDS), aE = smem_u32(sE),
-                     aW = smem_u32(sW);
+      const uint32_t aC = smem_u32(sC), aB = smem_u32(sB), aDS = smem_u32(sDS);
       bool ok = mbar_wait(cb_full, 0, abort_flag, p.status);
       if (ok) {
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aC, kk), kdesc(aB, kk), ID_SS, kk != 0);
       }
-      // pass A: dM = sum over p-blocks of dY X^T
       for (int pb = 0; pb < npb && ok; ++pb) {
-        if (!mbar_wait(t_full, pb & 1, abort_flag, p.status)) { ok = false; break; }
+        const int buf = pb & 1;
+        if (!mbar_wait(&t_full[buf], (pb >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t aX = smem_u32(sT + buf * L::T_SET), aDY = aX + T_NP, aH = aX + 2 * T_NP, aDH = aX + 3 * T_NP;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_DM, kdesc(aDY, kk), kdesc(aX, kk), ID_SS, (pb > 0 || kk > 0));
-        tc_commit(t_free);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc = (pb > 0 || kk > 0) ? 1u : 0u;
+          tc_mma_f16(TM_DM, kdesc(aDY, kk), kdesc(aX, kk), ID_SS, acc);
+          tc_mma_f16(TM_CP, kdesc(aDY, kk), kdesc(aH, kk), ID_SS, acc);
+          tc_mma_f16(TM_BP, kdesc(aX, kk), kdesc(aDH, kk), ID_SS, acc);
+        }
+        tc_commit(&t_free[buf]);
       }
       if (ok) {
         tc_commit(sdm_full);
@@ -778,18 +777,8 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
         for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_S, kdesc(aDS, kk), mdesc(aB, kk), ID_DC1, kk != 0);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) tc_mma_f16(TM_DM, mdesc(aDS, kk), mdesc(aC, kk), ID_DB1, kk != 0);
+        tc_commit(out_full);
       }
-      // pass C: + E H^T and + W dH^T per p-block
-      for (int pb = 0; pb < npb && ok; ++pb) {
-        if (!mbar_wait(ew_ready, pb & 1, abort_flag, p.status)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_S, kdesc(aE, kk), kdesc(aH, kk), ID_SS, 1u);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc_mma_f16(TM_DM, kdesc(aW, kk), kdesc(aDH, kk), ID_SS, 1u);
-        tc_commit(t_free);
-      }
-      if (ok) tc_commit(out_full);
     }
     __syncwarp();
   } else {
@@ -819,14 +808,14 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
           float v[2];
 #pragma unroll
           for (int e2 = 0; e2 < 2; ++e2) {
-            const int s = q * 32 + t + e2;
-            const float d = (s <= m) ? __expf(lam - s_lam[s]) : 0.f;
+            const int s2 = q * 32 + t + e2;
+            const float d = (s2 <= m) ? __expf(lam - s_lam[s2]) : 0.f;
             const float dm = __uint_as_float(dr[t + e2]) * d;
-            v[e2] = dm * s_gam[s];
+            v[e2] = dm * s_gam[s2];
             float cs = dm * __uint_as_float(sr[t + e2]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-            if (lane == 0) atomicAdd(&s_col[s], cs);
+            if (lane == 0) atomicAdd(&s_col[s2], cs);
           }
           pk[t / 2] = pack_bf16(v[0], v[1]);
         }
@@ -843,43 +832,30 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       math_bar();
       atomicAdd(p.dgamma + si, s_col[m]);
     }
-    // pass C inputs: E = diag(exp lam) dY_pb, W = diag(w) X_pb (row m)
-    const float e = __expf(lam);
-    const float w = __expf(lam_end - lam) * gm;
-    for (int pb = 0; pb < npb && ok; ++pb) {
-      const int li = npb + pb;
-      if (!mbar_wait(t_full, li & 1, abort_flag, p.status)) { ok = false; break; }
-      // E / W of the previous p-block were read by the MMAs that freed this load slot
-      float v[64];
-      load_row64(sDY, m, v);
-#pragma unroll
-      for (int k = 0; k < 64; ++k) v[k] *= e;
-      store_row64(sE, m, v);
-      load_row64(sX, m, v);
-#pragma unroll
-      for (int k = 0; k < 64; ++k) v[k] *= w;
-      store_row64(sW, m, v);
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ew_ready);
-    }
     if (ok && mbar_wait(out_full, 0, abort_flag, p.status)) {
       tc_fence_after();
       // row m: dC_t (t = m) and dB_s (s = m), 128 values each, written once
+      const float e = __expf(lam);
+      const float w = __expf(lam_end - lam) * gm;
       float* dcr = p.dC + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
       float* dbr = p.dB + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
-        float v[64];
+        float v[64], u[64];
         tmem_row64(TM_S + lb + half * 64, v);
+        tmem_row64(TM_CP + lb + half * 64, u);
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          reinterpret_cast<float4*>(dcr + half * 64)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          reinterpret_cast<float4*>(dcr + half * 64)[k] =
+              make_float4(v[4 * k] + e * u[4 * k], v[4 * k + 1] + e * u[4 * k + 1], v[4 * k + 2] + e * u[4 * k + 2],
+                          v[4 * k + 3] + e * u[4 * k + 3]);
         tmem_row64(TM_DM + lb + half * 64, v);
+        tmem_row64(TM_BP + lb + half * 64, u);
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          reinterpret_cast<float4*>(dbr + half * 64)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          reinterpret_cast<float4*>(dbr + half * 64)[k] =
+              make_float4(v[4 * k] + w * u[4 * k], v[4 * k + 1] + w * u[4 * k + 1], v[4 * k + 2] + w * u[4 * k + 2],
+                          v[4 * k + 3] + w * u[4 * k + 3]);
       }
     }
   }
@@ -887,7 +863,7 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
