@@ -216,6 +216,19 @@ def run_once(what: str):
         out = torch.zeros(2048, 2048, device="cuda")
         for _ in range(3):
             mm(a, b, a_t=True, b_t=True, out=out, beta=1.0)
+    elif what in ("ssd_m2", "ssd_m3"):
+        # one tensor-core SSD forward + backward: the hybrid's Mamba2 shape at batch 4,
+        # or the Mamba3 shape at batch 1 (P = 256 after the MIMO up-projection)
+        from ..ops.ssd_tc import ssd_tc
+        B, S, H, P = (4, 1024, 24, 64) if what == "ssd_m2" else (1, 4096, 32, 256)
+        G = 1 if what == "ssd_m2" else H
+        x = torch.randn(B, S, H, P, device="cuda").bfloat16().requires_grad_()
+        dt = (torch.rand(B, S, H, device="cuda") * 0.1 + 0.001).requires_grad_()
+        A = -torch.rand(H, device="cuda") - 0.5
+        Bm = torch.randn(B, S, G, 128, device="cuda").bfloat16().requires_grad_()
+        Cm = torch.randn(B, S, G, 128, device="cuda").bfloat16().requires_grad_()
+        for _ in range(3):
+            ssd_tc(x, dt, A, Bm, Cm).backward(torch.ones(B, S, H, P, device="cuda"))
     torch.cuda.synchronize()
     print(f"{what}: ok")
 
@@ -223,7 +236,8 @@ def run_once(what: str):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attn", "ssm", "once"])
-    ap.add_argument("--kernel", default="fa_fwd", help="for 'once': fa_fwd | fa_bwd | gemm | gemm_dw")
+    ap.add_argument("--kernel", default="fa_fwd",
+                    help="for 'once': fa_fwd | fa_bwd | gemm | gemm_dw | ssd_m2 | ssd_m3")
     ap.add_argument("--shapes", nargs="*", default=None, help="M,N,K[,layout] with layout nn|nt|tt")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)
