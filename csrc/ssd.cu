@@ -668,7 +668,9 @@ struct Bwd2Smem {
   static constexpr int TOTAL = OFF_BAR + 128 + 1024;
 };
 
-__global__ void __launch_bounds__(SSD_THREADS, 1)
+constexpr int BWD2_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 math (two per TMEM lane quarter)
+
+__global__ void __launch_bounds__(BWD2_THREADS, 1)
     ssd_bwd2_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmDY,
                     const __grid_constant__ CUtensorMap tmHS, const __grid_constant__ CUtensorMap tmDHS, SsdParams p) {
@@ -701,7 +703,7 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
     mbar_init(&t_free[0], 1);
     mbar_init(&t_free[1], 1);
     mbar_init(sdm_full, 1);
-    mbar_init(ds_ready, 4);
+    mbar_init(ds_ready, 8);
     mbar_init(out_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -782,27 +784,33 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
     }
     __syncwarp();
   } else {
+    // row m (TMEM lane) of the chunk; the two warps of a lane quarter split the columns
     const int m = (warp & 3) * 32 + lane;
+    const int colhalf = (warp - 2) >> 2;
     const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
     const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
-    const float lam = chunk_cumsum(p.loga[si], m, s_part);
-    const float gm = p.gamma[si];
-    s_lam[m] = lam;
-    s_gam[m] = gm;
-    s_col[m] = 0.f;
-    math_bar();
+    if (colhalf == 0) {
+      const float lam0 = chunk_cumsum(p.loga[si], m, s_part);  // named barrier over these 128 threads
+      s_lam[m] = lam0;
+      s_gam[m] = p.gamma[si];
+      s_col[m] = 0.f;
+    }
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    const float lam = s_lam[m];
+    const float gm = s_gam[m];
     const float lam_end = s_lam[SL - 1];
     bool ok = mbar_wait(sdm_full, 0, abort_flag, p.status);
     if (ok) {
       tc_fence_after();
       // dS = dM o decay o g (row t = m);  column sums of dM o S o decay -> dg
 #pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 2 * colhalf; q < 2 * colhalf + 2; ++q) {
         uint32_t sr[32], dr[32];
         tmem_ld32(TM_S + lb + q * 32, sr);
         tmem_ld32(TM_DM + lb + q * 32, dr);
         tc_wait_ld();
         uint32_t pk[16];
+        float cs[32];  // this row's dM o S o D over the 32 columns of chunk q
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
           float v[2];
@@ -812,13 +820,26 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
             const float d = (s2 <= m) ? __expf(lam - s_lam[s2]) : 0.f;
             const float dm = __uint_as_float(dr[t + e2]) * d;
             v[e2] = dm * s_gam[s2];
-            float cs = dm * __uint_as_float(sr[t + e2]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-            if (lane == 0) atomicAdd(&s_col[s2], cs);
+            cs[t + e2] = dm * __uint_as_float(sr[t + e2]);
           }
           pk[t / 2] = pack_bf16(v[0], v[1]);
         }
+        // column sums over the warp's 32 rows by recursive halving: after the
+        // exchanges at distances 16, 8, 4, 2, 1 lane L holds column q*32 + L
+        // (31 shuffles instead of 5 per column)
+#pragma unroll
+        for (int o = 16, w = 32; o > 0; o >>= 1, w >>= 1) {
+          const bool up = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (i < w / 2) {
+              const float send = up ? cs[i] : cs[i + w / 2];
+              const float keep = up ? cs[i + w / 2] : cs[i];
+              cs[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+          }
+        }
+        atomicAdd(&s_col[q * 32 + lane], cs[0]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int ch = q * 4 + j;
@@ -829,8 +850,8 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
-      math_bar();
-      atomicAdd(p.dgamma + si, s_col[m]);
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      if (colhalf == 0) atomicAdd(p.dgamma + si, s_col[m]);
     }
     if (ok && mbar_wait(out_full, 0, abort_flag, p.status)) {
       tc_fence_after();
@@ -839,8 +860,8 @@ __global__ void __launch_bounds__(SSD_THREADS, 1)
       const float w = __expf(lam_end - lam) * gm;
       float* dcr = p.dC + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
       float* dbr = p.dB + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
+      {
+        const int half = colhalf;
         float v[64], u[64];
         tmem_row64(TM_S + lb + half * 64, v);
         tmem_row64(TM_CP + lb + half * 64, u);
@@ -950,7 +971,7 @@ void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st) {
   ssd_dx_kernel<<<grid, SSD_THREADS, DxSmem::TOTAL, st>>>(tb, tc, tdy, tdhs, reinterpret_cast<const __nv_bfloat16*>(io.x),
                                                           io.ldx, p);
   OXI_CUDA_CHECK(cudaGetLastError());
-  ssd_bwd2_kernel<<<grid, SSD_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs, p);
+  ssd_bwd2_kernel<<<grid, BWD2_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
