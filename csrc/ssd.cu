@@ -108,6 +108,35 @@ __device__ __forceinline__ void store_row64(uint8_t* tile, int m, const float* v
                   make_uint4(pack_bf16(v[c * 8], v[c * 8 + 1]), pack_bf16(v[c * 8 + 2], v[c * 8 + 3]),
                              pack_bf16(v[c * 8 + 4], v[c * 8 + 5]), pack_bf16(v[c * 8 + 6], v[c * 8 + 7])));
 }
+// row m, columns [32 h, 32 h + 32) of a [128][64] bf16 SW128 tile -> 32 floats
+__device__ __forceinline__ void load_row32(const uint8_t* tile, int m, int h, float* out) {
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    const int c = h * 4 + cc;
+    const uint4 u = *reinterpret_cast<const uint4*>(tile + m * 128 + (((c ^ (m & 7)) & 7) << 4));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16(w[i]);
+      out[cc * 8 + 2 * i] = f.x;
+      out[cc * 8 + 2 * i + 1] = f.y;
+    }
+  }
+}
+// 32 TMEM columns -> 32 floats
+__device__ __forceinline__ void tmem_row32(uint32_t addr, float* out) {
+  uint32_t r0[32];
+  tmem_ld32(addr, r0);
+  tc_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(r0[i]);
+}
+// SSD kernels with eight math warps: warps w and w + 4 share TMEM lane quarter
+// (w & 3) and split the columns.  The 128 threads of the first four run the
+// chunk cumsum (named barrier 1), then all 256 meet at named barrier 2.
+constexpr int SSD_THREADS8 = 320;
+__device__ __forceinline__ void math8_bar() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+
 // TMEM row (lane base + 64 columns from col0) -> 64 floats
 __device__ __forceinline__ void tmem_row64(uint32_t addr, float* out) {
   uint32_t r0[32], r1[32];
@@ -288,7 +317,7 @@ struct OutSmem {
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
 };
 
-__global__ void __launch_bounds__(SSD_THREADS)
+__global__ void __launch_bounds__(SSD_THREADS8, 2)
     ssd_out_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH, SsdParams p) {
   using L = OutSmem;
@@ -314,10 +343,10 @@ __global__ void __launch_bounds__(SSD_THREADS)
   if (threadIdx.x == 0) {
     mbar_init(ld_cb, 1);
     mbar_init(s_full, 1);
-    mbar_init(m_ready, 4);
+    mbar_init(m_ready, 8);
     mbar_init(ld_xh, 1);
     mbar_init(y_full, 1);
-    mbar_init(y_free, 4);
+    mbar_init(y_free, 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -377,19 +406,22 @@ __global__ void __launch_bounds__(SSD_THREADS)
     __syncwarp();
   } else {
     const int m = (warp & 3) * 32 + lane;  // chunk step t
+    const int colhalf = (warp - 2) >> 2;
     const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
     const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
-    const float lam = chunk_cumsum(p.loga[si], m, s_part);
-    s_lam[m] = lam;
-    s_gam[m] = p.gamma[si];
-    math_bar();
+    if (colhalf == 0) {
+      s_lam[m] = chunk_cumsum(p.loga[si], m, s_part);
+      s_gam[m] = p.gamma[si];
+    }
+    math8_bar();
+    const float lam = s_lam[m];
     const float dsk = p.out ? p.dskip[p.dskip_per_row ? si : h] : 0.f;
     bool ok = mbar_wait(s_full, 0, abort_flag, p.status);
     if (ok) {
       tc_fence_after();
       // M = (C B^T) o decay o g -> over B's tile (B was only needed for S)
 #pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 2 * colhalf; q < 2 * colhalf + 2; ++q) {
         uint32_t sr[32];
         tmem_ld32(TM_S + lb + q * 32, sr);
         tc_wait_ld();
@@ -404,8 +436,6 @@ __global__ void __launch_bounds__(SSD_THREADS)
           }
           pk[t / 2] = pack_bf16(v[0], v[1]);
         }
-        // every thread of this warp has read its S row chunk before any M row lands in sB
-        __syncwarp();
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int ch = q * 4 + j;
@@ -415,8 +445,8 @@ __global__ void __launch_bounds__(SSD_THREADS)
       }
       // C row t scaled by exp(Lam_t): the inter-chunk term joins the same accumulator
       const float el = __expf(lam);
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
+      {
+        const int half = colhalf;
         float cv[64];
         load_row64(sC + half * 16384, m, cv);
 #pragma unroll
@@ -431,21 +461,21 @@ __global__ void __launch_bounds__(SSD_THREADS)
     for (int pb = 0; pb < npb && ok; ++pb) {
       if (!mbar_wait(y_full, pb & 1, abort_flag, p.status)) break;
       tc_fence_after();
-      float yv[64];
-      tmem_row64(TM_Y + lb, yv);
-      const int64_t orow = (int64_t)(r + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
+      float yv[32];
+      tmem_row32(TM_Y + lb + colhalf * 32, yv);
+      const int64_t orow = (int64_t)(r + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP + colhalf * 32;
       float* yr = p.y + orow;
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
+      for (int i = 0; i < 8; ++i)
         reinterpret_cast<float4*>(yr)[i] = make_float4(yv[4 * i], yv[4 * i + 1], yv[4 * i + 2], yv[4 * i + 3]);
       if (p.out) {
-        float xv[64];
-        load_row64(sX, m, xv);
+        float xv[32];
+        load_row32(sX, m, colhalf, xv);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) yv[i] += dsk * xv[i];
+        for (int i = 0; i < 32; ++i) yv[i] += dsk * xv[i];
         uint4* orp = reinterpret_cast<uint4*>(p.out + orow);
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+        for (int q = 0; q < 4; ++q)
           orp[q] = make_uint4(pack_bf16(yv[q * 8], yv[q * 8 + 1]), pack_bf16(yv[q * 8 + 2], yv[q * 8 + 3]),
                               pack_bf16(yv[q * 8 + 4], yv[q * 8 + 5]), pack_bf16(yv[q * 8 + 6], yv[q * 8 + 7]));
       }
@@ -476,7 +506,7 @@ struct DxSmem {
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
 };
 
-__global__ void __launch_bounds__(SSD_THREADS)
+__global__ void __launch_bounds__(SSD_THREADS8, 2)
     ssd_dx_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
                   const __grid_constant__ CUtensorMap tmDY, const __grid_constant__ CUtensorMap tmDH,
                   const __nv_bfloat16* __restrict__ x, int64_t ldx, SsdParams p) {
@@ -503,10 +533,10 @@ __global__ void __launch_bounds__(SSD_THREADS)
   if (threadIdx.x == 0) {
     mbar_init(ld_cb, 1);
     mbar_init(s_full, 1);
-    mbar_init(m_ready, 4);
+    mbar_init(m_ready, 8);
     mbar_init(ld_t, 1);
     mbar_init(d_full, 1);
-    mbar_init(d_free, 4);
+    mbar_init(d_free, 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -566,19 +596,22 @@ __global__ void __launch_bounds__(SSD_THREADS)
     __syncwarp();
   } else {
     const int m = (warp & 3) * 32 + lane;  // chunk step (t for M rows, s for dx rows)
+    const int colhalf = (warp - 2) >> 2;
     const uint32_t lb = (uint32_t)((warp & 3) * 32) << 16;
     const int64_t si = ((int64_t)b * p.S + c * SL + m) * p.H + h;
-    const float lam = chunk_cumsum(p.loga[si], m, s_part);
-    const float gm = p.gamma[si];
-    s_lam[m] = lam;
-    s_gam[m] = gm;
-    math_bar();
+    if (colhalf == 0) {
+      s_lam[m] = chunk_cumsum(p.loga[si], m, s_part);
+      s_gam[m] = p.gamma[si];
+    }
+    math8_bar();
+    const float lam = s_lam[m];
+    const float gm = s_gam[m];
     const float lam_end = s_lam[SL - 1];
     bool ok = mbar_wait(s_full, 0, abort_flag, p.status);
     if (ok) {
       tc_fence_after();
 #pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 2 * colhalf; q < 2 * colhalf + 2; ++q) {
         uint32_t sr[32];
         tmem_ld32(TM_S + lb + q * 32, sr);
         tc_wait_ld();
@@ -612,14 +645,15 @@ __global__ void __launch_bounds__(SSD_THREADS)
     for (int pb = 0; pb < npb && ok; ++pb) {
       if (!mbar_wait(d_full, pb & 1, abort_flag, p.status)) { ok = false; break; }
       tc_fence_after();
-      float dxv[64];
-      tmem_row64(TM_DX + lb, dxv);
+      float dxv[32];
+      tmem_row32(TM_DX + lb + colhalf * 32, dxv);
       if (!last) {
-        float bd[64];
-        tmem_row64(TM_BDH + lb, bd);
-        const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)(r + m) * ldx + h * p.P + pb * SP);
+        float bd[32];
+        tmem_row32(TM_BDH + lb + colhalf * 32, bd);
+        const uint4* xr =
+            reinterpret_cast<const uint4*>(x + (int64_t)(r + m) * ldx + h * p.P + pb * SP + colhalf * 32);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           const uint4 u = __ldg(xr + q);
           const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -629,14 +663,14 @@ __global__ void __launch_bounds__(SSD_THREADS)
           }
         }
 #pragma unroll
-        for (int k = 0; k < 64; ++k) dxv[k] += w * bd[k];
+        for (int k = 0; k < 32; ++k) dxv[k] += w * bd[k];
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(d_free);
-      float* dr = p.dx + (int64_t)(r + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP;
+      float* dr = p.dx + (int64_t)(r + m) * ((int64_t)p.H * p.P) + h * p.P + pb * SP + colhalf * 32;
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
+      for (int k = 0; k < 8; ++k)
         reinterpret_cast<float4*>(dr)[k] = make_float4(dxv[4 * k], dxv[4 * k + 1], dxv[4 * k + 2], dxv[4 * k + 3]);
     }
     if (ok && !last) atomicAdd(p.dgamma + si, dec * dot);
@@ -668,7 +702,7 @@ struct Bwd2Smem {
   static constexpr int TOTAL = OFF_BAR + 128 + 1024;
 };
 
-constexpr int BWD2_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 math (two per TMEM lane quarter)
+constexpr int BWD2_THREADS = SSD_THREADS8;
 
 __global__ void __launch_bounds__(BWD2_THREADS, 1)
     ssd_bwd2_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
@@ -929,7 +963,7 @@ void launch_ssd_fwd(const SsdTcIO& io, cudaStream_t st) {
   ssd_state_scan_kernel<false><<<dim3((unsigned)((per + 255) / 256), io.B * io.H), 256, 0, st>>>(
       p.hloc, p.lamend, p.hs, nc, io.P);
   OXI_CUDA_CHECK(cudaGetLastError());
-  ssd_out_kernel<<<grid, SSD_THREADS, OutSmem::TOTAL, st>>>(tx, tb, tc, ths, p);
+  ssd_out_kernel<<<grid, SSD_THREADS8, OutSmem::TOTAL, st>>>(tx, tb, tc, ths, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -968,7 +1002,7 @@ void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st) {
   ssd_state_scan_kernel<true><<<dim3((unsigned)((per + 255) / 256), io.B * io.H), 256, 0, st>>>(
       p.hloc, p.lamend, p.dhs, nc, io.P);
   OXI_CUDA_CHECK(cudaGetLastError());
-  ssd_dx_kernel<<<grid, SSD_THREADS, DxSmem::TOTAL, st>>>(tb, tc, tdy, tdhs, reinterpret_cast<const __nv_bfloat16*>(io.x),
+  ssd_dx_kernel<<<grid, SSD_THREADS8, DxSmem::TOTAL, st>>>(tb, tc, tdy, tdhs, reinterpret_cast<const __nv_bfloat16*>(io.x),
                                                           io.ldx, p);
   OXI_CUDA_CHECK(cudaGetLastError());
   ssd_bwd2_kernel<<<grid, BWD2_THREADS, Bwd2Smem::TOTAL, st>>>(tx, tb, tc, tdy, ths, tdhs, p);
