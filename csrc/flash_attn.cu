@@ -3,13 +3,16 @@
 // One CTA per (128-query tile, query head, batch).  Q (128 x D) stays in
 // shared memory; K/V tiles of 128 keys stream through a 2-stage TMA ring.
 //   S_j = Q K_j^T        tcgen05.mma, f32 accumulator in TMEM (2 buffers)
-//   P_j = exp2(S_j*c - m) softmax warps: one thread per query row, P written
-//                        to shared memory in the 128B-swizzled K-major layout
-//   O  += P_j V_j        tcgen05.mma, f32 accumulator in TMEM (V as MN-major B)
+//   P_j = exp2(S_j*c - m) softmax warps: one thread per query row; P (bf16) is
+//                        written back into the TMEM columns of S_j
+//   O  += P_j V_j        tcgen05.mma with A = P from TMEM, f32 accumulator in
+//                        TMEM (V as MN-major B from shared memory)
 // The running max is only moved (and O rescaled) when the row max grows by
 // more than 2^8, so the TMEM read-modify-write of O is rare after the first
-// tiles.  The MMA warp issues S_{j+1} before waiting for P_j, so QK^T of the
-// next tile overlaps the softmax of the current one.
+// tiles.  S is double-buffered and P lives in its S buffer, so the softmax of
+// tile j+1 never waits for PV_j (only an O rescale does); the MMA warp issues
+// S_{j+1} before waiting for P_j.  MMAs issued by one thread run in order, so
+// S_{j+2} overwrites P_j only after PV_j has read it.
 //
 // Layout: q/k are row-major [B*S, H*DQ] views and v [B*S, Hk*DV] (row strides
 // ld*), head h at columns [h*DQ, (h+1)*DQ) resp. [h*DV, ...); GQA maps query
@@ -49,14 +52,12 @@ struct FaSmem {
   static constexpr int Q_BYTES = FA_BM * KBQ * 128;
   static constexpr int K_BYTES = FA_BN * KBQ * 128;
   static constexpr int V_BYTES = FA_BN * KBV * 128;
-  static constexpr int P_BYTES = FA_BM * FA_BN * 2;
-  static constexpr int KST = 3;                // K stages: K_j is freed as soon as S_j is done
-  static constexpr int VST = DV <= 64 ? 3 : 2; // V stages: V_j is freed after PV_j
+  static constexpr int KST = 3;  // K stages: K_j is freed as soon as S_j is done
+  static constexpr int VST = 3;  // V stages: V_j is freed after PV_j
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + KST * K_BYTES;
-  static constexpr int OFF_P = OFF_V + VST * V_BYTES;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int OFF_BAR = OFF_V + VST * V_BYTES;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
   static_assert(TOTAL <= 232448, "shared memory budget");
 };
@@ -77,7 +78,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   uint8_t* sQ = smem + L::OFF_Q;
   uint8_t* sK = smem + L::OFF_K;
   uint8_t* sV = smem + L::OFF_V;
-  uint8_t* sP = smem + L::OFF_P;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [3]
@@ -85,7 +85,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   uint64_t* v_full = bars + 7;    // [3]
   uint64_t* v_empty = bars + 10;  // [3]
   uint64_t* s_full = bars + 13;   // [2]
-  uint64_t* s_empty = bars + 15;  // [2]
   uint64_t* p_full = bars + 17;
   uint64_t* pv_done = bars + 18;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
@@ -110,10 +109,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);  // one arrival per softmax warp
-    }
+    for (int i = 0; i < 2; ++i) mbar_init(&s_full[i], 1);
     mbar_init(p_full, 4);
     mbar_init(pv_done, 1);
     *abort_flag = 0;
@@ -174,11 +170,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       constexpr uint32_t IDESC_O = umma_idesc_bf16(FA_BM, DV, false, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status);
       const uint32_t aQ = smem_u32(sQ);
+      // S_j's buffer last held P_{j-2}, read by PV_{j-2}, issued earlier by this thread
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1, u = j >> 1;
+        const int st = j & 1;
         const int ks = j % L::KST, ku = j / L::KST;
         if (!mbar_wait(&k_full[ks], ku & 1, abort_flag, p.status)) return false;
-        if (!mbar_wait(&s_empty[st], (u & 1) ^ 1, abort_flag, p.status)) return false;
         tc_fence_after();
         const uint32_t aK = smem_u32(sK + ks * L::K_BYTES);
 #pragma unroll
@@ -196,12 +192,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         const int vs = j % L::VST, vu = j / L::VST;
         if (!mbar_wait(&v_full[vs], vu & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t aP = smem_u32(sP);
+        const uint32_t tP = TM_S0 + (j & 1) * FA_BN;  // P_j: bf16 pairs in S_j's first 64 columns
         const uint32_t aV = smem_u32(sV + vs * L::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < FA_BN / 16; ++kk)
-          tc_mma_f16(TM_O, kmajor_desc(aP, kk, FA_BM * 128), umma_desc_sw128(aV + kk * 2048, FA_BN * 128, 1024),
-                     IDESC_O, (j | kk) != 0);
+          tc_mma_f16_ts(TM_O, tP + kk * 8, umma_desc_sw128(aV + kk * 2048, FA_BN * 128, 1024), IDESC_O,
+                        (j | kk) != 0);
         tc_commit(pv_done);
         tc_commit(&v_empty[vs]);
       }
@@ -233,9 +229,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       tmem_ld32(s_base + 64, rr[2]);
       tmem_ld32(s_base + 96, rr[3]);
       tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[st]);  // S buffer may be overwritten now
       // 8 independent max accumulators keep the dependency chains short
       float mx[8];
 #pragma unroll
@@ -260,11 +253,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const float mref = (m_new == -INFINITY) ? 0.f : m_new;
       const bool rescale_warp = __any_sync(0xffffffffu, move && j > 0);
       m = m_new;
-      if (j > 0) {
-        // P buffer and O are owned by the previous PV MMA until it completes
+      if (j > 0 && rescale_warp) {
+        // O is owned by the previous PV MMA until it completes (PV_j cannot have
+        // completed yet, so the parity wait cannot skip a phase)
         if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
-        if (rescale_warp) {
+        {
 #pragma unroll 1
           for (int c = 0; c < DV / 32; c += 2) {
             uint32_t o0[32], o1[32];
@@ -295,16 +289,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           rsa[(t >> 1) & 7] += a + bb;
           pk[t / 2] = pack_bf16(a, bb);
         }
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = c * 4 + q;  // 8-key chunk index 0..15
-          sw128_store16(sP + (ch >> 3) * (FA_BM * 128), r, ch & 7,
-                        make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2], pk[q * 4 + 3]));
-        }
+        tmem_st16(s_base + c * 16, pk);  // keys 32c..32c+31 -> columns 16c..16c+15
       }
       const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
       l = l * alpha + rs;
-      fence_proxy_async_smem();
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
