@@ -20,7 +20,8 @@
 // concatenates a RoPE part to q and k): a DQ that is not a multiple of 64 is
 // staged in whole 64-column blocks and the QK^T MMA stops at DQ.
 // Outputs: o [B*S, Hq*DV] bf16, lse [B, Hq, S] f32 (natural log).
-// Warps: 0 TMA, 1 MMA + TMEM owner, 2..5 softmax/correction/epilogue.
+// Warps: 0 TMA, 1 MMA + TMEM owner, 2..9 softmax/correction/epilogue (two per
+// 32-row TMEM lane quarter, splitting the keys of each tile).
 // Every TMA load here reads local memory for one CTA; every wait is bounded.
 #include <algorithm>
 #include <cudaTypedefs.h>
@@ -32,7 +33,7 @@ namespace oxi {
 namespace {
 
 constexpr int FA_BM = 128, FA_BN = 128;
-constexpr int FA_THREADS = 192;
+constexpr int FA_THREADS = 320;      // TMA warp, MMA warp, 8 softmax/epilogue warps
 constexpr int FA_BWD_THREADS = 320;  // TMA warp, MMA warp, 8 softmax/epilogue warps
 
 struct FaParams {
@@ -52,12 +53,13 @@ struct FaSmem {
   static constexpr int Q_BYTES = FA_BM * KBQ * 128;
   static constexpr int K_BYTES = FA_BN * KBQ * 128;
   static constexpr int V_BYTES = FA_BN * KBV * 128;
-  static constexpr int KST = 3;  // K stages: K_j is freed as soon as S_j is done
-  static constexpr int VST = 3;  // V stages: V_j is freed after PV_j
+  static constexpr int KST = 3;                 // K stages: K_j is freed as soon as S_j is done
+  static constexpr int VST = DV <= 64 ? 3 : 2;  // V stages: V_j is freed after PV_j
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + KST * K_BYTES;
-  static constexpr int OFF_BAR = OFF_V + VST * V_BYTES;
+  static constexpr int OFF_RED = OFF_V + VST * V_BYTES;  // row-max exchange [2][2][128] + row sums [2][128]
+  static constexpr int OFF_BAR = OFF_RED + 768 * 4;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
   static_assert(TOTAL <= 232448, "shared memory budget");
 };
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) mbar_init(&s_full[i], 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(pv_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -205,36 +207,42 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     __syncwarp();
   } else {
     // ---------------------------------------------------- softmax warps
+    // Eight warps: warps w and w + 4 own TMEM lane quarter (w & 3), i.e. the same
+    // 32 query rows, and split the keys of a tile (and O's columns) in halves.
+    // The two halves agree on the row max through shared memory once per tile.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;       // query row within the tile (== TMEM lane)
     const int qpos = q0 + r;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float* s_xmax = reinterpret_cast<float*>(smem + L::OFF_RED);  // [tile parity][half][128]
+    float* s_lsum = s_xmax + 512;                                 // [half][128]
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nk && ok; ++j) {
+    // After a failed wait the loop keeps running without work so that every
+    // softmax warp still meets the other half at each named barrier.
+    for (int j = 0; j < nk; ++j) {
       const int st = j & 1, u = j >> 1;
-      if (!mbar_wait(&s_full[st], u & 1, abort_flag, p.status)) { ok = false; break; }
+      if (ok && !mbar_wait(&s_full[st], u & 1, abort_flag, p.status)) ok = false;
+      if (!ok) {
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        continue;
+      }
       tc_fence_after();
-      // Two compact passes over 32-column TMEM chunks: (1) row max, (2) exp2,
-      // row sum, bf16 P to shared memory.  Masking is branch-free: keys past
-      // `lim` (causal diagonal or sequence end) become -inf.
-      const int k0 = j * FA_BN;
-      const bool need_mask = (p.causal && k0 + FA_BN - 1 > q0) || (k0 + FA_BN > p.S);
+      // Masking is branch-free: keys past `lim` (causal diagonal or sequence end) become -inf.
+      const int k0 = j * FA_BN + half * 64;
+      const bool need_mask = (p.causal && k0 + 63 > q0) || (k0 + 64 > p.S);
       const int lim = p.causal ? min(qpos, p.S - 1) : p.S - 1;
       const uint32_t s_base = TM_S0 + st * FA_BN + lane_base;
-      // the whole S row (128 columns) in one batch of TMEM loads, one wait
-      uint32_t rr[4][32];
-      tmem_ld32(s_base + 0, rr[0]);
-      tmem_ld32(s_base + 32, rr[1]);
-      tmem_ld32(s_base + 64, rr[2]);
-      tmem_ld32(s_base + 96, rr[3]);
+      uint32_t rr[2][32];
+      tmem_ld32(s_base + half * 64, rr[0]);
+      tmem_ld32(s_base + half * 64 + 32, rr[1]);
       tc_wait_ld();
-      // 8 independent max accumulators keep the dependency chains short
       float mx[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) mx[q] = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         const int kc = k0 + c * 32;
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
@@ -244,8 +252,16 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           mx[t & 7] = fmaxf(mx[t & 7], v);
         }
       }
-      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float mloc = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      float* xm = s_xmax + (j & 1) * 256;
+      xm[half * 128 + r] = mloc;
+      // every S column of this tile has been read into registers before either
+      // half writes P over the S buffer
+      tc_fence_before();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      tc_fence_after();
+      const float mt = fmaxf(mloc, xm[(half ^ 1) * 128 + r]);
       // move the reference max only when it grows by more than 2^8
       const bool move = (mt > m + 8.f);
       const float m_new = move ? mt : m;
@@ -256,31 +272,27 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       if (j > 0 && rescale_warp) {
         // O is owned by the previous PV MMA until it completes (PV_j cannot have
         // completed yet, so the parity wait cannot skip a phase)
-        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        tc_fence_after();
-        {
-#pragma unroll 1
-          for (int c = 0; c < DV / 32; c += 2) {
-            uint32_t o0[32], o1[32];
-            tmem_ld32(TM_O + lane_base + c * 32, o0);
-            tmem_ld32(TM_O + lane_base + c * 32 + 32, o1);
-            tc_wait_ld();
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              o0[t] = __float_as_uint(__uint_as_float(o0[t]) * alpha);
-              o1[t] = __float_as_uint(__uint_as_float(o1[t]) * alpha);
-            }
-            tmem_st32(TM_O + lane_base + c * 32, o0);
-            tmem_st32(TM_O + lane_base + c * 32 + 32, o1);
-          }
-          tc_wait_st();
+        if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, p.status)) {
+          ok = false;
+          continue;
         }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = half * (DV / 64); c < (half + 1) * (DV / 64); ++c) {
+          uint32_t o0[32];
+          tmem_ld32(TM_O + lane_base + c * 32, o0);
+          tc_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) o0[t] = __float_as_uint(__uint_as_float(o0[t]) * alpha);
+          tmem_st32(TM_O + lane_base + c * 32, o0);
+        }
+        tc_wait_st();
       }
       float rsa[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) rsa[q] = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
@@ -289,7 +301,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           rsa[(t >> 1) & 7] += a + bb;
           pk[t / 2] = pack_bf16(a, bb);
         }
-        tmem_st16(s_base + c * 16, pk);  // keys 32c..32c+31 -> columns 16c..16c+15
+        // keys 64 half + 32c .. +31 -> P columns 32 half + 16c .. +15
+        tmem_st16(s_base + half * 32 + c * 16, pk);
       }
       const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
       l = l * alpha + rs;
@@ -298,13 +311,17 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(pv_done, (nk - 1) & 1, abort_flag, p.status)) {
+    if (ok && !mbar_wait(pv_done, (nk - 1) & 1, abort_flag, p.status)) ok = false;
+    s_lsum[half * 128 + r] = l;
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // reached by every softmax warp
+    if (ok) {
       tc_fence_after();
-      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      const float lt = l + s_lsum[(half ^ 1) * 128 + r];
+      const float inv_l = (lt > 0.f) ? 1.f / lt : 0.f;
       const bool valid = qpos < p.S;
       __nv_bfloat16* orow = p.o + (int64_t)(row0 + qpos) * p.ldo + h * DV;
 #pragma unroll 1
-      for (int c = 0; c < DV / 32; ++c) {
+      for (int c = half * (DV / 64); c < (half + 1) * (DV / 64); ++c) {
         uint32_t o[32];
         tmem_ld32(TM_O + lane_base + c * 32, o);
         tc_wait_ld();
@@ -321,7 +338,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           }
         }
       }
-      if (valid) p.lse[((int64_t)b * p.Hq + h) * p.S + qpos] = (m + __log2f(l)) * 0.69314718055994530942f;
+      if (valid && half == 0) p.lse[((int64_t)b * p.Hq + h) * p.S + qpos] = (m + __log2f(lt)) * 0.69314718055994530942f;
     }
   }
 
@@ -567,7 +584,9 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const int kpos = k0 + r;
     bool ok = true;
-    for (int it = 0; it < n_it && ok; ++it) {
+    // After a failed wait the loop keeps running without work so that every
+    // softmax warp still reaches each named barrier.
+    for (int it = 0; it < n_it; ++it) {
       const int h = hk * group + it / n_i;
       const int i = i_start + it % n_i;
       const int q0 = i * 128;
@@ -582,7 +601,8 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
         }
       }
       named_bar_sync(1, 256);
-      if (!mbar_wait(sdp_full, it & 1, abort_flag, p.status)) { ok = false; break; }
+      if (!ok) continue;
+      if (!mbar_wait(sdp_full, it & 1, abort_flag, p.status)) { ok = false; continue; }
       // dS^T smem is free once the previous pair's MMAs completed (waited in the previous dQ step)
       tc_fence_after();
       const bool diag = p.causal && (q0 < k0 + 128);
@@ -624,7 +644,7 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
       // dQ of this (h, i): thread r owns query row r; the two halves take alternate 32-column chunks
-      if (!mbar_wait(it_done, it & 1, abort_flag, p.status)) { ok = false; break; }
+      if (!mbar_wait(it_done, it & 1, abort_flag, p.status)) { ok = false; continue; }
       tc_fence_after();
       const int qp = q0 + r;
       float* dqrow = p.dq_acc + (int64_t)(row0 + qp) * p.ld_dq + h * DQ;
