@@ -156,6 +156,8 @@ def main():
     ap.add_argument("--impl", default="oxidizr_b200", choices=["oxidizr_b200", "reference"])
     ap.add_argument("--sync-backend", default=os.environ.get("OXI_SYNC_BACKEND", "auto"))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cuda-graph", action="store_true",
+                    help="capture the training step in a CUDA graph (one GPU only; replayed every step)")
     ap.add_argument("--model", default="llama", choices=sorted(MODELS),
                     help="llama = the headline config; hybrid / mamba3 / moe = the other BASELINE configs")
     args = ap.parse_args()
@@ -222,7 +224,7 @@ def main():
             return blk[:, :-1], blk[:, 1:]
 
     trainer = Trainer(cfg, model, opt, DeviceBatches(), device=dev, headless=True, rank=rank, world_size=world,
-                      out=lambda s: None)
+                      out=lambda s: None, cuda_graph=args.cuda_graph)
 
     def barrier():
         if world > 1:
@@ -272,7 +274,7 @@ def main():
         D.write_tokens(path, D.synthetic_tokens(V, n_tok, seed=7))
         loader = D.TokenDataLoader(path, B, S, device=dev, rank=rank, world_size=world, prefetch=2)
         trainer2 = Trainer(cfg, model, opt, loader, device=dev, headless=True, rank=rank, world_size=world,
-                           out=lambda s: None)
+                           out=lambda s: None, cuda_graph=args.cuda_graph)
         for _ in range(args.warmup):
             float(trainer2.training_step()[0])
         barrier()
@@ -303,6 +305,7 @@ def main():
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded uniform u32 tokens, random-init weights)",
         "config": {"model": MODELS[args.model][0], "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}" + (f"+ep{ep}" if ep > 1 else ""),
                    "micro_batch_per_gpu": B, "grad_accum": 1, "sync_backend": backend,
+                   "cuda_graph": bool(trainer.cuda_graph),
                    "l2": "no flush: per-step working set (weights, optimizer state, activations: GBs) >> 126 MB L2"},
         "clocks": clocks, "e2e": e2e, "gpu_launches": n_launch,
         "model_tflops_per_gpu": round(achieved_tf, 1),

@@ -226,15 +226,22 @@ void sqsum(torch::Tensor g, torch::Tensor out) {
   oxi::launch_sqsum(g.data_ptr<float>(), g.numel(), out.data_ptr<float>(), stream());
 }
 
-void clip_coef(torch::Tensor sq, double max_norm, double pre_scale, torch::Tensor coef, torch::Tensor norm) {
+void clip_coef(torch::Tensor sq, double max_norm, double pre_scale, torch::Tensor coef, torch::Tensor norm,
+               c10::optional<torch::Tensor> step_state, double b1, double b2) {
   c10::cuda::CUDAGuard gd(sq.device());
+  float* ss = nullptr;
+  if (step_state.has_value() && step_state->defined()) {
+    TORCH_CHECK(step_state->scalar_type() == torch::kFloat32 && step_state->is_contiguous() &&
+                    step_state->numel() == 3, "step_state: f32 [3]");
+    ss = step_state->data_ptr<float>();
+  }
   oxi::launch_clip_coef(sq.data_ptr<float>(), (float)max_norm, (float)pre_scale, coef.data_ptr<float>(),
-                        norm.data_ptr<float>(), stream());
+                        norm.data_ptr<float>(), stream(), ss, (float)b1, (float)b2);
 }
 
 void adamw(torch::Tensor p, c10::optional<torch::Tensor> p16, torch::Tensor g, torch::Tensor m, torch::Tensor v,
            double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
-           c10::optional<torch::Tensor> gscale) {
+           c10::optional<torch::Tensor> gscale, c10::optional<torch::Tensor> bc_dev) {
   c10::cuda::CUDAGuard gd(p.device());
   TORCH_CHECK(p.scalar_type() == torch::kFloat32 && g.scalar_type() == torch::kFloat32 && p.is_contiguous() &&
                   g.is_contiguous() && m.is_contiguous() && v.is_contiguous() && p.numel() == g.numel() &&
@@ -246,7 +253,8 @@ void adamw(torch::Tensor p, c10::optional<torch::Tensor> p16, torch::Tensor g, t
   }
   oxi::launch_adamw(p.data_ptr<float>(), p16p, g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
                     p.numel(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
-                    gscale.has_value() && gscale->defined() ? gscale->data_ptr<float>() : nullptr, stream());
+                    gscale.has_value() && gscale->defined() ? gscale->data_ptr<float>() : nullptr, stream(),
+                    bc_dev.has_value() && bc_dev->defined() ? bc_dev->data_ptr<float>() : nullptr);
 }
 
 // ------------------------------------------------------------ attention
@@ -965,8 +973,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd, "embedding scatter-add into f32 grad");
   m.def("rope_bwd", &rope_bwd, "in-place inverse rotate-half RoPE");
   m.def("sqsum", &sqsum, "sum of squares (atomically added into out)");
-  m.def("clip_coef", &clip_coef, "global-norm clip coefficient on device");
-  m.def("adamw", &adamw, "flat multi-tensor AdamW (f32 master, bf16 copy)");
+  m.def("clip_coef", &clip_coef, "global-norm clip coefficient (and device step state) on device", py::arg("sq"),
+        py::arg("max_norm"), py::arg("pre_scale"), py::arg("coef"), py::arg("norm"),
+        py::arg("step_state") = py::none(), py::arg("b1") = 0.9, py::arg("b2") = 0.999);
+  m.def("adamw", &adamw, "flat multi-tensor AdamW (f32 master, bf16 copy)", py::arg("p"), py::arg("p16"),
+        py::arg("g"), py::arg("m"), py::arg("v"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"),
+        py::arg("wd"), py::arg("bc1"), py::arg("bc2"), py::arg("gscale") = py::none(),
+        py::arg("bc_dev") = py::none());
   m.def("flash_fwd", &flash_fwd, "causal flash attention forward (tcgen05)");
   m.def("flash_bwd", &flash_bwd, "causal flash attention backward (tcgen05)");
   m.def("flash_supported", &flash_supported, "whether a flash kernel exists for head dims (qk, v)");

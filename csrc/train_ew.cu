@@ -160,13 +160,22 @@ __global__ void sqsum_kernel(const float* __restrict__ g, int64_t n, float* __re
 }
 
 // coef = min(1, max_norm / (sqrt(sqsum) + 1e-6)) * pre_scale; also writes the norm.
+// step_state (nullable) = [t, 1 - b1^t, 1 - b2^t] kept on the device so that a
+// captured step (CUDA graph) advances the bias correction on every replay.
 __global__ void clip_coef_kernel(const float* __restrict__ sqsum, float max_norm, float pre_scale,
-                                 float* __restrict__ coef, float* __restrict__ norm_out) {
+                                 float* __restrict__ coef, float* __restrict__ norm_out,
+                                 float* __restrict__ step_state, float b1, float b2) {
   const float nrm = sqrtf(*sqsum) * pre_scale;
   *norm_out = nrm;
   float c = pre_scale;
   if (max_norm > 0.f && nrm > max_norm) c *= max_norm / (nrm + 1e-6f);
   *coef = c;
+  if (step_state) {
+    const float t = step_state[0] + 1.f;
+    step_state[0] = t;
+    step_state[1] = 1.f - powf(b1, t);
+    step_state[2] = 1.f - powf(b2, t);
+  }
 }
 
 // ------------------------------------------------------------------- AdamW
@@ -174,9 +183,11 @@ __global__ void clip_coef_kernel(const float* __restrict__ sqsum, float max_norm
 // model copy.  g is scaled by *gscale (clip coefficient and 1/world).
 __global__ void adamw_kernel(float* __restrict__ p, __nv_bfloat16* __restrict__ p16, const float* __restrict__ g,
                              float* __restrict__ m, float* __restrict__ v, int64_t n, float lr, float b1, float b2,
-                             float eps, float wd, float bc1, float bc2, const float* __restrict__ gscale) {
+                             float eps, float wd, float bc1, float bc2, const float* __restrict__ gscale,
+                             const float* __restrict__ bc_dev) {
   const float gs = gscale ? *gscale : 1.f;
-  const float rb1 = 1.f / bc1, rb2 = 1.f / bc2;
+  // bias corrections from the device step state when given (graph-capturable step)
+  const float rb1 = 1.f / (bc_dev ? bc_dev[0] : bc1), rb2 = 1.f / (bc_dev ? bc_dev[1] : bc2);
   const int64_t nv = n / 4;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
     float4 pv = reinterpret_cast<float4*>(p)[i];
@@ -273,13 +284,14 @@ void launch_sqsum(const float* g, int64_t n, float* out, cudaStream_t st) {
 }
 
 void launch_clip_coef(const float* sqsum, float max_norm, float pre_scale, float* coef, float* norm_out,
-                      cudaStream_t st) {
-  clip_coef_kernel<<<1, 1, 0, st>>>(sqsum, max_norm, pre_scale, coef, norm_out);
+                      cudaStream_t st, float* step_state, float b1, float b2) {
+  clip_coef_kernel<<<1, 1, 0, st>>>(sqsum, max_norm, pre_scale, coef, norm_out, step_state, b1, b2);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_adamw(float* p, void* p16, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
-                  float eps, float wd, float bc1, float bc2, const float* gscale, cudaStream_t st) {
+                  float eps, float wd, float bc1, float bc2, const float* gscale, cudaStream_t st,
+                  const float* bc_dev) {
   if (!n) return;
   OXI_CHECK((reinterpret_cast<uintptr_t>(p) & 15) == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0 &&
                 (reinterpret_cast<uintptr_t>(m) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0 &&
@@ -287,7 +299,7 @@ void launch_adamw(float* p, void* p16, const float* g, float* m, float* v, int64
             "AdamW buffers must be 16-byte aligned");
   const unsigned grid = (unsigned)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)sm_count() * 8);
   adamw_kernel<<<grid, 256, 0, st>>>(p, reinterpret_cast<__nv_bfloat16*>(p16), g, m, v, n, lr, b1, b2, eps, wd, bc1,
-                                     bc2, gscale);
+                                     bc2, gscale, bc_dev);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

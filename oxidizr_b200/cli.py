@@ -42,6 +42,8 @@ def _add_train_args(p: argparse.ArgumentParser, legacy: bool = False):
     p.add_argument("--max-checkpoints", dest="max_checkpoints", type=int, default=None)
     p.add_argument("--dtype", default=None if legacy else "f32")
     p.add_argument("--seed", type=int, default=None, help="seed for init and synthetic tokens")
+    p.add_argument("--cuda-graph", dest="cuda_graph", action="store_true",
+                   help="capture the whole training step in a CUDA graph (one GPU; replayed each step)")
 
 
 def build_parser() -> argparse.ArgumentParser:
@@ -287,7 +289,8 @@ def run_train(args, argv: List[str]) -> int:
 
     trainer = Trainer(cfg, model, opt, loader, device=device, headless=headless,
                       steps_json_path=os.path.join(run_dir, "steps.json"), start_step=start_step,
-                      data_file_path=args.data_file, rank=rank, world_size=world, out=out)
+                      data_file_path=args.data_file, rank=rank, world_size=world, out=out,
+                      cuda_graph=bool(getattr(args, "cuda_graph", False)))
     if not headless and rank == 0:
         _banner(cfg, loader, trainer)
     status, err = "completed", None

@@ -160,6 +160,9 @@ class AdamW:
         self._sq = torch.zeros(1, dtype=torch.float32, device=dev)
         self._coef = torch.ones(1, dtype=torch.float32, device=dev)
         self._norm = torch.zeros(1, dtype=torch.float32, device=dev)
+        # [t, 1 - b1^t, 1 - b2^t] advanced on the device, so a captured step (CUDA
+        # graph) gets the right bias correction on every replay
+        self._step_state = torch.zeros(3, dtype=torch.float32, device=dev)
 
     @property
     def lr(self) -> float:
@@ -183,9 +186,10 @@ class AdamW:
             e.sqsum(f.grad, self._sq)
             if self.local is not None:
                 self._local_sq(self._sq)
-            e.clip_coef(self._sq, float(c.max_grad_norm or 0.0), float(grad_scale), self._coef, self._norm)
+            e.clip_coef(self._sq, float(c.max_grad_norm or 0.0), float(grad_scale), self._coef, self._norm,
+                        self._step_state, c.beta1, c.beta2)
             e.adamw(f.master, f.flat if f.flat is not f.master else None, f.grad, self.m, self.v, c.lr, c.beta1,
-                    c.beta2, c.eps, c.weight_decay, bc1, bc2, self._coef)
+                    c.beta2, c.eps, c.weight_decay, bc1, bc2, self._coef, self._step_state[1:])
             if self.local is not None:
                 self.local.update(self._coef, t)
         else:
@@ -233,4 +237,6 @@ class AdamW:
                 self.flat.flat.copy_(self.flat.master)
             self.m.copy_(d["exp_avg"].to(self.m.device))
             self.v.copy_(d["exp_avg_sq"].to(self.v.device))
+            self._step_state.fill_(0.0)
+            self._step_state[0] = float(step)
         self.step_count = int(step)

@@ -69,7 +69,8 @@ class Trainer:
     def __init__(self, cfg: LitConfig, model, optimizer, loader, *, device, headless: bool = True,
                  steps_json_path: Optional[str] = None, start_step: int = 0, data_file_path: Optional[str] = None,
                  rank: int = 0, world_size: int = 1, dataset_size: Optional[int] = None,
-                 out: Callable[[str], None] = print, on_checkpoint: Optional[Callable] = None):
+                 out: Callable[[str], None] = print, on_checkpoint: Optional[Callable] = None,
+                 cuda_graph: bool = False):
         self.cfg = cfg
         self.tc = cfg.trainer
         self.model = model
@@ -92,6 +93,20 @@ class Trainer:
         self.on_checkpoint = on_checkpoint
         self.last_loss = None
         self.last_grad_norm = None
+        # whole-step CUDA graph (forward, backward, optimizer): one replay per step
+        self.cuda_graph = bool(cuda_graph) and self._graph_eligible()
+        self._graph = None
+        self._graph_warm = 0
+        self._graph_in = None
+        self._graph_out = None
+        self._graph_launches = 0
+
+    def _graph_eligible(self) -> bool:
+        """A captured step needs one process (the NVLink sync kernels take per-step
+        epochs as launch arguments), a CUDA device and an optimizer whose bias
+        correction lives on the device."""
+        return (self.device.type == "cuda" and self.world_size == 1
+                and hasattr(self.opt, "_step_state") and getattr(self.opt, "local", None) is None)
 
     @property
     def effective_steps(self) -> int:
@@ -102,16 +117,31 @@ class Trainer:
     # ------------------------------------------------------------ one step
     def training_step(self):
         """Returns (mean CE loss, grad norm) as device scalars."""
-        from .utils.faults import fault_for, nvtx_range, profile_window
+        from .utils.faults import fault_for, profile_window
         fault = fault_for(self.rank, self.global_step)
         profile_window(self.global_step)
         accum = self.tc.gradient_accumulation
+        if self.cuda_graph:
+            batches = [self.loader.next_batch() for _ in range(accum)]
+            total_ce, gnorm = self._graph_step(batches)
+        else:
+            total_ce, gnorm = self._step_body(self.loader.next_batch for _ in range(accum))
+        self.global_step += 1
+        if fault == "nan":
+            total_ce = total_ce * float("nan")
+        return total_ce, gnorm
+
+    def _step_body(self, batches):
+        """Forward + backward over the micro-batches, then the optimizer; no host sync.
+        ``batches`` yields (inputs, targets) pairs or callables returning them."""
+        from .utils.faults import nvtx_range
+        accum = self.tc.gradient_accumulation
         alpha = float(self.tc.load_balance_alpha)
         total_ce = torch.zeros((), dtype=torch.float32, device=self.device)
-        for micro in range(accum):
+        for micro, b in enumerate(batches):
             if hasattr(self.opt, "accumulating"):
                 self.opt.accumulating = micro < accum - 1
-            x, y = self.loader.next_batch()
+            x, y = b() if callable(b) else b
             with nvtx_range("forward"):
                 ce, aux = self.model(x, y)
             loss = ce.float()
@@ -122,10 +152,34 @@ class Trainer:
             total_ce = total_ce + ce.detach().float()
         with nvtx_range("optimizer"):
             gnorm = self.opt.step()
-        self.global_step += 1
-        if fault == "nan":
-            total_ce = total_ce * float("nan")
         return total_ce / accum, gnorm
+
+    def _graph_step(self, batches):
+        """Eager warm-up steps (kernel attributes, allocator), then capture the whole
+        step into a CUDA graph over static input buffers and replay it every step."""
+        from .ops._C import launch_counter
+        if self._graph is None:
+            self._graph_warm += 1
+            if self._graph_warm <= 2:
+                return self._step_body(batches)
+            self._graph_in = [(x.clone(), y.clone()) for x, y in batches]
+            torch.cuda.synchronize(self.device)
+            torch.cuda.empty_cache()  # the graph gets its own pool; drop the eager steps' cache
+            graph = torch.cuda.CUDAGraph()
+            was, n0 = launch_counter.enabled, launch_counter.count
+            launch_counter.enabled = True
+            with torch.cuda.graph(graph):
+                self._graph_out = self._step_body(self._graph_in)
+            self._graph_launches = launch_counter.count - n0
+            launch_counter.enabled, launch_counter.count = was, n0
+            self._graph = graph
+        for (xs, ys), (x, y) in zip(self._graph_in, batches):
+            xs.copy_(x, non_blocking=True)
+            ys.copy_(y, non_blocking=True)
+        self._graph.replay()
+        if launch_counter.enabled:
+            launch_counter.count += self._graph_launches
+        return self._graph_out
 
     def _check_finite(self, loss: float):
         if not math.isfinite(loss):
