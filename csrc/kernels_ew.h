@@ -21,6 +21,8 @@ void launch_embed_bwd(const int64_t* ids, const void* dy, float* dw, int64_t row
 void launch_rope_bwd(void* x, int64_t ld, int64_t rows, int ncols_rot, int hd, const float* cos, const float* sin,
                      int seq, cudaStream_t st);
 void launch_sqsum(const float* g, int64_t n, float* out, cudaStream_t st);
+// out[c] += sum over rows of a bf16 [rows, N] matrix with row stride ld (bias gradients)
+void launch_colsum_bf16(const void* x, int64_t rows, int N, int64_t ld, float* out, cudaStream_t st);
 // step_state (nullable): device [t, 1 - b1^t, 1 - b2^t], advanced by one here.
 void launch_clip_coef(const float* sqsum, float max_norm, float pre_scale, float* coef, float* norm_out,
                       cudaStream_t st, float* step_state = nullptr, float b1 = 0.9f, float b2 = 0.999f);

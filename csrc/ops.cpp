@@ -226,6 +226,15 @@ void sqsum(torch::Tensor g, torch::Tensor out) {
   oxi::launch_sqsum(g.data_ptr<float>(), g.numel(), out.data_ptr<float>(), stream());
 }
 
+void colsum_add(torch::Tensor x, torch::Tensor out) {
+  c10::cuda::CUDAGuard gd(x.device());
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.scalar_type() == torch::kBFloat16 && x.stride(1) == 1,
+              "colsum: bf16 [rows, N] with unit inner stride");
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous() && out.numel() == x.size(1),
+              "colsum: out f32 [N]");
+  oxi::launch_colsum_bf16(x.data_ptr(), x.size(0), (int)x.size(1), x.stride(0), out.data_ptr<float>(), stream());
+}
+
 void clip_coef(torch::Tensor sq, double max_norm, double pre_scale, torch::Tensor coef, torch::Tensor norm,
                c10::optional<torch::Tensor> step_state, double b1, double b2) {
   c10::cuda::CUDAGuard gd(sq.device());
@@ -973,6 +982,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd, "embedding scatter-add into f32 grad");
   m.def("rope_bwd", &rope_bwd, "in-place inverse rotate-half RoPE");
   m.def("sqsum", &sqsum, "sum of squares (atomically added into out)");
+  m.def("colsum_add", &colsum_add, "out += column sums of a bf16 matrix (bias gradients)");
   m.def("clip_coef", &clip_coef, "global-norm clip coefficient (and device step state) on device", py::arg("sq"),
         py::arg("max_norm"), py::arg("pre_scale"), py::arg("coef"), py::arg("norm"),
         py::arg("step_state") = py::none(), py::arg("b1") = 0.9, py::arg("b2") = 0.999);

@@ -178,6 +178,50 @@ __global__ void clip_coef_kernel(const float* __restrict__ sqsum, float max_norm
   }
 }
 
+// ----------------------------------------------------- column sums (bias grads)
+// out[c] += sum_r x[r, c] for a bf16 [rows, N] matrix of row stride ld.  A block is
+// 32 column lanes (8 consecutive columns each, one 16-byte load) x 8 row lanes;
+// blockIdx.y splits the rows; one f32 atomic per column per block.
+__global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int N,
+                                                          int64_t ld, bool vec, float* __restrict__ out) {
+  __shared__ float part[8][257];
+  const int cl = threadIdx.x & 31, rl = threadIdx.x >> 5;
+  const int c0 = (blockIdx.x * 32 + cl) * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < N) {
+    const bool full = vec && c0 + 8 <= N;
+    for (int64_t r = (int64_t)blockIdx.y * 8 + rl; r < rows; r += (int64_t)gridDim.y * 8) {
+      const __nv_bfloat16* row = x + r * ld + c0;
+      if (full) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack_bf16(w[i]);
+          acc[2 * i] += f.x;
+          acc[2 * i + 1] += f.y;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (c0 + j < N) acc[j] += __bfloat162float(row[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[rl][cl * 8 + j] = acc[j];
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    const int c = blockIdx.x * 256 + i;
+    if (c < N) {
+      float sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) sum += part[q][i];
+      atomicAdd(out + c, sum);
+    }
+  }
+}
+
 // ------------------------------------------------------------------- AdamW
 // Decoupled AdamW on flat f32 master weights, f32 moments; writes the bf16
 // model copy.  g is scaled by *gscale (clip coefficient and 1/world).
@@ -280,6 +324,16 @@ void launch_sqsum(const float* g, int64_t n, float* out, cudaStream_t st) {
   if (!n) return;
   const unsigned grid = (unsigned)std::min<int64_t>((n / 4 + 255) / 256 + 1, (int64_t)sm_count() * 4);
   sqsum_kernel<<<grid, 256, 0, st>>>(g, n, out);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_colsum_bf16(const void* x, int64_t rows, int N, int64_t ld, float* out, cudaStream_t st) {
+  if (rows <= 0 || N <= 0) return;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ld % 8 == 0;
+  const int gx = (N + 255) / 256;
+  const int64_t want = std::max<int64_t>(1, (int64_t)sm_count() * 8 / gx);
+  const int gy = (int)std::min<int64_t>(want, std::max<int64_t>(1, rows / 64));
+  colsum_bf16_kernel<<<dim3(gx, gy), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), rows, N, ld, vec, out);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

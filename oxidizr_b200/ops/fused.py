@@ -44,6 +44,20 @@ def _vec_grad(p: torch.nn.Parameter, g32: torch.Tensor):
     return g32.to(p.dtype).view(p.shape)
 
 
+def _bias_grad(p: torch.nn.Parameter, dy2: torch.Tensor):
+    """Column sums of dy2 [T, N] (bf16) accumulated straight into the bias's main_grad."""
+    mg = getattr(p, "main_grad", None)
+    if dy2.is_cuda and dy2.dtype == torch.bfloat16 and dy2.stride(1) == 1:
+        if mg is not None and mg.is_contiguous():
+            ext().colsum_add(dy2, mg.view(-1))
+            _ready(p)
+            return None
+        g32 = torch.zeros(dy2.shape[1], dtype=torch.float32, device=dy2.device)
+        ext().colsum_add(dy2, g32)
+        return _vec_grad(p, g32)
+    return _vec_grad(p, dy2.sum(0, dtype=torch.float32))
+
+
 def _c(t: torch.Tensor) -> torch.Tensor:
     return t if t.is_contiguous() else t.contiguous()
 
@@ -129,7 +143,7 @@ class Linear(torch.autograd.Function):
         dy2 = _c(dy.reshape(-1, w.shape[0]))
         dx = mm(dy2, w, b_t=True).view(*dy.shape[:-1], w.shape[1]) if ctx.needs_input_grad[0] else None
         gw = _wgrad_gemm(w, dy2, x2)
-        gb = _vec_grad(ctx.bias, dy2.sum(0, dtype=torch.float32)) if ctx.has_bias else None
+        gb = _bias_grad(ctx.bias, dy2) if ctx.has_bias else None
         dres = dy if ctx.has_resid else None
         return dx, gw, gb, dres
 

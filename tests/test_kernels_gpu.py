@@ -199,3 +199,14 @@ def test_router_topk_vs_torch(T, E, k, dt):
     assert torch.equal(counts.long().cpu(), torch.bincount(ti.reshape(-1), minlength=E).cpu())
     ((tw * cw).sum() + 3.0 * probs.mean(0).pow(2).mean()).backward()
     assert _rel(logits.grad, lr.grad) < (1e-2 if dt == torch.bfloat16 else 1e-4)
+
+
+@pytest.mark.parametrize("T,N,ld", [(300, 1284, 1284), (4096, 256, 264), (5, 7, 7)])
+def test_colsum_bias_grad_kernel(T, N, ld):
+    from oxidizr_b200.ops._C import ext
+    torch.manual_seed(3)
+    x = torch.randn(T, ld, device="cuda").bfloat16()[:, :N]
+    out = torch.ones(N, device="cuda")
+    ext().colsum_add(x, out)
+    ref = 1 + x.double().sum(0)
+    assert torch.allclose(out.double(), ref, rtol=1e-4, atol=1e-3)
