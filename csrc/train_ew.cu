@@ -194,10 +194,10 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
       const __nv_bfloat16* row = x + r * ld + c0;
       if (full) {
         const uint4 u = __ldg(reinterpret_cast<const uint4*>(row));
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float2 f = unpack_bf16(w[i]);
+          const float2 f = __bfloat1622float2(h2[i]);
           acc[2 * i] += f.x;
           acc[2 * i + 1] += f.y;
         }
