@@ -53,8 +53,9 @@ struct SsdTcIO {
   const void* dy;
   void* dhs;
   float* dx;
-  float* dB;
+  float* dB;            // f32, or bf16 when dbc_bf16
   float* dC;
+  int dbc_bf16;
   float* dgamma;
   float* hloc;          // forward scratch [B*H*nc*N, P] f32
   float* lamend;        // forward scratch [B*H*nc] f32
@@ -72,16 +73,16 @@ namespace oxi {
 // Mamba3 B/C prologue (mamba3.cu): rmsnorm + bias + complex RoPE, written as
 // per-head bf16 B_rot / C_rot [B, S, H, N] plus bcdot f32 [B, S, H] =
 // <B_rot, C_rot>.  braw/craw bf16 rows of stride ldr (group g at column g*N);
-// ang f32 [B, S, H, N/2].  Backward: db/dc f32 [B, S, H, N], dbcdot f32
-// [B, S, H] or null; dbraw/dcraw f32 rows of stride ldd; dw [N], dbb/dcb
+// ang f32 [B, S, H, N/2].  Backward: db/dc [B, S, H, N] (f32, or bf16 when
+// grads_bf16), dbcdot f32 [B, S, H] or null; dbraw/dcraw f32 rows of stride ldd; dw [N], dbb/dcb
 // [H, N] accumulated (zero them); dang f32 [B, S, H, N/2].
 void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
                       const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* bout,
                       void* cout, float* bcdot, cudaStream_t st);
 void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
-                      const void* cbias, const float* ang, const float* db, const float* dc, const float* dbcdot,
-                      int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw,
-                      float* dbb, float* dcb, float* dang, cudaStream_t st);
+                      const void* cbias, const float* ang, const void* db, const void* dc, bool grads_bf16,
+                      const float* dbcdot, int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw,
+                      int64_t ldd, float* dw, float* dbb, float* dcb, float* dang, cudaStream_t st);
 }  // namespace oxi
 
 namespace oxi {

@@ -103,14 +103,21 @@ __global__ void __launch_bounds__(256) m3_bc_fwd_kernel(const __nv_bfloat16* __r
   }
 }
 
-// db/dc: f32 gradients of B_rot / C_rot [B, S, H, N]; dbcdot [B, S, H] (may be null).
+__device__ __forceinline__ void load_grad4(const float* p, float* v) {
+  const float4 d = *reinterpret_cast<const float4*>(p);
+  v[0] = d.x; v[1] = d.y; v[2] = d.z; v[3] = d.w;
+}
+__device__ __forceinline__ void load_grad4(const __nv_bfloat16* p, float* v) { load4(p, v); }
+
+// db/dc: gradients of B_rot / C_rot [B, S, H, N] (f32 or bf16); dbcdot [B, S, H] (may be null).
+template <typename GT>
 __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __restrict__ braw,
                                                         const __nv_bfloat16* __restrict__ craw, int64_t ldr,
                                                         const __nv_bfloat16* __restrict__ w,
                                                         const __nv_bfloat16* __restrict__ bbias,
                                                         const __nv_bfloat16* __restrict__ cbias,
-                                                        const float* __restrict__ ang, const float* __restrict__ db2,
-                                                        const float* __restrict__ dc2,
+                                                        const float* __restrict__ ang, const GT* __restrict__ db2,
+                                                        const GT* __restrict__ dc2,
                                                         const float* __restrict__ dbcdot, int Bsz, int S, int H, int G,
                                                         float eps, float* __restrict__ dbraw, float* __restrict__ dcraw,
                                                         int64_t ldd, float* __restrict__ dw, float* __restrict__ dbb,
@@ -139,10 +146,9 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
       for (int hh = 0; hh < hpg; ++hh) {
         const int h = g * hpg + hh;
         const int64_t it = bt * H + h;
-        const float4 d1 = *reinterpret_cast<const float4*>(db2 + it * M3N + lane * 4);
-        float dB[4] = {d1.x, d1.y, d1.z, d1.w};
-        const float4 d3 = *reinterpret_cast<const float4*>(dc2 + it * M3N + lane * 4);
-        float dC[4] = {d3.x, d3.y, d3.z, d3.w};
+        float dB[4], dC[4];
+        load_grad4(db2 + it * M3N + lane * 4, dB);
+        load_grad4(dc2 + it * M3N + lane * 4, dC);
         float bb[4], cb[4];
         load4(bbias + h * M3N + lane * 4, bb);
         load4(cbias + h * M3N + lane * 4, cb);
@@ -233,19 +239,31 @@ void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const voi
 }
 
 void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
-                      const void* cbias, const float* ang, const float* db2, const float* dc2, const float* dbcdot,
-                      int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw, int64_t ldd, float* dw, float* dbb,
-                      float* dcb, float* dang, cudaStream_t st) {
+                      const void* cbias, const float* ang, const void* db, const void* dc, bool grads_bf16,
+                      const float* dbcdot, int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw,
+                      int64_t ldd, float* dw, float* dbb, float* dcb, float* dang, cudaStream_t st) {
   OXI_CHECK(N == M3N && H % G == 0 && H <= 64, "Mamba3 B/C prologue supports state size 128, <= 64 heads");
   const int64_t blocks = std::min<int64_t>(((int64_t)B * S + 7) / 8, 148 * 4);
   const int smem = 2 * H * M3N * (int)sizeof(float);
-  if (smem > 48 * 1024)
-    OXI_CUDA_CHECK(cudaFuncSetAttribute(m3_bc_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  m3_bc_bwd_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, smem, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(braw), reinterpret_cast<const __nv_bfloat16*>(craw), ldr,
-      reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<const __nv_bfloat16*>(bbias),
-      reinterpret_cast<const __nv_bfloat16*>(cbias), ang, db2, dc2, dbcdot, B, S, H, G, eps, dbraw, dcraw, ldd, dw, dbb, dcb,
-      dang);
+  const auto* br = reinterpret_cast<const __nv_bfloat16*>(braw);
+  const auto* cr = reinterpret_cast<const __nv_bfloat16*>(craw);
+  const auto* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+  const auto* bb = reinterpret_cast<const __nv_bfloat16*>(bbias);
+  const auto* cb = reinterpret_cast<const __nv_bfloat16*>(cbias);
+  const unsigned grid = (unsigned)std::max<int64_t>(blocks, 1);
+  if (grads_bf16) {
+    auto kern = m3_bc_bwd_kernel<__nv_bfloat16>;
+    if (smem > 48 * 1024) OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, 256, smem, st>>>(br, cr, ldr, wb, bb, cb, ang, reinterpret_cast<const __nv_bfloat16*>(db),
+                                  reinterpret_cast<const __nv_bfloat16*>(dc), dbcdot, B, S, H, G, eps, dbraw, dcraw,
+                                  ldd, dw, dbb, dcb, dang);
+  } else {
+    auto kern = m3_bc_bwd_kernel<float>;
+    if (smem > 48 * 1024) OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, 256, smem, st>>>(br, cr, ldr, wb, bb, cb, ang, reinterpret_cast<const float*>(db),
+                                  reinterpret_cast<const float*>(dc), dbcdot, B, S, H, G, eps, dbraw, dcraw, ldd, dw,
+                                  dbb, dcb, dang);
+  }
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

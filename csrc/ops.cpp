@@ -574,8 +574,10 @@ std::vector<torch::Tensor> ssd_tc_bwd(torch::Tensor x, torch::Tensor Bm, torch::
   TORCH_CHECK(hs.is_contiguous() && hs.scalar_type() == torch::kBFloat16, "hs");
   auto f32 = x.options().dtype(torch::kFloat32);
   auto dx = torch::empty({B * S, H * P}, f32);
-  auto dB = torch::empty({B * S, H * 128}, f32);  // every row written by the chunk pass
-  auto dC = torch::empty({B * S, H * 128}, f32);
+  // every row written by the chunk pass; per-head B/C (G == H, bf16) get bf16 gradients
+  const bool dbc_bf16 = G == H && Bm.scalar_type() == torch::kBFloat16;
+  auto dB = torch::empty({B * S, H * 128}, dbc_bf16 ? x.options() : f32);
+  auto dC = torch::empty({B * S, H * 128}, dbc_bf16 ? x.options() : f32);
   auto dg = torch::zeros({B, S, H}, f32);
   auto dhs = torch::empty_like(hs);
   oxi::SsdTcIO io{};
@@ -585,7 +587,9 @@ std::vector<torch::Tensor> ssd_tc_bwd(torch::Tensor x, torch::Tensor Bm, torch::
   io.Cm = Cm.data_ptr(); io.ldc = Cm.stride(0);
   io.loga = loga.data_ptr<float>(); io.gamma = gamma.data_ptr<float>();
   io.hs = hs.data_ptr(); io.dy = dy.data_ptr(); io.dhs = dhs.data_ptr();
-  io.dx = dx.data_ptr<float>(); io.dB = dB.data_ptr<float>(); io.dC = dC.data_ptr<float>();
+  io.dx = dx.data_ptr<float>();
+  io.dB = reinterpret_cast<float*>(dB.data_ptr()); io.dC = reinterpret_cast<float*>(dC.data_ptr());
+  io.dbc_bf16 = dbc_bf16 ? 1 : 0;
   io.dgamma = dg.data_ptr<float>();
   const int64_t nc = S / 128;
   auto hloc = torch::empty({B * H * nc * 128, P}, f32);
@@ -622,9 +626,10 @@ std::vector<torch::Tensor> m3_bc_bwd(torch::Tensor braw, torch::Tensor craw, tor
                                      c10::optional<torch::Tensor> dbcdot, int64_t B, int64_t S, int64_t H, int64_t G,
                                      double eps) {
   c10::cuda::CUDAGuard g(braw.device());
-  TORCH_CHECK(db.scalar_type() == torch::kFloat32 && dc.scalar_type() == torch::kFloat32 && db.is_contiguous() &&
-                  dc.is_contiguous() && db.numel() == B * S * H * 128 && dc.numel() == db.numel(),
-              "db / dc: f32 contiguous [B, S, H, N]");
+  TORCH_CHECK(db.scalar_type() == dc.scalar_type() &&
+                  (db.scalar_type() == torch::kFloat32 || db.scalar_type() == torch::kBFloat16) &&
+                  db.is_contiguous() && dc.is_contiguous() && db.numel() == B * S * H * 128 && dc.numel() == db.numel(),
+              "db / dc: f32 or bf16 contiguous [B, S, H, N]");
   const float* dd = nullptr;
   if (dbcdot.has_value() && dbcdot->defined()) {
     TORCH_CHECK(dbcdot->scalar_type() == torch::kFloat32 && dbcdot->is_contiguous() && dbcdot->numel() == B * S * H,
@@ -639,7 +644,8 @@ std::vector<torch::Tensor> m3_bc_bwd(torch::Tensor braw, torch::Tensor craw, tor
   auto dcb = torch::zeros({H, 128}, f32);
   auto dang = torch::empty({B, S, H, 64}, f32);
   oxi::launch_m3_bc_bwd(braw.data_ptr(), craw.data_ptr(), braw.stride(0), w.data_ptr(), bbias.data_ptr(),
-                        cbias.data_ptr(), ang.data_ptr<float>(), db.data_ptr<float>(), dc.data_ptr<float>(), dd,
+                        cbias.data_ptr(), ang.data_ptr<float>(), db.data_ptr(), dc.data_ptr(),
+                        db.scalar_type() == torch::kBFloat16, dd,
                         (int)B, (int)S, (int)H, (int)G, 128, (float)eps, dbraw.data_ptr<float>(),
                         dcraw.data_ptr<float>(), dbraw.stride(0), dw.data_ptr<float>(), dbb.data_ptr<float>(),
                         dcb.data_ptr<float>(), dang.data_ptr<float>(), stream());

@@ -58,8 +58,9 @@ struct SsdParams {
   __nv_bfloat16* hs;          // [B*H*nc*N, P] chunk-start states (fwd writes, bwd reads via TMA)
   __nv_bfloat16* dhs;         // [B*H*nc*N, P] chunk-end adjoints (bwd pass 1 writes)
   float* dx;                  // [B*S, H*P] f32
-  float* dB;                  // [B*S, H*N] f32
-  float* dC;                  // [B*S, H*N] f32
+  float* dB;                  // [B*S, H*N] f32 (bf16 when dbc_bf16)
+  float* dC;                  // [B*S, H*N] f32 (bf16 when dbc_bf16)
+  int dbc_bf16;
   float* dgamma;              // [B, S, H] f32 (atomics)
   float* hloc;                // [B*H*nc*N, P] f32 chunk-local end states (chunk-parallel forward)
   float* lamend;              // [B*H*nc] f32 sum of loga over each chunk
@@ -108,6 +109,22 @@ __device__ __forceinline__ void store_row64(uint8_t* tile, int m, const float* v
                   make_uint4(pack_bf16(v[c * 8], v[c * 8 + 1]), pack_bf16(v[c * 8 + 2], v[c * 8 + 3]),
                              pack_bf16(v[c * 8 + 4], v[c * 8 + 5]), pack_bf16(v[c * 8 + 6], v[c * 8 + 7])));
 }
+// 64 consecutive outputs at element offset `off` of an f32 (or, when bf16, a
+// bf16-typed) buffer
+__device__ __forceinline__ void store_row_out(float* base, int64_t off, const float* v, int bf16) {
+  if (bf16) {
+    uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + off);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      d[q] = make_uint4(pack_bf16(v[q * 8], v[q * 8 + 1]), pack_bf16(v[q * 8 + 2], v[q * 8 + 3]),
+                        pack_bf16(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16(v[q * 8 + 6], v[q * 8 + 7]));
+  } else {
+    float4* d = reinterpret_cast<float4*>(base + off);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) d[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  }
+}
+
 // row m, columns [32 h, 32 h + 32) of a [128][64] bf16 SW128 tile -> 32 floats
 __device__ __forceinline__ void load_row32(const uint8_t* tile, int m, int h, float* out) {
 #pragma unroll
@@ -892,25 +909,19 @@ __global__ void __launch_bounds__(BWD2_THREADS, 1)
       // row m: dC_t (t = m) and dB_s (s = m), 128 values each, written once
       const float e = __expf(lam);
       const float w = __expf(lam_end - lam) * gm;
-      float* dcr = p.dC + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
-      float* dbr = p.dB + ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN;
+      const int64_t orow = ((int64_t)row0 + c * SL + m) * ((int64_t)p.H * SN) + h * SN + colhalf * 64;
       {
-        const int half = colhalf;
         float v[64], u[64];
-        tmem_row64(TM_S + lb + half * 64, v);
-        tmem_row64(TM_CP + lb + half * 64, u);
+        tmem_row64(TM_S + lb + colhalf * 64, v);
+        tmem_row64(TM_CP + lb + colhalf * 64, u);
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-          reinterpret_cast<float4*>(dcr + half * 64)[k] =
-              make_float4(v[4 * k] + e * u[4 * k], v[4 * k + 1] + e * u[4 * k + 1], v[4 * k + 2] + e * u[4 * k + 2],
-                          v[4 * k + 3] + e * u[4 * k + 3]);
-        tmem_row64(TM_DM + lb + half * 64, v);
-        tmem_row64(TM_BP + lb + half * 64, u);
+        for (int k = 0; k < 64; ++k) v[k] += e * u[k];
+        store_row_out(p.dC, orow, v, p.dbc_bf16);
+        tmem_row64(TM_DM + lb + colhalf * 64, v);
+        tmem_row64(TM_BP + lb + colhalf * 64, u);
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-          reinterpret_cast<float4*>(dbr + half * 64)[k] =
-              make_float4(v[4 * k] + w * u[4 * k], v[4 * k + 1] + w * u[4 * k + 1], v[4 * k + 2] + w * u[4 * k + 2],
-                          v[4 * k + 3] + w * u[4 * k + 3]);
+        for (int k = 0; k < 64; ++k) v[k] += w * u[k];
+        store_row_out(p.dB, orow, v, p.dbc_bf16);
       }
     }
   }
@@ -983,7 +994,7 @@ void launch_ssd_bwd(const SsdTcIO& io, cudaStream_t st) {
   p.loga = io.loga; p.gamma = io.gamma;
   p.hs = reinterpret_cast<__nv_bfloat16*>(io.hs);
   p.dhs = reinterpret_cast<__nv_bfloat16*>(io.dhs);
-  p.dx = io.dx; p.dB = io.dB; p.dC = io.dC; p.dgamma = io.dgamma;
+  p.dx = io.dx; p.dB = io.dB; p.dC = io.dC; p.dgamma = io.dgamma; p.dbc_bf16 = io.dbc_bf16;
   p.hloc = io.hloc; p.lamend = io.lamend;
   p.status = io.status;
   OXI_CHECK(io.hloc && io.lamend, "backward scratch missing");

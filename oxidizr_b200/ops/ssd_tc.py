@@ -142,7 +142,10 @@ class Mamba3BC(torch.autograd.Function):
     def backward(ctx, db, dc, ddot):
         b2d, c2d, w, bbias, cbias, angc = ctx.saved_tensors
         Bsz, S, H, G, eps, shape = ctx.cfg
-        z = lambda t: torch.zeros(Bsz, S, H, 128, device=angc.device) if t is None else t.float().contiguous()
+        def z(t):  # bf16 gradients (per-head B/C from the tensor-core scan) are read as bf16
+            if t is None:
+                return torch.zeros(Bsz, S, H, 128, device=angc.device)
+            return t.contiguous() if t.dtype == torch.bfloat16 else t.float().contiguous()
         dd = None if ddot is None else ddot.float().contiguous()
         dbr, dcr, dw, dbb, dcb, dang = ext().m3_bc_bwd(b2d, c2d, w.contiguous(), bbias.contiguous(),
                                                        cbias.contiguous(), angc, z(db), z(dc), dd, Bsz, S, H, G, eps)
