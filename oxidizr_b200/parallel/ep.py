@@ -114,9 +114,11 @@ class EPGroup:
 class EPLayerBuffers:
     """The symmetric receive/output buffers of one MoE layer (grown collectively)."""
 
-    # receive-buffer growth is a collective (IPC handle exchange), so it must be
-    # rare: the first size leaves room for routing imbalance, growth is 1.5x
-    HEADROOM = 1.5
+    # receive-buffer growth is a collective (IPC handle exchange plus a device
+    # sync), so it must be rare: the first size and every growth leave 2x room for
+    # routing imbalance (routers drift while training; at 1.5x a 4-GPU run still
+    # regrew five of sixteen layers in eight steps)
+    HEADROOM = 2.0
     reallocs = 0  # class-wide count, reported by the benchmark
 
     def __init__(self, grp: EPGroup, H: int):
