@@ -105,6 +105,22 @@ class EPGroup:
         t = timeout_s if timeout_s is not None else float(os.environ.get("OXI_PEER_TIMEOUT_S", 30.0))
         self.wait_ns = int(t * 1e9)
         self.seq = 0
+        # gradient rows pushed to expert owners live only inside one layer's
+        # backward, so every layer of the group shares one buffer
+        self.dyrecv = None
+        self.dyrecv_bytes = 0
+
+    def shared_dyrecv(self, nbytes: int):
+        """The group's gradient receive buffer, grown collectively to at least nbytes."""
+        if nbytes > self.dyrecv_bytes:
+            from .fused_ar import SymmetricBuffer
+            torch.cuda.synchronize(self.device)
+            if self.dyrecv is not None:
+                self.dyrecv.close()
+                dist.barrier(group=self.group)
+            self.dyrecv = SymmetricBuffer(nbytes, self.device, self.group)
+            self.dyrecv_bytes = nbytes
+        return self.dyrecv
 
     def next_seq(self) -> int:
         self.seq += 1
@@ -136,22 +152,25 @@ class EPLayerBuffers:
         EPLayerBuffers.reallocs += 1
         torch.cuda.synchronize(g.device)
         if self.bufs is not None:
-            for b in self.bufs.values():
-                b.close()
+            for name, b in self.bufs.items():
+                if name != "dyrecv":  # the group's shared buffer
+                    b.close()
             dist.barrier(group=g.group)
         H = self.H
         self.bufs = {
             "xrecv": SymmetricBuffer(cap * H * 2, g.device, g.group),
             "yout": SymmetricBuffer(cap * H * 2, g.device, g.group),
-            "dyrecv": SymmetricBuffer(cap * H * 2, g.device, g.group),
             "metaw": SymmetricBuffer(cap * 4, g.device, g.group),
             "dwrow": SymmetricBuffer(cap * 4, g.device, g.group),
         }
+        self.bufs["dyrecv"] = g.shared_dyrecv(cap * H * 2)
         self.cap = cap
 
     def local(self, name: str, dtype, cols: int = 0) -> torch.Tensor:
         t = self.bufs[name].local.view(dtype)
-        return t.view(self.cap, cols) if cols else t
+        if cols:
+            return t[: self.cap * cols].view(self.cap, cols)
+        return t[: self.cap] if dtype == torch.float32 else t
 
     def table(self, name: str) -> torch.Tensor:
         return self.bufs[name].ptr_table
