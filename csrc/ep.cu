@@ -5,11 +5,13 @@
 // rank holds, mapped by all peers:
 //   xrecv  bf16 [cap, H]  token rows routed to its experts, one 128-aligned
 //                         segment per local expert (sources in rank order)
-//   yout   bf16 [cap, H]  expert outputs (forward); the gradient of xrecv
-//                         (backward, once yout has been consumed)
-//   dyrecv bf16 [cap, H]  output gradients pushed back by the sources
+//   srcidx int32 [cap]    source of each received row: rank * T*k + pair, -1 = padding
+//   yret   bf16 [T*k, H]  this rank's own (token, slot) pairs: the expert output
+//                         rows (forward), then their input gradients (backward),
+//                         written by the owners' expert GEMM epilogues
+//   dyrecv bf16 [cap, H]  output gradients pushed back by the sources (one
+//                         buffer shared by all layers)
 //   metaw  f32  [cap]     routing weight of each received row
-//   dwrow  f32  [cap]     d loss / d weight of each received row
 //   pad    int32          flags [EP_NKIND][EP_MAXW] + counts [EP_MAXW][EP_MAXE]
 //
 // One step of a MoE layer (seq = a number that grows by one per exchange, the
@@ -17,16 +19,19 @@
 //   counts   : all-gather the per-expert selection counts through the pads
 //              (-> every rank knows every segment of every peer)
 //   dispatch : warp per (token, slot): P2P 16-byte stores of the token row
-//              into the owner's xrecv; last CTA posts flag DISPATCHED
-//   wait(DISPATCHED) ; grouped expert GEMMs on xrecv -> yout ; signal(YREADY)
-//   combine  : warp per token: wait YREADY, P2P loads of the k expert rows,
-//              y = resid + sum_j w_j * row_j (f32 accumulate)
+//              into the owner's xrecv (+ its srcidx, metaw); last CTA posts DISPATCHED
+//   wait(DISPATCHED) ; gate/up grouped GEMM ; down-projection grouped GEMM
+//              whose epilogue stores every output row straight into its
+//              source's yret (P2P, overlapping the remaining tiles) and whose
+//              last CTA posts YREADY
+//   wait(YREADY) ; combine locally: y = resid + sum_j w_j yret[t k + j]
 // backward:
-//   push_dy  : warp per (token, slot): P2P stores of dy into the owner's dyrecv;
-//              last CTA posts DYPUSHED
-//   wait(DYPUSHED) ; scale_rows: dwrow = <dyrecv, yout>, dyrecv *= metaw, pad
-//   rows zeroed ; grouped backward GEMMs (dxrecv into yout) ; signal(DXREADY)
-//   gather   : warp per token: wait DXREADY, dx = sum_j dxrecv_j, dw_j = dwrow_j
+//   push_dy  : warp per (token, slot): P2P stores of dy into the owner's dyrecv
+//              and dw_j = <dy_t, yret[t k + j]> (local); last CTA posts DYPUSHED
+//   wait(DYPUSHED) ; scale_rows: dyrecv *= metaw, pad rows zeroed ; grouped
+//              backward GEMMs, the last one scattering the input-gradient rows
+//              into the sources' yret and posting DXREADY
+//   wait(DXREADY) ; gather locally: dx_t = sum_j yret[t k + j]
 // Every wait is bounded; a timeout records OXI_ERR_TIMEOUT_PEER in the status
 // word and the kernel skips its remote accesses.  No TMA is used here.
 #include <cuda_bf16.h>
@@ -142,8 +147,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t ldx, const int64_t* __restrict__ topi,
     const float* __restrict__ topw, int64_t T, int k, int H, const int* __restrict__ all_counts, int rank, int W,
     int E, int* __restrict__ cursor, const uint64_t* __restrict__ peers_xrecv, const uint64_t* __restrict__ peers_metaw,
-    int* __restrict__ pos_out, int* __restrict__ done_ctr, const uint64_t* __restrict__ peer_pads, int seq,
-    const int* status) {
+    const uint64_t* __restrict__ peers_srcidx, int* __restrict__ pos_out, int* __restrict__ done_ctr,
+    const uint64_t* __restrict__ peer_pads, int seq, const int* status) {
   __shared__ int s_base[EP_MAXE];
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_base[e] = dest_base(all_counts, rank, W, E, e);
   __syncthreads();
@@ -167,10 +172,19 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
       if (lane == 0) {
         pos_out[p] = pos;
         reinterpret_cast<float*>(peers_metaw[dest])[pos] = topw[p];
+        reinterpret_cast<int*>(peers_srcidx[dest])[pos] = rank * (int)pairs + (int)p;
       }
     }
   }
   ep_last_cta_post(done_ctr, peer_pads, EP_K_DISPATCHED, rank, W, seq);
+}
+
+// srcidx of the padding rows of every local expert segment = -1 (peers write
+// only real rows, so this never races with a dispatch)
+__global__ void ep_mark_pad_kernel(const int* __restrict__ seg_off, const int* __restrict__ recv_counts, int El,
+                                   int* __restrict__ srcidx) {
+  const int e = blockIdx.x;
+  for (int r = seg_off[e] + recv_counts[e] + threadIdx.x; r < seg_off[e + 1]; r += blockDim.x) srcidx[r] = -1;
 }
 
 __global__ void ep_wait_kernel(const int* my_pad, int kind, int W, int seq, int* status, uint64_t wait_ns) {
@@ -181,77 +195,13 @@ __global__ void ep_signal_kernel(const uint64_t* peer_pads, int kind, int rank, 
   if (threadIdx.x == 0 && blockIdx.x == 0) ep_post_all(peer_pads, kind, rank, W, seq);
 }
 
-// ------------------------------------------------------------------ combine
-// warp per token; each lane owns 8 columns of a 256-column chunk; all k remote
-// rows of a chunk are loaded before any is accumulated.
-template <int KMAX>
-__global__ void __launch_bounds__(256) ep_combine_kernel(
-    const int64_t* __restrict__ topi, const float* __restrict__ topw, const int* __restrict__ pos, int64_t T, int k,
-    int H, int El, const uint64_t* __restrict__ peers_yout, const __nv_bfloat16* __restrict__ resid,
-    __nv_bfloat16* __restrict__ y, const int* my_pad, int W, int seq, int* status, uint64_t wait_ns) {
-  // the wait for every owner's expert outputs ran in ep_wait_kernel just before
-  // this launch (one thread spins, not the whole grid)
-  const int ok_s = (status == nullptr || *reinterpret_cast<const volatile int*>(status) == 0) ? 1 : 0;
-  const int lane = threadIdx.x & 31;
-  const int nvec = H / 8;
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T;
-       t += (int64_t)gridDim.x * (blockDim.x / 32)) {
-    const uint4* rows[KMAX];
-    float w[KMAX];
-#pragma unroll
-    for (int j = 0; j < KMAX; ++j) {
-      if (j < k) {
-        const int e = (int)topi[t * k + j];
-        rows[j] = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers_yout[e / El]) +
-                                                 (int64_t)pos[t * k + j] * H);
-        w[j] = topw[t * k + j];
-      }
-    }
-    for (int v = lane; v < nvec; v += 32) {
-      float acc[8];
-      if (resid) {
-        const uint4 r = reinterpret_cast<const uint4*>(resid + t * H)[v];
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __bfloat1622float2(h[q]);
-          acc[2 * q] = f.x;
-          acc[2 * q + 1] = f.y;
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-      }
-      if (ok_s) {
-        uint4 u[KMAX];
-#pragma unroll
-        for (int j = 0; j < KMAX; ++j)
-          if (j < k) u[j] = rows[j][v];
-#pragma unroll
-        for (int j = 0; j < KMAX; ++j) {
-          if (j < k) {
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 f = __bfloat1622float2(h[q]);
-              acc[2 * q] += w[j] * f.x;
-              acc[2 * q + 1] += w[j] * f.y;
-            }
-          }
-        }
-      }
-      reinterpret_cast<uint4*>(y + t * H)[v] =
-          make_uint4(pack_bf16(acc[0], acc[1]), pack_bf16(acc[2], acc[3]), pack_bf16(acc[4], acc[5]),
-                     pack_bf16(acc[6], acc[7]));
-    }
-  }
-}
-
-// ------------------------------------------------------------------ backward
+// warp per (token, slot) pair p: dy row -> owner's dyrecv (P2P stores) and
+// dw[p] = <dy_t, yret[p]> from this rank's copy of the expert output row
 __global__ void __launch_bounds__(256) ep_push_dy_kernel(
     const __nv_bfloat16* __restrict__ dy, const int64_t* __restrict__ topi, const int* __restrict__ pos, int64_t T,
-    int k, int H, int El, const uint64_t* __restrict__ peers_dyrecv, int* __restrict__ done_ctr,
-    const uint64_t* __restrict__ peer_pads, int rank, int W, int seq, const int* status) {
+    int k, int H, int El, const uint64_t* __restrict__ peers_dyrecv, const __nv_bfloat16* __restrict__ yret,
+    float* __restrict__ dw, int* __restrict__ done_ctr, const uint64_t* __restrict__ peer_pads, int rank, int W,
+    int seq, const int* status) {
   const bool failed = status && *reinterpret_cast<const volatile int*>(status) != 0;
   const int lane = threadIdx.x & 31;
   const int nvec = H / 8;
@@ -260,19 +210,34 @@ __global__ void __launch_bounds__(256) ep_push_dy_kernel(
          p += (int64_t)gridDim.x * (blockDim.x / 32)) {
       const int e = (int)topi[p];
       const uint4* src = reinterpret_cast<const uint4*>(dy + (p / k) * H);
+      const uint4* yr = reinterpret_cast<const uint4*>(yret + p * H);
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers_dyrecv[e / El]) +
                                             (int64_t)pos[p] * H);
-      for (int v = lane; v < nvec; v += 32) dst[v] = src[v];
+      float dot = 0.f;
+      for (int v = lane; v < nvec; v += 32) {
+        const uint4 a = src[v];
+        dst[v] = a;
+        const uint4 b = yr[v];
+        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 fa = __bfloat1622float2(ha[q]), fb = __bfloat1622float2(hb[q]);
+          dot += fa.x * fb.x + fa.y * fb.y;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (lane == 0) dw[p] = dot;
     }
   }
   ep_last_cta_post(done_ctr, peer_pads, EP_K_DYPUSHED, rank, W, seq);
 }
 
-// Owner side, local: dwrow[r] = <dyrecv[r], yout[r]>, dyrecv[r] *= metaw[r];
-// padding rows of dyrecv are zeroed.  Warp per row.
+// Owner side, local: dyrecv[r] *= metaw[r]; padding rows of dyrecv are zeroed.
+// Warp per row.
 __global__ void __launch_bounds__(256) ep_scale_rows_kernel(__nv_bfloat16* __restrict__ dyrecv,
-                                                            const __nv_bfloat16* __restrict__ yout,
-                                                            const float* __restrict__ metaw, float* __restrict__ dwrow,
+                                                            const float* __restrict__ metaw,
                                                             const int* __restrict__ seg_off,
                                                             const int* __restrict__ recv_counts, int El, int H) {
   const int lane = threadIdx.x & 31;
@@ -290,71 +255,57 @@ __global__ void __launch_bounds__(256) ep_scale_rows_kernel(__nv_bfloat16* __res
       for (int v = lane; v < nvec; v += 32) d[v] = make_uint4(0u, 0u, 0u, 0u);
       continue;
     }
-    const uint4* yr = reinterpret_cast<const uint4*>(yout + (int64_t)r * H);
     const float w = metaw[r];
-    float dot = 0.f;
     for (int v = lane; v < nvec; v += 32) {
       uint4 a = d[v];
-      const uint4 b = yr[v];
       __nv_bfloat162* ha = reinterpret_cast<__nv_bfloat162*>(&a);
-      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float2 fa = __bfloat1622float2(ha[q]), fb = __bfloat1622float2(hb[q]);
-        dot += fa.x * fb.x + fa.y * fb.y;
+        const float2 fa = __bfloat1622float2(ha[q]);
         ha[q] = __floats2bfloat162_rn(fa.x * w, fa.y * w);
       }
       d[v] = a;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    if (lane == 0) dwrow[r] = dot;
   }
 }
 
-template <int KMAX>
-__global__ void __launch_bounds__(256) ep_gather_kernel(
-    const int64_t* __restrict__ topi, const int* __restrict__ pos, int64_t T, int k, int H, int El,
-    const uint64_t* __restrict__ peers_dx, const uint64_t* __restrict__ peers_dwrow, __nv_bfloat16* __restrict__ dx,
-    float* __restrict__ dw, const int* my_pad, int W, int seq, int* status, uint64_t wait_ns) {
-  // the wait for every owner's input gradients ran in ep_wait_kernel just before this launch
-  const int ok_s = (status == nullptr || *reinterpret_cast<const volatile int*>(status) == 0) ? 1 : 0;
+// local combine / gather over this rank's own pairs: out[t] = (resid[t]) +
+// sum_j (w ? w[t k + j] : 1) * rows[t k + j]  (warp per token, f32 accumulate)
+__global__ void __launch_bounds__(256) ep_sum_pairs_kernel(const __nv_bfloat16* __restrict__ rows,
+                                                           const float* __restrict__ w, int64_t T, int k, int H,
+                                                           const __nv_bfloat16* __restrict__ resid,
+                                                           __nv_bfloat16* __restrict__ out, const int* status) {
+  const bool ok_s = status == nullptr || *reinterpret_cast<const volatile int*>(status) == 0;
   const int lane = threadIdx.x & 31;
   const int nvec = H / 8;
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T;
        t += (int64_t)gridDim.x * (blockDim.x / 32)) {
-    const uint4* rows[KMAX];
-#pragma unroll
-    for (int j = 0; j < KMAX; ++j) {
-      if (j < k) {
-        const int e = (int)topi[t * k + j];
-        const int pj = pos[t * k + j];
-        rows[j] = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(peers_dx[e / El]) +
-                                                 (int64_t)pj * H);
-        if (lane == j) dw[t * k + j] = ok_s ? reinterpret_cast<const float*>(peers_dwrow[e / El])[pj] : 0.f;
-      }
-    }
     for (int v = lane; v < nvec; v += 32) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (resid) {
+        const uint4 r = reinterpret_cast<const uint4*>(resid + t * H)[v];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          acc[2 * q] = f.x;
+          acc[2 * q + 1] = f.y;
+        }
+      }
       if (ok_s) {
-        uint4 u[KMAX];
+        for (int j = 0; j < k; ++j) {
+          const uint4 u = reinterpret_cast<const uint4*>(rows + (t * k + j) * H)[v];
+          const float wj = w ? w[t * k + j] : 1.f;
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int j = 0; j < KMAX; ++j)
-          if (j < k) u[j] = rows[j][v];
-#pragma unroll
-        for (int j = 0; j < KMAX; ++j) {
-          if (j < k) {
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 f = __bfloat1622float2(h[q]);
-              acc[2 * q] += f.x;
-              acc[2 * q + 1] += f.y;
-            }
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(h[q]);
+            acc[2 * q] += wj * f.x;
+            acc[2 * q + 1] += wj * f.y;
           }
         }
       }
-      reinterpret_cast<uint4*>(dx + t * H)[v] =
+      reinterpret_cast<uint4*>(out + t * H)[v] =
           make_uint4(pack_bf16(acc[0], acc[1]), pack_bf16(acc[2], acc[3]), pack_bf16(acc[4], acc[5]),
                      pack_bf16(acc[6], acc[7]));
     }
@@ -389,13 +340,19 @@ void launch_ep_counts(const int* local_counts, const uint64_t* peer_pads, int* m
 
 void launch_ep_dispatch(const void* x, int64_t ldx, const int64_t* topi, const float* topw, int64_t T, int k, int H,
                         const int* all_counts, int rank, int W, int E, int* cursor, const uint64_t* peers_xrecv,
-                        const uint64_t* peers_metaw, int* pos_out, int* done_ctr, const uint64_t* peer_pads, int seq,
-                        const int* status, cudaStream_t st) {
+                        const uint64_t* peers_metaw, const uint64_t* peers_srcidx, int* pos_out, int* done_ctr,
+                        const uint64_t* peer_pads, int seq, const int* status, cudaStream_t st) {
   OXI_CHECK(H % 8 == 0 && ldx % 8 == 0, "hidden size must be a multiple of 8");
+  OXI_CHECK((int64_t)W * T * k < (1ll << 31), "source index must fit int32");
   OXI_CUDA_CHECK(cudaMemsetAsync(cursor, 0, sizeof(int) * E, st));
   ep_dispatch_kernel<<<warp_grid(T * k), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, topi, topw, T,
                                                        k, H, all_counts, rank, W, E, cursor, peers_xrecv, peers_metaw,
-                                                       pos_out, done_ctr, peer_pads, seq, status);
+                                                       peers_srcidx, pos_out, done_ctr, peer_pads, seq, status);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
+void launch_ep_mark_pad(const int* seg_off, const int* recv_counts, int El, int* srcidx, cudaStream_t st) {
+  ep_mark_pad_kernel<<<El, 128, 0, st>>>(seg_off, recv_counts, El, srcidx);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -409,56 +366,31 @@ void launch_ep_signal(const uint64_t* peer_pads, int kind, int rank, int W, int 
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_ep_combine(const int64_t* topi, const float* topw, const int* pos, int64_t T, int k, int H, int El,
-                       const uint64_t* peers_yout, const void* resid, void* y, const int* my_pad, int W, int seq,
-                       int* status, int64_t wait_ns, cudaStream_t st) {
-  OXI_CHECK(k >= 1 && k <= 16 && H % 8 == 0, "combine: k <= 16, H % 8 == 0");
-  ep_wait_kernel<<<1, 32, 0, st>>>(my_pad, EP_K_YREADY, W, seq, status, (uint64_t)wait_ns);
-  const auto* r = reinterpret_cast<const __nv_bfloat16*>(resid);
-  auto* yy = reinterpret_cast<__nv_bfloat16*>(y);
-  if (k <= 4)
-    ep_combine_kernel<4><<<warp_grid(T), 256, 0, st>>>(topi, topw, pos, T, k, H, El, peers_yout, r, yy, my_pad, W,
-                                                       seq, status, (uint64_t)wait_ns);
-  else if (k <= 8)
-    ep_combine_kernel<8><<<warp_grid(T), 256, 0, st>>>(topi, topw, pos, T, k, H, El, peers_yout, r, yy, my_pad, W,
-                                                       seq, status, (uint64_t)wait_ns);
-  else
-    ep_combine_kernel<16><<<warp_grid(T), 256, 0, st>>>(topi, topw, pos, T, k, H, El, peers_yout, r, yy, my_pad, W,
-                                                        seq, status, (uint64_t)wait_ns);
+void launch_ep_sum_pairs(const void* rows, const float* w, int64_t T, int k, int H, const void* resid, void* out,
+                         const int* my_pad, int wait_kind, int W, int seq, int* status, int64_t wait_ns,
+                         cudaStream_t st) {
+  OXI_CHECK(H % 8 == 0, "hidden size must be a multiple of 8");
+  // one thread waits for every owner's rows (the grid does not spin)
+  ep_wait_kernel<<<1, 32, 0, st>>>(my_pad, wait_kind, W, seq, status, (uint64_t)wait_ns);
+  ep_sum_pairs_kernel<<<warp_grid(T), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(rows), w, T, k, H,
+                                                    reinterpret_cast<const __nv_bfloat16*>(resid),
+                                                    reinterpret_cast<__nv_bfloat16*>(out), status);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_ep_push_dy(const void* dy, const int64_t* topi, const int* pos, int64_t T, int k, int H, int El,
-                       const uint64_t* peers_dyrecv, int* done_ctr, const uint64_t* peer_pads, int rank, int W, int seq,
-                       const int* status, cudaStream_t st) {
+                       const uint64_t* peers_dyrecv, const void* yret, float* dw, int* done_ctr,
+                       const uint64_t* peer_pads, int rank, int W, int seq, const int* status, cudaStream_t st) {
   ep_push_dy_kernel<<<warp_grid(T * k), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(dy), topi, pos, T, k, H,
-                                                      El, peers_dyrecv, done_ctr, peer_pads, rank, W, seq, status);
+                                                      El, peers_dyrecv, reinterpret_cast<const __nv_bfloat16*>(yret),
+                                                      dw, done_ctr, peer_pads, rank, W, seq, status);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
-void launch_ep_scale_rows(void* dyrecv, const void* yout, const float* metaw, float* dwrow, const int* seg_off,
-                          const int* recv_counts, int El, int H, int64_t cap_rows, cudaStream_t st) {
-  ep_scale_rows_kernel<<<warp_grid(cap_rows), 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(dyrecv),
-                                                            reinterpret_cast<const __nv_bfloat16*>(yout), metaw, dwrow,
-                                                            seg_off, recv_counts, El, H);
-  OXI_CUDA_CHECK(cudaGetLastError());
-}
-
-void launch_ep_gather(const int64_t* topi, const int* pos, int64_t T, int k, int H, int El, const uint64_t* peers_dx,
-                      const uint64_t* peers_dwrow, void* dx, float* dw, const int* my_pad, int W, int seq, int* status,
-                      int64_t wait_ns, cudaStream_t st) {
-  OXI_CHECK(k >= 1 && k <= 16 && H % 8 == 0, "gather: k <= 16, H % 8 == 0");
-  ep_wait_kernel<<<1, 32, 0, st>>>(my_pad, EP_K_DXREADY, W, seq, status, (uint64_t)wait_ns);
-  auto* d = reinterpret_cast<__nv_bfloat16*>(dx);
-  if (k <= 4)
-    ep_gather_kernel<4><<<warp_grid(T), 256, 0, st>>>(topi, pos, T, k, H, El, peers_dx, peers_dwrow, d, dw, my_pad, W,
-                                                      seq, status, (uint64_t)wait_ns);
-  else if (k <= 8)
-    ep_gather_kernel<8><<<warp_grid(T), 256, 0, st>>>(topi, pos, T, k, H, El, peers_dx, peers_dwrow, d, dw, my_pad, W,
-                                                      seq, status, (uint64_t)wait_ns);
-  else
-    ep_gather_kernel<16><<<warp_grid(T), 256, 0, st>>>(topi, pos, T, k, H, El, peers_dx, peers_dwrow, d, dw, my_pad,
-                                                       W, seq, status, (uint64_t)wait_ns);
+void launch_ep_scale_rows(void* dyrecv, const float* metaw, const int* seg_off, const int* recv_counts, int El, int H,
+                          int64_t cap_rows, cudaStream_t st) {
+  ep_scale_rows_kernel<<<warp_grid(cap_rows), 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(dyrecv), metaw, seg_off,
+                                                            recv_counts, El, H);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -29,6 +29,7 @@
 #include <cstdlib>
 
 #include "host_util.h"
+#include "kernels_ep.h"
 
 #include "ptx.cuh"
 
@@ -79,6 +80,18 @@ struct GemmParams {
   int64_t b_group_stride;  // B tensor-map rows per expert
   int64_t d_group_stride;  // output elements per expert (group-K)
   int cg;                  // 2: CTA-pair tiles (256 x 256, cta_group::2); else one CTA per 128 x 256 tile
+  // BF16 epilogue, row scatter to peers (expert-parallel combine fused into the
+  // expert GEMM): output row r goes to row (i % scatter_rows) of the buffer at
+  // scatter_ptrs[i / scatter_rows], i = scatter_idx[r]; rows with i < 0 are
+  // dropped.  The buffers may be other GPUs' memory (plain P2P stores).
+  const int* scatter_idx;
+  const uint64_t* scatter_ptrs;
+  int scatter_rows;
+  // after its last store the last CTA to finish posts flag (post_kind, post_rank)
+  // = post_seq into every peer's signal pad (expert-parallel pad layout)
+  int* post_ctr;
+  const uint64_t* post_pads;
+  int post_kind, post_rank, post_W, post_seq;
 };
 
 // CTA-pair configuration: each CTA holds 128 rows of A and 128 of B's 256 per
@@ -403,6 +416,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
           if constexpr (EPI == EPI_BF16) {
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
+            if (p.scatter_idx) {
+              const int si = __ldg(p.scatter_idx + row);
+              if (si < 0) continue;
+              dst = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[si / p.scatter_rows]) +
+                    (int64_t)(si % p.scatter_rows) * p.ldd + col;
+            }
             if (p.bias) {
               float bb[32];
               load_bf16_row(p.bias + col, bb, nvalid, (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
@@ -573,8 +592,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 
   tc_fence_before();
+  if (p.post_ctr) __threadfence_system();  // this thread's (peer) stores before the flag
   if constexpr (CG == 2) cluster_sync();  // no remote arrive or pair MMA is still aimed at this CTA
   else __syncthreads();
+  if (p.post_ctr && threadIdx.x == 0) {
+    if (atomicAdd(p.post_ctr, 1) == (int)gridDim.x - 1) {
+      *p.post_ctr = 0;
+      __threadfence_system();
+      for (int i = 0; i < p.post_W; ++i) {
+        int* f = reinterpret_cast<int*>(p.post_pads[i]) + EP_FLAGS + p.post_kind * EP_MAXW + p.post_rank;
+        asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(p.post_seq) : "memory");
+      }
+    }
+  }
   if (warp == 1) {
     tc_fence_after();
     if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, TMEM_COLS);
@@ -743,14 +773,25 @@ inline int b_tile_rows(const GemmParams& p) { return p.cg == 2 ? PAIR_B_ROWS : B
 
 // Split K across CTAs when there are too few output tiles to fill the GPU
 // (weight-gradient GEMMs: small M x N, K = tokens).  Only valid for an
-// accumulating f32 output, whose epilogue adds with atomics.
+// accumulating f32 output, whose epilogue adds with atomics.  The split count
+// is chosen for wave fill over the units that run at once (CTAs, or clusters
+// for CTA pairs): the smallest count within 2 % of the best fill, at least 16
+// k-blocks per split.
 inline void choose_splits(GemmParams& p) {
   const int tiles = p.tiles_m * p.tiles_n;
   const int num_kb = (p.K + BK - 1) / BK;
-  const int sms = num_sms();
-  if (tiles >= 2 * sms || num_kb < 32) return;
-  int s = (2 * sms + tiles - 1) / tiles;
-  s = std::min(s, num_kb / 16);
+  const int slots = p.cg == 2 ? num_sms() / 2 : num_sms();
+  if (tiles >= 2 * slots || num_kb < 32) return;
+  const int smax = std::max(1, std::min(num_kb / 16, (4 * slots + tiles - 1) / tiles));
+  auto fill = [&](int s) {
+    const int64_t u = (int64_t)tiles * s;
+    const int64_t waves = (u + slots - 1) / slots;
+    return (double)u / (double)(waves * slots);
+  };
+  double best = 0.0;
+  for (int s = 1; s <= smax; ++s) best = std::max(best, fill(s));
+  int s = 1;
+  while (s < smax && fill(s) < best - 0.02) ++s;
   if (s <= 1) return;
   p.kb_per_split = (num_kb + s - 1) / s;
   p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;

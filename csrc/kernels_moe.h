@@ -14,9 +14,20 @@ void launch_moe_combine(const void* yp, const int* pos, const float* w, int64_t 
 void launch_moe_combine_bwd(const void* dy, const void* yp, const int* pos, const float* w, int64_t T, int k, int H,
                             void* dyp, float* dw, cudaStream_t st);
 void launch_moe_gather_sum(const void* dxp, const int* pos, int64_t T, int k, int H, void* dx, cudaStream_t st);
+// Optional for the bf16 epilogue of group-M: scatter output rows into peers'
+// buffers and post a flag when done (see GemmParams::scatter_idx / post_ctr).
+struct GroupedScatter {
+  const int* idx = nullptr;        // [rows] peer * rows_per_peer + row, or -1
+  const uint64_t* ptrs = nullptr;  // [W] destination buffers
+  int rows_per_peer = 0;
+  int* post_ctr = nullptr;
+  const uint64_t* post_pads = nullptr;
+  int post_kind = 0, post_rank = 0, post_W = 0, post_seq = 0;
+};
 void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& b, bool b_mn, int n_groups,
                          const int* seg_off, int64_t group_rows_b, void* out, int64_t ldo, void* out2, int64_t ldo2,
-                         const void* aux, int64_t ldaux, int* status, cudaStream_t st);
+                         const void* aux, int64_t ldaux, int* status, cudaStream_t st,
+                         const GroupedScatter* scatter = nullptr);
 // Router (router.cu): logits [T, E] (bf16 or f32, row stride ld) -> top-k
 // indices / weights [T, k], mean routing probability usage [E] (f32), and
 // optional per-expert selection counts [E].

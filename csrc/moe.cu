@@ -226,7 +226,8 @@ void launch_moe_gather_sum(const void* dxp, const int* pos, int64_t T, int k, in
 //      3 SwiGLU backward (out = dgu [rows, 2N], aux = gu).
 void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& b, bool b_mn, int n_groups,
                          const int* seg_off, int64_t group_rows_b, void* out, int64_t ldo, void* out2, int64_t ldo2,
-                         const void* aux, int64_t ldaux, int* status, cudaStream_t st) {
+                         const void* aux, int64_t ldaux, int* status, cudaStream_t st,
+                         const GroupedScatter* scatter) {
   Operand oa = op_of(a, a_mn), ob = op_of(b, b_mn);
   GemmParams p{};
   p.group_mode = mode;
@@ -261,6 +262,18 @@ void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& 
   CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
   p.D = out;
   p.ldd = ldo;
+  if (scatter) {
+    OXI_CHECK(mode == 1 && epi == 0 && scatter->rows_per_peer > 0, "row scatter: group-M bf16 epilogue only");
+    p.scatter_idx = scatter->idx;
+    p.scatter_ptrs = scatter->ptrs;
+    p.scatter_rows = scatter->rows_per_peer;
+    p.post_ctr = scatter->post_ctr;
+    p.post_pads = scatter->post_pads;
+    p.post_kind = scatter->post_kind;
+    p.post_rank = scatter->post_rank;
+    p.post_W = scatter->post_W;
+    p.post_seq = scatter->post_seq;
+  }
   switch (epi) {
     case 0:
       p.vec_ok = aligned16(out, ldo, 2);

@@ -403,8 +403,8 @@ std::vector<torch::Tensor> ep_counts(torch::Tensor local_counts, torch::Tensor p
 
 torch::Tensor ep_dispatch(torch::Tensor x, torch::Tensor topi, torch::Tensor topw, torch::Tensor all_counts,
                           int64_t rank, int64_t W, torch::Tensor cursor, torch::Tensor peers_xrecv,
-                          torch::Tensor peers_metaw, torch::Tensor done_ctr, torch::Tensor peer_pads, int64_t seq,
-                          torch::Tensor status) {
+                          torch::Tensor peers_metaw, torch::Tensor peers_srcidx, torch::Tensor done_ctr,
+                          torch::Tensor peer_pads, int64_t seq, torch::Tensor status) {
   c10::cuda::CUDAGuard g(x.device());
   TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [T, H]");
   TORCH_CHECK(topi.scalar_type() == torch::kInt64 && topi.is_contiguous() && topw.is_contiguous() &&
@@ -413,9 +413,16 @@ torch::Tensor ep_dispatch(torch::Tensor x, torch::Tensor topi, torch::Tensor top
   auto pos = torch::empty({T * k}, torch::TensorOptions().dtype(torch::kInt32).device(x.device()));
   oxi::launch_ep_dispatch(x.data_ptr(), x.stride(0), topi.data_ptr<int64_t>(), topw.data_ptr<float>(), T, (int)k,
                           (int)x.size(1), all_counts.data_ptr<int>(), (int)rank, (int)W, (int)E, cursor.data_ptr<int>(),
-                          u64p(peers_xrecv), u64p(peers_metaw), pos.data_ptr<int>(), done_ctr.data_ptr<int>(),
-                          u64p(peer_pads), (int)seq, status_ptr(status), stream());
+                          u64p(peers_xrecv), u64p(peers_metaw), u64p(peers_srcidx), pos.data_ptr<int>(),
+                          done_ctr.data_ptr<int>(), u64p(peer_pads), (int)seq, status_ptr(status), stream());
   return pos;
+}
+
+void ep_mark_pad(torch::Tensor seg_off, torch::Tensor recv_counts, torch::Tensor srcidx) {
+  c10::cuda::CUDAGuard g(srcidx.device());
+  TORCH_CHECK(srcidx.scalar_type() == torch::kInt32 && srcidx.is_contiguous(), "srcidx int32");
+  oxi::launch_ep_mark_pad(seg_off.data_ptr<int>(), recv_counts.data_ptr<int>(), (int)recv_counts.numel(),
+                          srcidx.data_ptr<int>(), stream());
 }
 
 void ep_wait(torch::Tensor my_pad, int64_t kind, int64_t W, int64_t seq, torch::Tensor status, int64_t wait_ns) {
@@ -428,54 +435,78 @@ void ep_signal(torch::Tensor peer_pads, int64_t kind, int64_t rank, int64_t W, i
   oxi::launch_ep_signal(u64p(peer_pads), (int)kind, (int)rank, (int)W, (int)seq, stream());
 }
 
-torch::Tensor ep_combine(torch::Tensor topi, torch::Tensor topw, torch::Tensor pos, int64_t El, int64_t H,
-                         torch::Tensor peers_yout, c10::optional<torch::Tensor> resid, torch::Tensor my_pad, int64_t W,
-                         int64_t seq, torch::Tensor status, int64_t wait_ns) {
-  c10::cuda::CUDAGuard g(topi.device());
-  const int64_t T = topi.size(0), k = topi.size(1);
-  auto y = torch::empty({T, H}, torch::TensorOptions().dtype(torch::kBFloat16).device(topi.device()));
+// Grouped expert GEMM (group-M, bf16) whose epilogue stores row r into row
+// srcidx[r] % rows_per_peer of peer srcidx[r] / rows_per_peer's buffer (P2P) and
+// whose last CTA posts flag `kind` to every peer.
+void ep_expert_gemm_scatter(torch::Tensor a, torch::Tensor b, bool b_mn, int64_t n_groups, torch::Tensor seg_off,
+                            int64_t group_rows_b, torch::Tensor srcidx, torch::Tensor peers_out, int64_t rows_per_peer,
+                            torch::Tensor post_ctr, torch::Tensor peer_pads, int64_t kind, int64_t rank, int64_t W,
+                            int64_t seq, torch::Tensor status) {
+  c10::cuda::CUDAGuard g(a.device());
+  Mat ma = bf16_mat(a, "a"), mb = bf16_mat(b, "b");
+  TORCH_CHECK(seg_off.scalar_type() == torch::kInt32 && seg_off.numel() == n_groups + 1, "seg_off");
+  TORCH_CHECK(srcidx.scalar_type() == torch::kInt32 && srcidx.numel() >= a.size(0), "srcidx int32 [rows]");
+  const int64_t N = b_mn ? b.size(1) : group_rows_b;
+  oxi::GroupedScatter sc;
+  sc.idx = srcidx.data_ptr<int>();
+  sc.ptrs = u64p(peers_out);
+  sc.rows_per_peer = (int)rows_per_peer;
+  sc.post_ctr = post_ctr.data_ptr<int>();
+  sc.post_pads = u64p(peer_pads);
+  sc.post_kind = (int)kind;
+  sc.post_rank = (int)rank;
+  sc.post_W = (int)W;
+  sc.post_seq = (int)seq;
+  // the destination rows are N wide and contiguous (row stride N)
+  oxi::launch_gemm_grouped(1, 0, ma, false, mb, b_mn, (int)n_groups, seg_off.data_ptr<int>(), group_rows_b, nullptr,
+                           N, nullptr, 0, nullptr, 0, status_ptr(status), stream(), &sc);
+}
+
+// wait for flag `wait_kind` from every owner, then out = (resid) + sum_j (w) * rows[t*k + j]
+torch::Tensor ep_sum_pairs(torch::Tensor rows, c10::optional<torch::Tensor> w, int64_t T, int64_t k,
+                           c10::optional<torch::Tensor> resid, torch::Tensor my_pad, int64_t wait_kind, int64_t W,
+                           int64_t seq, torch::Tensor status, int64_t wait_ns) {
+  c10::cuda::CUDAGuard g(rows.device());
+  TORCH_CHECK(rows.scalar_type() == torch::kBFloat16 && rows.is_contiguous() && rows.dim() == 2 &&
+                  rows.size(0) >= T * k, "rows bf16 [>= T*k, H]");
+  const int64_t H = rows.size(1);
+  auto out = torch::empty({T, H}, rows.options());
+  const float* wp = nullptr;
+  if (w.has_value() && w->defined()) {
+    TORCH_CHECK(w->scalar_type() == torch::kFloat32 && w->is_contiguous() && w->numel() == T * k, "w f32 [T, k]");
+    wp = w->data_ptr<float>();
+  }
   const void* rp = nullptr;
   if (resid.has_value() && resid->defined()) {
     TORCH_CHECK(resid->is_contiguous() && resid->numel() == T * H && resid->scalar_type() == torch::kBFloat16,
                 "resid bf16 [T, H] contiguous");
     rp = resid->data_ptr();
   }
-  oxi::launch_ep_combine(topi.data_ptr<int64_t>(), topw.data_ptr<float>(), pos.data_ptr<int>(), T, (int)k, (int)H,
-                         (int)El, u64p(peers_yout), rp, y.data_ptr(), my_pad.data_ptr<int>(), (int)W, (int)seq,
-                         status_ptr(status), wait_ns, stream());
-  return y;
+  oxi::launch_ep_sum_pairs(rows.data_ptr(), wp, T, (int)k, (int)H, rp, out.data_ptr(), my_pad.data_ptr<int>(),
+                           (int)wait_kind, (int)W, (int)seq, status_ptr(status), wait_ns, stream());
+  return out;
 }
 
-void ep_push_dy(torch::Tensor dy, torch::Tensor topi, torch::Tensor pos, int64_t El, torch::Tensor peers_dyrecv,
-                torch::Tensor done_ctr, torch::Tensor peer_pads, int64_t rank, int64_t W, int64_t seq,
-                torch::Tensor status) {
+torch::Tensor ep_push_dy(torch::Tensor dy, torch::Tensor topi, torch::Tensor pos, int64_t El,
+                         torch::Tensor peers_dyrecv, torch::Tensor yret, torch::Tensor done_ctr,
+                         torch::Tensor peer_pads, int64_t rank, int64_t W, int64_t seq, torch::Tensor status) {
   c10::cuda::CUDAGuard g(dy.device());
   TORCH_CHECK(dy.scalar_type() == torch::kBFloat16 && dy.is_contiguous(), "dy bf16 contiguous");
   const int64_t T = topi.size(0), k = topi.size(1);
+  TORCH_CHECK(yret.scalar_type() == torch::kBFloat16 && yret.is_contiguous() && yret.size(0) >= T * k &&
+                  yret.size(1) == dy.size(-1), "yret bf16 [>= T*k, H]");
+  auto dw = torch::empty({T, k}, torch::TensorOptions().dtype(torch::kFloat32).device(dy.device()));
   oxi::launch_ep_push_dy(dy.data_ptr(), topi.data_ptr<int64_t>(), pos.data_ptr<int>(), T, (int)k, (int)dy.size(-1),
-                         (int)El, u64p(peers_dyrecv), done_ctr.data_ptr<int>(), u64p(peer_pads), (int)rank, (int)W,
-                         (int)seq, status_ptr(status), stream());
+                         (int)El, u64p(peers_dyrecv), yret.data_ptr(), dw.data_ptr<float>(), done_ctr.data_ptr<int>(),
+                         u64p(peer_pads), (int)rank, (int)W, (int)seq, status_ptr(status), stream());
+  return dw;
 }
 
-void ep_scale_rows(torch::Tensor dyrecv, torch::Tensor yout, torch::Tensor metaw, torch::Tensor dwrow,
-                   torch::Tensor seg_off, torch::Tensor recv_counts, int64_t El) {
+void ep_scale_rows(torch::Tensor dyrecv, torch::Tensor metaw, torch::Tensor seg_off, torch::Tensor recv_counts,
+                   int64_t El) {
   c10::cuda::CUDAGuard g(dyrecv.device());
-  oxi::launch_ep_scale_rows(dyrecv.data_ptr(), yout.data_ptr(), metaw.data_ptr<float>(), dwrow.data_ptr<float>(),
-                            seg_off.data_ptr<int>(), recv_counts.data_ptr<int>(), (int)El, (int)dyrecv.size(1),
-                            dyrecv.size(0), stream());
-}
-
-std::vector<torch::Tensor> ep_gather(torch::Tensor topi, torch::Tensor pos, int64_t H, int64_t El,
-                                     torch::Tensor peers_dx, torch::Tensor peers_dwrow, torch::Tensor my_pad,
-                                     int64_t W, int64_t seq, torch::Tensor status, int64_t wait_ns) {
-  c10::cuda::CUDAGuard g(topi.device());
-  const int64_t T = topi.size(0), k = topi.size(1);
-  auto dx = torch::empty({T, H}, torch::TensorOptions().dtype(torch::kBFloat16).device(topi.device()));
-  auto dw = torch::empty({T, k}, torch::TensorOptions().dtype(torch::kFloat32).device(topi.device()));
-  oxi::launch_ep_gather(topi.data_ptr<int64_t>(), pos.data_ptr<int>(), T, (int)k, (int)H, (int)El, u64p(peers_dx),
-                        u64p(peers_dwrow), dx.data_ptr(), dw.data_ptr<float>(), my_pad.data_ptr<int>(), (int)W,
-                        (int)seq, status_ptr(status), wait_ns, stream());
-  return {dx, dw};
+  oxi::launch_ep_scale_rows(dyrecv.data_ptr(), metaw.data_ptr<float>(), seg_off.data_ptr<int>(),
+                            recv_counts.data_ptr<int>(), (int)El, (int)dyrecv.size(1), dyrecv.size(0), stream());
 }
 
 // ------------------------------------------------------------ NVLink microbenchmarks
@@ -1030,10 +1061,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch", &ep_dispatch, "expert-parallel token dispatch (P2P stores)");
   m.def("ep_wait", &ep_wait, "bounded wait for an expert-parallel flag from every peer");
   m.def("ep_signal", &ep_signal, "post an expert-parallel flag to every peer");
-  m.def("ep_combine", &ep_combine, "expert-parallel weighted combine (P2P loads) + residual");
-  m.def("ep_push_dy", &ep_push_dy, "expert-parallel backward: push output gradients to the owners");
-  m.def("ep_scale_rows", &ep_scale_rows, "owner side: routing-weight gradient and scaling of received rows");
-  m.def("ep_gather", &ep_gather, "expert-parallel backward: gather input gradients and weight gradients");
+  m.def("ep_mark_pad", &ep_mark_pad, "mark the padding rows of the expert segments (srcidx = -1)");
+  m.def("ep_expert_gemm_scatter", &ep_expert_gemm_scatter,
+        "grouped expert GEMM whose epilogue stores rows into the sources' buffers over NVLink, then posts a flag");
+  m.def("ep_sum_pairs", &ep_sum_pairs, "wait for the owners, then the local weighted sum of each token's k rows");
+  m.def("ep_push_dy", &ep_push_dy, "expert-parallel backward: push output gradients to the owners, routing-weight grads");
+  m.def("ep_scale_rows", &ep_scale_rows, "owner side: scale received gradient rows by their routing weights");
   m.def("enable_peer_access", &enable_peer_access, "cudaDeviceEnablePeerAccess(device -> peer)");
   m.def("p2p_read", &p2p_read, "microbenchmark: SM loads from (peer) memory");
   m.def("p2p_write", &p2p_write, "microbenchmark: SM stores to (peer) memory");

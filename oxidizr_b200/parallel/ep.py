@@ -100,7 +100,7 @@ class EPGroup:
         self.rank = dist.get_rank(group)
         self.pad = SymmetricBuffer(ext().ep_pad_words() * 4, self.device, group)
         self.pad_local = self.pad.local.view(torch.int32)
-        self.done = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.done = torch.zeros(4, dtype=torch.int32, device=self.device)  # last-CTA counters
         self.cursor = torch.zeros(256, dtype=torch.int32, device=self.device)
         t = timeout_s if timeout_s is not None else float(os.environ.get("OXI_PEER_TIMEOUT_S", 30.0))
         self.wait_ns = int(t * 1e9)
@@ -141,6 +141,21 @@ class EPLayerBuffers:
         self.grp, self.H = grp, H
         self.cap = 0
         self.bufs = None
+        self.pairs = 0
+        self.yret = None  # [T*k, H]: this rank's expert output rows, then their input gradients
+
+    def ensure_pairs(self, pairs: int):
+        """yret holds one row per (token, slot) of this rank; its size only changes with
+        the batch shape, identically on every rank (collective)."""
+        if pairs != self.pairs:
+            from .fused_ar import SymmetricBuffer
+            g = self.grp
+            torch.cuda.synchronize(g.device)
+            if self.yret is not None:
+                self.yret.close()
+                dist.barrier(group=g.group)
+            self.yret = SymmetricBuffer(pairs * self.H * 2, g.device, g.group)
+            self.pairs = pairs
 
     def ensure(self, rows: int, balanced_rows: int = 0):
         if rows <= self.cap:
@@ -159,9 +174,8 @@ class EPLayerBuffers:
         H = self.H
         self.bufs = {
             "xrecv": SymmetricBuffer(cap * H * 2, g.device, g.group),
-            "yout": SymmetricBuffer(cap * H * 2, g.device, g.group),
             "metaw": SymmetricBuffer(cap * 4, g.device, g.group),
-            "dwrow": SymmetricBuffer(cap * 4, g.device, g.group),
+            "srcidx": SymmetricBuffer(cap * 4, g.device, g.group),
         }
         self.bufs["dyrecv"] = g.shared_dyrecv(cap * H * 2)
         self.cap = cap
@@ -170,7 +184,7 @@ class EPLayerBuffers:
         t = self.bufs[name].local.view(dtype)
         if cols:
             return t[: self.cap * cols].view(self.cap, cols)
-        return t[: self.cap] if dtype == torch.float32 else t
+        return t[: self.cap] if dtype in (torch.float32, torch.int32) else t
 
     def table(self, name: str) -> torch.Tensor:
         return self.bufs[name].ptr_table
@@ -183,7 +197,12 @@ def _rows_needed(all_counts: torch.Tensor, W: int, El: int) -> int:
 
 
 class EPExperts(torch.autograd.Function):
-    """resid + sum_j topw[t, j] * SwiGLU_{topi[t, j]}(x_t), experts spread over the group (NVLink)."""
+    """resid + sum_j topw[t, j] * SwiGLU_{topi[t, j]}(x_t), experts spread over the group (NVLink).
+
+    The combine is fused into the owners' down-projection GEMM: its epilogue stores
+    every output row straight into the source rank's ``yret`` (P2P) as the tiles
+    finish, and its last CTA posts the flag; the source then sums its k rows per
+    token locally.  The backward does the same with the input-gradient rows."""
 
     @staticmethod
     def forward(ctx, x, topi, topw, counts, w_gu, w_down, resid, moe):
@@ -194,6 +213,7 @@ class EPExperts(torch.autograd.Function):
         T, H = x.shape
         El, I2, _ = w_gu.shape
         I = I2 // 2
+        k = topi.shape[1]
         W, rank = g.W, g.rank
         st = status(x.device)
         xc = x if x.stride(1) == 1 else x.contiguous()
@@ -203,21 +223,23 @@ class EPExperts(torch.autograd.Function):
         all_counts, seg, rc = e.ep_counts(counts.int().contiguous(), g.pad.ptr_table, g.pad_local, rank, W, seq, st,
                                           g.wait_ns)
         # every rank sees the same counts, so every rank takes the same (collective) decision
-        buf.ensure(_rows_needed(all_counts.cpu(), W, El), balanced_rows=T * topi.shape[1])
+        buf.ensure(_rows_needed(all_counts.cpu(), W, El), balanced_rows=T * k)
+        buf.ensure_pairs(T * k)
         cap = buf.cap
         xr = buf.local("xrecv", torch.bfloat16, H)
-        yo = buf.local("yout", torch.bfloat16, H)
         e.moe_zero_pad(seg, rc, xr)
+        e.ep_mark_pad(seg, rc, buf.local("srcidx", torch.int32))
         pos = e.ep_dispatch(xc, topi, tw, all_counts, rank, W, g.cursor, buf.table("xrecv"), buf.table("metaw"),
-                            g.done[0:1], g.pad.ptr_table, seq, st)
+                            buf.table("srcidx"), g.done[0:1], g.pad.ptr_table, seq, st)
         e.ep_wait(g.pad_local, K_DISPATCHED, W, seq, st, g.wait_ns)
         h = torch.empty(cap, I, dtype=x.dtype, device=x.device)
         gu = torch.empty(cap, I2, dtype=x.dtype, device=x.device)
         e.gemm_grouped(1, 2, xr, False, w_gu.view(El * I2, H), False, El, seg, I2, h, gu, None, st)
-        e.gemm_grouped(1, 0, h, False, w_down.view(El * H, I), False, El, seg, H, yo, None, None, st)
-        e.ep_signal(g.pad.ptr_table, K_YREADY, rank, W, seq)
-        y = e.ep_combine(topi, tw, pos, El, H, buf.table("yout"), resid.contiguous() if resid is not None else None,
-                         g.pad_local, W, seq, st, g.wait_ns)
+        e.ep_expert_gemm_scatter(h, w_down.view(El * H, I), False, El, seg, H, buf.local("srcidx", torch.int32),
+                                 buf.yret.ptr_table, T * k, g.done[2:3], g.pad.ptr_table, K_YREADY, rank, W, seq, st)
+        yret = buf.yret.local.view(torch.bfloat16).view(T * k, H)
+        y = e.ep_sum_pairs(yret, tw, T, k, resid.contiguous() if resid is not None else None, g.pad_local, K_YREADY,
+                           W, seq, st, g.wait_ns)
         ctx.save_for_backward(topi, tw, pos, h, gu, seg, rc)
         ctx.moe, ctx.w_gu, ctx.w_down, ctx.has_resid = moe, w_gu, w_down, resid is not None
         return y
@@ -234,25 +256,28 @@ class EPExperts(torch.autograd.Function):
         w_gu, w_down = ctx.w_gu, ctx.w_down
         El, I2, H = w_gu.shape
         I = I2 // 2
+        T, k = topi.shape
         W, rank = g.W, g.rank
         st = status(dy.device)
         dy = dy.contiguous()
         seq = g.next_seq()
         xr = buf.local("xrecv", torch.bfloat16, H)
-        yo = buf.local("yout", torch.bfloat16, H)
         dyr = buf.local("dyrecv", torch.bfloat16, H)
-        e.ep_push_dy(dy, topi, pos, El, buf.table("dyrecv"), g.done[1:2], g.pad.ptr_table, rank, W, seq, st)
+        yret = buf.yret.local.view(torch.bfloat16).view(T * k, H)
+        # dy rows to the owners; d topw from this rank's copy of the expert outputs
+        dtw = e.ep_push_dy(dy, topi, pos, El, buf.table("dyrecv"), yret, g.done[1:2], g.pad.ptr_table, rank, W, seq,
+                           st)
         e.ep_wait(g.pad_local, K_DYPUSHED, W, seq, st, g.wait_ns)
-        e.ep_scale_rows(dyr, yo, buf.local("metaw", torch.float32), buf.local("dwrow", torch.float32), seg, rc, El)
+        e.ep_scale_rows(dyr, buf.local("metaw", torch.float32), seg, rc, El)
         g_down = _wgrad_grouped(w_down, dyr, h, seg, El)
         dgu = torch.empty_like(gu)
         e.gemm_grouped(1, 3, dyr, False, w_down.view(El * H, I), True, El, seg, H, dgu, None, gu, st)
         g_gu = _wgrad_grouped(w_gu, dgu, xr, seg, El)
-        # the gradient of the received rows overwrites yout (consumed above)
-        e.gemm_grouped(1, 0, dgu, False, w_gu.view(El * I2, H), True, El, seg, I2, yo, None, None, st)
-        e.ep_signal(g.pad.ptr_table, K_DXREADY, rank, W, seq)
-        dx, dtw = e.ep_gather(topi, pos, H, El, buf.table("yout"), buf.table("dwrow"), g.pad_local, W, seq, st,
-                              g.wait_ns)
+        # input-gradient rows straight into the sources' yret (their forward rows were
+        # consumed by their push_dy, which finished before DYPUSHED)
+        e.ep_expert_gemm_scatter(dgu, w_gu.view(El * I2, H), True, El, seg, I2, buf.local("srcidx", torch.int32),
+                                 buf.yret.ptr_table, T * k, g.done[3:4], g.pad.ptr_table, K_DXREADY, rank, W, seq, st)
+        dx = e.ep_sum_pairs(yret, None, T, k, None, g.pad_local, K_DXREADY, W, seq, st, g.wait_ns)
         return dx, None, dtw, None, g_gu, g_down, (dy if ctx.has_resid else None), None
 
 
