@@ -167,9 +167,8 @@ class EPLayerBuffers:
         EPLayerBuffers.reallocs += 1
         torch.cuda.synchronize(g.device)
         if self.bufs is not None:
-            for name, b in self.bufs.items():
-                if name != "dyrecv":  # the group's shared buffer
-                    b.close()
+            for b in self.bufs.values():
+                b.close()
             dist.barrier(group=g.group)
         H = self.H
         self.bufs = {
@@ -177,17 +176,20 @@ class EPLayerBuffers:
             "metaw": SymmetricBuffer(cap * 4, g.device, g.group),
             "srcidx": SymmetricBuffer(cap * 4, g.device, g.group),
         }
-        self.bufs["dyrecv"] = g.shared_dyrecv(cap * H * 2)
+        g.shared_dyrecv(cap * H * 2)  # looked up at use time: a later growth replaces it
         self.cap = cap
 
+    def _buf(self, name: str):
+        return self.grp.dyrecv if name == "dyrecv" else self.bufs[name]
+
     def local(self, name: str, dtype, cols: int = 0) -> torch.Tensor:
-        t = self.bufs[name].local.view(dtype)
+        t = self._buf(name).local.view(dtype)
         if cols:
             return t[: self.cap * cols].view(self.cap, cols)
         return t[: self.cap] if dtype in (torch.float32, torch.int32) else t
 
     def table(self, name: str) -> torch.Tensor:
-        return self.bufs[name].ptr_table
+        return self._buf(name).ptr_table
 
 
 def _rows_needed(all_counts: torch.Tensor, W: int, El: int) -> int:

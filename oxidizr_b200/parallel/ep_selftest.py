@@ -38,6 +38,8 @@ def main(argv=None):
     ap.add_argument("--hidden", type=int, default=256)
     ap.add_argument("--inter", type=int, default=128)
     ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--two-layers", action="store_true",
+                    help="a second MoE layer on the same group with twice the tokens (grows shared buffers)")
     ap.add_argument("--out", default=None)
     args = ap.parse_args(argv)
     os.environ["OXI_EP_BACKEND"] = args.backend
@@ -67,32 +69,49 @@ def main(argv=None):
     gen_dev = dev
     sharded.reset_parameters(0.05, torch.Generator(device=gen_dev).manual_seed(11))
     whole.reset_parameters(0.05, torch.Generator(device=gen_dev).manual_seed(11))
+    pairs = [(sharded, whole, args.tokens)]
+    if args.two_layers:
+        sb = MoE(cfg, dev, dtype, ep_group=dist.group.WORLD)
+        wb = MoE(cfg, dev, dtype, ep_group=None)
+        sb.reset_parameters(0.05, torch.Generator(device=gen_dev).manual_seed(12))
+        wb.reset_parameters(0.05, torch.Generator(device=gen_dev).manual_seed(12))
+        pairs.append((sb, wb, 2 * args.tokens))
     El = args.experts // world
     lo = rank * El
     assert torch.equal(sharded.w_gu.detach(), whole.w_gu.detach()[lo:lo + El])
     g = torch.Generator(device="cpu").manual_seed(100 + rank)
     for step in range(args.steps):
-        for m in (sharded, whole):
-            for p in m.parameters():
-                p.grad = None
-        x = (torch.randn(1, args.tokens, args.hidden, generator=g)).to(dev, dtype)
-        resid = (torch.randn(1, args.tokens, args.hidden, generator=g)).to(dev, dtype)
-        dy = (torch.randn(1, args.tokens, args.hidden, generator=g)).to(dev, dtype)
-        xs = x.clone().requires_grad_()
-        xw = x.clone().requires_grad_()
-        ys, aux_s = sharded(xs, resid)
-        yw, aux_w = whole(xw, resid)
-        (ys.float() * dy.float()).sum().add(aux_s).backward()
-        (yw.float() * dy.float()).sum().add(aux_w).backward()
-        e = {"y": _rel(ys, yw), "dx": _rel(xs.grad, xw.grad), "router": _rel(sharded.router.grad, whole.router.grad)}
-        for name in ("w_gu", "w_down"):
-            full = getattr(whole, name).grad.float().clone()
-            dist.all_reduce(full)
-            e[name] = _rel(getattr(sharded, name).grad, full[lo:lo + El])
-        t = torch.tensor([max(e.values())], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e["max_over_ranks"] = float(t)
-        errs.append(e)
+        for sh, wh, _ in pairs:
+            for m in (sh, wh):
+                for p in m.parameters():
+                    p.grad = None
+        outs = []
+        loss_s, loss_w = 0.0, 0.0
+        # every layer's forward first, then one backward: the layers' exchanges
+        # interleave the way they do in a model
+        for sh, wh, ntok in pairs:
+            x = (torch.randn(1, ntok, args.hidden, generator=g)).to(dev, dtype)
+            resid = (torch.randn(1, ntok, args.hidden, generator=g)).to(dev, dtype)
+            dy = (torch.randn(1, ntok, args.hidden, generator=g)).to(dev, dtype)
+            xs = x.clone().requires_grad_()
+            xw = x.clone().requires_grad_()
+            ys, aux_s = sh(xs, resid)
+            yw, aux_w = wh(xw, resid)
+            loss_s = loss_s + (ys.float() * dy.float()).sum() + aux_s
+            loss_w = loss_w + (yw.float() * dy.float()).sum() + aux_w
+            outs.append((sh, wh, xs, xw, ys, yw))
+        loss_s.backward()
+        loss_w.backward()
+        for sh, wh, xs, xw, ys, yw in outs:
+            e = {"y": _rel(ys, yw), "dx": _rel(xs.grad, xw.grad), "router": _rel(sh.router.grad, wh.router.grad)}
+            for name in ("w_gu", "w_down"):
+                full = getattr(wh, name).grad.float().clone()
+                dist.all_reduce(full)
+                e[name] = _rel(getattr(sh, name).grad, full[lo:lo + El])
+            t = torch.tensor([max(e.values())], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e["max_over_ranks"] = float(t)
+            errs.append(e)
     if args.device == "cuda":
         from ..ops._C import check_status
         torch.cuda.synchronize()

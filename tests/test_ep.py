@@ -41,13 +41,15 @@ def test_ep_gloo_matches_whole_layer(tmp_path):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("backend", ["nvlink", "nccl"])
-@pytest.mark.parametrize("shape", [("300", "8", "2", "256", "128"), ("1000", "16", "4", "512", "256")])
+@pytest.mark.parametrize("shape", [("300", "8", "2", "256", "128", ""), ("1000", "16", "4", "512", "256", ""),
+                                   ("700", "16", "4", "512", "256", "--two-layers")])
 def test_ep_gpu_matches_whole_layer(tmp_path, backend, shape):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    T, E, k, H, I = shape
+    T, E, k, H, I, extra = shape
     res = _run(tmp_path, "cuda", backend,
-               extra=("--tokens", T, "--experts", E, "--topk", k, "--hidden", H, "--inter", I))
+               extra=("--tokens", T, "--experts", E, "--topk", k, "--hidden", H, "--inter", I)
+               + ((extra,) if extra else ()))
     for e in res["errors"]:
         assert e["y"] < 2e-2 and e["dx"] < 3e-2 and e["router"] < 5e-2, e
         assert e["w_gu"] < 3e-2 and e["w_down"] < 3e-2, e
