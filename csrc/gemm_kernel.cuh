@@ -160,6 +160,20 @@ __device__ __forceinline__ Unit unit_info(int t, const GemmParams& p, int num_kb
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
 
 // ------------------------------------------------------------------ stores
+// 32 values -> bf16 at a 32-byte aligned address with two 32-byte stores (used
+// for rows that go to another GPU: full-sector NVLink writes instead of 16-byte ones)
+__device__ __forceinline__ void store_bf16_row32b(__nv_bfloat16* dst, const float* v) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = pack_bf16(v[q * 16 + 2 * i], v[q * 16 + 2 * i + 1]);
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst + q * 16), "r"(w[0]), "r"(w[1]),
+                 "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+  }
+}
+
 __device__ __forceinline__ void store_bf16_row(__nv_bfloat16* dst, const float* v, int ncols_valid, bool vec) {
   if (vec && ncols_valid >= 32) {
     uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -421,6 +435,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               if (si < 0) continue;
               dst = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[si / p.scatter_rows]) +
                     (int64_t)(si % p.scatter_rows) * p.ldd + col;
+              if (vec && nvalid >= 32 && (reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+                store_bf16_row32b(dst, v);
+                continue;
+              }
             }
             if (p.bias) {
               float bb[32];
