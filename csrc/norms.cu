@@ -217,15 +217,107 @@ __global__ void norm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv
   }
 }
 
-int norm_grid(int64_t rows) {
+// Backward with a CTA per row (H / 8 threads, thread t owns columns 8t..8t+7):
+// x, dy (and gate) are loaded once and kept in registers across the two
+// reductions; the weight-gradient partials stay per thread (the same columns
+// for every row of this CTA) and are added with one atomic per column at the end.
+template <int MODE>
+__global__ void __launch_bounds__(512) norm_bwd_row_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ gate,
+    const void* __restrict__ w, int wf32, const float* __restrict__ stat_rstd, const float* __restrict__ stat_mean,
+    const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dgate,
+    float* __restrict__ dw, float* __restrict__ db, int64_t rows, int H) {
+  __shared__ float red[2][2][16];  // [row parity][a1 | a2][warp]
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
+  const int c0 = t * 8;
+  float wv[8], pdw[8], pdb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    wv[j] = ldw(w, wf32, c0 + j);
+    pdw[j] = 0.f;
+    pdb[j] = 0.f;
+  }
+  const float inv_h = 1.f / (float)H;
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+    const float rstd = stat_rstd[row];
+    const float mean = MODE == 1 ? stat_mean[row] : 0.f;
+    float xv[8], dv[8], g[8], xh[8];
+    ld8(x + row * H + c0, xv);
+    ld8(dy + row * H + c0, dv);
+    if (MODE == 2) ld8(gate + row * H + c0, g);
+    float a1 = 0.f, a2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float xin = MODE == 2 ? xv[j] * (g[j] / (1.f + __expf(-g[j]))) : xv[j];
+      xh[j] = (xin - mean) * rstd;
+      const float wd = dv[j] * wv[j];
+      pdw[j] += dv[j] * xh[j];
+      if (MODE == 1) pdb[j] += dv[j];
+      a1 += wd;
+      a2 += wd * xh[j];
+    }
+    a1 = warp_sum(a1);
+    a2 = warp_sum(a2);
+    float(*rb)[16] = red[it & 1];
+    if (lane == 0) {
+      rb[0][wid] = a1;
+      rb[1][wid] = a2;
+    }
+    __syncthreads();
+    a1 = 0.f;
+    a2 = 0.f;
+    for (int i = 0; i < nw; ++i) {
+      a1 += rb[0][i];
+      a2 += rb[1][i];
+    }
+    a1 *= inv_h;
+    a2 *= inv_h;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float wd = dv[j] * wv[j];
+      o[j] = (MODE == 1) ? rstd * (wd - a1 - xh[j] * a2) : rstd * (wd - xh[j] * a2);
+    }
+    if (MODE == 2) {
+      float dg[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float sg = 1.f / (1.f + __expf(-g[j]));
+        const float dh = o[j];
+        o[j] = dh * g[j] * sg;
+        dg[j] = dh * xv[j] * sg * (1.f + g[j] * (1.f - sg));
+      }
+      st8(dgate + row * H + c0, dg);
+    }
+    if (dres) {
+      float r[8];
+      ld8(dres + row * H + c0, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] += r[j];
+    }
+    st8(dx + row * H + c0, o);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    atomicAdd(&dw[c0 + j], pdw[j]);
+    if (MODE == 1) atomicAdd(&db[c0 + j], pdb[j]);
+  }
+}
+
+int num_sms_norm() {
   static int sms = 0;
   if (!sms) {
     int dev;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
+  return sms;
+}
+
+int norm_grid(int64_t rows) {
   int64_t need = (rows + NW - 1) / NW;
-  return (int)std::min<int64_t>(need, (int64_t)sms * 4);
+  return (int)std::min<int64_t>(need, (int64_t)num_sms_norm() * 4);
 }
 
 }  // namespace
@@ -254,6 +346,25 @@ void launch_norm_bwd(int mode, const void* dy, const void* x, const void* gate, 
                      float* db, int64_t rows, int H, cudaStream_t st) {
   OXI_CHECK(H % 8 == 0 && H <= 32 * 8 * MAXV, "norm: hidden must be a multiple of 8 and <= 4096");
   if (rows == 0) return;
+  if (H % 256 == 0 && H <= 4096) {
+    // CTA per row: H / 8 threads; enough CTAs for every SM to hold 2048 threads
+    const int threads = H / 8;
+    const int grid = (int)std::min<int64_t>(rows, (int64_t)num_sms_norm() * (2048 / threads));
+    auto DY_ = reinterpret_cast<const __nv_bfloat16*>(dy);
+    auto X_ = reinterpret_cast<const __nv_bfloat16*>(x);
+    auto G_ = reinterpret_cast<const __nv_bfloat16*>(gate);
+    auto DR_ = reinterpret_cast<const __nv_bfloat16*>(dres);
+    auto DX_ = reinterpret_cast<__nv_bfloat16*>(dx);
+    auto DG_ = reinterpret_cast<__nv_bfloat16*>(dgate);
+    if (mode == 0)
+      norm_bwd_row_kernel<0><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, rows, H);
+    else if (mode == 1)
+      norm_bwd_row_kernel<1><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, rows, H);
+    else
+      norm_bwd_row_kernel<2><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, rows, H);
+    OXI_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int grid = norm_grid(rows);
   const size_t smem = 2 * H * sizeof(float);
   auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);

@@ -11,7 +11,7 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("mode", [0, 1, 2])
-@pytest.mark.parametrize("H", [256, 2048, 1536, 4096])
+@pytest.mark.parametrize("H", [256, 2048, 1536, 4096, 520])
 def test_norms_fwd_bwd(mode, H):
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops.fused import Norm
