@@ -33,6 +33,10 @@ namespace oxi {
 namespace {
 
 constexpr int FA_BM = 128, FA_BN = 128;
+// Forward key tile: 64 keys, so that a CTA needs 256 TMEM columns (two S tiles +
+// O) and about 100 KB of shared memory, and two CTAs share an SM: one CTA's
+// softmax overlaps the other's MMAs and its prologue/epilogue the other's loop.
+constexpr int FA_BNF = 64;
 constexpr int FA_THREADS = 320;      // TMA warp, MMA warp, 8 softmax/epilogue warps
 constexpr int FA_BWD_THREADS = 320;  // TMA warp, MMA warp, 8 softmax/epilogue warps
 
@@ -51,17 +55,17 @@ struct FaSmem {
   static constexpr int KBQ = (DQ + 63) / 64;  // 64-column blocks of a q/k row
   static constexpr int KBV = DV / 64;         // 64-column blocks of a v row
   static constexpr int Q_BYTES = FA_BM * KBQ * 128;
-  static constexpr int K_BYTES = FA_BN * KBQ * 128;
-  static constexpr int V_BYTES = FA_BN * KBV * 128;
-  static constexpr int KST = 3;                 // K stages: K_j is freed as soon as S_j is done
-  static constexpr int VST = DV <= 64 ? 3 : 2;  // V stages: V_j is freed after PV_j
+  static constexpr int K_BYTES = FA_BNF * KBQ * 128;
+  static constexpr int V_BYTES = FA_BNF * KBV * 128;
+  static constexpr int KST = 2;  // K stages: K_j is freed as soon as S_j is done
+  static constexpr int VST = 2;  // V stages: V_j is freed after PV_j
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + KST * K_BYTES;
   static constexpr int OFF_RED = OFF_V + VST * V_BYTES;  // row-max exchange [2][2][128] + row sums [2][128]
   static constexpr int OFF_BAR = OFF_RED + 768 * 4;
   static constexpr int TOTAL = OFF_BAR + 256 + 1024;
-  static_assert(TOTAL <= 232448, "shared memory budget");
+  static_assert(2 * (TOTAL + 1024) <= 233472, "two CTAs per SM");
 };
 
 // UMMA descriptor of the kk-th K=16 slice of a K-major SW128 tile whose K
@@ -71,7 +75,7 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, uint32_t 
 }
 
 template <int DQ, int DV>
-__global__ void __launch_bounds__(FA_THREADS, 1)
+__global__ void __launch_bounds__(FA_THREADS, 2)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, FaParams p) {
   using L = FaSmem<DQ, DV>;
@@ -99,8 +103,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const int hk = h / (p.Hq / p.Hk);
   const int q0 = qt * FA_BM;
   const int row0 = b * p.S;
-  const int n_kt_all = (p.S + FA_BN - 1) / FA_BN;
-  const int nk = p.causal ? min(n_kt_all, (q0 + FA_BM - 1) / FA_BN + 1) : n_kt_all;
+  const int n_kt_all = (p.S + FA_BNF - 1) / FA_BNF;
+  const int nk = p.causal ? min(n_kt_all, (q0 + FA_BM - 1) / FA_BNF + 1) : n_kt_all;
   constexpr int KBQ = L::KBQ, KBV = L::KBV;
 
   if (threadIdx.x == 0) {
@@ -121,14 +125,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     tma_prefetch_desc(&tmV);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t TM_S0 = tmem, TM_O = tmem + 2 * FA_BN;
+  const uint32_t TM_S0 = tmem, TM_O = tmem + 2 * FA_BNF;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -145,8 +149,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         mbar_arrive_expect_tx(&k_full[ks], L::K_BYTES);
 #pragma unroll
         for (int kb = 0; kb < KBQ; ++kb)
-          tma_load_2d(sK + ks * L::K_BYTES + kb * FA_BN * 128, &tmK, &k_full[ks], hk * DQ + kb * 64,
-                      row0 + j * FA_BN);
+          tma_load_2d(sK + ks * L::K_BYTES + kb * FA_BNF * 128, &tmK, &k_full[ks], hk * DQ + kb * 64,
+                      row0 + j * FA_BNF);
         // issue every V load whose stage is already free (never more than one behind K)
         while (jv <= j) {
           const int vs = jv % L::VST, vu = jv / L::VST;
@@ -155,8 +159,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           mbar_arrive_expect_tx(&v_full[vs], L::V_BYTES);
 #pragma unroll
           for (int kb = 0; kb < KBV; ++kb)
-            tma_load_2d(sV + vs * L::V_BYTES + kb * FA_BN * 128, &tmV, &v_full[vs], hk * DV + kb * 64,
-                        row0 + jv * FA_BN);
+            tma_load_2d(sV + vs * L::V_BYTES + kb * FA_BNF * 128, &tmV, &v_full[vs], hk * DV + kb * 64,
+                        row0 + jv * FA_BNF);
           ++jv;
         }
       }
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = umma_idesc_bf16(FA_BM, FA_BN, false, false);
+      constexpr uint32_t IDESC_S = umma_idesc_bf16(FA_BM, FA_BNF, false, false);
       constexpr uint32_t IDESC_O = umma_idesc_bf16(FA_BM, DV, false, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status);
       const uint32_t aQ = smem_u32(sQ);
@@ -181,7 +185,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         const uint32_t aK = smem_u32(sK + ks * L::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < DQ / 16; ++kk)
-          tc_mma_f16(TM_S0 + st * FA_BN, kmajor_desc(aQ, kk, FA_BM * 128), kmajor_desc(aK, kk, FA_BN * 128),
+          tc_mma_f16(TM_S0 + st * FA_BNF, kmajor_desc(aQ, kk, FA_BM * 128), kmajor_desc(aK, kk, FA_BNF * 128),
                      IDESC_S, kk != 0);
         tc_commit(&s_full[st]);
         tc_commit(&k_empty[ks]);
@@ -194,11 +198,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         const int vs = j % L::VST, vu = j / L::VST;
         if (!mbar_wait(&v_full[vs], vu & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t tP = TM_S0 + (j & 1) * FA_BN;  // P_j: bf16 pairs in S_j's first 64 columns
+        const uint32_t tP = TM_S0 + (j & 1) * FA_BNF;  // P_j: bf16 pairs in S_j's first half
         const uint32_t aV = smem_u32(sV + vs * L::V_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < FA_BN / 16; ++kk)
-          tc_mma_f16_ts(TM_O, tP + kk * 8, umma_desc_sw128(aV + kk * 2048, FA_BN * 128, 1024), IDESC_O,
+        for (int kk = 0; kk < FA_BNF / 16; ++kk)
+          tc_mma_f16_ts(TM_O, tP + kk * 8, umma_desc_sw128(aV + kk * 2048, FA_BNF * 128, 1024), IDESC_O,
                         (j | kk) != 0);
         tc_commit(pv_done);
         tc_commit(&v_empty[vs]);
@@ -230,19 +234,21 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       }
       tc_fence_after();
       // Masking is branch-free: keys past `lim` (causal diagonal or sequence end) become -inf.
-      const int k0 = j * FA_BN + half * 64;
-      const bool need_mask = (p.causal && k0 + 63 > q0) || (k0 + 64 > p.S);
+      constexpr int KPT = FA_BNF / 2;   // keys per thread (the two halves split a tile)
+      constexpr int NCH = KPT / 32;     // 32-key TMEM chunks per thread
+      const int k0 = j * FA_BNF + half * KPT;
+      const bool need_mask = (p.causal && k0 + KPT - 1 > q0) || (k0 + KPT > p.S);
       const int lim = p.causal ? min(qpos, p.S - 1) : p.S - 1;
-      const uint32_t s_base = TM_S0 + st * FA_BN + lane_base;
-      uint32_t rr[2][32];
-      tmem_ld32(s_base + half * 64, rr[0]);
-      tmem_ld32(s_base + half * 64 + 32, rr[1]);
+      const uint32_t s_base = TM_S0 + st * FA_BNF + lane_base;
+      uint32_t rr[NCH][32];
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) tmem_ld32(s_base + half * KPT + c * 32, rr[c]);
       tc_wait_ld();
       float mx[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) mx[q] = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < NCH; ++c) {
         const int kc = k0 + c * 32;
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
       for (int q = 0; q < 8; ++q) rsa[q] = 0.f;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < NCH; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
@@ -301,8 +307,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           rsa[(t >> 1) & 7] += a + bb;
           pk[t / 2] = pack_bf16(a, bb);
         }
-        // keys 64 half + 32c .. +31 -> P columns 32 half + 16c .. +15
-        tmem_st16(s_base + half * 32 + c * 16, pk);
+        // keys KPT half + 32c .. +31 -> P columns KPT/2 half + 16c .. +15
+        tmem_st16(s_base + half * (KPT / 2) + c * 16, pk);
       }
       const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
       l = l * alpha + rs;
@@ -346,7 +352,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -357,8 +363,8 @@ void launch_fa_fwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   using L = FaSmem<DQ, DV>;
   const int64_t T = (int64_t)B * S;
   CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * DQ, ldq, 64, FA_BM);
-  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * DQ, ldk, 64, FA_BN);
-  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * DV, ldv, 64, FA_BN);
+  CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * DQ, ldk, 64, FA_BNF);
+  CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * DV, ldv, 64, FA_BNF);
   FaParams p;
   p.B = B; p.S = S; p.Hq = Hq; p.Hk = Hk;
   p.scale_log2 = scale * 1.4426950408889634f;
