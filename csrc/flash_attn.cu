@@ -715,25 +715,36 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
 }
 
 // delta[b, h, s] = sum_d dO * O  (one warp per (token, head) row)
+// delta[b, h, s] = <dO_row, O_row>: D / 8 threads per row, 16-byte loads,
+// shuffle reduction within the row's lane group (D in {64, 96, 128, ...}, D / 8
+// a power of two up to 32 -> groups never straddle a warp).
 __global__ void fa_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, int64_t ldo,
                                    const __nv_bfloat16* __restrict__ dout, int64_t lddo, float* __restrict__ delta,
                                    int B, int S, int Hq, int D) {
-  const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
+  const int per = D / 8;  // threads per row
+  const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t w = gt / per;
+  const int sub = (int)(gt % per);
   const int64_t rows = (int64_t)B * S * Hq;
-  if (w >= rows) return;
-  const int64_t t = w / Hq;
-  const int h = (int)(w % Hq);
-  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(o + t * ldo + (int64_t)h * D);
-  const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(dout + t * lddo + (int64_t)h * D);
+  const bool live = w < rows;
   float s = 0.f;
-  for (int i = lane; i < D / 2; i += 32) {
-    const float2 x = __bfloat1622float2(a[i]), y = __bfloat1622float2(g[i]);
-    s += x.x * y.x + x.y * y.y;
-  }
+  int64_t t = 0;
+  int h = 0;
+  if (live) {
+    t = w / Hq;
+    h = (int)(w % Hq);
+    const uint4 ua = *reinterpret_cast<const uint4*>(o + t * ldo + (int64_t)h * D + sub * 8);
+    const uint4 ug = *reinterpret_cast<const uint4*>(dout + t * lddo + (int64_t)h * D + sub * 8);
+    const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&ua);
+    const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&ug);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) {
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = __bfloat1622float2(a[i]), y = __bfloat1622float2(g[i]);
+      s += x.x * y.x + x.y * y.y;
+    }
+  }
+  for (int off = per / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (live && sub == 0) {
     const int b = (int)(t / S), sp = (int)(t % S);
     delta[((int64_t)b * Hq + h) * S + sp] = s;
   }
@@ -829,7 +840,9 @@ void launch_fa_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const
   if (B == 0 || S == 0) return;
   const int64_t T = (int64_t)B * S;
   const int64_t rows = T * Hq;
-  fa_bwd_prep_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+  OXI_CHECK(Dv % 8 == 0 && (Dv / 8) <= 32 && ((Dv / 8) & (Dv / 8 - 1)) == 0 && ldo % 8 == 0 && lddo % 8 == 0,
+            "flash backward prep: v head dim / 8 must be a power of two <= 32");
+  fa_bwd_prep_kernel<<<(unsigned)((rows * (Dv / 8) + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(o), ldo, reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B,
       S, Hq, Dv);
   OXI_CUDA_CHECK(cudaGetLastError());

@@ -8,9 +8,12 @@ namespace oxi {
 // mode: 0 RMSNorm, 1 LayerNorm, 2 gated RMSNorm (rmsnorm(x * silu(gate)))
 void launch_norm_fwd(int mode, const void* x, const void* gate, const void* w, bool wf32, const void* b, void* y,
                      float* rstd, float* mean, int64_t rows, int H, float eps, cudaStream_t st);
+// part (nullable): f32 scratch [part_rows, 2H] for per-CTA weight-gradient partials
+// (part_rows >= norm_bwd_partial_rows(rows, H)); without it the CTAs add with atomics.
 void launch_norm_bwd(int mode, const void* dy, const void* x, const void* gate, const void* w, bool wf32,
                      const float* rstd, const float* mean, const void* dres, void* dx, void* dgate, float* dw,
-                     float* db, int64_t rows, int H, cudaStream_t st);
+                     float* db, int64_t rows, int H, cudaStream_t st, float* part = nullptr, int part_rows = 0);
+int norm_bwd_partial_rows(int64_t rows, int H);
 
 void launch_ce_finish(const float* pmax, const float* psum, int nt, const float* tgt_logit, const int64_t* targets,
                       float* lse, float* loss, int64_t rows, cudaStream_t st);

@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(512) norm_bwd_row_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ gate,
     const void* __restrict__ w, int wf32, const float* __restrict__ stat_rstd, const float* __restrict__ stat_mean,
     const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dgate,
-    float* __restrict__ dw, float* __restrict__ db, int64_t rows, int H) {
+    float* __restrict__ dw, float* __restrict__ db, float* __restrict__ part, int64_t rows, int H) {
   __shared__ float red[2][2][16];  // [row parity][a1 | a2][warp]
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
   const int c0 = t * 8;
@@ -298,11 +298,35 @@ __global__ void __launch_bounds__(512) norm_bwd_row_kernel(
     }
     st8(dx + row * H + c0, o);
   }
+  if (part) {
+    // per-CTA partials [gridDim.x][2H], summed over CTAs by norm_part_sum_kernel
+    float* pw = part + (int64_t)blockIdx.x * 2 * H;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      pw[c0 + j] = pdw[j];
+      if (MODE == 1) pw[H + c0 + j] = pdb[j];
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     atomicAdd(&dw[c0 + j], pdw[j]);
     if (MODE == 1) atomicAdd(&db[c0 + j], pdb[j]);
   }
+}
+
+// dw[c] += sum_g part[g][c] (and db from the second half): one thread per column,
+// the only writer of its column, so no atomics (thousands of CTAs adding into the
+// same H addresses serialise in L2)
+__global__ void norm_part_sum_kernel(const float* __restrict__ part, int G, int H, float* __restrict__ dw,
+                                     float* __restrict__ db) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int width = db ? 2 * H : H;
+  if (c >= width) return;
+  float s = 0.f;
+  for (int g = 0; g < G; ++g) s += part[(int64_t)g * 2 * H + c];
+  if (c < H) dw[c] += s;
+  else db[c - H] += s;
 }
 
 int num_sms_norm() {
@@ -314,6 +338,16 @@ int num_sms_norm() {
   }
   return sms;
 }
+
+}  // namespace
+
+// CTAs of the row-per-CTA norm backward (rows of its weight-gradient partials)
+int norm_bwd_partial_rows(int64_t rows, int H) {
+  if (H % 256 != 0 || H > 4096) return 0;
+  return (int)std::min<int64_t>(rows, (int64_t)num_sms_norm() * (2048 / (H / 8)));
+}
+
+namespace {
 
 int norm_grid(int64_t rows) {
   int64_t need = (rows + NW - 1) / NW;
@@ -343,26 +377,35 @@ void launch_norm_fwd(int mode, const void* x, const void* gate, const void* w, b
 
 void launch_norm_bwd(int mode, const void* dy, const void* x, const void* gate, const void* w, bool wf32,
                      const float* rstd, const float* mean, const void* dres, void* dx, void* dgate, float* dw,
-                     float* db, int64_t rows, int H, cudaStream_t st) {
+                     float* db, int64_t rows, int H, cudaStream_t st, float* part, int part_rows) {
   OXI_CHECK(H % 8 == 0 && H <= 32 * 8 * MAXV, "norm: hidden must be a multiple of 8 and <= 4096");
   if (rows == 0) return;
   if (H % 256 == 0 && H <= 4096) {
     // CTA per row: H / 8 threads; enough CTAs for every SM to hold 2048 threads
     const int threads = H / 8;
-    const int grid = (int)std::min<int64_t>(rows, (int64_t)num_sms_norm() * (2048 / threads));
+    const int grid = norm_bwd_partial_rows(rows, H);
     auto DY_ = reinterpret_cast<const __nv_bfloat16*>(dy);
     auto X_ = reinterpret_cast<const __nv_bfloat16*>(x);
     auto G_ = reinterpret_cast<const __nv_bfloat16*>(gate);
     auto DR_ = reinterpret_cast<const __nv_bfloat16*>(dres);
     auto DX_ = reinterpret_cast<__nv_bfloat16*>(dx);
     auto DG_ = reinterpret_cast<__nv_bfloat16*>(dgate);
+    float* pp = part && grid <= part_rows ? part : nullptr;
     if (mode == 0)
-      norm_bwd_row_kernel<0><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, rows, H);
+      norm_bwd_row_kernel<0><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, pp, rows,
+                                                       H);
     else if (mode == 1)
-      norm_bwd_row_kernel<1><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, rows, H);
+      norm_bwd_row_kernel<1><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, pp, rows,
+                                                       H);
     else
-      norm_bwd_row_kernel<2><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, rows, H);
+      norm_bwd_row_kernel<2><<<grid, threads, 0, st>>>(DY_, X_, G_, w, wf32, rstd, mean, DR_, DX_, DG_, dw, db, pp, rows,
+                                                       H);
     OXI_CUDA_CHECK(cudaGetLastError());
+    if (pp) {
+      const int width = mode == 1 ? 2 * H : H;
+      norm_part_sum_kernel<<<(width + 255) / 256, 256, 0, st>>>(pp, grid, H, dw, mode == 1 ? db : nullptr);
+      OXI_CUDA_CHECK(cudaGetLastError());
+    }
     return;
   }
   const int grid = norm_grid(rows);

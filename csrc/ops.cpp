@@ -173,11 +173,15 @@ void norm_bwd(int64_t mode, torch::Tensor dy, torch::Tensor x, c10::optional<tor
     check_bf16_rows(*dres, rows, H, "dres");
     dr = dres->data_ptr();
   }
+  const int prow = oxi::norm_bwd_partial_rows(rows, (int)H);
+  torch::Tensor part;
+  if (prow > 0) part = torch::empty({prow, 2 * H}, x.options().dtype(torch::kFloat32));
   oxi::launch_norm_bwd((int)mode, dy.data_ptr(), x.data_ptr(), mode == 2 ? gate->data_ptr() : nullptr, w.data_ptr(),
                        w.scalar_type() == torch::kFloat32, rstd.data_ptr<float>(),
                        mode == 1 ? mean->data_ptr<float>() : nullptr, dr, dx.data_ptr(),
                        mode == 2 ? dgate->data_ptr() : nullptr, dw.data_ptr<float>(),
-                       mode == 1 ? db->data_ptr<float>() : nullptr, rows, (int)H, stream());
+                       mode == 1 ? db->data_ptr<float>() : nullptr, rows, (int)H, stream(),
+                       prow > 0 ? part.data_ptr<float>() : nullptr, prow);
 }
 
 // ------------------------------------------------------------ CE

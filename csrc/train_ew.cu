@@ -138,6 +138,43 @@ __global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int64
   }
 }
 
+// Same, 8 rotation pairs per thread with 16-byte loads and stores: one CTA per
+// row (grid-stride), threads over (head, 8-pair group).  Needs half % 8 == 0 and
+// 16-byte aligned rows.
+__global__ void __launch_bounds__(256) rope_bwd_vec_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int64_t rows,
+                                                           int ncols_rot, int hd, const float* __restrict__ cos,
+                                                           const float* __restrict__ sin, int seq) {
+  const int half = hd / 2;
+  const int groups = half / 8;
+  const int items = (ncols_rot / hd) * groups;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int pos = (int)(row % seq);
+    const float* cr = cos + (int64_t)pos * half;
+    const float* sr = sin + (int64_t)pos * half;
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+      const int head = it / groups, j = (it % groups) * 8;
+      __nv_bfloat16* base = x + row * ld + head * hd;
+      uint4 ua = *reinterpret_cast<const uint4*>(base + j);
+      uint4 ub = *reinterpret_cast<const uint4*>(base + j + half);
+      const float4 c0 = __ldg(reinterpret_cast<const float4*>(cr + j)), c1 = __ldg(reinterpret_cast<const float4*>(cr + j + 4));
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(sr + j)), s1 = __ldg(reinterpret_cast<const float4*>(sr + j + 4));
+      const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      __nv_bfloat162* ha = reinterpret_cast<__nv_bfloat162*>(&ua);
+      __nv_bfloat162* hb = reinterpret_cast<__nv_bfloat162*>(&ub);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 a = __bfloat1622float2(ha[q]), b = __bfloat1622float2(hb[q]);
+        const float c_0 = cc[2 * q], c_1 = cc[2 * q + 1], s_0 = ss[2 * q], s_1 = ss[2 * q + 1];
+        ha[q] = __floats2bfloat162_rn(a.x * c_0 + b.x * s_0, a.y * c_1 + b.y * s_1);
+        hb[q] = __floats2bfloat162_rn(b.x * c_0 - a.x * s_0, b.y * c_1 - a.y * s_1);
+      }
+      *reinterpret_cast<uint4*>(base + j) = ua;
+      *reinterpret_cast<uint4*>(base + j + half) = ub;
+    }
+  }
+}
+
 // --------------------------------------------------------- grad norm / clip
 __global__ void sqsum_kernel(const float* __restrict__ g, int64_t n, float* __restrict__ out) {
   float s = 0.f;
@@ -314,6 +351,14 @@ void launch_embed_bwd(const int64_t* ids, const void* dy, float* dw, int64_t row
 void launch_rope_bwd(void* x, int64_t ld, int64_t rows, int ncols_rot, int hd, const float* cos, const float* sin,
                      int seq, cudaStream_t st) {
   if (!rows || !ncols_rot) return;
+  if ((hd / 2) % 8 == 0 && ncols_rot % hd == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(cos) & 15) == 0 && (reinterpret_cast<uintptr_t>(sin) & 15) == 0) {
+    const unsigned grid = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 8);
+    rope_bwd_vec_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), ld, rows, ncols_rot, hd, cos, sin,
+                                              seq);
+    OXI_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int64_t total = rows * (ncols_rot / 2);
   const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)sm_count() * 16);
   rope_bwd_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), ld, rows, ncols_rot, hd, cos, sin, seq);

@@ -77,17 +77,19 @@ def test_embedding_and_rope_bwd():
     y.backward(dy)
     ref = torch.zeros(V, H, device="cuda").index_add_(0, ids.reshape(-1), dy.reshape(-1, H).float())
     assert _rel(w.grad, ref) < 1e-2
-    # rope backward == transpose of the forward rotation
-    S, hd = 64, 128
-    cos, sin = R.rope_tables(hd, S, 10000.0, device="cuda")
-    x = torch.randn(2, S, 3, hd, device="cuda")
-    d = torch.randn(2 * S, 3 * hd, device="cuda").bfloat16()
-    xr = x.requires_grad_()
-    yr = R.apply_rope(xr.transpose(1, 2), cos, sin).transpose(1, 2)
-    yr.backward(d.float().view(2, S, 3, hd))
-    dd = d.clone()
-    ext().rope_bwd(dd, 3 * hd, hd, cos.contiguous(), sin.contiguous())
-    assert _rel(dd.view(2, S, 3, hd), xr.grad) < 1e-2
+    # rope backward == transpose of the forward rotation; columns past the rotated
+    # heads (the v part of a fused qkv gradient) stay as they are
+    for S, hd in ((64, 128), (50, 64)):
+        cos, sin = R.rope_tables(hd, S, 10000.0, device="cuda")
+        x = torch.randn(2, S, 3, hd, device="cuda")
+        d = torch.randn(2 * S, 4 * hd, device="cuda").bfloat16()
+        xr = x.requires_grad_()
+        yr = R.apply_rope(xr.transpose(1, 2), cos, sin).transpose(1, 2)
+        yr.backward(d[:, :3 * hd].float().view(2, S, 3, hd))
+        dd = d.clone()
+        ext().rope_bwd(dd, 3 * hd, hd, cos.contiguous(), sin.contiguous())
+        assert _rel(dd[:, :3 * hd].reshape(2, S, 3, hd), xr.grad) < 1e-2
+        assert torch.equal(dd[:, 3 * hd:], d[:, 3 * hd:])
 
 
 def test_adamw_kernel_matches_reference():
