@@ -23,6 +23,9 @@ void launch_embed_fwd(const int64_t* ids, const void* w, void* out, int64_t rows
 void launch_embed_bwd(const int64_t* ids, const void* dy, float* dw, int64_t rows, int H, cudaStream_t st);
 void launch_rope_bwd(void* x, int64_t ld, int64_t rows, int ncols_rot, int hd, const float* cos, const float* sin,
                      int seq, cudaStream_t st);
+// out of place: dst[:, :ncols_rot] = rope backward of src, dst[:, ncols_rot:ncols] = src
+void launch_rope_bwd_to(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t rows, int ncols_rot, int ncols,
+                        int hd, const float* cos, const float* sin, int seq, cudaStream_t st);
 void launch_sqsum(const float* g, int64_t n, float* out, cudaStream_t st);
 // out[c] += sum over rows of a bf16 [rows, N] matrix with row stride ld (bias gradients)
 void launch_colsum_bf16(const void* x, int64_t rows, int N, int64_t ld, float* out, cudaStream_t st);

@@ -223,6 +223,16 @@ void rope_bwd(torch::Tensor x, int64_t ncols_rot, int64_t hd, torch::Tensor cos,
                        sin.data_ptr<float>(), (int)cos.size(0), stream());
 }
 
+torch::Tensor rope_bwd_to(torch::Tensor x, int64_t ncols_rot, int64_t hd, torch::Tensor cos, torch::Tensor sin) {
+  c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "rope_bwd_to x");
+  auto out = torch::empty({x.size(0), x.size(1)}, x.options());
+  oxi::launch_rope_bwd_to(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), x.size(0), (int)ncols_rot,
+                          (int)x.size(1), (int)hd, cos.data_ptr<float>(), sin.data_ptr<float>(), (int)cos.size(0),
+                          stream());
+  return out;
+}
+
 // ------------------------------------------------------------ optimizer
 void sqsum(torch::Tensor g, torch::Tensor out) {
   c10::cuda::CUDAGuard gd(g.device());
@@ -1021,6 +1031,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd", &ce_bwd, "in-place softmax-minus-onehot gradient of the logits");
   m.def("embed_fwd", &embed_fwd, "embedding gather");
   m.def("embed_bwd", &embed_bwd, "embedding scatter-add into f32 grad");
+  m.def("rope_bwd_to", &rope_bwd_to, "out-of-place RoPE backward (+ copy of the unrotated columns)");
   m.def("rope_bwd", &rope_bwd, "in-place inverse rotate-half RoPE");
   m.def("sqsum", &sqsum, "sum of squares (atomically added into out)");
   m.def("colsum_add", &colsum_add, "out += column sums of a bf16 matrix (bias gradients)");

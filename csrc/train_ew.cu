@@ -141,8 +141,11 @@ __global__ void rope_bwd_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int64
 // Same, 8 rotation pairs per thread with 16-byte loads and stores: one CTA per
 // row (grid-stride), threads over (head, 8-pair group).  Needs half % 8 == 0 and
 // 16-byte aligned rows.
-__global__ void __launch_bounds__(256) rope_bwd_vec_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int64_t rows,
-                                                           int ncols_rot, int hd, const float* __restrict__ cos,
+// src may differ from x (out of place; then the columns past ncols_rot, up to
+// ncols, are copied as they are).
+__global__ void __launch_bounds__(256) rope_bwd_vec_kernel(const __nv_bfloat16* src, int64_t lds, __nv_bfloat16* x,
+                                                           int64_t ld, int64_t rows, int ncols_rot, int ncols, int hd,
+                                                           const float* __restrict__ cos,
                                                            const float* __restrict__ sin, int seq) {
   const int half = hd / 2;
   const int groups = half / 8;
@@ -154,8 +157,9 @@ __global__ void __launch_bounds__(256) rope_bwd_vec_kernel(__nv_bfloat16* __rest
     for (int it = threadIdx.x; it < items; it += blockDim.x) {
       const int head = it / groups, j = (it % groups) * 8;
       __nv_bfloat16* base = x + row * ld + head * hd;
-      uint4 ua = *reinterpret_cast<const uint4*>(base + j);
-      uint4 ub = *reinterpret_cast<const uint4*>(base + j + half);
+      const __nv_bfloat16* sbase = src + row * lds + head * hd;
+      uint4 ua = *reinterpret_cast<const uint4*>(sbase + j);
+      uint4 ub = *reinterpret_cast<const uint4*>(sbase + j + half);
       const float4 c0 = __ldg(reinterpret_cast<const float4*>(cr + j)), c1 = __ldg(reinterpret_cast<const float4*>(cr + j + 4));
       const float4 s0 = __ldg(reinterpret_cast<const float4*>(sr + j)), s1 = __ldg(reinterpret_cast<const float4*>(sr + j + 4));
       const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
@@ -172,6 +176,9 @@ __global__ void __launch_bounds__(256) rope_bwd_vec_kernel(__nv_bfloat16* __rest
       *reinterpret_cast<uint4*>(base + j) = ua;
       *reinterpret_cast<uint4*>(base + j + half) = ub;
     }
+    if (src != x)
+      for (int c = ncols_rot + threadIdx.x * 8; c < ncols; c += blockDim.x * 8)
+        *reinterpret_cast<uint4*>(x + row * ld + c) = *reinterpret_cast<const uint4*>(src + row * lds + c);
   }
 }
 
@@ -348,15 +355,29 @@ void launch_embed_bwd(const int64_t* ids, const void* dy, float* dw, int64_t row
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
+bool rope_bwd_vec_ok(const void* p, int64_t ld, int ncols_rot, int hd) {
+  return (hd / 2) % 8 == 0 && ncols_rot % hd == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+void launch_rope_bwd_to(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t rows, int ncols_rot, int ncols,
+                        int hd, const float* cos, const float* sin, int seq, cudaStream_t st) {
+  OXI_CHECK(rope_bwd_vec_ok(src, lds, ncols_rot, hd) && rope_bwd_vec_ok(dst, ldd, ncols_rot, hd) && ncols % 8 == 0 &&
+                (reinterpret_cast<uintptr_t>(cos) & 15) == 0 && (reinterpret_cast<uintptr_t>(sin) & 15) == 0,
+            "rope_bwd_to: 16-byte aligned rows, half head a multiple of 8");
+  if (!rows) return;
+  const unsigned grid = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 8);
+  rope_bwd_vec_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(src), lds,
+                                            reinterpret_cast<__nv_bfloat16*>(dst), ldd, rows, ncols_rot, ncols, hd,
+                                            cos, sin, seq);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
 void launch_rope_bwd(void* x, int64_t ld, int64_t rows, int ncols_rot, int hd, const float* cos, const float* sin,
                      int seq, cudaStream_t st) {
   if (!rows || !ncols_rot) return;
-  if ((hd / 2) % 8 == 0 && ncols_rot % hd == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
-      (reinterpret_cast<uintptr_t>(cos) & 15) == 0 && (reinterpret_cast<uintptr_t>(sin) & 15) == 0) {
-    const unsigned grid = (unsigned)std::min<int64_t>(rows, (int64_t)sm_count() * 8);
-    rope_bwd_vec_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), ld, rows, ncols_rot, hd, cos, sin,
-                                              seq);
-    OXI_CUDA_CHECK(cudaGetLastError());
+  if (rope_bwd_vec_ok(x, ld, ncols_rot, hd) && (reinterpret_cast<uintptr_t>(cos) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(sin) & 15) == 0) {
+    launch_rope_bwd_to(x, ld, x, ld, rows, ncols_rot, ncols_rot, hd, cos, sin, seq, st);
     return;
   }
   const int64_t total = rows * (ncols_rot / 2);

@@ -165,8 +165,12 @@ class LinearRope(torch.autograd.Function):
     def backward(ctx, dy):
         x2, cos, sin = ctx.saved_tensors
         w = ctx.w
-        dy2 = dy.reshape(-1, w.shape[0]).contiguous().clone()
-        ext().rope_bwd(dy2, ctx.rot, ctx.hd, cos, sin)
+        d = dy.reshape(-1, w.shape[0])
+        if d.stride(1) == 1 and d.stride(0) % 8 == 0 and d.data_ptr() % 16 == 0 and w.shape[0] % 8 == 0:
+            dy2 = ext().rope_bwd_to(d, ctx.rot, ctx.hd, cos, sin)  # one pass, no copy first
+        else:
+            dy2 = d.contiguous().clone()
+            ext().rope_bwd(dy2, ctx.rot, ctx.hd, cos, sin)
         dx = mm(dy2, w, b_t=True).view(*dy.shape[:-1], w.shape[1])
         gw = _wgrad_gemm(w, dy2, x2)
         return dx, gw, None, None, None, None, None

@@ -90,6 +90,7 @@ def test_embedding_and_rope_bwd():
         ext().rope_bwd(dd, 3 * hd, hd, cos.contiguous(), sin.contiguous())
         assert _rel(dd[:, :3 * hd].reshape(2, S, 3, hd), xr.grad) < 1e-2
         assert torch.equal(dd[:, 3 * hd:], d[:, 3 * hd:])
+        assert torch.equal(ext().rope_bwd_to(d, 3 * hd, hd, cos.contiguous(), sin.contiguous()), dd)
 
 
 def test_adamw_kernel_matches_reference():
