@@ -8,6 +8,7 @@
 // f32 global buffer with one atomic per column per CTA.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdint>
 
 #include "host_util.h"
@@ -315,18 +316,19 @@ __global__ void __launch_bounds__(512) norm_bwd_row_kernel(
   }
 }
 
-// dw[c] += sum_g part[g][c] (and db from the second half): one thread per column,
-// the only writer of its column, so no atomics (thousands of CTAs adding into the
-// same H addresses serialise in L2)
+// dw[c] += sum_g part[g][c] (and db from the second half).  A CTA sums a slice of
+// the CTAs' partials for 256 columns and adds it with one atomic per column: a
+// few dozen adds per address instead of one per row-CTA.
 __global__ void norm_part_sum_kernel(const float* __restrict__ part, int G, int H, float* __restrict__ dw,
                                      float* __restrict__ db) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int width = db ? 2 * H : H;
   if (c >= width) return;
+  const int per = (G + gridDim.y - 1) / gridDim.y;
+  const int g0 = blockIdx.y * per, g1 = min(G, g0 + per);
   float s = 0.f;
-  for (int g = 0; g < G; ++g) s += part[(int64_t)g * 2 * H + c];
-  if (c < H) dw[c] += s;
-  else db[c - H] += s;
+  for (int g = g0; g < g1; ++g) s += part[(int64_t)g * 2 * H + c];
+  if (g1 > g0) atomicAdd(c < H ? dw + c : db + (c - H), s);
 }
 
 int num_sms_norm() {
@@ -403,7 +405,9 @@ void launch_norm_bwd(int mode, const void* dy, const void* x, const void* gate, 
     OXI_CUDA_CHECK(cudaGetLastError());
     if (pp) {
       const int width = mode == 1 ? 2 * H : H;
-      norm_part_sum_kernel<<<(width + 255) / 256, 256, 0, st>>>(pp, grid, H, dw, mode == 1 ? db : nullptr);
+      const int slices = std::max(1, std::min(grid / 16, 64));
+      norm_part_sum_kernel<<<dim3((width + 255) / 256, slices), 256, 0, st>>>(pp, grid, H, dw,
+                                                                              mode == 1 ? db : nullptr);
       OXI_CUDA_CHECK(cudaGetLastError());
     }
     return;
