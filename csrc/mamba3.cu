@@ -27,6 +27,21 @@ namespace {
 
 constexpr int M3N = 128;
 
+// sin / cos of a rotation angle that can be large (a cumulative sum over the
+// sequence): Cody-Waite range reduction (Cody & Waite, "Software Manual for the
+// Elementary Functions", 1980) by 2*pi split into a short head (few significant
+// bits, so k * head is exact for |k| < 2^16) and the tail, then sincosf on the
+// reduced angle in [-pi, pi], which stays on its short path.
+__device__ __forceinline__ void rot_sincos(float a, float* s, float* c) {
+  constexpr float kInv2Pi = 0.15915494309189535f;
+  constexpr float kHead = 6.28125f;                   // 2*pi rounded to 8 significant bits
+  constexpr float kTail = 1.9353071795864769e-3f;     // 2*pi - kHead
+  const float k = rintf(a * kInv2Pi);
+  float r = fmaf(-k, kHead, a);
+  r = fmaf(-k, kTail, r);
+  sincosf(r, s, c);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -89,8 +104,8 @@ __global__ void __launch_bounds__(256) m3_bc_fwd_kernel(const __nv_bfloat16* __r
     const float rib = rsqrtf(sb / M3N + eps), ric = rsqrtf(sc / M3N + eps);
     const float2 a = *reinterpret_cast<const float2*>(ang + it * (M3N / 2) + lane * 2);
     float s0, c0, s1, c1;
-    sincosf(a.x, &s0, &c0);
-    sincosf(a.y, &s1, &c1);
+    rot_sincos(a.x, &s0, &c0);
+    rot_sincos(a.y, &s1, &c1);
     float ob[4], oc[4];
     norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
     norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);
@@ -154,8 +169,8 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
         load4(cbias + h * M3N + lane * 4, cb);
         const float2 a = *reinterpret_cast<const float2*>(ang + it * (M3N / 2) + lane * 2);
         float s0, c0, s1, c1;
-        sincosf(a.x, &s0, &c0);
-        sincosf(a.y, &s1, &c1);
+        rot_sincos(a.x, &s0, &c0);
+        rot_sincos(a.y, &s1, &c1);
         float ob[4], oc[4];
         norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
         norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);

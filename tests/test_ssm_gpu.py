@@ -222,7 +222,9 @@ def test_mamba3_bc_prologue_kernel():
     w = (1 + 0.1 * torch.randn(N, device="cuda")).bfloat16().requires_grad_()
     bb = (1 + 0.1 * torch.randn(H, N, device="cuda")).bfloat16().requires_grad_()
     cb = (1 + 0.1 * torch.randn(H, N, device="cuda")).bfloat16().requires_grad_()
-    ang = (3 * torch.randn(B, S, H, N // 2, device="cuda")).requires_grad_()
+    # angles are cumulative sums over the sequence: include large ones
+    ang = (3 * torch.randn(B, S, H, N // 2, device="cuda") + 2000 * torch.rand(B, S, 1, 1, device="cuda")
+           ).requires_grad_()
     bo, co, dot = Mamba3BC.apply(braw, craw, w, bb, cb, ang, H, 1e-6)
     torch.cuda.synchronize()
     gb, gc = torch.randn_like(bo, dtype=torch.float32), torch.randn_like(co, dtype=torch.float32)
