@@ -73,6 +73,9 @@ __device__ __forceinline__ void norm_bias_rot(const float* raw, float rinv, cons
   out[3] = n[2] * s1 + n[3] * c1;
 }
 
+// one warp per token: the RMSNorm statistics of the token's raw B / C rows are
+// computed once per group, then every head of the group is biased, rotated and
+// stored (heads unrolled by four for independent loads and shuffles)
 __global__ void __launch_bounds__(256) m3_bc_fwd_kernel(const __nv_bfloat16* __restrict__ braw,
                                                         const __nv_bfloat16* __restrict__ craw, int64_t ldr,
                                                         const __nv_bfloat16* __restrict__ w,
@@ -83,38 +86,41 @@ __global__ void __launch_bounds__(256) m3_bc_fwd_kernel(const __nv_bfloat16* __r
                                                         __nv_bfloat16* __restrict__ cout,
                                                         float* __restrict__ bcdot) {
   const int lane = threadIdx.x & 31;
-  const int64_t items = (int64_t)Bsz * S * H;
+  const int64_t tokens = (int64_t)Bsz * S;
   const int hpg = H / G;
   float wv[4];
   load4(w + lane * 4, wv);
-  for (int64_t it = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; it < items;
-       it += (int64_t)gridDim.x * (blockDim.x / 32)) {
-    const int h = (int)(it % H);
-    const int64_t bt = it / H;  // b * S + t
-    const int t = (int)(bt % S);
-    const int64_t b = bt / S;
-    const int g = h / hpg;
-    float rb[4], rc[4], bb[4], cb[4];
-    load4(braw + bt * ldr + g * M3N + lane * 4, rb);
-    load4(craw + bt * ldr + g * M3N + lane * 4, rc);
-    load4(bbias + h * M3N + lane * 4, bb);
-    load4(cbias + h * M3N + lane * 4, cb);
-    const float sb = warp_sum(rb[0] * rb[0] + rb[1] * rb[1] + rb[2] * rb[2] + rb[3] * rb[3]);
-    const float sc = warp_sum(rc[0] * rc[0] + rc[1] * rc[1] + rc[2] * rc[2] + rc[3] * rc[3]);
-    const float rib = rsqrtf(sb / M3N + eps), ric = rsqrtf(sc / M3N + eps);
-    const float2 a = *reinterpret_cast<const float2*>(ang + it * (M3N / 2) + lane * 2);
-    float s0, c0, s1, c1;
-    rot_sincos(a.x, &s0, &c0);
-    rot_sincos(a.y, &s1, &c1);
-    float ob[4], oc[4];
-    norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
-    norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);
-    round4(ob);
-    round4(oc);
-    store4(bout + it * M3N + lane * 4, ob);
-    store4(cout + it * M3N + lane * 4, oc);
-    const float d = warp_sum(ob[0] * oc[0] + ob[1] * oc[1] + ob[2] * oc[2] + ob[3] * oc[3]);
-    if (lane == 0) bcdot[it] = d;
+  for (int64_t bt = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; bt < tokens;
+       bt += (int64_t)gridDim.x * (blockDim.x / 32)) {
+    for (int g = 0; g < G; ++g) {
+      float rb[4], rc[4];
+      load4(braw + bt * ldr + g * M3N + lane * 4, rb);
+      load4(craw + bt * ldr + g * M3N + lane * 4, rc);
+      const float sb = warp_sum(rb[0] * rb[0] + rb[1] * rb[1] + rb[2] * rb[2] + rb[3] * rb[3]);
+      const float sc = warp_sum(rc[0] * rc[0] + rc[1] * rc[1] + rc[2] * rc[2] + rc[3] * rc[3]);
+      const float rib = rsqrtf(sb / M3N + eps), ric = rsqrtf(sc / M3N + eps);
+#pragma unroll 4
+      for (int hh = 0; hh < hpg; ++hh) {
+        const int h = g * hpg + hh;
+        const int64_t it = bt * H + h;
+        float bb[4], cb[4];
+        load4(bbias + h * M3N + lane * 4, bb);
+        load4(cbias + h * M3N + lane * 4, cb);
+        const float2 a = *reinterpret_cast<const float2*>(ang + it * (M3N / 2) + lane * 2);
+        float s0, c0, s1, c1;
+        rot_sincos(a.x, &s0, &c0);
+        rot_sincos(a.y, &s1, &c1);
+        float ob[4], oc[4];
+        norm_bias_rot(rb, rib, wv, bb, c0, s0, c1, s1, ob);
+        norm_bias_rot(rc, ric, wv, cb, c0, s0, c1, s1, oc);
+        round4(ob);
+        round4(oc);
+        store4(bout + it * M3N + lane * 4, ob);
+        store4(cout + it * M3N + lane * 4, oc);
+        const float d = warp_sum(ob[0] * oc[0] + ob[1] * oc[1] + ob[2] * oc[2] + ob[3] * oc[3]);
+        if (lane == 0) bcdot[it] = d;
+      }
+    }
   }
 }
 
@@ -158,6 +164,7 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
       const float sc = warp_sum(rc[0] * rc[0] + rc[1] * rc[1] + rc[2] * rc[2] + rc[3] * rc[3]);
       const float rib = rsqrtf(sb / M3N + eps), ric = rsqrtf(sc / M3N + eps);
       float gb[4] = {0.f, 0.f, 0.f, 0.f}, gc[4] = {0.f, 0.f, 0.f, 0.f};  // sum over heads of d_n
+#pragma unroll 4
       for (int hh = 0; hh < hpg; ++hh) {
         const int h = g * hpg + hh;
         const int64_t it = bt * H + h;
@@ -245,7 +252,7 @@ void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const voi
                       const void* cbias, const float* ang, int B, int S, int H, int G, int N, float eps, void* bout,
                       void* cout, float* bcdot, cudaStream_t st) {
   OXI_CHECK(N == M3N && H % G == 0 && ldr % 4 == 0, "Mamba3 B/C prologue supports state size 128");
-  m3_bc_fwd_kernel<<<grid_of((int64_t)B * S * H), 256, 0, st>>>(
+  m3_bc_fwd_kernel<<<grid_of((int64_t)B * S), 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(braw), reinterpret_cast<const __nv_bfloat16*>(craw), ldr,
       reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<const __nv_bfloat16*>(bbias),
       reinterpret_cast<const __nv_bfloat16*>(cbias), ang, B, S, H, G, eps, reinterpret_cast<__nv_bfloat16*>(bout),
