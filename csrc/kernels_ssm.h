@@ -82,7 +82,10 @@ void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const voi
 void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
                       const void* cbias, const float* ang, const void* db, const void* dc, bool grads_bf16,
                       const float* dbcdot, int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw,
-                      int64_t ldd, float* dw, float* dbb, float* dcb, float* dang, cudaStream_t st);
+                      int64_t ldd, float* dw, float* dbb, float* dcb, float* dang, cudaStream_t st,
+                      float* part = nullptr);
+// blocks of the prologue backward = rows of its bias-gradient partials `part` [rows, 2 * H * N]
+int m3_bc_bwd_blocks(int64_t tokens);
 }  // namespace oxi
 
 namespace oxi {

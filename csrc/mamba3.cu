@@ -142,7 +142,8 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
                                                         const float* __restrict__ dbcdot, int Bsz, int S, int H, int G,
                                                         float eps, float* __restrict__ dbraw, float* __restrict__ dcraw,
                                                         int64_t ldd, float* __restrict__ dw, float* __restrict__ dbb,
-                                                        float* __restrict__ dcb, float* __restrict__ dang) {
+                                                        float* __restrict__ dcb, float* __restrict__ dang,
+                                                        float* __restrict__ part) {
   extern __shared__ float s_db[];  // [2][H][N] bias-gradient partials of this block
   float* s_dbb = s_db;
   float* s_dcb = s_db + H * M3N;
@@ -235,10 +236,26 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
 #pragma unroll
   for (int i = 0; i < 4; ++i) atomicAdd(dw + lane * 4 + i, dw_acc[i]);
   __syncthreads();
+  if (part) {  // block partials, summed by m3_part_sum_kernel (no same-address atomics)
+    for (int i = threadIdx.x; i < 2 * H * M3N; i += blockDim.x) part[(int64_t)blockIdx.x * 2 * H * M3N + i] = s_db[i];
+    return;
+  }
   for (int i = threadIdx.x; i < H * M3N; i += blockDim.x) {
     atomicAdd(dbb + i, s_dbb[i]);
     atomicAdd(dcb + i, s_dcb[i]);
   }
+}
+
+// out[c] += sum over a slice of the blocks' partials [G][2 * HN] (c < HN -> dbb, else dcb)
+__global__ void m3_part_sum_kernel(const float* __restrict__ part, int G, int HN, float* __restrict__ dbb,
+                                   float* __restrict__ dcb) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= 2 * HN) return;
+  const int per = (G + gridDim.y - 1) / gridDim.y;
+  const int g0 = blockIdx.y * per, g1 = min(G, g0 + per);
+  float sum = 0.f;
+  for (int g = g0; g < g1; ++g) sum += part[(int64_t)g * 2 * HN + c];
+  if (g1 > g0) atomicAdd(c < HN ? dbb + c : dcb + (c - HN), sum);
 }
 
 unsigned grid_of(int64_t warps_needed) {
@@ -263,9 +280,10 @@ void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const voi
 void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
                       const void* cbias, const float* ang, const void* db, const void* dc, bool grads_bf16,
                       const float* dbcdot, int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw,
-                      int64_t ldd, float* dw, float* dbb, float* dcb, float* dang, cudaStream_t st) {
+                      int64_t ldd, float* dw, float* dbb, float* dcb, float* dang, cudaStream_t st,
+                      float* part) {
   OXI_CHECK(N == M3N && H % G == 0 && H <= 64, "Mamba3 B/C prologue supports state size 128, <= 64 heads");
-  const int64_t blocks = std::min<int64_t>(((int64_t)B * S + 7) / 8, 148 * 4);
+  const int64_t blocks = m3_bc_bwd_blocks((int64_t)B * S);
   const int smem = 2 * H * M3N * (int)sizeof(float);
   const auto* br = reinterpret_cast<const __nv_bfloat16*>(braw);
   const auto* cr = reinterpret_cast<const __nv_bfloat16*>(craw);
@@ -278,15 +296,23 @@ void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const voi
     if (smem > 48 * 1024) OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<grid, 256, smem, st>>>(br, cr, ldr, wb, bb, cb, ang, reinterpret_cast<const __nv_bfloat16*>(db),
                                   reinterpret_cast<const __nv_bfloat16*>(dc), dbcdot, B, S, H, G, eps, dbraw, dcraw,
-                                  ldd, dw, dbb, dcb, dang);
+                                  ldd, dw, dbb, dcb, dang, part);
   } else {
     auto kern = m3_bc_bwd_kernel<float>;
     if (smem > 48 * 1024) OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<grid, 256, smem, st>>>(br, cr, ldr, wb, bb, cb, ang, reinterpret_cast<const float*>(db),
                                   reinterpret_cast<const float*>(dc), dbcdot, B, S, H, G, eps, dbraw, dcraw, ldd, dw,
-                                  dbb, dcb, dang);
+                                  dbb, dcb, dang, part);
   }
   OXI_CUDA_CHECK(cudaGetLastError());
+  if (part) {
+    const int HN = H * M3N;
+    const int slices = std::max(1, std::min((int)grid / 16, 64));
+    m3_part_sum_kernel<<<dim3((2 * HN + 255) / 256, slices), 256, 0, st>>>(part, (int)grid, HN, dbb, dcb);
+    OXI_CUDA_CHECK(cudaGetLastError());
+  }
 }
+
+int m3_bc_bwd_blocks(int64_t tokens) { return (int)std::max<int64_t>(1, std::min<int64_t>((tokens + 7) / 8, 148 * 4)); }
 
 }  // namespace oxi

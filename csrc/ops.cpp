@@ -688,12 +688,13 @@ std::vector<torch::Tensor> m3_bc_bwd(torch::Tensor braw, torch::Tensor craw, tor
   auto dbb = torch::zeros({H, 128}, f32);
   auto dcb = torch::zeros({H, 128}, f32);
   auto dang = torch::empty({B, S, H, 64}, f32);
+  auto part = torch::empty({oxi::m3_bc_bwd_blocks(B * S), 2 * H * 128}, f32);
   oxi::launch_m3_bc_bwd(braw.data_ptr(), craw.data_ptr(), braw.stride(0), w.data_ptr(), bbias.data_ptr(),
                         cbias.data_ptr(), ang.data_ptr<float>(), db.data_ptr(), dc.data_ptr(),
                         db.scalar_type() == torch::kBFloat16, dd,
                         (int)B, (int)S, (int)H, (int)G, 128, (float)eps, dbraw.data_ptr<float>(),
                         dcraw.data_ptr<float>(), dbraw.stride(0), dw.data_ptr<float>(), dbb.data_ptr<float>(),
-                        dcb.data_ptr<float>(), dang.data_ptr<float>(), stream());
+                        dcb.data_ptr<float>(), dang.data_ptr<float>(), stream(), part.data_ptr<float>());
   return {dbraw, dcraw, dw, dbb, dcb, dang};
 }
 
