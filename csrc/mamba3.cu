@@ -205,8 +205,9 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
         nc[2] = dC[2] * c1 + dC[3] * s1;  nc[3] = -dC[2] * s1 + dC[3] * c1;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          atomicAdd(s_dbb + h * M3N + lane * 4 + i, nb[i]);
-          atomicAdd(s_dcb + h * M3N + lane * 4 + i, nc[i]);
+          // element lane*4+i kept at i*32+lane: the 32 lanes of one add hit 32 banks
+          atomicAdd(s_dbb + h * M3N + i * 32 + lane, nb[i]);
+          atomicAdd(s_dcb + h * M3N + i * 32 + lane, nc[i]);
           gb[i] += nb[i];
           gc[i] += nc[i];
         }
@@ -236,13 +237,16 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
 #pragma unroll
   for (int i = 0; i < 4; ++i) atomicAdd(dw + lane * 4 + i, dw_acc[i]);
   __syncthreads();
+  // position i*32+lane of a head's slot holds element lane*4+i
+  auto slot = [](int e) { return (e / M3N) * M3N + (e % 4) * 32 + (e % M3N) / 4; };
   if (part) {  // block partials, summed by m3_part_sum_kernel (no same-address atomics)
-    for (int i = threadIdx.x; i < 2 * H * M3N; i += blockDim.x) part[(int64_t)blockIdx.x * 2 * H * M3N + i] = s_db[i];
+    for (int e = threadIdx.x; e < 2 * H * M3N; e += blockDim.x)
+      part[(int64_t)blockIdx.x * 2 * H * M3N + e] = s_db[slot(e)];
     return;
   }
-  for (int i = threadIdx.x; i < H * M3N; i += blockDim.x) {
-    atomicAdd(dbb + i, s_dbb[i]);
-    atomicAdd(dcb + i, s_dcb[i]);
+  for (int e = threadIdx.x; e < H * M3N; e += blockDim.x) {
+    atomicAdd(dbb + e, s_dbb[slot(e)]);
+    atomicAdd(dcb + e, s_dcb[slot(e)]);
   }
 }
 
