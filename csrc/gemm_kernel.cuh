@@ -794,13 +794,14 @@ inline int b_tile_rows(const GemmParams& p) { return p.cg == 2 ? PAIR_B_ROWS : B
 // accumulating f32 output, whose epilogue adds with atomics.  The split count
 // is chosen for wave fill over the units that run at once (CTAs, or clusters
 // for CTA pairs): the smallest count within 2 % of the best fill, at least 16
-// k-blocks per split, at most eight waves of units.
+// k-blocks per split, at most four waves of units (more splits cost more in f32
+// atomics than the better fill gains; measured on the dW shapes).
 inline void choose_splits(GemmParams& p) {
   const int tiles = p.tiles_m * p.tiles_n;
   const int num_kb = (p.K + BK - 1) / BK;
   const int slots = p.cg == 2 ? num_sms() / 2 : num_sms();
-  if (tiles >= 8 * slots || num_kb < 32) return;
-  const int smax = std::max(1, std::min(num_kb / 16, (8 * slots + tiles - 1) / tiles));
+  if (tiles >= 2 * slots || num_kb < 32) return;
+  const int smax = std::max(1, std::min(num_kb / 16, (4 * slots + tiles - 1) / tiles));
   auto fill = [&](int s) {
     const int64_t u = (int64_t)tiles * s;
     const int64_t waves = (u + slots - 1) / slots;
