@@ -643,11 +643,25 @@ inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
+// cuTensorMapEncodeTiled is a driver call and needs a current context.  Autograd runs
+// backward on a thread of its own; when one of these ops is the first CUDA work there,
+// no runtime call has made the primary context current yet (the device guard does
+// nothing when the device already matches).  cudaSetDevice makes it current (CUDA 12).
+inline void ensure_current_context() {
+  thread_local unsigned long long ready = 0;
+  int dev = 0;
+  OXI_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 64 && ((ready >> dev) & 1ull)) return;
+  OXI_CUDA_CHECK(cudaSetDevice(dev));
+  if (dev < 64) ready |= 1ull << dev;
+}
+
 // 2-D bf16 tensor map over a row-major matrix [rows, cols] with row stride
 // `ld` elements, box {box_cols, box_rows}, 128-byte swizzle, zero OOB fill.
 inline CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
   OXI_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
   OXI_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes (ld % 8 == 0)");
+  ensure_current_context();
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};

@@ -30,8 +30,9 @@ constexpr int M3N = 128;
 // sin / cos of a rotation angle that can be large (a cumulative sum over the
 // sequence): Cody-Waite range reduction (Cody & Waite, "Software Manual for the
 // Elementary Functions", 1980) by 2*pi split into a short head (few significant
-// bits, so k * head is exact for |k| < 2^16) and the tail, then sincosf on the
-// reduced angle in [-pi, pi], which stays on its short path.
+// bits, so k * head is exact for |k| < 2^16) and the tail, then the hardware
+// __sincosf on the reduced angle in [-pi, pi], where its absolute error is about
+// 1e-6 (far below the bf16 rounding of the outputs).
 __device__ __forceinline__ void rot_sincos(float a, float* s, float* c) {
   constexpr float kInv2Pi = 0.15915494309189535f;
   constexpr float kHead = 6.28125f;                   // 2*pi rounded to 8 significant bits
@@ -39,7 +40,7 @@ __device__ __forceinline__ void rot_sincos(float a, float* s, float* c) {
   const float k = rintf(a * kInv2Pi);
   float r = fmaf(-k, kHead, a);
   r = fmaf(-k, kTail, r);
-  sincosf(r, s, c);
+  __sincosf(r, s, c);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

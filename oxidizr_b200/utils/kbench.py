@@ -229,6 +229,97 @@ def run_once(what: str):
         Cm = torch.randn(B, S, G, 128, device="cuda").bfloat16().requires_grad_()
         for _ in range(3):
             ssd_tc(x, dt, A, Bm, Cm).backward(torch.ones(B, S, H, P, device="cuda"))
+    elif what == "norm":
+        # RMSNorm forward + backward at the Llama shape (16384 tokens x 2048), x 64 MB
+        from ..ops import api
+        x = torch.randn(16384, 2048, device="cuda").bfloat16().requires_grad_()
+        w = torch.nn.Parameter(torch.ones(2048, device="cuda").bfloat16())
+        for _ in range(3):
+            api.rmsnorm(x, w, 1e-5).backward(torch.ones(16384, 2048, device="cuda").bfloat16())
+    elif what == "conv1d":
+        # causal depthwise conv1d (k = 4) + SiLU at the hybrid's Mamba2 xBC shape
+        from ..ops import api
+        B, S, C = 16, 1024, 1792
+        x = torch.randn(B, S, C, device="cuda").bfloat16().requires_grad_()
+        w = torch.nn.Parameter((torch.randn(C, 1, 4, device="cuda") * 0.3).bfloat16())
+        b = torch.nn.Parameter(torch.zeros(C, device="cuda").bfloat16())
+        for _ in range(3):
+            api.causal_conv1d(x, w, b, True).backward(torch.ones(B, S, C, device="cuda").bfloat16())
+    elif what in ("swiglu", "qkv_rope"):
+        # Llama shapes: gate/up GEMM with the SwiGLU epilogue + down GEMM, or the QKV GEMM
+        # with the RoPE epilogue (16 q heads, 8 kv heads, head dim 128), forward + backward
+        from ..ops import api
+        T, H = 16384, 2048
+        x = (torch.randn(T, H, device="cuda") * 0.5).bfloat16().requires_grad_()
+        if what == "swiglu":
+            wgu = torch.nn.Parameter((torch.randn(2 * 5632, H, device="cuda") * 0.02).bfloat16())
+            wd = torch.nn.Parameter((torch.randn(H, 5632, device="cuda") * 0.02).bfloat16())
+            f = lambda: api.swiglu_mlp(x, wgu, wd)
+            gy = torch.ones(T, H, device="cuda").bfloat16()
+        else:
+            w = torch.nn.Parameter((torch.randn(4096, H, device="cuda") * 0.02).bfloat16())
+            ang = torch.arange(2048, device="cuda")[:, None].float() * torch.pow(
+                10000.0, -torch.arange(64, device="cuda").float() / 64)[None, :]
+            cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+            xs = x.view(8, 2048, H)
+            f = lambda: api.qkv_rope(xs, w, cos, sin, 128, 2048, 1024)
+            gy = torch.ones(8, 2048, 4096, device="cuda").bfloat16()
+        for _ in range(3):
+            f().backward(gy)
+    elif what == "ce":
+        # lm_head GEMM with the cross-entropy epilogue over the 128354-token vocabulary, 4096 tokens
+        from ..ops import api
+        T, H, V = 4096, 2048, 128354
+        x = (torch.randn(T, H, device="cuda") * 0.5).bfloat16().requires_grad_()
+        w = torch.nn.Parameter((torch.randn(V, H, device="cuda") * 0.02).bfloat16())
+        tgt = torch.randint(0, V, (T,), device="cuda")
+        for _ in range(3):
+            api.linear_cross_entropy(x, w, tgt).backward()
+    elif what == "fa_mla":
+        # latent attention of the hybrid config: 12 heads, q/k head dim 64 + 32 RoPE, v 64
+        from ..ops.flash import FlashAttention
+        B, S, H, Dqk, Dv = 4, 1024, 12, 96, 64
+        q = torch.randn(B, S, H, Dqk, device="cuda").bfloat16().requires_grad_()
+        k = torch.randn(B, S, H, Dqk, device="cuda").bfloat16().requires_grad_()
+        v = torch.randn(B, S, H, Dv, device="cuda").bfloat16().requires_grad_()
+        for _ in range(3):
+            FlashAttention.apply(q, k, v, 1.0 / math.sqrt(Dqk), True).backward(
+                torch.ones(B, S, H, Dv, device="cuda").bfloat16())
+    elif what == "moe":
+        # router top-8 of 64 + grouped expert SwiGLU GEMMs at the MoE config's shapes, 4096 tokens
+        from ..ops.moe_kernels import GroupedExperts, RouterTopK
+        T, H, E, k, I = 4096, 2048, 64, 8, 1024
+        x = (torch.randn(T, H, device="cuda") * 0.5).bfloat16().requires_grad_()
+        wr = torch.nn.Parameter((torch.randn(E, H, device="cuda") * 0.02).bfloat16())
+        wgu = torch.nn.Parameter((torch.randn(E, 2 * I, H, device="cuda") * 0.02).bfloat16())
+        wd = torch.nn.Parameter((torch.randn(E, H, I, device="cuda") * 0.02).bfloat16())
+        for _ in range(3):
+            topi, topw, usage, _ = RouterTopK.apply(x @ wr.t(), k)
+            y = GroupedExperts.apply(x, topi, topw, wgu, wd, None)
+            (y.float().sum() + usage.sum()).backward()
+    elif what == "m3_bc":
+        # Mamba3 B/C prologue (norm + bias + complex RoPE + <B, C>) at the Mamba3 config's
+        # shape: 4 x 4096 tokens, 32 heads, one B/C group of state 128
+        from ..ops.ssd_tc import Mamba3BC
+        B, S, H, G = 4, 4096, 32, 1
+        bc = torch.randn(B, S, 2 * G * 128, device="cuda").bfloat16().requires_grad_()
+        w = torch.nn.Parameter(torch.ones(128, device="cuda").bfloat16())
+        bb = torch.nn.Parameter(torch.ones(H, 128, device="cuda").bfloat16())
+        cb = torch.nn.Parameter(torch.ones(H, 128, device="cuda").bfloat16())
+        ang = torch.randn(B, S, H, 64, device="cuda") * 10
+        for _ in range(3):
+            bo, co, dot = Mamba3BC.apply(bc[..., :128], bc[..., 128:], w, bb, cb, ang, H, 1e-6)
+            (bo.float().sum() + co.float().sum() + dot.sum()).backward()
+    elif what == "adamw":
+        # global-norm + clip + AdamW over 128 M bf16 parameters (f32 master, m, v, grad)
+        from ..optim import AdamW, AdamWConfig, FlatParams
+        p = torch.nn.Parameter((torch.randn(128 << 20, device="cuda") * 0.02).bfloat16())
+        opt = AdamW(FlatParams([("w", p)], torch.device("cuda")), AdamWConfig(lr=1e-4, max_grad_norm=1.0))
+        for _ in range(3):
+            opt.flat.grad.normal_()
+            opt.step()
+    else:
+        raise SystemExit(f"unknown kernel target {what!r}")
     torch.cuda.synchronize()
     print(f"{what}: ok")
 
@@ -237,7 +328,8 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attn", "ssm", "once"])
     ap.add_argument("--kernel", default="fa_fwd",
-                    help="for 'once': fa_fwd | fa_bwd | gemm | gemm_dw | ssd_m2 | ssd_m3")
+                    help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_dw | ssd_m2 | ssd_m3 | norm | "
+                         "conv1d | swiglu | qkv_rope | ce | moe | m3_bc | adamw")
     ap.add_argument("--shapes", nargs="*", default=None, help="M,N,K[,layout] with layout nn|nt|tt")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)

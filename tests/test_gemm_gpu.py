@@ -175,3 +175,33 @@ def test_gemm_splitk_accumulate(M, N, K):
     mm(a, b, a_t=True, b_t=True, out=out, beta=1.0)
     ref = base + a.float().t() @ b.float()
     assert _rel(out, ref) < 1e-4
+
+
+def test_gemm_first_cuda_call_of_a_new_thread():
+    """Autograd runs backward on its own thread; a GEMM there may be the thread's first CUDA
+    work, before any runtime call has made the context current (tensor-map encoding is a
+    driver call)."""
+    import threading
+    from oxidizr_b200.ops._C import status
+    from oxidizr_b200.ops.gemm import mm
+    torch.manual_seed(0)
+    a = torch.randn(512, 256, device="cuda").bfloat16()
+    b = torch.randn(384, 256, device="cuda").bfloat16()
+    out = torch.empty(512, 384, device="cuda", dtype=torch.bfloat16)
+    status(a.device)
+    torch.cuda.synchronize()
+    err = []
+
+    def work():
+        try:
+            mm(a, b, out=out)
+        except Exception as e:  # noqa: BLE001 - reported below
+            err.append(e)
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join()
+    assert not err, err
+    torch.cuda.synchronize()
+    ref = a.float() @ b.float().t()
+    assert (out.float() - ref).abs().max().item() < 0.05 * ref.abs().max().item()

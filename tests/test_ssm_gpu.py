@@ -9,9 +9,9 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-8)).item()
 
 
-@pytest.mark.parametrize("K", [2, 4])
+@pytest.mark.parametrize("K", [2, 3, 4])
 @pytest.mark.parametrize("act", [True, False])
-@pytest.mark.parametrize("B,S,C", [(2, 100, 64), (1, 300, 1792), (3, 64, 8)])
+@pytest.mark.parametrize("B,S,C", [(2, 100, 64), (1, 300, 1792), (3, 64, 8), (4, 1024, 1792)])
 def test_conv1d(K, act, B, S, C):
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops.ssm_kernels import CausalConv1d
