@@ -78,6 +78,8 @@ void launch_gemm_rope(const Mat& x, const Mat& w, void* out, int64_t ldo, const 
   use_pairs(p);
   OXI_CHECK(hd == 64 || hd == 128, "RoPE epilogue supports head_dim 64 or 128");
   OXI_CHECK(q_cols % hd == 0 && k_cols % hd == 0 && p.N % hd == 0, "RoPE regions must be whole heads");
+  OXI_CHECK((reinterpret_cast<uintptr_t>(cos) & 15) == 0 && (reinterpret_cast<uintptr_t>(sin) & 15) == 0,
+            "RoPE cos/sin tables must be 16-byte aligned");
   p.D = out;
   p.ldd = ldo;
   p.vec_ok = aligned16(out, ldo, 2);

@@ -575,6 +575,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int col = n0 + c * 32;
           const int in_head = (c * 32) % hd;   // tiles start at head boundaries (BN % hd == 0)
           if (in_head >= half) continue;        // handled with its partner
+          const bool rot = col < p.rope_q_cols + p.rope_k_cols;
+          // cos / sin of this row's position: 16-byte loads issued before the TMEM loads so
+          // their latency overlaps (table rows are 16-byte aligned, in_head % 32 == 0)
+          float cj[32], sj[32];
+          if (rot) {
+            const float4* cs4 = reinterpret_cast<const float4*>(p.rope_cos + (int64_t)pos * half + in_head);
+            const float4* sn4 = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)pos * half + in_head);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 cv = __ldg(cs4 + q), sv = __ldg(sn4 + q);
+              cj[4 * q] = cv.x; cj[4 * q + 1] = cv.y; cj[4 * q + 2] = cv.z; cj[4 * q + 3] = cv.w;
+              sj[4 * q] = sv.x; sj[4 * q + 1] = sv.y; sj[4 * q + 2] = sv.z; sj[4 * q + 3] = sv.w;
+            }
+          }
           uint32_t r1[32], r2[32];
           tmem_ld32(tbase + c * 32, r1);
           tmem_ld32(tbase + (c + pair_off) * 32, r2);
@@ -586,16 +600,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           float x1[32], x2[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) { x1[j] = __uint_as_float(r1[j]); x2[j] = __uint_as_float(r2[j]); }
-          const bool rot = col < p.rope_q_cols + p.rope_k_cols;
           if (rot) {
-            const float* cs = p.rope_cos + (int64_t)pos * half + in_head;
-            const float* sn = p.rope_sin + (int64_t)pos * half + in_head;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float cj = cs[j], sj = sn[j];
               const float a = x1[j], b = x2[j];
-              x1[j] = a * cj - b * sj;
-              x2[j] = b * cj + a * sj;
+              x1[j] = a * cj[j] - b * sj[j];
+              x2[j] = b * cj[j] + a * sj[j];
             }
           }
           __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
