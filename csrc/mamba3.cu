@@ -62,6 +62,18 @@ __device__ __forceinline__ void round4(float* v) {
   for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(__float2bfloat16(v[i]));
 }
 
+// (already normalised) n [4] + bias -> rotated [4] for one lane
+__device__ __forceinline__ void bias_rot(const float* nrm, const float* bias, float c0, float s0, float c1, float s1,
+                                         float* out) {
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = nrm[i] + bias[i];
+  out[0] = n[0] * c0 - n[1] * s0;
+  out[1] = n[0] * s0 + n[1] * c0;
+  out[2] = n[2] * c1 - n[3] * s1;
+  out[3] = n[2] * s1 + n[3] * c1;
+}
+
 // raw [4] -> rotated [4] for one lane; returns nothing, fills out
 __device__ __forceinline__ void norm_bias_rot(const float* raw, float rinv, const float* w, const float* bias,
                                               float c0, float s0, float c1, float s1, float* out) {
@@ -251,6 +263,153 @@ __global__ void __launch_bounds__(256) m3_bc_bwd_kernel(const __nv_bfloat16* __r
   }
 }
 
+// Heads-per-warp variant for one B/C group (G == 1) and H == 8 * HPW: a block takes tiles of
+// 8 tokens; warp w owns heads w, w + 8, ... for the whole kernel, so their bias gradients stay in
+// registers (no shared-memory atomics).  Per tile: (A) warp w normalises token w's raw rows into
+// shared memory; (B) every warp runs its heads over the 8 tokens and leaves, per token, the sum
+// over its heads of the normalised-row gradient in its own shared slot; (C) warp w adds the 8
+// slots of token w and runs the RMSNorm backward.
+// (four or more heads per warp keep every head's loads in flight at once: one block per SM
+// with the whole register file instead of spilling at 128 registers)
+template <typename GT, int HPW>
+__global__ void __launch_bounds__(256, HPW >= 4 ? 1 : 2) m3_bc_bwd_hw_kernel(
+    const __nv_bfloat16* __restrict__ braw, const __nv_bfloat16* __restrict__ craw, int64_t ldr,
+    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ bbias, const __nv_bfloat16* __restrict__ cbias,
+    const float* __restrict__ ang, const GT* __restrict__ db2, const GT* __restrict__ dc2,
+    const float* __restrict__ dbcdot, int64_t tokens, float eps, float* __restrict__ dbraw, float* __restrict__ dcraw,
+    int64_t ldd, float* __restrict__ dw, float* __restrict__ dbb, float* __restrict__ dcb, float* __restrict__ dang,
+    float* __restrict__ part) {
+  constexpr int TT = 8, H = 8 * HPW;
+  extern __shared__ float4 smem4[];
+  float4* s_nb = smem4;                 // [TT][32]   normalised x r w rows (4 elements per lane)
+  float4* s_nc = s_nb + TT * 32;
+  float4* s_gb = s_nc + TT * 32;        // [8 warps][TT][32] per-warp head sums of the gradient
+  float4* s_gc = s_gb + 8 * TT * 32;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float wv[4];
+  load4(w + lane * 4, wv);
+  float accb[HPW][4], accc[HPW][4];
+#pragma unroll
+  for (int hi = 0; hi < HPW; ++hi)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) accb[hi][i] = accc[hi][i] = 0.f;
+  float dw_acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int64_t t0 = (int64_t)blockIdx.x * TT; t0 < tokens; t0 += (int64_t)gridDim.x * TT) {
+    // (A) token t0 + wid
+    const int64_t tw = t0 + wid;
+    float rb[4] = {0.f, 0.f, 0.f, 0.f}, rc[4] = {0.f, 0.f, 0.f, 0.f}, rib = 0.f, ric = 0.f;
+    if (tw < tokens) {
+      load4(braw + tw * ldr + lane * 4, rb);
+      load4(craw + tw * ldr + lane * 4, rc);
+      const float sb = warp_sum(rb[0] * rb[0] + rb[1] * rb[1] + rb[2] * rb[2] + rb[3] * rb[3]);
+      const float sc = warp_sum(rc[0] * rc[0] + rc[1] * rc[1] + rc[2] * rc[2] + rc[3] * rc[3]);
+      rib = rsqrtf(sb / M3N + eps);
+      ric = rsqrtf(sc / M3N + eps);
+    }
+    s_nb[wid * 32 + lane] = make_float4(rb[0] * rib * wv[0], rb[1] * rib * wv[1], rb[2] * rib * wv[2], rb[3] * rib * wv[3]);
+    s_nc[wid * 32 + lane] = make_float4(rc[0] * ric * wv[0], rc[1] * ric * wv[1], rc[2] * ric * wv[2], rc[3] * ric * wv[3]);
+    __syncthreads();
+    // (B) this warp's heads over the tile's tokens
+    const int nt = tokens - t0 < TT ? (int)(tokens - t0) : TT;
+    for (int t = 0; t < nt; ++t) {
+      const int64_t tok = t0 + t;
+      const float4 nb4 = s_nb[t * 32 + lane], nc4 = s_nc[t * 32 + lane];
+      float gsb[4] = {0.f, 0.f, 0.f, 0.f}, gsc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int hi = 0; hi < HPW; ++hi) {
+        const int64_t it = tok * H + wid + 8 * hi;
+        float dB[4], dC[4];
+        load_grad4(db2 + it * M3N + lane * 4, dB);
+        load_grad4(dc2 + it * M3N + lane * 4, dC);
+        const float2 a = *reinterpret_cast<const float2*>(ang + it * (M3N / 2) + lane * 2);
+        const float gdot = dbcdot ? dbcdot[it] : 0.f;
+        float s0, c0, s1, c1;
+        rot_sincos(a.x, &s0, &c0);
+        rot_sincos(a.y, &s1, &c1);
+        const float nbv[4] = {nb4.x, nb4.y, nb4.z, nb4.w}, ncv[4] = {nc4.x, nc4.y, nc4.z, nc4.w};
+        float bb[4], cb[4], ob[4], oc[4];  // per-head biases: L1-resident
+        load4(bbias + (wid + 8 * hi) * M3N + lane * 4, bb);
+        load4(cbias + (wid + 8 * hi) * M3N + lane * 4, cb);
+        bias_rot(nbv, bb, c0, s0, c1, s1, ob);
+        bias_rot(ncv, cb, c0, s0, c1, s1, oc);
+        if (dbcdot) {
+          float rob[4] = {ob[0], ob[1], ob[2], ob[3]}, roc[4] = {oc[0], oc[1], oc[2], oc[3]};
+          round4(rob);
+          round4(roc);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            dB[i] += gdot * roc[i];
+            dC[i] += gdot * rob[i];
+          }
+        }
+        const float da0 = dB[0] * (-ob[1]) + dB[1] * ob[0] + dC[0] * (-oc[1]) + dC[1] * oc[0];
+        const float da1 = dB[2] * (-ob[3]) + dB[3] * ob[2] + dC[2] * (-oc[3]) + dC[3] * oc[2];
+        *reinterpret_cast<float2*>(dang + it * (M3N / 2) + lane * 2) = make_float2(da0, da1);
+        float nb[4], nc[4];
+        nb[0] = dB[0] * c0 + dB[1] * s0;  nb[1] = -dB[0] * s0 + dB[1] * c0;
+        nb[2] = dB[2] * c1 + dB[3] * s1;  nb[3] = -dB[2] * s1 + dB[3] * c1;
+        nc[0] = dC[0] * c0 + dC[1] * s0;  nc[1] = -dC[0] * s0 + dC[1] * c0;
+        nc[2] = dC[2] * c1 + dC[3] * s1;  nc[3] = -dC[2] * s1 + dC[3] * c1;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          accb[hi][i] += nb[i];
+          accc[hi][i] += nc[i];
+          gsb[i] += nb[i];
+          gsc[i] += nc[i];
+        }
+      }
+      s_gb[(wid * TT + t) * 32 + lane] = make_float4(gsb[0], gsb[1], gsb[2], gsb[3]);
+      s_gc[(wid * TT + t) * 32 + lane] = make_float4(gsc[0], gsc[1], gsc[2], gsc[3]);
+    }
+    __syncthreads();
+    // (C) RMSNorm backward of token t0 + wid: u = w * g
+    if (tw < tokens) {
+      float gb[4] = {0.f, 0.f, 0.f, 0.f}, gc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 x = s_gb[(q * TT + wid) * 32 + lane], y = s_gc[(q * TT + wid) * 32 + lane];
+        gb[0] += x.x; gb[1] += x.y; gb[2] += x.z; gb[3] += x.w;
+        gc[0] += y.x; gc[1] += y.y; gc[2] += y.z; gc[3] += y.w;
+      }
+      float ub[4], uc[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ub[i] = wv[i] * gb[i];
+        uc[i] = wv[i] * gc[i];
+        dw_acc[i] += gb[i] * rb[i] * rib + gc[i] * rc[i] * ric;
+      }
+      const float pb = warp_sum(ub[0] * rb[0] + ub[1] * rb[1] + ub[2] * rb[2] + ub[3] * rb[3]) / M3N;
+      const float pc = warp_sum(uc[0] * rc[0] + uc[1] * rc[1] + uc[2] * rc[2] + uc[3] * rc[3]) / M3N;
+      const float rb3 = rib * rib * rib * pb, rc3 = ric * ric * ric * pc;
+      *reinterpret_cast<float4*>(dbraw + tw * ldd + lane * 4) =
+          make_float4(rib * ub[0] - rb[0] * rb3, rib * ub[1] - rb[1] * rb3, rib * ub[2] - rb[2] * rb3,
+                      rib * ub[3] - rb[3] * rb3);
+      *reinterpret_cast<float4*>(dcraw + tw * ldd + lane * 4) =
+          make_float4(ric * uc[0] - rc[0] * rc3, ric * uc[1] - rc[1] * rc3, ric * uc[2] - rc[2] * rc3,
+                      ric * uc[3] - rc[3] * rc3);
+    }
+    __syncthreads();  // the next tile rewrites s_nb / s_gb
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) atomicAdd(dw + lane * 4 + i, dw_acc[i]);
+#pragma unroll
+  for (int hi = 0; hi < HPW; ++hi) {
+    const int e = (wid + 8 * hi) * M3N + lane * 4;
+    if (part) {
+      float* pb = part + (int64_t)blockIdx.x * 2 * H * M3N;
+      *reinterpret_cast<float4*>(pb + e) = make_float4(accb[hi][0], accb[hi][1], accb[hi][2], accb[hi][3]);
+      *reinterpret_cast<float4*>(pb + H * M3N + e) =
+          make_float4(accc[hi][0], accc[hi][1], accc[hi][2], accc[hi][3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        atomicAdd(dbb + e + i, accb[hi][i]);
+        atomicAdd(dcb + e + i, accc[hi][i]);
+      }
+    }
+  }
+}
+
 // out[c] += sum over a slice of the blocks' partials [G][2 * HN] (c < HN -> dbb, else dcb)
 __global__ void m3_part_sum_kernel(const float* __restrict__ part, int G, int HN, float* __restrict__ dbb,
                                    float* __restrict__ dcb) {
@@ -296,7 +455,25 @@ void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const voi
   const auto* bb = reinterpret_cast<const __nv_bfloat16*>(bbias);
   const auto* cb = reinterpret_cast<const __nv_bfloat16*>(cbias);
   const unsigned grid = (unsigned)std::max<int64_t>(blocks, 1);
-  if (grads_bf16) {
+  const int64_t tokens = (int64_t)B * S;
+  if (G == 1 && (H == 8 || H == 16 || H == 32 || H == 64)) {
+    const int hsmem = (2 * 8 + 2 * 8 * 8) * 32 * (int)sizeof(float4);  // 72 KB
+    auto go = [&](auto kern, const auto* dbp, const auto* dcp) {
+      OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, hsmem));
+      kern<<<grid, 256, hsmem, st>>>(br, cr, ldr, wb, bb, cb, ang, dbp, dcp, dbcdot, tokens, eps, dbraw, dcraw, ldd,
+                                     dw, dbb, dcb, dang, part);
+    };
+    const auto* dbh = reinterpret_cast<const __nv_bfloat16*>(db);
+    const auto* dch = reinterpret_cast<const __nv_bfloat16*>(dc);
+    const auto* dbf = reinterpret_cast<const float*>(db);
+    const auto* dcf = reinterpret_cast<const float*>(dc);
+    switch (H) {
+      case 8: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 1>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 1>, dbf, dcf); break;
+      case 16: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 2>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 2>, dbf, dcf); break;
+      case 32: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 4>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 4>, dbf, dcf); break;
+      default: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 8>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 8>, dbf, dcf); break;
+    }
+  } else if (grads_bf16) {
     auto kern = m3_bc_bwd_kernel<__nv_bfloat16>;
     if (smem > 48 * 1024) OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<grid, 256, smem, st>>>(br, cr, ldr, wb, bb, cb, ang, reinterpret_cast<const __nv_bfloat16*>(db),

@@ -310,6 +310,18 @@ def run_once(what: str):
         for _ in range(3):
             bo, co, dot = Mamba3BC.apply(bc[..., :128], bc[..., 128:], w, bb, cb, ang, H, 1e-6)
             (bo.float().sum() + co.float().sum() + dot.sum()).backward()
+    elif what == "mamba1":
+        # Mamba1 selective scan forward + backward (state 16, f32 in / out) at a hidden-768 block:
+        # 4 x 1024 tokens, d_inner 1536
+        from ..ops.ssm_kernels import Mamba1Scan
+        B, S, D, N = 4, 1024, 1536, 16
+        u = torch.randn(B, S, D, device="cuda").requires_grad_()
+        dl = (torch.rand(B, S, D, device="cuda") * 0.1).requires_grad_()
+        A = (torch.rand(D, N, device="cuda") + 0.5).requires_grad_()
+        Bm = torch.randn(B, S, N, device="cuda").requires_grad_()
+        Cm = torch.randn(B, S, N, device="cuda").requires_grad_()
+        for _ in range(3):
+            Mamba1Scan.apply(u, dl, A, Bm, Cm, 30.0).backward(torch.ones(B, S, D, device="cuda"))
     elif what == "adamw":
         # global-norm + clip + AdamW over 128 M bf16 parameters (f32 master, m, v, grad)
         from ..optim import AdamW, AdamWConfig, FlatParams
@@ -329,7 +341,7 @@ def main(argv=None):
     ap.add_argument("what", choices=["gemm", "attn", "ssm", "once"])
     ap.add_argument("--kernel", default="fa_fwd",
                     help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_dw | ssd_m2 | ssd_m3 | norm | "
-                         "conv1d | swiglu | qkv_rope | ce | moe | m3_bc | adamw")
+                         "conv1d | swiglu | qkv_rope | ce | moe | m3_bc | mamba1 | adamw")
     ap.add_argument("--shapes", nargs="*", default=None, help="M,N,K[,layout] with layout nn|nt|tt")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)

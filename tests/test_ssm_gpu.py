@@ -210,12 +210,14 @@ def test_angle_cumsum_kernel():
     assert _rel(dt.grad, dr.grad) < 1e-5
 
 
-def test_mamba3_bc_prologue_kernel():
-    """Fused B/C prologue vs torch: rmsnorm + bias + rotation, <B, C>, and grads."""
+@pytest.mark.parametrize("B,S,H,G", [(2, 64, 4, 2), (1, 100, 32, 1), (2, 40, 16, 1), (1, 24, 64, 1), (1, 36, 8, 1)])
+def test_mamba3_bc_prologue_kernel(B, S, H, G):
+    """Fused B/C prologue vs torch: rmsnorm + bias + rotation, <B, C>, and grads (one B/C group
+    with 8, 16, 32 or 64 heads takes the heads-per-warp backward)."""
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops.ssd_tc import Mamba3BC
     torch.manual_seed(7)
-    B, S, H, G, N = 2, 64, 4, 2, 128
+    N = 128
     wide = torch.randn(B, S, 2 * G * N + 8, device="cuda").bfloat16()
     braw = wide[..., :G * N].detach().requires_grad_()
     craw = wide[..., G * N:2 * G * N].detach().requires_grad_()
