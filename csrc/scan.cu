@@ -28,8 +28,12 @@
 //
 // Mamba1 (mamba.rs:212-291): per channel d, state h (N = 16):
 //   h_t = exp(delta_t A_d) h_{t-1} + delta_t x_t B_t ;  y_t = C_t . h_t
-// one thread per (b, d); the backward reads the per-step states the forward
-// saved.
+// The upstream clamp of every state to +-clamp makes the recurrence nonlinear, so
+// it stays sequential in t; the parallelism is (b, d, n): a half-warp per channel,
+// one lane per state, y / du / d delta as 16-lane shuffle sums.  The backward reads
+// the per-step states the forward saved; its dB / dC terms (sums over channels)
+// are staged per 32-step chunk in shared memory, summed over the block's warps and
+// added with one atomic per (step, n) per block.
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -233,76 +237,101 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32) ssm_scan_bwd_kernel(ScanArgs 
 // ---------------------------------------------------------------- Mamba1
 constexpr int M1N = 16;
 
-__global__ void mamba1_fwd_kernel(const float* __restrict__ u, const float* __restrict__ delta,
-                                  const float* __restrict__ A, const float* __restrict__ Bm,
-                                  const float* __restrict__ Cm, float* __restrict__ y, float* __restrict__ hs,
-                                  int Bsz, int S, int Dch, float clamp) {
-  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (id >= (int64_t)Bsz * Dch) return;
-  const int b = (int)(id / Dch), d = (int)(id % Dch);
-  float h[M1N], Ad[M1N];
-#pragma unroll
-  for (int n = 0; n < M1N; ++n) {
-    h[n] = 0.f;
-    Ad[n] = A[d * M1N + n];
-  }
+constexpr int M1_CH = 32;  // backward chunk (steps) for the dB / dC staging
+
+// block = 8 warps x 2 channels x 16 states: 16 channels of one batch row; grid (ceil(D / 16), B)
+__global__ void __launch_bounds__(256) mamba1_fwd_kernel(const float* __restrict__ u, const float* __restrict__ delta,
+                                                         const float* __restrict__ A, const float* __restrict__ Bm,
+                                                         const float* __restrict__ Cm, float* __restrict__ y,
+                                                         float* __restrict__ hs, int S, int Dch, float clamp) {
+  const int lane = threadIdx.x & 31, n = lane & 15;
+  const int d = blockIdx.x * 16 + (threadIdx.x >> 5) * 2 + (lane >> 4);
+  const int b = blockIdx.y;
+  const bool live = d < Dch;
+  const float a = live ? A[d * M1N + n] : 0.f;
+  float h = 0.f;
+#pragma unroll 4
   for (int t = 0; t < S; ++t) {
     const int64_t r = (int64_t)b * S + t;
-    const float dl = delta[r * Dch + d], xv = u[r * Dch + d];
-    float acc = 0.f;
+    const float dl = live ? delta[r * Dch + d] : 0.f, xv = live ? u[r * Dch + d] : 0.f;
+    const float bv = Bm[r * M1N + n], cv = Cm[r * M1N + n];
+    float v = __expf(dl * a) * h + dl * xv * bv;
+    if (clamp > 0.f) v = fminf(fmaxf(v, -clamp), clamp);
+    h = v;
+    if (live) hs[(r * Dch + d) * M1N + n] = v;
+    float p = v * cv;
 #pragma unroll
-    for (int n = 0; n < M1N; ++n) {
-      float v = __expf(dl * Ad[n]) * h[n] + dl * xv * Bm[r * M1N + n];
-      if (clamp > 0.f) v = fminf(fmaxf(v, -clamp), clamp);
-      h[n] = v;
-      acc += v * Cm[r * M1N + n];
-      hs[(r * Dch + d) * M1N + n] = v;
-    }
-    y[r * Dch + d] = acc;
+    for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+    if (live && n == 0) y[r * Dch + d] = p;
   }
 }
 
-__global__ void mamba1_bwd_kernel(const float* __restrict__ u, const float* __restrict__ delta,
-                                  const float* __restrict__ A, const float* __restrict__ Bm,
-                                  const float* __restrict__ Cm, const float* __restrict__ hs,
-                                  const float* __restrict__ dy, float* __restrict__ du, float* __restrict__ ddelta,
-                                  float* __restrict__ dA, float* __restrict__ dB, float* __restrict__ dC, int Bsz,
-                                  int S, int Dch, float clamp) {
-  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (id >= (int64_t)Bsz * Dch) return;
-  const int b = (int)(id / Dch), d = (int)(id % Dch);
-  float g[M1N], Ad[M1N], dAd[M1N];
-#pragma unroll
-  for (int n = 0; n < M1N; ++n) {
-    g[n] = 0.f;
-    Ad[n] = A[d * M1N + n];
-    dAd[n] = 0.f;
-  }
-  for (int t = S - 1; t >= 0; --t) {
-    const int64_t r = (int64_t)b * S + t;
-    const float dl = delta[r * Dch + d], xv = u[r * Dch + d], gy = dy[r * Dch + d];
-    float dxv = 0.f, ddl = 0.f;
-#pragma unroll
-    for (int n = 0; n < M1N; ++n) {
-      const float hn = hs[(r * Dch + d) * M1N + n];
-      const float hp = t > 0 ? hs[((r - 1) * Dch + d) * M1N + n] : 0.f;
+__global__ void __launch_bounds__(256) mamba1_bwd_kernel(const float* __restrict__ u, const float* __restrict__ delta,
+                                                         const float* __restrict__ A, const float* __restrict__ Bm,
+                                                         const float* __restrict__ Cm, const float* __restrict__ hs,
+                                                         const float* __restrict__ dy, float* __restrict__ du,
+                                                         float* __restrict__ ddelta, float* __restrict__ dA,
+                                                         float* __restrict__ dB, float* __restrict__ dC, int S,
+                                                         int Dch, float clamp) {
+  __shared__ float s_db[8][M1_CH][M1N], s_dc[8][M1_CH][M1N];
+  const int lane = threadIdx.x & 31, n = lane & 15, wid = threadIdx.x >> 5;
+  const int d = blockIdx.x * 16 + wid * 2 + (lane >> 4);
+  const int b = blockIdx.y;
+  const bool live = d < Dch;
+  const float a = live ? A[d * M1N + n] : 0.f;
+  const int64_t base = (int64_t)b * S;
+  float g = 0.f, dAacc = 0.f;
+  for (int t1 = S; t1 > 0; t1 -= M1_CH) {
+    const int t0 = t1 > M1_CH ? t1 - M1_CH : 0;
+    float hn = live ? hs[((base + t1 - 1) * Dch + d) * M1N + n] : 0.f;
+    for (int t = t1 - 1; t >= t0; --t) {
+      const int64_t r = base + t;
+      const float hp = (live && t > 0) ? hs[((r - 1) * Dch + d) * M1N + n] : 0.f;
+      const float dl = live ? delta[r * Dch + d] : 0.f, xv = live ? u[r * Dch + d] : 0.f;
+      const float gy = live ? dy[r * Dch + d] : 0.f;
       const float cv = Cm[r * M1N + n], bv = Bm[r * M1N + n];
-      g[n] += gy * cv;
-      atomicAdd(&dC[r * M1N + n], gy * hn);
-      // clamp: gradient passes only where the state was not clipped
-      if (clamp > 0.f && (hn >= clamp || hn <= -clamp)) g[n] = 0.f;
-      const float e = __expf(dl * Ad[n]);
-      ddl += g[n] * (Ad[n] * e * hp + xv * bv);
-      dAd[n] += g[n] * dl * e * hp;
-      dxv += g[n] * dl * bv;
-      atomicAdd(&dB[r * M1N + n], g[n] * dl * xv);
-      g[n] *= e;  // propagate to h_{t-1}
-    }
-    du[r * Dch + d] = dxv;
-    ddelta[r * Dch + d] = ddl;
-  }
+      g += gy * cv;
+      float cdc = gy * hn;
+      // clamp: the gradient passes only where the state was not clipped
+      if (clamp > 0.f && (hn >= clamp || hn <= -clamp)) g = 0.f;
+      const float e = __expf(dl * a);
+      float ddl = g * (a * e * hp + xv * bv);
+      dAacc += g * dl * e * hp;
+      float dxv = g * dl * bv;
+      float cdb = g * dl * xv;
+      g *= e;  // to h_{t-1}
 #pragma unroll
-  for (int n = 0; n < M1N; ++n) atomicAdd(&dA[d * M1N + n], dAd[n]);
+      for (int o = 8; o > 0; o >>= 1) {
+        ddl += __shfl_xor_sync(0xffffffffu, ddl, o);
+        dxv += __shfl_xor_sync(0xffffffffu, dxv, o);
+      }
+      cdc += __shfl_xor_sync(0xffffffffu, cdc, 16);  // the warp's two channels
+      cdb += __shfl_xor_sync(0xffffffffu, cdb, 16);
+      if (lane < 16) {
+        s_dc[wid][t - t0][n] = cdc;
+        s_db[wid][t - t0][n] = cdb;
+      }
+      if (live && n == 0) {
+        du[r * Dch + d] = dxv;
+        ddelta[r * Dch + d] = ddl;
+      }
+      hn = hp;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < (t1 - t0) * M1N; e += blockDim.x) {
+      const int j = e / M1N, k = e % M1N;
+      float sb = 0.f, sc = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        sb += s_db[w][j][k];
+        sc += s_dc[w][j][k];
+      }
+      atomicAdd(&dB[(base + t0 + j) * M1N + k], sb);
+      atomicAdd(&dC[(base + t0 + j) * M1N + k], sc);
+    }
+    __syncthreads();
+  }
+  if (live) atomicAdd(&dA[d * M1N + n], dAacc);
 }
 
 template <int NL, int PW>
@@ -370,7 +399,9 @@ void launch_mamba1_fwd(const float* u, const float* delta, const float* A, const
                        float* hs, int Bsz, int S, int Dch, float clamp, cudaStream_t st) {
   const int64_t n = (int64_t)Bsz * Dch;
   if (!n || !S) return;
-  mamba1_fwd_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(u, delta, A, Bm, Cm, y, hs, Bsz, S, Dch, clamp);
+  OXI_CHECK(Bsz <= 65535, "mamba1 scan: batch too large for one launch");
+  mamba1_fwd_kernel<<<dim3((unsigned)((Dch + 15) / 16), (unsigned)Bsz), 256, 0, st>>>(u, delta, A, Bm, Cm, y, hs, S,
+                                                                                     Dch, clamp);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -379,8 +410,9 @@ void launch_mamba1_bwd(const float* u, const float* delta, const float* A, const
                        int Bsz, int S, int Dch, float clamp, cudaStream_t st) {
   const int64_t n = (int64_t)Bsz * Dch;
   if (!n || !S) return;
-  mamba1_bwd_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(u, delta, A, Bm, Cm, hs, dy, du, ddelta, dA, dB, dC,
-                                                                 Bsz, S, Dch, clamp);
+  OXI_CHECK(Bsz <= 65535, "mamba1 scan: batch too large for one launch");
+  mamba1_bwd_kernel<<<dim3((unsigned)((Dch + 15) / 16), (unsigned)Bsz), 256, 0, st>>>(u, delta, A, Bm, Cm, hs, dy, du,
+                                                                                     ddelta, dA, dB, dC, S, Dch, clamp);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

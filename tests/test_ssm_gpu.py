@@ -80,11 +80,11 @@ def test_mamba3_scan(B, S, H, P, N):
 
 
 @pytest.mark.parametrize("clamp", [None, 30.0])
-def test_mamba1_scan(clamp):
+@pytest.mark.parametrize("B,S,D", [(2, 40, 96), (1, 70, 100)])
+def test_mamba1_scan(clamp, B, S, D):
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops import ssm
     torch.manual_seed(3)
-    B, S, D = 2, 40, 96
     u = torch.randn(B, S, D, device="cuda").requires_grad_()
     delta = (torch.rand(B, S, D, device="cuda") * 0.5).requires_grad_()
     A = (-torch.rand(D, 16, device="cuda") * 3).requires_grad_()
