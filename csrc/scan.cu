@@ -31,7 +31,8 @@
 // The upstream clamp of every state to +-clamp makes the recurrence nonlinear, so
 // it stays sequential in t; the parallelism is (b, d, n): a half-warp per channel,
 // one lane per state, y / du / d delta as 16-lane shuffle sums.  The backward reads
-// the per-step states the forward saved; its dB / dC terms (sums over channels)
+// the per-step states the forward saved; both kernels load the operands of their
+// next few steps while computing the current ones.  The dB / dC terms (sums over channels)
 // are staged per 32-step chunk in shared memory, summed over the block's warps and
 // added with one atomic per (step, n) per block.
 #include <cuda_runtime.h>
@@ -238,8 +239,11 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32) ssm_scan_bwd_kernel(ScanArgs 
 constexpr int M1N = 16;
 
 constexpr int M1_CH = 32;  // backward chunk (steps) for the dB / dC staging
+constexpr int M1_PFF = 8;  // forward steps whose operands are loaded one group ahead
+constexpr int M1_PFB = 4;  // backward steps per prefetch group (M1_CH is a multiple)
 
-// block = 8 warps x 2 channels x 16 states: 16 channels of one batch row; grid (ceil(D / 16), B)
+// block = 8 warps x 2 channels x 16 states: 16 channels of one batch row; grid (ceil(D / 16), B).
+// Each thread loads the operands of its next M1_PFF steps while it computes the current ones.
 __global__ void __launch_bounds__(256) mamba1_fwd_kernel(const float* __restrict__ u, const float* __restrict__ delta,
                                                          const float* __restrict__ A, const float* __restrict__ Bm,
                                                          const float* __restrict__ Cm, float* __restrict__ y,
@@ -249,20 +253,59 @@ __global__ void __launch_bounds__(256) mamba1_fwd_kernel(const float* __restrict
   const int b = blockIdx.y;
   const bool live = d < Dch;
   const float a = live ? A[d * M1N + n] : 0.f;
-  float h = 0.f;
-#pragma unroll 4
-  for (int t = 0; t < S; ++t) {
-    const int64_t r = (int64_t)b * S + t;
-    const float dl = live ? delta[r * Dch + d] : 0.f, xv = live ? u[r * Dch + d] : 0.f;
-    const float bv = Bm[r * M1N + n], cv = Cm[r * M1N + n];
-    float v = __expf(dl * a) * h + dl * xv * bv;
-    if (clamp > 0.f) v = fminf(fmaxf(v, -clamp), clamp);
-    h = v;
-    if (live) hs[(r * Dch + d) * M1N + n] = v;
-    float p = v * cv;
+  const int64_t base = (int64_t)b * S;
+  auto load = [&](int tg, float* dl, float* xv, float* bv, float* cv) {
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-    if (live && n == 0) y[r * Dch + d] = p;
+    for (int i = 0; i < M1_PFF; ++i) {
+      const int t = tg + i;
+      const bool ok = t < S;
+      const int64_t r = base + (ok ? t : 0);
+      dl[i] = (live && ok) ? delta[r * Dch + d] : 0.f;
+      xv[i] = (live && ok) ? u[r * Dch + d] : 0.f;
+      bv[i] = ok ? Bm[r * M1N + n] : 0.f;
+      cv[i] = ok ? Cm[r * M1N + n] : 0.f;
+    }
+  };
+  float dl[M1_PFF], xv[M1_PFF], bv[M1_PFF], cv[M1_PFF];
+  load(0, dl, xv, bv, cv);
+  float h = 0.f;
+  for (int tg = 0; tg < S; tg += M1_PFF) {
+    float ndl[M1_PFF], nxv[M1_PFF], nbv[M1_PFF], ncv[M1_PFF];
+    if (tg + M1_PFF < S) load(tg + M1_PFF, ndl, nxv, nbv, ncv);
+    // decays and inputs of the group do not depend on h: computed together
+    float e[M1_PFF], wb[M1_PFF], p[M1_PFF];
+#pragma unroll
+    for (int i = 0; i < M1_PFF; ++i) {
+      e[i] = __expf(dl[i] * a);
+      wb[i] = dl[i] * xv[i] * bv[i];
+    }
+    // the sequential part: one FMA (and the clamp) per step
+#pragma unroll
+    for (int i = 0; i < M1_PFF; ++i) {
+      float v = e[i] * h + wb[i];
+      if (clamp > 0.f) v = fminf(fmaxf(v, -clamp), clamp);
+      h = v;
+      p[i] = v * cv[i];
+      if (live && tg + i < S) hs[((base + tg + i) * Dch + d) * M1N + n] = v;
+    }
+    // the group's 16-lane sums, shuffles of all steps interleaved per level
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < M1_PFF; ++i) p[i] += __shfl_xor_sync(0xffffffffu, p[i], o);
+    if (live && n < M1_PFF && tg + n < S) {
+      float yv = p[0];
+#pragma unroll
+      for (int i = 1; i < M1_PFF; ++i) yv = n == i ? p[i] : yv;
+      y[(base + tg + n) * Dch + d] = yv;
+    }
+#pragma unroll
+    for (int i = 0; i < M1_PFF; ++i) {
+      dl[i] = ndl[i];
+      xv[i] = nxv[i];
+      bv[i] = nbv[i];
+      cv[i] = ncv[i];
+    }
   }
 }
 
@@ -280,56 +323,95 @@ __global__ void __launch_bounds__(256) mamba1_bwd_kernel(const float* __restrict
   const bool live = d < Dch;
   const float a = live ? A[d * M1N + n] : 0.f;
   const int64_t base = (int64_t)b * S;
+  // group k holds steps S-1-k*PF .. S-PF-k*PF (descending); q: 0 h_{t-1}, 1 delta, 2 x, 3 dy, 4 C, 5 B
+  auto load = [&](int k, float (*q)[M1_PFB]) {
+#pragma unroll
+    for (int i = 0; i < M1_PFB; ++i) {
+      const int t = S - 1 - k * M1_PFB - i;
+      const bool ok = t >= 0;
+      const int64_t r = base + (ok ? t : 0);
+      q[0][i] = (live && t > 0) ? hs[((r - 1) * Dch + d) * M1N + n] : 0.f;
+      q[1][i] = (live && ok) ? delta[r * Dch + d] : 0.f;
+      q[2][i] = (live && ok) ? u[r * Dch + d] : 0.f;
+      q[3][i] = (live && ok) ? dy[r * Dch + d] : 0.f;
+      q[4][i] = ok ? Cm[r * M1N + n] : 0.f;
+      q[5][i] = ok ? Bm[r * M1N + n] : 0.f;
+    }
+  };
+  const int ngroups = (S + M1_PFB - 1) / M1_PFB;
+  constexpr int GPC = M1_CH / M1_PFB;  // groups per chunk (chunks are aligned from the top step)
+  float cur[6][M1_PFB];
+  load(0, cur);
+  float hn = live ? hs[((base + S - 1) * Dch + d) * M1N + n] : 0.f;
   float g = 0.f, dAacc = 0.f;
-  for (int t1 = S; t1 > 0; t1 -= M1_CH) {
-    const int t0 = t1 > M1_CH ? t1 - M1_CH : 0;
-    float hn = live ? hs[((base + t1 - 1) * Dch + d) * M1N + n] : 0.f;
-    for (int t = t1 - 1; t >= t0; --t) {
-      const int64_t r = base + t;
-      const float hp = (live && t > 0) ? hs[((r - 1) * Dch + d) * M1N + n] : 0.f;
-      const float dl = live ? delta[r * Dch + d] : 0.f, xv = live ? u[r * Dch + d] : 0.f;
-      const float gy = live ? dy[r * Dch + d] : 0.f;
-      const float cv = Cm[r * M1N + n], bv = Bm[r * M1N + n];
+  for (int k = 0; k < ngroups; ++k) {
+    float nxt[6][M1_PFB];
+    if (k + 1 < ngroups) load(k + 1, nxt);
+    const int t1 = S - M1_CH * (k / GPC), t0 = t1 > M1_CH ? t1 - M1_CH : 0;
+    // decays of the group first (independent of the adjoint); then the sequential adjoint chain;
+    // then the group's reductions with the shuffles of all steps interleaved per level
+    float e[M1_PFB], ddl[M1_PFB], dxv[M1_PFB], cdb[M1_PFB], cdc[M1_PFB];
+#pragma unroll
+    for (int i = 0; i < M1_PFB; ++i) e[i] = __expf(cur[1][i] * a);
+#pragma unroll
+    for (int i = 0; i < M1_PFB; ++i) {
+      const float hp = cur[0][i], dl = cur[1][i], xv = cur[2][i], gy = cur[3][i], cv = cur[4][i], bv = cur[5][i];
+      // steps past the start (t < 0) have zero inputs: their terms vanish
       g += gy * cv;
-      float cdc = gy * hn;
+      cdc[i] = gy * hn;
       // clamp: the gradient passes only where the state was not clipped
       if (clamp > 0.f && (hn >= clamp || hn <= -clamp)) g = 0.f;
-      const float e = __expf(dl * a);
-      float ddl = g * (a * e * hp + xv * bv);
-      dAacc += g * dl * e * hp;
-      float dxv = g * dl * bv;
-      float cdb = g * dl * xv;
-      g *= e;  // to h_{t-1}
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) {
-        ddl += __shfl_xor_sync(0xffffffffu, ddl, o);
-        dxv += __shfl_xor_sync(0xffffffffu, dxv, o);
-      }
-      cdc += __shfl_xor_sync(0xffffffffu, cdc, 16);  // the warp's two channels
-      cdb += __shfl_xor_sync(0xffffffffu, cdb, 16);
-      if (lane < 16) {
-        s_dc[wid][t - t0][n] = cdc;
-        s_db[wid][t - t0][n] = cdb;
-      }
-      if (live && n == 0) {
-        du[r * Dch + d] = dxv;
-        ddelta[r * Dch + d] = ddl;
-      }
+      ddl[i] = g * (a * e[i] * hp + xv * bv);
+      dAacc += g * dl * e[i] * hp;
+      dxv[i] = g * dl * bv;
+      cdb[i] = g * dl * xv;
+      g *= e[i];  // to h_{t-1}
       hn = hp;
     }
-    __syncthreads();
-    for (int e = threadIdx.x; e < (t1 - t0) * M1N; e += blockDim.x) {
-      const int j = e / M1N, k = e % M1N;
-      float sb = 0.f, sc = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        sb += s_db[w][j][k];
-        sc += s_dc[w][j][k];
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < M1_PFB; ++i) {
+        ddl[i] += __shfl_xor_sync(0xffffffffu, ddl[i], o);
+        dxv[i] += __shfl_xor_sync(0xffffffffu, dxv[i], o);
       }
-      atomicAdd(&dB[(base + t0 + j) * M1N + k], sb);
-      atomicAdd(&dC[(base + t0 + j) * M1N + k], sc);
+#pragma unroll
+    for (int i = 0; i < M1_PFB; ++i) {
+      cdc[i] += __shfl_xor_sync(0xffffffffu, cdc[i], 16);  // the warp's two channels
+      cdb[i] += __shfl_xor_sync(0xffffffffu, cdb[i], 16);
     }
-    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < M1_PFB; ++i) {
+      const int t = S - 1 - k * M1_PFB - i;
+      if (t < 0) break;
+      if (lane < 16) {
+        s_dc[wid][t - t0][n] = cdc[i];
+        s_db[wid][t - t0][n] = cdb[i];
+      }
+      if (live && n == 0) {
+        du[(base + t) * Dch + d] = dxv[i];
+        ddelta[(base + t) * Dch + d] = ddl[i];
+      }
+    }
+    if (k % GPC == GPC - 1 || k == ngroups - 1) {
+      __syncthreads();
+      for (int e = threadIdx.x; e < (t1 - t0) * M1N; e += blockDim.x) {
+        const int j = e / M1N, c = e % M1N;
+        float sb = 0.f, sc = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          sb += s_db[w][j][c];
+          sc += s_dc[w][j][c];
+        }
+        atomicAdd(&dB[(base + t0 + j) * M1N + c], sb);
+        atomicAdd(&dC[(base + t0 + j) * M1N + c], sc);
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < 6; ++q)
+#pragma unroll
+      for (int i = 0; i < M1_PFB; ++i) cur[q][i] = nxt[q][i];
   }
   if (live) atomicAdd(&dA[d * M1N + n], dAacc);
 }
