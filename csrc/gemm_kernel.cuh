@@ -526,39 +526,45 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       } else if constexpr (EPI == EPI_CE) {
+        // two 32-column chunks per TMEM round trip (both loads, then one wait)
         float run_max = -INFINITY, run_sum = 0.f;
         const int64_t tgt = row_ok ? p.targets[row] : -1;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
+        for (int c = 0; c < BN / 32; c += 2) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tbase + c * 32, r0);
+          tmem_ld32(tbase + (c + 1) * 32, r1);
           tc_wait_ld();
-          if (c == BN / 32 - 1) { tc_fence_before(); release_acc(acc); }
+          if (c + 2 == BN / 32) { tc_fence_before(); release_acc(acc); }
           const int col = n0 + c * 32;
-          const int nvalid = min(32, p.N - col);
+          const int nvalid = min(64, p.N - col);
           if (!row_ok || nvalid <= 0) continue;
-          float v[32];
+          float v[64];
           float cmax = -INFINITY;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            v[j] = __uint_as_float(r[j]) * p.alpha;
+          for (int j = 0; j < 64; ++j) {
+            v[j] = __uint_as_float(j < 32 ? r0[j] : r1[j - 32]) * p.alpha;
             if (j < nvalid) cmax = fmaxf(cmax, v[j]);
           }
           const float nmax = fmaxf(run_max, cmax);
           float s = 0.f;
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
+          for (int j = 0; j < 64; ++j)
             if (j < nvalid) s += __expf(v[j] - nmax);
           run_sum = run_sum * __expf(run_max - nmax) + s;
           run_max = nmax;
           if (tgt >= col && tgt < col + nvalid) {
             float tv = 0.f;
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
+            for (int j = 0; j < 64; ++j)
               if (col + j == tgt) tv = v[j];
             p.tgt_logit[row] = tv;
           }
-          if (Dp) store_bf16_row(reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col, v, nvalid, vec);
+          if (Dp) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
+            store_bf16_row(dst, v, min(32, nvalid), vec);
+            if (nvalid > 32) store_bf16_row(dst + 32, v + 32, nvalid - 32, vec);
+          }
         }
         if (row_ok) {
           p.part_max[(int64_t)row * p.tiles_n + tn] = run_max;
