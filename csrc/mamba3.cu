@@ -441,6 +441,26 @@ void launch_m3_bc_fwd(const void* braw, const void* craw, int64_t ldr, const voi
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
+namespace {
+// the shared-memory opt-in once per instantiation (outside any CUDA-graph capture: the
+// trainer runs eager steps before it captures one)
+template <typename GT, int HPW>
+void launch_bc_bwd_hw(unsigned grid, cudaStream_t st, const __nv_bfloat16* br, const __nv_bfloat16* cr, int64_t ldr,
+                      const __nv_bfloat16* wb, const __nv_bfloat16* bb, const __nv_bfloat16* cb, const float* ang,
+                      const GT* db, const GT* dc, const float* dbcdot, int64_t tokens, float eps, float* dbraw,
+                      float* dcraw, int64_t ldd, float* dw, float* dbb, float* dcb, float* dang, float* part) {
+  constexpr int kSmem = (2 * 8 + 2 * 8 * 8) * 32 * (int)sizeof(float4);  // 72 KB
+  auto kern = m3_bc_bwd_hw_kernel<GT, HPW>;
+  static bool attr = false;
+  if (!attr) {
+    OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    attr = true;
+  }
+  kern<<<grid, 256, kSmem, st>>>(br, cr, ldr, wb, bb, cb, ang, db, dc, dbcdot, tokens, eps, dbraw, dcraw, ldd, dw, dbb,
+                                 dcb, dang, part);
+}
+}  // namespace
+
 void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const void* w, const void* bbias,
                       const void* cbias, const float* ang, const void* db, const void* dc, bool grads_bf16,
                       const float* dbcdot, int B, int S, int H, int G, int N, float eps, float* dbraw, float* dcraw,
@@ -457,31 +477,41 @@ void launch_m3_bc_bwd(const void* braw, const void* craw, int64_t ldr, const voi
   const unsigned grid = (unsigned)std::max<int64_t>(blocks, 1);
   const int64_t tokens = (int64_t)B * S;
   if (G == 1 && (H == 8 || H == 16 || H == 32 || H == 64)) {
-    const int hsmem = (2 * 8 + 2 * 8 * 8) * 32 * (int)sizeof(float4);  // 72 KB
-    auto go = [&](auto kern, const auto* dbp, const auto* dcp) {
-      OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, hsmem));
-      kern<<<grid, 256, hsmem, st>>>(br, cr, ldr, wb, bb, cb, ang, dbp, dcp, dbcdot, tokens, eps, dbraw, dcraw, ldd,
-                                     dw, dbb, dcb, dang, part);
-    };
     const auto* dbh = reinterpret_cast<const __nv_bfloat16*>(db);
     const auto* dch = reinterpret_cast<const __nv_bfloat16*>(dc);
     const auto* dbf = reinterpret_cast<const float*>(db);
     const auto* dcf = reinterpret_cast<const float*>(dc);
+#define OXI_M3_HW(hpw)                                                                                            \
+  if (grads_bf16)                                                                                                 \
+    launch_bc_bwd_hw<__nv_bfloat16, hpw>(grid, st, br, cr, ldr, wb, bb, cb, ang, dbh, dch, dbcdot, tokens, eps, dbraw, \
+                                         dcraw, ldd, dw, dbb, dcb, dang, part);                                   \
+  else                                                                                                            \
+    launch_bc_bwd_hw<float, hpw>(grid, st, br, cr, ldr, wb, bb, cb, ang, dbf, dcf, dbcdot, tokens, eps, dbraw, dcraw, \
+                                 ldd, dw, dbb, dcb, dang, part);
     switch (H) {
-      case 8: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 1>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 1>, dbf, dcf); break;
-      case 16: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 2>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 2>, dbf, dcf); break;
-      case 32: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 4>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 4>, dbf, dcf); break;
-      default: grads_bf16 ? go(m3_bc_bwd_hw_kernel<__nv_bfloat16, 8>, dbh, dch) : go(m3_bc_bwd_hw_kernel<float, 8>, dbf, dcf); break;
+      case 8: OXI_M3_HW(1) break;
+      case 16: OXI_M3_HW(2) break;
+      case 32: OXI_M3_HW(4) break;
+      default: OXI_M3_HW(8) break;
     }
+#undef OXI_M3_HW
   } else if (grads_bf16) {
     auto kern = m3_bc_bwd_kernel<__nv_bfloat16>;
-    if (smem > 48 * 1024) OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    static bool attr = false;  // once, for the largest block (64 heads)
+    if (!attr) {
+      OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 64 * M3N * 4));
+      attr = true;
+    }
     kern<<<grid, 256, smem, st>>>(br, cr, ldr, wb, bb, cb, ang, reinterpret_cast<const __nv_bfloat16*>(db),
                                   reinterpret_cast<const __nv_bfloat16*>(dc), dbcdot, B, S, H, G, eps, dbraw, dcraw,
                                   ldd, dw, dbb, dcb, dang, part);
   } else {
     auto kern = m3_bc_bwd_kernel<float>;
-    if (smem > 48 * 1024) OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    static bool attr = false;
+    if (!attr) {
+      OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 64 * M3N * 4));
+      attr = true;
+    }
     kern<<<grid, 256, smem, st>>>(br, cr, ldr, wb, bb, cb, ang, reinterpret_cast<const float*>(db),
                                   reinterpret_cast<const float*>(dc), dbcdot, B, S, H, G, eps, dbraw, dcraw, ldd, dw,
                                   dbb, dcb, dang, part);
