@@ -169,6 +169,11 @@ def canary_gemm_sweep(device: torch.device) -> Dict[str, GuardReport]:
             for b_t in (False, True):
                 a = torch.randn((K, M) if a_t else (M, K), device=device).bfloat16()
                 b = torch.randn((K, N) if b_t else (N, K), device=device).bfloat16()
+                # 16-byte aligned rows for the TMA descriptors (else mm takes its torch path)
+                if a_t and M % 8:
+                    a = torch.nn.functional.pad(a, (0, 8 - M % 8))[:, :M]
+                if b_t and N % 8:
+                    b = torch.nn.functional.pad(b, (0, 8 - N % 8))[:, :N]
                 gb = Guarded((M, N), torch.bfloat16, device)
                 mm(a, b, a_t=a_t, b_t=b_t, out=gb.tensor)
                 gf = Guarded((M, N), torch.float32, device, fill=0.0)
