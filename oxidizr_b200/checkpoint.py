@@ -17,6 +17,7 @@ from __future__ import annotations
 import datetime
 import json
 import os
+import threading
 import re
 from typing import Dict, Optional, Tuple
 
@@ -29,8 +30,30 @@ from .utils.hashing import compute_file_hash, compute_model_config_hash
 _STEP_RE = re.compile(r"_step_(\d+)\.safetensors$")
 
 
+def _owns_storage(t: torch.Tensor) -> bool:
+    """A contiguous host tensor that is the whole of its storage (shares memory with nothing)."""
+    return (t.device.type == "cpu" and t.is_contiguous() and t.storage_offset() == 0
+            and t.untyped_storage().nbytes() == t.numel() * t.element_size())
+
+
 def _cpu_contig(sd: Dict[str, torch.Tensor]) -> Dict[str, torch.Tensor]:
-    return {k: v.detach().to("cpu").contiguous().clone() for k, v in sd.items()}
+    """Host tensors that safetensors accepts: views of a shared buffer (flat parameters) are
+    copied out; tensors that already own their storage are passed through once (a second
+    name for the same storage gets a copy)."""
+    out, seen = {}, set()
+    for k, v in sd.items():
+        v = v.detach()
+        if _owns_storage(v) and v.data_ptr() not in seen:
+            seen.add(v.data_ptr())
+            out[k] = v
+        else:
+            out[k] = v.to("cpu").contiguous().clone()
+    return out
+
+
+def host_snapshot(sd: Dict[str, torch.Tensor]) -> Dict[str, torch.Tensor]:
+    """Host copies, each owning its storage, taken now (the originals keep changing)."""
+    return {k: v.detach().to("cpu", copy=True).contiguous() for k, v in sd.items()}
 
 
 class CheckpointMeta:
@@ -166,6 +189,53 @@ def save_checkpoint(model, optimizer, step: int, model_cfg: ModelConfig, checkpo
     if max_checkpoints > 0:
         cleanup_old_checkpoints(checkpoint_dir, max_checkpoints)
     return path
+
+
+class OptimizerSnapshot:
+    """The parts of an optimizer that ``save_checkpoint`` reads, frozen at one step (host copies)."""
+
+    def __init__(self, step_count: int, state: Dict[str, torch.Tensor]):
+        self.step_count = step_count
+        self._state = state
+
+    def state_tensors(self) -> Dict[str, torch.Tensor]:
+        return self._state
+
+
+class AsyncCheckpointWriter:
+    """Writes checkpoint files on a background thread, so a training step only waits for the
+    device-to-host snapshot, not for serialisation and disk.  At most one write is in flight:
+    ``submit`` first waits for the previous one.  The thread is not a daemon, so the process
+    finishes a pending write before it exits; an error in a write is raised by the next
+    ``submit`` or ``wait``."""
+
+    def __init__(self):
+        self._thread: Optional[threading.Thread] = None
+        self._error: Optional[BaseException] = None
+
+    def submit(self, fn, *args, **kwargs) -> None:
+        self.wait()
+
+        def run():
+            try:
+                fn(*args, **kwargs)
+            except BaseException as e:  # noqa: BLE001 - handed to the training thread
+                self._error = e
+
+        self._thread = threading.Thread(target=run, name="oxidizr-checkpoint-writer", daemon=False)
+        self._thread.start()
+
+    def wait(self) -> None:
+        if self._thread is not None:
+            self._thread.join()
+            self._thread = None
+        if self._error is not None:
+            err, self._error = self._error, None
+            raise err
+
+    @property
+    def busy(self) -> bool:
+        return self._thread is not None and self._thread.is_alive()
 
 
 def cleanup_old_checkpoints(checkpoint_dir: str, max_checkpoints: int) -> None:

@@ -29,7 +29,8 @@ from typing import Callable, Optional
 
 import torch
 
-from .checkpoint import save_blazr_config_if_needed, save_checkpoint, save_final
+from .checkpoint import (AsyncCheckpointWriter, OptimizerSnapshot, host_snapshot, save_blazr_config_if_needed,
+                         save_checkpoint, save_final)
 from .config import LitConfig, serde_json_dumps
 
 
@@ -100,6 +101,8 @@ class Trainer:
         self._graph_in = None
         self._graph_out = None
         self._graph_launches = 0
+        # rank 0 writes periodic checkpoints on a background thread (OXI_SYNC_CHECKPOINT=1: inline)
+        self._writer = None if os.environ.get("OXI_SYNC_CHECKPOINT", "0") == "1" else AsyncCheckpointWriter()
 
     def _graph_eligible(self) -> bool:
         """A captured step needs one process (the NVLink sync kernels take per-step
@@ -269,15 +272,29 @@ class Trainer:
         prefix = self.cfg.model.checkpoint_prefix()
         path = os.path.join(self.tc.checkpoint_dir, f"{prefix}_step_{step}.safetensors")
         if self.rank == 0:
-            save_checkpoint(self.model, self.opt, step, self.cfg.model, self.tc.checkpoint_dir, self.data_file_path,
-                            self.tc.max_checkpoints, extra={"data_cursor": getattr(self.loader, "cursor", 0)},
-                            state_dict=sd, optim_state=st)
+            extra = {"data_cursor": getattr(self.loader, "cursor", 0)}
+            if self._writer is None:
+                save_checkpoint(self.model, self.opt, step, self.cfg.model, self.tc.checkpoint_dir,
+                                self.data_file_path, self.tc.max_checkpoints, extra=extra, state_dict=sd,
+                                optim_state=st)
+            else:
+                # host copies now (training goes on updating the device tensors), files later
+                sd_h, st_h = host_snapshot(sd), host_snapshot(st)
+                self._writer.submit(save_checkpoint, None, OptimizerSnapshot(self.opt.step_count, st_h), step,
+                                    self.cfg.model, self.tc.checkpoint_dir, self.data_file_path,
+                                    self.tc.max_checkpoints, extra=extra, state_dict=sd_h, optim_state=st_h)
         local = getattr(self.opt, "local", None)
         if local is not None:
             os.makedirs(self.tc.checkpoint_dir, exist_ok=True)
             save_local_optimizer(local, path, self.rank, step)
 
+    def flush_checkpoints(self) -> None:
+        """Wait for a checkpoint write in flight (and raise its error, if it failed)."""
+        if self._writer is not None:
+            self._writer.wait()
+
     def _final(self):
+        self.flush_checkpoints()
         sd = self._gather_weights()
         if self.rank == 0:
             prefix = self.cfg.model.checkpoint_prefix()

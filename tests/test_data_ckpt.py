@@ -115,3 +115,75 @@ def test_checkpoint_roundtrip_and_rotation(tmp_path):
 def test_step_from_filename():
     assert C.step_from_filename("/a/nano_512_117m_bf16_step_100.safetensors") == 100
     assert C.step_from_filename("x_final.safetensors") == 0
+
+
+def test_async_checkpoint_writes_the_state_of_the_save_call(tmp_path, monkeypatch):
+    """A periodic checkpoint is written on a background thread from host copies taken when
+    ``save`` is called: a training step that runs while the write is pending changes nothing
+    in the files."""
+    import threading
+    from safetensors.torch import load_file
+    from oxidizr_b200 import trainer as T
+    from oxidizr_b200.config import LitConfig
+    from oxidizr_b200.models import build_model
+    from oxidizr_b200.optim import AdamW, AdamWConfig, FlatParams
+
+    monkeypatch.delenv("OXI_SYNC_CHECKPOINT", raising=False)
+    cfg = LitConfig.from_dict({"model": {
+        "name": "asyncck", "hidden_size": 64, "num_layers": 1, "num_heads": 2, "kv_heads": 1,
+        "intermediate_size": 128, "vocab_size": 97, "max_seq_len": 16, "rope_theta": 10000.0, "dtype": "f32"},
+        "trainer": {"learning_rate": 1e-2, "batch_size": 2, "max_steps": 0, "num_epochs": 1,
+                    "gradient_accumulation": 1, "checkpoint_dir": str(tmp_path / "ck"), "log_interval": 1,
+                    "save_interval": 1000, "max_checkpoints": 2, "load_balance_alpha": 0.0, "group_size": 4,
+                    "beta_kl": 0.0}})
+    dev = torch.device("cpu")
+    model = build_model(cfg.model, device=dev, seed=0)
+    opt = AdamW(FlatParams(list(model.named_parameters()), dev), AdamWConfig(lr=1e-2))
+    blk = torch.randint(0, 97, (2, 17), generator=torch.Generator().manual_seed(0))
+
+    class Batches:
+        batch_size, seq_len = 2, 16
+
+        def dataset_size(self):
+            return 10 ** 6
+
+        def next_batch(self):
+            return blk[:, :-1], blk[:, 1:]
+
+    gate = threading.Event()
+    real = T.save_checkpoint
+
+    def slow_save(*a, **k):
+        assert gate.wait(30)
+        return real(*a, **k)
+
+    monkeypatch.setattr(T, "save_checkpoint", slow_save)
+    tr = T.Trainer(cfg, model, opt, Batches(), device=dev, out=lambda s: None)
+    tr.training_step()
+    at_save = {k: v.clone() for k, v in model.export_ref().items()}
+    step_at_save = opt.step_count
+    tr.save(1)
+    assert tr._writer.busy
+    tr.training_step()  # changes the parameters while the write waits
+    assert any(not torch.equal(at_save[k], v) for k, v in model.export_ref().items())
+    gate.set()
+    tr.flush_checkpoints()
+    path = os.path.join(cfg.trainer.checkpoint_dir, f"{cfg.model.checkpoint_prefix()}_step_1.safetensors")
+    saved = load_file(path)
+    assert set(saved) == set(at_save)
+    assert all(torch.equal(saved[k], at_save[k]) for k in at_save)
+    from safetensors import safe_open
+    with safe_open(C.optim_sidecar_path(path), "pt") as fh:
+        assert fh.metadata()["step"] == str(step_at_save)
+
+
+def test_async_checkpoint_writer_reports_a_failed_write():
+    w = C.AsyncCheckpointWriter()
+
+    def boom():
+        raise OSError("disk full")
+
+    w.submit(boom)
+    with pytest.raises(OSError, match="disk full"):
+        w.wait()
+    w.wait()  # reported once
