@@ -213,8 +213,11 @@ __global__ void clip_coef_kernel(const float* __restrict__ sqsum, float max_norm
   *norm_out = nrm;
   float c = pre_scale;
   if (max_norm > 0.f && nrm > max_norm) c *= max_norm / (nrm + 1e-6f);
-  *coef = c;
-  if (step_state) {
+  // a non-finite gradient norm skips this update: the coefficient is NaN, which every
+  // AdamW launch reading it takes as "leave p, m, v as they are"; the step count stays
+  const bool finite = isfinite(nrm);
+  *coef = finite ? c : __int_as_float(0x7fc00000);
+  if (step_state && finite) {
     const float t = step_state[0] + 1.f;
     step_state[0] = t;
     step_state[1] = 1.f - powf(b1, t);
@@ -274,6 +277,7 @@ __global__ void adamw_kernel(float* __restrict__ p, __nv_bfloat16* __restrict__ 
                              float eps, float wd, float bc1, float bc2, const float* __restrict__ gscale,
                              const float* __restrict__ bc_dev) {
   const float gs = gscale ? *gscale : 1.f;
+  if (gs != gs) return;  // NaN coefficient: non-finite gradient norm, the step is skipped
   // bias corrections from the device step state when given (graph-capturable step)
   const float rb1 = 1.f / (bc_dev ? bc_dev[0] : bc1), rb2 = 1.f / (bc_dev ? bc_dev[1] : bc2);
   const int64_t nv = n / 4;

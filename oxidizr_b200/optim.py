@@ -201,6 +201,12 @@ class AdamW:
                 sq = sq + lsq[0] * grad_scale * grad_scale
             nrm = sq.sqrt()
             self._norm.copy_(nrm.reshape(1))
+            if not bool(torch.isfinite(nrm)):
+                # as on the device: a non-finite gradient norm skips the update
+                f.zero_grad()
+                if self.local is not None:
+                    self.local.flat.zero_grad()
+                return self._norm
             coef = 1.0
             if c.max_grad_norm and nrm.item() > c.max_grad_norm:
                 coef = c.max_grad_norm / (nrm.item() + 1e-6)

@@ -184,9 +184,12 @@ class Trainer:
             launch_counter.count += self._graph_launches
         return self._graph_out
 
-    def _check_finite(self, loss: float):
+    def _check_finite(self, loss: float, grad_norm: float = 0.0):
         if not math.isfinite(loss):
             raise NonFiniteLoss("NaN loss detected")
+        if not math.isfinite(grad_norm):
+            # the optimizer already skipped that step on the device; stop as for a NaN loss
+            raise NonFiniteLoss("non-finite gradient norm detected")
 
     # ------------------------------------------------------------ loops
     def fit(self):
@@ -203,7 +206,7 @@ class Trainer:
             loss_t, gn_t = self.training_step()
             if step % self.tc.log_interval == 0 or step == 0:
                 loss, gn = float(loss_t), float(gn_t)
-                self._check_finite(loss)
+                self._check_finite(loss, gn)
                 self.last_loss, self.last_grad_norm = loss, gn
                 elapsed = time.perf_counter() - t0
                 samples = (step + 1 - self.start_step) * self.batch_size * self.tc.gradient_accumulation
@@ -230,7 +233,7 @@ class Trainer:
             its = 1.0 / avg if avg > 0 else 0.0
             if step % self.tc.log_interval == 0 or step == 0:
                 loss, gn = float(loss_t), float(gn_t)
-                self._check_finite(loss)
+                self._check_finite(loss, gn)
                 self.last_loss, self.last_grad_norm = loss, gn
                 epoch = (step + 1) / self.steps_per_epoch
                 if self.rank == 0:
