@@ -100,3 +100,34 @@ def test_failure_detection_gloo(tmp_path, kind):
     assert run["status"] == "failed"
     if kind == "nan":
         assert "NaN" in run["error"]
+
+
+def test_pack_then_push_with_a_fake_hf(tmp_path):
+    """pack copies the final checkpoint and config into hf/<user>/<model>/ with a model card;
+    push runs `hf upload <user>/<model> <dir> --repo-type model [--token] [--private]`
+    (a fake `hf` on PATH records its arguments; nothing is uploaded)."""
+    cfg, data = _cfg(tmp_path, steps=2, save_interval=1000)
+    r, _ = _train(tmp_path, cfg, data)
+    assert r.returncode == 0, r.stderr[-3000:]
+    e = dict(os.environ, PYTHONPATH=REPO, OXIDIZED_RUN_DIR=str(tmp_path / "run"))
+    rp = subprocess.run([sys.executable, "-m", "oxidizr_b200", "pack", "--checkpoint-dir", str(tmp_path / "ckpt"),
+                         "-c", "final", "-u", "alice", "-n", "tiny-test"], cwd=str(tmp_path), env=e,
+                        capture_output=True, text=True, timeout=120)
+    assert rp.returncode == 0, rp.stderr[-2000:]
+    out = tmp_path / "hf" / "alice" / "tiny-test"
+    for f in ("model.safetensors", "config.json", "README.md"):
+        assert (out / f).exists(), f
+    bindir = tmp_path / "bin"
+    bindir.mkdir()
+    rec = tmp_path / "hf_args.txt"
+    fake = bindir / "hf"
+    fake.write_text(f'#!/bin/sh\nprintf "%s\\n" "$@" > "{rec}"\n')
+    fake.chmod(0o755)
+    e2 = dict(e, PATH=f"{bindir}{os.pathsep}{os.environ.get('PATH', '')}")
+    e2.pop("HF_TOKEN", None)
+    ru = subprocess.run([sys.executable, "-m", "oxidizr_b200", "push", "-m", "alice/tiny-test", "--private",
+                         "-t", "tok123", "-y"], cwd=str(tmp_path), env=e2, capture_output=True, text=True, timeout=120)
+    assert ru.returncode == 0, ru.stderr[-2000:]
+    assert rec.read_text().split("\n")[:-1] == ["upload", "alice/tiny-test", os.path.join("hf", "alice", "tiny-test"),
+                                                 "--repo-type", "model", "--token", "tok123", "--private"]
+    assert "Upload complete: https://huggingface.co/alice/tiny-test" in ru.stdout

@@ -187,3 +187,58 @@ def test_async_checkpoint_writer_reports_a_failed_write():
     with pytest.raises(OSError, match="disk full"):
         w.wait()
     w.wait()  # reported once
+
+
+def test_baseline_config1_cpu_checkpoint_roundtrip(tmp_path):
+    """BASELINE config 1 (Llama decoder, CPU fp32: hidden 512, 8 layers, 8 / 4 heads of 64,
+    SwiGLU 2048, vocab 128354, seq 512, batch 2, AdamW lr 3e-4, seeded uniform u32 tokens):
+    train, save, load into a differently initialised model and optimizer, and check bitwise-equal
+    parameters and the identical next-step loss."""
+    from oxidizr_b200.models import build_model
+    from oxidizr_b200.optim import AdamW, AdamWConfig, FlatParams
+    from oxidizr_b200.trainer import Trainer
+
+    cfg = LitConfig.from_dict({"model": {
+        "name": "config1", "hidden_size": 512, "num_layers": 8, "num_heads": 8, "kv_heads": 4,
+        "intermediate_size": 2048, "vocab_size": 128354, "max_seq_len": 512, "rope_theta": 10000.0, "dtype": "f32"},
+        "trainer": {"learning_rate": 3e-4, "batch_size": 2, "max_steps": 20, "num_epochs": 1,
+                    "gradient_accumulation": 1, "checkpoint_dir": str(tmp_path / "ck"), "log_interval": 1,
+                    "save_interval": 1000, "load_balance_alpha": 0.0, "group_size": 4, "beta_kl": 0.0}})
+    assert cfg.model.hidden_size // cfg.model.num_heads == 64
+    dev = torch.device("cpu")
+    toks = torch.from_numpy(D.synthetic_tokens(128354, 2 * 513 * 4, seed=11).astype(np.int64)).view(4, 2, 513)
+
+    class Batches:
+        batch_size, seq_len = 2, 512
+
+        def __init__(self):
+            self.i = 0
+
+        def dataset_size(self):
+            return 10 ** 9
+
+        def next_batch(self):
+            b = toks[self.i % 4]
+            self.i += 1
+            return b[:, :-1], b[:, 1:]
+
+    def make(seed):
+        model = build_model(cfg.model, device=dev, seed=seed)
+        opt = AdamW(FlatParams(list(model.named_parameters()), dev), AdamWConfig(lr=3e-4))
+        batches = Batches()
+        return model, opt, batches, Trainer(cfg, model, opt, batches, device=dev, out=lambda s: None)
+
+    model_a, opt_a, bat_a, tr_a = make(0)
+    losses = [float(tr_a.training_step()[0]) for _ in range(3)]
+    assert all(np.isfinite(losses)) and abs(losses[0] - np.log(128354)) < 1.0
+    path = C.save_checkpoint(model_a, opt_a, 3, cfg.model, cfg.trainer.checkpoint_dir, None, 2)
+
+    model_b, opt_b, bat_b, tr_b = make(123)
+    C.load_weights(model_b, path)
+    meta = C.load_optimizer_sidecar(opt_b, path)
+    assert meta is not None and opt_b.step_count == 3
+    for (n, pa), (_, pb) in zip(model_a.named_parameters(), model_b.named_parameters()):
+        assert torch.equal(pa, pb), n
+    bat_b.i = bat_a.i
+    la, lb = float(tr_a.training_step()[0]), float(tr_b.training_step()[0])
+    assert la == lb
