@@ -147,7 +147,8 @@ def test_gqa_model_matches_cpu_reference(hd_heads):
         assert _rel(gg[k].cpu(), gc[k]) < 6e-2, k
 
 
-@pytest.mark.parametrize("T,H,I,E,k", [(300, 256, 128, 4, 2), (1000, 512, 256, 8, 3), (64, 256, 128, 16, 1)])
+@pytest.mark.parametrize("T,H,I,E,k", [(300, 256, 128, 4, 2), (1000, 512, 256, 8, 3), (64, 256, 128, 16, 1),
+                                       (500, 256, 128, 6, 2)])
 def test_grouped_experts_vs_dense(T, H, I, E, k):
     """Sparse grouped-GEMM experts == per-token dense reference (fwd + grads)."""
     from oxidizr_b200.models.common import split_gu
@@ -182,7 +183,8 @@ def test_grouped_experts_vs_dense(T, H, I, E, k):
 
 
 @pytest.mark.parametrize("T,E,k,dt", [(1000, 32, 4, torch.bfloat16), (777, 64, 8, torch.float32),
-                                      (300, 256, 16, torch.bfloat16), (50, 8, 2, torch.float32)])
+                                      (300, 256, 16, torch.bfloat16), (50, 8, 2, torch.float32),
+                                      (333, 12, 3, torch.float32), (129, 100, 5, torch.bfloat16)])
 def test_router_topk_vs_torch(T, E, k, dt):
     from oxidizr_b200.models.moe import aux_from_usage, route
     from oxidizr_b200.ops.moe_kernels import RouterTopK
