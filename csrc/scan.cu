@@ -28,8 +28,8 @@
 //
 // Mamba1 (mamba.rs:212-291): per channel d, state h (N = 16):
 //   h_t = exp(delta_t A_d) h_{t-1} + delta_t x_t B_t ;  y_t = C_t . h_t
-// The upstream clamp of every state to +-clamp makes the recurrence nonlinear, so
-// it stays sequential in t; the parallelism is (b, d, n): a half-warp per channel,
+// The compatibility clamp of every state to +-clamp makes the recurrence nonlinear,
+// so the kernel stays sequential in t (for both modes); the parallelism is (b, d, n): a half-warp per channel,
 // one lane per state, y / du / d delta as 16-lane shuffle sums.  The backward reads
 // the per-step states the forward saved; both kernels load the operands of their
 // next few steps while computing the current ones.  The dB / dC terms (sums over channels)
