@@ -1,6 +1,6 @@
 #!/usr/bin/env python
 """Headline benchmark: training tokens/s of the Llama-style GQA decoder
-(BASELINE config 2: hidden 2048, 16 layers, 16 heads / 8 KV heads, SwiGLU
+(BASELINE.json config 2: hidden 2048, 16 layers, 16 heads / 8 KV heads, SwiGLU
 5632, vocab 128354, RoPE theta 1e4, seq 2048, micro-batch 8 per GPU, bf16,
 AdamW, grad accumulation 1), data-parallel over N GPUs of one node.
 
@@ -159,7 +159,7 @@ def main():
     ap.add_argument("--cuda-graph", action="store_true",
                     help="capture the training step in a CUDA graph (one GPU only; replayed every step)")
     ap.add_argument("--model", default="llama", choices=sorted(MODELS),
-                    help="llama = the headline config; hybrid / mamba3 / moe = the other BASELINE configs")
+                    help="llama = the headline config; hybrid / mamba3 / moe = the other BASELINE.json configs")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)

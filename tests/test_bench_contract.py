@@ -1,5 +1,5 @@
 """bench.py's contract with its caller, on the CPU: the reference arm's one-line JSON, the
-clock sampler's parsing of nvidia-smi lines, and the model configs against the BASELINE
+clock sampler's parsing of nvidia-smi lines, and the model configs against the BASELINE.json
 configs they claim to be."""
 import json
 import os

@@ -190,7 +190,7 @@ def test_async_checkpoint_writer_reports_a_failed_write():
 
 
 def test_baseline_config1_cpu_checkpoint_roundtrip(tmp_path):
-    """BASELINE config 1 (Llama decoder, CPU fp32: hidden 512, 8 layers, 8 / 4 heads of 64,
+    """BASELINE.json config 1 (Llama decoder, CPU fp32: hidden 512, 8 layers, 8 / 4 heads of 64,
     SwiGLU 2048, vocab 128354, seq 512, batch 2, AdamW lr 3e-4, seeded uniform u32 tokens):
     train, save, load into a differently initialised model and optimizer, and check bitwise-equal
     parameters and the identical next-step loss."""
