@@ -149,8 +149,20 @@ def save_blazr_config_if_needed(checkpoint_dir: str, model_cfg: ModelConfig) -> 
     return True
 
 
+def _save_atomic(tensors: Dict[str, torch.Tensor], path: str, metadata: Optional[Dict[str, str]] = None) -> None:
+    """safetensors file written under a temporary name and renamed into place: a crash mid-write
+    (or a background write cut short) never leaves a truncated file under the real name."""
+    tmp = f"{path}.tmp{os.getpid()}"
+    try:
+        save_file(tensors, tmp, metadata=metadata)
+        os.replace(tmp, path)
+    finally:
+        if os.path.exists(tmp):
+            os.remove(tmp)
+
+
 def save_weights(model, path: str, state_dict: Optional[Dict[str, torch.Tensor]] = None) -> None:
-    save_file(_cpu_contig(state_dict if state_dict is not None else model.export_ref()), path)
+    _save_atomic(_cpu_contig(state_dict if state_dict is not None else model.export_ref()), path)
 
 
 def load_weights(model, path: str) -> None:
@@ -180,7 +192,7 @@ def save_checkpoint(model, optimizer, step: int, model_cfg: ModelConfig, checkpo
         meta = {"step": str(optimizer.step_count), "format": "oxidizr_b200.flat_adamw.v1"}
         if extra:
             meta.update({k: str(v) for k, v in extra.items()})
-        save_file(_cpu_contig(st), optim_sidecar_path(path), metadata=meta)
+        _save_atomic(_cpu_contig(st), optim_sidecar_path(path), metadata=meta)
     if data_file_path:
         try:
             CheckpointMeta.new(step, model_cfg, data_file_path, path).save(checkpoint_dir)
@@ -274,8 +286,8 @@ def local_sidecar_path(weights_path: str, rank: int) -> str:
 
 
 def save_local_optimizer(local_opt, weights_path: str, rank: int, step: int) -> None:
-    save_file(_cpu_contig(local_opt.state_tensors()), local_sidecar_path(weights_path, rank),
-              metadata={"step": str(step), "format": "oxidizr_b200.flat_adamw.v1"})
+    _save_atomic(_cpu_contig(local_opt.state_tensors()), local_sidecar_path(weights_path, rank),
+                 metadata={"step": str(step), "format": "oxidizr_b200.flat_adamw.v1"})
 
 
 def load_local_optimizer(local_opt, weights_path: str, rank: int) -> bool:

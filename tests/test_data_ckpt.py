@@ -242,3 +242,23 @@ def test_baseline_config1_cpu_checkpoint_roundtrip(tmp_path):
     bat_b.i = bat_a.i
     la, lb = float(tr_a.training_step()[0]), float(tr_b.training_step()[0])
     assert la == lb
+
+
+def test_checkpoint_files_are_written_whole(tmp_path, monkeypatch):
+    """A write that fails part way leaves no file under the real name (and no temporary file)."""
+    import safetensors.torch as st
+    path = str(tmp_path / "w.safetensors")
+    real = st.save_file
+
+    def failing(tensors, filename, metadata=None):
+        with open(filename, "wb") as fh:
+            fh.write(b"partial")
+        raise OSError("disk full")
+
+    monkeypatch.setattr(C, "save_file", failing)
+    with pytest.raises(OSError):
+        C._save_atomic({"a": torch.ones(3)}, path)
+    assert os.listdir(tmp_path) == []
+    monkeypatch.setattr(C, "save_file", real)
+    C._save_atomic({"a": torch.ones(3)}, path)
+    assert os.listdir(tmp_path) == ["w.safetensors"]
