@@ -53,7 +53,9 @@ def main(argv=None):
     ap.add_argument("--chunk", type=float, default=32e6)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--bucket-mb", type=int, default=32)
-    ap.add_argument("--rs-ctas", default="16", help="comma list: CTA budgets of the reduce-scatter to sweep")
+    ap.add_argument("--rs-ctas", default="64",
+                    help="comma list: CTA budgets of the reduce-scatter to sweep (the first is used for the full "
+                         "fused step; 64 is the trainer's default)")
     args = ap.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
