@@ -131,3 +131,30 @@ def test_pack_then_push_with_a_fake_hf(tmp_path):
     assert rec.read_text().split("\n")[:-1] == ["upload", "alice/tiny-test", os.path.join("hf", "alice", "tiny-test"),
                                                  "--repo-type", "model", "--token", "tok123", "--private"]
     assert "Upload complete: https://huggingface.co/alice/tiny-test" in ru.stdout
+
+
+def test_throughput_sweep_on_cpu(tmp_path):
+    """The (seq, batch, accumulation) sweep writes upstream's logs.txt / results.csv layout with
+    the numbers read from the trainer's JSON lines."""
+    from oxidizr_b200.utils import sweep
+    cfg, data = _cfg(tmp_path, steps=4)
+    res = sweep.run([(16, 1, 1), (16, 2, 2)], cfg, 1, ["-d", data, "--target-device", "cpu"],
+                    str(tmp_path / "benchmark"), timeout=240)
+    lines = open(res).read().splitlines()
+    assert lines[0] == sweep.HEADER and len(lines) == 3
+    rows = [ln.split(",") for ln in lines[1:]]
+    assert [r[:4] for r in rows] == [["16", "1", "1", "1"], ["16", "2", "2", "4"]]
+    assert all(r[6] == "" and float(r[5]) > 0 for r in rows), rows
+    assert os.path.exists(os.path.join(os.path.dirname(res), "logs.txt"))
+    assert len(sweep.DEFAULT_GRID) == 50
+
+
+def test_sweep_classifies_failures():
+    from oxidizr_b200.utils.sweep import classify
+    assert classify(1, "RuntimeError: CUDA out of memory. Tried to allocate")[0] == "OOM"
+    assert classify(1, "Traceback (most recent call last):\nValueError: bad")[0] == "ERROR"
+    assert classify(3, "")[0] == "UNKNOWN_ERROR"
+    assert classify(None, "")[0] == "TIMEOUT"
+    assert classify(0, "no json here")[0] == "NO_OUTPUT"
+    notes, rec = classify(0, '{"step": 1, "loss": 6.1, "it/s": 3.25, "vram": "0"}\nSaving final checkpoint')
+    assert notes == "" and rec["it/s"] == 3.25
