@@ -24,6 +24,8 @@
 // store of the flag; the waiter acquires the flag before reading data.  All
 // waits are bounded (OXI_WAIT_LIMIT_NS); on timeout the kernel records
 // OXI_ERR_TIMEOUT_PEER in the status word, skips its work and returns.
+// Upstream: gradient synchronisation distributed/nccl.rs:153-184 and
+// distributed/cpu_staging.rs:146-172; AdamW distributed/optimizer.rs:126-192; clipping trainer.rs:560-574.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>

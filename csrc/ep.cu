@@ -34,6 +34,8 @@
 //   wait(DXREADY) ; gather locally: dx_t = sum_j yret[t k + j]
 // Every wait is bounded; a timeout records OXI_ERR_TIMEOUT_PEER in the status
 // word and the kernel skips its remote accesses.  No TMA is used here.
+// Upstream: the MoE layer model.rs:541-593 (dense on one GPU in the reference; expert
+// parallelism over NVLink is new here).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <algorithm>

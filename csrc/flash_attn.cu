@@ -23,6 +23,8 @@
 // Warps: 0 TMA, 1 MMA + TMEM owner, 2..9 softmax/correction/epilogue (two per
 // 32-row TMEM lane quarter, splitting the keys of each tile).
 // Every TMA load here reads local memory for one CTA; every wait is bounded.
+// Upstream: GQA attention model.rs:333-386 (repeat_kv model.rs:388-399, causal mask
+// model.rs:402-425); multi-head latent attention model.rs:196-256.
 #include <algorithm>
 #include <cudaTypedefs.h>
 

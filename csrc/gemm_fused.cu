@@ -1,4 +1,6 @@
 // GEMM launchers with fused epilogues (kernel in gemm_kernel.cuh).
+// Upstream: SwiGLU MLP model.rs:430-455; RoPE on q/k model.rs:68-117 (applied at
+// model.rs:333-386); lm_head + cross-entropy model.rs:1002, trainer.rs:166-171.
 #include "gemm_kernel.cuh"
 #include "kernels.h"
 

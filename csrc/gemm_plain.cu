@@ -1,4 +1,6 @@
 // Plain GEMM launcher (kernel in gemm_kernel.cuh): bf16 or f32 output.
+// Upstream: the reference's Linear / matmul calls (Candle on cuBLAS), e.g. model.rs:238,248,367,377,
+// mamba2.rs:563,611,673,732.
 #include "gemm_kernel.cuh"
 #include "kernels.h"
 

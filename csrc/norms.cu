@@ -1,11 +1,16 @@
 // Row-wise normalisation kernels (bandwidth bound): RMSNorm, LayerNorm and the
 // gated RMSNorm of the Mamba2/3 mixers, forward and backward.
 //
-// One warp per row, 16-byte vector loads, f32 math.  Backward kernels
+// Forward: one warp per row, 16-byte vector loads, f32 math.  Backward kernels
 // optionally add an incoming residual-stream gradient (dres) into dx, which
-// removes the separate autograd add of the pre-norm residual.  Weight (and
-// bias) gradients are reduced per CTA in shared memory and then added to an
-// f32 global buffer with one atomic per column per CTA.
+// removes the separate autograd add of the pre-norm residual.  Widths that are
+// multiples of 256 (up to 4096) take the row kernel: one CTA per row (H/8
+// threads, the row in registers), weight / bias gradients written as per-CTA
+// partials that a sliced pass sums (no same-address atomics).  Other widths take
+// the warp-per-row kernel, which reduces per CTA in shared memory and adds one
+// f32 atomic per column per CTA.
+// Upstream: RMSNorm model.rs:9-32 (eps 1e-5 at model.rs:796,971); gated RMSNorm
+// mamba2.rs:185-217; the Mamba2/3 pre-LayerNorm mamba2.rs:768, mamba3.rs:959.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <algorithm>

@@ -2,6 +2,9 @@
 // gather/scatter, RoPE backward, gradient-norm, clip coefficient and the flat
 // multi-tensor AdamW update.  All are single-pass over their data with 16-byte
 // vector accesses; none synchronises with the host.
+// Upstream: cross-entropy trainer.rs:166-171 and model.rs:1002; embedding model.rs:964;
+// RoPE model.rs:68-117; gradient norm trainer.rs:560-574; AdamW trainer.rs:60-64,245 and
+// distributed/optimizer.rs:126-192.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>

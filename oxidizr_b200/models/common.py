@@ -4,6 +4,9 @@ Modules in this package keep some parameters fused for the kernels (q|k|v,
 gate|up interleaved in 128-row blocks, MLA down projections, stacked experts)
 and translate to/from the upstream per-tensor names (``model.rs``,
 ``mamba*.rs`` ``vb.pp(...)`` prefixes) in ``export_ref`` / ``import_ref``.
+
+Upstream: weight names from ``VarBuilder`` prefixes (model.rs:320-323,442-444,517-530,856-866,
+model.rs:964-972; mamba.rs:71-97; mamba2.rs:263-300; mamba3.rs:303-378); RoPE tables model.rs:43-66.
 """
 from __future__ import annotations
 

@@ -3,6 +3,10 @@
 bf16 CUDA tensors run the sm_100a kernels (``ops.fused`` and friends); CPU
 tensors (and non-bf16 CUDA tensors, e.g. an f32 model moved to the GPU) run
 the PyTorch statement of the same math from ``ops.reference`` under autograd.
+
+Upstream: RMSNorm model.rs:9-32, gated RMSNorm mamba2.rs:185-217, Mamba2 LayerNorm
+mamba2.rs:768, RoPE model.rs:68-117, SwiGLU model.rs:430-455, attention model.rs:333-386 and
+model.rs:196-256, lm_head model.rs:1002.
 """
 from __future__ import annotations
 

@@ -6,6 +6,9 @@ accumulates its gradient there with a fused GEMM epilogue (``C += A B^T``) or
 an atomic scatter, then calls ``param._oxi_grad_ready()`` if present (the DDP
 bucket hook), and returns ``None`` to autograd.  Without ``main_grad`` the
 gradient is returned normally.
+
+Upstream: RMSNorm model.rs:9-32, RoPE model.rs:68-117, GQA projections model.rs:320-323,
+SwiGLU MLP model.rs:430-455, embedding / lm_head model.rs:964-1002, cross-entropy trainer.rs:166-171.
 """
 from __future__ import annotations
 

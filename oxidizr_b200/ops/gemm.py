@@ -7,6 +7,9 @@ three GEMMs of ``y = x W^T`` (forward, dX, dW) run without transposes:
 * forward  ``y  = x  @ W^T``   : A = x  [T, K] (K-major),  B = W [N, K] (K-major)
 * dX       ``dx = dy @ W``     : A = dy [T, N] (K-major),  B = W stored [N, K] = [K', N'] (MN-major)
 * dW       ``dW = dy^T @ x``   : A = dy stored [T, N] (MN-major), B = x stored [T, K] (MN-major)
+
+Upstream: every ``Linear`` / ``matmul`` of the reference (Candle on cuBLAS), e.g. model.rs:238,248,
+model.rs:367,377 and mamba2.rs:563,611,673,732.
 """
 from __future__ import annotations
 

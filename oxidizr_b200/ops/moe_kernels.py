@@ -7,6 +7,9 @@ weighted combine (fused with the residual add).  Backward mirrors it with the
 SwiGLU-backward epilogue, two per-expert weight-gradient GEMMs reducing over
 each expert's token segment, and a gather-sum back to token order.  No host
 synchronisation: segment offsets stay on the device.
+
+Upstream: ``Router`` model.rs:485-499, ``MoeLayer::forward`` model.rs:541-593 (dense loop
+model.rs:561-565, aux loss model.rs:585-590), ``top_k`` model.rs:604-654, routing matrix model.rs:722-751.
 """
 from __future__ import annotations
 

@@ -4,6 +4,10 @@ Mamba3 trapezoidal scan and the Mamba1 selective scan.
 bf16 CUDA tensors use the sm_100a kernels in ``csrc/ssm*.cu`` when the
 extension provides them; everything else runs the float32 statement in
 ``ops.reference`` under autograd.
+
+Upstream: conv1d mamba2.rs:344-352; ``ssd_forward`` mamba2.rs:381-482 (``segment_sum``
+mamba2.rs:116-180); ``ssd_forward_trapezoidal`` mamba3.rs:638-752; ``selective_scan_sequential``
+mamba.rs:212-291.
 """
 from __future__ import annotations
 

@@ -1,4 +1,8 @@
-"""Autograd functions over the SSM kernels (csrc/conv1d.cu, csrc/ssd.cu)."""
+"""Autograd functions over the SSM kernels (csrc/conv1d.cu, csrc/ssd.cu).
+
+Upstream: causal conv1d mamba2.rs:344-352, mamba.rs:137-141; Mamba1 selective scan
+mamba.rs:212-291; chunked SSD mamba2.rs:381-482; Mamba3 trapezoidal scan mamba3.rs:638-752.
+"""
 from __future__ import annotations
 
 import torch

@@ -10,6 +10,11 @@ card.
 
 push: validate ``hf/<user>/<model>`` and run
 ``hf upload <user>/<model> <dir> --repo-type model [--token T] [--private]``.
+
+Upstream lines: ``PackArgs`` commands/pack.rs:15-35, ``scan_checkpoints`` commands/pack.rs:58-77,
+``select_checkpoint`` commands/pack.rs:124-167, ``generate_model_card`` commands/pack.rs:228-400,
+``run_pack`` commands/pack.rs:525-638; ``PushArgs`` commands/push.rs:14-34, ``scan_packaged_models``
+commands/push.rs:76-128, ``run_push`` commands/push.rs:172-277 (command at commands/push.rs:240-255).
 """
 from __future__ import annotations
 

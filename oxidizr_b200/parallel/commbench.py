@@ -18,6 +18,9 @@ The roofline of the fused step is the slower of the NVLink bytes (reduce-
 scatter in + all-gather out, (W-1)/W of the bf16 gradient each way, at the
 measured 770 GB/s per direction) and the HBM bytes of the sharded AdamW at the
 measured copy bandwidth.  Rank 0 prints one JSON line.
+
+Upstream path it replaces: distributed/nccl.rs:153-184 (per-parameter NCCL all-reduce
+through host copies) and distributed/optimizer.rs:126-192 (AdamW).
 """
 from __future__ import annotations
 
