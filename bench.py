@@ -2,7 +2,9 @@
 """Headline benchmark: training tokens/s of the Llama-style GQA decoder
 (hidden 2048, 16 layers, 16 heads / 8 KV heads, SwiGLU
 5632, vocab 128354, RoPE theta 1e4, seq 2048, micro-batch 8 per GPU, bf16,
-AdamW, grad accumulation 1), data-parallel over N GPUs of one node.
+AdamW, grad accumulation 1), data-parallel over N GPUs of one node.  Upstream's benchmark is the
+run_benchmark.sh:46-183 sweep (headless it/s per (seq, batch, accumulation) point; our counterpart
+is oxidizr_b200/utils/sweep.py); this harness times the BASELINE.json configs on the device.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
     (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...)

@@ -24,6 +24,9 @@
 //                   heads using per-position cos/sin tables
 //
 // Every TMA load here is issued by one CTA for itself and reads local memory.
+// Upstream: the reference's Linear / matmul calls on cuBLAS through Candle (e.g. model.rs:238,248,367,377,
+// mamba2.rs:563,611,673,732) and the fused epilogue math of model.rs:68-117 (RoPE), model.rs:430-455
+// (SwiGLU) and trainer.rs:166-171 (cross-entropy).
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <cstdlib>
