@@ -262,3 +262,25 @@ def test_checkpoint_files_are_written_whole(tmp_path, monkeypatch):
     monkeypatch.setattr(C, "save_file", real)
     C._save_atomic({"a": torch.ones(3)}, path)
     assert os.listdir(tmp_path) == ["w.safetensors"]
+
+
+def test_host_copies_for_safetensors(tmp_path):
+    """Views of one flat buffer are copied out, a tensor that owns its storage passes through once,
+    a second name for it gets a copy, and the snapshot never aliases live tensors."""
+    from safetensors.torch import load_file
+    flat = torch.arange(12, dtype=torch.float32)
+    own = torch.ones(3)
+    sd = {"a": flat[:6].view(2, 3), "b": flat[6:], "own": own, "own_again": own}
+    out = C._cpu_contig(sd)
+    assert out["own"] is not None and out["own"].data_ptr() == own.data_ptr()
+    assert out["own_again"].data_ptr() != own.data_ptr()
+    assert out["a"].data_ptr() != flat.data_ptr() and out["b"].untyped_storage().nbytes() == 6 * 4
+    path = str(tmp_path / "x.safetensors")
+    C._save_atomic(out, path)
+    back = load_file(path)
+    assert all(torch.equal(back[k], sd[k]) for k in sd)
+    snap = C.host_snapshot(sd)
+    flat.add_(100.0)
+    own.add_(1.0)
+    assert torch.equal(snap["a"], torch.arange(6, dtype=torch.float32).view(2, 3))
+    assert torch.equal(snap["own"], torch.ones(3))
