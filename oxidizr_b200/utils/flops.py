@@ -5,7 +5,7 @@ twice that in the backward (6 x active matmul parameters per token); causal
 attention adds 3 x S x heads x (d_qk + d_v) per token (half of the S x S
 scores, fwd + bwd); a chunked SSD scan adds 3 x its per-token tensor work
 (intra-chunk C B^T and (L o C B^T) X over half a chunk, state update and
-readout).  MoE layers count the routed top-k experts plus the shared ones, and
+readout), once for Mamba3 as well (its two-term update is computed as one scan).  MoE layers count the routed top-k experts plus the shared ones, and
 the router.
 """
 from __future__ import annotations
@@ -55,7 +55,9 @@ def _mamba2(cfg, mamba3: bool):
         if (cfg.mamba3_mimo_rank or 0) > 1:
             params += 2 * hs * P * P * R
         width = P * R
-        terms = 2  # trapezoidal: two SSD terms
+        # the trapezoidal update runs as ONE scan over the shifted state (the second term
+        # folds into the input coefficient and the D skip), so one SSD term is counted
+        terms = 1
     else:
         params = H * (2 * I + 2 * g * N + hs) + I * H
         width = P
