@@ -158,6 +158,8 @@ def main():
     ap.add_argument("--impl", default="oxidizr_b200", choices=["oxidizr_b200", "reference"])
     ap.add_argument("--sync-backend", default=os.environ.get("OXI_SYNC_BACKEND", "auto"))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-baseline", action="store_true",
+                    help="N > 1: skip timing the like-for-like NCCL path (nccl_sharded) after the fused one")
     ap.add_argument("--cuda-graph", action="store_true",
                     help="capture the training step in a CUDA graph (one GPU only; replayed every step)")
     ap.add_argument("--model", default="llama", choices=sorted(MODELS),
@@ -201,7 +203,7 @@ def main():
         if backend == "auto":
             backend = "fused"
         from oxidizr_b200.parallel.ddp import make_ddp_optimizer
-        opt = make_ddp_optimizer(model.named_parameters(), ocfg, dev, backend)
+        opt = make_ddp_optimizer(model.named_parameters(), ocfg, dev, backend, model=model)
     else:
         backend = "single"
         opt = AdamW(FlatParams(list(model.named_parameters()), dev), ocfg)
@@ -317,10 +319,34 @@ def main():
     if ep > 1:
         from oxidizr_b200.parallel.ep import EPLayerBuffers
         out["ep_buffer_reallocs"] = EPLayerBuffers.reallocs
-    if rank == 0:
-        print(json.dumps(out), flush=True)
     if hasattr(opt, "close"):
         opt.close()
+    # ---------------- N > 1: the same model and step over the like-for-like NCCL transport
+    if world > 1 and backend == "fused" and not args.no_baseline:
+        from oxidizr_b200.parallel.ddp import make_ddp_optimizer
+        del trainer, opt
+        torch.cuda.empty_cache()
+        bopt = make_ddp_optimizer(model.named_parameters(), ocfg, dev, "nccl_sharded", model=model)
+        btrainer = Trainer(cfg, model, bopt, DeviceBatches(), device=dev, headless=True, rank=rank,
+                           world_size=world, out=lambda s: None)
+        for _ in range(args.warmup):
+            btrainer.training_step()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(args.steps):
+            btrainer.training_step()
+        g1.record()
+        barrier()
+        ms_b = max_over_ranks(g0.elapsed_time(g1) / args.steps)
+        bval = tokens_per_step / (ms_b / 1e3)
+        out["baseline"] = {"value": round(bval, 1), "ms_per_step": round(ms_b, 3), "sync_backend": "nccl_sharded",
+                           "what": "this framework's same model and sharded step with NCCL bf16 reduce-scatter / "
+                                   "all-gather as the transport (no published reference number exists)"}
+        out["vs_baseline"] = round(value / bval, 4)
+        bopt.close()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

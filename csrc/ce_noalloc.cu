@@ -7,50 +7,28 @@
 // cudaFree synchronise the device in the middle of its work.  Such a caller
 // passes only its inputs and outputs; the scratch the kernels need lives in a
 // file-scope device array of fixed size instead of a per-call allocation.
-//
-//   int oxi_linear_ce_fwd_noalloc(x, M, K, ldx, w, V, ldw, targets,
-//                                 loss, lse, stream)
-//
-//   x       bf16 [M, K] row stride ldx (elements)     hidden states
-//   w       bf16 [V, K] row stride ldw                lm_head weight
-//   targets int64 [M]; a negative target marks an ignored row (loss 0)
-//   loss    f32 [M] per-row cross-entropy (output)
-//   lse     f32 [M] per-row log-sum-exp of the logits (output)
-//
-// Limits: M <= OXI_CE_NOALLOC_MAX_ROWS and M * ceil(V / 256) <=
-// OXI_CE_NOALLOC_MAX_PARTIALS.  Larger problems are rejected with
-// OXI_CE_NOALLOC_TOO_LARGE before anything is launched; split them into row
-// blocks.  The scratch array takes about 8.3 MB on every GPU that loads this
-// library and stays there until the process exits.
+// The interface, limits, return codes and sharing rules are declared in
+// ce_noalloc.h.
 //
 // Set-up: the first call on a device looks up the device address of the
 // scratch array (cudaGetSymbolAddress, with that device current) and caches
-// it; make that first call on each device before any stream capture.
-//
-// Sharing: every call uses the same scratch array, which keeps the contents
-// of the last call (this entry point clears what must start at zero).  Calls
-// whose kernels overlap on the GPU (different streams, no ordering between
-// them) race on the scratch array and give wrong results; order them.
+// it together with the id of the current CUDA context; a call under a new
+// context (after cudaDeviceReset) looks it up again.  Make the first call on
+// each device before any stream capture.
 //
 // Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+#include <cuda.h>
+
 #include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <exception>
+#include <mutex>
 
+#include "ce_noalloc.h"
 #include "gemm_kernel.cuh"
 #include "kernels.h"
 #include "kernels_ew.h"
-
-#define OXI_CE_NOALLOC_MAX_ROWS (1 << 16)
-#define OXI_CE_NOALLOC_MAX_PARTIALS (1 << 20)
-
-enum : int {
-  OXI_CE_NOALLOC_OK = 0,
-  OXI_CE_NOALLOC_TOO_LARGE = 1,
-  OXI_CE_NOALLOC_BAD_ARGUMENT = 2,
-  OXI_CE_NOALLOC_CUDA_ERROR = 3,
-};
 
 namespace {
 
@@ -64,9 +42,31 @@ struct CeScratch {
 static __device__ __align__(256) CeScratch g_ce_scratch;
 
 constexpr int kMaxDevices = 128;
-std::atomic<CeScratch*> g_scratch_addr[kMaxDevices];
+
+// Per device: the scratch address and the id of the context it was looked up in.
+struct ScratchSlot {
+  CeScratch* addr = nullptr;
+  unsigned long long ctx_id = 0;
+};
+ScratchSlot g_slots[kMaxDevices];
+std::mutex g_slots_mu;
 
 thread_local char g_last_error[512];
+
+// Driver calls through the runtime's entry-point query, so the library does
+// not link libcuda directly (it still imports on a machine without a driver).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+template <typename F>
+F driver_fn(const char* name, int version) {
+  void* ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion(name, &ptr, version, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<F>(ptr);
+}
 
 int set_error(int code, const char* msg) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
@@ -80,16 +80,27 @@ int scratch_for_current_device(CeScratch** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(OXI_CE_NOALLOC_CUDA_ERROR, cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return set_error(OXI_CE_NOALLOC_BAD_ARGUMENT, "device ordinal out of range");
-  CeScratch* p = g_scratch_addr[dev].load(std::memory_order_acquire);
-  if (!p) {
+  // make the device's primary context current (CUDA 12 initialises it here), then identify it
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return set_error(OXI_CE_NOALLOC_CUDA_ERROR, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lk(g_slots_mu);
+  static const CtxGetCurrentFn get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent", 4000);
+  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId", 12000);
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return set_error(OXI_CE_NOALLOC_CUDA_ERROR, "no current CUDA context");
+  ScratchSlot& slot = g_slots[dev];
+  if (slot.addr == nullptr || slot.ctx_id != id) {
     void* addr = nullptr;
     e = cudaGetSymbolAddress(&addr, g_ce_scratch);
     if (e != cudaSuccess || addr == nullptr)
       return set_error(OXI_CE_NOALLOC_CUDA_ERROR, e != cudaSuccess ? cudaGetErrorString(e) : "null symbol address");
-    p = static_cast<CeScratch*>(addr);
-    g_scratch_addr[dev].store(p, std::memory_order_release);
+    slot.addr = static_cast<CeScratch*>(addr);
+    slot.ctx_id = id;
   }
-  *out = p;
+  *out = slot.addr;
   return OXI_CE_NOALLOC_OK;
 }
 
@@ -97,10 +108,8 @@ int scratch_for_current_device(CeScratch** out) {
 
 extern "C" {
 
-// Message for the last non-zero return code of this thread.
-__attribute__((visibility("default"))) const char* oxi_linear_ce_noalloc_last_error() { return g_last_error; }
+__attribute__((visibility("default"))) const char* oxi_linear_ce_noalloc_last_error(void) { return g_last_error; }
 
-// Largest supported sizes (for callers that split their problem).
 __attribute__((visibility("default"))) void oxi_linear_ce_noalloc_limits(int64_t* max_rows, int64_t* max_partials) {
   if (max_rows) *max_rows = OXI_CE_NOALLOC_MAX_ROWS;
   if (max_partials) *max_partials = OXI_CE_NOALLOC_MAX_PARTIALS;
@@ -137,7 +146,33 @@ __attribute__((visibility("default"))) int oxi_linear_ce_fwd_noalloc(const void*
                         stream);
     oxi::launch_ce_finish(s->part_max, s->part_sum, (int)tiles_n, s->tgt_logit, targets, lse, loss, M, stream);
   } catch (const std::exception& ex) {
+    // a failed launch or runtime call leaves a CUDA error behind; a failed
+    // shape / stride / alignment check does not
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      char buf[512];
+      std::snprintf(buf, sizeof(buf), "%s (%s)", cudaGetErrorString(e), ex.what());
+      return set_error(OXI_CE_NOALLOC_CUDA_ERROR, buf);
+    }
     return set_error(OXI_CE_NOALLOC_BAD_ARGUMENT, ex.what());
+  }
+  return OXI_CE_NOALLOC_OK;
+}
+
+__attribute__((visibility("default"))) int oxi_linear_ce_noalloc_status(int* status_out) {
+  g_last_error[0] = '\0';
+  CeScratch* s = nullptr;
+  int rc = scratch_for_current_device(&s);
+  if (rc) return rc;
+  int word = 0;
+  // a blocking device-to-host copy of one int from the fixed array (no allocation)
+  const cudaError_t e = cudaMemcpy(&word, s->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_error(OXI_CE_NOALLOC_CUDA_ERROR, cudaGetErrorString(e));
+  if (status_out) *status_out = word;
+  if (word != 0) {
+    char buf[128];
+    std::snprintf(buf, sizeof(buf), "the kernels of the last call recorded error code %d", word);
+    return set_error(OXI_CE_NOALLOC_KERNEL_ERROR, buf);
   }
   return OXI_CE_NOALLOC_OK;
 }

@@ -344,23 +344,38 @@ void ipc_close(int64_t ptr, int64_t device) {
 
 int64_t pad_words() { return oxi::PAD_WORDS; }
 
-void grad_to_bf16(torch::Tensor g, torch::Tensor out) {
+void grad_to_bf16(torch::Tensor g, torch::Tensor out, bool zero) {
   c10::cuda::CUDAGuard gd(g.device());
   TORCH_CHECK(g.scalar_type() == torch::kFloat32 && out.scalar_type() == torch::kBFloat16 && g.numel() == out.numel()
               && g.is_contiguous() && out.is_contiguous(), "grad_to_bf16");
-  oxi::launch_grad_to_bf16(g.data_ptr<float>(), out.data_ptr(), g.numel(), stream());
+  oxi::launch_grad_to_bf16(g.data_ptr<float>(), out.data_ptr(), g.numel(), zero, stream());
 }
 
-void rs_bucket(int64_t mode, torch::Tensor grad, torch::Tensor peers_buf, torch::Tensor my_buf, torch::Tensor peer_pads,
-               torch::Tensor my_pad, torch::Tensor done_ctr, int64_t rank, int64_t W, int64_t bucket, int64_t epoch,
-               int64_t lo, int64_t len, torch::Tensor rgrad_shard, torch::Tensor sumsq, int64_t ctas,
-               torch::Tensor status, int64_t wait_ns) {
+void bf16_to_f32_sumsq(torch::Tensor src, torch::Tensor dst, torch::Tensor sumsq) {
+  c10::cuda::CUDAGuard gd(src.device());
+  TORCH_CHECK(src.scalar_type() == torch::kBFloat16 && dst.scalar_type() == torch::kFloat32 &&
+                  src.numel() == dst.numel() && src.is_contiguous() && dst.is_contiguous() &&
+                  sumsq.scalar_type() == torch::kFloat32,
+              "bf16_to_f32_sumsq: bf16 src, f32 dst of the same size, f32 sumsq");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(src.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(dst.data_ptr()) & 15) == 0,
+              "bf16_to_f32_sumsq: 16-byte aligned buffers");
+  oxi::launch_bf16_to_f32_sumsq(src.data_ptr(), dst.data_ptr<float>(), src.numel(), sumsq.data_ptr<float>(),
+                                stream());
+}
+
+void rs_bucket(int64_t mode, torch::Tensor grad, bool zero_grad, torch::Tensor peers_buf, torch::Tensor my_buf,
+               int64_t mc_buf, torch::Tensor peer_pads, torch::Tensor my_pad, torch::Tensor done_ctr, int64_t rank,
+               int64_t W, int64_t bucket, int64_t epoch, int64_t lo, int64_t len, torch::Tensor rgrad_shard,
+               torch::Tensor sumsq, int64_t ctas, torch::Tensor status, int64_t wait_ns) {
   c10::cuda::CUDAGuard gd(my_pad.device());
   TORCH_CHECK(grad.scalar_type() == torch::kFloat32 && grad.is_contiguous(), "grad must be contiguous f32");
   TORCH_CHECK(done_ctr.scalar_type() == torch::kInt32 && done_ctr.numel() >= oxi::PAD_MAXB, "done_ctr");
-  oxi::launch_rs_bucket((int)mode, grad.data_ptr<float>(),
+  TORCH_CHECK(lo >= 0 && len >= 0 && lo + len <= grad.numel() && rgrad_shard.numel() >= len / std::max<int64_t>(W, 1),
+              "bucket range outside the gradient buffer");
+  oxi::launch_rs_bucket((int)mode, grad.data_ptr<float>(), zero_grad,
                         reinterpret_cast<const uint64_t*>(peers_buf.data_ptr<int64_t>()), my_buf.data_ptr(),
-                        reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()),
+                        reinterpret_cast<void*>(mc_buf), reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()),
                         my_pad.data_ptr<int>(), done_ctr.data_ptr<int>(), (int)rank, (int)W, (int)bucket, (int)epoch,
                         lo, len, rgrad_shard.data_ptr<float>(), sumsq.data_ptr<float>(), (int)ctas,
                         status_ptr(status), wait_ns, stream());
@@ -375,21 +390,32 @@ void norm_exchange(torch::Tensor peer_pads, torch::Tensor my_pad, int64_t rank, 
                             coef.data_ptr<float>(), norm.data_ptr<float>(), status_ptr(status), wait_ns, stream());
 }
 
-void adamw_allgather(torch::Tensor buckets, int64_t rank, int64_t W, torch::Tensor rgrad, torch::Tensor master,
-                     torch::Tensor m, torch::Tensor v, torch::Tensor peers_param, torch::Tensor peer_pads,
-                     torch::Tensor my_pad, int64_t epoch, double lr, double b1, double b2, double eps, double wd,
-                     double bc1, double bc2, torch::Tensor coef, torch::Tensor done_ctr, torch::Tensor status,
-                     int64_t wait_ns) {
+void adamw_ag_bucket(int64_t mode, int64_t lo, int64_t len, int64_t so, int64_t W, int64_t rank, int64_t ndst,
+                     torch::Tensor rgrad, torch::Tensor master, torch::Tensor m, torch::Tensor v,
+                     torch::Tensor peers_param, int64_t mc_param, c10::optional<torch::Tensor> peer_pads,
+                     int64_t bucket, int64_t epoch, double lr, double b1, double b2, double eps, double wd, double bc1,
+                     double bc2, torch::Tensor coef, torch::Tensor done_ctr, torch::Tensor status, int64_t ctas) {
+  c10::cuda::CUDAGuard gd(master.device());
+  TORCH_CHECK(rgrad.scalar_type() == torch::kFloat32 && master.scalar_type() == torch::kFloat32 &&
+                  m.scalar_type() == torch::kFloat32 && v.scalar_type() == torch::kFloat32,
+              "adamw_ag_bucket: f32 shard state");
+  TORCH_CHECK(W >= 1 && so >= 0 && so + len / W <= master.numel() && rgrad.numel() == master.numel() &&
+                  m.numel() == master.numel() && v.numel() == master.numel(),
+              "adamw_ag_bucket: shard range outside the optimizer state");
+  const uint64_t* pads = nullptr;
+  if (peer_pads.has_value() && peer_pads->defined())
+    pads = reinterpret_cast<const uint64_t*>(peer_pads->data_ptr<int64_t>());
+  oxi::launch_adamw_ag_bucket((int)mode, lo, len, so, (int)W, (int)rank, (int)ndst, rgrad.data_ptr<float>(),
+                              master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                              reinterpret_cast<const uint64_t*>(peers_param.data_ptr<int64_t>()),
+                              reinterpret_cast<void*>(mc_param), pads, (int)bucket, (int)epoch, (float)lr, (float)b1,
+                              (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2, coef.data_ptr<float>(),
+                              done_ctr.data_ptr<int>(), status_ptr(status), (int)ctas, stream());
+}
+
+void ag_wait(torch::Tensor my_pad, int64_t W, int64_t bucket, int64_t epoch, torch::Tensor status, int64_t wait_ns) {
   c10::cuda::CUDAGuard gd(my_pad.device());
-  TORCH_CHECK(buckets.scalar_type() == torch::kInt64 && buckets.is_cuda() && buckets.dim() == 2 && buckets.size(1) == 3,
-              "buckets must be int64 CUDA [nb, 3]");
-  oxi::launch_adamw_allgather(buckets.data_ptr<int64_t>(), (int)buckets.size(0), (int)rank, (int)W,
-                              rgrad.data_ptr<float>(), master.data_ptr<float>(), m.data_ptr<float>(),
-                              v.data_ptr<float>(), reinterpret_cast<const uint64_t*>(peers_param.data_ptr<int64_t>()),
-                              reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
-                              (int)epoch, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1,
-                              (float)bc2, coef.data_ptr<float>(), done_ctr.data_ptr<int>(), status_ptr(status),
-                              wait_ns, stream());
+  oxi::launch_ag_wait(my_pad.data_ptr<int>(), (int)W, (int)bucket, (int)epoch, status_ptr(status), wait_ns, stream());
 }
 
 // ------------------------------------------------------------ expert parallelism (NVLink)
@@ -536,24 +562,6 @@ bool enable_peer_access(int64_t device, int64_t peer) {
   }
   C10_CUDA_CHECK(e);
   return true;
-}
-
-void p2p_read(int64_t src, int64_t bytes, torch::Tensor sink, int64_t ctas, int64_t threads, int64_t unr) {
-  c10::cuda::CUDAGuard g(sink.device());
-  oxi::launch_p2p_read(reinterpret_cast<const void*>(src), bytes, sink.data_ptr(), (int)ctas, (int)threads, (int)unr,
-                       stream());
-}
-
-void p2p_write(int64_t dst, int64_t bytes, torch::Tensor on_device, int64_t ctas, int64_t threads, int64_t unr) {
-  c10::cuda::CUDAGuard g(on_device.device());
-  oxi::launch_p2p_write(reinterpret_cast<void*>(dst), bytes, (int)ctas, (int)threads, (int)unr, stream());
-}
-
-void p2p_bulk(bool write, int64_t peer, int64_t bytes, int64_t ctas, int64_t chunk, int64_t stages,
-              torch::Tensor status) {
-  c10::cuda::CUDAGuard g(status.device());
-  oxi::launch_p2p_bulk(write, reinterpret_cast<void*>(peer), bytes, (int)ctas, (int)chunk, (int)stages,
-                       status_ptr(status), stream());
 }
 
 // ------------------------------------------------------------ tensor-core SSD
@@ -1084,15 +1092,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_push_dy", &ep_push_dy, "expert-parallel backward: push output gradients to the owners, routing-weight grads");
   m.def("ep_scale_rows", &ep_scale_rows, "owner side: scale received gradient rows by their routing weights");
   m.def("enable_peer_access", &enable_peer_access, "cudaDeviceEnablePeerAccess(device -> peer)");
-  m.def("p2p_read", &p2p_read, "microbenchmark: SM loads from (peer) memory");
-  m.def("p2p_write", &p2p_write, "microbenchmark: SM stores to (peer) memory");
-  m.def("p2p_bulk", &p2p_bulk, "microbenchmark: bulk (TMA engine) copies from/to (peer) memory");
   m.def("ipc_alloc", &ipc_alloc, "zeroed device buffer exportable over CUDA IPC");
   m.def("ipc_open", &ipc_open, "map a peer's IPC buffer");
   m.def("ipc_close", &ipc_close, "unmap a peer's IPC buffer");
   m.def("pad_words", &pad_words, "int32 words of one signal pad");
-  m.def("grad_to_bf16", &grad_to_bf16, "f32 gradient -> bf16 NVLink payload");
-  m.def("rs_bucket", &rs_bucket, "NVLink push + local reduce of one gradient bucket");
+  m.def("grad_to_bf16", &grad_to_bf16, "f32 gradient -> bf16 NVLink payload (optionally clearing the source)");
+  m.def("bf16_to_f32_sumsq", &bf16_to_f32_sumsq, "bf16 shard -> f32 copy + sum of squares");
+  m.def("ag_wait", &ag_wait, "bounded wait for every rank's all-gather of one bucket");
+  m.def("rs_bucket", &rs_bucket, "reduce-scatter of one gradient bucket (pull, push or NVLS)");
   m.def("norm_exchange", &norm_exchange, "cross-rank gradient norm and clip coefficient");
-  m.def("adamw_allgather", &adamw_allgather, "sharded AdamW + P2P bf16 parameter all-gather");
+  m.def("adamw_ag_bucket", &adamw_ag_bucket, "sharded AdamW + bf16 parameter all-gather of one bucket");
 }

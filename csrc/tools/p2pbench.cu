@@ -2,12 +2,13 @@
 // or write another GPU's memory, as a function of CTAs, bytes in flight per
 // thread, and thread loads/stores versus bulk (TMA engine) copies.  Used to
 // size the reduce-scatter / all-gather / expert-dispatch kernels.  No kernel
-// here waits on another GPU; each just moves `bytes` bytes.
+// here waits on another GPU; each just moves `bytes` bytes.  Built as its own
+// extension (oxidizr_b200_tools), not part of the training library.
 #include <cuda_runtime.h>
 #include <cstdint>
 
 #include "host_util.h"
-#include "kernels_comm.h"
+#include "p2pbench.h"
 #include "ptx.cuh"
 
 namespace oxi {

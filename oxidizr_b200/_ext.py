@@ -32,6 +32,13 @@ NVCC_FLAGS = [
 _lock = threading.Lock()
 _mod = None
 
+# Measurement tools (NVLink access microbenchmark) live in a separate
+# extension built from csrc/tools/, so the training library carries none of them.
+TOOLS_DIR = os.path.join(CSRC, "tools")
+TOOLS_BUILD_DIR = os.path.join(REPO, "build", "oxidizr_b200_tools")
+TOOLS_NAME = "oxidizr_b200_tools"
+_tools = None
+
 
 def sources():
     return sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
@@ -100,3 +107,26 @@ def load(required: bool = True):
                 raise RuntimeError(f"oxidizr_b200 CUDA extension unavailable: {e}") from e
             return None
         return _mod
+
+
+def tools_sources():
+    return sorted(glob.glob(os.path.join(TOOLS_DIR, "*.cu"))) + sorted(glob.glob(os.path.join(TOOLS_DIR, "*.cpp")))
+
+
+def build_tools(verbose: bool = False):
+    """Compile the measurement-tools extension (csrc/tools/) for sm_100a."""
+    os.makedirs(TOOLS_BUILD_DIR, exist_ok=True)
+    from torch.utils.cpp_extension import load as _load
+    return _load(name=TOOLS_NAME, sources=tools_sources(), extra_cflags=["-O3", "-std=c++17"],
+                 extra_cuda_cflags=NVCC_FLAGS, extra_include_paths=[CSRC, TOOLS_DIR],
+                 build_directory=TOOLS_BUILD_DIR, with_cuda=True, verbose=verbose)
+
+
+def load_tools():
+    """The measurement-tools extension module (built on first use)."""
+    global _tools
+    with _lock:
+        if _tools is None:
+            import torch  # noqa: F401
+            _tools = build_tools(verbose=bool(os.environ.get("OXI_BUILD_VERBOSE")))
+        return _tools

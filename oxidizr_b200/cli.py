@@ -136,7 +136,7 @@ def run_train(args, argv: List[str]) -> int:
     run_dir = os.environ.get("OXIDIZED_RUN_DIR")
     if run_dir is None:
         run_dir = os.path.join(".", "runs", datetime.datetime.now().strftime("%Y%m%d_%H%M%S"))
-        os.makedirs(run_dir, exist_ok=True)
+    os.makedirs(run_dir, exist_ok=True)
     say = (lambda s: out(s)) if (not headless and rank == 0) else (lambda s: None)
     say("=== Oxidizr Training Framework ===")
     say(f"Run directory: {run_dir}\n")
@@ -210,10 +210,10 @@ def run_train(args, argv: List[str]) -> int:
     if world > 1:
         from .parallel.ddp import make_ddp_optimizer
         be = backend if backend != "single" else "nccl"
-        if be == "fused" and device.type != "cuda":
+        if be in ("fused", "nccl_sharded") and device.type != "cuda":
             be = "cpustaging"
-        opt = make_ddp_optimizer(model.named_parameters(), ocfg, device, be, group=group)
-        flat = getattr(opt, "flat", None) if be != "fused" else None
+        opt = make_ddp_optimizer(model.named_parameters(), ocfg, device, be, group=group, model=model)
+        flat = getattr(opt, "flat", None) if be not in ("fused", "nccl_sharded") else None
     else:
         flat = FlatParams(list(model.named_parameters()), device)
         opt = AdamW(flat, ocfg)

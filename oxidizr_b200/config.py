@@ -52,7 +52,7 @@ def torch_dtype(s: str):
     return {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[s]
 
 
-SYNC_BACKENDS = ("single", "cpustaging", "nccl", "fused")
+SYNC_BACKENDS = ("single", "cpustaging", "nccl", "nccl_sharded", "fused")
 
 
 def parse_sync_backend(s: str) -> str:
@@ -64,9 +64,11 @@ def parse_sync_backend(s: str) -> str:
         return "cpustaging"
     if v == "nccl":
         return "nccl"
+    if v in ("nccl_sharded", "nccl-sharded"):
+        return "nccl_sharded"
     if v == "fused":
         return "fused"
-    raise ConfigError(f"Unknown sync backend: {s}. Valid options: single, cpu, nccl, fused")
+    raise ConfigError(f"Unknown sync backend: {s}. Valid options: single, cpu, nccl, nccl_sharded, fused")
 
 
 _REQUIRED = object()

@@ -84,6 +84,10 @@ class LitGPT(RefModule):
         self.layers = nn.ModuleList([make_block(cfg, i, device, dtype, ep_group) for i in range(cfg.num_layers)])
         self.norm = NormW(H, device=device, dtype=dtype)
         self.lm_head = nn.Parameter(torch.empty(V, H, device=device, dtype=dtype))
+        # Optional callable given the parameters a part of the forward is about to
+        # use; a sharded data-parallel optimizer sets it so that the forward waits
+        # for each parameter bucket's all-gather only when it first needs it.
+        self._param_gate = None
 
     def reset_parameters(self, seed: Optional[int] = None):
         gen = None
@@ -100,12 +104,19 @@ class LitGPT(RefModule):
 
     # ------------------------------------------------------------ forward
     def hidden(self, ids: torch.Tensor) -> Tuple[torch.Tensor, List[torch.Tensor]]:
+        gate = self._param_gate
+        if gate is not None:
+            gate((self.embed_tokens,))
         x = api.embedding(ids, self.embed_tokens)
         aux = []
         for layer in self.layers:
+            if gate is not None:
+                gate(layer.parameters())
             x, a = layer(x)
             if a is not None:
                 aux.append(a)
+        if gate is not None:
+            gate((self.norm.weight, self.lm_head))
         x = api.rmsnorm(x, self.norm.weight, 1e-5)
         return x, aux
 

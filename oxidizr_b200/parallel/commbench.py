@@ -1,23 +1,30 @@
 """Data-parallel gradient-sync microbenchmark (one process per GPU).
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
-        -m oxidizr_b200.parallel.commbench --params 1280e6 [--iters 5]
+        -m oxidizr_b200.parallel.commbench --params 1280e6 [--iters 5] [--modes pull,nvls]
 
 Times, on the device with CUDA events (max over ranks), for a flat model of
-``--params`` bf16 parameters split into 32 M-element tensors:
+``--params`` bf16 parameters split into 32 M-element tensors, the whole
+synchronisation + optimizer step that follows backward (every bucket's
+reduce-scatter, the clip-norm exchange, the sharded AdamW and the parameter
+all-gather, waited for by the compute stream):
 
-* ``fused``      -- the NVLink path of :class:`FusedDDPAdamW` after backward:
-                    bf16 reduce-scatter of every bucket (NVLink push + local sum), norm
-                    exchange + clip, sharded AdamW, P2P parameter all-gather;
-* ``fused_rs``   -- the reduce-scatter part alone;
-* ``nccl_ar``    -- NCCL all-reduce of the f32 gradient + full AdamW (the
-                    ``nccl`` backend without overlap);
-* ``nccl_rs_ag`` -- NCCL bf16 reduce-scatter + all-gather (transfer only).
+* ``fused_<mode>``  -- :class:`FusedDDPAdamW` over NVLink with our kernels
+                       (``pull``/``push`` P2P, ``nvls`` multicast), at the
+                       trainer's default CTA budgets;
+* ``nccl_sharded``  -- the same algorithm with NCCL bf16 reduce-scatter and
+                       all-gather as the transport (like-for-like baseline);
+* ``nccl_ar``       -- NCCL f32 all-reduce + replicated AdamW (the ``nccl``
+                       backend, upstream's algorithm), for reference.
 
-The roofline of the fused step is the slower of the NVLink bytes (reduce-
-scatter in + all-gather out, (W-1)/W of the bf16 gradient each way, at the
-measured 770 GB/s per direction) and the HBM bytes of the sharded AdamW at the
-measured copy bandwidth.  Rank 0 prints one JSON line.
+Roofline of a step (per GPU): the slower of its NVLink bytes at the measured
+770 GB/s per direction and its HBM bytes at the measured copy bandwidth.
+With N parameters and W ranks: HBM = cast (read f32, write bf16, clear f32:
+10N) + send buffer read by the owners (2N) + reduced shard (4N/W) + sharded
+AdamW (28N/W) + parameters received (2N); NVLink out = 4N(W-1)/W for P2P
+(each phase sends (W-1)/W of the bf16 gradient) or 2N + 2N/W for NVLS (the
+switch reads the whole send buffer once, the all-gather multicasts the shard
+once).  Rank 0 prints one JSON line.
 
 Upstream path it replaces: distributed/nccl.rs:153-184 (per-parameter NCCL all-reduce
 through host copies) and distributed/optimizer.rs:126-192 (AdamW).
@@ -35,19 +42,35 @@ import torch.distributed as dist
 NVLINK_GBS = 770.0  # measured peer copy, GB/s per direction per GPU
 
 
-def _time(fn, iters, dev):
+def _time(fn, iters, dev, prep=None):
+    """Max over ranks of the mean device time of fn() (prep() runs untimed before each call)."""
+    if prep:
+        prep()
     fn()
     torch.cuda.synchronize(dev)
     dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    tot = 0.0
     for _ in range(iters):
+        if prep:
+            prep()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         fn()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    ms = torch.tensor([e0.elapsed_time(e1) / iters], device=dev, dtype=torch.float64)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        tot += e0.elapsed_time(e1)
+    ms = torch.tensor([tot / iters], device=dev, dtype=torch.float64)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     return float(ms.item())
+
+
+def roofline_ms(N: int, W: int, mode: str, hbm_gbs: float) -> dict:
+    hbm = 10 * N + 2 * N + 4 * N / W + 28 * N / W + 2 * N
+    nvl = (2 * N + 2 * N / W) if mode == "nvls" else 4 * N * (W - 1) / W
+    t_h = hbm / (hbm_gbs * 1e9) * 1e3
+    t_n = nvl / (NVLINK_GBS * 1e9) * 1e3
+    return {"hbm_ms": round(t_h, 3), "nvlink_ms": round(t_n, 3), "roofline_ms": round(max(t_h, t_n), 3),
+            "bound": "hbm" if t_h >= t_n else "nvlink"}
 
 
 def main(argv=None):
@@ -56,9 +79,10 @@ def main(argv=None):
     ap.add_argument("--chunk", type=float, default=32e6)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--bucket-mb", type=int, default=32)
-    ap.add_argument("--rs-ctas", default="64",
-                    help="comma list: CTA budgets of the reduce-scatter to sweep (the first is used for the full "
-                         "fused step; 64 is the trainer's default)")
+    ap.add_argument("--modes", default="auto",
+                    help="comma list of fused transports to time: pull, push, nvls (auto: pull, plus nvls "
+                         "when the GPUs support multicast)")
+    ap.add_argument("--no-nccl-ar", action="store_true")
     args = ap.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -67,79 +91,61 @@ def main(argv=None):
     W, rank = dist.get_world_size(), dist.get_rank()
     from ..optim import AdamW, AdamWConfig, FlatParams
     from ..ops._C import check_status
-    from .fused_ar import FusedDDPAdamW
+    from ..utils.kbench import measured_peaks
+    from .fused_ar import FusedDDPAdamW, NcclShardedAdamW, multicast_supported
+    hbm = measured_peaks()["hbm_gbs"]
     n_total, chunk = int(args.params), int(args.chunk)
     sizes = [chunk] * (n_total // chunk) + ([n_total % chunk] if n_total % chunk else [])
     gen = torch.Generator(device=dev).manual_seed(rank)
     params = [torch.nn.Parameter(torch.randn(n, device=dev, generator=gen).mul_(0.02).bfloat16()) for n in sizes]
     cfg = AdamWConfig(lr=1e-4)
-    res = {"params": n_total, "world": W}
+    res = {"params": n_total, "world": W, "hbm_gbs": hbm, "nvlink_gbs": NVLINK_GBS,
+           "multicast_supported": multicast_supported(dev)}
+    modes = args.modes.split(",") if args.modes != "auto" else (["pull"] + (["nvls"] if res["multicast_supported"]
+                                                                           else []))
 
-    sweep = [int(c) for c in str(args.rs_ctas).split(",")]
-    opt = FusedDDPAdamW([(f"p{i}", p) for i, p in enumerate(params)], cfg, dev, bucket_bytes=args.bucket_mb << 20,
-                        rs_ctas=sweep[0])
-    opt.grad.normal_(generator=gen)
+    def time_sharded(opt):
+        def refill():
+            opt.grad.normal_(generator=gen)  # the casts clear the gradient as they read it
+        return _time(opt.step, args.iters, dev, prep=refill)
 
-    def fused_step():
-        opt.step()
-        opt.grad.normal_(generator=gen)  # step() zeroes the gradient
+    named = [(f"p{i}", p) for i, p in enumerate(params)]
+    for mode in modes:
+        opt = FusedDDPAdamW(named, cfg, dev, bucket_bytes=args.bucket_mb << 20, mode=mode)
+        key = f"fused_{opt.mode}"
+        if opt.mode != mode:
+            res[f"fused_{mode}_unavailable"] = f"fell back to {opt.mode}"
+        ms = time_sharded(opt)
+        rf = roofline_ms(opt.N, W, opt.mode, hbm)
+        res[key] = {"ms": round(ms, 3), **rf, "frac_of_roofline": round(rf["roofline_ms"] / ms, 3),
+                    "rs_ctas": opt.rs_ctas, "ag_ctas": opt.ag_ctas}
+        torch.cuda.synchronize(dev)
+        check_status(dev)
+        opt.close()
+        del opt
+        torch.cuda.empty_cache()
 
-    def grad_refill():
-        opt.grad.normal_(generator=gen)
-
-    ms_refill = _time(grad_refill, args.iters, dev)
-    res["fused_ms"] = round(_time(fused_step, args.iters, dev) - ms_refill, 3)
-
-    def fused_rs():
-        opt._launched = [False] * len(opt.buckets)
-        opt._sumsq_zeroed = False
-        for bi in range(len(opt.buckets)):
-            opt._launch(bi)
-        torch.cuda.current_stream(dev).wait_stream(opt.comm_stream)
-        opt.epoch += 1
-
-    # the reduce-scatter alone: bump the epoch on every rank in lockstep
-    res["fused_rs_ms"] = round(_time(fused_rs, args.iters, dev), 3)
-    for c in sweep[1:]:
-        opt.rs_ctas = c
-        res[f"fused_rs_ms_ctas{c}"] = round(_time(fused_rs, args.iters, dev), 3)
-    opt.rs_ctas = sweep[0]
-    torch.cuda.synchronize(dev)
-    check_status(dev)
+    opt = NcclShardedAdamW(named, cfg, dev, bucket_bytes=args.bucket_mb << 20)
+    ms = time_sharded(opt)
+    rf = roofline_ms(opt.N, W, "pull", hbm)
+    res["nccl_sharded"] = {"ms": round(ms, 3), **rf, "frac_of_roofline": round(rf["roofline_ms"] / ms, 3)}
     opt.close()
     del opt
     torch.cuda.empty_cache()
+    best = min((v["ms"], k) for k, v in res.items() if k.startswith("fused_") and isinstance(v, dict))
+    res["best_fused"] = best[1]
+    res["speedup_vs_nccl_sharded"] = round(res["nccl_sharded"]["ms"] / best[0], 3)
 
-    flat = FlatParams([(f"p{i}", p) for i, p in enumerate(params)], dev)
-    base = AdamW(flat, cfg)
-    flat.grad.normal_(generator=gen)
+    if not args.no_nccl_ar:
+        flat = FlatParams(named, dev)
+        base = AdamW(flat, cfg)
+        flat.grad.normal_(generator=gen)
 
-    def nccl_ar():
-        dist.all_reduce(flat.grad)
-        base.step(1.0 / W)
+        def nccl_ar():
+            dist.all_reduce(flat.grad)
+            base.step(1.0 / W)
 
-    res["nccl_ar_ms"] = round(_time(nccl_ar, args.iters, dev), 3)
-    g16 = torch.randn(n_total // (W * 8) * W * 8, device=dev, generator=gen).bfloat16()
-    shard = torch.empty(g16.numel() // W, device=dev, dtype=torch.bfloat16)
-
-    def nccl_rs_ag():
-        dist.reduce_scatter_tensor(shard, g16)
-        dist.all_gather_into_tensor(g16, shard)
-
-    res["nccl_rs_ag_ms"] = round(_time(nccl_rs_ag, args.iters, dev), 3)
-    # rooflines
-    from ..utils.kbench import measured_peaks
-    hbm = measured_peaks()["hbm_gbs"]
-    nvl_bytes = (W - 1) / W * n_total * 2  # per direction per GPU, each phase
-    rs_ms = nvl_bytes / (NVLINK_GBS * 1e9) * 1e3
-    adam_bytes = n_total / W * (4 * 7) + n_total * 2 * 2  # shard f32 state r/w + bf16 grads/params
-    adam_ms = adam_bytes / (hbm * 1e9) * 1e3
-    res["roofline_rs_ms"] = round(rs_ms, 3)
-    res["roofline_fused_ms"] = round(max(2 * rs_ms, adam_ms), 3)
-    res["fused_rs_frac_of_roofline"] = round(rs_ms / res["fused_rs_ms"], 3)
-    res["fused_frac_of_roofline"] = round(res["roofline_fused_ms"] / res["fused_ms"], 3)
-    res["fused_rs_gbs_per_dir"] = round(nvl_bytes / (res["fused_rs_ms"] * 1e-3) / 1e9, 1)
-    res["nccl_rs_ag_gbs_per_dir"] = round(2 * nvl_bytes / (res["nccl_rs_ag_ms"] * 1e-3) / 1e9, 1)
+        res["nccl_ar_ms"] = round(_time(nccl_ar, args.iters, dev), 3)
     if rank == 0:
         print(json.dumps(res), flush=True)
     dist.barrier()

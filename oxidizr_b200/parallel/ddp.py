@@ -10,6 +10,10 @@ really reduced:
   host-staged GPU tensors); used by the CPU multi-process tests;
 * ``nccl``       -- bucketed NCCL all-reduce, each bucket launched on a side
   stream as soon as backward has produced all of its gradients (baseline);
+* ``nccl_sharded`` -- the sharded algorithm of the product path (bucketed
+  bf16 reduce-scatter overlapped with backward, sharded AdamW, bucketed bf16
+  all-gather overlapped with the next forward) with NCCL as the transport:
+  the like-for-like baseline of ``fused``;
 * ``fused``      -- the sm_100a NVLink reduce-scatter + clip + AdamW +
   all-gather kernels of :mod:`oxidizr_b200.parallel.fused_ar` (product path).
 
@@ -118,14 +122,20 @@ class DDPAdamW(AdamW):
         return super().step(grad_scale / self.world)
 
 
-def make_ddp_optimizer(named_params, cfg: AdamWConfig, device, backend: str, group=None, **kw):
+def make_ddp_optimizer(named_params, cfg: AdamWConfig, device, backend: str, group=None, model=None, **kw):
     """Data-parallel AdamW over a model's parameters for ``backend`` in
-    ``cpustaging | nccl | fused``.  Expert-parallel shards (``_oxi_ep_local``)
-    are updated locally; everything else is averaged over the group."""
+    ``cpustaging | nccl | nccl_sharded | fused``.  Expert-parallel shards
+    (``_oxi_ep_local``) are updated locally; everything else is averaged over
+    the group.  With ``model`` (a LitGPT) the sharded backends overlap their
+    parameter all-gather with the model's next forward."""
     named_params = list(named_params)
-    if backend == "fused":
-        from .fused_ar import FusedDDPAdamW
-        return FusedDDPAdamW(named_params, cfg, device, group=group, **kw)
+    if backend in ("fused", "nccl_sharded"):
+        from .fused_ar import FusedDDPAdamW, NcclShardedAdamW
+        cls = FusedDDPAdamW if backend == "fused" else NcclShardedAdamW
+        opt = cls(named_params, cfg, device, group=group, **kw)
+        if model is not None:
+            opt.attach(model)
+        return opt
     rep, loc = split_local(named_params)
     local = LocalAdamW(loc, cfg, device) if loc else None
     return DDPAdamW(FlatParams(rep, device), cfg, backend=backend, group=group, local=local, **kw)

@@ -40,7 +40,7 @@ def main(argv=None):
     args = ap.parse_args(argv)
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
-    use_cuda = args.backend in ("nccl", "fused")
+    use_cuda = args.backend in ("nccl", "nccl_sharded", "fused")
     if use_cuda:
         local = int(os.environ.get("LOCAL_RANK", rank))
         torch.cuda.set_device(local)
@@ -55,7 +55,8 @@ def main(argv=None):
     model = build_model(cfg.model, device=dev, seed=0)
     ocfg = AdamWConfig(lr=1e-3)
     from .ddp import make_ddp_optimizer
-    opt = make_ddp_optimizer(model.named_parameters(), ocfg, dev, args.backend, bucket_bytes=1 << 18)
+    kw = {"model": model} if args.backend in ("fused", "nccl_sharded") else {}
+    opt = make_ddp_optimizer(model.named_parameters(), ocfg, dev, args.backend, bucket_bytes=1 << 18, **kw)
     g = torch.Generator(device="cpu").manual_seed(100 + rank)
     losses, norms = [], []
     for step in range(args.steps):
@@ -67,7 +68,9 @@ def main(argv=None):
         dist.all_reduce(lt)
         losses.append(float(lt) / world)
         norms.append(float(gn))
-        # replicas must stay identical
+        # replicas must stay identical (a sharded optimizer's all-gather lands first)
+        if hasattr(opt, "sync_params"):
+            opt.sync_params()
         flat = torch.cat([p.detach().float().reshape(-1) for p in model.parameters()])
         ck = torch.stack([flat.sum(), flat.abs().sum()]).to(dev)
         allck = [torch.zeros_like(ck) for _ in range(world)]

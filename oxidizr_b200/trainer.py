@@ -256,6 +256,9 @@ class Trainer:
     # ------------------------------------------------------------ checkpoints
     def _gather_weights(self):
         """Weights in upstream names on rank 0 (collective when experts are sharded)."""
+        sync = getattr(self.opt, "sync_params", None)
+        if sync is not None:
+            sync()  # a sharded optimizer's parameter all-gather may still be landing
         if hasattr(self.model, "export_ref_gathered"):
             return self.model.export_ref_gathered()
         return self.model.export_ref() if self.rank == 0 else None

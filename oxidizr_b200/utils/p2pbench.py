@@ -8,6 +8,8 @@ threads x 16-byte vectors in flight per thread), bulk copies through the TMA
 engine (chunk bytes x stages in flight per CTA), and the copy engine
 (cudaMemcpyPeerAsync via torch).  Prints one JSON line per configuration and
 a summary of the best of each kind (GB/s, CUDA-event timed after warm-up).
+The kernels are in the separate tools extension (csrc/tools/), not in the
+training library.
 """
 from __future__ import annotations
 
@@ -33,10 +35,11 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--mb", type=int, default=1024)
     args = ap.parse_args(argv)
+    from .. import _ext
     from ..ops._C import ext, status
     assert torch.cuda.device_count() >= 2, "needs two GPUs"
-    e = ext()
-    ok = e.enable_peer_access(0, 1)
+    ok = ext().enable_peer_access(0, 1)
+    e = _ext.load_tools()
     nbytes = args.mb << 20
     torch.cuda.set_device(0)
     remote = torch.empty(nbytes, dtype=torch.uint8, device="cuda:1")

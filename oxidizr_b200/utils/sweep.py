@@ -86,6 +86,9 @@ def run(grid, config: Optional[str], max_steps: int, extra: Sequence[str], out_r
                "--seq-len", str(seq), "--batch-size", str(batch), "--grad-accum", str(grad),
                "--max-steps", str(max_steps), *extra]
         print(f"Running: seq={seq}, batch={batch}, grad_accum={grad}", flush=True)
+        # each point's run.json / steps.json go under the sweep's own directory,
+        # never into the caller's working directory
+        env["OXIDIZED_RUN_DIR"] = os.path.join(bench_dir, "runs", f"seq{seq}_b{batch}_g{grad}")
         try:
             r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
             rc, output = r.returncode, r.stdout + r.stderr

@@ -22,12 +22,13 @@ def _port():
         return s.getsockname()[1]
 
 
-def _run(backend, world, tmp_path, steps=3, timeout=240):
-    out = str(tmp_path / f"{backend}_{world}.json")
+def _run(backend, world, tmp_path, steps=3, timeout=240, env_extra=None):
+    tag = "_".join(f"{k}{v}" for k, v in sorted((env_extra or {}).items()))
+    out = str(tmp_path / f"{backend}_{world}{tag}.json")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr=127.0.0.1", f"--master-port={_port()}", "-m", "oxidizr_b200.parallel.selftest",
            "--backend", backend, "--steps", str(steps), "--out", out]
-    env = dict(os.environ, PYTHONPATH=REPO, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="1")
+    env = dict(os.environ, PYTHONPATH=REPO, NCCL_NVLS_ENABLE="0", OMP_NUM_THREADS="1", **(env_extra or {}))
     r = subprocess.run(["timeout", "-k", "30", str(timeout)] + cmd, cwd=REPO, env=env, capture_output=True,
                        text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
@@ -51,6 +52,28 @@ def test_fused_ddp_matches_nccl(tmp_path):
         assert abs(la - lb) < 2e-2 * abs(la), (a["losses"], b["losses"])
     for na, nb in zip(a["grad_norms"], b["grad_norms"]):
         assert abs(na - nb) < 5e-2 * abs(na) + 1e-3, (a["grad_norms"], b["grad_norms"])
+
+
+def _multicast_ok() -> bool:
+    from oxidizr_b200.parallel.fused_ar import multicast_supported
+    return multicast_supported(torch.device("cuda", 0))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["pull", "push", "nvls"])
+def test_sharded_transports_agree(tmp_path, mode):
+    """The NVLink transports (P2P pull / push, NVLS multicast) against the same
+    sharded algorithm over NCCL: the same losses, norms and replicas."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    if mode == "nvls" and not _multicast_ok():
+        pytest.skip("no multicast support on these GPUs")
+    a = _run("nccl_sharded", 2, tmp_path, steps=4)
+    b = _run("fused", 2, tmp_path, steps=4, env_extra={"OXI_AR_MODE": mode})
+    for la, lb in zip(a["losses"], b["losses"]):
+        assert abs(la - lb) < 1e-2 * abs(la), (a["losses"], b["losses"])
+    for na, nb in zip(a["grad_norms"], b["grad_norms"]):
+        assert abs(na - nb) < 3e-2 * abs(na) + 1e-3, (a["grad_norms"], b["grad_norms"])
 
 
 @pytest.mark.gpu

@@ -28,7 +28,15 @@ def _lib():
                   ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                   ctypes.c_void_p]
     lib.oxi_linear_ce_noalloc_last_error.restype = ctypes.c_char_p
+    lib.oxi_linear_ce_noalloc_status.restype = ctypes.c_int
+    lib.oxi_linear_ce_noalloc_status.argtypes = [ctypes.POINTER(ctypes.c_int)]
     return lib
+
+
+def _status(lib):
+    word = ctypes.c_int(-1)
+    rc = lib.oxi_linear_ce_noalloc_status(ctypes.byref(word))
+    return rc, word.value
 
 
 def _regular(x, w, tg):
@@ -80,6 +88,8 @@ def test_noalloc_matches_regular_entry_point_twice():
         ce = full - logits.gather(1, tg.clamp_min(0)[:, None])[:, 0]
         assert torch.allclose(loss[valid], ce[valid], atol=2e-3, rtol=1e-3)
         assert torch.all(loss[~valid] == 0)
+        # the kernels recorded no error (status word read back after the sync)
+        assert _status(lib) == (0, 0), lib.oxi_linear_ce_noalloc_last_error()
 
 
 def test_noalloc_rejects_oversized_problem():
@@ -93,3 +103,45 @@ def test_noalloc_rejects_oversized_problem():
                                        out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == 1
     assert b"too large" in lib.oxi_linear_ce_noalloc_last_error()
+
+
+def _raw_call(lib, x_ptr, M, K, ldx, w_ptr, V, ldw, tg_ptr, loss_ptr, lse_ptr):
+    return lib.oxi_linear_ce_fwd_noalloc(x_ptr, M, K, ldx, w_ptr, V, ldw, tg_ptr, loss_ptr, lse_ptr,
+                                         torch.cuda.current_stream().cuda_stream)
+
+
+def test_noalloc_argument_paths_launch_nothing():
+    """Zero rows, bad strides, null pointers and the partials limit are
+    answered before any kernel is queued; outputs stay untouched."""
+    lib = _lib()
+    K, V = 64, 1000
+    x = torch.zeros(8, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.zeros(V, K, device="cuda", dtype=torch.bfloat16)
+    tg = torch.zeros(8, device="cuda", dtype=torch.int64)
+    loss = torch.full((8,), 7.0, device="cuda")
+    lse = torch.full((8,), 7.0, device="cuda")
+    args = (x.data_ptr(), 8, K, K, w.data_ptr(), V, K, tg.data_ptr(), loss.data_ptr(), lse.data_ptr())
+    # M = 0: nothing to do
+    a = list(args)
+    a[1] = 0
+    assert _raw_call(lib, *a) == 0
+    # row stride shorter than a row
+    a = list(args)
+    a[3] = K - 8
+    assert _raw_call(lib, *a) == 2
+    # null output pointer
+    a = list(args)
+    a[8] = None
+    assert _raw_call(lib, *a) == 2
+    # rows within the row limit but M * ceil(V / 256) partials beyond the partials limit
+    max_rows, max_part = ctypes.c_int64(), ctypes.c_int64()
+    lib.oxi_linear_ce_noalloc_limits(ctypes.byref(max_rows), ctypes.byref(max_part))
+    M = 60000
+    Vbig = 256 * (max_part.value // M + 1)
+    assert M <= max_rows.value and M * (Vbig // 256) > max_part.value
+    a = list(args)
+    a[1], a[5] = M, Vbig
+    assert _raw_call(lib, *a) == 1
+    assert b"too large" in lib.oxi_linear_ce_noalloc_last_error()
+    torch.cuda.synchronize()
+    assert torch.all(loss == 7.0) and torch.all(lse == 7.0)
