@@ -36,7 +36,7 @@ def test_conv1d(K, act, B, S, C):
 @pytest.mark.parametrize("G", [1, 2, 4])
 @pytest.mark.parametrize("B,S,H,P,N", [(2, 70, 4, 16, 32), (1, 130, 4, 64, 128)])
 def test_ssd_scan_mamba2(G, B, S, H, P, N):
-    """Mamba2 SSD via the scan kernel vs the chunked reference (fwd + all grads)."""
+    """Mamba2 SSD via the scan kernel vs the sequential recurrence (fwd + all grads)."""
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops import ssm
     torch.manual_seed(G + S + P)
@@ -50,7 +50,7 @@ def test_ssd_scan_mamba2(G, B, S, H, P, N):
     y.backward(dy)
     ref_in = [t.detach().double().requires_grad_() for t in (x, dt, A, Bg, Cg)]
     xr, dtr, Ar, Br, Cr = ref_in
-    yr = R.ssd_chunked(xr, dtr, Ar, Br.repeat_interleave(H // G, 2), Cr.repeat_interleave(H // G, 2), 32)
+    yr = R.ssd_sequential(xr, dtr, Ar, Br.repeat_interleave(H // G, 2), Cr.repeat_interleave(H // G, 2))
     yr.backward(dy.double())
     assert _rel(y, yr) < 1e-4
     for g, r in zip((x.grad, dt.grad, A.grad, Bg.grad, Cg.grad), (xr.grad, dtr.grad, Ar.grad, Br.grad, Cr.grad)):
@@ -72,7 +72,7 @@ def test_mamba3_scan(B, S, H, P, N):
     dy = torch.randn_like(y)
     y.backward(dy)
     ins = [t.detach().double().requires_grad_() for t in (x, dt, A, Bm, Cm, lam)]
-    yr = R.mamba3_scan(*ins, 32)
+    yr = R.mamba3_sequential(*ins)
     yr.backward(dy.double())
     assert _rel(y, yr) < 1e-4
     for g, r in zip((x.grad, dt.grad, A.grad, Bm.grad, Cm.grad, lam.grad), [t.grad for t in ins]):
@@ -113,7 +113,7 @@ def _tc_inputs(B, S, H, P, N, G, seed):
 
 @pytest.mark.parametrize("B,S,H,P,G", [(2, 256, 4, 64, 1), (1, 384, 4, 128, 2), (2, 128, 2, 64, 2)])
 def test_ssd_tensor_core_mamba2(B, S, H, P, G):
-    """tcgen05 chunked SSD (bf16 operands, f32 state) vs the fp64 chunked reference."""
+    """tcgen05 chunked SSD (bf16 operands, f32 state) vs the fp64 sequential recurrence."""
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops.ssd_tc import ssd_tc, tc_ok
     from oxidizr_b200.ops._C import check_status
@@ -127,7 +127,7 @@ def test_ssd_tensor_core_mamba2(B, S, H, P, G):
     check_status("cuda")
     ins = [t.detach().double().requires_grad_() for t in (x, dt, A, Bg, Cg)]
     xr, dtr, Ar, Br, Cr = ins
-    yr = R.ssd_chunked(xr, dtr, Ar, Br.repeat_interleave(H // G, 2), Cr.repeat_interleave(H // G, 2), 64)
+    yr = R.ssd_sequential(xr, dtr, Ar, Br.repeat_interleave(H // G, 2), Cr.repeat_interleave(H // G, 2))
     yr.backward(dy.double())
     assert _rel(y, yr) < 2e-2, _rel(y, yr)
     for name, g, r in zip(("x", "dt", "A", "B", "C"), (x.grad, dt.grad, A.grad, Bg.grad, Cg.grad), [t.grad for t in ins]):
@@ -136,7 +136,7 @@ def test_ssd_tensor_core_mamba2(B, S, H, P, G):
 
 @pytest.mark.parametrize("B,S,H,P", [(1, 128, 2, 64), (2, 256, 2, 128)])
 def test_ssd_tensor_core_mamba3(B, S, H, P):
-    """Mamba3 two-term scan through the shifted-state tensor-core SSD vs the fp64 reference."""
+    """Mamba3 two-term scan through the shifted-state tensor-core SSD vs the fp64 sequential recurrence."""
     from oxidizr_b200.ops import reference as R
     from oxidizr_b200.ops.ssd_tc import mamba3_tc
     from oxidizr_b200.ops._C import check_status
@@ -151,7 +151,7 @@ def test_ssd_tensor_core_mamba3(B, S, H, P):
     torch.cuda.synchronize()
     check_status("cuda")
     ins = [t.detach().double().requires_grad_() for t in (x, dt, A, Bm, Cm, lam)]
-    yr = R.mamba3_scan(*ins, 32)
+    yr = R.mamba3_sequential(*ins)
     yr.backward(dy.double())
     assert _rel(y, yr) < 2e-2, _rel(y, yr)
     # dA sums d loga dt over every step and head, with cancellation: bf16 operand
