@@ -315,10 +315,11 @@ __global__ void __launch_bounds__(512) rs_pull_kernel(const uint64_t* __restrict
 }
 
 // Exchange partial sums of squares; coef = min(1, max_norm / (norm + 1e-6)) / W.
+// skip (nullable): a non-zero word skips the update (NaN coefficient) with the norm as measured.
 __global__ void norm_exchange_kernel(const uint64_t* __restrict__ peer_pads, int* __restrict__ my_pad, int rank,
                                      int W, int epoch, const float* __restrict__ sumsq, float max_norm,
                                      float* __restrict__ coef, float* __restrict__ norm_out, int* status,
-                                     uint64_t wait_ns) {
+                                     uint64_t wait_ns, const int* __restrict__ skip) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   const float mine = *sumsq;
   for (int i = 0; i < W; ++i) {
@@ -340,7 +341,7 @@ __global__ void norm_exchange_kernel(const uint64_t* __restrict__ peer_pads, int
   if (max_norm > 0.f && nrm > max_norm) c *= max_norm / (nrm + 1e-6f);
   // a non-finite norm skips the update on every rank: the AdamW kernels take a
   // NaN coefficient as "leave p, m, v as they are" (parameters are still sent)
-  *coef = isfinite(nrm) ? c : __int_as_float(0x7fc00000);
+  *coef = (isfinite(nrm) && !(skip && *skip)) ? c : __int_as_float(0x7fc00000);
 }
 
 // ---------------------------------------------------------------- NVLS (multicast) reduce-scatter
@@ -469,52 +470,32 @@ __device__ __forceinline__ void ag_publish(const uint64_t* __restrict__ peer_pad
   }
 }
 
-// P2P / local all-gather.  One CTA updates 2048-element chunks of the owned
-// shard of bucket [lo, lo + len) (8 elements per thread), stages the bf16
-// result in shared memory and sends it to the `ndst` parameter buffers of the
-// table (every rank, itself included; ndst = 1: only its own buffer, the NCCL
-// baseline gathers afterwards) with bulk stores; the copy engine carries the
-// NVLink writes while the threads go on with the next chunk (double-buffered).
-constexpr int AG_CHUNK = 2048;
-
+// P2P / local all-gather: each thread updates 8 consecutive elements of the
+// owned shard of bucket [lo, lo + len) and stores the 16 bytes of new bf16
+// parameters straight into the `ndst` parameter buffers of the table (every
+// rank, itself included; ndst = 1: only its own buffer, the NCCL baseline
+// gathers afterwards).  No shared memory, so its CTAs can sit on an SM next to
+// a GEMM's CTA while the forward runs.
 __global__ void __launch_bounds__(256) adamw_ag_bucket_kernel(
     int64_t lo, int64_t len, int64_t so, int W, int rank, int ndst, const float* __restrict__ rgrad,
     float* __restrict__ master, float* __restrict__ m, float* __restrict__ v, const uint64_t* __restrict__ peers_param,
     const uint64_t* __restrict__ peer_pads, int bucket, int epoch, float lr, float b1, float b2, float eps, float wd,
     float bc1, float bc2, const float* __restrict__ coef, int* __restrict__ done_ctr, const int* status) {
-  __shared__ __align__(128) uint4 stage[2][AG_CHUNK / 8];
   const float gs = *coef;
   const bool apply = isfinite(gs);
   const float rb1 = 1.f / bc1, rb2 = 1.f / bc2;
   const bool failed = status && *reinterpret_cast<const volatile int*>(status) != 0;
-  int sb = 0;
   if (!failed) {
     const int64_t shard = len / W;
     const int64_t p0 = lo + rank * shard;
-    const int64_t nch = (shard + AG_CHUNK - 1) / AG_CHUNK;
-    for (int64_t c = blockIdx.x; c < nch; c += gridDim.x) {
-      const int64_t c0 = c * AG_CHUNK;
-      const int n = (int)min((int64_t)AG_CHUNK, shard - c0);
-      // the staging buffer is free once the bulk stores issued from it two chunks ago have read it
-      if (threadIdx.x == 0) bulk_wait_read<1>();
-      __syncthreads();
-      const int i = threadIdx.x;
-      if (i * 8 < n) stage[sb][i] = adamw8(so + c0 + i * 8, rgrad, master, m, v, gs, apply, b1, b2, rb1, rb2, lr, eps, wd);
-      fence_proxy_async_smem();  // the staged bytes are read by the bulk-copy (async) proxy
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        for (int j = 0; j < ndst; ++j) {
-          const int dst = (rank + j) % ndst;
-          bulk_store(reinterpret_cast<__nv_bfloat16*>(peers_param[dst]) + p0 + c0, &stage[sb][0], (uint32_t)(n * 2));
-        }
-        bulk_commit();
-      }
-      sb ^= 1;
+    const int64_t nv = shard / 8;
+    uint4* dst[PAD_MAXW];
+    for (int j = 0; j < ndst; ++j)
+      dst[j] = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers_param[(rank + j) % ndst]) + p0);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 u = adamw8(so + i * 8, rgrad, master, m, v, gs, apply, b1, b2, rb1, rb2, lr, eps, wd);
+      for (int j = 0; j < ndst; ++j) dst[j][i] = u;
     }
-  }
-  if (threadIdx.x == 0) {
-    bulk_wait<0>();
-    fence_proxy_async_global();
   }
   ag_publish(peer_pads, W, rank, bucket, epoch, done_ctr);
 }
@@ -651,10 +632,10 @@ void launch_rs_bucket(int mode, float* grad, bool zero_grad, const uint64_t* pee
 }
 
 void launch_norm_exchange(const uint64_t* peer_pads, int* my_pad, int rank, int W, int epoch, const float* sumsq,
-                          float max_norm, float* coef, float* norm_out, int* status, int64_t wait_ns,
+                          float max_norm, float* coef, float* norm_out, int* status, int64_t wait_ns, const int* skip,
                           cudaStream_t st) {
   norm_exchange_kernel<<<1, 32, 0, st>>>(peer_pads, my_pad, rank, W, epoch, sumsq, max_norm, coef, norm_out, status,
-                                         (uint64_t)wait_ns);
+                                         (uint64_t)wait_ns, skip);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -674,7 +655,7 @@ void launch_adamw_ag_bucket(int mode, int64_t lo, int64_t len, int64_t so, int W
                                             b1, b2, eps, wd, bc1, bc2, coef, done_ctr, status);
   } else {
     OXI_CHECK(ndst >= 1 && ndst <= PAD_MAXW, "bad destination count");
-    const int g = (int)std::max<int64_t>(1, std::min<int64_t>((shard + AG_CHUNK - 1) / AG_CHUNK, (int64_t)ctas));
+    const int g = (int)std::max<int64_t>(1, std::min<int64_t>((shard / 8 + 255) / 256, (int64_t)ctas));
     adamw_ag_bucket_kernel<<<g, 256, 0, st>>>(lo, len, so, W, rank, ndst, rgrad, master, m, v, peers_param,
                                               peer_pads, bucket, epoch, lr, b1, b2, eps, wd, bc1, bc2, coef, done_ctr,
                                               status);

@@ -98,7 +98,8 @@ __device__ __forceinline__ int align128(int n) { return (n + 127) & ~127; }
 __global__ void ep_counts_kernel(const int* __restrict__ local_counts, const uint64_t* __restrict__ peer_pads,
                                  int* __restrict__ my_pad, int rank, int W, int E, int seq,
                                  int* __restrict__ all_counts, int* __restrict__ seg_off, int* __restrict__ recv_counts,
-                                 int* status, uint64_t wait_ns) {
+                                 int cap, int* __restrict__ overflow, int* __restrict__ need_max, int* status,
+                                 uint64_t wait_ns) {
   __shared__ int ok_s;
   const int El = E / W;
   for (int i = 0; i < W; ++i) {
@@ -118,15 +119,35 @@ __global__ void ep_counts_kernel(const int* __restrict__ local_counts, const uin
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    // capacity check: every rank sees the same counts, so every rank reaches the
+    // same verdict for every owner's receive buffer (all have `cap` rows)
+    int need = 0;
+    for (int d = 0; d < W; ++d) {
+      int off = 0;
+      for (int le = 0; le < El; ++le) {
+        int c = 0;
+        for (int s = 0; s < W; ++s) c += all_counts[s * E + d * El + le];
+        off += align128(c);
+      }
+      need = max(need, off);
+    }
+    const bool skip = need > cap;
+    if (skip) {
+      // nothing of this layer is exchanged or computed: empty segments, and a
+      // sticky flag that makes the optimizer skip this step's update
+      atomicMax(need_max, need);
+      atomicExch(overflow, 1);
+    }
     int off = 0;
     for (int le = 0; le < El; ++le) {
       int c = 0;
       for (int s = 0; s < W; ++s) c += all_counts[s * E + rank * El + le];
-      recv_counts[le] = c;
+      recv_counts[le] = skip ? 0 : c;
       seg_off[le] = off;
-      off += align128(c);
+      if (!skip) off += align128(c);
     }
     seg_off[El] = off;
+    seg_off[El + 1] = skip ? 1 : 0;
   }
 }
 
@@ -150,13 +171,14 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const float* __restrict__ topw, int64_t T, int k, int H, const int* __restrict__ all_counts, int rank, int W,
     int E, int* __restrict__ cursor, const uint64_t* __restrict__ peers_xrecv, const uint64_t* __restrict__ peers_metaw,
     const uint64_t* __restrict__ peers_srcidx, int* __restrict__ pos_out, int* __restrict__ done_ctr,
-    const uint64_t* __restrict__ peer_pads, int seq, const int* status) {
+    const uint64_t* __restrict__ peer_pads, int seq, const int* __restrict__ seg_off, const int* status) {
   __shared__ int s_base[EP_MAXE];
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_base[e] = dest_base(all_counts, rank, W, E, e);
   __syncthreads();
-  const bool failed = status && *reinterpret_cast<const volatile int*>(status) != 0;
-  const int lane = threadIdx.x & 31;
   const int El = E / W;
+  // a layer over capacity (seg_off[El + 1]) sends nothing
+  const bool failed = (status && *reinterpret_cast<const volatile int*>(status) != 0) || seg_off[El + 1] != 0;
+  const int lane = threadIdx.x & 31;
   const int64_t pairs = T * k;
   const int nvec = H / 8;
   if (!failed) {
@@ -203,8 +225,9 @@ __global__ void __launch_bounds__(256) ep_push_dy_kernel(
     const __nv_bfloat16* __restrict__ dy, const int64_t* __restrict__ topi, const int* __restrict__ pos, int64_t T,
     int k, int H, int El, const uint64_t* __restrict__ peers_dyrecv, const __nv_bfloat16* __restrict__ yret,
     float* __restrict__ dw, int* __restrict__ done_ctr, const uint64_t* __restrict__ peer_pads, int rank, int W,
-    int seq, const int* status) {
-  const bool failed = status && *reinterpret_cast<const volatile int*>(status) != 0;
+    int seq, const int* __restrict__ seg_off, const int* status) {
+  // a layer over capacity (seg_off[El + 1]) sent nothing forward: nothing goes back
+  const bool failed = (status && *reinterpret_cast<const volatile int*>(status) != 0) || seg_off[El + 1] != 0;
   const int lane = threadIdx.x & 31;
   const int nvec = H / 8;
   if (!failed) {
@@ -332,24 +355,25 @@ unsigned warp_grid(int64_t items) {
 }  // namespace
 
 void launch_ep_counts(const int* local_counts, const uint64_t* peer_pads, int* my_pad, int rank, int W, int E, int seq,
-                      int* all_counts, int* seg_off, int* recv_counts, int* status, int64_t wait_ns,
-                      cudaStream_t st) {
+                      int* all_counts, int* seg_off, int* recv_counts, int cap, int* overflow, int* need_max,
+                      int* status, int64_t wait_ns, cudaStream_t st) {
   OXI_CHECK(W >= 1 && W <= EP_MAXW && E <= EP_MAXE && E % W == 0, "expert parallelism: W <= 8, E <= 256, W | E");
   ep_counts_kernel<<<1, 256, 0, st>>>(local_counts, peer_pads, my_pad, rank, W, E, seq, all_counts, seg_off,
-                                      recv_counts, status, (uint64_t)wait_ns);
+                                      recv_counts, cap, overflow, need_max, status, (uint64_t)wait_ns);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
 void launch_ep_dispatch(const void* x, int64_t ldx, const int64_t* topi, const float* topw, int64_t T, int k, int H,
                         const int* all_counts, int rank, int W, int E, int* cursor, const uint64_t* peers_xrecv,
                         const uint64_t* peers_metaw, const uint64_t* peers_srcidx, int* pos_out, int* done_ctr,
-                        const uint64_t* peer_pads, int seq, const int* status, cudaStream_t st) {
+                        const uint64_t* peer_pads, int seq, const int* seg_off, const int* status, cudaStream_t st) {
   OXI_CHECK(H % 8 == 0 && ldx % 8 == 0, "hidden size must be a multiple of 8");
   OXI_CHECK((int64_t)W * T * k < (1ll << 31), "source index must fit int32");
   OXI_CUDA_CHECK(cudaMemsetAsync(cursor, 0, sizeof(int) * E, st));
   ep_dispatch_kernel<<<warp_grid(T * k), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, topi, topw, T,
                                                        k, H, all_counts, rank, W, E, cursor, peers_xrecv, peers_metaw,
-                                                       peers_srcidx, pos_out, done_ctr, peer_pads, seq, status);
+                                                       peers_srcidx, pos_out, done_ctr, peer_pads, seq, seg_off,
+                                                       status);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -382,10 +406,11 @@ void launch_ep_sum_pairs(const void* rows, const float* w, int64_t T, int k, int
 
 void launch_ep_push_dy(const void* dy, const int64_t* topi, const int* pos, int64_t T, int k, int H, int El,
                        const uint64_t* peers_dyrecv, const void* yret, float* dw, int* done_ctr,
-                       const uint64_t* peer_pads, int rank, int W, int seq, const int* status, cudaStream_t st) {
+                       const uint64_t* peer_pads, int rank, int W, int seq, const int* seg_off, const int* status,
+                       cudaStream_t st) {
   ep_push_dy_kernel<<<warp_grid(T * k), 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(dy), topi, pos, T, k, H,
                                                       El, peers_dyrecv, reinterpret_cast<const __nv_bfloat16*>(yret),
-                                                      dw, done_ctr, peer_pads, rank, W, seq, status);
+                                                      dw, done_ctr, peer_pads, rank, W, seq, seg_off, status);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

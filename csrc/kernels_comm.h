@@ -39,8 +39,9 @@ void launch_rs_bucket(int mode, float* grad, bool zero_grad, const uint64_t* pee
                       const uint64_t* peer_pads, int* my_pad, int* done_ctr, int rank, int W, int bucket, int epoch,
                       int64_t lo, int64_t len, float* rgrad, float* sumsq, int ctas, int* status, int64_t wait_ns,
                       cudaStream_t st);
+// skip (nullable): a non-zero word skips the update (NaN coefficient), the norm stays as measured.
 void launch_norm_exchange(const uint64_t* peer_pads, int* my_pad, int rank, int W, int epoch, const float* sumsq,
-                          float max_norm, float* coef, float* norm_out, int* status, int64_t wait_ns,
+                          float max_norm, float* coef, float* norm_out, int* status, int64_t wait_ns, const int* skip,
                           cudaStream_t st);
 // AdamW on this rank's shard of bucket [lo, lo + len) (shard state at offset
 // `so`) and the bf16 all-gather of the result: mode 0/1 bulk-stores it into the

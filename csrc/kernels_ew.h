@@ -31,7 +31,8 @@ void launch_sqsum(const float* g, int64_t n, float* out, cudaStream_t st);
 void launch_colsum_bf16(const void* x, int64_t rows, int N, int64_t ld, float* out, cudaStream_t st);
 // step_state (nullable): device [t, 1 - b1^t, 1 - b2^t], advanced by one here.
 void launch_clip_coef(const float* sqsum, float max_norm, float pre_scale, float* coef, float* norm_out,
-                      cudaStream_t st, float* step_state = nullptr, float b1 = 0.9f, float b2 = 0.999f);
+                      cudaStream_t st, float* step_state = nullptr, float b1 = 0.9f, float b2 = 0.999f,
+                      const int* skip = nullptr);
 // bc_dev (nullable): device [1 - b1^t, 1 - b2^t] used instead of bc1 / bc2.
 void launch_adamw(float* p, void* p16, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
                   float eps, float wd, float bc1, float bc2, const float* gscale, cudaStream_t st,

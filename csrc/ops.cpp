@@ -250,7 +250,7 @@ void colsum_add(torch::Tensor x, torch::Tensor out) {
 }
 
 void clip_coef(torch::Tensor sq, double max_norm, double pre_scale, torch::Tensor coef, torch::Tensor norm,
-               c10::optional<torch::Tensor> step_state, double b1, double b2) {
+               c10::optional<torch::Tensor> step_state, double b1, double b2, c10::optional<torch::Tensor> skip) {
   c10::cuda::CUDAGuard gd(sq.device());
   float* ss = nullptr;
   if (step_state.has_value() && step_state->defined()) {
@@ -258,8 +258,13 @@ void clip_coef(torch::Tensor sq, double max_norm, double pre_scale, torch::Tenso
                     step_state->numel() == 3, "step_state: f32 [3]");
     ss = step_state->data_ptr<float>();
   }
+  const int* sk = nullptr;
+  if (skip.has_value() && skip->defined()) {
+    TORCH_CHECK(skip->scalar_type() == torch::kInt32 && skip->is_cuda(), "skip: int32 CUDA word");
+    sk = skip->data_ptr<int>();
+  }
   oxi::launch_clip_coef(sq.data_ptr<float>(), (float)max_norm, (float)pre_scale, coef.data_ptr<float>(),
-                        norm.data_ptr<float>(), stream(), ss, (float)b1, (float)b2);
+                        norm.data_ptr<float>(), stream(), ss, (float)b1, (float)b2, sk);
 }
 
 void adamw(torch::Tensor p, c10::optional<torch::Tensor> p16, torch::Tensor g, torch::Tensor m, torch::Tensor v,
@@ -383,11 +388,17 @@ void rs_bucket(int64_t mode, torch::Tensor grad, bool zero_grad, torch::Tensor p
 
 void norm_exchange(torch::Tensor peer_pads, torch::Tensor my_pad, int64_t rank, int64_t W, int64_t epoch,
                    torch::Tensor sumsq, double max_norm, torch::Tensor coef, torch::Tensor norm, torch::Tensor status,
-                   int64_t wait_ns) {
+                   int64_t wait_ns, c10::optional<torch::Tensor> skip) {
   c10::cuda::CUDAGuard gd(my_pad.device());
+  const int* sk = nullptr;
+  if (skip.has_value() && skip->defined()) {
+    TORCH_CHECK(skip->scalar_type() == torch::kInt32 && skip->is_cuda(), "skip: int32 CUDA word");
+    sk = skip->data_ptr<int>();
+  }
   oxi::launch_norm_exchange(reinterpret_cast<const uint64_t*>(peer_pads.data_ptr<int64_t>()), my_pad.data_ptr<int>(),
                             (int)rank, (int)W, (int)epoch, sumsq.data_ptr<float>(), (float)max_norm,
-                            coef.data_ptr<float>(), norm.data_ptr<float>(), status_ptr(status), wait_ns, stream());
+                            coef.data_ptr<float>(), norm.data_ptr<float>(), status_ptr(status), wait_ns, sk,
+                            stream());
 }
 
 void adamw_ag_bucket(int64_t mode, int64_t lo, int64_t len, int64_t so, int64_t W, int64_t rank, int64_t ndst,
@@ -429,22 +440,26 @@ const uint64_t* u64p(const torch::Tensor& t) {
 int64_t ep_pad_words() { return oxi::EP_PAD_WORDS; }
 
 std::vector<torch::Tensor> ep_counts(torch::Tensor local_counts, torch::Tensor peer_pads, torch::Tensor my_pad,
-                                     int64_t rank, int64_t W, int64_t seq, torch::Tensor status, int64_t wait_ns) {
+                                     int64_t rank, int64_t W, int64_t seq, int64_t cap, torch::Tensor overflow,
+                                     torch::Tensor status, int64_t wait_ns) {
   c10::cuda::CUDAGuard g(my_pad.device());
   TORCH_CHECK(local_counts.scalar_type() == torch::kInt32 && local_counts.is_contiguous(), "counts int32");
+  TORCH_CHECK(overflow.scalar_type() == torch::kInt32 && overflow.is_cuda() && overflow.numel() >= 2,
+              "overflow: int32 CUDA [2] (flag, rows needed)");
   const int64_t E = local_counts.numel(), El = E / W;
   auto io = torch::TensorOptions().dtype(torch::kInt32).device(my_pad.device());
-  auto all = torch::empty({W, E}, io), seg = torch::empty({El + 1}, io), rc = torch::empty({El}, io);
+  auto all = torch::empty({W, E}, io), seg = torch::empty({El + 2}, io), rc = torch::empty({El}, io);
+  int* ov = overflow.data_ptr<int>();
   oxi::launch_ep_counts(local_counts.data_ptr<int>(), u64p(peer_pads), my_pad.data_ptr<int>(), (int)rank, (int)W,
-                        (int)E, (int)seq, all.data_ptr<int>(), seg.data_ptr<int>(), rc.data_ptr<int>(),
-                        status_ptr(status), wait_ns, stream());
+                        (int)E, (int)seq, all.data_ptr<int>(), seg.data_ptr<int>(), rc.data_ptr<int>(), (int)cap, ov,
+                        ov + 1, status_ptr(status), wait_ns, stream());
   return {all, seg, rc};
 }
 
 torch::Tensor ep_dispatch(torch::Tensor x, torch::Tensor topi, torch::Tensor topw, torch::Tensor all_counts,
                           int64_t rank, int64_t W, torch::Tensor cursor, torch::Tensor peers_xrecv,
                           torch::Tensor peers_metaw, torch::Tensor peers_srcidx, torch::Tensor done_ctr,
-                          torch::Tensor peer_pads, int64_t seq, torch::Tensor status) {
+                          torch::Tensor peer_pads, int64_t seq, torch::Tensor seg_off, torch::Tensor status) {
   c10::cuda::CUDAGuard g(x.device());
   TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [T, H]");
   TORCH_CHECK(topi.scalar_type() == torch::kInt64 && topi.is_contiguous() && topw.is_contiguous() &&
@@ -454,7 +469,8 @@ torch::Tensor ep_dispatch(torch::Tensor x, torch::Tensor topi, torch::Tensor top
   oxi::launch_ep_dispatch(x.data_ptr(), x.stride(0), topi.data_ptr<int64_t>(), topw.data_ptr<float>(), T, (int)k,
                           (int)x.size(1), all_counts.data_ptr<int>(), (int)rank, (int)W, (int)E, cursor.data_ptr<int>(),
                           u64p(peers_xrecv), u64p(peers_metaw), u64p(peers_srcidx), pos.data_ptr<int>(),
-                          done_ctr.data_ptr<int>(), u64p(peer_pads), (int)seq, status_ptr(status), stream());
+                          done_ctr.data_ptr<int>(), u64p(peer_pads), (int)seq, seg_off.data_ptr<int>(),
+                          status_ptr(status), stream());
   return pos;
 }
 
@@ -529,7 +545,8 @@ torch::Tensor ep_sum_pairs(torch::Tensor rows, c10::optional<torch::Tensor> w, i
 
 torch::Tensor ep_push_dy(torch::Tensor dy, torch::Tensor topi, torch::Tensor pos, int64_t El,
                          torch::Tensor peers_dyrecv, torch::Tensor yret, torch::Tensor done_ctr,
-                         torch::Tensor peer_pads, int64_t rank, int64_t W, int64_t seq, torch::Tensor status) {
+                         torch::Tensor peer_pads, int64_t rank, int64_t W, int64_t seq, torch::Tensor seg_off,
+                         torch::Tensor status) {
   c10::cuda::CUDAGuard g(dy.device());
   TORCH_CHECK(dy.scalar_type() == torch::kBFloat16 && dy.is_contiguous(), "dy bf16 contiguous");
   const int64_t T = topi.size(0), k = topi.size(1);
@@ -538,7 +555,8 @@ torch::Tensor ep_push_dy(torch::Tensor dy, torch::Tensor topi, torch::Tensor pos
   auto dw = torch::empty({T, k}, torch::TensorOptions().dtype(torch::kFloat32).device(dy.device()));
   oxi::launch_ep_push_dy(dy.data_ptr(), topi.data_ptr<int64_t>(), pos.data_ptr<int>(), T, (int)k, (int)dy.size(-1),
                          (int)El, u64p(peers_dyrecv), yret.data_ptr(), dw.data_ptr<float>(), done_ctr.data_ptr<int>(),
-                         u64p(peer_pads), (int)rank, (int)W, (int)seq, status_ptr(status), stream());
+                         u64p(peer_pads), (int)rank, (int)W, (int)seq, seg_off.data_ptr<int>(), status_ptr(status),
+                         stream());
   return dw;
 }
 
@@ -1046,7 +1064,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("colsum_add", &colsum_add, "out += column sums of a bf16 matrix (bias gradients)");
   m.def("clip_coef", &clip_coef, "global-norm clip coefficient (and device step state) on device", py::arg("sq"),
         py::arg("max_norm"), py::arg("pre_scale"), py::arg("coef"), py::arg("norm"),
-        py::arg("step_state") = py::none(), py::arg("b1") = 0.9, py::arg("b2") = 0.999);
+        py::arg("step_state") = py::none(), py::arg("b1") = 0.9, py::arg("b2") = 0.999,
+        py::arg("skip") = py::none());
   m.def("adamw", &adamw, "flat multi-tensor AdamW (f32 master, bf16 copy)", py::arg("p"), py::arg("p16"),
         py::arg("g"), py::arg("m"), py::arg("v"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"),
         py::arg("wd"), py::arg("bc1"), py::arg("bc2"), py::arg("gscale") = py::none(),
@@ -1100,6 +1119,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bf16_to_f32_sumsq", &bf16_to_f32_sumsq, "bf16 shard -> f32 copy + sum of squares");
   m.def("ag_wait", &ag_wait, "bounded wait for every rank's all-gather of one bucket");
   m.def("rs_bucket", &rs_bucket, "reduce-scatter of one gradient bucket (pull, push or NVLS)");
-  m.def("norm_exchange", &norm_exchange, "cross-rank gradient norm and clip coefficient");
+  m.def("norm_exchange", &norm_exchange, "cross-rank gradient norm and clip coefficient", py::arg("peer_pads"),
+        py::arg("my_pad"), py::arg("rank"), py::arg("W"), py::arg("epoch"), py::arg("sumsq"), py::arg("max_norm"),
+        py::arg("coef"), py::arg("norm"), py::arg("status"), py::arg("wait_ns"), py::arg("skip") = py::none());
   m.def("adamw_ag_bucket", &adamw_ag_bucket, "sharded AdamW + bf16 parameter all-gather of one bucket");
 }

@@ -209,16 +209,18 @@ __global__ void sqsum_kernel(const float* __restrict__ g, int64_t n, float* __re
 // coef = min(1, max_norm / (sqrt(sqsum) + 1e-6)) * pre_scale; also writes the norm.
 // step_state (nullable) = [t, 1 - b1^t, 1 - b2^t] kept on the device so that a
 // captured step (CUDA graph) advances the bias correction on every replay.
+// skip (nullable): a non-zero word also skips the update (an expert-parallel layer
+// that ran over its receive capacity this step) while the norm stays as measured.
 __global__ void clip_coef_kernel(const float* __restrict__ sqsum, float max_norm, float pre_scale,
                                  float* __restrict__ coef, float* __restrict__ norm_out,
-                                 float* __restrict__ step_state, float b1, float b2) {
+                                 float* __restrict__ step_state, float b1, float b2, const int* __restrict__ skip) {
   const float nrm = sqrtf(*sqsum) * pre_scale;
   *norm_out = nrm;
   float c = pre_scale;
   if (max_norm > 0.f && nrm > max_norm) c *= max_norm / (nrm + 1e-6f);
   // a non-finite gradient norm skips this update: the coefficient is NaN, which every
   // AdamW launch reading it takes as "leave p, m, v as they are"; the step count stays
-  const bool finite = isfinite(nrm);
+  const bool finite = isfinite(nrm) && !(skip && *skip);
   *coef = finite ? c : __int_as_float(0x7fc00000);
   if (step_state && finite) {
     const float t = step_state[0] + 1.f;
@@ -411,8 +413,8 @@ void launch_colsum_bf16(const void* x, int64_t rows, int N, int64_t ld, float* o
 }
 
 void launch_clip_coef(const float* sqsum, float max_norm, float pre_scale, float* coef, float* norm_out,
-                      cudaStream_t st, float* step_state, float b1, float b2) {
-  clip_coef_kernel<<<1, 1, 0, st>>>(sqsum, max_norm, pre_scale, coef, norm_out, step_state, b1, b2);
+                      cudaStream_t st, float* step_state, float b1, float b2, const int* skip) {
+  clip_coef_kernel<<<1, 1, 0, st>>>(sqsum, max_norm, pre_scale, coef, norm_out, step_state, b1, b2, skip);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -23,6 +23,18 @@ import torch
 ALIGN = 64  # elements; keeps every parameter view 256-byte aligned in f32
 
 
+def _ep_skip_word(device):
+    """Device word set when an expert-parallel layer ran over its receive capacity
+    this step (the update is then skipped), or None (see parallel/ep.py)."""
+    from .parallel.ep import ep_skip_word
+    return ep_skip_word(device)
+
+
+def _ep_step_end(device) -> None:
+    from .parallel.ep import ep_step_end
+    ep_step_end(device)
+
+
 @dataclass
 class AdamWConfig:
     lr: float = 3e-4
@@ -186,12 +198,14 @@ class AdamW:
             e.sqsum(f.grad, self._sq)
             if self.local is not None:
                 self._local_sq(self._sq)
+            skip = _ep_skip_word(f.device) if self.local is not None else None
             e.clip_coef(self._sq, float(c.max_grad_norm or 0.0), float(grad_scale), self._coef, self._norm,
-                        self._step_state, c.beta1, c.beta2)
+                        self._step_state, c.beta1, c.beta2, skip)
             e.adamw(f.master, f.flat if f.flat is not f.master else None, f.grad, self.m, self.v, c.lr, c.beta1,
                     c.beta2, c.eps, c.weight_decay, bc1, bc2, self._coef, self._step_state[1:])
             if self.local is not None:
                 self.local.update(self._coef, t)
+                _ep_step_end(f.device)
         else:
             g = f.grad * grad_scale
             sq = g.pow(2).sum()

@@ -13,7 +13,13 @@ each of its top-k experts.  Two implementations of the same exchange:
   reads the k expert rows of each token back over NVLink and adds them,
   weighted, to the residual.  Backward pushes output gradients to the owners,
   which compute the routing-weight gradients and the expert backward GEMMs;
-  the sources gather the input gradients.  Every wait is bounded.
+  the sources gather the input gradients.  Every wait is bounded.  No host
+  synchronisation: receive buffers have a fixed capacity (2x the balanced
+  load); the count kernel checks it on the device, and a layer whose routing
+  would overflow any owner is skipped on every rank (all see the same counts)
+  and flags the step, whose update the optimizer then skips.  The host reads
+  that flag once per step, lazily, and regrows the buffers collectively before
+  the next step's first MoE layer.
 * ``nccl`` (baseline, and the CPU/gloo path, :func:`ep_moe`): NCCL/gloo
   all-to-all of the permuted rows (``torch.distributed.nn`` keeps it
   differentiable), split sizes read on the host.
@@ -109,6 +115,14 @@ class EPGroup:
         # backward, so every layer of the group shares one buffer
         self.dyrecv = None
         self.dyrecv_bytes = 0
+        # [over-capacity flag of this step, most receive rows any layer needed]:
+        # written by the count kernels, read by the optimizer's clip kernel (skip)
+        # and, one step later, by the host (regrow)
+        self.overflow = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self._ovf_host = torch.zeros(2, dtype=torch.int32).pin_memory()
+        self._ovf_event = None
+        self.layers = []
+        self.regrows = 0
 
     def shared_dyrecv(self, nbytes: int):
         """The group's gradient receive buffer, grown collectively to at least nbytes."""
@@ -125,6 +139,46 @@ class EPGroup:
     def next_seq(self) -> int:
         self.seq += 1
         return self.seq
+
+    def step_end(self) -> None:
+        """After the optimizer has read this step's flag: copy it to the host
+        (asynchronously) and clear it for the next step."""
+        self._ovf_host.copy_(self.overflow, non_blocking=True)
+        self._ovf_event = torch.cuda.Event()
+        self._ovf_event.record()
+        self.overflow.zero_()
+
+    def check_regrow(self) -> None:
+        """Before a step's first MoE layer: if the previous step ran over a receive
+        capacity, grow every layer's buffers (collective; every rank saw the same
+        flag).  Waits for the previous step's flag copy only."""
+        ev, self._ovf_event = self._ovf_event, None
+        if ev is None:
+            return
+        ev.synchronize()
+        flag, need = int(self._ovf_host[0]), int(self._ovf_host[1])
+        if flag:
+            self.regrows += 1
+            for buf in self.layers:
+                buf.ensure(max(need, buf.cap + 1))
+
+
+def _groups_on(device):
+    idx = torch.device(device).index
+    return [g for (gid, di), g in EPGroup._groups.items() if di == idx]
+
+
+def ep_skip_word(device) -> Optional[torch.Tensor]:
+    """The device word that makes an optimizer skip this step's update (an expert-
+    parallel layer ran over its receive capacity), or None without expert parallelism."""
+    gs = _groups_on(device)
+    return gs[0].overflow[0:1] if gs else None
+
+
+def ep_step_end(device) -> None:
+    """Called by the optimizers after their update launches."""
+    for g in _groups_on(device):
+        g.step_end()
 
 
 class EPLayerBuffers:
@@ -143,6 +197,7 @@ class EPLayerBuffers:
         self.bufs = None
         self.pairs = 0
         self.yret = None  # [T*k, H]: this rank's expert output rows, then their input gradients
+        grp.layers.append(self)
 
     def ensure_pairs(self, pairs: int):
         """yret holds one row per (token, slot) of this rank; its size only changes with
@@ -157,13 +212,16 @@ class EPLayerBuffers:
             self.yret = SymmetricBuffer(pairs * self.H * 2, g.device, g.group)
             self.pairs = pairs
 
-    def ensure(self, rows: int, balanced_rows: int = 0):
-        if rows <= self.cap:
+    def ensure(self, rows: int, balanced_rows: int = 0, exact: bool = False):
+        if rows <= self.cap and not (balanced_rows and self.cap == 0):
             return
         from .fused_ar import SymmetricBuffer
         g = self.grp
-        want = max(rows * self.HEADROOM, balanced_rows * self.HEADROOM, self.cap * self.HEADROOM)
-        cap = max(128, (int(want) + 1023) // 1024 * 1024)
+        if exact:
+            cap = max(128, (rows + 127) // 128 * 128)
+        else:
+            want = max(rows * self.HEADROOM, balanced_rows * self.HEADROOM, self.cap * self.HEADROOM)
+            cap = max(128, (int(want) + 1023) // 1024 * 1024)
         EPLayerBuffers.reallocs += 1
         torch.cuda.synchronize(g.device)
         if self.bufs is not None:
@@ -192,12 +250,6 @@ class EPLayerBuffers:
         return self._buf(name).ptr_table
 
 
-def _rows_needed(all_counts: torch.Tensor, W: int, El: int) -> int:
-    """Largest 128-aligned receive-buffer size any rank needs (same on every rank)."""
-    per_expert = all_counts.sum(0).view(W, El)  # [dest, local expert]
-    return int((((per_expert + 127) // 128) * 128).sum(1).max().item())
-
-
 class EPExperts(torch.autograd.Function):
     """resid + sum_j topw[t, j] * SwiGLU_{topi[t, j]}(x_t), experts spread over the group (NVLink).
 
@@ -222,17 +274,20 @@ class EPExperts(torch.autograd.Function):
         topi = topi.contiguous()
         tw = topw.float().contiguous()
         seq = g.next_seq()
-        all_counts, seg, rc = e.ep_counts(counts.int().contiguous(), g.pad.ptr_table, g.pad_local, rank, W, seq, st,
-                                          g.wait_ns)
-        # every rank sees the same counts, so every rank takes the same (collective) decision
-        buf.ensure(_rows_needed(all_counts.cpu(), W, El), balanced_rows=T * k)
+        if buf.cap == 0:  # first use: 2x the balanced load plus every segment's alignment
+            forced = int(os.environ.get("OXI_EP_INITIAL_ROWS", "0"))  # tests: start over capacity
+            buf.ensure(forced, exact=True) if forced else buf.ensure(0, balanced_rows=T * k + El * 128)
         buf.ensure_pairs(T * k)
+        # the counts kernel checks every owner's rows against the capacity on the
+        # device (no host read); over capacity, the layer is skipped on every rank
+        all_counts, seg, rc = e.ep_counts(counts.int().contiguous(), g.pad.ptr_table, g.pad_local, rank, W, seq,
+                                          buf.cap, g.overflow, st, g.wait_ns)
         cap = buf.cap
         xr = buf.local("xrecv", torch.bfloat16, H)
         e.moe_zero_pad(seg, rc, xr)
         e.ep_mark_pad(seg, rc, buf.local("srcidx", torch.int32))
         pos = e.ep_dispatch(xc, topi, tw, all_counts, rank, W, g.cursor, buf.table("xrecv"), buf.table("metaw"),
-                            buf.table("srcidx"), g.done[0:1], g.pad.ptr_table, seq, st)
+                            buf.table("srcidx"), g.done[0:1], g.pad.ptr_table, seq, seg, st)
         e.ep_wait(g.pad_local, K_DISPATCHED, W, seq, st, g.wait_ns)
         h = torch.empty(cap, I, dtype=x.dtype, device=x.device)
         gu = torch.empty(cap, I2, dtype=x.dtype, device=x.device)
@@ -268,7 +323,7 @@ class EPExperts(torch.autograd.Function):
         yret = buf.yret.local.view(torch.bfloat16).view(T * k, H)
         # dy rows to the owners; d topw from this rank's copy of the expert outputs
         dtw = e.ep_push_dy(dy, topi, pos, El, buf.table("dyrecv"), yret, g.done[1:2], g.pad.ptr_table, rank, W, seq,
-                           st)
+                           seg, st)
         e.ep_wait(g.pad_local, K_DYPUSHED, W, seq, st, g.wait_ns)
         e.ep_scale_rows(dyr, buf.local("metaw", torch.float32), seg, rc, El)
         g_down = _wgrad_grouped(w_down, dyr, h, seg, El)
@@ -295,4 +350,5 @@ def ep_moe_nvlink(moe, x, topi, topw, counts, resid):
     if getattr(moe, "_ep", None) is None:
         moe._ep = EPGroup.get(moe.ep_group, x.device)
         moe._ep_buf = EPLayerBuffers(moe._ep, x.shape[1])
+    moe._ep.check_regrow()
     return EPExperts.apply(x, topi, topw, counts, moe.w_gu, moe.w_down, resid, moe)

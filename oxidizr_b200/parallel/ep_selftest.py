@@ -40,9 +40,14 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--two-layers", action="store_true",
                     help="a second MoE layer on the same group with twice the tokens (grows shared buffers)")
+    ap.add_argument("--initial-rows", type=int, default=0,
+                    help="start the receive buffers this small (the first step runs over capacity, is flagged as "
+                         "skipped, and the buffers regrow before the next step)")
     ap.add_argument("--out", default=None)
     args = ap.parse_args(argv)
     os.environ["OXI_EP_BACKEND"] = args.backend
+    if args.initial_rows:
+        os.environ["OXI_EP_INITIAL_ROWS"] = str(args.initial_rows)
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     if args.device == "cuda":
@@ -102,6 +107,13 @@ def main(argv=None):
             outs.append((sh, wh, xs, xw, ys, yw))
         loss_s.backward()
         loss_w.backward()
+        skipped = 0
+        if args.device == "cuda" and args.backend == "nvlink":
+            # what an optimizer does after its update: read the over-capacity word, then end the step
+            from .ep import ep_skip_word, ep_step_end
+            w = ep_skip_word(dev)
+            skipped = int(w.item()) if w is not None else 0
+            ep_step_end(dev)
         for sh, wh, xs, xw, ys, yw in outs:
             e = {"y": _rel(ys, yw), "dx": _rel(xs.grad, xw.grad), "router": _rel(sh.router.grad, wh.router.grad)}
             for name in ("w_gu", "w_down"):
@@ -111,12 +123,16 @@ def main(argv=None):
             t = torch.tensor([max(e.values())], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e["max_over_ranks"] = float(t)
+            e["step"], e["skipped"] = step, skipped
             errs.append(e)
     if args.device == "cuda":
         from ..ops._C import check_status
         torch.cuda.synchronize()
         check_status(dev)
     res["errors"] = errs
+    if args.device == "cuda" and args.backend == "nvlink":
+        from .ep import EPGroup
+        res["regrows"] = sum(g.regrows for g in EPGroup._groups.values())
     if rank == 0 and args.out:
         with open(args.out, "w") as fh:
             json.dump(res, fh)

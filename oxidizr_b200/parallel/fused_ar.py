@@ -239,6 +239,13 @@ class ShardedDDPAdamW:
     def lr(self) -> float:
         return self.cfg.lr
 
+    def _skip_word(self):
+        """Expert-parallel over-capacity flag of this step (skips the update), if any."""
+        if self.local is None:
+            return None
+        from .ep import ep_skip_word
+        return ep_skip_word(self.device)
+
     # ------------------------------------------------------------ overlap with the forward
     def attach(self, model) -> None:
         """Let ``model`` (a LitGPT) wait for each bucket's parameters just before
@@ -316,6 +323,8 @@ class ShardedDDPAdamW:
                 self._ag(bi, c.lr, bc1, bc2)
         if self.local is not None:
             self.local.update(self._coef, t)
+            from .ep import ep_step_end
+            ep_step_end(self.device)
         self._ag_epoch = self.epoch
         self._waited = set()
         self.epoch += 1
@@ -426,7 +435,7 @@ class FusedDDPAdamW(ShardedDDPAdamW):
 
     def _norm_coef(self, max_norm):
         ext().norm_exchange(self.pad.ptr_table, self.pad_local, self.rank, self.W, self.epoch, self._sumsq, max_norm,
-                            self._coef, self._norm, status(self.device), self.wait_ns)
+                            self._coef, self._norm, status(self.device), self.wait_ns, self._skip_word())
 
     def _ag(self, bi, lr, bc1, bc2):
         lo, ln, so, _ = self.buckets[bi]
@@ -470,7 +479,8 @@ class NcclShardedAdamW(ShardedDDPAdamW):
 
     def _norm_coef(self, max_norm):
         dist.all_reduce(self._sumsq, group=self.group)
-        ext().clip_coef(self._sumsq, max_norm, 1.0 / self.W, self._coef, self._norm, None, 0.0, 0.0)
+        ext().clip_coef(self._sumsq, max_norm, 1.0 / self.W, self._coef, self._norm, None, 0.0, 0.0,
+                        self._skip_word())
 
     def _ag(self, bi, lr, bc1, bc2):
         lo, ln, so, _ = self.buckets[bi]

@@ -53,3 +53,26 @@ def test_ep_gpu_matches_whole_layer(tmp_path, backend, shape):
     for e in res["errors"]:
         assert e["y"] < 2e-2 and e["dx"] < 3e-2 and e["router"] < 5e-2, e
         assert e["w_gu"] < 3e-2 and e["w_down"] < 3e-2, e
+        assert not e.get("skipped"), e
+    assert res.get("regrows", 0) == 0
+
+
+@pytest.mark.gpu
+def test_ep_over_capacity_skips_then_regrows(tmp_path):
+    """Receive buffers that start too small: the first step's layers run over capacity on
+    the device, are skipped on every rank and flag the step (the optimizer would skip its
+    update); the host regrows the buffers before the next step, which matches the whole
+    layer.  No host read of the routing counts happens inside a step."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run(tmp_path, "cuda", "nvlink",
+               extra=("--tokens", "1000", "--experts", "16", "--topk", "4", "--hidden", "512", "--inter", "256",
+                      "--steps", "3", "--initial-rows", "256"))
+    first = [e for e in res["errors"] if e["step"] == 0]
+    later = [e for e in res["errors"] if e["step"] > 0]
+    assert first and all(e["skipped"] for e in first), first
+    assert res["regrows"] == 1
+    for e in later:
+        assert not e["skipped"], e
+        assert e["y"] < 2e-2 and e["dx"] < 3e-2 and e["router"] < 5e-2, e
+        assert e["w_gu"] < 3e-2 and e["w_down"] < 3e-2, e

@@ -35,6 +35,11 @@ CONFIGS = {
 }
 
 
+# parameters with one value per SSM head (or per state pair): gradients are whole-sequence sums
+PER_HEAD_SCALARS = {"A_log", "dt_bias", "D", "a_log", "d"}
+PER_HEAD_BIASES = ("theta_proj.bias", "lambda_proj.bias")
+
+
 def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
@@ -71,13 +76,23 @@ def test_model_family_matches_cpu_reference(name):
     check_status("cuda")
     gg = dict(zip([n for n, _ in gpu.named_parameters()], [p.grad for p in gpu.parameters()]))
     gc = dict(zip([n for n, _ in cpu.named_parameters()], [p.grad for p in cpu.parameters()]))
-    worst = []
+    worst, scalars = [], []
     for k, ref in gc.items():
         if ref is None or ref.norm() == 0:
             continue
         assert gg[k] is not None, f"no gradient for {k} on the GPU"
-        worst.append((_rel(gg[k].cpu(), ref), k))
+        g = gg[k].cpu().float()
+        if k.rsplit(".", 1)[-1] in PER_HEAD_SCALARS or k.endswith(PER_HEAD_BIASES):
+            cos = torch.nn.functional.cosine_similarity(g.reshape(1, -1), ref.reshape(1, -1)).item()
+            scalars.append((_rel(g, ref), cos, k))
+        else:
+            worst.append((_rel(g, ref), k))
     worst.sort(reverse=True)
     # bf16 operands through several SSM / attention layers: a few percent; routing
     # decisions that flip on near ties move a handful of expert rows
     assert worst[0][0] < 0.1, worst[:5]
+    # per-head scalars (decay, step-size and rotation biases) sum d/dlog(alpha)-type terms
+    # over every token; at random init those sums cancel to near the bf16 noise of the
+    # chunked scan, so they get a looser relative bound and must point the same way
+    for rel, cos, k in scalars:
+        assert rel < 0.3 and cos > 0.95, (k, rel, cos)
