@@ -8,6 +8,7 @@
 #include "kernels_ew.h"
 #include "kernels_attn.h"
 #include "kernels_comm.h"
+#include "kernels_mla.h"
 #include "kernels_ssm.h"
 #include "kernels_moe.h"
 #include "kernels_ep.h"
@@ -427,6 +428,55 @@ void adamw_ag_bucket(int64_t mode, int64_t lo, int64_t len, int64_t so, int64_t 
 void ag_wait(torch::Tensor my_pad, int64_t W, int64_t bucket, int64_t epoch, torch::Tensor status, int64_t wait_ns) {
   c10::cuda::CUDAGuard gd(my_pad.device());
   oxi::launch_ag_wait(my_pad.data_ptr<int>(), (int)W, (int)bucket, (int)epoch, status_ptr(status), wait_ns, stream());
+}
+
+// ------------------------------------------------------------ multi-head latent attention
+namespace {
+void mla_check(const torch::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.dim() == 2 && t.stride(1) == 1 &&
+                  (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0,
+              what, ": bf16 CUDA [rows, cols] with unit inner stride and a 16-byte aligned start");
+}
+}  // namespace
+
+std::vector<torch::Tensor> mla_pack_fwd(torch::Tensor qc, torch::Tensor kv, torch::Tensor rp, torch::Tensor cos_t,
+                                        torch::Tensor sin_t, int64_t S, int64_t nh, int64_t hd, int64_t dr) {
+  c10::cuda::CUDAGuard g(qc.device());
+  mla_check(qc, "q_c");
+  mla_check(kv, "kv");
+  TORCH_CHECK(rp.is_cuda() && rp.scalar_type() == torch::kBFloat16 && rp.dim() == 2 && rp.stride(1) == 1, "rope block");
+  const int64_t T = qc.size(0);
+  TORCH_CHECK(qc.size(1) == nh * hd && kv.size(0) == T && kv.size(1) == 2 * nh * hd && rp.size(0) == T &&
+                  rp.size(1) == dr + nh * dr && T % S == 0,
+              "MLA pack: q_c [T, nh*hd], kv [T, 2*nh*hd], rope block [T, dr + nh*dr], T a multiple of S");
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && sin_t.scalar_type() == torch::kFloat32 &&
+                  cos_t.is_contiguous() && sin_t.is_contiguous() && cos_t.size(0) >= S && cos_t.size(1) == dr / 2,
+              "RoPE tables: f32 [>= S, dr/2]");
+  auto o = qc.options();
+  auto q = torch::empty({T, nh, hd + dr}, o), k = torch::empty({T, nh, hd + dr}, o), v = torch::empty({T, nh, hd}, o);
+  oxi::launch_mla_pack_fwd(qc.data_ptr(), qc.stride(0), kv.data_ptr(), kv.stride(0), rp.data_ptr(), rp.stride(0),
+                           cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), T, (int)S, (int)nh, (int)hd, (int)dr,
+                           q.data_ptr(), k.data_ptr(), v.data_ptr(), stream());
+  return {q, k, v};
+}
+
+std::vector<torch::Tensor> mla_pack_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor cos_t,
+                                        torch::Tensor sin_t, int64_t S, int64_t nh, int64_t hd, int64_t dr) {
+  c10::cuda::CUDAGuard g(dq.device());
+  const int64_t T = dq.size(0);
+  for (const torch::Tensor* t : {&dq, &dk, &dv})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->is_contiguous() && t->size(0) == T &&
+                    (reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0,
+                "MLA pack backward: contiguous bf16 gradients with 16-byte aligned starts");
+  TORCH_CHECK(dq.numel() == T * nh * (hd + dr) && dk.numel() == dq.numel() && dv.numel() == T * nh * hd && T % S == 0,
+              "MLA pack backward: dq, dk [T, nh, hd + dr], dv [T, nh, hd]");
+  auto o = dq.options();
+  auto dqc = torch::empty({T, nh * hd}, o), dkv = torch::empty({T, 2 * nh * hd}, o),
+       drp = torch::empty({T, dr + nh * dr}, o);
+  oxi::launch_mla_pack_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), cos_t.data_ptr<float>(),
+                           sin_t.data_ptr<float>(), T, (int)S, (int)nh, (int)hd, (int)dr, dqc.data_ptr(),
+                           dkv.data_ptr(), drp.data_ptr(), stream());
+  return {dqc, dkv, drp};
 }
 
 // ------------------------------------------------------------ expert parallelism (NVLink)
@@ -1100,6 +1150,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather_sum", &moe_gather_sum, "sum permuted rows back per token");
   m.def("gemm_grouped", &gemm_grouped, "grouped (per-expert) tcgen05 GEMM");
   m.def("ep_pad_words", &ep_pad_words, "int32 words of one expert-parallel signal pad");
+  m.def("mla_pack_fwd", &mla_pack_fwd, "MLA: q, k (shared k_rope, RoPE applied) and packed v from the projections");
+  m.def("mla_pack_bwd", &mla_pack_bwd, "MLA: gradients of q_c, kv and the rope block from dq, dk, dv");
   m.def("ep_counts", &ep_counts, "expert-parallel count all-gather over NVLink");
   m.def("ep_dispatch", &ep_dispatch, "expert-parallel token dispatch (P2P stores)");
   m.def("ep_wait", &ep_wait, "bounded wait for an expert-parallel flag from every peer");

@@ -8,7 +8,6 @@ import torch
 from torch import nn
 
 from ..ops import api
-from ..ops import reference as R
 from .common import RefModule, RopeCache, _assign, interleave_gu, normal_, split_gu, take
 
 
@@ -95,19 +94,13 @@ class MLAAttention(RefModule):
         B, S, _ = h.shape
         nh, hd, dr = self.nh, self.hd, self.dr
         d = api.linear(h, self.w_down)
-        c_kv = d[..., :self.kvl]
-        c_q = d[..., self.kvl:self.kvl + self.ql]
-        k_r = d[..., self.kvl + self.ql:self.kvl + self.ql + dr].reshape(B, S, 1, dr)
-        q_r = d[..., self.kvl + self.ql + dr:].reshape(B, S, nh, dr)
+        # c_kv | c_q | k_rope | q_rope blocks as views; one gradient buffer in the backward
+        c_kv, c_q, rp = api.split_cols(d, [self.kvl, self.ql, dr + nh * dr])
+        q_c = api.linear(c_q, self.w_uq)
+        kv = api.linear(c_kv, self.w_ukv)
         cos, sin = RopeCache.get(dr, S, self.theta, h.device)
-        q_r = R.apply_rope(q_r.transpose(1, 2), cos, sin).transpose(1, 2)
-        k_r = R.apply_rope(k_r.transpose(1, 2), cos, sin).transpose(1, 2)
-        q_c = api.linear(c_q.contiguous(), self.w_uq).view(B, S, nh, hd)
-        kv = api.linear(c_kv.contiguous(), self.w_ukv)
-        k_c = kv[..., :nh * hd].view(B, S, nh, hd)
-        v = kv[..., nh * hd:].view(B, S, nh, hd)
-        q = torch.cat([q_c, q_r.to(q_c.dtype)], -1)
-        k = torch.cat([k_c, k_r.to(k_c.dtype).expand(B, S, nh, dr)], -1)
+        # RoPE on the rope parts and the shared k_rope broadcast to every head, in one kernel
+        q, k, v = api.mla_qkv(q_c, kv, rp, cos, sin, nh, hd, dr)
         o = api.attention(q, k, v, self.scale, causal=True).reshape(B, S, nh * hd)
         return api.linear(o, self.o_proj, resid=resid)
 

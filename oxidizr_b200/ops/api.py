@@ -107,6 +107,24 @@ def qkv_rope(x, w_qkv, cos, sin, hd: int, q_cols: int, k_cols: int):
     return torch.cat([q, k, y[..., q_cols + k_cols:]], -1)
 
 
+def mla_qkv(qc, kv, rp, cos, sin, nh: int, hd: int, dr: int):
+    """MLA attention operands (model.rs:196-256): q = [q_c, rope(q_rope)], k = [k_c, rope(k_rope)]
+    with the one k_rope of a token shared by every head, and v, from q_c [B, S, nh*hd],
+    kv [B, S, 2*nh*hd] (k | v) and the rope block rp [B, S, dr + nh*dr] (k_rope | q_rope).
+    Returns q, k [B, S, nh, hd + dr] and v [B, S, nh, hd]."""
+    B, S = qc.shape[0], qc.shape[1]
+    if _native(qc) and hd % 8 == 0 and dr % 2 == 0 and dr <= 64:
+        from .mla import MlaPack
+        return MlaPack.apply(qc, kv, rp, cos, sin, nh, hd, dr)
+    k_r = rp[..., :dr].reshape(B, S, 1, dr)
+    q_r = rp[..., dr:].reshape(B, S, nh, dr)
+    q_r = R.apply_rope(q_r.transpose(1, 2), cos[:S], sin[:S]).transpose(1, 2)
+    k_r = R.apply_rope(k_r.transpose(1, 2), cos[:S], sin[:S]).transpose(1, 2)
+    q = torch.cat([qc.view(B, S, nh, hd), q_r.to(qc.dtype)], -1)
+    k = torch.cat([kv[..., :nh * hd].view(B, S, nh, hd), k_r.to(kv.dtype).expand(B, S, nh, dr)], -1)
+    return q, k, kv[..., nh * hd:].view(B, S, nh, hd)
+
+
 def swiglu_mlp(x, w_gu, w_down, resid=None):
     """resid + down(silu(gate x) * up x); w_gu rows interleaved [g 128 | u 128]..."""
     I = w_gu.shape[0] // 2

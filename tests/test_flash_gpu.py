@@ -7,6 +7,10 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
 def _ref(q, k, v, scale, causal=True):
     from oxidizr_b200.ops import reference as R
     o = R.attention(q.float().transpose(1, 2), k.float().transpose(1, 2), v.float().transpose(1, 2), scale, causal)
@@ -95,3 +99,33 @@ def test_flash_mla_head_dims(Dqk, Dv, B, S, H):
     for name, a, r in (("q", q.grad, qr.grad), ("k", k.grad, kr.grad), ("v", v.grad, vr.grad)):
         e = ((a.float() - r).norm() / r.norm()).item()
         assert e < 3e-2, (name, e)
+
+
+@pytest.mark.parametrize("B,S,nh,hd,dr", [(2, 128, 12, 64, 32), (1, 256, 4, 128, 64), (3, 64, 2, 64, 16)])
+def test_mla_pack_matches_reference(B, S, nh, hd, dr):
+    """MLA operand packing (RoPE on the rope parts, shared k_rope broadcast, v packed) and its
+    backward against the fp32 PyTorch statement (model.rs:196-256)."""
+    from oxidizr_b200.models.common import RopeCache
+    from oxidizr_b200.ops import reference as R
+    from oxidizr_b200.ops.mla import MlaPack
+    torch.manual_seed(B + S + dr)
+    qc = torch.randn(B, S, nh * hd, device="cuda").bfloat16().requires_grad_()
+    kv = torch.randn(B, S, 2 * nh * hd, device="cuda").bfloat16().requires_grad_()
+    big = torch.randn(B, S, 40 + dr + nh * dr, device="cuda").bfloat16()
+    rp = big[..., 40:].detach().requires_grad_()  # a column block of a wider projection, like the model's
+    cos, sin = RopeCache.get(dr, S, 10000.0, "cuda")
+    q, k, v = MlaPack.apply(qc, kv, rp, cos, sin, nh, hd, dr)
+    gq, gk, gv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
+    (q.float() * gq.float()).sum().add((k.float() * gk.float()).sum()).add((v.float() * gv.float()).sum()).backward()
+    # reference in f32
+    qc_r, kv_r, rp_r = (t.detach().float().requires_grad_() for t in (qc, kv, rp))
+    q_r = R.apply_rope(rp_r[..., dr:].reshape(B, S, nh, dr).transpose(1, 2), cos, sin).transpose(1, 2)
+    k_r = R.apply_rope(rp_r[..., :dr].reshape(B, S, 1, dr).transpose(1, 2), cos, sin).transpose(1, 2)
+    qr = torch.cat([qc_r.view(B, S, nh, hd), q_r], -1)
+    kr = torch.cat([kv_r[..., :nh * hd].view(B, S, nh, hd), k_r.expand(B, S, nh, dr)], -1)
+    vr = kv_r[..., nh * hd:].view(B, S, nh, hd)
+    (qr * gq.float()).sum().add((kr * gk.float()).sum()).add((vr * gv.float()).sum()).backward()
+    assert _rel(q, qr) < 5e-3 and _rel(k, kr) < 5e-3 and torch.equal(v.float(), vr.detach())
+    assert _rel(qc.grad, qc_r.grad) < 5e-3
+    assert _rel(kv.grad, kv_r.grad) < 5e-3
+    assert _rel(rp.grad, rp_r.grad) < 1e-2
