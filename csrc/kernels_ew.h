@@ -18,7 +18,8 @@ int norm_bwd_partial_rows(int64_t rows, int H);
 void launch_ce_finish(const float* pmax, const float* psum, int nt, const float* tgt_logit, const int64_t* targets,
                       float* lse, float* loss, int64_t rows, cudaStream_t st);
 void launch_ce_bwd(void* logits, int64_t ld, int64_t V, int64_t rows, const float* lse, const int64_t* targets,
-                   const float* gscale, float inv_count, cudaStream_t st);
+                   const float* gscale, float inv_count, cudaStream_t st,
+                   int64_t col0 = 0);
 void launch_embed_fwd(const int64_t* ids, const void* w, void* out, int64_t rows, int H, cudaStream_t st);
 void launch_embed_bwd(const int64_t* ids, const void* dy, float* dw, int64_t rows, int H, cudaStream_t st);
 void launch_rope_bwd(void* x, int64_t ld, int64_t rows, int ncols_rot, int hd, const float* cos, const float* sin,

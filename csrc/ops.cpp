@@ -195,11 +195,13 @@ void ce_finish(torch::Tensor pmax, torch::Tensor psum, torch::Tensor tgt_logit, 
 }
 
 void ce_bwd(torch::Tensor logits, int64_t V, torch::Tensor lse, torch::Tensor targets, torch::Tensor gscale,
-            double inv_count) {
+            double inv_count, int64_t col0) {
   c10::cuda::CUDAGuard g(logits.device());
   TORCH_CHECK(logits.scalar_type() == torch::kBFloat16 && logits.stride(1) == 1, "logits");
+  TORCH_CHECK(logits.size(1) >= V && lse.numel() == logits.size(0) && targets.numel() == logits.size(0),
+              "ce_bwd: logits [M, >= V], lse / targets [M]");
   oxi::launch_ce_bwd(logits.data_ptr(), logits.stride(0), V, logits.size(0), lse.data_ptr<float>(),
-                     targets.data_ptr<int64_t>(), gscale.data_ptr<float>(), (float)inv_count, stream());
+                     targets.data_ptr<int64_t>(), gscale.data_ptr<float>(), (float)inv_count, stream(), col0);
 }
 
 // ------------------------------------------------------------ embedding / rope
@@ -1105,7 +1107,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_fwd", &norm_fwd, "RMSNorm / LayerNorm / gated RMSNorm forward");
   m.def("norm_bwd", &norm_bwd, "RMSNorm / LayerNorm / gated RMSNorm backward");
   m.def("ce_finish", &ce_finish, "combine CE partials into lse and per-row loss");
-  m.def("ce_bwd", &ce_bwd, "in-place softmax-minus-onehot gradient of the logits");
+  m.def("ce_bwd", &ce_bwd, "in-place softmax-minus-onehot gradient of the logits (of a column chunk from col0)",
+        py::arg("logits"), py::arg("V"), py::arg("lse"), py::arg("targets"), py::arg("gscale"), py::arg("inv_count"),
+        py::arg("col0") = 0);
   m.def("embed_fwd", &embed_fwd, "embedding gather");
   m.def("embed_bwd", &embed_bwd, "embedding scatter-add into f32 grad");
   m.def("rope_bwd_to", &rope_bwd_to, "out-of-place RoPE backward (+ copy of the unrotated columns)");

@@ -65,13 +65,17 @@ __global__ void ce_finish_kernel(const float* __restrict__ pmax, const float* __
 // ------------------------------------------------------------------ CE bwd
 // In place: logits[r, v] <- (exp(logits - lse[r]) - [v == t_r]) * scale, where
 // scale = (*gscale) * inv_count.  Rows with target < 0 get zero gradient.
+// col0: vocabulary index of the buffer's first column (a column chunk of the
+// logits recomputed in the logit-free backward); a target outside the chunk adds
+// no one-hot term, an ignored row (target < 0) is zero.
 __global__ void ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, int64_t V,
                               const float* __restrict__ lse, const int64_t* __restrict__ targets,
-                              const float* __restrict__ gscale, float inv_count) {
+                              const float* __restrict__ gscale, float inv_count, int64_t col0) {
   const int64_t row = blockIdx.y;
   const float l = lse[row];
-  const int64_t t = targets[row];
-  const float sc = (t >= 0) ? (*gscale) * inv_count : 0.f;
+  const int64_t t0 = targets[row];
+  const float sc = (t0 >= 0) ? (*gscale) * inv_count : 0.f;
+  const int64_t t = t0 - col0;
   __nv_bfloat16* rp = logits + row * ld;
   const int64_t nvec = V / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
@@ -336,7 +340,7 @@ void launch_ce_finish(const float* pmax, const float* psum, int nt, const float*
 }
 
 void launch_ce_bwd(void* logits, int64_t ld, int64_t V, int64_t rows, const float* lse, const int64_t* targets,
-                   const float* gscale, float inv_count, cudaStream_t st) {
+                   const float* gscale, float inv_count, cudaStream_t st, int64_t col0) {
   if (!rows) return;
   OXI_CHECK(ld % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0, "logits rows must be 16-byte aligned");
   OXI_CHECK(rows < 65536 * 32768LL, "too many rows");
@@ -344,7 +348,7 @@ void launch_ce_bwd(void* logits, int64_t ld, int64_t V, int64_t rows, const floa
   unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 64));
   dim3 grid(gx, (unsigned)rows);
   ce_bwd_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, V, lse, targets, gscale,
-                                      inv_count);
+                                      inv_count, col0);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -15,6 +15,8 @@ from __future__ import annotations
 import math
 from typing import Optional
 
+import os
+
 import torch
 
 from ._C import ext, status
@@ -211,14 +213,33 @@ class SwiGLUMLP(torch.autograd.Function):
 
 
 # ------------------------------------------------------------- LM head + CE
+# Logits larger than this (bytes of bf16 [T, V]) are never materialised: the
+# backward recomputes them in column chunks instead (OXI_CE_MODE = full |
+# chunked | auto overrides).  Materialising is faster when it fits (one GEMM
+# fewer); the chunked path keeps only per-row log-sum-exp.
+CE_LOGITS_BUDGET = int(float(os.environ.get("OXI_CE_LOGITS_BUDGET", 16e9)))
+CE_CHUNK = int(os.environ.get("OXI_CE_CHUNK", 8192))
+
+
+def ce_mode(M: int, V: int) -> str:
+    mode = os.environ.get("OXI_CE_MODE", "auto")
+    if mode in ("full", "chunked"):
+        return mode
+    return "chunked" if M * V * 2 > CE_LOGITS_BUDGET else "full"
+
+
 class LinearCrossEntropy(torch.autograd.Function):
     """Mean token cross-entropy of logits = x W^T without a separate softmax pass.
 
-    Forward: one GEMM whose epilogue writes the bf16 logits plus per-(row,
-    256-column tile) max and sum-of-exp partials and the target logit; a small
-    kernel combines the partials into log-sum-exp and per-row loss.
-    Backward: softmax-minus-one-hot in place on the saved logits, then the dX
-    and dW GEMMs read it directly.
+    Forward: one GEMM whose epilogue writes per-(row, 256-column tile) max and
+    sum-of-exp partials and the target logit (and, in ``full`` mode, the bf16
+    logits); a small kernel combines the partials into log-sum-exp and per-row
+    loss.
+    Backward, ``full``: softmax-minus-one-hot in place on the saved logits, then
+    the dX and dW GEMMs read it directly.  ``chunked`` (logit-free): per column
+    chunk of ``CE_CHUNK`` vocabulary rows, recompute that chunk's logits, form
+    softmax-minus-one-hot from the saved log-sum-exp, accumulate dX (f32) and
+    write that chunk's rows of dW; no [T, V] buffer exists at any point.
     """
 
     @staticmethod
@@ -230,8 +251,11 @@ class LinearCrossEntropy(torch.autograd.Function):
         if ignore_index != -1:
             tg = torch.where(tg == ignore_index, torch.full_like(tg, -1), tg)
         nt = (V + 255) // 256
-        ldl = (V + 7) // 8 * 8
-        logits = torch.empty(M, ldl, dtype=x.dtype, device=x.device)
+        mode = ce_mode(M, V)
+        logits = None
+        if mode == "full":
+            ldl = (V + 7) // 8 * 8
+            logits = torch.empty(M, ldl, dtype=x.dtype, device=x.device)
         pm = torch.empty(M, nt, dtype=torch.float32, device=x.device)
         ps = torch.empty_like(pm)
         tl = torch.zeros(M, dtype=torch.float32, device=x.device)
@@ -240,20 +264,44 @@ class LinearCrossEntropy(torch.autograd.Function):
         loss = torch.empty(M, dtype=torch.float32, device=x.device)
         ext().ce_finish(pm, ps, tl, tg, lse, loss)
         count = (tg >= 0).sum().clamp_min(1)
-        ctx.save_for_backward(x2, logits, lse, tg, count)
-        ctx.w, ctx.V, ctx.xshape = w, V, x.shape
+        if logits is None:
+            ctx.save_for_backward(x2, lse, tg, count)
+        else:
+            ctx.save_for_backward(x2, logits, lse, tg, count)
+        ctx.w, ctx.V, ctx.xshape, ctx.mode = w, V, x.shape, mode
         return loss.sum() / count
 
     @staticmethod
     def backward(ctx, dloss):
-        x2, logits, lse, tg, count = ctx.saved_tensors
         w, V = ctx.w, ctx.V
+        if ctx.mode == "full":
+            x2, logits, lse, tg, count = ctx.saved_tensors
+            gscale = (dloss.float() / count.float()).reshape(1).contiguous()
+            ext().ce_bwd(logits, V, lse, tg, gscale, 1.0)
+            dl = logits[:, :V]
+            dx = mm(dl, w, b_t=True)
+            gw = _wgrad_gemm(w, dl, x2)
+            return dx.view(ctx.xshape), gw, None, None
+        x2, lse, tg, count = ctx.saved_tensors
         gscale = (dloss.float() / count.float()).reshape(1).contiguous()
-        ext().ce_bwd(logits, V, lse, tg, gscale, 1.0)
-        dl = logits[:, :V]
-        dx = mm(dl, w, b_t=True)
-        gw = _wgrad_gemm(w, dl, x2)
-        return dx.view(ctx.xshape), gw, None, None
+        M, K = x2.shape
+        C = max(8, min(CE_CHUNK, V) // 8 * 8)
+        buf = torch.empty(M, C, dtype=x2.dtype, device=x2.device)  # one chunk of logits, reused
+        dx32 = torch.empty(M, K, dtype=torch.float32, device=x2.device)
+        mg = getattr(w, "main_grad", None)
+        gw = None if mg is not None else torch.zeros(V, K, dtype=torch.float32, device=x2.device)
+        for c0 in range(0, V, C):
+            n = min(C, V - c0)
+            wc = w[c0:c0 + n]
+            lc = buf[:, :n]
+            mm(x2, wc, out=lc)
+            ext().ce_bwd(lc, n, lse, tg, gscale, 1.0, c0)
+            mm(lc, wc, b_t=True, out=dx32, beta=0.0 if c0 == 0 else 1.0)
+            dst = (mg.view(V, K) if mg is not None else gw)[c0:c0 + n]
+            mm(lc, x2, a_t=True, b_t=True, out=dst, beta=1.0)
+        if mg is not None:
+            _ready(w)
+        return dx32.to(x2.dtype).view(ctx.xshape), (gw.to(w.dtype) if gw is not None else None), None, None
 
 
 # -------------------------------------------------------------- attention

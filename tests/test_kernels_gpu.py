@@ -63,6 +63,46 @@ def test_linear_cross_entropy():
     assert _rel(w.grad, wr.grad) < 3e-2
 
 
+@pytest.mark.parametrize("T,H,V,chunk", [(1000, 512, 5003, 1024), (2048, 256, 30011, 8192), (300, 128, 777, 96)])
+def test_linear_cross_entropy_logit_free(monkeypatch, T, H, V, chunk):
+    """The chunked (logit-free) backward against the materialised one and fp32 torch; its
+    peak extra memory is one [T, chunk] block, never the [T, V] logits."""
+    from oxidizr_b200.ops import fused
+    torch.manual_seed(T + V)
+    x0 = torch.randn(T, H, device="cuda").bfloat16()
+    w0 = (torch.randn(V, H, device="cuda") / H ** 0.5).bfloat16()
+    t = torch.randint(0, V, (T,), device="cuda")
+    t[::11] = -100
+    res = {}
+    for mode in ("full", "chunked"):
+        monkeypatch.setenv("OXI_CE_MODE", mode)
+        monkeypatch.setattr(fused, "CE_CHUNK", chunk)
+        x = x0.clone().requires_grad_()
+        w = w0.clone().requires_grad_()
+        w.main_grad = torch.zeros(V, H, device="cuda")  # the trainer's f32 gradient view
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        loss = fused.LinearCrossEntropy.apply(x, w, t, -100)
+        loss.backward()
+        torch.cuda.synchronize()
+        res[mode] = (loss.detach(), x.grad, w.main_grad, torch.cuda.max_memory_allocated() - base)
+    lf, dxf, dwf, _ = res["full"]
+    lc, dxc, dwc, peak = res["chunked"]
+    assert abs(lc.item() - lf.item()) < 1e-5 * abs(lf.item())
+    assert _rel(dxc, dxf) < 1e-2 and _rel(dwc, dwf) < 1e-2
+    # the chunked path holds an f32 [T, H] dX, one [T, chunk] logits block and the
+    # partials; the full logits alone would be 2 T V bytes
+    if V > 4 * chunk:
+        assert peak < 2 * T * V, (peak, 2 * T * V)
+    xr = x0.float().requires_grad_()
+    wr = w0.float().requires_grad_()
+    lr = torch.nn.functional.cross_entropy(xr @ wr.t(), t, ignore_index=-100)
+    lr.backward()
+    assert abs(lc.item() - lr.item()) < 2e-3 * abs(lr.item())
+    assert _rel(dxc, xr.grad) < 3e-2 and _rel(dwc, wr.grad) < 3e-2
+
+
 def test_embedding_and_rope_bwd():
     from oxidizr_b200.ops._C import ext
     from oxidizr_b200.ops.fused import Embedding
