@@ -3,7 +3,7 @@
 //
 // E experts are split over W ranks (El = E / W local experts each).  Every
 // rank holds, mapped by all peers:
-//   xrecv  bf16 [cap, H]  token rows routed to its experts, one 128-aligned
+//   xrecv  bf16 [cap, H]  token rows routed to its experts, one MOE_SEG_ALIGN-aligned
 //                         segment per local expert (sources in rank order)
 //   srcidx int32 [cap]    source of each received row: rank * T*k + pair, -1 = padding
 //   yret   bf16 [T*k, H]  this rank's own (token, slot) pairs: the expert output
@@ -43,6 +43,7 @@
 
 #include "host_util.h"
 #include "kernels_ep.h"
+#include "kernels_moe.h"
 #include "ptx.cuh"
 
 namespace oxi {
@@ -92,7 +93,8 @@ __device__ void ep_last_cta_post(int* ctr, const uint64_t* peer_pads, int kind, 
   }
 }
 
-__device__ __forceinline__ int align128(int n) { return (n + 127) & ~127; }
+// expert segments of a receive buffer start on MOE_SEG_ALIGN-row boundaries (CTA-pair tiles)
+__device__ __forceinline__ int align_seg(int n) { return (n + MOE_SEG_ALIGN - 1) / MOE_SEG_ALIGN * MOE_SEG_ALIGN; }
 
 // ------------------------------------------------------------------ counts
 __global__ void ep_counts_kernel(const int* __restrict__ local_counts, const uint64_t* __restrict__ peer_pads,
@@ -127,7 +129,7 @@ __global__ void ep_counts_kernel(const int* __restrict__ local_counts, const uin
       for (int le = 0; le < El; ++le) {
         int c = 0;
         for (int s = 0; s < W; ++s) c += all_counts[s * E + d * El + le];
-        off += align128(c);
+        off += align_seg(c);
       }
       need = max(need, off);
     }
@@ -144,7 +146,7 @@ __global__ void ep_counts_kernel(const int* __restrict__ local_counts, const uin
       for (int s = 0; s < W; ++s) c += all_counts[s * E + rank * El + le];
       recv_counts[le] = skip ? 0 : c;
       seg_off[le] = off;
-      if (!skip) off += align128(c);
+      if (!skip) off += align_seg(c);
     }
     seg_off[El] = off;
     seg_off[El + 1] = skip ? 1 : 0;
@@ -159,7 +161,7 @@ __device__ int dest_base(const int* __restrict__ all_counts, int rank, int W, in
   for (int l = 0; l < le; ++l) {
     int c = 0;
     for (int s = 0; s < W; ++s) c += all_counts[s * E + dest * El + l];
-    off += align128(c);
+    off += align_seg(c);
   }
   for (int s = 0; s < rank; ++s) off += all_counts[s * E + e];
   return off;

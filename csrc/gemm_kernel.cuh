@@ -75,8 +75,8 @@ struct GemmParams {
   int* status;
   // grouped (MoE) modes: 0 none; 1 group-M (A rows split into expert segments,
   // B rows offset by expert); 2 group-K (K split into expert segments, one
-  // output matrix per expert).  seg_off[0..n_groups] are 128-aligned row
-  // offsets of the segments, on the device.
+  // output matrix per expert).  seg_off[0..n_groups] are row offsets of the
+  // segments (128-aligned; 256-aligned for CTA-pair group-M tiles), on the device.
   int group_mode;
   int n_groups;
   const int* seg_off;
@@ -139,7 +139,7 @@ __device__ __forceinline__ Unit unit_info(int t, const GemmParams& p, int num_kb
     u.tn = t % p.tiles_n;
     u.kb0 = 0;
     u.kb1 = num_kb;
-    const int m0 = u.tm * BM;
+    const int m0 = u.tm * BM * p.cg;  // a pair tile covers 2 * BM rows of one segment
     u.valid = m0 < __ldg(p.seg_off + p.n_groups);
     if (u.valid) {
       int lo = 0, hi = p.n_groups;  // last e with seg_off[e] <= m0
@@ -817,6 +817,22 @@ inline void use_pairs(GemmParams& p) {
   p.cg = 2;
   p.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
   p.num_tiles = p.tiles_m * p.tiles_n;
+}
+
+// The same for the grouped (MoE) GEMMs: group-M tiles need expert segments
+// aligned to the pair's 2 * BM rows (seg_align); group-K pairs tile the weight
+// rows of each expert's output and take any segment alignment.
+inline void use_pairs_grouped(GemmParams& p, int seg_align) {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = getenv("OXI_GEMM_CG");
+    mode = (e && e[0] == '1') ? 1 : 2;
+  }
+  if (mode != 2 || p.M <= BM) return;
+  if (p.group_mode == 1 && seg_align % (2 * BM) != 0) return;
+  p.cg = 2;
+  p.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+  p.num_tiles = (p.group_mode == 2 ? p.n_groups : 1) * p.tiles_m * p.tiles_n;
 }
 
 // Rows of B per CTA tile (the box height of B's tensor map when K-major).

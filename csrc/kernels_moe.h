@@ -6,6 +6,11 @@
 #include "kernels.h"
 
 namespace oxi {
+// Expert segments of the permuted rows start on multiples of this many rows
+// (the padding rows are zero), so a 256-row CTA-pair tile of the grouped
+// expert GEMM never straddles two experts.
+constexpr int MOE_SEG_ALIGN = 256;
+
 void launch_moe_permute(const void* x, int64_t ldx, const int64_t* topi, int64_t T, int k, int E, int H, int* counts,
                         int* seg_off, int* cursor, int* pos, void* xp, cudaStream_t st);
 void launch_moe_zero_pad(const int* seg_off, const int* counts, int E, void* m, int H, cudaStream_t st);

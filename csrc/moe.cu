@@ -1,12 +1,13 @@
-// Mixture-of-experts token permutation (counting sort into 128-row-aligned
+// Mixture-of-experts token permutation (counting sort into MOE_SEG_ALIGN-row-aligned
 // expert segments), weighted combine, their backward passes, and the grouped
 // GEMM launchers that run every expert's GEMM in one persistent launch.
 //
 // Layout: for T tokens with top-k routing, the permuted matrix X_perm has
 // rows seg_off[e] .. seg_off[e] + count[e] for expert e, where seg_off is the
-// prefix sum of counts rounded up to 128 (rows past count[e] are zero), so no
-// GEMM tile straddles two experts and the grouped weight-gradient GEMMs can
-// reduce over whole 64-row k-blocks.  pos[t, j] is the row of token t's j-th
+// prefix sum of counts rounded up to MOE_SEG_ALIGN = 256 (rows past count[e]
+// are zero), so no GEMM tile - one CTA's 128 rows or a CTA pair's 256 - straddles
+// two experts and the grouped weight-gradient GEMMs can reduce over whole
+// 64-row k-blocks.  pos[t, j] is the row of token t's j-th
 // expert.  Upstream computes every expert on every token (model.rs:561-565);
 // the sparse result is the same for the same routing.
 #include <cuda_bf16.h>
@@ -27,7 +28,7 @@ __global__ void moe_count_kernel(const int64_t* __restrict__ topi, int64_t n, in
   }
 }
 
-// single block: seg_off[e] = sum_{e' < e} roundup(count[e'], 128); cursor = seg_off
+// single block: seg_off[e] = sum_{e' < e} roundup(count[e'], MOE_SEG_ALIGN); cursor = seg_off
 __global__ void moe_offsets_kernel(const int* __restrict__ counts, int E, int* __restrict__ seg_off,
                                    int* __restrict__ cursor) {
   if (threadIdx.x == 0) {
@@ -35,7 +36,7 @@ __global__ void moe_offsets_kernel(const int* __restrict__ counts, int E, int* _
     for (int e = 0; e < E; ++e) {
       seg_off[e] = o;
       cursor[e] = o;
-      o += (counts[e] + 127) / 128 * 128;
+      o += (counts[e] + MOE_SEG_ALIGN - 1) / MOE_SEG_ALIGN * MOE_SEG_ALIGN;
     }
     seg_off[E] = o;
   }
@@ -259,7 +260,11 @@ void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& 
   }
   p.kb_per_split = (p.K + BK - 1) / BK;
   if (p.M == 0 || p.num_tiles == 0) return;
-  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, BN);
+  // CTA pairs (256 x 256 tiles, each CTA loading its own half of A and of B's
+  // rows): group-M needs segments aligned to the pair's 256 rows; group-K tiles
+  // the weight rows (the segments are its K range), so any alignment works.
+  use_pairs_grouped(p, MOE_SEG_ALIGN);
+  CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
   p.D = out;
   p.ldd = ldo;
   if (scatter) {

@@ -1,6 +1,6 @@
 """Sparse mixture-of-experts compute over the grouped tcgen05 GEMMs (csrc/moe.cu).
 
-Forward: counting-sort permutation of token rows into 128-aligned expert
+Forward: counting-sort permutation of token rows into 256-aligned expert
 segments; one grouped GEMM for every expert's gate|up projection with the
 SwiGLU epilogue; one grouped GEMM for every expert's down projection; a
 weighted combine (fused with the residual add).  Backward mirrors it with the
@@ -20,7 +20,8 @@ from .fused import _ready
 
 
 def rows_capacity(T: int, k: int, E: int) -> int:
-    return ((T * k + E * 128) + 127) // 128 * 128
+    # expert segments start on 256-row boundaries (MOE_SEG_ALIGN, CTA-pair tiles)
+    return ((T * k + E * 256) + 255) // 256 * 256
 
 
 def _wgrad_grouped(p, a, b, seg, E):

@@ -218,10 +218,10 @@ class EPLayerBuffers:
         from .fused_ar import SymmetricBuffer
         g = self.grp
         if exact:
-            cap = max(128, (rows + 127) // 128 * 128)
+            cap = max(256, (rows + 255) // 256 * 256)
         else:
             want = max(rows * self.HEADROOM, balanced_rows * self.HEADROOM, self.cap * self.HEADROOM)
-            cap = max(128, (int(want) + 1023) // 1024 * 1024)
+            cap = max(256, (int(want) + 1023) // 1024 * 1024)
         EPLayerBuffers.reallocs += 1
         torch.cuda.synchronize(g.device)
         if self.bufs is not None:
@@ -276,7 +276,7 @@ class EPExperts(torch.autograd.Function):
         seq = g.next_seq()
         if buf.cap == 0:  # first use: 2x the balanced load plus every segment's alignment
             forced = int(os.environ.get("OXI_EP_INITIAL_ROWS", "0"))  # tests: start over capacity
-            buf.ensure(forced, exact=True) if forced else buf.ensure(0, balanced_rows=T * k + El * 128)
+            buf.ensure(forced, exact=True) if forced else buf.ensure(0, balanced_rows=T * k + El * 256)
         buf.ensure_pairs(T * k)
         # the counts kernel checks every owner's rows against the capacity on the
         # device (no host read); over capacity, the layer is skipped on every rank

@@ -154,6 +154,47 @@ def bench_attn_mla(B=16, S=1024, H=12, Dqk=96, Dv=64, iters=20):
     return out
 
 
+def bench_ce(shapes=((16384, 2048, 128354), (16384, 768, 100277)), iters=5, chunks=(4096, 8192, 16384)):
+    """lm_head + cross-entropy forward + backward, logits materialised vs logit-free
+    (chunked recompute): device time and peak extra memory at the bench configs' shapes."""
+    import os
+    from ..ops import fused
+    peaks = measured_peaks()
+    out = []
+    for (T, H, V) in shapes:
+        x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_()
+        w = (torch.randn(V, H, device="cuda") / H ** 0.5).bfloat16().requires_grad_()
+        w.main_grad = torch.zeros(V, H, device="cuda")
+        t = torch.randint(0, V, (T,), device="cuda")
+
+        def step():
+            x.grad = None
+            fused.LinearCrossEntropy.apply(x, w, t, -100).backward()
+
+        row = {"T": T, "H": H, "V": V, "gemm_flops_per_gemm": 2.0 * T * V * H}
+        for mode, chunk in [("full", None)] + [("chunked", c) for c in chunks]:
+            os.environ["OXI_CE_MODE"] = mode
+            if chunk:
+                fused.CE_CHUNK = chunk
+            torch.cuda.synchronize()
+            base = torch.cuda.memory_allocated()
+            torch.cuda.reset_peak_memory_stats()
+            ms = time_fn(step, iters, warmup=2)
+            peak = torch.cuda.max_memory_allocated() - base
+            key = mode if chunk is None else f"chunked_{chunk}"
+            gemms = 3 if mode == "full" else 4
+            row[key] = {"ms": round(ms, 3), "peak_extra_gb": round(peak / 1e9, 2),
+                        "tflops": round(gemms * row["gemm_flops_per_gemm"] / ms / 1e9, 1),
+                        "frac_of_peak": round(gemms * row["gemm_flops_per_gemm"] / ms / 1e9
+                                              / peaks["bf16_tflops"], 3)}
+        os.environ.pop("OXI_CE_MODE", None)
+        print(json.dumps(row), flush=True)
+        out.append(row)
+        del x, w, t
+        torch.cuda.empty_cache()
+    return out
+
+
 def bench_ssm(iters=10):
     """Selective-scan kernels at the hybrid (Mamba2) and Mamba3 bench shapes: time and the
     effective HBM rate of the scan inputs/outputs (f32)."""
@@ -338,7 +379,7 @@ def run_once(what: str):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn", "ssm", "once"])
+    ap.add_argument("what", choices=["gemm", "attn", "ssm", "ce", "once"])
     ap.add_argument("--kernel", default="fa_fwd",
                     help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_dw | ssd_m2 | ssd_m3 | norm | "
                          "conv1d | swiglu | qkv_rope | ce | moe | m3_bc | mamba1 | adamw")
@@ -355,6 +396,9 @@ def main(argv=None):
         return
     if args.what == "ssm":
         bench_ssm(iters=args.iters)
+        return
+    if args.what == "ce":
+        bench_ce(iters=min(args.iters, 5))
         return
     if args.what == "gemm":
         if args.shapes:
