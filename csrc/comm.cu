@@ -50,6 +50,11 @@
 namespace oxi {
 namespace {
 
+// The reduce-scatter kernels run next to backward's persistent GEMMs: 128-thread
+// CTAs (about 16K registers each) fit on an SM beside a GEMM CTA (192 threads, up
+// to 202 registers), so a GEMM launched meanwhile does not wait for them.
+constexpr int RS_THREADS = 128;
+
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -138,7 +143,7 @@ __global__ void __launch_bounds__(512) bf16_to_f32_sumsq_kernel(const __nv_bfloa
 // NVLink stores are posted writes, so no thread waits on a round trip.  The
 // last CTA to finish publishes the bucket's epoch in every peer's pad.
 template <int W>
-__global__ void __launch_bounds__(512) push_bucket_kernel(float* __restrict__ grad, bool zero, int64_t lo, int64_t len,
+__global__ void __launch_bounds__(RS_THREADS) push_bucket_kernel(float* __restrict__ grad, bool zero, int64_t lo, int64_t len,
                                                           int rank, const uint64_t* __restrict__ peers_recv,
                                                           const uint64_t* __restrict__ peer_pads, int bucket,
                                                           int epoch, int* __restrict__ done_ctr) {
@@ -188,7 +193,7 @@ __global__ void __launch_bounds__(512) push_bucket_kernel(float* __restrict__ gr
 // this rank's shard from local memory (f32), store the reduced shard and add
 // its sum of squares.
 template <int W>
-__global__ void __launch_bounds__(512) reduce_bucket_kernel(const __nv_bfloat16* __restrict__ recv,
+__global__ void __launch_bounds__(RS_THREADS) reduce_bucket_kernel(const __nv_bfloat16* __restrict__ recv,
                                                             int* __restrict__ my_pad, int bucket, int epoch,
                                                             int64_t lo, int64_t len, float* __restrict__ rgrad,
                                                             float* __restrict__ sumsq, int* status,
@@ -261,7 +266,7 @@ __global__ void rs_flags_kernel(const uint64_t* __restrict__ peer_pads, int* __r
 // thread) just before this kernel on the same stream, so no SM spins here
 // while peers are still in their backward pass.
 template <int W>
-__global__ void __launch_bounds__(512) rs_pull_kernel(const uint64_t* __restrict__ peers_send, int rank, int64_t lo,
+__global__ void __launch_bounds__(RS_THREADS) rs_pull_kernel(const uint64_t* __restrict__ peers_send, int rank, int64_t lo,
                                                       int64_t len, float* __restrict__ rgrad,
                                                       float* __restrict__ sumsq, const int* status) {
   constexpr int UNR = (16 / W) < 1 ? 1 : ((16 / W) > 8 ? 8 : 16 / W);
@@ -366,7 +371,7 @@ __device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.
 // multimem.ld_reduce (NVSwitch fetches the W copies and sums them, f32
 // accumulation) and keeps the f32 result.  UNR 16-byte reductions per thread
 // are in flight.
-__global__ void __launch_bounds__(512) rs_nvls_kernel(const __nv_bfloat16* __restrict__ mc_send, int rank, int W,
+__global__ void __launch_bounds__(RS_THREADS) rs_nvls_kernel(const __nv_bfloat16* __restrict__ mc_send, int rank, int W,
                                                       int64_t lo, int64_t len, float* __restrict__ rgrad,
                                                       float* __restrict__ sumsq, const int* status) {
   constexpr int UNR = 4;
@@ -595,33 +600,37 @@ void launch_rs_bucket(int mode, float* grad, bool zero_grad, const uint64_t* pee
     OXI_CHECK(mc_buf != nullptr, "NVLS reduce-scatter needs the multicast address of the send buffer");
     launch_grad_to_bf16(grad + lo, reinterpret_cast<__nv_bfloat16*>(my_buf) + lo, len, zero_grad, st);
     rs_flags_kernel<<<1, 32, 0, st>>>(peer_pads, my_pad, rank, W, bucket, epoch, status, (uint64_t)wait_ns);
-    const int g = (int)std::max<int64_t>(1, std::min<int64_t>((len / W / 8 + 511) / 512, (int64_t)ctas));
-    rs_nvls_kernel<<<g, 512, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(mc_buf), rank, W, lo, len, rgrad, sumsq,
+    const int g = (int)std::max<int64_t>(1, std::min<int64_t>((len / W / 8 + RS_THREADS - 1) / RS_THREADS,
+                                                               (int64_t)ctas));
+    rs_nvls_kernel<<<g, RS_THREADS, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(mc_buf), rank, W, lo, len, rgrad, sumsq,
                                       status);
   } else if (mode == 0) {
     // pull: local cast into the send buffer, then the owner sums the W slices of its shard
     launch_grad_to_bf16(grad + lo, reinterpret_cast<__nv_bfloat16*>(my_buf) + lo, len, zero_grad, st);
     rs_flags_kernel<<<1, 32, 0, st>>>(peer_pads, my_pad, rank, W, bucket, epoch, status, (uint64_t)wait_ns);
-    const int g = (int)std::max<int64_t>(1, std::min<int64_t>((len / W / 8 + 511) / 512, (int64_t)ctas));
+    const int g = (int)std::max<int64_t>(1, std::min<int64_t>((len / W / 8 + RS_THREADS - 1) / RS_THREADS,
+                                                               (int64_t)ctas));
     switch (W) {
 #define OXI_RS(N)                                                                                                \
   case N:                                                                                                        \
-    rs_pull_kernel<N><<<g, 512, 0, st>>>(peers_buf, rank, lo, len, rgrad, sumsq, status);                        \
+    rs_pull_kernel<N><<<g, RS_THREADS, 0, st>>>(peers_buf, rank, lo, len, rgrad, sumsq, status);                 \
     break;
       OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)
 #undef OXI_RS
     }
   } else {
     // push: cast + NVLink stores into the owners' receive slots, then a local reduction
-    const int push_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / 8 + 511) / 512, 1), (int64_t)ctas);
-    const int red_ctas = (int)std::min<int64_t>(std::max<int64_t>((len / W / 8 + 511) / 512, 1), (int64_t)ctas);
+    const int push_ctas =
+        (int)std::min<int64_t>(std::max<int64_t>((len / 8 + RS_THREADS - 1) / RS_THREADS, 1), (int64_t)ctas);
+    const int red_ctas =
+        (int)std::min<int64_t>(std::max<int64_t>((len / W / 8 + RS_THREADS - 1) / RS_THREADS, 1), (int64_t)ctas);
     const __nv_bfloat16* rv = reinterpret_cast<const __nv_bfloat16*>(my_buf);
     switch (W) {
 #define OXI_RS(N)                                                                                                \
   case N:                                                                                                        \
-    push_bucket_kernel<N><<<push_ctas, 512, 0, st>>>(grad, zero_grad, lo, len, rank, peers_buf, peer_pads,       \
+    push_bucket_kernel<N><<<push_ctas, RS_THREADS, 0, st>>>(grad, zero_grad, lo, len, rank, peers_buf, peer_pads,       \
                                                      bucket, epoch, done_ctr);                                   \
-    reduce_bucket_kernel<N><<<red_ctas, 512, 0, st>>>(rv, my_pad, bucket, epoch, lo, len, rgrad, sumsq, status, \
+    reduce_bucket_kernel<N><<<red_ctas, RS_THREADS, 0, st>>>(rv, my_pad, bucket, epoch, lo, len, rgrad, sumsq, status, \
                                                       (uint64_t)wait_ns);                                        \
     break;
       OXI_RS(1) OXI_RS(2) OXI_RS(3) OXI_RS(4) OXI_RS(5) OXI_RS(6) OXI_RS(7) OXI_RS(8)

@@ -552,7 +552,7 @@ void ep_expert_gemm_scatter(torch::Tensor a, torch::Tensor b, bool b_mn, int64_t
                             int64_t seq, torch::Tensor status) {
   c10::cuda::CUDAGuard g(a.device());
   Mat ma = bf16_mat(a, "a"), mb = bf16_mat(b, "b");
-  TORCH_CHECK(seg_off.scalar_type() == torch::kInt32 && seg_off.numel() == n_groups + 1, "seg_off");
+  TORCH_CHECK(seg_off.scalar_type() == torch::kInt32 && seg_off.numel() >= n_groups + 1, "seg_off");
   TORCH_CHECK(srcidx.scalar_type() == torch::kInt32 && srcidx.numel() >= a.size(0), "srcidx int32 [rows]");
   const int64_t N = b_mn ? b.size(1) : group_rows_b;
   oxi::GroupedScatter sc;
@@ -1075,7 +1075,7 @@ void gemm_grouped(int64_t mode, int64_t epi, torch::Tensor a, bool a_mn, torch::
                   c10::optional<torch::Tensor> aux, torch::Tensor status) {
   c10::cuda::CUDAGuard g(a.device());
   Mat ma = bf16_mat(a, "a"), mb = bf16_mat(b, "b");
-  TORCH_CHECK(seg_off.scalar_type() == torch::kInt32 && seg_off.numel() == n_groups + 1, "seg_off");
+  TORCH_CHECK(seg_off.scalar_type() == torch::kInt32 && seg_off.numel() >= n_groups + 1, "seg_off");
   TORCH_CHECK(out.stride(-1) == 1, "out inner stride");
   void* o2 = nullptr;
   int64_t ld2 = 0;

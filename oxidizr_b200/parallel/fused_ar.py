@@ -132,9 +132,10 @@ class ShardedDDPAdamW:
         self.group = group
         self.rank = dist.get_rank(group)
         self.W = dist.get_world_size(group)
-        # CTAs per reduce-scatter / all-gather kernel (they share SMs with the GEMMs they overlap)
-        self.rs_ctas = int(rs_ctas if rs_ctas is not None else os.environ.get("OXI_RS_CTAS", 64))
-        self.ag_ctas = int(ag_ctas if ag_ctas is not None else os.environ.get("OXI_AG_CTAS", 64))
+        # CTAs per reduce-scatter (128 threads each) / all-gather (256 threads each) kernel;
+        # both are small enough to sit on an SM beside the GEMM CTA they overlap
+        self.rs_ctas = int(rs_ctas if rs_ctas is not None else os.environ.get("OXI_RS_CTAS", 256))
+        self.ag_ctas = int(ag_ctas if ag_ctas is not None else os.environ.get("OXI_AG_CTAS", 148))
         # a peer that has not posted its flag within this time is reported as failed
         self.wait_ns = int(peer_timeout_s * 1e9)
         named_params, local = split_local(list(named_params))

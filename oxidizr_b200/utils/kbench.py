@@ -326,6 +326,30 @@ def run_once(what: str):
         for _ in range(3):
             FlashAttention.apply(q, k, v, 1.0 / math.sqrt(Dqk), True).backward(
                 torch.ones(B, S, H, Dv, device="cuda").bfloat16())
+    elif what == "mla_pack":
+        # MLA operand packing of the hybrid config (12 heads, head dim 64, rope dim 32, 16 x 1024 tokens)
+        from ..models.common import RopeCache
+        from ..ops.mla import MlaPack
+        B, S, nh, hd, dr = 16, 1024, 12, 64, 32
+        qc = torch.randn(B, S, nh * hd, device="cuda").bfloat16().requires_grad_()
+        kv = torch.randn(B, S, 2 * nh * hd, device="cuda").bfloat16().requires_grad_()
+        d = torch.randn(B, S, 768 + dr + nh * dr, device="cuda").bfloat16()
+        rp = d[..., 768:].detach().requires_grad_()
+        cos, sin = RopeCache.get(dr, S, 10000.0, "cuda")
+        for _ in range(3):
+            q, k, v = MlaPack.apply(qc, kv, rp, cos, sin, nh, hd, dr)
+            (q.float().sum() + k.float().sum() + v.float().sum()).backward()
+    elif what == "ce_chunked":
+        # logit-free lm_head + cross-entropy backward (recomputed 8192-column chunks), 4096 tokens
+        import os
+        from ..ops import api
+        os.environ["OXI_CE_MODE"] = "chunked"
+        T, H, V = 4096, 2048, 128354
+        x = (torch.randn(T, H, device="cuda") * 0.5).bfloat16().requires_grad_()
+        w = torch.nn.Parameter((torch.randn(V, H, device="cuda") * 0.02).bfloat16())
+        tgt = torch.randint(0, V, (T,), device="cuda")
+        for _ in range(3):
+            api.linear_cross_entropy(x, w, tgt).backward()
     elif what == "moe":
         # router top-8 of 64 + grouped expert SwiGLU GEMMs at the MoE config's shapes, 4096 tokens
         from ..ops.moe_kernels import GroupedExperts, RouterTopK
@@ -382,7 +406,7 @@ def main(argv=None):
     ap.add_argument("what", choices=["gemm", "attn", "ssm", "ce", "once"])
     ap.add_argument("--kernel", default="fa_fwd",
                     help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_dw | ssd_m2 | ssd_m3 | norm | "
-                         "conv1d | swiglu | qkv_rope | ce | moe | m3_bc | mamba1 | adamw")
+                         "conv1d | swiglu | qkv_rope | ce | ce_chunked | mla_pack | moe | m3_bc | mamba1 | adamw")
     ap.add_argument("--shapes", nargs="*", default=None, help="M,N,K[,layout] with layout nn|nt|tt")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)
