@@ -11,7 +11,8 @@
 //             the shared k_rope rotated once per token and stored to every head.
 //   backward: dq_c [T, nh*hd], dkv [T, 2*nh*hd] and drp [T, dr + nh*dr]: the
 //             inverse rotation of dq_rope, and of the head sum of dk_rope.
-// One warp per token; 16-byte loads / stores for the no-RoPE columns.
+// One warp per token, its lanes spread over every head: 16-byte loads / stores
+// for the no-RoPE columns, (head, pair) items for the RoPE columns.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <algorithm>
@@ -25,46 +26,48 @@ namespace {
 
 __device__ __forceinline__ float ldf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-// rows of nvec 16-byte vectors: dst[v] = src[v] for v in [lane, nvec) step 32
-__device__ __forceinline__ void copy_vecs(uint4* __restrict__ dst, const uint4* __restrict__ src, int nvec, int lane) {
-  for (int v = lane; v < nvec; v += 32) dst[v] = src[v];
-}
-
+// The warp of token t spreads every column block of the token over its lanes:
+// the no-RoPE parts as 16-byte vectors (nh * hd / 8 of them per tensor), the RoPE
+// parts as (head, pair) items, nh * dr / 2 of them; lane l always owns pair
+// index e = l % (dr / 2) when dr / 2 divides 32, so the head sum of dk_rope
+// needs one shuffle at the end.
 __global__ void __launch_bounds__(256) mla_pack_fwd_kernel(
     const __nv_bfloat16* __restrict__ qc, int64_t ldqc, const __nv_bfloat16* __restrict__ kv, int64_t ldkv,
     const __nv_bfloat16* __restrict__ rp, int64_t ldrp, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, int64_t T, int S, int nh, int hd, int dr, __nv_bfloat16* __restrict__ q,
     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v) {
   const int lane = threadIdx.x & 31;
-  const int dq = hd + dr, half = dr / 2;
+  const int dq = hd + dr, half = dr / 2, vph = hd / 8, nvec = nh * vph, npair = nh * half;
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T;
        t += (int64_t)gridDim.x * (blockDim.x / 32)) {
     const int pos = (int)(t % S);
+    const uint4* qsrc = reinterpret_cast<const uint4*>(qc + t * ldqc);
+    const uint4* ksrc = reinterpret_cast<const uint4*>(kv + t * ldkv);
+    const uint4* vsrc = reinterpret_cast<const uint4*>(kv + t * ldkv + (int64_t)nh * hd);
+    uint4* vdst = reinterpret_cast<uint4*>(v + t * (int64_t)nh * hd);
+#pragma unroll 4
+    for (int i = lane; i < nvec; i += 32) {
+      const int h = i / vph, j = i - h * vph;
+      const uint4 a = qsrc[i], b = ksrc[i], c = vsrc[i];
+      reinterpret_cast<uint4*>(q + (t * nh + h) * dq)[j] = a;
+      reinterpret_cast<uint4*>(k + (t * nh + h) * dq)[j] = b;
+      vdst[i] = c;
+    }
+    const __nv_bfloat16* rrow = rp + t * ldrp;
     const float* ct = cos_t + (int64_t)pos * half;
     const float* st = sin_t + (int64_t)pos * half;
-    const __nv_bfloat16* rrow = rp + t * ldrp;
-    // shared k_rope, rotated once: lane i < half owns the pair (i, i + half)
-    float kr1 = 0.f, kr2 = 0.f;
-    if (lane < half) {
-      const float x1 = ldf(rrow + lane), x2 = ldf(rrow + lane + half), c = ct[lane], s = st[lane];
-      kr1 = x1 * c - x2 * s;
-      kr2 = x2 * c + x1 * s;
-    }
-    for (int h = 0; h < nh; ++h) {
-      __nv_bfloat16* qo = q + (t * nh + h) * dq;
-      __nv_bfloat16* ko = k + (t * nh + h) * dq;
-      copy_vecs(reinterpret_cast<uint4*>(qo), reinterpret_cast<const uint4*>(qc + t * ldqc + h * hd), hd / 8, lane);
-      copy_vecs(reinterpret_cast<uint4*>(ko), reinterpret_cast<const uint4*>(kv + t * ldkv + h * hd), hd / 8, lane);
-      copy_vecs(reinterpret_cast<uint4*>(v + (t * nh + h) * hd),
-                reinterpret_cast<const uint4*>(kv + t * ldkv + (int64_t)nh * hd + h * hd), hd / 8, lane);
-      if (lane < half) {
-        const __nv_bfloat16* qr = rrow + dr + h * dr;
-        const float x1 = ldf(qr + lane), x2 = ldf(qr + lane + half), c = ct[lane], s = st[lane];
-        qo[hd + lane] = __float2bfloat16(x1 * c - x2 * s);
-        qo[hd + lane + half] = __float2bfloat16(x2 * c + x1 * s);
-        ko[hd + lane] = __float2bfloat16(kr1);
-        ko[hd + lane + half] = __float2bfloat16(kr2);
-      }
+    for (int i = lane; i < npair; i += 32) {
+      const int h = i / half, e = i - h * half;
+      const float c = ct[e], s = st[e];
+      const __nv_bfloat16* qr = rrow + dr + h * dr;
+      const float x1 = ldf(qr + e), x2 = ldf(qr + e + half);
+      const float y1 = ldf(rrow + e), y2 = ldf(rrow + e + half);  // the shared k_rope
+      __nv_bfloat16* qo = q + (t * nh + h) * dq + hd;
+      __nv_bfloat16* ko = k + (t * nh + h) * dq + hd;
+      qo[e] = __float2bfloat16(x1 * c - x2 * s);
+      qo[e + half] = __float2bfloat16(x2 * c + x1 * s);
+      ko[e] = __float2bfloat16(y1 * c - y2 * s);
+      ko[e + half] = __float2bfloat16(y2 * c + y1 * s);
     }
   }
 }
@@ -74,38 +77,64 @@ __global__ void __launch_bounds__(256) mla_pack_bwd_kernel(
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int64_t T, int S, int nh, int hd, int dr,
     __nv_bfloat16* __restrict__ dqc, __nv_bfloat16* __restrict__ dkv, __nv_bfloat16* __restrict__ drp) {
   const int lane = threadIdx.x & 31;
-  const int dqw = hd + dr, half = dr / 2;
+  const int dqw = hd + dr, half = dr / 2, vph = hd / 8, nvec = nh * vph, npair = nh * half;
+  const bool lane_pairs = (32 % half) == 0;  // lane l always owns pair e = l % half
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < T;
        t += (int64_t)gridDim.x * (blockDim.x / 32)) {
     const int pos = (int)(t % S);
-    float c = 0.f, s = 0.f;
-    if (lane < half) {
-      c = cos_t[(int64_t)pos * half + lane];
-      s = sin_t[(int64_t)pos * half + lane];
+    uint4* qdst = reinterpret_cast<uint4*>(dqc + t * (int64_t)nh * hd);
+    uint4* kdst = reinterpret_cast<uint4*>(dkv + t * (int64_t)2 * nh * hd);
+    uint4* vdst = reinterpret_cast<uint4*>(dkv + t * (int64_t)2 * nh * hd + (int64_t)nh * hd);
+    const uint4* vsrc = reinterpret_cast<const uint4*>(dv + t * (int64_t)nh * hd);
+#pragma unroll 4
+    for (int i = lane; i < nvec; i += 32) {
+      const int h = i / vph, j = i - h * vph;
+      const uint4 a = reinterpret_cast<const uint4*>(dq + (t * nh + h) * dqw)[j];
+      const uint4 b = reinterpret_cast<const uint4*>(dk + (t * nh + h) * dqw)[j];
+      const uint4 c = vsrc[i];
+      qdst[i] = a;
+      kdst[i] = b;
+      vdst[i] = c;
     }
     __nv_bfloat16* rrow = drp + t * (int64_t)(dr + nh * dr);
-    float ks1 = 0.f, ks2 = 0.f;  // head sum of dk_rope
-    for (int h = 0; h < nh; ++h) {
-      const __nv_bfloat16* dqi = dq + (t * nh + h) * dqw;
-      const __nv_bfloat16* dki = dk + (t * nh + h) * dqw;
-      copy_vecs(reinterpret_cast<uint4*>(dqc + t * (int64_t)nh * hd + h * hd), reinterpret_cast<const uint4*>(dqi),
-                hd / 8, lane);
-      copy_vecs(reinterpret_cast<uint4*>(dkv + t * (int64_t)2 * nh * hd + h * hd), reinterpret_cast<const uint4*>(dki),
-                hd / 8, lane);
-      copy_vecs(reinterpret_cast<uint4*>(dkv + t * (int64_t)2 * nh * hd + (int64_t)nh * hd + h * hd),
-                reinterpret_cast<const uint4*>(dv + (t * nh + h) * hd), hd / 8, lane);
-      if (lane < half) {
-        // inverse rotation: dx1 = dy1 c + dy2 s, dx2 = dy2 c - dy1 s
-        const float y1 = ldf(dqi + hd + lane), y2 = ldf(dqi + hd + lane + half);
-        rrow[dr + h * dr + lane] = __float2bfloat16(y1 * c + y2 * s);
-        rrow[dr + h * dr + lane + half] = __float2bfloat16(y2 * c - y1 * s);
-        ks1 += ldf(dki + hd + lane);
-        ks2 += ldf(dki + hd + lane + half);
+    const float* ct = cos_t + (int64_t)pos * half;
+    const float* st = sin_t + (int64_t)pos * half;
+    float ks1 = 0.f, ks2 = 0.f;  // this lane's part of the head sum of dk_rope (pair lane % half)
+    for (int i = lane; i < npair; i += 32) {
+      const int h = i / half, e = i - h * half;
+      const float c = ct[e], s = st[e];
+      const __nv_bfloat16* dqi = dq + (t * nh + h) * dqw + hd;
+      const __nv_bfloat16* dki = dk + (t * nh + h) * dqw + hd;
+      // inverse rotation: dx1 = dy1 c + dy2 s, dx2 = dy2 c - dy1 s
+      const float y1 = ldf(dqi + e), y2 = ldf(dqi + e + half);
+      rrow[dr + h * dr + e] = __float2bfloat16(y1 * c + y2 * s);
+      rrow[dr + h * dr + e + half] = __float2bfloat16(y2 * c - y1 * s);
+      if (lane_pairs) {
+        ks1 += ldf(dki + e);
+        ks2 += ldf(dki + e + half);
       }
     }
-    if (lane < half) {
-      rrow[lane] = __float2bfloat16(ks1 * c + ks2 * s);
-      rrow[lane + half] = __float2bfloat16(ks2 * c - ks1 * s);
+    if (lane_pairs) {
+      // lanes with the same pair index: l, l + half, l + 2 half, ...
+      for (int o = half; o < 32; o <<= 1) {
+        ks1 += __shfl_xor_sync(0xffffffffu, ks1, o);
+        ks2 += __shfl_xor_sync(0xffffffffu, ks2, o);
+      }
+      if (lane < half) {
+        const float c = ct[lane], s = st[lane];
+        rrow[lane] = __float2bfloat16(ks1 * c + ks2 * s);
+        rrow[lane + half] = __float2bfloat16(ks2 * c - ks1 * s);
+      }
+    } else if (lane < half) {
+      float a1 = 0.f, a2 = 0.f;
+      for (int h = 0; h < nh; ++h) {
+        const __nv_bfloat16* dki = dk + (t * nh + h) * dqw + hd;
+        a1 += ldf(dki + lane);
+        a2 += ldf(dki + lane + half);
+      }
+      const float c = ct[lane], s = st[lane];
+      rrow[lane] = __float2bfloat16(a1 * c + a2 * s);
+      rrow[lane + half] = __float2bfloat16(a2 * c - a1 * s);
     }
   }
 }

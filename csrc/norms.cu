@@ -32,6 +32,15 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+__device__ __forceinline__ void unpack8(uint4 u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
 __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float* f) {
   uint4 u = *reinterpret_cast<const uint4*>(p);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -48,6 +57,18 @@ __device__ __forceinline__ void st8(__nv_bfloat16* p, const float* f) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
   *reinterpret_cast<uint4*>(p) = u;
+}
+// 8 consecutive weights (or biases) from column c, a multiple of 8: one 16-byte
+// load for bf16, two for f32
+__device__ __forceinline__ void ldw8(const void* w, int wf32, int c, float* f) {
+  if (wf32) {
+    const float4 a = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(w) + c)[0];
+    const float4 b = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(w) + c)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    ld8(reinterpret_cast<const __nv_bfloat16*>(w) + c, f);
+  }
 }
 __device__ __forceinline__ float ldw(const void* w, int wf32, int i) {
   return wf32 ? reinterpret_cast<const float*>(w)[i] : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(w)[i]);
@@ -98,12 +119,13 @@ __global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_
   for (int i = 0; i < VPL; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nv) {
-      float o[8];
+      float o[8], wv[8], bv[8];
+      ldw8(w, wf32, vi * 8, wv);
+      if (MODE == 1) ldw8(b, wf32, vi * 8, bv);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int c = vi * 8 + j;
-        float t = (v[i][j] - mean) * rstd * ldw(w, wf32, c);
-        if (MODE == 1) t += ldw(b, wf32, c);
+        float t = (v[i][j] - mean) * rstd * wv[j];
+        if (MODE == 1) t += bv[j];
         o[j] = t;
       }
       st8(y + row * H + vi * 8, o);
@@ -237,21 +259,36 @@ __global__ void __launch_bounds__(512) norm_bwd_row_kernel(
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
   const int c0 = t * 8;
   float wv[8], pdw[8], pdb[8];
+  ldw8(w, wf32, c0, wv);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    wv[j] = ldw(w, wf32, c0 + j);
     pdw[j] = 0.f;
     pdb[j] = 0.f;
   }
   const float inv_h = 1.f / (float)H;
+  // the next row's operands are loaded (raw 16-byte vectors) before this row's
+  // reductions, so each thread keeps two rows of loads in flight
+  uint4 nx = make_uint4(0u, 0u, 0u, 0u), nd = nx, ng = nx, nr = nx;
+  float nrstd = 0.f, nmean = 0.f;
+  auto fetch = [&](int64_t r) {
+    nx = *reinterpret_cast<const uint4*>(x + r * H + c0);
+    nd = *reinterpret_cast<const uint4*>(dy + r * H + c0);
+    if (MODE == 2) ng = *reinterpret_cast<const uint4*>(gate + r * H + c0);
+    if (dres) nr = *reinterpret_cast<const uint4*>(dres + r * H + c0);
+    nrstd = stat_rstd[r];
+    if (MODE == 1) nmean = stat_mean[r];
+  };
+  if ((int64_t)blockIdx.x < rows) fetch(blockIdx.x);
   int it = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
-    const float rstd = stat_rstd[row];
-    const float mean = MODE == 1 ? stat_mean[row] : 0.f;
-    float xv[8], dv[8], g[8], xh[8];
-    ld8(x + row * H + c0, xv);
-    ld8(dy + row * H + c0, dv);
-    if (MODE == 2) ld8(gate + row * H + c0, g);
+    const float rstd = nrstd;
+    const float mean = MODE == 1 ? nmean : 0.f;
+    float xv[8], dv[8], g[8], xh[8], rv[8];
+    unpack8(nx, xv);
+    unpack8(nd, dv);
+    if (MODE == 2) unpack8(ng, g);
+    if (dres) unpack8(nr, rv);
+    if (row + gridDim.x < rows) fetch(row + gridDim.x);
     float a1 = 0.f, a2 = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -297,10 +334,8 @@ __global__ void __launch_bounds__(512) norm_bwd_row_kernel(
       st8(dgate + row * H + c0, dg);
     }
     if (dres) {
-      float r[8];
-      ld8(dres + row * H + c0, r);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] += r[j];
+      for (int j = 0; j < 8; ++j) o[j] += rv[j];
     }
     st8(dx + row * H + c0, o);
   }
@@ -366,6 +401,8 @@ int norm_grid(int64_t rows) {
 void launch_norm_fwd(int mode, const void* x, const void* gate, const void* w, bool wf32, const void* b, void* y,
                      float* rstd, float* mean, int64_t rows, int H, float eps, cudaStream_t st) {
   OXI_CHECK(H % 8 == 0 && H <= 32 * 8 * MAXV, "norm: hidden must be a multiple of 8 and <= 4096, got ", H);
+  OXI_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0,
+            "norm: weight and bias must be 16-byte aligned (8-element vector loads)");
   if (rows == 0) return;
   dim3 grid((unsigned)((rows + NW - 1) / NW)), block(NW * 32);
   auto X = reinterpret_cast<const __nv_bfloat16*>(x);
@@ -386,6 +423,7 @@ void launch_norm_bwd(int mode, const void* dy, const void* x, const void* gate, 
                      const float* rstd, const float* mean, const void* dres, void* dx, void* dgate, float* dw,
                      float* db, int64_t rows, int H, cudaStream_t st, float* part, int part_rows) {
   OXI_CHECK(H % 8 == 0 && H <= 32 * 8 * MAXV, "norm: hidden must be a multiple of 8 and <= 4096");
+  OXI_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0, "norm: weight must be 16-byte aligned (8-element vector loads)");
   if (rows == 0) return;
   if (H % 256 == 0 && H <= 4096) {
     // CTA per row: H / 8 threads; enough CTAs for every SM to hold 2048 threads

@@ -195,6 +195,56 @@ def bench_ce(shapes=((16384, 2048, 128354), (16384, 768, 100277)), iters=5, chun
     return out
 
 
+def bench_moe_gemms(T=16384, H=2048, E=64, k=8, I=1024, iters=10):
+    """The six grouped expert GEMMs of one MoE layer at the MoE config's per-GPU shape
+    (one GPU holding all experts): useful TFLOP/s counts real rows only (set
+    OXI_GEMM_CG=1 to time single-CTA tiles instead of CTA pairs)."""
+    import os
+    from ..ops._C import ext, status
+    from ..ops.moe_kernels import rows_capacity
+    peaks = measured_peaks()
+    torch.manual_seed(0)
+    x = (torch.randn(T, H, device="cuda") * 0.5).bfloat16()
+    topi = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)]) if T <= 4096 else \
+        torch.randint(0, E, (T, k), device="cuda")
+    cap = rows_capacity(T, k, E)
+    counts, seg, pos, xp = ext().moe_permute(x, topi.contiguous(), E, cap)
+    wgu = (torch.randn(E, 2 * I, H, device="cuda") * 0.02).bfloat16()
+    wd = (torch.randn(E, H, I, device="cuda") * 0.02).bfloat16()
+    h = torch.empty(cap, I, dtype=torch.bfloat16, device="cuda")
+    gu = torch.empty(cap, 2 * I, dtype=torch.bfloat16, device="cuda")
+    yp = torch.empty(cap, H, dtype=torch.bfloat16, device="cuda")
+    dyp = torch.randn(cap, H, device="cuda").bfloat16()
+    dgu = torch.empty_like(gu)
+    dxp = torch.empty_like(xp)
+    g_gu = torch.zeros(E, 2 * I, H, device="cuda")
+    g_d = torch.zeros(E, H, I, device="cuda")
+    st = status("cuda")
+    rows = T * k
+    cases = {
+        "gate_up_swiglu": (lambda: ext().gemm_grouped(1, 2, xp, False, wgu.view(E * 2 * I, H), False, E, seg, 2 * I,
+                                                      h, gu, None, st), 2.0 * rows * 2 * I * H),
+        "down": (lambda: ext().gemm_grouped(1, 0, h, False, wd.view(E * H, I), False, E, seg, H, yp, None, None, st),
+                 2.0 * rows * H * I),
+        "down_dx_swiglu_bwd": (lambda: ext().gemm_grouped(1, 3, dyp, False, wd.view(E * H, I), True, E, seg, H, dgu,
+                                                          None, gu, st), 2.0 * rows * H * I),
+        "down_wgrad": (lambda: ext().gemm_grouped(2, 1, dyp, True, h, True, E, seg, 0, g_d, None, None, st),
+                       2.0 * rows * H * I),
+        "gate_up_dx": (lambda: ext().gemm_grouped(1, 0, dgu, False, wgu.view(E * 2 * I, H), True, E, seg, 2 * I, dxp,
+                                                  None, None, st), 2.0 * rows * 2 * I * H),
+        "gate_up_wgrad": (lambda: ext().gemm_grouped(2, 1, dgu, True, xp, True, E, seg, 0, g_gu, None, None, st),
+                          2.0 * rows * 2 * I * H),
+    }
+    out = {"T": T, "E": E, "k": k, "H": H, "I": I, "rows_per_expert": rows / E, "cap": cap,
+           "tiles": "single-CTA" if os.environ.get("OXI_GEMM_CG") == "1" else "CTA pairs"}
+    for name, (fn, fl) in cases.items():
+        ms = time_fn(fn, iters)
+        out[name] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
+                     "frac_of_peak": round(fl / ms / 1e9 / peaks["bf16_tflops"], 3)}
+    print(json.dumps(out), flush=True)
+    return out
+
+
 def bench_ssm(iters=10):
     """Selective-scan kernels at the hybrid (Mamba2) and Mamba3 bench shapes: time and the
     effective HBM rate of the scan inputs/outputs (f32)."""
@@ -403,7 +453,7 @@ def run_once(what: str):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn", "ssm", "ce", "once"])
+    ap.add_argument("what", choices=["gemm", "attn", "ssm", "ce", "moe", "once"])
     ap.add_argument("--kernel", default="fa_fwd",
                     help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_dw | ssd_m2 | ssd_m3 | norm | "
                          "conv1d | swiglu | qkv_rope | ce | ce_chunked | mla_pack | moe | m3_bc | mamba1 | adamw")
@@ -423,6 +473,10 @@ def main(argv=None):
         return
     if args.what == "ce":
         bench_ce(iters=min(args.iters, 5))
+        return
+    if args.what == "moe":
+        bench_moe_gemms(iters=min(args.iters, 10))
+        bench_moe_gemms(T=16384, H=768, E=32, k=4, I=512, iters=min(args.iters, 10))
         return
     if args.what == "gemm":
         if args.shapes:
