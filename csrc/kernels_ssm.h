@@ -108,4 +108,16 @@ void launch_dskip_bwd(const void* g, const void* x, const float* y, const float*
                       int64_t rows, int H, int P, bool per_row, void* dx, float* dd, float* e, cudaStream_t st);
 void launch_ssd_dloga(const float* e, const float* ga, const float* dg, int B, int S, int H, float* sums, float* dla,
                       cudaStream_t st);
+// Mamba3 per-(token, head) scan coefficients (m3_glue.cu).  dt_raw, lam_raw bf16 [T, H]
+// contiguous, bias bf16 [H], A f32 [H]; out f32 [T, H]: dt (softplus + clamp), loga = A dt,
+// gamma' = lam dt + c, c (shifted-state coefficient).  Backward takes the gradients of the
+// four outputs (any may be null) and writes d dt_raw, d lam_raw (bf16) and adds d dt_bias,
+// d A (f32 [H]).
+void launch_m3_coef_fwd(const void* dt_raw, const void* bias, const void* lam_raw, const float* A, int64_t T, int S,
+                        int H, float lo, float hi, float* dt_out, float* loga, float* gp, float* c_out,
+                        cudaStream_t st);
+void launch_m3_coef_bwd(const void* dt_raw, const void* bias, const void* lam_raw, const float* A, int64_t T, int S,
+                        int H, float lo, float hi, const float* d_dt, const float* d_loga, const float* d_gp,
+                        const float* d_c, void* d_dt_raw, void* d_lam_raw, float* d_bias, float* d_A,
+                        cudaStream_t st);
 }  // namespace oxi

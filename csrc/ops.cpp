@@ -432,6 +432,54 @@ void ag_wait(torch::Tensor my_pad, int64_t W, int64_t bucket, int64_t epoch, tor
   oxi::launch_ag_wait(my_pad.data_ptr<int>(), (int)W, (int)bucket, (int)epoch, status_ptr(status), wait_ns, stream());
 }
 
+// ------------------------------------------------------------ Mamba3 scan coefficients
+namespace {
+void m3c_check(const torch::Tensor& t, int64_t T, int64_t H, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.is_contiguous() && t.numel() == T * H, what,
+              ": bf16 contiguous [T, H]");
+}
+const float* opt_f32(const c10::optional<torch::Tensor>& t, int64_t n) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous() && t->numel() == n,
+              "coefficient gradient: f32 contiguous [T, H]");
+  return t->data_ptr<float>();
+}
+}  // namespace
+
+std::vector<torch::Tensor> m3_coef_fwd(torch::Tensor dt_raw, torch::Tensor bias, torch::Tensor lam_raw,
+                                       torch::Tensor A, int64_t S, double lo, double hi) {
+  c10::cuda::CUDAGuard g(dt_raw.device());
+  const int64_t H = bias.numel(), T = dt_raw.numel() / std::max<int64_t>(H, 1);
+  m3c_check(dt_raw, T, H, "dt_raw");
+  m3c_check(lam_raw, T, H, "lam_raw");
+  TORCH_CHECK(bias.scalar_type() == torch::kBFloat16 && bias.is_contiguous() && A.scalar_type() == torch::kFloat32 &&
+                  A.is_contiguous() && A.numel() == H, "dt_bias bf16 [H], A f32 [H]");
+  auto o = dt_raw.options().dtype(torch::kFloat32);
+  auto dt = torch::empty({T, H}, o), loga = torch::empty({T, H}, o), gp = torch::empty({T, H}, o),
+       c = torch::empty({T, H}, o);
+  oxi::launch_m3_coef_fwd(dt_raw.data_ptr(), bias.data_ptr(), lam_raw.data_ptr(), A.data_ptr<float>(), T, (int)S,
+                          (int)H, (float)lo, (float)hi, dt.data_ptr<float>(), loga.data_ptr<float>(),
+                          gp.data_ptr<float>(), c.data_ptr<float>(), stream());
+  return {dt, loga, gp, c};
+}
+
+std::vector<torch::Tensor> m3_coef_bwd(torch::Tensor dt_raw, torch::Tensor bias, torch::Tensor lam_raw,
+                                       torch::Tensor A, int64_t S, double lo, double hi,
+                                       c10::optional<torch::Tensor> d_dt, c10::optional<torch::Tensor> d_loga,
+                                       c10::optional<torch::Tensor> d_gp, c10::optional<torch::Tensor> d_c) {
+  c10::cuda::CUDAGuard g(dt_raw.device());
+  const int64_t H = bias.numel(), T = dt_raw.numel() / std::max<int64_t>(H, 1);
+  m3c_check(dt_raw, T, H, "dt_raw");
+  m3c_check(lam_raw, T, H, "lam_raw");
+  auto ddt_raw = torch::empty_like(dt_raw), dlam_raw = torch::empty_like(lam_raw);
+  auto dbias = torch::zeros({H}, dt_raw.options().dtype(torch::kFloat32)), dA = torch::zeros_like(dbias);
+  oxi::launch_m3_coef_bwd(dt_raw.data_ptr(), bias.data_ptr(), lam_raw.data_ptr(), A.data_ptr<float>(), T, (int)S,
+                          (int)H, (float)lo, (float)hi, opt_f32(d_dt, T * H), opt_f32(d_loga, T * H),
+                          opt_f32(d_gp, T * H), opt_f32(d_c, T * H), ddt_raw.data_ptr(), dlam_raw.data_ptr(),
+                          dbias.data_ptr<float>(), dA.data_ptr<float>(), stream());
+  return {ddt_raw, dlam_raw, dbias, dA};
+}
+
 // ------------------------------------------------------------ multi-head latent attention
 namespace {
 void mla_check(const torch::Tensor& t, const char* what) {
@@ -1154,6 +1202,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather_sum", &moe_gather_sum, "sum permuted rows back per token");
   m.def("gemm_grouped", &gemm_grouped, "grouped (per-expert) tcgen05 GEMM");
   m.def("ep_pad_words", &ep_pad_words, "int32 words of one expert-parallel signal pad");
+  m.def("m3_coef_fwd", &m3_coef_fwd, "Mamba3 scan coefficients (dt, log alpha, gamma', c) in one pass");
+  m.def("m3_coef_bwd", &m3_coef_bwd, "backward of the Mamba3 scan coefficients");
   m.def("mla_pack_fwd", &mla_pack_fwd, "MLA: q, k (shared k_rope, RoPE applied) and packed v from the projections");
   m.def("mla_pack_bwd", &mla_pack_bwd, "MLA: gradients of q_c, kv and the rope block from dq, dk, dv");
   m.def("ep_counts", &ep_counts, "expert-parallel count all-gather over NVLink");

@@ -300,10 +300,11 @@ class Mamba3Mixer(RefModule):
             Cm = xbc[..., self.I + bc:]
         else:
             x = F.silu(x)
-        lam = torch.sigmoid(self.lambda_proj(h).float())
-        dtv = _softplus_dt(dt, self.dt_bias)
         fused = self._fused_ok(h, x, S)
         if fused:
+            # step size, lambda and the shifted-state coefficients in one kernel
+            from ..ops.ssd_tc import Mamba3Coef
+            dtv, loga, gp, cshift = Mamba3Coef.apply(dt, self.dt_bias, self.lambda_proj(h), self.A())
             # fused prologue (norm + bias + complex RoPE) straight into the tensor-core scan layout
             from ..ops.ssd_tc import Mamba3BC
             if self.complex_rope:
@@ -317,10 +318,12 @@ class Mamba3Mixer(RefModule):
             xh = x.reshape(B, S, self.Hs, self.P)
             if self.mimo_x_up is not None:
                 xh = self.mimo_x_up(xh)
-            from ..ops.ssd_tc import mamba3_tc_skip
+            from ..ops.ssd_tc import mamba3_tc_skip_coef
             # the shifted-state diagonal correction rides on the fused D skip
-            y = mamba3_tc_skip(xh, dtv, self.A(), bro, cro, lam, self.D, bcdot)
+            y = mamba3_tc_skip_coef(xh, dtv, loga, gp, cshift, bro, cro, self.D, bcdot)
             return self._finish(y, xh, gate, h, resid, B, S, skipped=True)
+        lam = torch.sigmoid(self.lambda_proj(h).float())
+        dtv = _softplus_dt(dt, self.dt_bias)
         Bm = Bm.reshape(B, S, self.g, self.N)
         Cm = Cm.reshape(B, S, self.g, self.N)
         rep = self.Hs // self.g

@@ -103,6 +103,45 @@ def mamba3_coeffs(dt, A, lam):
     return loga, lamf * dtf + c, c
 
 
+class Mamba3Coef(torch.autograd.Function):
+    """Per-(token, head) inputs of the shifted-state Mamba3 scan in one kernel each way
+    (csrc/m3_glue.cu): from the raw step-size projection ``dt_raw`` and the raw
+    lambda projection ``lam_raw`` (bf16 [B, S, H]), ``dt_bias`` [H] and A [H]:
+    dt = clamp(softplus(dt_raw + dt_bias), 1e-3, 0.1), log alpha = A dt,
+    gamma' = sigmoid(lam_raw) dt + c and c_t = (1 - lambda_{t+1}) dt_{t+1}, all f32."""
+
+    LO, HI = 1e-3, 0.1
+
+    @staticmethod
+    def forward(ctx, dt_raw, dt_bias, lam_raw, A):
+        Bsz, S, H = dt_raw.shape
+        dtc = dt_raw.to(torch.bfloat16).contiguous()
+        lmc = lam_raw.to(torch.bfloat16).contiguous()
+        bias = dt_bias.to(torch.bfloat16).contiguous()
+        Af = A.float().contiguous()
+        dt, loga, gp, c = ext().m3_coef_fwd(dtc, bias, lmc, Af, S, Mamba3Coef.LO, Mamba3Coef.HI)
+        ctx.save_for_backward(dtc, bias, lmc, Af)
+        ctx.S, ctx.dtypes = S, (dt_raw.dtype, dt_bias.dtype, lam_raw.dtype, A.dtype)
+        sh = (Bsz, S, H)
+        return dt.view(sh), loga.view(sh), gp.view(sh), c.view(sh)
+
+    @staticmethod
+    def backward(ctx, d_dt, d_loga, d_gp, d_c):
+        dtc, bias, lmc, Af = ctx.saved_tensors
+        f = lambda g: None if g is None else g.float().contiguous()
+        ddt, dlam, dbias, dA = ext().m3_coef_bwd(dtc, bias, lmc, Af, ctx.S, Mamba3Coef.LO, Mamba3Coef.HI, f(d_dt),
+                                                 f(d_loga), f(d_gp), f(d_c))
+        t_dt, t_bias, t_lam, t_A = ctx.dtypes
+        return ddt.view(dtc.shape).to(t_dt), dbias.to(t_bias), dlam.view(lmc.shape).to(t_lam), dA.to(t_A)
+
+
+def mamba3_tc_skip_coef(x, dtv, loga, gp, c, Bm, Cm, D, bcdot):
+    """Mamba3 scan + D skip from precomputed coefficients (``Mamba3Coef``):
+    y = y_K + (D - c <B, C>) x, bf16 [B, S, H, P]."""
+    dskip = D.float()[None, None, :] - c * bcdot
+    return SSDChunkTC.apply(x, Bm, Cm, loga, gp, dskip)
+
+
 def mamba3_tc_skip(x, dt, A, Bm, Cm, lam, D, bcdot):
     """Mamba3 scan + D skip through the shifted state, bf16 [B, S, H, P]:
     y = y_K + (D - c <B, C>) x.  Bm/Cm per head [B, S, H, N] bf16, bcdot = <B, C> [B, S, H]."""

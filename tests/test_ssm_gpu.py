@@ -279,3 +279,35 @@ def test_dskip_epilogue_kernels(P, per_row):
     assert _rel(dx.view(T, H, P), dx_scan.view(T, H, P) + dv * gf) < 1e-2
     assert _rel(dd, (gf * x.float().view(T, H, P)).sum(-1)) < 1e-5
     assert _rel(e, (gf * y.view(T, H, P)).sum(-1)) < 1e-5
+
+
+@pytest.mark.parametrize("B,S,H", [(2, 100, 8), (1, 256, 32), (3, 7, 5)])
+def test_mamba3_coefficients(B, S, H):
+    """Step size, lambda and the shifted-state coefficients (csrc/m3_glue.cu) against the fp32
+    torch statement: dt = clamp(softplus(dt_raw + dt_bias), 1e-3, 0.1), lam = sigmoid(l_raw),
+    log alpha = A dt, c_t = (1 - lam_{t+1}) dt_{t+1} (0 at the end), gamma' = lam dt + c."""
+    from oxidizr_b200.ops.ssd_tc import Mamba3Coef
+    torch.manual_seed(B * S + H)
+    # raw step sizes around the clamp edges so that both sides of each get exercised
+    dt_raw = (torch.randn(B, S, H, device="cuda") * 3 - 3).bfloat16().requires_grad_()
+    bias = (torch.randn(H, device="cuda") * 0.5).bfloat16().requires_grad_()
+    l_raw = torch.randn(B, S, H, device="cuda").bfloat16().requires_grad_()
+    A = (-torch.rand(H, device="cuda") * 2 - 0.1).requires_grad_()
+    outs = Mamba3Coef.apply(dt_raw, bias, l_raw, A)
+    gs = [torch.randn_like(o) for o in outs]
+    sum((o * g).sum() for o, g in zip(outs, gs)).backward()
+    dr, br, lr, Ar = (t.detach().float().requires_grad_() for t in (dt_raw, bias, l_raw, A))
+    dt = torch.nn.functional.softplus(dr + br).clamp(1e-3, 0.1)
+    lam = torch.sigmoid(lr)
+    loga = Ar[None, None, :] * dt
+    w = (1 - lam) * dt
+    c = torch.cat([w[:, 1:], torch.zeros_like(w[:, :1])], 1)
+    gp = lam * dt + c
+    ref = (dt, loga, gp, c)
+    sum((o * g).sum() for o, g in zip(ref, gs)).backward()
+    for o, r in zip(outs, ref):
+        assert _rel(o, r) < 1e-5
+    assert _rel(dt_raw.grad, dr.grad) < 1e-2
+    assert _rel(l_raw.grad, lr.grad) < 1e-2
+    assert _rel(bias.grad, br.grad) < 1e-2
+    assert _rel(A.grad, Ar.grad) < 1e-4
