@@ -9,7 +9,8 @@
 // Forward, per (token t, head h):
 //   dt = clamp(softplus(z), lo, hi), z = dt_raw + dt_bias;  lam = sigmoid(l_raw)
 //   loga = A dt;  c = w_{t+1}, w = (1 - lam) dt;  gamma' = lam dt + c
-// Backward (d_w_t = d_c_{t-1}):
+// Backward (d_w_t = d_c_{t-1} + d_gamma'_{t-1}, since c_{t-1} = w_t is both an output and
+// part of gamma'_{t-1}):
 //   d_lam = (d_gamma' - d_w) dt
 //   d_dt  = d_dt_in + d_loga A + d_gamma' lam + d_w (1 - lam)
 //   d_z   = d_dt sigmoid(z) where lo <= softplus(z) <= hi, else 0
@@ -89,7 +90,9 @@ __global__ void __launch_bounds__(M3C_THREADS) m3_coef_bwd_kernel(
     const int h = (int)(i - t * H);
     const Coef k = coef_at(dt_raw, bias, lam_raw, i, h, lo, hi);
     const float gdt = d_dt ? d_dt[i] : 0.f, gla = d_loga ? d_loga[i] : 0.f, ggp = d_gp ? d_gp[i] : 0.f;
-    const float gw = (d_c && (int)(t % S) > 0) ? d_c[i - H] : 0.f;
+    // w_t = (1 - lam_t) dt_t is c_{t-1}, which gamma'_{t-1} also contains
+    float gw = 0.f;
+    if ((int)(t % S) > 0) gw = (d_c ? d_c[i - H] : 0.f) + (d_gp ? d_gp[i - H] : 0.f);
     const float dlam = (ggp - gw) * k.dt;
     const float ddt = gdt + gla * A[h] + ggp * k.lam + gw * (1.f - k.lam);
     const float dz = (k.sp >= lo && k.sp <= hi) ? ddt * sigmoid_f(k.z) : 0.f;

@@ -118,9 +118,17 @@ def multicast_supported(device: torch.device) -> bool:
         return False
 
 
+class _NoStream:
+    """Stand-in for a CUDA stream on the CPU (everything is ordered there)."""
+
+    def wait_stream(self, other):
+        pass
+
+
 class ShardedDDPAdamW:
     """Bucket layout, sharded optimizer state and the overlap logic shared by
-    the NVLink transport (:class:`FusedDDPAdamW`) and the NCCL one."""
+    the NVLink transport (:class:`FusedDDPAdamW`) and the NCCL one (and, on the
+    CPU, a gloo transport used by the host-logic tests)."""
 
     collective_state = True  # state_tensors() gathers the shards: every rank calls it
 
@@ -199,7 +207,8 @@ class ShardedDDPAdamW:
         self._norm = torch.zeros(1, dtype=torch.float32, device=dev)
         self._done = torch.zeros(1, dtype=torch.int32, device=dev)
         self._push_done = torch.zeros(512, dtype=torch.int32, device=dev)
-        self.comm_stream = torch.cuda.Stream(device=dev)
+        self._cuda = dev.type == "cuda"
+        self.comm_stream = torch.cuda.Stream(device=dev) if self._cuda else _NoStream()
         self.epoch = 1
         self.step_count = 0
         self.accumulating = False
@@ -213,8 +222,20 @@ class ShardedDDPAdamW:
         for bi, b in enumerate(self.buckets):
             for i in b[3]:
                 self.params[i]._oxi_grad_ready = (lambda k=bi: self._on_ready(k))
-        torch.cuda.synchronize(dev)
+        self._sync()
         dist.barrier(group=group)
+
+    # ------------------------------------------------------------ streams (no-ops on the CPU)
+    def _cur(self):
+        return torch.cuda.current_stream(self.device) if self._cuda else _NoStream()
+
+    def _on_comm(self):
+        import contextlib
+        return torch.cuda.stream(self.comm_stream) if self._cuda else contextlib.nullcontext()
+
+    def _sync(self):
+        if self._cuda:
+            torch.cuda.synchronize(self.device)
 
     # ------------------------------------------------------------ transport hooks
     def _alloc_transport(self):
@@ -290,9 +311,9 @@ class ShardedDDPAdamW:
         # have finished with only once every bucket of it has landed here
         self.sync_params()
         self._launched[bi] = True
-        cur = torch.cuda.current_stream(self.device)
+        cur = self._cur()
         self.comm_stream.wait_stream(cur)
-        with torch.cuda.stream(self.comm_stream):
+        with self._on_comm():
             if not self._sumsq_zeroed:
                 self._sumsq.zero_()
                 self._sumsq_zeroed = True
@@ -306,7 +327,7 @@ class ShardedDDPAdamW:
                 p.grad = None
         for bi in range(len(self.buckets)):
             self._launch(bi)
-        cur = torch.cuda.current_stream(self.device)
+        cur = self._cur()
         cur.wait_stream(self.comm_stream)
         c = self.cfg
         self.step_count += 1
@@ -318,7 +339,7 @@ class ShardedDDPAdamW:
             self._coef.mul_(grad_scale)
         bc1, bc2 = 1.0 - c.beta1 ** t, 1.0 - c.beta2 ** t
         self.comm_stream.wait_stream(cur)
-        with torch.cuda.stream(self.comm_stream):
+        with self._on_comm():
             # the forward uses the last buckets first (reverse parameter order)
             for bi in reversed(range(len(self.buckets))):
                 self._ag(bi, c.lr, bc1, bc2)
@@ -350,7 +371,7 @@ class ShardedDDPAdamW:
     def state_tensors(self):
         """Full master / moments in flat layout (collective: every rank must call)."""
         self.sync_params()
-        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+        self._cur().wait_stream(self.comm_stream)
         return {"master": self._gather_full(self.master), "exp_avg": self._gather_full(self.m),
                 "exp_avg_sq": self._gather_full(self.v)}
 
@@ -366,7 +387,7 @@ class ShardedDDPAdamW:
 
     def load_state_tensors(self, d, step: int):
         self.sync_params()
-        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+        self._cur().wait_stream(self.comm_stream)
         with torch.no_grad():
             for key, dst in (("master", self.master), ("exp_avg", self.m), ("exp_avg_sq", self.v)):
                 full = d[key].to(self.device)
@@ -381,7 +402,7 @@ class ShardedDDPAdamW:
     def close(self):
         # every peer's writes into this rank's buffers must have landed before they are unmapped
         self.sync_params()
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=self.group)
 
 
