@@ -412,10 +412,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int m0 = un.tm * BM * CG + (int)rank * BM, n0 = un.tn * BN;
       void* Dp = p.D;
       if (p.group_mode == 2) Dp = (char*)p.D + un.e * p.d_group_stride * (EPI == EPI_F32 ? 4 : 2);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
-      tc_fence_after();
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
+      // SwiGLU backward reads the saved gate / up values of its row: the 16-byte
+      // vectors of the next 32-column chunk are loaded one chunk ahead (the first
+      // before the accumulator wait), so their latency hides behind the TMEM loads
+      // and the math of the current chunk instead of stalling every chunk.
+      uint4 pre_g[4], pre_u[4];
+      auto swb_full = [&](int cc) { return row_ok && vec && n0 + cc * 32 + 32 <= p.N; };
+      auto swb_fetch = [&](int cc) {
+        const int col = n0 + cc * 32;
+        const uint4* gq = reinterpret_cast<const uint4*>(p.R + (int64_t)row * p.ldr + (col / 128) * 256 + col % 128);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          pre_g[q] = gq[q];
+          pre_u[q] = gq[q + 16];  // the up block sits 128 columns after the gate block
+        }
+      };
+      if constexpr (EPI == EPI_SWIGLU_BWD) {
+        if (swb_full(0)) swb_fetch(0);
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
+      tc_fence_after();
       const uint32_t tbase = tmem_base + lane_base + acc * BN;
 
       if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_SWIGLU_BWD) {
@@ -423,6 +441,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
+          uint4 cur_g[4], cur_u[4];
+          if constexpr (EPI == EPI_SWIGLU_BWD) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              cur_g[q] = pre_g[q];
+              cur_u[q] = pre_u[q];
+            }
+            if (c + 1 < BN / 32 && swb_full(c + 1)) swb_fetch(c + 1);
+          }
           tc_wait_ld();
           if (c == BN / 32 - 1) { tc_fence_before(); release_acc(acc); }
           const int col = n0 + c * 32;
@@ -487,8 +514,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const __nv_bfloat16* gp = p.R + (int64_t)row * p.ldr + blk * 256 + off;
             const __nv_bfloat16* up = gp + 128;
             float g[32], u[32];
-            load_bf16_row(gp, g, nvalid, vec);
-            load_bf16_row(up, u, nvalid, vec);
+            if (swb_full(c)) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint32_t gw[4] = {cur_g[q].x, cur_g[q].y, cur_g[q].z, cur_g[q].w};
+                const uint32_t uw[4] = {cur_u[q].x, cur_u[q].y, cur_u[q].z, cur_u[q].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const float2 a = unpack_bf16(gw[k]), b = unpack_bf16(uw[k]);
+                  g[q * 8 + 2 * k] = a.x;
+                  g[q * 8 + 2 * k + 1] = a.y;
+                  u[q * 8 + 2 * k] = b.x;
+                  u[q * 8 + 2 * k + 1] = b.y;
+                }
+              }
+            } else {
+              load_bf16_row(gp, g, nvalid, vec);
+              load_bf16_row(up, u, nvalid, vec);
+            }
             float dg[32], du[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
