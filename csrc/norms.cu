@@ -32,15 +32,6 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ void unpack8(uint4 u, float* f) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
 __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float* f) {
   uint4 u = *reinterpret_cast<const uint4*>(p);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -266,29 +257,15 @@ __global__ void __launch_bounds__(512) norm_bwd_row_kernel(
     pdb[j] = 0.f;
   }
   const float inv_h = 1.f / (float)H;
-  // the next row's operands are loaded (raw 16-byte vectors) before this row's
-  // reductions, so each thread keeps two rows of loads in flight
-  uint4 nx = make_uint4(0u, 0u, 0u, 0u), nd = nx, ng = nx, nr = nx;
-  float nrstd = 0.f, nmean = 0.f;
-  auto fetch = [&](int64_t r) {
-    nx = *reinterpret_cast<const uint4*>(x + r * H + c0);
-    nd = *reinterpret_cast<const uint4*>(dy + r * H + c0);
-    if (MODE == 2) ng = *reinterpret_cast<const uint4*>(gate + r * H + c0);
-    if (dres) nr = *reinterpret_cast<const uint4*>(dres + r * H + c0);
-    nrstd = stat_rstd[r];
-    if (MODE == 1) nmean = stat_mean[r];
-  };
-  if ((int64_t)blockIdx.x < rows) fetch(blockIdx.x);
   int it = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
-    const float rstd = nrstd;
-    const float mean = MODE == 1 ? nmean : 0.f;
+    const float rstd = stat_rstd[row];
+    const float mean = MODE == 1 ? stat_mean[row] : 0.f;
     float xv[8], dv[8], g[8], xh[8], rv[8];
-    unpack8(nx, xv);
-    unpack8(nd, dv);
-    if (MODE == 2) unpack8(ng, g);
-    if (dres) unpack8(nr, rv);
-    if (row + gridDim.x < rows) fetch(row + gridDim.x);
+    ld8(x + row * H + c0, xv);
+    ld8(dy + row * H + c0, dv);
+    if (MODE == 2) ld8(gate + row * H + c0, g);
+    if (dres) ld8(dres + row * H + c0, rv);
     float a1 = 0.f, a2 = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
