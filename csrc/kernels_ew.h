@@ -39,4 +39,7 @@ void launch_adamw(float* p, void* p16, const float* g, float* m, float* v, int64
                   float eps, float wd, float bc1, float bc2, const float* gscale, cudaStream_t st,
                   const float* bc_dev = nullptr);
 
+// SwiGLU backward from dH [rows, I] and the saved GU [rows, 2I] (gate / up interleaved in
+// 128-column blocks) into dGU [rows, 2I] (same layout); all contiguous bf16.
+void launch_swiglu_bwd(const void* dh, const void* gu, void* dgu, int64_t rows, int I, cudaStream_t st);
 }  // namespace oxi

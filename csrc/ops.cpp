@@ -98,6 +98,16 @@ void gemm_swiglu_bwd(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, t
                               status_ptr(status), stream());
 }
 
+void swiglu_bwd(torch::Tensor dh, torch::Tensor gu, torch::Tensor dgu) {
+  c10::cuda::CUDAGuard g(dh.device());
+  TORCH_CHECK(dh.scalar_type() == torch::kBFloat16 && gu.scalar_type() == torch::kBFloat16 &&
+                  dgu.scalar_type() == torch::kBFloat16 && dh.is_contiguous() && gu.is_contiguous() &&
+                  dgu.is_contiguous() && dh.dim() == 2 && gu.sizes() == dgu.sizes() && gu.size(0) == dh.size(0) &&
+                  gu.size(1) == 2 * dh.size(1),
+              "swiglu_bwd: contiguous bf16 dH [rows, I], GU / dGU [rows, 2I]");
+  oxi::launch_swiglu_bwd(dh.data_ptr(), gu.data_ptr(), dgu.data_ptr(), dh.size(0), (int)dh.size(1), stream());
+}
+
 void gemm_ce(torch::Tensor x, torch::Tensor w, torch::Tensor targets, torch::Tensor part_max,
              torch::Tensor part_sum, torch::Tensor tgt_logit, c10::optional<torch::Tensor> logits, double alpha,
              torch::Tensor status) {
@@ -1155,6 +1165,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_fwd", &norm_fwd, "RMSNorm / LayerNorm / gated RMSNorm forward");
   m.def("norm_bwd", &norm_bwd, "RMSNorm / LayerNorm / gated RMSNorm backward");
   m.def("ce_finish", &ce_finish, "combine CE partials into lse and per-row loss");
+  m.def("swiglu_bwd", &swiglu_bwd, "SwiGLU backward, element-wise: dH and the saved gate / up -> dGU");
   m.def("ce_bwd", &ce_bwd, "in-place softmax-minus-onehot gradient of the logits (of a column chunk from col0)",
         py::arg("logits"), py::arg("V"), py::arg("lse"), py::arg("targets"), py::arg("gscale"), py::arg("inv_count"),
         py::arg("col0") = 0);

@@ -436,4 +436,50 @@ void launch_adamw(float* p, void* p16, const float* g, float* m, float* v, int64
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
+// ------------------------------------------------------------ SwiGLU backward (element-wise)
+// From dH [rows, I] (the down projection's input gradient) and the saved
+// pre-activations GU [rows, 2I] (gate / up interleaved in blocks of 128 columns):
+//   dG = dH * u * s * (1 + g (1 - s)),  dU = dH * g * s,  s = sigmoid(g)
+// written to dGU in GU's layout.  8 columns (16 bytes) per thread.
+namespace {
+__global__ void __launch_bounds__(256) swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh,
+                                                         const __nv_bfloat16* __restrict__ gu,
+                                                         __nv_bfloat16* __restrict__ dgu, int64_t rows, int I) {
+  const int vpr = I / 8;  // 8-column vectors per row of dH
+  const int64_t n = rows * vpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vpr;
+    const int c = (int)(i - r * vpr) * 8;
+    const int64_t gcol = (int64_t)(c / 128) * 256 + c % 128;
+    const uint4 hv = *reinterpret_cast<const uint4*>(dh + r * I + c);
+    const uint4 gv = *reinterpret_cast<const uint4*>(gu + r * 2 * I + gcol);
+    const uint4 uv = *reinterpret_cast<const uint4*>(gu + r * 2 * I + gcol + 128);
+    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t dg[4], du[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 h = unpack_bf16(hw[k]), g = unpack_bf16(gw[k]), u = unpack_bf16(uw[k]);
+      const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+      dg[k] = pack_bf16(h.x * u.x * s0 * (1.f + g.x * (1.f - s0)), h.y * u.y * s1 * (1.f + g.y * (1.f - s1)));
+      du[k] = pack_bf16(h.x * g.x * s0, h.y * g.y * s1);
+    }
+    *reinterpret_cast<uint4*>(dgu + r * 2 * I + gcol) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+    *reinterpret_cast<uint4*>(dgu + r * 2 * I + gcol + 128) = make_uint4(du[0], du[1], du[2], du[3]);
+  }
+}
+}  // namespace
+
+void launch_swiglu_bwd(const void* dh, const void* gu, void* dgu, int64_t rows, int I, cudaStream_t st) {
+  OXI_CHECK(I % 128 == 0, "SwiGLU backward: intermediate size must be a multiple of 128");
+  OXI_CHECK(((reinterpret_cast<uintptr_t>(dh) | reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(dgu)) &
+             15) == 0, "SwiGLU backward: 16-byte aligned buffers");
+  if (!rows) return;
+  const int64_t n = rows * (I / 8);
+  const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 16);
+  swiglu_bwd_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(dh),
+                                          reinterpret_cast<const __nv_bfloat16*>(gu),
+                                          reinterpret_cast<__nv_bfloat16*>(dgu), rows, I);
+  OXI_CUDA_CHECK(cudaGetLastError());
+}
+
 }  // namespace oxi

@@ -23,6 +23,15 @@ from ._C import ext, status
 from .gemm import mm
 
 
+# SwiGLU backward: the down projection's dX GEMM with a plain epilogue followed by
+# one element-wise kernel (split, default), or with the SwiGLU-backward epilogue
+# fused into the GEMM (OXI_SWIGLU_BWD=fused).  The fused epilogue has to load the
+# saved gate / up rows and evaluate the sigmoid per element while the MMAs of the
+# next tile wait on its accumulator; at the Llama shape it ran at about 490
+# TFLOP/s, against about 1.2 PFLOP/s for the plain GEMM plus a memory-bound pass.
+SWIGLU_BWD_SPLIT = os.environ.get("OXI_SWIGLU_BWD", "split") != "fused"
+
+
 def _ready(p):
     cb = getattr(p, "_oxi_grad_ready", None)
     if cb is not None:
@@ -206,7 +215,12 @@ class SwiGLUMLP(torch.autograd.Function):
         dy2 = _c(dy.reshape(-1, w_down.shape[0]))
         g_down = _wgrad_gemm(w_down, dy2, h)
         dgu = torch.empty_like(gu)
-        ext().gemm_swiglu_bwd(dy2, w_down, gu, dgu, status(dy.device))
+        if SWIGLU_BWD_SPLIT:
+            # dH with the plain epilogue, then one element-wise pass for dG / dU
+            dh = mm(dy2, w_down, b_t=True)
+            ext().swiglu_bwd(dh, gu, dgu)
+        else:
+            ext().gemm_swiglu_bwd(dy2, w_down, gu, dgu, status(dy.device))
         g_gu = _wgrad_gemm(w_gu, dgu, x2)
         dx = mm(dgu, w_gu, b_t=True).view(*dy.shape[:-1], w_gu.shape[1])
         return dx, g_gu, g_down, (dy if ctx.has_resid else None)

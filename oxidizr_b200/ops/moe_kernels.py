@@ -24,6 +24,20 @@ def rows_capacity(T: int, k: int, E: int) -> int:
     return ((T * k + E * 256) + 255) // 256 * 256
 
 
+def swiglu_bwd_grouped(dy, w_down, gu, dgu, E, seg, st):
+    """dGU of every expert's SwiGLU from the down projection's output gradient: the
+    grouped dX GEMM with a plain epilogue, then the element-wise SwiGLU backward
+    (or the fused epilogue with OXI_SWIGLU_BWD=fused, see ops/fused.py)."""
+    from .fused import SWIGLU_BWD_SPLIT
+    _, H, I = w_down.shape
+    if SWIGLU_BWD_SPLIT:
+        dh = torch.empty(dy.shape[0], I, dtype=dy.dtype, device=dy.device)
+        ext().gemm_grouped(1, 0, dy, False, w_down.view(E * H, I), True, E, seg, H, dh, None, None, st)
+        ext().swiglu_bwd(dh, gu, dgu)
+    else:
+        ext().gemm_grouped(1, 3, dy, False, w_down.view(E * H, I), True, E, seg, H, dgu, None, gu, st)
+
+
 def _wgrad_grouped(p, a, b, seg, E):
     """dW[e] = a[seg_e]^T b[seg_e] accumulated into p.main_grad (or returned)."""
     mg = getattr(p, "main_grad", None)
@@ -76,7 +90,7 @@ class GroupedExperts(torch.autograd.Function):
         ext().moe_zero_pad(seg, counts, dyp)
         g_down = _wgrad_grouped(w_down, dyp, h, seg, E)
         dgu = torch.empty_like(gu)
-        ext().gemm_grouped(1, 3, dyp, False, w_down.view(E * H, I), True, E, seg, H, dgu, None, gu, st)
+        swiglu_bwd_grouped(dyp, w_down, gu, dgu, E, seg, st)
         g_gu = _wgrad_grouped(w_gu, dgu, xp, seg, E)
         dxp = torch.empty_like(xp)
         ext().gemm_grouped(1, 0, dgu, False, w_gu.view(E * I2, H), True, E, seg, I2, dxp, None, None, st)

@@ -304,7 +304,7 @@ class EPExperts(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         from ..ops._C import ext, status
-        from ..ops.moe_kernels import _wgrad_grouped
+        from ..ops.moe_kernels import _wgrad_grouped, swiglu_bwd_grouped
         e = ext()
         topi, tw, pos, h, gu, seg, rc = ctx.saved_tensors
         moe = ctx.moe
@@ -328,7 +328,7 @@ class EPExperts(torch.autograd.Function):
         e.ep_scale_rows(dyr, buf.local("metaw", torch.float32), seg, rc, El)
         g_down = _wgrad_grouped(w_down, dyr, h, seg, El)
         dgu = torch.empty_like(gu)
-        e.gemm_grouped(1, 3, dyr, False, w_down.view(El * H, I), True, El, seg, H, dgu, None, gu, st)
+        swiglu_bwd_grouped(dyr, w_down, gu, dgu, El, seg, st)
         g_gu = _wgrad_grouped(w_gu, dgu, xr, seg, El)
         # input-gradient rows straight into the sources' yret (their forward rows were
         # consumed by their push_dy, which finished before DYPUSHED)

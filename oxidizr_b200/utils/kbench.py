@@ -201,7 +201,7 @@ def bench_moe_gemms(T=16384, H=2048, E=64, k=8, I=1024, iters=10):
     OXI_GEMM_CG=1 to time single-CTA tiles instead of CTA pairs)."""
     import os
     from ..ops._C import ext, status
-    from ..ops.moe_kernels import rows_capacity
+    from ..ops.moe_kernels import rows_capacity, swiglu_bwd_grouped
     peaks = measured_peaks()
     torch.manual_seed(0)
     x = (torch.randn(T, H, device="cuda") * 0.5).bfloat16()
@@ -226,8 +226,7 @@ def bench_moe_gemms(T=16384, H=2048, E=64, k=8, I=1024, iters=10):
                                                       h, gu, None, st), 2.0 * rows * 2 * I * H),
         "down": (lambda: ext().gemm_grouped(1, 0, h, False, wd.view(E * H, I), False, E, seg, H, yp, None, None, st),
                  2.0 * rows * H * I),
-        "down_dx_swiglu_bwd": (lambda: ext().gemm_grouped(1, 3, dyp, False, wd.view(E * H, I), True, E, seg, H, dgu,
-                                                          None, gu, st), 2.0 * rows * H * I),
+        "down_dx_swiglu_bwd": (lambda: swiglu_bwd_grouped(dyp, wd, gu, dgu, E, seg, st), 2.0 * rows * H * I),
         "down_wgrad": (lambda: ext().gemm_grouped(2, 1, dyp, True, h, True, E, seg, 0, g_d, None, None, st),
                        2.0 * rows * H * I),
         "gate_up_dx": (lambda: ext().gemm_grouped(1, 0, dgu, False, wgu.view(E * 2 * I, H), True, E, seg, 2 * I, dxp,

@@ -112,6 +112,11 @@ def test_gemm_swiglu_fwd_bwd():
     du = dh * gg * s
     ref2 = torch.stack([dg.view(M, I // 128, 128), du.view(M, I // 128, 128)], 2).reshape(M, 2 * I)
     assert _rel(dgu, ref2) < 2e-2
+    # the split form: plain dX GEMM, then the element-wise SwiGLU backward
+    from oxidizr_b200.ops.gemm import mm
+    dgu2 = torch.empty_like(gu)
+    ext().swiglu_bwd(mm(dy, wd, b_t=True), gu, dgu2)
+    assert _rel(dgu2, ref2) < 2e-2
 
 
 def test_gemm_ce_partials():
