@@ -100,8 +100,11 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_qt = (p.S + FA_BM - 1) / FA_BM;
-  const int qt = n_qt - 1 - blockIdx.x;  // longest (causal) tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // the query tile is the slowest grid index and runs backwards, so every head's
+  // longest (causal) tiles are issued before any shorter one: longest-first
+  // scheduling across the whole grid, not just within one head
+  const int qt = n_qt - 1 - blockIdx.z;
+  const int h = blockIdx.x, b = blockIdx.y;
   const int hk = h / (p.Hq / p.Hk);
   const int q0 = qt * FA_BM;
   const int row0 = b * p.S;
@@ -381,7 +384,7 @@ void launch_fa_fwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
     OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     attr = true;
   }
-  dim3 grid((S + FA_BM - 1) / FA_BM, Hq, B);
+  dim3 grid(Hq, B, (S + FA_BM - 1) / FA_BM);
   kern<<<grid, FA_THREADS, L::TOTAL, st>>>(tq, tk, tv, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
@@ -472,7 +475,9 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int jt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  // the key tile is the slowest grid index: under causal masking key tile 0 has the
+  // most query tiles, so every head's longest tiles are issued first
+  const int jt = blockIdx.z, hk = blockIdx.x, b = blockIdx.y;
   const int group = p.Hq / p.Hk;
   const int n_qt = (p.S + 127) / 128;
   const int i_start = p.causal ? jt : 0;
@@ -797,7 +802,7 @@ void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
     OXI_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
     attr = true;
   }
-  dim3 grid((S + 127) / 128, Hk, B);
+  dim3 grid(Hk, B, (S + 127) / 128);
   kern<<<grid, FA_BWD_THREADS, L::TOTAL, st>>>(tq, tk, tv, tdo, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
