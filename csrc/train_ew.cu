@@ -11,6 +11,7 @@
 
 #include "host_util.h"
 #include "kernels_ew.h"
+#include "ptx.cuh"
 
 namespace oxi {
 
