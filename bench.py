@@ -316,6 +316,10 @@ def main():
         "mfu_vs_measured_sustained": round(achieved_tf / pk["bf16_tflops_sustained"], 3),
         "loss_after_timed_steps": round(loss_dev, 4),
     }
+    if m.mamba_layers:
+        # the tensor-core scan runs 128-step chunks whatever the config asks: chunking is exact
+        # (outside compat mode), so the config's chunk size changes no result, only the tiling
+        out["config"]["ssd_chunk"] = {"config": m.mamba2_chunk_size, "kernel": 128}
     if ep > 1:
         from oxidizr_b200.parallel.ep import EPLayerBuffers
         out["ep_buffer_reallocs"] = EPLayerBuffers.reallocs
