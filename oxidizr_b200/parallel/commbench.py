@@ -84,8 +84,11 @@ def main(argv=None):
     ap.add_argument("--modes", default="auto",
                     help="comma list of fused transports to time: pull, push, nvls (auto: pull, plus nvls "
                          "when the GPUs support multicast)")
-    ap.add_argument("--rs-ctas", default="64", help="comma list: CTA budgets of the reduce-scatter kernels")
-    ap.add_argument("--ag-ctas", default="64", help="comma list: CTA budgets of the AdamW + all-gather kernels")
+    ap.add_argument("--rs-ctas", default="256",
+                    help="comma list: CTA budgets of the reduce-scatter kernels (first: the training default)")
+    ap.add_argument("--ag-ctas", default="148,296",
+                    help="comma list: CTA budgets of the AdamW + all-gather kernels (first: the training "
+                         "default, which leaves SMs to the forward it overlaps)")
     ap.add_argument("--no-nccl-ar", action="store_true")
     args = ap.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", "0"))
