@@ -412,6 +412,8 @@ struct FaBwdParams {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   int64_t ld_dk, ld_dv;
+  const float* rope_cos;  // [S, DQ/2] or null: dk is the gradient of the unrotated k
+  const float* rope_sin;
   int* status;
 };
 
@@ -682,8 +684,44 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     if (ok && n_it > 0) {
       tc_fence_after();
       const bool valid = kpos < p.S;
+      // with RoPE, dK leaves through the inverse rotation: column j and j + DQ/2 form a pair,
+      // so half h takes the 32-column chunks h and h + DQ/64 together
+      const int n_which = (DQ == DV && p.rope_cos != nullptr) ? 1 : 2;
+      if (n_which == 1) {
+        constexpr int HC = DQ / 64;  // 32-column chunks in half a head
+        __nv_bfloat16* dst = p.dk + (int64_t)(row0 + kpos) * p.ld_dk + hk * DQ;
+        const float* cs = p.rope_cos + (int64_t)kpos * (DQ / 2);
+        const float* sn = p.rope_sin + (int64_t)kpos * (DQ / 2);
 #pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
+        for (int c = half; c < HC; c += 2) {
+          uint32_t o1[32], o2[32];
+          tmem_ld32(TM_DK + lane_base + c * 32, o1);
+          tmem_ld32(TM_DK + lane_base + (c + HC) * 32, o2);
+          tc_wait_ld();
+          if (valid) {
+            uint4* d1 = reinterpret_cast<uint4*>(dst + c * 32);
+            uint4* d2 = reinterpret_cast<uint4*>(dst + (c + HC) * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float a[8], bb[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int j = c * 32 + q * 8 + e;
+                const float cj = __ldg(cs + j), sj = __ldg(sn + j);
+                const float x1 = __uint_as_float(o1[q * 8 + e]), x2 = __uint_as_float(o2[q * 8 + e]);
+                a[e] = x1 * cj + x2 * sj;
+                bb[e] = x2 * cj - x1 * sj;
+              }
+              d1[q] = make_uint4(pack_bf16(a[0], a[1]), pack_bf16(a[2], a[3]), pack_bf16(a[4], a[5]),
+                                 pack_bf16(a[6], a[7]));
+              d2[q] = make_uint4(pack_bf16(bb[0], bb[1]), pack_bf16(bb[2], bb[3]), pack_bf16(bb[4], bb[5]),
+                                 pack_bf16(bb[6], bb[7]));
+            }
+          }
+        }
+      }
+#pragma unroll 1
+      for (int which = 0; which < n_which; ++which) {
         __nv_bfloat16* dst = which == 0 ? p.dv + (int64_t)(row0 + kpos) * p.ld_dv + hk * DV
                                         : p.dk + (int64_t)(row0 + kpos) * p.ld_dk + hk * DQ;
         const uint32_t src = (which == 0 ? TM_DV : TM_DK) + lane_base;
@@ -757,6 +795,45 @@ __global__ void fa_bwd_prep_kernel(const __nv_bfloat16* __restrict__ o, int64_t 
   }
 }
 
+// dq (bf16, row stride lddq) = the inverse rotate-half RoPE of dq_acc (f32): one
+// thread per 8 rotation pairs (columns j..j+7 and j+hd/2..j+hd/2+7 of a head),
+// position = row % S.
+__global__ void fa_dq_convert_rope_kernel(const float* __restrict__ acc, int64_t ldacc,
+                                          __nv_bfloat16* __restrict__ dq, int64_t lddq, int64_t rows, int cols,
+                                          int hd, int S, const float* __restrict__ cs, const float* __restrict__ sn) {
+  const int half = hd / 2;
+  const int per_row = cols / 16;  // (heads) x (half / 8) items
+  const int64_t nv = rows * per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row;
+    const int it = (int)(i % per_row);
+    const int head = it / (half / 8), j = (it % (half / 8)) * 8;
+    const int pos = (int)(r % S);
+    const float* a = acc + r * ldacc + head * hd + j;
+    const float4 a0 = *reinterpret_cast<const float4*>(a), a1 = *reinterpret_cast<const float4*>(a + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(a + half), b1 = *reinterpret_cast<const float4*>(a + half + 4);
+    const float4 c0 = *reinterpret_cast<const float4*>(cs + (int64_t)pos * half + j);
+    const float4 c1 = *reinterpret_cast<const float4*>(cs + (int64_t)pos * half + j + 4);
+    const float4 s0 = *reinterpret_cast<const float4*>(sn + (int64_t)pos * half + j);
+    const float4 s1 = *reinterpret_cast<const float4*>(sn + (int64_t)pos * half + j + 4);
+    const float x1[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float x2[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float y1[8], y2[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      y1[e] = x1[e] * cc[e] + x2[e] * ss[e];
+      y2[e] = x2[e] * cc[e] - x1[e] * ss[e];
+    }
+    __nv_bfloat16* d = dq + r * lddq + head * hd + j;
+    *reinterpret_cast<uint4*>(d) =
+        make_uint4(pack_bf16(y1[0], y1[1]), pack_bf16(y1[2], y1[3]), pack_bf16(y1[4], y1[5]), pack_bf16(y1[6], y1[7]));
+    *reinterpret_cast<uint4*>(d + half) =
+        make_uint4(pack_bf16(y2[0], y2[1]), pack_bf16(y2[2], y2[3]), pack_bf16(y2[4], y2[5]), pack_bf16(y2[6], y2[7]));
+  }
+}
+
 // dq (bf16, row stride lddq) = dq_acc (f32)
 __global__ void fa_dq_convert_kernel(const float* __restrict__ acc, int64_t ldacc, __nv_bfloat16* __restrict__ dq,
                                      int64_t lddq, int64_t rows, int cols) {
@@ -775,7 +852,8 @@ template <int DQ, int DV>
 void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                      const void* dout, int64_t lddo, const float* lse, const float* delta, float* dq_acc,
                      int64_t ld_dq, void* dk, int64_t ld_dk, void* dv, int64_t ld_dv, int B, int S, int Hq, int Hk,
-                     float scale, bool causal, int* status, cudaStream_t st) {
+                     float scale, bool causal, int* status, cudaStream_t st, const float* rope_cos,
+                     const float* rope_sin) {
   using L = FaBwdSmem<DQ, DV>;
   const int64_t T = (int64_t)B * S;
   CUtensorMap tq = make_tmap_bf16(q, T, (int64_t)Hq * DQ, ldq, 64, 128);
@@ -795,6 +873,8 @@ void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
   p.ld_dk = ld_dk;
   p.ld_dv = ld_dv;
+  p.rope_cos = rope_cos;
+  p.rope_sin = rope_sin;
   p.status = status;
   auto kern = fa_bwd_kernel<DQ, DV>;
   static bool attr = false;
@@ -839,8 +919,14 @@ void launch_fa_fwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const
 void launch_fa_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                    const void* o, int64_t ldo, const void* dout, int64_t lddo, const float* lse, float* delta,
                    float* dq_acc, void* dq, int64_t lddq, void* dk, int64_t ld_dk, void* dv, int64_t ld_dv, int B,
-                   int S, int Hq, int Hk, int Dqk, int Dv, float scale, bool causal, int* status, cudaStream_t st) {
+                   int S, int Hq, int Hk, int Dqk, int Dv, float scale, bool causal, int* status, cudaStream_t st,
+                   const float* rope_cos, const float* rope_sin) {
   OXI_CHECK(Hq % Hk == 0, "query heads must be a multiple of kv heads");
+  const bool rope = rope_cos != nullptr;
+  OXI_CHECK(!rope || (rope_sin != nullptr && Dqk == Dv && (Dqk == 64 || Dqk == 128) &&
+                      (reinterpret_cast<uintptr_t>(rope_cos) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(rope_sin) & 15) == 0),
+            "flash backward with RoPE: head dims 64 / 128 (qk == v), 16-byte aligned cos / sin tables");
   OXI_CHECK(ld_dk % 8 == 0 && ld_dv % 8 == 0 && lddq % 8 == 0, "gradient rows must be 16-byte aligned");
   OXI_CHECK(fa_bwd_supported(Dqk, Dv), "flash attention backward has no kernel for head dims (qk ", Dqk, ", v ", Dv,
             ")");
@@ -857,12 +943,20 @@ void launch_fa_bwd(const void* q, int64_t ldq, const void* k, int64_t ldk, const
 #define OXI_FA_BWD(DQ_, DV_)                                                                                       \
   if (Dqk == DQ_ && Dv == DV_)                                                                                    \
     launch_fa_bwd_t<DQ_, DV_>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq_acc, (int64_t)Hq * Dqk, dk, ld_dk, \
-                              dv, ld_dv, B, S, Hq, Hk, scale, causal, status, st);
+                              dv, ld_dv, B, S, Hq, Hk, scale, causal, status, st, rope_cos, rope_sin);
   OXI_FA_BWD(64, 64)
   OXI_FA_BWD(128, 128)
   OXI_FA_BWD(96, 64)
   OXI_FA_BWD(128, 64)
 #undef OXI_FA_BWD
+  if (rope) {
+    const int64_t nr = T * (Hq * Dqk / 16);
+    fa_dq_convert_rope_kernel<<<(unsigned)std::min<int64_t>((nr + 255) / 256, 148 * 16), 256, 0, st>>>(
+        dq_acc, (int64_t)Hq * Dqk, reinterpret_cast<__nv_bfloat16*>(dq), lddq, T, Hq * Dqk, Dqk, S, rope_cos,
+        rope_sin);
+    OXI_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int64_t nv = T * (Hq * Dqk / 8);
   fa_dq_convert_kernel<<<(unsigned)std::min<int64_t>((nv + 255) / 256, 148 * 16), 256, 0, st>>>(
       dq_acc, (int64_t)Hq * Dqk, reinterpret_cast<__nv_bfloat16*>(dq), lddq, T, Hq * Dqk);

@@ -318,7 +318,8 @@ void flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
 void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
                torch::Tensor lse, torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dq, torch::Tensor dk,
                torch::Tensor dv, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t Dqk, int64_t Dv, double scale,
-               bool causal, torch::Tensor status) {
+               bool causal, torch::Tensor status, std::optional<torch::Tensor> rope_cos,
+               std::optional<torch::Tensor> rope_sin) {
   c10::cuda::CUDAGuard g(q.device());
   for (auto* t : {&q, &k, &v, &o, &dout, &dq, &dk, &dv})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 &&
@@ -327,11 +328,21 @@ void flash_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor 
   TORCH_CHECK(dq_acc.scalar_type() == torch::kFloat32 && dq_acc.is_contiguous() && dq_acc.numel() == B * S * Hq * Dqk,
               "dq_acc must be contiguous f32 [B*S, Hq*Dqk]");
   TORCH_CHECK(delta.scalar_type() == torch::kFloat32 && delta.numel() == B * Hq * S, "delta");
+  const float* rc = nullptr;
+  const float* rs = nullptr;
+  if (rope_cos.has_value() && rope_cos->defined()) {
+    TORCH_CHECK(rope_sin.has_value() && rope_sin->defined(), "rope_cos without rope_sin");
+    for (auto* t : {&*rope_cos, &*rope_sin})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat32 && t->is_contiguous() &&
+                      t->numel() >= S * (Dqk / 2), "RoPE tables must be contiguous f32 [>= S, Dqk/2]");
+    rc = rope_cos->data_ptr<float>();
+    rs = rope_sin->data_ptr<float>();
+  }
   oxi::launch_fa_bwd(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0), o.data_ptr(),
                      o.stride(0), dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(),
                      dq_acc.data_ptr<float>(), dq.data_ptr(), dq.stride(0), dk.data_ptr(), dk.stride(0), dv.data_ptr(),
                      dv.stride(0), (int)B, (int)S, (int)Hq, (int)Hk, (int)Dqk, (int)Dv, (float)scale, causal,
-                     status_ptr(status), stream());
+                     status_ptr(status), stream(), rc, rs);
 }
 
 bool flash_supported(int64_t Dqk, int64_t Dv, bool backward) {

@@ -40,9 +40,7 @@ class GQAAttention(RefModule):
     def forward(self, h: torch.Tensor, resid: torch.Tensor) -> torch.Tensor:
         B, S, _ = h.shape
         cos, sin = RopeCache.get(self.hd, S, self.theta, h.device)
-        qc, kc = self.nh * self.hd, self.kvh * self.hd
-        qkv = api.qkv_rope(h, self.w_qkv, cos, sin, self.hd, qc, kc)
-        o = api.attention_qkv(qkv, self.nh, self.kvh, self.hd, self.scale, causal=True)
+        o = api.attention_rope(h, self.w_qkv, cos, sin, self.nh, self.kvh, self.hd, self.scale)
         return api.linear(o, self.o_proj, resid=resid)
 
     def export_ref(self, prefix, out):

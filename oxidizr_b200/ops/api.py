@@ -107,6 +107,18 @@ def qkv_rope(x, w_qkv, cos, sin, hd: int, q_cols: int, k_cols: int):
     return torch.cat([q, k, y[..., q_cols + k_cols:]], -1)
 
 
+def attention_rope(x, w_qkv, cos, sin, nh: int, kvh: int, hd: int, scale: float):
+    """Causal GQA attention from the block input: qkv_rope + attention_qkv in one autograd
+    node whose backward un-rotates dq / dk inside the flash backward."""
+    from .attention import native_ok
+    S = x.shape[1]
+    if _native(x) and hd in (64, 128) and native_ok(hd) and cos.shape[0] >= S and x.shape[-1] % 8 == 0:
+        from .fused import AttentionQKVRope
+        return AttentionQKVRope.apply(x, w_qkv, cos, sin, nh, kvh, hd, scale)
+    qkv = qkv_rope(x, w_qkv, cos, sin, hd, nh * hd, kvh * hd)
+    return attention_qkv(qkv, nh, kvh, hd, scale, causal=True)
+
+
 def mla_qkv(qc, kv, rp, cos, sin, nh: int, hd: int, dr: int):
     """MLA attention operands (model.rs:196-256): q = [q_c, rope(q_rope)], k = [k_c, rope(k_rope)]
     with the one k_rope of a token shared by every head, and v, from q_c [B, S, nh*hd],

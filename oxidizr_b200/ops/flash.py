@@ -23,12 +23,15 @@ def _fwd(q2, k2, v2, B, S, Hq, Hk, D, scale, causal, Dv=None):
     return o, lse
 
 
-def _bwd(q2, k2, v2, o, lse, do2, dq, dk, dv, B, S, Hq, Hk, D, scale, causal, Dv=None):
+def _bwd(q2, k2, v2, o, lse, do2, dq, dk, dv, B, S, Hq, Hk, D, scale, causal, Dv=None, rope=None):
+    """rope = (cos, sin) tables: q and k were rotate-half RoPE outputs and dq / dk come
+    back as the gradients of the unrotated q and k."""
     Dv = D if Dv is None else Dv
     delta = torch.empty(B, Hq, S, dtype=torch.float32, device=q2.device)
     dq_acc = torch.empty(B * S, Hq * D, dtype=torch.float32, device=q2.device)
+    cos, sin = rope if rope is not None else (None, None)
     ext().flash_bwd(q2, k2, v2, o, do2, lse, delta, dq_acc, dq, dk, dv, B, S, Hq, Hk, D, Dv, scale, causal,
-                    status(q2.device))
+                    status(q2.device), cos, sin)
 
 
 class FlashAttentionQKV(torch.autograd.Function):

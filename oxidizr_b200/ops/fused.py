@@ -190,6 +190,41 @@ class LinearRope(torch.autograd.Function):
         return dx, gw, None, None, None, None, None
 
 
+class AttentionQKVRope(torch.autograd.Function):
+    """Causal GQA attention of one block from its input: qkv = rope(x W_qkv^T) (RoPE in the
+    GEMM epilogue), o = flash(q, k, v).  The backward takes the inverse rotation inside
+    the flash backward (dK epilogue, dQ conversion), so the QKV projection's dX / dW GEMMs
+    read the unrotated gradient with no separate RoPE pass.  Upstream: model.rs:333-386."""
+
+    @staticmethod
+    def forward(ctx, x, w, cos, sin, nh: int, kvh: int, hd: int, scale: float):
+        from .flash import _fwd
+        B, S, K = x.shape
+        x2 = _c(x.reshape(-1, K))
+        qc, kc = nh * hd, kvh * hd
+        qkv = torch.empty(x2.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+        ext().gemm_rope(x2, w, qkv, cos, sin, hd, qc, kc, status(x.device))
+        o, lse = _fwd(qkv[:, :qc], qkv[:, qc:qc + kc], qkv[:, qc + kc:], B, S, nh, kvh, hd, scale, True)
+        ctx.save_for_backward(x2, qkv, o, lse, cos, sin)
+        ctx.w, ctx.cfg = w, (B, S, nh, kvh, hd, scale)
+        return o.view(B, S, qc)
+
+    @staticmethod
+    def backward(ctx, do):
+        from .flash import _bwd
+        x2, qkv, o, lse, cos, sin = ctx.saved_tensors
+        w = ctx.w
+        B, S, nh, kvh, hd, scale = ctx.cfg
+        qc, kc = nh * hd, kvh * hd
+        do2 = _c(do.reshape(B * S, qc))
+        dqkv = torch.empty_like(qkv)
+        _bwd(qkv[:, :qc], qkv[:, qc:qc + kc], qkv[:, qc + kc:], o, lse, do2, dqkv[:, :qc], dqkv[:, qc:qc + kc],
+             dqkv[:, qc + kc:], B, S, nh, kvh, hd, scale, True, rope=(cos, sin))
+        dx = mm(dqkv, w, b_t=True).view(B, S, w.shape[1]) if ctx.needs_input_grad[0] else None
+        gw = _wgrad_gemm(w, dqkv, x2)
+        return dx, gw, None, None, None, None, None, None
+
+
 class SwiGLUMLP(torch.autograd.Function):
     """y = resid + (silu(x Wg^T) * (x Wu^T)) Wd^T with W_gu interleaved in 128-row blocks."""
 

@@ -129,3 +129,42 @@ def test_mla_pack_matches_reference(B, S, nh, hd, dr):
     assert _rel(qc.grad, qc_r.grad) < 5e-3
     assert _rel(kv.grad, kv_r.grad) < 5e-3
     assert _rel(rp.grad, rp_r.grad) < 1e-2
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("B,S,Hq,Hk,H", [(2, 300, 4, 2, 256), (1, 512, 8, 1, 512)])
+def test_attention_rope_fused_backward(hd, B, S, Hq, Hk, H):
+    """One attention node from the block input (QKV GEMM with RoPE, flash forward; the
+    backward un-rotates dq / dk inside the flash backward) against fp32 torch: the
+    output, dX and dW of the QKV projection."""
+    from oxidizr_b200.ops import reference as R
+    from oxidizr_b200.ops._C import check_status
+    from oxidizr_b200.ops.fused import AttentionQKVRope
+    from oxidizr_b200.models.common import RopeCache
+    torch.manual_seed(hd + S)
+    N = (Hq + 2 * Hk) * hd
+    x = (torch.randn(B, S, H, device="cuda") * 0.5).bfloat16().requires_grad_()
+    w = (torch.randn(N, H, device="cuda") / math.sqrt(H)).bfloat16().requires_grad_()
+    cos, sin = RopeCache.get(hd, S, 10000.0, x.device)
+    scale = 1.0 / math.sqrt(hd)
+    o = AttentionQKVRope.apply(x, w, cos, sin, Hq, Hk, hd, scale)
+    do = torch.randn_like(o)
+    o.backward(do)
+    torch.cuda.synchronize()
+    check_status("cuda")
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    y = xr @ wr.t()
+    q = y[..., :Hq * hd].reshape(B, S, Hq, hd).transpose(1, 2)
+    k = y[..., Hq * hd:(Hq + Hk) * hd].reshape(B, S, Hk, hd).transpose(1, 2)
+    v = y[..., (Hq + Hk) * hd:].reshape(B, S, Hk, hd)
+    q = R.apply_rope(q, cos[:S], sin[:S]).transpose(1, 2)
+    k = R.apply_rope(k, cos[:S], sin[:S]).transpose(1, 2)
+    ref = _ref(q, k, v, scale).reshape(B, S, Hq * hd)
+    ref.backward(do.float())
+    assert _rel(o, ref) < 1e-2
+    assert _rel(x.grad, xr.grad) < 3e-2, _rel(x.grad, xr.grad)
+    # per block of the projection's rows: q, k (un-rotated in the flash backward) and v
+    for name, sl in (("q", slice(0, Hq * hd)), ("k", slice(Hq * hd, (Hq + Hk) * hd)), ("v", slice((Hq + Hk) * hd, N))):
+        e = _rel(w.grad[sl], wr.grad[sl])
+        assert e < 3e-2, (name, e)
