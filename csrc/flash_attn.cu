@@ -397,7 +397,7 @@ void launch_fa_fwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
 //   P^T  = exp2(S^T c - lse_i), dS^T = P^T (dP^T - delta_i) * scale
 //                                              (softmax warps -> swizzled smem)
 //   dV += P^T dO_i, dK += dS^T Q_i             (TMEM accumulators)
-//   dQ_i = dS K -> f32 atomics into dq_acc     (TMEM, aliases S^T)
+//   dQ_i = dS K -> TMA reduce-add into dq_acc  (TMEM, aliases dP^T)
 // dS^T in shared memory serves as the K-major A of dK and, read as MN-major,
 // as the A of dQ; Q, dO and K are read as K-major or MN-major B operands from
 // the same tiles.
@@ -448,13 +448,15 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 //        P^T is written back into TMEM as bf16 (the A operand of dV), dS^T to
 //        128B-swizzled shared memory (A of dK, and read MN-major, A of dQ)
 //   dV += P^T dO_i, dK += dS^T Q_i                (TMEM accumulators)
-//   dQ_i = dS K -> f32 atomics into dq_acc        (TMEM, in the dP^T columns)
-// Q_i / dO_i are double-buffered so the next pair's loads overlap this one.
+//   dQ_i = dS K -> TMA reduce-add into dq_acc     (TMEM, in the dP^T columns)
+// Q_i / dO_i are double-buffered so the next pair's loads overlap this one; the
+// next pair's S^T MMA is issued before this pair's dQ has been drained (only its
+// dP^T MMA waits for that), and lse / delta are loaded one pair ahead.
 template <int DQ, int DV>
 __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                  FaBwdParams p) {
+                  const __grid_constant__ CUtensorMap tmDQ, FaBwdParams p) {
   using L = FaBwdSmem<DQ, DV>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -505,6 +507,7 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -558,16 +561,16 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
         const int st = it & 1;
         const uint32_t aQ = smem_u32(sQ + st * L::TQ_BYTES), aDO = smem_u32(sDO + st * L::TV_BYTES);
         if (!mbar_wait(&qdo_full[st], (it >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        if (it > 0) {
-          // S^T columns hold P^T of the previous pair until its dV MMA completed;
-          // the dP^T columns hold its dQ until the softmax warps read it
-          if (!mbar_wait(it_done, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
-          if (!mbar_wait(dq_read, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        }
         tc_fence_after();
+        // S^T columns hold P^T of the previous pair until its dV MMA has read them; that
+        // MMA was issued earlier by this thread, so S^T can be issued now and runs while
+        // the softmax warps drain the previous dQ
 #pragma unroll
         for (int kk = 0; kk < DQ / 16; ++kk)
           tc_mma_f16(TM_S, kmajor_desc(aK, kk, 128 * 128), kmajor_desc(aQ, kk, 128 * 128), ID_SS, kk != 0);
+        // the dP^T columns hold the previous dQ until the softmax warps have read it
+        if (it > 0 && !mbar_wait(dq_read, (it - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < DV / 16; ++kk)
           tc_mma_f16(TM_DP, kmajor_desc(aV, kk, 128 * 128), kmajor_desc(aDO, kk, 128 * 128), ID_SS, kk != 0);
@@ -599,6 +602,19 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const int kpos = k0 + r;
     bool ok = true;
+    // lse / delta of a pair's 128 queries: the first 128 softmax threads load one
+    // element each, one pair ahead (registers), so no global load latency sits
+    // between the pairs
+    const int vtid = threadIdx.x - 64;
+    float nx_lse = 0.f, nx_delta = 0.f;
+    auto load_vec = [&](int it2) {
+      const int h2 = hk * group + it2 / n_i;
+      const int qp = (i_start + it2 % n_i) * 128 + vtid;
+      const int64_t vi = ((int64_t)b * p.Hq + h2) * p.S + qp;
+      nx_lse = qp < p.S ? __ldg(p.lse + vi) * 1.4426950408889634f : 0.f;
+      nx_delta = qp < p.S ? __ldg(p.delta + vi) : 0.f;
+    };
+    if (vtid < 128 && n_it > 0) load_vec(0);
     // After a failed wait the loop keeps running without work so that every
     // softmax warp still reaches each named barrier.
     for (int it = 0; it < n_it; ++it) {
@@ -606,14 +622,10 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       const int i = i_start + it % n_i;
       const int q0 = i * 128;
       named_bar_sync(1, 256);  // every softmax warp is done with the previous pair's vectors
-      {
-        const int tid = threadIdx.x - 64;
-        if (tid < 128) {
-          const int qp = q0 + tid;
-          const int64_t vi = ((int64_t)b * p.Hq + h) * p.S + qp;
-          s_lse[tid] = qp < p.S ? p.lse[vi] * 1.4426950408889634f : 0.f;
-          s_delta[tid] = qp < p.S ? p.delta[vi] : 0.f;
-        }
+      if (vtid < 128) {
+        s_lse[vtid] = nx_lse;
+        s_delta[vtid] = nx_delta;
+        if (it + 1 < n_it) load_vec(it + 1);
       }
       named_bar_sync(1, 256);
       if (!ok) continue;
@@ -658,28 +670,42 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
-      // dQ of this (h, i): thread r owns query row r; the two halves take alternate 32-column chunks
+      // dQ of this (h, i): thread r owns query row r; the two halves take alternate 32-column
+      // chunks.  Each warp stages its 32 rows x 32 columns (f32, 128B-swizzled) in its own
+      // 4 KB slab of the dS^T buffer -- the slab it writes dS^T into, free once this pair's
+      // MMAs have completed -- and adds it to dq_acc with one TMA reduce-add (rows past the
+      // sequence end are clipped by the tensor map).
       if (!mbar_wait(it_done, it & 1, abort_flag, p.status)) { ok = false; continue; }
       tc_fence_after();
-      const int qp = q0 + r;
-      float* dqrow = p.dq_acc + (int64_t)(row0 + qp) * p.ld_dq + h * DQ;
+      uint8_t* slab = sDSt + half * (128 * 128) + quarter * (32 * 128);
 #pragma unroll 1
       for (int c = half; c < DQ / 32; c += 2) {
         uint32_t o[32];
         tmem_ld32(TM_DQ + lane_base + c * 32, o);
         tc_wait_ld();
-        if (qp < p.S) {
-          float4* d4 = reinterpret_cast<float4*>(dqrow + c * 32);
+        if (c != half) {  // the previous chunk's reduce has finished reading the slab
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            atomicAdd(d4 + q, make_float4(__uint_as_float(o[q * 4]), __uint_as_float(o[q * 4 + 1]),
-                                          __uint_as_float(o[q * 4 + 2]), __uint_as_float(o[q * 4 + 3])));
+        for (int u = 0; u < 8; ++u)
+          sw128_store16(slab, lane, u, make_uint4(o[u * 4], o[u * 4 + 1], o[u * 4 + 2], o[u * 4 + 3]));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && q0 + quarter * 32 < p.S) {  // a box wholly past the sequence end adds nothing
+          tma_reduce_add_3d(&tmDQ, slab, h * DQ + c * 32, q0 + quarter * 32, b);
+          bulk_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dq_read);
+      if (lane == 0) {
+        mbar_arrive(dq_read);
+        bulk_wait_read<0>();  // the slab is written again by the next pair's softmax
+      }
+      __syncwarp();
     }
+    if (lane == 0) bulk_wait<0>();  // every dQ reduce issued by this warp has been performed
     // dK, dV of this key tile (thread r owns key row r; halves take alternate chunks)
     if (ok && n_it > 0) {
       tc_fence_after();
@@ -848,6 +874,26 @@ __global__ void fa_dq_convert_kernel(const float* __restrict__ acc, int64_t ldac
   }
 }
 
+// 3-D f32 tensor map over dq_acc viewed as [B][S][cols] (row stride ld), box of 32
+// columns x 32 rows x 1 batch, 128-byte swizzle: the target of the dQ reduce-adds.
+// Rows past S are outside the map, so a box that reaches past a sequence's end is
+// clipped there instead of spilling into the next sequence.
+inline CUtensorMap make_tmap_dq(float* base, int B, int S, int64_t cols, int64_t ld) {
+  OXI_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0 && (ld * 4) % 16 == 0 && cols % 32 == 0,
+            "dq accumulator: 16-byte aligned rows, a multiple of 32 columns");
+  ensure_current_context();
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(ld * 4 * S)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  OXI_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (dq accumulator) failed: ", (int)r);
+  return m;
+}
+
 template <int DQ, int DV>
 void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                      const void* dout, int64_t lddo, const float* lse, const float* delta, float* dq_acc,
@@ -860,6 +906,7 @@ void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
   CUtensorMap tk = make_tmap_bf16(k, T, (int64_t)Hk * DQ, ldk, 64, 128);
   CUtensorMap tv = make_tmap_bf16(v, T, (int64_t)Hk * DV, ldv, 64, 128);
   CUtensorMap tdo = make_tmap_bf16(dout, T, (int64_t)Hq * DV, lddo, 64, 128);
+  CUtensorMap tdq = make_tmap_dq(dq_acc, B, S, (int64_t)Hq * DQ, ld_dq);
   FaBwdParams p;
   p.B = B; p.S = S; p.Hq = Hq; p.Hk = Hk;
   p.scale = scale;
@@ -883,7 +930,7 @@ void launch_fa_bwd_t(const void* q, int64_t ldq, const void* k, int64_t ldk, con
     attr = true;
   }
   dim3 grid(Hk, B, (S + 127) / 128);
-  kern<<<grid, FA_BWD_THREADS, L::TOTAL, st>>>(tq, tk, tv, tdo, p);
+  kern<<<grid, FA_BWD_THREADS, L::TOTAL, st>>>(tq, tk, tv, tdo, tdq, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

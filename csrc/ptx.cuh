@@ -126,6 +126,17 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// 3-D tiled reduce-add shared -> global (element type and swizzle from the tensor
+// map; bulk-group completion).  The shared source must have been written before a
+// fence.proxy.async.shared::cta; coordinates must be non-negative (the box is
+// clipped at the tensor's upper bounds).
+__device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 // 2-D tiled load global -> shared (this CTA only), completion on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int c0, int c1) {
   asm volatile(
