@@ -155,7 +155,8 @@ class Mamba1Block(RefModule):
         self.norm.reset_parameters()
 
     def forward(self, x):
-        return self.mamba(api.rmsnorm(x, self.norm.weight, 1e-5), x), None
+        h, x = api.rmsnorm_resid(x, self.norm.weight, 1e-5)
+        return self.mamba(h, x), None
 
 
 # =========================================================================
@@ -226,7 +227,8 @@ class Mamba2Block(RefModule):
         self.mixer.reset_parameters(std, gen)
 
     def forward(self, x):
-        return self.mixer(api.layernorm(x, self.norm.weight, self.norm.bias, 1e-6), x), None
+        h, x = api.layernorm_resid(x, self.norm.weight, self.norm.bias, 1e-6)
+        return self.mixer(h, x), None
 
 
 # =========================================================================
@@ -376,4 +378,5 @@ class Mamba3Block(RefModule):
         self.mixer.reset_parameters(std, gen)
 
     def forward(self, x):
-        return self.mixer(api.layernorm(x, self.norm.weight, self.norm.bias, 1e-6), x), None
+        h, x = api.layernorm_resid(x, self.norm.weight, self.norm.bias, 1e-6)
+        return self.mixer(h, x), None

@@ -51,9 +51,9 @@ class AttnBlock(RefModule):
         self.post_attention_layernorm.reset_parameters()
 
     def forward(self, x):
-        h = api.rmsnorm(x, self.input_layernorm.weight, 1e-5)
+        h, x = api.rmsnorm_resid(x, self.input_layernorm.weight, 1e-5)
         x = self.self_attn(h, x)
-        h = api.rmsnorm(x, self.post_attention_layernorm.weight, 1e-5)
+        h, x = api.rmsnorm_resid(x, self.post_attention_layernorm.weight, 1e-5)
         if self.moe is not None:
             return self.moe(h, x)
         return self.mlp(h, x), None

@@ -36,6 +36,23 @@ def rmsnorm(x, w, eps: float = 1e-5):
     return R.rmsnorm(x, w, eps)
 
 
+def rmsnorm_resid(x, w, eps: float = 1e-5):
+    """(rmsnorm(x, w), x) where the second output is the residual stream to add back after
+    the sublayer: on the GPU its gradient is added inside the norm backward kernel."""
+    if _native(x):
+        from .fused import NormResid
+        return NormResid.apply(x, w, None, 0, eps)
+    return rmsnorm(x, w, eps), x
+
+
+def layernorm_resid(x, w, b, eps: float = 1e-6):
+    """(layernorm(x, w, b), x), the residual stream passing through like rmsnorm_resid."""
+    if _native(x):
+        from .fused import NormResid
+        return NormResid.apply(x, w, b, 1, eps)
+    return layernorm(x, w, b, eps), x
+
+
 def layernorm(x, w, b, eps: float = 1e-6):
     if _native(x):
         from .fused import Norm

@@ -122,18 +122,70 @@ class Norm(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        xc, gc, rstd, mean = ctx.saved_tensors
-        w, b, mode = ctx.w, ctx.b, ctx.mode
-        H = xc.shape[-1]
-        dyc = _c(dy)
-        dx = torch.empty_like(xc)
-        dgate = torch.empty_like(gc) if mode == 2 else None
-        dw = torch.zeros(H, dtype=torch.float32, device=xc.device)
-        db = torch.zeros(H, dtype=torch.float32, device=xc.device) if mode == 1 else None
-        ext().norm_bwd(mode, dyc, xc, gc, w, rstd, mean, None, dx, dgate, dw, db)
-        gw = _vec_grad(w, dw)
-        gb = _vec_grad(b, db) if mode == 1 else None
+        dx, dgate, gw, gb = _norm_bwd(ctx, dy, None)
         return dx, dgate, gw, gb, None, None
+
+
+def _grad_target(p, H: int, device):
+    """(f32 [H] buffer the norm kernel adds its weight gradient into, whether it is p.main_grad)."""
+    mg = getattr(p, "main_grad", None) if p is not None else None
+    if mg is not None and mg.dtype == torch.float32 and mg.is_contiguous() and mg.numel() == H:
+        return mg.view(-1), True
+    return torch.zeros(H, dtype=torch.float32, device=device), False
+
+
+def _norm_bwd(ctx, dy, dres):
+    """Norm backward; dres (the gradient of a residual stream that passed through) is added
+    to dx inside the kernel.  Weight gradients accumulate straight into main_grad (the kernel
+    adds with atomics), so no zero fill or separate add runs."""
+    xc, gc, rstd, mean = ctx.saved_tensors
+    w, b, mode = ctx.w, ctx.b, ctx.mode
+    H = xc.shape[-1]
+    dyc = _c(dy)
+    dx = torch.empty_like(xc)
+    dgate = torch.empty_like(gc) if mode == 2 else None
+    dw, w_direct = _grad_target(w, H, xc.device)
+    db, b_direct = _grad_target(b, H, xc.device) if mode == 1 else (None, False)
+    dr = _c(dres.reshape(xc.shape)) if dres is not None else None
+    ext().norm_bwd(mode, dyc, xc, gc, w, rstd, mean, dr, dx, dgate, dw, db)
+    if w_direct:
+        _ready(w)
+        gw = None
+    else:
+        gw = _vec_grad(w, dw)
+    if mode != 1:
+        gb = None
+    elif b_direct:
+        _ready(b)
+        gb = None
+    else:
+        gb = _vec_grad(b, db)
+    return dx, dgate, gw, gb
+
+
+class NormResid(torch.autograd.Function):
+    """(norm(x), x) for mode 0 (RMSNorm(x) w) or 1 (LayerNorm(x) w + b): the residual stream
+    x passes through this node, so the gradient that comes back for it is added to the
+    norm's input gradient inside the norm backward kernel (no separate add of the two
+    gradient branches).  Upstream: the pre-norm blocks x + f(norm(x)) of model.rs:874-939."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, mode: int, eps: float):
+        xc = _c(x)
+        H = x.shape[-1]
+        rows = xc.numel() // H
+        y = torch.empty_like(xc)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        mean = torch.empty(rows, dtype=torch.float32, device=x.device) if mode == 1 else None
+        ext().norm_fwd(mode, xc, None, w, b, y, rstd, mean, eps)
+        ctx.save_for_backward(xc, None, rstd, mean)
+        ctx.w, ctx.b, ctx.mode = w, b, mode
+        return y, x
+
+    @staticmethod
+    def backward(ctx, dy, dres):
+        dx, _, gw, gb = _norm_bwd(ctx, dy, dres)
+        return dx, gw, gb, None, None
 
 
 # ----------------------------------------------------------------- linears

@@ -44,6 +44,38 @@ def test_norms_fwd_bwd(mode, H):
         assert _rel(g.grad, gr.grad) < 2e-2
 
 
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("H", [2048, 520])
+def test_norm_resid_adds_residual_gradient_and_accumulates_main_grad(mode, H):
+    """(norm(x), x) with the residual branch's gradient added inside the norm backward, and
+    the weight / bias gradients added straight into existing main_grad buffers."""
+    from oxidizr_b200.ops import reference as R
+    from oxidizr_b200.ops.fused import NormResid
+    torch.manual_seed(11 + mode + H)
+    T = 333
+    x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_()
+    w = torch.nn.Parameter((1 + 0.1 * torch.randn(H, device="cuda")).bfloat16())
+    b = torch.nn.Parameter((0.1 * torch.randn(H, device="cuda")).bfloat16()) if mode == 1 else None
+    w.main_grad = torch.full((H,), 0.25, device="cuda")
+    if b is not None:
+        b.main_grad = torch.full((H,), -0.5, device="cuda")
+    y, xp = NormResid.apply(x, w, b, mode, 1e-5)
+    dy, dr = torch.randn_like(y), torch.randn_like(y)
+    torch.autograd.backward([y, xp], [dy, dr])
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    br = b.detach().float().requires_grad_() if mode == 1 else None
+    yr = R.rmsnorm(xr, wr, 1e-5) if mode == 0 else R.layernorm(xr, wr, br, 1e-5)
+    torch.autograd.backward([yr, xr * 1.0], [dy.float(), dr.float()])
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 2e-2
+    assert w.grad is None
+    assert _rel(w.main_grad - 0.25, wr.grad) < 2e-2
+    if mode == 1:
+        assert b.grad is None
+        assert _rel(b.main_grad + 0.5, br.grad) < 2e-2
+
+
 def test_linear_cross_entropy():
     from oxidizr_b200.ops.fused import LinearCrossEntropy
     torch.manual_seed(0)
