@@ -287,7 +287,7 @@ def run_once(what: str):
     torch.manual_seed(0)
     if what in ("fa_fwd", "fa_bwd"):
         from ..ops.flash import FlashAttentionQKV
-        B, S, Hq, Hk, D = 1, 2048, 16, 8, 128
+        B, S, Hq, Hk, D = 4, 2048, 16, 8, 128  # 512 backward CTAs: several waves, like the bench shape
         qkv = torch.randn(B, S, (Hq + 2 * Hk) * D, device="cuda").bfloat16().requires_grad_()
         for _ in range(3):
             o = FlashAttentionQKV.apply(qkv, Hq, Hk, D, 1.0 / math.sqrt(D), True)
