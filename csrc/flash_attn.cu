@@ -252,19 +252,23 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
       float mx[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) mx[q] = -INFINITY;
+      // the max is taken over the raw scores and scaled once (the scale is positive); the
+      // scale is applied inside the exponent's FFMA below
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         const int kc = k0 + c * 32;
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          float v = __uint_as_float(rr[c][t]) * p.scale_log2;
-          if (need_mask) v = (kc + t > lim) ? -INFINITY : v;
-          rr[c][t] = __float_as_uint(v);
+          float v = __uint_as_float(rr[c][t]);
+          if (need_mask) {
+            v = (kc + t > lim) ? -INFINITY : v;
+            rr[c][t] = __float_as_uint(v);
+          }
           mx[t & 7] = fmaxf(mx[t & 7], v);
         }
       }
       const float mloc = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * p.scale_log2;
       float* xm = s_xmax + (j & 1) * 256;
       xm[half * 128 + r] = mloc;
       // every S column of this tile has been read into registers before either
@@ -307,8 +311,8 @@ __global__ void __launch_bounds__(FA_THREADS, 2)
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const float a = ex2_approx(__uint_as_float(rr[c][t]) - mref);
-          const float bb = ex2_approx(__uint_as_float(rr[c][t + 1]) - mref);
+          const float a = ex2_approx(fmaf(__uint_as_float(rr[c][t]), p.scale_log2, -mref));
+          const float bb = ex2_approx(fmaf(__uint_as_float(rr[c][t + 1]), p.scale_log2, -mref));
           rsa[(t >> 1) & 7] += a + bb;
           pk[t / 2] = pack_bf16(a, bb);
         }
