@@ -60,9 +60,32 @@ def _stale() -> bool:
     return any(os.path.getmtime(s) > t for s in sources() + _headers())
 
 
+# torch's builder serialises builds of one directory through a ``lock`` file that it
+# deletes when done.  A copy of the tree taken while a build ran carries that file, and a
+# build in the copy would then wait for it forever; no build here runs this long, so an
+# older lock file is left over and is removed.
+STALE_LOCK_S = 20 * 60
+
+
+def _clear_stale_lock(build_dir: str) -> None:
+    import time
+    path = os.path.join(build_dir, "lock")
+    try:
+        age = time.time() - os.path.getmtime(path)
+    except OSError:
+        return
+    if age > STALE_LOCK_S:
+        print(f"oxidizr_b200: removing a stale build lock ({age / 60:.0f} min old): {path}", file=sys.stderr)
+        try:
+            os.remove(path)
+        except OSError:
+            pass
+
+
 def build(verbose: bool = False):
     """Compile every CUDA/C++ source of the extension for sm_100a."""
     os.makedirs(BUILD_DIR, exist_ok=True)
+    _clear_stale_lock(BUILD_DIR)
     from torch.utils.cpp_extension import load
     os.environ.setdefault("MAX_JOBS", str(max(os.cpu_count() or 4, 4)))
     mod = load(
@@ -116,6 +139,7 @@ def tools_sources():
 def build_tools(verbose: bool = False):
     """Compile the measurement-tools extension (csrc/tools/) for sm_100a."""
     os.makedirs(TOOLS_BUILD_DIR, exist_ok=True)
+    _clear_stale_lock(TOOLS_BUILD_DIR)
     from torch.utils.cpp_extension import load as _load
     return _load(name=TOOLS_NAME, sources=tools_sources(), extra_cflags=["-O3", "-std=c++17"],
                  extra_cuda_cflags=NVCC_FLAGS, extra_include_paths=[CSRC, TOOLS_DIR],

@@ -40,6 +40,8 @@ def _native():
         if not os.path.exists(so) or os.path.getmtime(so) < os.path.getmtime(_SRC):
             os.makedirs(_BUILD, exist_ok=True)
             from torch.utils.cpp_extension import load
+            from ._ext import _clear_stale_lock
+            _clear_stale_lock(_BUILD)
             _mod = load(name="oxidizr_b200_data", sources=[_SRC], extra_cflags=["-O3", "-std=c++17"],
                         build_directory=_BUILD, with_cuda=False, verbose=False)
         else:
