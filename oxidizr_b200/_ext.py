@@ -61,29 +61,36 @@ def _stale() -> bool:
 
 
 # torch's builder serialises builds of one directory through a ``lock`` file that it
-# deletes when done.  A copy of the tree taken while a build ran carries that file, and a
-# build in the copy would then wait for it forever; no build here runs this long, so an
-# older lock file is left over and is removed.
-STALE_LOCK_S = 20 * 60
+# deletes when done, and waits without limit while another build holds it.  A copy of the
+# tree taken while a build ran carries that file, so a build in the copy would wait
+# forever.  Before building, wait for a lock file only until it is STALE_LOCK_S old (no
+# build here takes that long), then treat it as left over and remove it.
+STALE_LOCK_S = 10 * 60
 
 
 def _clear_stale_lock(build_dir: str) -> None:
     import time
     path = os.path.join(build_dir, "lock")
-    try:
-        age = time.time() - os.path.getmtime(path)
-    except OSError:
-        return
-    if age > STALE_LOCK_S:
-        print(f"oxidizr_b200: removing a stale build lock ({age / 60:.0f} min old): {path}", file=sys.stderr)
+    while True:
         try:
-            os.remove(path)
+            age = time.time() - os.path.getmtime(path)
         except OSError:
-            pass
+            return  # no lock (or it went away): go ahead
+        if age > STALE_LOCK_S:
+            print(f"oxidizr_b200: removing a stale build lock ({age / 60:.0f} min old): {path}", file=sys.stderr)
+            try:
+                os.remove(path)
+            except OSError:
+                pass
+            return
+        time.sleep(min(5.0, STALE_LOCK_S - age + 0.1))
 
 
-def build(verbose: bool = False):
-    """Compile every CUDA/C++ source of the extension for sm_100a."""
+def build(verbose: bool = False, force: bool = False):
+    """Compile every CUDA/C++ source of the extension for sm_100a (imports the built module
+    without invoking the builder when it is newer than every source, unless ``force``)."""
+    if not force and not _stale():
+        return _import_built()
     os.makedirs(BUILD_DIR, exist_ok=True)
     _clear_stale_lock(BUILD_DIR)
     from torch.utils.cpp_extension import load
@@ -122,7 +129,7 @@ def load(required: bool = True):
         import torch  # noqa: F401  (the extension links against torch)
         try:
             if _stale() or os.environ.get("OXI_FORCE_BUILD"):
-                _mod = build(verbose=bool(os.environ.get("OXI_BUILD_VERBOSE")))
+                _mod = build(verbose=bool(os.environ.get("OXI_BUILD_VERBOSE")), force=True)
             else:
                 _mod = _import_built()
         except Exception as e:  # pragma: no cover - only hit without a toolchain
