@@ -479,7 +479,8 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
   uint64_t* p_ready = bars + 6;
   uint64_t* it_done = bars + 7;
   uint64_t* dq_read = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* dq_full = bars + 9;    // dK and dQ MMAs of the pair done (dS^T free, dQ readable)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -505,6 +506,7 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
     mbar_init(p_ready, 8);   // one arrival per softmax warp
     mbar_init(it_done, 1);
     mbar_init(dq_read, 8);
+    mbar_init(dq_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -581,16 +583,22 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
         tc_commit(sdp_full);
         if (!mbar_wait(p_ready, it & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
+        // dK and dQ (the two readers of dS^T) first: the softmax warps drain dQ while dV runs
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk) {
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          tc_mma_f16(TM_DK, kmajor_desc(aDSt, kk, 128 * 128), umma_desc_sw128(aQ + kk * 2048, 128 * 128, 1024),
+                     ID_K, acc);
+          tc_mma_f16(TM_DQ, umma_desc_sw128(aDSt + kk * 2048, 128 * 128, 1024),
+                     umma_desc_sw128(aK + kk * 2048, 128 * 128, 1024), ID_Q, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(dq_full);
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
           // P^T (bf16 in TMEM): queries 0..63 in columns 0..31, 64..127 in columns 64..95
           const uint32_t aP = TM_S + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
           tc_mma_f16_ts(TM_DV, aP, umma_desc_sw128(aDO + kk * 2048, 128 * 128, 1024), ID_V, acc);
-          tc_mma_f16(TM_DK, kmajor_desc(aDSt, kk, 128 * 128), umma_desc_sw128(aQ + kk * 2048, 128 * 128, 1024),
-                     ID_K, acc);
-          tc_mma_f16(TM_DQ, umma_desc_sw128(aDSt + kk * 2048, 128 * 128, 1024),
-                     umma_desc_sw128(aK + kk * 2048, 128 * 128, 1024), ID_Q, kk > 0 ? 1u : 0u);
         }
         tc_commit(it_done);
         tc_commit(&qdo_empty[st]);
@@ -677,9 +685,9 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       // dQ of this (h, i): thread r owns query row r; the two halves take alternate 32-column
       // chunks.  Each warp stages its 32 rows x 32 columns (f32, 128B-swizzled) in its own
       // 4 KB slab of the dS^T buffer -- the slab it writes dS^T into, free once this pair's
-      // MMAs have completed -- and adds it to dq_acc with one TMA reduce-add (rows past the
-      // sequence end are clipped by the tensor map).
-      if (!mbar_wait(it_done, it & 1, abort_flag, p.status)) { ok = false; continue; }
+      // dK and dQ MMAs have completed -- and adds it to dq_acc with one TMA reduce-add (rows
+      // past the sequence end are clipped by the tensor map).  The dV MMA runs meanwhile.
+      if (!mbar_wait(dq_full, it & 1, abort_flag, p.status)) { ok = false; continue; }
       tc_fence_after();
       uint8_t* slab = sDSt + half * (128 * 128) + quarter * (32 * 128);
 #pragma unroll 1
@@ -710,6 +718,8 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       __syncwarp();
     }
     if (lane == 0) bulk_wait<0>();  // every dQ reduce issued by this warp has been performed
+    // the last pair's dV MMA (issued after its dQ) completes the accumulators
+    if (ok && n_it > 0 && !mbar_wait(it_done, (n_it - 1) & 1, abort_flag, p.status)) ok = false;
     // dK, dV of this key tile (thread r owns key row r; halves take alternate chunks)
     if (ok && n_it > 0) {
       tc_fence_after();

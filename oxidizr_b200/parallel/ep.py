@@ -250,6 +250,16 @@ class EPLayerBuffers:
         return self._buf(name).ptr_table
 
 
+def _mark(moe, name: str) -> None:
+    """Record a CUDA event named ``name`` on the current stream when the layer carries a
+    phase timer (``moe._ep_timer``, a list set by the expert-parallel microbenchmark)."""
+    tm = getattr(moe, "_ep_timer", None)
+    if tm is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        tm.append((name, ev))
+
+
 class EPExperts(torch.autograd.Function):
     """resid + sum_j topw[t, j] * SwiGLU_{topi[t, j]}(x_t), experts spread over the group (NVLink).
 
@@ -278,6 +288,7 @@ class EPExperts(torch.autograd.Function):
             forced = int(os.environ.get("OXI_EP_INITIAL_ROWS", "0"))  # tests: start over capacity
             buf.ensure(forced, exact=True) if forced else buf.ensure(0, balanced_rows=T * k + El * 256)
         buf.ensure_pairs(T * k)
+        _mark(moe, "fwd_start")
         # the counts kernel checks every owner's rows against the capacity on the
         # device (no host read); over capacity, the layer is skipped on every rank
         all_counts, seg, rc = e.ep_counts(counts.int().contiguous(), g.pad.ptr_table, g.pad_local, rank, W, seq,
@@ -289,14 +300,17 @@ class EPExperts(torch.autograd.Function):
         pos = e.ep_dispatch(xc, topi, tw, all_counts, rank, W, g.cursor, buf.table("xrecv"), buf.table("metaw"),
                             buf.table("srcidx"), g.done[0:1], g.pad.ptr_table, seq, seg, st)
         e.ep_wait(g.pad_local, K_DISPATCHED, W, seq, st, g.wait_ns)
+        _mark(moe, "dispatched")
         h = torch.empty(cap, I, dtype=x.dtype, device=x.device)
         gu = torch.empty(cap, I2, dtype=x.dtype, device=x.device)
         e.gemm_grouped(1, 2, xr, False, w_gu.view(El * I2, H), False, El, seg, I2, h, gu, None, st)
+        _mark(moe, "gate_up")
         e.ep_expert_gemm_scatter(h, w_down.view(El * H, I), False, El, seg, H, buf.local("srcidx", torch.int32),
                                  buf.yret.ptr_table, T * k, g.done[2:3], g.pad.ptr_table, K_YREADY, rank, W, seq, st)
         yret = buf.yret.local.view(torch.bfloat16).view(T * k, H)
         y = e.ep_sum_pairs(yret, tw, T, k, resid.contiguous() if resid is not None else None, g.pad_local, K_YREADY,
                            W, seq, st, g.wait_ns)
+        _mark(moe, "combined")
         ctx.save_for_backward(topi, tw, pos, h, gu, seg, rc)
         ctx.moe, ctx.w_gu, ctx.w_down, ctx.has_resid = moe, w_gu, w_down, resid is not None
         return y
@@ -318,6 +332,7 @@ class EPExperts(torch.autograd.Function):
         st = status(dy.device)
         dy = dy.contiguous()
         seq = g.next_seq()
+        _mark(moe, "bwd_start")
         xr = buf.local("xrecv", torch.bfloat16, H)
         dyr = buf.local("dyrecv", torch.bfloat16, H)
         yret = buf.yret.local.view(torch.bfloat16).view(T * k, H)
@@ -325,16 +340,19 @@ class EPExperts(torch.autograd.Function):
         dtw = e.ep_push_dy(dy, topi, pos, El, buf.table("dyrecv"), yret, g.done[1:2], g.pad.ptr_table, rank, W, seq,
                            seg, st)
         e.ep_wait(g.pad_local, K_DYPUSHED, W, seq, st, g.wait_ns)
+        _mark(moe, "dy_pushed")
         e.ep_scale_rows(dyr, buf.local("metaw", torch.float32), seg, rc, El)
         g_down = _wgrad_grouped(w_down, dyr, h, seg, El)
         dgu = torch.empty_like(gu)
         swiglu_bwd_grouped(dyr, w_down, gu, dgu, El, seg, st)
         g_gu = _wgrad_grouped(w_gu, dgu, xr, seg, El)
+        _mark(moe, "expert_grads")
         # input-gradient rows straight into the sources' yret (their forward rows were
         # consumed by their push_dy, which finished before DYPUSHED)
         e.ep_expert_gemm_scatter(dgu, w_gu.view(El * I2, H), True, El, seg, I2, buf.local("srcidx", torch.int32),
                                  buf.yret.ptr_table, T * k, g.done[3:4], g.pad.ptr_table, K_DXREADY, rank, W, seq, st)
         dx = e.ep_sum_pairs(yret, None, T, k, None, g.pad_local, K_DXREADY, W, seq, st, g.wait_ns)
+        _mark(moe, "dx_combined")
         return dx, None, dtw, None, g_gu, g_down, (dy if ctx.has_resid else None), None
 
 
