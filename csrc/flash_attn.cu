@@ -636,7 +636,7 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       named_bar_sync(1, 256);  // every softmax warp is done with the previous pair's vectors
       if (vtid < 128) {
         s_lse[vtid] = nx_lse;
-        s_delta[vtid] = nx_delta * p.scale;  // delta pre-scaled: dS = P (dP scale - delta scale)
+        s_delta[vtid] = nx_delta;
         if (it + 1 < n_it) load_vec(it + 1);
       }
       named_bar_sync(1, 256);
@@ -645,8 +645,6 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
       // dS^T smem is free once the previous pair's MMAs completed (waited in the previous dQ step)
       tc_fence_after();
       const bool diag = p.causal && (q0 < k0 + 128);
-      // only diagonal tiles, a ragged last query tile or key rows past the end need masking
-      const bool need_mask = diag || (q0 + 128 > p.S) || (kpos >= p.S);
 #pragma unroll 1
       for (int cc = 0; cc < 2; ++cc) {
         const int c = half * 2 + cc;  // 32-query chunk 0..3
@@ -656,27 +654,19 @@ __global__ void __launch_bounds__(FA_BWD_THREADS, 1)
         tc_wait_ld();
         uint32_t pk[16], dk[16];
 #pragma unroll
-        for (int t = 0; t < 32; t += 4) {
-          // the four queries' (lse, delta * scale) as one broadcast 16-byte load each
-          const float4 l4 = *reinterpret_cast<const float4*>(s_lse + c * 32 + t);
-          const float4 d4 = *reinterpret_cast<const float4*>(s_delta + c * 32 + t);
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-          const float dl[4] = {d4.x, d4.y, d4.z, d4.w};
-          float pv[4], dsv[4];
+        for (int t = 0; t < 32; t += 2) {
+          float pv[2], dsv[2];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float pp = ex2_approx(fmaf(__uint_as_float(sr[t + e]), p.scale_log2, -lv[e]));
-            if (need_mask) {
-              const int qp = q0 + c * 32 + t + e;
-              pp = ((qp < p.S) && (kpos < p.S) && (!diag || qp >= kpos)) ? pp : 0.f;
-            }
+          for (int e = 0; e < 2; ++e) {
+            const int qc = c * 32 + t + e;
+            const int qp = q0 + qc;
+            const bool valid = (qp < p.S) && (kpos < p.S) && (!diag || qp >= kpos);
+            const float pp = valid ? ex2_approx(__uint_as_float(sr[t + e]) * p.scale_log2 - s_lse[qc]) : 0.f;
             pv[e] = pp;
-            dsv[e] = pp * fmaf(__uint_as_float(dr[t + e]), p.scale, -dl[e]);
+            dsv[e] = pp * (__uint_as_float(dr[t + e]) - s_delta[qc]) * p.scale;
           }
           pk[t / 2] = pack_bf16(pv[0], pv[1]);
-          pk[t / 2 + 1] = pack_bf16(pv[2], pv[3]);
           dk[t / 2] = pack_bf16(dsv[0], dsv[1]);
-          dk[t / 2 + 1] = pack_bf16(dsv[2], dsv[3]);
         }
         // P^T (bf16 pairs) back into this half's own, already read, S^T columns
         tmem_st16(TM_S + lane_base + (half * 64 + cc * 16), pk);
