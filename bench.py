@@ -81,6 +81,12 @@ def bench_config(model: str = "llama"):
     return LitConfig.from_dict(d)
 
 
+def _ep_regrows() -> int:
+    """Collective expert-parallel receive-buffer regrows so far (all groups of this process)."""
+    from oxidizr_b200.parallel.ep import EPGroup
+    return sum(g.regrows for g in EPGroup._groups.values())
+
+
 def flops_per_token(m) -> float:
     from oxidizr_b200.utils.flops import flops_per_token as f
     return f(m)
@@ -253,11 +259,13 @@ def main():
     launch_counter.enabled = True
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rg0 = _ep_regrows()
     e0.record()
     for _ in range(args.steps):
         loss_t, gn_t = trainer.training_step()
     e1.record()
     barrier()
+    rg_timed = _ep_regrows() - rg0
     launch_counter.enabled = False
     n_launch = launch_counter.count
     clocks = sampler.stop()
@@ -283,10 +291,12 @@ def main():
             float(trainer2.training_step()[0])
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        rg1 = _ep_regrows()
         f0.record()
         for _ in range(args.steps):
             loss_host = float(trainer2.training_step()[0])  # D2H of the step's loss
         f1.record()
+        rg2 = _ep_regrows()
         barrier()
         ms_e2e = max_over_ranks(f0.elapsed_time(f1) / args.steps)
         loader.close()
@@ -323,6 +333,9 @@ def main():
     if ep > 1:
         from oxidizr_b200.parallel.ep import EPLayerBuffers
         out["ep_buffer_reallocs"] = EPLayerBuffers.reallocs
+        # collective receive-buffer regrows (each follows a step that ran over capacity and
+        # skipped its update) inside the timed windows
+        out["ep_regrows"] = {"timed": rg_timed, "e2e": (rg2 - rg1) if not args.no_e2e else None}
     if hasattr(opt, "close"):
         opt.close()
     # ---------------- N > 1: the same model and step over the like-for-like NCCL transport
