@@ -65,11 +65,16 @@ def bench_gemm(shapes, iters=20):
     peaks = measured_peaks()
     rows = []
     for (M, N, K, lay) in shapes:
-        a_t, b_t = lay[0] == "t", lay[1] == "t"
+        # layout: a_t / b_t letters (n: K-major, t: MN-major), "+" for an f32 += output (the
+        # weight-gradient form: beta 1, split-K when the tiles do not fill the GPU)
+        a_t, b_t, acc = lay[0] == "t", lay[1] == "t", lay.endswith("+")
         a = torch.randn((K, M) if a_t else (M, K), device="cuda").bfloat16()
         b = torch.randn((K, N) if b_t else (N, K), device="cuda").bfloat16()
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        ms = time_fn(lambda: mm(a, b, a_t=a_t, b_t=b_t, out=out), iters)
+        out = torch.zeros(M, N, device="cuda", dtype=torch.float32 if acc else torch.bfloat16)
+        if acc:
+            ms = time_fn(lambda: mm(a, b, a_t=a_t, b_t=b_t, out=out, beta=1.0), iters)
+        else:
+            ms = time_fn(lambda: mm(a, b, a_t=a_t, b_t=b_t, out=out), iters)
         A = a.t() if a_t else a
         B = b.t() if b_t else b
         ms_ref = time_fn(lambda: torch.matmul(A, B.t()), iters)
@@ -456,7 +461,8 @@ def main(argv=None):
     ap.add_argument("--kernel", default="fa_fwd",
                     help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_dw | ssd_m2 | ssd_m3 | norm | "
                          "conv1d | swiglu | qkv_rope | ce | ce_chunked | mla_pack | moe | m3_bc | mamba1 | adamw")
-    ap.add_argument("--shapes", nargs="*", default=None, help="M,N,K[,layout] with layout nn|nt|tt")
+    ap.add_argument("--shapes", nargs="*", default=None,
+                    help="M,N,K[,layout] with layout nn|nt|tt, a trailing + for an f32 += output")
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args(argv)
     if args.what == "once":
