@@ -298,12 +298,17 @@ def run_once(what: str):
             o = FlashAttentionQKV.apply(qkv, Hq, Hk, D, 1.0 / math.sqrt(D), True)
             if what == "fa_bwd":
                 o.backward(torch.ones_like(o))
-    elif what == "gemm":
+    elif what in ("gemm", "gemm_torch"):
+        # the same 8192 x 8192 x 4096 NN product through our kernel or through torch
+        # (cuBLAS): the pair of captures compares the two kernels' counters
         from ..ops.gemm import mm
         a = torch.randn(8192, 4096, device="cuda").bfloat16()
         b = torch.randn(8192, 4096, device="cuda").bfloat16()
         for _ in range(3):
-            mm(a, b)
+            if what == "gemm":
+                mm(a, b)
+            else:
+                torch.matmul(a, b.t())
     elif what == "gemm_dw":
         from ..ops.gemm import mm
         a = torch.randn(16384, 2048, device="cuda").bfloat16()
@@ -459,7 +464,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attn", "ssm", "ce", "moe", "once"])
     ap.add_argument("--kernel", default="fa_fwd",
-                    help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_dw | ssd_m2 | ssd_m3 | norm | "
+                    help="for 'once': fa_fwd | fa_bwd | fa_mla | gemm | gemm_torch | gemm_dw | ssd_m2 | ssd_m3 | norm | "
                          "conv1d | swiglu | qkv_rope | ce | ce_chunked | mla_pack | moe | m3_bc | mamba1 | adamw")
     ap.add_argument("--shapes", nargs="*", default=None,
                     help="M,N,K[,layout] with layout nn|nt|tt, a trailing + for an f32 += output")
