@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 
 #include "host_util.h"
 #include "kernels_ep.h"
@@ -38,19 +39,32 @@
 
 namespace oxi {
 
+// An integer tuning knob from the environment, clamped to [lo, hi].
+inline int gemm_env_int(const char* name, int dflt, int lo, int hi) {
+  const char* e = getenv(name);
+  if (!e || !*e) return dflt;
+  return std::max(lo, std::min(hi, atoi(e)));
+}
+
+
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * BK * 2;   // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;   // 32 KB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int GEMM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr int GROUP_M = 8;
+constexpr int GROUP_M = 8;  // default row-tile grouping of the raster (OXI_GEMM_GROUP_M)
 
 enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_SWIGLU_BWD = 3, EPI_CE = 4, EPI_ROPE = 5 };
 
 struct GemmParams {
   int M, N, K;
   int tiles_m, tiles_n, num_tiles;  // num_tiles counts work units (tiles x splits)
+  int group_m;                       // row tiles per raster group (consecutive units share B)
+  int nst;                           // CTA-pair pipeline stages in use (<= PAIR_STAGES)
+  int diag_nostore;                  // diagnostics: the epilogue drains TMEM but stores nothing
+  int tma_out;                       // epilogue through shared memory + TMA: 0 off, 1 bf16 store,
+                                     // 2 f32 store, 3 f32 reduce-add (the tmD map covers D)
   int splits;                        // split-K factor (F32 accumulate epilogue only)
   int kb_per_split;
   void* D;                 // main output
@@ -98,17 +112,21 @@ struct GemmParams {
 };
 
 // CTA-pair configuration: each CTA holds 128 rows of A and 128 of B's 256 per
-// k-block (32 KB per stage), so six stages fit.
+// k-block (32 KB per stage); six stages fit beside the epilogue's staging buffers
+// (how many are used is a launch parameter, OXI_GEMM_PAIR_STAGES).
 constexpr int PAIR_STAGES = 6;
+// Epilogue staging for TMA stores: per epilogue warp two 4 KB boxes of 32 rows x 128 bytes.
+constexpr int EPI_SMEM = 4 * 2 * 4096;
 constexpr int PAIR_B_ROWS = 128;
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
   // Group GROUP_M row-tiles together so consecutive CTAs share B tiles in L2.
   t /= p.splits;
-  const int per_group = GROUP_M * p.tiles_n;
+  const int group_m = p.group_m > 0 ? p.group_m : GROUP_M;
+  const int per_group = group_m * p.tiles_n;
   const int g = t / per_group;
-  const int first_m = g * GROUP_M;
-  const int gm = min(p.tiles_m - first_m, GROUP_M);
+  const int first_m = g * group_m;
+  const int gm = min(p.tiles_m - first_m, group_m);
   const int r = t - g * per_group;
   tm = first_m + (r % gm);
   tn = r / gm;
@@ -220,8 +238,10 @@ __device__ __forceinline__ void load_bf16_row(const __nv_bfloat16* src, float* v
 // leader's `tempty`.  Every load reads global memory of this GPU only.
 template <bool A_MN, bool B_MN, int EPI, int CG = 1>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
-  constexpr int NST = CG == 2 ? PAIR_STAGES : STAGES;
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmD, GemmParams p) {
+  constexpr int NST = CG == 2 ? PAIR_STAGES : STAGES;  // shared-memory layout (maximum)
+  const int nst = CG == 2 ? (p.nst >= 2 && p.nst <= NST ? p.nst : NST) : STAGES;  // ring length in use
   constexpr int BROWS = CG == 2 ? PAIR_B_ROWS : BN;   // B rows held by this CTA
   constexpr int B_BYTES = BROWS * BK * 2;
   constexpr int ST_BYTES = A_STAGE_BYTES + B_BYTES;
@@ -230,7 +250,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + NST * A_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NST * ST_BYTES);
+  uint8_t* sEpi = smem + NST * ST_BYTES;  // 1024-aligned: stages are multiples of 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + EPI_SMEM);
   uint64_t* full = bars;
   uint64_t* empty = bars + NST;
   uint64_t* tfull = bars + 2 * NST;
@@ -336,7 +357,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 tma_load_2d(b_dst + q * BK * 128, &tmB, &full[stage], n0 + 64 * q, k0 + boff);
             }
           }
-          if (++stage == NST) { stage = 0; phase ^= 1; }
+          if (++stage == nst) { stage = 0; phase ^= 1; }
         }
       }
       if (!ok) {
@@ -383,7 +404,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           } else {
             tc_commit(&empty[stage]);
           }
-          if (++stage == NST) { stage = 0; phase ^= 1; }
+          if (++stage == nst) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
         if constexpr (CG == 2) {
@@ -405,6 +426,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool vec = p.vec_ok != 0;
+    // TMA epilogue: this warp's two 4 KB staging boxes, and how many boxes it has issued
+    uint8_t* eslab = sEpi + (warp - 2) * 8192;
+    int ebox = 0;
     for (int t = unit0; t < p.num_tiles; t += unit_step) {
       const Unit un = unit_info(t, p, num_kb);
       if (!un.valid) continue;
@@ -436,7 +460,74 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + lane_base + acc * BN;
 
-      if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_SWIGLU_BWD) {
+      if ((EPI == EPI_BF16 || EPI == EPI_F32) && p.tma_out) {
+        // Through shared memory: each warp stages its 32 rows of a 128-byte-wide column
+        // block (64 bf16 or 32 f32 columns, 128B-swizzled) and one lane issues a TMA
+        // store (or, for an accumulating f32 output, a TMA reduce-add performed in L2)
+        // of the 32 x 128-byte box.  Full-line writes, no read of D by the threads; the
+        // map clips rows past M and columns past N.
+        const int y = m0 + quarter * 32;
+        constexpr int CPB = EPI == EPI_BF16 ? 2 : 1;  // 32-column chunks per box
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tc_wait_ld();
+          if (c == BN / 32 - 1) { tc_fence_before(); release_acc(acc); }
+          const int col = n0 + c * 32;
+          const int nvalid = min(32, p.N - col);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+          if constexpr (EPI == EPI_BF16) {
+            if (row_ok && nvalid > 0) {
+              if (p.bias) {
+                float bb[32];
+                load_bf16_row(p.bias + col, bb, nvalid, vec);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += bb[j];
+              }
+              if (p.R) {
+                float rr[32];
+                load_bf16_row(p.R + (int64_t)row * p.ldr + col, rr, nvalid, vec);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += rr[j];
+              }
+            }
+          }
+          uint8_t* buf = eslab + (ebox & 1) * 4096;
+          if (c % CPB == 0) {  // a new box: the box issued two boxes ago from this buffer was read
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+          }
+          if constexpr (EPI == EPI_BF16) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              sw128_store16(buf, lane, (c & 1) * 4 + q,
+                            make_uint4(pack_bf16(v[q * 8], v[q * 8 + 1]), pack_bf16(v[q * 8 + 2], v[q * 8 + 3]),
+                                       pack_bf16(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16(v[q * 8 + 6], v[q * 8 + 7])));
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              sw128_store16(buf, lane, q,
+                            make_uint4(__float_as_uint(v[q * 4]), __float_as_uint(v[q * 4 + 1]),
+                                       __float_as_uint(v[q * 4 + 2]), __float_as_uint(v[q * 4 + 3])));
+          }
+          if (c % CPB == CPB - 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const int x = n0 + (c - (CPB - 1)) * 32;
+              if (y < p.M && x < p.N && !p.diag_nostore) {
+                if (p.tma_out == 3) tma_reduce_add_2d(&tmD, buf, x, y);
+                else tma_store_2d(&tmD, buf, x, y);
+              }
+              bulk_commit();
+            }
+            ++ebox;
+          }
+        }
+      } else if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_SWIGLU_BWD) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -454,7 +545,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (c == BN / 32 - 1) { tc_fence_before(); release_acc(acc); }
           const int col = n0 + c * 32;
           const int nvalid = min(32, p.N - col);
-          if (!row_ok || nvalid <= 0) continue;
+          if (!row_ok || nvalid <= 0 || p.diag_nostore) continue;
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
@@ -669,6 +760,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (p.tma_out && lane == 0) bulk_wait<0>();  // every TMA store / reduce of this warp performed
   }
 
   tc_fence_before();
@@ -720,7 +812,8 @@ inline void ensure_current_context() {
 
 // 2-D bf16 tensor map over a row-major matrix [rows, cols] with row stride
 // `ld` elements, box {box_cols, box_rows}, 128-byte swizzle, zero OOB fill.
-inline CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
+inline CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows,
+                                  CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B) {
   OXI_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
   OXI_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes (ld % 8 == 0)");
   ensure_current_context();
@@ -730,10 +823,34 @@ inline CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, 
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   OXI_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
   return m;
+}
+
+// 2-D tensor map over the GEMM output D [rows, cols] (row stride ld elements) for the TMA
+// epilogue: boxes of 32 rows x 128 bytes (64 bf16 or 32 f32 columns), 128-byte swizzle.
+inline CUtensorMap make_tmap_out(void* base, int64_t rows, int64_t cols, int64_t ld, bool f32) {
+  const int es = f32 ? 4 : 2;
+  OXI_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0 && (ld * es) % 16 == 0, "TMA output alignment");
+  ensure_current_context();
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base,
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  OXI_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (GEMM output) failed: ", (int)r);
+  return m;
+}
+
+// Whether the TMA epilogue is enabled (OXI_GEMM_TMA_EPI=0 keeps per-thread stores).
+inline bool gemm_tma_epilogue() {
+  static const int on = gemm_env_int("OXI_GEMM_TMA_EPI", 1, 0, 1);
+  return on != 0;
 }
 
 inline int num_sms() {
@@ -746,8 +863,9 @@ inline int num_sms() {
   return n;
 }
 
-constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr int GEMM_PAIR_SMEM = PAIR_STAGES * (A_STAGE_BYTES + PAIR_B_ROWS * BK * 2) + 1024 + 256;
+constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + EPI_SMEM + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int GEMM_PAIR_SMEM = PAIR_STAGES * (A_STAGE_BYTES + PAIR_B_ROWS * BK * 2) + EPI_SMEM + 1024 + 256;
+static_assert(GEMM_SMEM <= 232448 && GEMM_PAIR_SMEM <= 232448, "GEMM shared memory budget");
 
 // Clusters of two (one CTA per SM) that fit on the device at once.
 template <typename K>
@@ -773,8 +891,13 @@ inline int max_pair_clusters(K kern) {
 }
 
 template <bool A_MN, bool B_MN, int EPI>
-static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, cudaStream_t st) {
+static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, cudaStream_t st,
+                     const CUtensorMap* td = nullptr) {
   if (p.num_tiles <= 0) return;
+  CUtensorMap tdv;
+  if (td) tdv = *td;
+  else memset(&tdv, 0, sizeof(tdv));
+  if (!td) p.tma_out = 0;
   if (p.cg == 2) {
     auto kern = gemm_kernel<A_MN, B_MN, EPI, 2>;
     static bool attr = false;
@@ -795,7 +918,7 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    OXI_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+    OXI_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tdv, p));
     return;
   }
   auto kern = gemm_kernel<A_MN, B_MN, EPI, 1>;
@@ -805,17 +928,27 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p
     attr = true;
   }
   int grid = std::min(p.num_tiles, num_sms());
-  kern<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, p);
+  kern<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, tdv, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 
 template <int EPI>
 static void launch_epi(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
-                       cudaStream_t st) {
-  if (!a_mn && !b_mn) launch_t<false, false, EPI>(ta, tb, p, st);
-  else if (!a_mn && b_mn) launch_t<false, true, EPI>(ta, tb, p, st);
-  else if (a_mn && !b_mn) launch_t<true, false, EPI>(ta, tb, p, st);
-  else launch_t<true, true, EPI>(ta, tb, p, st);
+                       cudaStream_t st, const CUtensorMap* td = nullptr) {
+  if (!a_mn && !b_mn) launch_t<false, false, EPI>(ta, tb, p, st, td);
+  else if (!a_mn && b_mn) launch_t<false, true, EPI>(ta, tb, p, st, td);
+  else if (a_mn && !b_mn) launch_t<true, false, EPI>(ta, tb, p, st, td);
+  else launch_t<true, true, EPI>(ta, tb, p, st, td);
+}
+
+// Launch tuning shared by every GEMM entry point (read once per process).
+inline void gemm_tuning(GemmParams& p) {
+  static const int gm = gemm_env_int("OXI_GEMM_GROUP_M", GROUP_M, 1, 64);
+  static const int ns = gemm_env_int("OXI_GEMM_PAIR_STAGES", PAIR_STAGES, 2, PAIR_STAGES);
+  static const int ns0 = gemm_env_int("OXI_GEMM_DIAG_NOSTORE", 0, 0, 1);
+  p.group_m = gm;
+  p.nst = ns;
+  p.diag_nostore = ns0;
 }
 
 // Operand description (row-major storage, unit inner stride):
@@ -828,9 +961,15 @@ struct Operand {
 };
 
 inline CUtensorMap operand_tmap(const Operand& o, int tile_rows) {
-  if (!o.mn) return make_tmap_bf16(o.ptr, o.rows, o.k, o.ld, BK, tile_rows);
+  // L2 sector promotion of the operand loads (OXI_GEMM_L2PROMO: 0 none, 1 64 B, 2 128 B, 3 256 B)
+  static const int pr = gemm_env_int("OXI_GEMM_L2PROMO", 3, 0, 3);
+  const CUtensorMapL2promotion promo = pr == 0 ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                                       : pr == 1 ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
+                                       : pr == 2 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+                                                 : CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+  if (!o.mn) return make_tmap_bf16(o.ptr, o.rows, o.k, o.ld, BK, tile_rows, promo);
   // stored [K, rows]; box = 64 row-elements (inner) x BK k-rows
-  return make_tmap_bf16(o.ptr, o.k, o.rows, o.ld, 64, BK);
+  return make_tmap_bf16(o.ptr, o.k, o.rows, o.ld, 64, BK, promo);
 }
 
 inline void fill_common(GemmParams& p, const Operand& a, const Operand& b) {
@@ -845,6 +984,7 @@ inline void fill_common(GemmParams& p, const Operand& a, const Operand& b) {
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.alpha = 1.f;
   p.cg = 1;
+  gemm_tuning(p);
 }
 
 // Switch a plain (ungrouped) GEMM to CTA-pair 256 x 256 tiles when it has more

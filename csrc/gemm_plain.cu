@@ -38,13 +38,26 @@ void launch_gemm(const Mat& a, bool a_mn, const Mat& b, bool b_mn, void* out, in
       p.ldr = ldr;
       p.vec_ok = p.vec_ok && aligned16(resid, ldr, 2);
     }
-    launch_epi<EPI_BF16>(a_mn, b_mn, ta, tb, p, st);
+    if (gemm_tma_epilogue() && aligned16(out, ldo, 2)) {
+      const CUtensorMap td = make_tmap_out(out, p.M, p.N, ldo, false);
+      p.tma_out = 1;
+      launch_epi<EPI_BF16>(a_mn, b_mn, ta, tb, p, st, &td);
+    } else {
+      launch_epi<EPI_BF16>(a_mn, b_mn, ta, tb, p, st);
+    }
   } else {
     OXI_CHECK(bias == nullptr, "bias epilogue only for bf16 output");
     p.vec_ok = aligned16(out, ldo, 4);
     p.beta = beta;
     if (beta == 1.0f) choose_splits(p);
-    launch_epi<EPI_F32>(a_mn, b_mn, ta, tb, p, st);
+    if (gemm_tma_epilogue() && aligned16(out, ldo, 4) && (beta == 0.0f || beta == 1.0f)) {
+      // beta 1 (weight gradients, split-K partials): the epilogue's TMA adds in L2
+      const CUtensorMap td = make_tmap_out(out, p.M, p.N, ldo, true);
+      p.tma_out = beta == 1.0f ? 3 : 2;
+      launch_epi<EPI_F32>(a_mn, b_mn, ta, tb, p, st, &td);
+    } else {
+      launch_epi<EPI_F32>(a_mn, b_mn, ta, tb, p, st);
+    }
   }
 }
 

@@ -231,6 +231,7 @@ void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& 
                          const GroupedScatter* scatter) {
   Operand oa = op_of(a, a_mn), ob = op_of(b, b_mn);
   GemmParams p{};
+  gemm_tuning(p);
   p.group_mode = mode;
   p.n_groups = n_groups;
   p.seg_off = seg_off;
