@@ -64,7 +64,8 @@ struct GemmParams {
   int nst;                           // CTA-pair pipeline stages in use (<= PAIR_STAGES)
   int diag_nostore;                  // diagnostics: the epilogue drains TMEM but stores nothing
   int tma_out;                       // epilogue through shared memory + TMA: 0 off, 1 bf16 store,
-                                     // 2 f32 store, 3 f32 reduce-add (the tmD map covers D)
+                                     // 2 f32 store, 3 f32 reduce-add (the tmD map covers D),
+                                     // 4 f32 reduce-add into expert e's slice of a 3-D [E][M][N] map
   int splits;                        // split-K factor (F32 accumulate epilogue only)
   int kb_per_split;
   void* D;                 // main output
@@ -519,7 +520,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (lane == 0) {
               const int x = n0 + (c - (CPB - 1)) * 32;
               if (y < p.M && x < p.N && !p.diag_nostore) {
-                if (p.tma_out == 3) tma_reduce_add_2d(&tmD, buf, x, y);
+                if (p.tma_out == 4) tma_reduce_add_3d(&tmD, buf, x, y, un.e);  // per-expert [E][M][N]
+                else if (p.tma_out == 3) tma_reduce_add_2d(&tmD, buf, x, y);
                 else tma_store_2d(&tmD, buf, x, y);
               }
               bulk_commit();
@@ -844,6 +846,25 @@ inline CUtensorMap make_tmap_out(void* base, int64_t rows, int64_t cols, int64_t
                                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   OXI_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (GEMM output) failed: ", (int)r);
+  return m;
+}
+
+// 3-D f32 map over per-expert outputs [groups][rows][cols] (row stride ld, expert stride
+// group_stride elements) for the grouped weight-gradient reduce-adds.
+inline CUtensorMap make_tmap_out3_f32(void* base, int64_t groups, int64_t rows, int64_t cols, int64_t ld,
+                                      int64_t group_stride) {
+  OXI_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0 && (ld * 4) % 16 == 0 && (group_stride * 4) % 16 == 0,
+            "TMA output alignment (grouped)");
+  ensure_current_context();
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)groups};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 4), (cuuint64_t)(group_stride * 4)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  OXI_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (grouped GEMM output) failed: ", (int)r);
   return m;
 }
 

@@ -281,16 +281,32 @@ void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& 
     p.post_seq = scatter->post_seq;
   }
   switch (epi) {
-    case 0:
+    case 0: {
       p.vec_ok = aligned16(out, ldo, 2);
-      if (!b_mn) launch_t<false, false, EPI_BF16>(ta, tb, p, st);
-      else launch_t<false, true, EPI_BF16>(ta, tb, p, st);
+      // rows stay in the concatenated segment order, so one 2-D map covers every expert;
+      // scattered rows (expert parallelism) keep per-thread stores
+      CUtensorMap td;
+      const bool tma = !scatter && gemm_tma_epilogue() && aligned16(out, ldo, 2);
+      if (tma) {
+        td = make_tmap_out(out, p.M, p.N, ldo, false);
+        p.tma_out = 1;
+      }
+      if (!b_mn) launch_t<false, false, EPI_BF16>(ta, tb, p, st, tma ? &td : nullptr);
+      else launch_t<false, true, EPI_BF16>(ta, tb, p, st, tma ? &td : nullptr);
       break;
-    case 1:
+    }
+    case 1: {
       p.vec_ok = aligned16(out, ldo, 4);
       p.beta = 1.f;
-      launch_t<true, true, EPI_F32>(ta, tb, p, st);
+      CUtensorMap td;
+      const bool tma = gemm_tma_epilogue() && aligned16(out, ldo, 4) && (p.d_group_stride * 4) % 16 == 0;
+      if (tma) {
+        td = make_tmap_out3_f32(out, n_groups, p.M, p.N, ldo, p.d_group_stride);
+        p.tma_out = 4;
+      }
+      launch_t<true, true, EPI_F32>(ta, tb, p, st, tma ? &td : nullptr);
       break;
+    }
     case 2:
       OXI_CHECK(!b_mn && p.N % 256 == 0, "grouped SwiGLU: K-major weights, 2I % 256 == 0");
       p.D2 = out2;
