@@ -240,7 +240,8 @@ __device__ __forceinline__ void load_bf16_row(const __nv_bfloat16* src, float* v
 template <bool A_MN, bool B_MN, int EPI, int CG = 1>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmD, GemmParams p) {
+                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
+                GemmParams p) {
   constexpr int NST = CG == 2 ? PAIR_STAGES : STAGES;  // shared-memory layout (maximum)
   const int nst = CG == 2 ? (p.nst >= 2 && p.nst <= NST ? p.nst : NST) : STAGES;  // ring length in use
   constexpr int BROWS = CG == 2 ? PAIR_B_ROWS : BN;   // B rows held by this CTA
@@ -638,6 +639,69 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             store_bf16_row(dgp + 128, du, nvalid, vec);
           }
         }
+      } else if (EPI == EPI_SWIGLU && p.tma_out) {
+        // TMA form: per pair of 32-column chunks, the 64 gate and 64 up pre-activation columns
+        // of gu (map tmD2) and the 64 columns of h = silu(gate) * up (map tmD) each leave as
+        // one 32-row x 128-byte box
+        const int y = m0 + quarter * 32;
+        auto box_begin = [&]() -> uint8_t* {
+          uint8_t* b = eslab + (ebox & 1) * 4096;
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          return b;
+        };
+        auto box_fill = [&](uint8_t* b, const float* lo, const float* hi) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            sw128_store16(b, lane, q, make_uint4(pack_bf16(lo[q * 8], lo[q * 8 + 1]), pack_bf16(lo[q * 8 + 2], lo[q * 8 + 3]),
+                                                 pack_bf16(lo[q * 8 + 4], lo[q * 8 + 5]), pack_bf16(lo[q * 8 + 6], lo[q * 8 + 7])));
+            sw128_store16(b, lane, 4 + q, make_uint4(pack_bf16(hi[q * 8], hi[q * 8 + 1]), pack_bf16(hi[q * 8 + 2], hi[q * 8 + 3]),
+                                                     pack_bf16(hi[q * 8 + 4], hi[q * 8 + 5]), pack_bf16(hi[q * 8 + 6], hi[q * 8 + 7])));
+          }
+        };
+        auto box_issue = [&](uint8_t* b, const CUtensorMap* tm, int x, int xmax) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (y < p.M && x < xmax && !p.diag_nostore) tma_store_2d(tm, b, x, y);
+            bulk_commit();
+          }
+          ++ebox;
+        };
+#pragma unroll 1
+        for (int c = 0; c < 4; c += 2) {
+          uint32_t rg0[32], ru0[32], rg1[32], ru1[32];
+          tmem_ld32(tbase + c * 32, rg0);
+          tmem_ld32(tbase + 128 + c * 32, ru0);
+          tmem_ld32(tbase + (c + 1) * 32, rg1);
+          tmem_ld32(tbase + 128 + (c + 1) * 32, ru1);
+          tc_wait_ld();
+          if (c == 2) { tc_fence_before(); release_acc(acc); }
+          float g0[32], g1[32], u0[32], u1[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            g0[j] = __uint_as_float(rg0[j]);
+            g1[j] = __uint_as_float(rg1[j]);
+            u0[j] = __uint_as_float(ru0[j]);
+            u1[j] = __uint_as_float(ru1[j]);
+          }
+          if (p.D2) {
+            uint8_t* b = box_begin();
+            box_fill(b, g0, g1);
+            box_issue(b, &tmD2, n0 + c * 32, p.N);
+            b = box_begin();
+            box_fill(b, u0, u1);
+            box_issue(b, &tmD2, n0 + 128 + c * 32, p.N);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            g0[j] = silu_f(g0[j]) * u0[j];
+            g1[j] = silu_f(g1[j]) * u1[j];
+          }
+          uint8_t* b = box_begin();
+          box_fill(b, g0, g1);
+          box_issue(b, &tmD, n0 / 2 + c * 32, p.N / 2);
+        }
       } else if constexpr (EPI == EPI_SWIGLU) {
         // tile columns [0,128) gate, [128,256) up, for output columns n0/2 + [0,128)
 #pragma unroll 1
@@ -913,11 +977,13 @@ inline int max_pair_clusters(K kern) {
 
 template <bool A_MN, bool B_MN, int EPI>
 static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p, cudaStream_t st,
-                     const CUtensorMap* td = nullptr) {
+                     const CUtensorMap* td = nullptr, const CUtensorMap* td2 = nullptr) {
   if (p.num_tiles <= 0) return;
-  CUtensorMap tdv;
+  CUtensorMap tdv, tdv2;
   if (td) tdv = *td;
   else memset(&tdv, 0, sizeof(tdv));
+  if (td2) tdv2 = *td2;
+  else memset(&tdv2, 0, sizeof(tdv2));
   if (!td) p.tma_out = 0;
   if (p.cg == 2) {
     auto kern = gemm_kernel<A_MN, B_MN, EPI, 2>;
@@ -939,7 +1005,7 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    OXI_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tdv, p));
+    OXI_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tdv, tdv2, p));
     return;
   }
   auto kern = gemm_kernel<A_MN, B_MN, EPI, 1>;
@@ -949,7 +1015,7 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p
     attr = true;
   }
   int grid = std::min(p.num_tiles, num_sms());
-  kern<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, tdv, p);
+  kern<<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(ta, tb, tdv, tdv2, p);
   OXI_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -312,7 +312,15 @@ void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& 
       p.D2 = out2;
       p.ldd2 = ldo2;
       p.vec_ok = aligned16(out, ldo, 2) && aligned16(out2, ldo2, 2);
-      launch_t<false, false, EPI_SWIGLU>(ta, tb, p, st);
+      if (gemm_tma_epilogue() && aligned16(out, ldo, 2) && (!out2 || aligned16(out2, ldo2, 2))) {
+        const CUtensorMap th = make_tmap_out(out, p.M, p.N / 2, ldo, false);
+        CUtensorMap tg;
+        if (out2) tg = make_tmap_out(out2, p.M, p.N, ldo2, false);
+        p.tma_out = 1;
+        launch_t<false, false, EPI_SWIGLU>(ta, tb, p, st, &th, out2 ? &tg : nullptr);
+      } else {
+        launch_t<false, false, EPI_SWIGLU>(ta, tb, p, st);
+      }
       break;
     case 3:
       OXI_CHECK(b_mn && p.N % 128 == 0, "grouped SwiGLU backward: MN-major weights");
