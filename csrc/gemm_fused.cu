@@ -26,7 +26,7 @@ void launch_gemm_swiglu(const Mat& x, const Mat& w, void* h, int64_t ldh, void* 
   p.status = status;
   if (p.M == 0) return;
   CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
-  if (gemm_tma_epilogue() && aligned16(h, ldh, 2) && (!gu || aligned16(gu, ldgu, 2))) {
+  if (gemm_tma_swiglu() && aligned16(h, ldh, 2) && (!gu || aligned16(gu, ldgu, 2))) {
     const CUtensorMap th = make_tmap_out(h, p.M, p.N / 2, ldh, false);
     CUtensorMap tg;
     if (gu) tg = make_tmap_out(gu, p.M, p.N, ldgu, false);

@@ -932,10 +932,15 @@ inline CUtensorMap make_tmap_out3_f32(void* base, int64_t groups, int64_t rows, 
   return m;
 }
 
-// Whether the TMA epilogue is enabled (OXI_GEMM_TMA_EPI=0 keeps per-thread stores).
+// Whether the TMA epilogue is enabled (OXI_GEMM_TMA_EPI=0 keeps per-thread stores;
+// OXI_GEMM_TMA_SWIGLU=0 only for the SwiGLU epilogue).
 inline bool gemm_tma_epilogue() {
   static const int on = gemm_env_int("OXI_GEMM_TMA_EPI", 1, 0, 1);
   return on != 0;
+}
+inline bool gemm_tma_swiglu() {
+  static const int on = gemm_env_int("OXI_GEMM_TMA_SWIGLU", 1, 0, 1);
+  return on != 0 && gemm_tma_epilogue();
 }
 
 inline int num_sms() {

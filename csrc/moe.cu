@@ -312,7 +312,7 @@ void launch_gemm_grouped(int mode, int epi, const Mat& a, bool a_mn, const Mat& 
       p.D2 = out2;
       p.ldd2 = ldo2;
       p.vec_ok = aligned16(out, ldo, 2) && aligned16(out2, ldo2, 2);
-      if (gemm_tma_epilogue() && aligned16(out, ldo, 2) && (!out2 || aligned16(out2, ldo2, 2))) {
+      if (gemm_tma_swiglu() && aligned16(out, ldo, 2) && (!out2 || aligned16(out2, ldo2, 2))) {
         const CUtensorMap th = make_tmap_out(out, p.M, p.N / 2, ldo, false);
         CUtensorMap tg;
         if (out2) tg = make_tmap_out(out2, p.M, p.N, ldo2, false);
