@@ -77,6 +77,13 @@ void launch_gemm_ce(const Mat& x, const Mat& w, const int64_t* targets, float* p
   p.status = status;
   if (p.M == 0) return;
   CUtensorMap ta = operand_tmap(oa, BM), tb = operand_tmap(ob, b_tile_rows(p));
+  if (logits && gemm_tma_ce() && aligned16(logits, ldl, 2)) {
+    // the bf16 logits leave through TMA stores (the row statistics stay per thread)
+    const CUtensorMap td = make_tmap_out(logits, p.M, p.N, ldl, false);
+    p.tma_out = 1;
+    launch_t<false, false, EPI_CE>(ta, tb, p, st, &td);
+    return;
+  }
   launch_t<false, false, EPI_CE>(ta, tb, p, st);
 }
 

@@ -461,6 +461,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + lane_base + acc * BN;
+      // TMA epilogue helpers: a 32-row x 128-byte box in one of this warp's two staging
+      // buffers (the box issued two boxes ago from it must have been read), filled from two
+      // 32-value halves as bf16, then stored by one lane
+      const int y = m0 + quarter * 32;  // first row of this warp's boxes
+      auto box_begin = [&]() -> uint8_t* {
+        uint8_t* b = eslab + (ebox & 1) * 4096;
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        return b;
+      };
+      auto box_fill = [&](uint8_t* b, const float* lo, const float* hi) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          sw128_store16(b, lane, q, make_uint4(pack_bf16(lo[q * 8], lo[q * 8 + 1]), pack_bf16(lo[q * 8 + 2], lo[q * 8 + 3]),
+                                               pack_bf16(lo[q * 8 + 4], lo[q * 8 + 5]), pack_bf16(lo[q * 8 + 6], lo[q * 8 + 7])));
+          sw128_store16(b, lane, 4 + q, make_uint4(pack_bf16(hi[q * 8], hi[q * 8 + 1]), pack_bf16(hi[q * 8 + 2], hi[q * 8 + 3]),
+                                                   pack_bf16(hi[q * 8 + 4], hi[q * 8 + 5]), pack_bf16(hi[q * 8 + 6], hi[q * 8 + 7])));
+        }
+      };
+      auto box_issue = [&](uint8_t* b, const CUtensorMap* tm, int x, int xmax) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (y < p.M && x < xmax && !p.diag_nostore) tma_store_2d(tm, b, x, y);
+          bulk_commit();
+        }
+        ++ebox;
+      };
 
       if ((EPI == EPI_BF16 || EPI == EPI_F32) && p.tma_out) {
         // Through shared memory: each warp stages its 32 rows of a 128-byte-wide column
@@ -468,7 +496,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // store (or, for an accumulating f32 output, a TMA reduce-add performed in L2)
         // of the 32 x 128-byte box.  Full-line writes, no read of D by the threads; the
         // map clips rows past M and columns past N.
-        const int y = m0 + quarter * 32;
         constexpr int CPB = EPI == EPI_BF16 ? 2 : 1;  // 32-column chunks per box
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -643,31 +670,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // TMA form: per pair of 32-column chunks, the 64 gate and 64 up pre-activation columns
         // of gu (map tmD2) and the 64 columns of h = silu(gate) * up (map tmD) each leave as
         // one 32-row x 128-byte box
-        const int y = m0 + quarter * 32;
-        auto box_begin = [&]() -> uint8_t* {
-          uint8_t* b = eslab + (ebox & 1) * 4096;
-          if (lane == 0) bulk_wait_read<1>();
-          __syncwarp();
-          return b;
-        };
-        auto box_fill = [&](uint8_t* b, const float* lo, const float* hi) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            sw128_store16(b, lane, q, make_uint4(pack_bf16(lo[q * 8], lo[q * 8 + 1]), pack_bf16(lo[q * 8 + 2], lo[q * 8 + 3]),
-                                                 pack_bf16(lo[q * 8 + 4], lo[q * 8 + 5]), pack_bf16(lo[q * 8 + 6], lo[q * 8 + 7])));
-            sw128_store16(b, lane, 4 + q, make_uint4(pack_bf16(hi[q * 8], hi[q * 8 + 1]), pack_bf16(hi[q * 8 + 2], hi[q * 8 + 3]),
-                                                     pack_bf16(hi[q * 8 + 4], hi[q * 8 + 5]), pack_bf16(hi[q * 8 + 6], hi[q * 8 + 7])));
-          }
-        };
-        auto box_issue = [&](uint8_t* b, const CUtensorMap* tm, int x, int xmax) {
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (y < p.M && x < xmax && !p.diag_nostore) tma_store_2d(tm, b, x, y);
-            bulk_commit();
-          }
-          ++ebox;
-        };
 #pragma unroll 1
         for (int c = 0; c < 4; c += 2) {
           uint32_t rg0[32], ru0[32], rg1[32], ru1[32];
@@ -741,7 +743,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (c + 2 == BN / 32) { tc_fence_before(); release_acc(acc); }
           const int col = n0 + c * 32;
           const int nvalid = min(64, p.N - col);
-          if (!row_ok || nvalid <= 0) continue;
+          // the TMA logit store is warp-wide: every lane takes part even without a row
+          if (!p.tma_out && (!row_ok || nvalid <= 0)) continue;
           float v[64];
           float cmax = -INFINITY;
 #pragma unroll
@@ -749,24 +752,32 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             v[j] = __uint_as_float(j < 32 ? r0[j] : r1[j - 32]) * p.alpha;
             if (j < nvalid) cmax = fmaxf(cmax, v[j]);
           }
-          const float nmax = fmaxf(run_max, cmax);
-          float s = 0.f;
-#pragma unroll
-          for (int j = 0; j < 64; ++j)
-            if (j < nvalid) s += __expf(v[j] - nmax);
-          run_sum = run_sum * __expf(run_max - nmax) + s;
-          run_max = nmax;
-          if (tgt >= col && tgt < col + nvalid) {
-            float tv = 0.f;
+          if (row_ok && nvalid > 0) {
+            const float nmax = fmaxf(run_max, cmax);
+            float s = 0.f;
 #pragma unroll
             for (int j = 0; j < 64; ++j)
-              if (col + j == tgt) tv = v[j];
-            p.tgt_logit[row] = tv;
+              if (j < nvalid) s += __expf(v[j] - nmax);
+            run_sum = run_sum * __expf(run_max - nmax) + s;
+            run_max = nmax;
+            if (tgt >= col && tgt < col + nvalid) {
+              float tv = 0.f;
+#pragma unroll
+              for (int j = 0; j < 64; ++j)
+                if (col + j == tgt) tv = v[j];
+              p.tgt_logit[row] = tv;
+            }
           }
           if (Dp) {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
-            store_bf16_row(dst, v, min(32, nvalid), vec);
-            if (nvalid > 32) store_bf16_row(dst + 32, v + 32, nvalid - 32, vec);
+            if (p.tma_out) {
+              uint8_t* b = box_begin();
+              box_fill(b, v, v + 32);
+              box_issue(b, &tmD, col, p.N);
+            } else {
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(Dp) + (int64_t)row * p.ldd + col;
+              store_bf16_row(dst, v, min(32, nvalid), vec);
+              if (nvalid > 32) store_bf16_row(dst + 32, v + 32, nvalid - 32, vec);
+            }
           }
         }
         if (row_ok) {
@@ -933,13 +944,17 @@ inline CUtensorMap make_tmap_out3_f32(void* base, int64_t groups, int64_t rows, 
 }
 
 // Whether the TMA epilogue is enabled (OXI_GEMM_TMA_EPI=0 keeps per-thread stores;
-// OXI_GEMM_TMA_SWIGLU=0 only for the SwiGLU epilogue).
+// OXI_GEMM_TMA_SWIGLU=0 / OXI_GEMM_TMA_CE=0 only for the SwiGLU / cross-entropy epilogue).
 inline bool gemm_tma_epilogue() {
   static const int on = gemm_env_int("OXI_GEMM_TMA_EPI", 1, 0, 1);
   return on != 0;
 }
 inline bool gemm_tma_swiglu() {
   static const int on = gemm_env_int("OXI_GEMM_TMA_SWIGLU", 1, 0, 1);
+  return on != 0 && gemm_tma_epilogue();
+}
+inline bool gemm_tma_ce() {  // OXI_GEMM_TMA_CE=0: the cross-entropy epilogue's logits per thread
+  static const int on = gemm_env_int("OXI_GEMM_TMA_CE", 1, 0, 1);
   return on != 0 && gemm_tma_epilogue();
 }
 
