@@ -44,6 +44,20 @@ PHASES = [
 ]
 
 
+def phase_rooflines(rows_out: int, rows_in: int, rows_local: int, H: int, I: int, peak_flops: float,
+                    nvlink_gbs: float = NVLINK_GBS) -> dict:
+    """Roofline (ms) of each phase kind for one rank: NVLink time of the larger of the rows
+    it sends and receives (H bf16 values each); GEMM FLOPs of the rows its experts process
+    at ``peak_flops``; the phases with a fused return scatter take the slower of the two."""
+    t_link = max(rows_out, rows_in) * 2 * H / (nvlink_gbs * 1e9) * 1e3
+    fl = {"gemm_gu": 2 * rows_local * H * 2 * I, "gemm_down_ret": 2 * rows_local * I * H,
+          "gemm_wgrad": 2 * rows_local * H * 3 * I, "gemm_dx_ret": 2 * rows_local * 2 * I * H}
+    roof = {"send_fwd": t_link, "send_bwd": t_link}
+    for kind, f in fl.items():
+        roof[kind] = max(f / peak_flops * 1e3, t_link if kind.endswith("_ret") else 0.0)
+    return roof
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384, help="tokens per rank (config 5: 4 x 4096)")
@@ -96,13 +110,7 @@ def main(argv=None):
     rows_out = int(mat[rank].sum() - mat[rank, rank])
     rows_in = int(mat[:, rank].sum() - mat[rank, rank])
     rows_local = int(mat[:, rank].sum())  # rows this rank's experts process
-    row_b = 2 * H
-    t_link = max(rows_out, rows_in) * row_b / (NVLINK_GBS * 1e9) * 1e3
-    fl = {"gemm_gu": 2 * rows_local * H * 2 * I, "gemm_down_ret": 2 * rows_local * I * H,
-          "gemm_wgrad": 2 * rows_local * H * 3 * I, "gemm_dx_ret": 2 * rows_local * 2 * I * H}
-    roof = {"send_fwd": t_link, "send_bwd": t_link}
-    for kind, f in fl.items():
-        roof[kind] = max(f / peak * 1e3, t_link if kind.endswith("_ret") else 0.0)
+    roof = phase_rooflines(rows_out, rows_in, rows_local, H, I, peak)
     res = {"world": W, "tokens_per_rank": T, "hidden": H, "experts": E, "topk": k, "inter": I,
            "rows_out": rows_out, "rows_in": rows_in, "rows_local": rows_local, "nvlink_gbs": NVLINK_GBS,
            "peak_tflops": peak / 1e12}
