@@ -69,28 +69,47 @@ __global__ void ce_finish_kernel(const float* __restrict__ pmax, const float* __
 // col0: vocabulary index of the buffer's first column (a column chunk of the
 // logits recomputed in the logit-free backward); a target outside the chunk adds
 // no one-hot term, an ignored row (target < 0) is zero.
-__global__ void ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, int64_t V,
-                              const float* __restrict__ lse, const int64_t* __restrict__ targets,
-                              const float* __restrict__ gscale, float inv_count, int64_t col0) {
+// In place: logits[row, c] <- (softmax - onehot) * scale for the columns c of a
+// vocabulary slice starting at col0.  Each thread handles CE_BWD_VEC 16-byte vectors
+// per pass (all loads issued before the math), so a row needs few CTAs and every
+// thread keeps several loads in flight.
+constexpr int CE_BWD_VEC = 4;
+
+__global__ void __launch_bounds__(256) ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, int64_t V,
+                                                     const float* __restrict__ lse,
+                                                     const int64_t* __restrict__ targets,
+                                                     const float* __restrict__ gscale, float inv_count, int64_t col0) {
   const int64_t row = blockIdx.y;
   const float l = lse[row];
   const int64_t t0 = targets[row];
   const float sc = (t0 >= 0) ? (*gscale) * inv_count : 0.f;
   const int64_t t = t0 - col0;
   __nv_bfloat16* rp = logits + row * ld;
+  uint4* rv = reinterpret_cast<uint4*>(rp);
   const int64_t nvec = V / 8;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
-    uint4 u = reinterpret_cast<uint4*>(rp)[i];
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nvec; base += stride * CE_BWD_VEC) {
+    uint4 u[CE_BWD_VEC];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float2 f = __bfloat1622float2(h[k]);
-      const int64_t c = i * 8 + 2 * k;
-      f.x = (__expf(f.x - l) - (c == t ? 1.f : 0.f)) * sc;
-      f.y = (__expf(f.y - l) - (c + 1 == t ? 1.f : 0.f)) * sc;
-      h[k] = __floats2bfloat162_rn(f.x, f.y);
+    for (int q = 0; q < CE_BWD_VEC; ++q) {
+      const int64_t i = base + q * stride;
+      if (i < nvec) u[q] = rv[i];
     }
-    reinterpret_cast<uint4*>(rp)[i] = u;
+#pragma unroll
+    for (int q = 0; q < CE_BWD_VEC; ++q) {
+      const int64_t i = base + q * stride;
+      if (i >= nvec) continue;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u[q]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 f = __bfloat1622float2(h[k]);
+        const int64_t c = i * 8 + 2 * k;
+        f.x = (__expf(f.x - l) - (c == t ? 1.f : 0.f)) * sc;
+        f.y = (__expf(f.y - l) - (c + 1 == t ? 1.f : 0.f)) * sc;
+        h[k] = __floats2bfloat162_rn(f.x, f.y);
+      }
+      rv[i] = u[q];
+    }
   }
   if (blockIdx.x == 0) {
     for (int64_t c = nvec * 8 + threadIdx.x; c < V; c += blockDim.x) {
@@ -346,7 +365,8 @@ void launch_ce_bwd(void* logits, int64_t ld, int64_t V, int64_t rows, const floa
   OXI_CHECK(ld % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0, "logits rows must be 16-byte aligned");
   OXI_CHECK(rows < 65536 * 32768LL, "too many rows");
   const int64_t nvec = V / 8;
-  unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 64));
+  // CTAs per row: enough for one pass of CE_BWD_VEC vectors per thread, at most 16
+  unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((nvec + 256 * CE_BWD_VEC - 1) / (256 * CE_BWD_VEC), 16));
   dim3 grid(gx, (unsigned)rows);
   ce_bwd_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, V, lse, targets, gscale,
                                       inv_count, col0);
