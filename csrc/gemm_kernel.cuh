@@ -1130,7 +1130,8 @@ inline int b_tile_rows(const GemmParams& p) { return p.cg == 2 ? PAIR_B_ROWS : B
 
 // Split K across CTAs when there are too few output tiles to fill the GPU
 // (weight-gradient GEMMs: small M x N, K = tokens).  Only valid for an
-// accumulating f32 output, whose epilogue adds with atomics.  The split count
+// accumulating f32 output, whose epilogue adds atomically (TMA reduce-add in L2,
+// or per-thread f32 atomics without the TMA epilogue).  The split count
 // is chosen for wave fill over the units that run at once (CTAs, or clusters
 // for CTA pairs): the smallest count within 2 % of the best fill, at least 16
 // k-blocks per split, at most four waves of units (more splits cost more in f32
